@@ -1,0 +1,360 @@
+"""Benchmark: utterance-seconds/sec of ResNet34 speaker embedding on B200s.
+
+Workload (sharded): synthetic clips with lengths U(2, 20) s,
+WeSpeaker ResNet34 with q8_0 weights; at N GPUs the global job is N x 8192 clips
+(config 4's 65,536 clips at N = 8) assigned to ranks by LPT on audio seconds
+(weak scaling: fixed work per GPU). One step = every rank embeds its shard
+(FBank -> CMN+stem -> 32 tcgen05 convs -> TSTP+FC+L2, length-bucketed) and one
+NCCL all-gather of the finished embeddings. Inputs (f32 PCM, ~5.8 GB per GPU)
+are device resident for `value`; larger than L2, so no flush is needed.
+
+`e2e` runs the same shard through the public C ABI call a user makes
+(voicedetect_capi_embed_pcm_batch) from host PCM to host embeddings.
+
+`--impl reference` times the reference's own CPU implementation of this path
+(src/fbank.cpp + src/directconv.cpp compiled unmodified, oracle/_ref) on this
+host's cores, on a bounded sample of the same workload per step.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "voice-detect.cpp_b200"))
+
+import vd_synth  # noqa: E402
+
+SR = 16000
+CLIPS_PER_GPU = 8192
+POOL = 64            # distinct synthetic sources the clips are cut from
+SEED = 20261201
+METRIC = "utterance-sec/sec ResNet34 embed"
+UNIT = "utterance-sec/sec"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_pool(n: int = POOL, seconds: float = 20.0) -> list[np.ndarray]:
+    n_s = int(seconds * SR)
+    return [vd_synth.clip_f32(vd_synth.make_clip(SEED + i, n_s)) for i in range(n)]
+
+
+def global_lengths(world: int, per_gpu: int) -> np.ndarray:
+    return vd_synth.clip_lengths(SEED, world * per_gpu, 2.0, 20.0)
+
+
+def lpt_shard(lengths: np.ndarray, world: int) -> list[list[int]]:
+    """Longest-processing-time-first assignment of clips to ranks."""
+    order = np.argsort(-lengths, kind="stable")
+    load = np.zeros(world, np.int64)
+    cnt = np.zeros(world, np.int64)
+    cap = (len(lengths) + world - 1) // world
+    shards: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        cand = np.where(cnt < cap)[0]
+        r = cand[np.argmin(load[cand])]
+        shards[r].append(int(i))
+        load[r] += lengths[i]
+        cnt[r] += 1
+    return shards
+
+
+def clip_of(pool, idx: int, n: int) -> np.ndarray:
+    src = pool[idx % len(pool)]
+    return src[:n]
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = tempfile.NamedTemporaryFile(prefix="clocks_", suffix=".csv", delete=False).name
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_rate(m: dict, pool, lengths: np.ndarray, idx: list[int], threads: int):
+    """The reference's CPU path (FBank + directconv ResNet34 + restated tail) on
+    `idx` clips; returns (audio_seconds, wall_seconds)."""
+    import oracle
+    L = oracle.ref_lib()
+    L.vdref_set_threads(threads)
+    R = oracle.RefResNet34(m)
+    warm = clip_of(pool, idx[0], int(lengths[idx[0]]))
+    R.embed(oracle.ref_fbank(warm))  # weight packing happens once, outside the timing
+    audio = 0.0
+    t0 = time.perf_counter()
+    for i in idx:
+        pcm = clip_of(pool, i, int(lengths[i]))
+        R.embed(oracle.ref_fbank(pcm))
+        audio += len(pcm) / SR
+    return audio, time.perf_counter() - t0
+
+
+def run_reference(args) -> int:
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    m = vd_synth.quantize_q8_0_model(vd_synth.resnet34_model(SEED))
+    pool = make_pool(8, 20.0)
+    lengths = global_lengths(world, args.clips_per_gpu)
+    rng = np.random.default_rng(SEED + 7)
+    per_step = args.ref_clips
+    times, audio_tot = [], 0.0
+    for s in range(args.warmup + args.steps):
+        idx = list(rng.choice(len(lengths), per_step, replace=False))
+        audio, wall = cpu_reference_rate(m, pool, lengths, idx, threads)
+        if s >= args.warmup:
+            times.append(wall)
+            audio_tot += audio
+    value = audio_tot / sum(times)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{per_step} clips per step drawn from the U(2,20) s workload; "
+                                   "reference src/fbank.cpp + src/directconv.cpp (blocked "
+                                   "island, AVX-512) compiled unmodified, q8_0 weights "
+                                   "dequantised to f32, restated TSTP/FC/L2 glue"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def config_dict(args, world):
+    return {"workload": f"BASELINE config 4 shard: ResNet34 q8_0 embed of {args.clips_per_gpu} "
+                        f"clips/GPU, lengths U(2,20) s, LPT-sharded, length-bucketed",
+            "model": "wespeaker_resnet34 (synthetic Kaiming weights, BN folded, q8_0)",
+            "global_batch": world * args.clips_per_gpu, "seq_len": "2-20 s (199-1998 frames)",
+            "parallelism": f"dp{world}", "l2_flush": "inputs larger than L2 (~5.8 GB PCM/GPU)"}
+
+
+def run_b200(args) -> int:
+    import torch
+    import torch.distributed as dist
+    import vd_b200
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local if world > 1 else 0)
+
+    tmp = tempfile.mkdtemp(prefix="vdbench_")
+    m = vd_synth.resnet34_model(SEED)
+    gguf = os.path.join(tmp, "resnet34_q8_0.gguf")
+    vd_synth.write_resnet_gguf(gguf, m, "q8_0")
+    model = vd_b200.Model(gguf)
+
+    pool = make_pool()
+    lengths = global_lengths(world, args.clips_per_gpu)
+    shard = lpt_shard(lengths, world)[rank]
+    n_local = len(shard)
+    lens = [int(lengths[i]) for i in shard]
+    offs = np.zeros(n_local, np.int64)
+    offs[1:] = np.cumsum(lens)[:-1]
+    total = int(sum(lens))
+    audio_local = total / SR
+    log(f"[rank {rank}] {n_local} clips, {audio_local:.0f} audio-s, {4 * total / 1e9:.2f} GB PCM")
+    host_pcm = np.empty(total, np.float32)
+    for k, i in enumerate(shard):
+        host_pcm[offs[k]:offs[k] + lens[k]] = clip_of(pool, i, lens[k])
+    d_pcm = torch.from_numpy(host_pcm).to(dev)
+    n_max = (len(lengths) + world - 1) // world
+    d_out = torch.zeros(n_max, model.dim, device=dev)
+    gathered = torch.empty(world * n_max, model.dim, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, d_out)
+        else:
+            gathered.copy_(d_out)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    model.profile(True)
+    model.profile_read()
+    launches = 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+        launches += model.last_launches()
+    end.record(stream)
+    torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(end)
+    conv_ms, conv_flops, conv_n = model.profile_read()
+    model.profile(False)
+    clk = clocks.stop()
+    model.sync()
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    tot_audio = torch.tensor([audio_local], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tot_audio)
+    value = float(tot_audio.item()) * args.steps / (max_ms / 1e3)
+
+    # e2e through the public C ABI with host buffers (PCM in, embeddings out)
+    clips = [host_pcm[offs[k]:offs[k] + lens[k]] for k in range(n_local)]
+    model.embed_batch(clips[:64])
+    if world > 1:
+        dist.barrier()
+    e2e_times = []
+    for _ in range(args.e2e_steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.embed_batch(clips)
+        e2e_times.append(time.perf_counter() - t0)
+    e_t = torch.tensor([sum(e2e_times) / len(e2e_times)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e2e_value = float(tot_audio.item()) / float(e_t.item())
+
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    achieved = conv_flops / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+    result = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 (f32 accumulate)",
+        "data": "synthetic (seeded harmonic+pink-noise clips, random-init weights)",
+        "config": config_dict(args, world),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * total,
+                "d2h_bytes_per_step": 4 * n_local * model.dim,
+                "api": "voicedetect_capi_embed_pcm_batch"},
+        "gpu_launches": launches,  # our kernels only (the NCCL all-gather is not counted)
+        "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+                     if peaks else "fallback 1.4 PFLOP/s sustained",
+                     "traffic": None, "conv_launches": conv_n,
+                     "conv_ms_per_step": conv_ms / args.steps,
+                     "conv_tflop_per_step": conv_flops / args.steps / 1e12},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        mq = vd_synth.quantize_q8_0_model(m)
+        rng = np.random.default_rng(SEED + 7)
+        idx = list(rng.choice(len(lengths), args.ref_clips, replace=False))
+        audio, wall = cpu_reference_rate(mq, pool, lengths, idx, threads)
+        result["cpu_baseline"] = {
+            "value": audio / wall, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{args.ref_clips} clips ({audio:.0f} audio-s) drawn from the same "
+                      "workload; reference FBank + blocked directconv ResNet34 compiled "
+                      "unmodified (oracle/_ref), all host threads"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--clips-per-gpu", type=int, default=CLIPS_PER_GPU)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--ref-clips", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,131 @@
+/* Op-level C ABI of the B200 engine: the conv / FBank / pooling kernels that the
+ * reference's encoders reach through ggml custom ops, re-dispatched as plain
+ * C calls on device buffers (no torch types, plain pointers and sizes).
+ *
+ * Reference interfaces these entry points replace:
+ *   vdb_conv            <- vd::blocked_conv3x3 / vd::blocked_conv1x1 /
+ *                          vd::blocked_add_relu / vd::directconv_conv3x3 /
+ *                          vd::winograd_conv3x3   (src/directconv.hpp:54,74-85,
+ *                          src/winograd.hpp:32; routing src/backend.cpp:665-793)
+ *   vdb_fbank           <- vd::FBank::compute without CMN (src/fbank.hpp:27-35,
+ *                          src/fbank.cpp:121-191)
+ *   vdb_cmn_stem        <- FBank CMN (src/fbank.cpp:194-201) + the ResNet stem
+ *                          conv2d_bias + ReLU (src/encoder_resnet.cpp:116-117)
+ *   vdb_pool_embed      <- TSTP + seg FC - mean_vec + host L2
+ *                          (src/encoder_resnet.cpp:143-183)
+ *
+ * Every function returns 0 on success and a nonzero status on error; the
+ * message is available from vdb_last_error() (thread-local). Pointers marked
+ * "device" must be device memory; `stream` is a cudaStream_t (NULL = legacy
+ * default stream). Calls are asynchronous with respect to the host.
+ *
+ * ---- Activation layouts (f16) ------------------------------------------------
+ * GRID  G(B, T, F, C): a zero-bordered NHWC tensor with time as rows. Row
+ *   r = (b*(T+2) + tp)*(F+2) + fp for tp in [0, T+2), fp in [0, F+2); element
+ *   (r, c) lives at r*C + c. Pixel (b, t, f) (time t, mel/freq f) is stored at
+ *   (tp, fp) = (t+1, f+1). Border positions and rows with t >= tvalid[b] hold 0.
+ * PHASE P(B, T, F, C): the same data as a G(B, T, F, C) tensor, split into the
+ *   4 stride-2 phases of its zero-bordered grid for a stride-2 consumer whose
+ *   output extents are To = (T-1)/2+1, Fo = (F-1)/2+1. Plane q = 2*(tp&1)+(fp&1)
+ *   is a G(B, To, Fo, C)-shaped block (planes contiguous, q-major); padded
+ *   position (tp, fp) of image b sits in plane q at row
+ *   (b*(To+2) + (tp>>1) + 1)*(Fo+2) + (fp>>1) + 1. Slots no position maps to
+ *   are never read by a valid output.
+ * Weights: f16 [OC][k*k][IC] with tap index kt*k + kf (kt = time tap = the
+ *   reference's kw, kf = freq tap = the reference's kh), i.e. torch
+ *   w[oc][ic][kf][kt] -> W[oc][kt*k + kf][ic].
+ */
+#ifndef VDB_OPS_H
+#define VDB_OPS_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+const char* vdb_last_error(void);
+
+/* Rows of a G(B, T, F, *) tensor and of a P(B, T, F, *) tensor. */
+long long vdb_grid_rows(int batch, int t, int f);
+long long vdb_phase_rows(int batch, int t, int f);
+
+typedef struct vdb_conv_args {
+    int batch;          /* B */
+    int t_out, f_out;   /* output extents; output is G(B, t_out, f_out, oc) (or P when y_phase) */
+    int oc;             /* output channels, multiple of 16 */
+    /* segment 0: the conv itself */
+    int k0;             /* kernel size: 3 (pad 1) or 1 (pad 0) */
+    int stride0;        /* 1: x0 is G(B, t_out, f_out, ic0); 2: x0 is P(B, t_in, f_in, ic0)
+                           whose stride-2 output extents are (t_out, f_out) */
+    int ic0;            /* input channels, multiple of 16 */
+    const void* x0;     /* device f16 */
+    const void* w0;     /* device f16 [oc][k0*k0][ic0] */
+    /* segment 1 (optional, x1 == NULL to disable): a 1x1 conv accumulated into the
+       same outputs (the fused BasicBlock downsample shortcut) */
+    int stride1;        /* 1: x1 is G(B, t_out, f_out, ic1); 2: x1 is P(...) */
+    int ic1;
+    const void* x1;
+    const void* w1;     /* device f16 [oc][ic1] */
+    /* epilogue: y = act(acc + bias [+ residual]) at valid pixels, 0 elsewhere */
+    const float* bias;      /* device f32 [oc] (sum of both segments' biases) */
+    const void* residual;   /* device f16 G(B, t_out, f_out, oc) or NULL */
+    int relu;               /* 1: max(0, .) */
+    float clamp_hi;         /* > 0: min(., clamp_hi) after ReLU (Hardtanh(0, hi)) */
+    const int* tvalid;      /* device int32 [B]: valid time extent of the output */
+    void* y;                /* device f16 output */
+    int y_phase;            /* 0: y is G(B, t_out, f_out, oc); 1: y is P(B, t_out, f_out, oc) */
+    int* err;               /* device int32 error word (may be NULL): kernel timeouts */
+} vdb_conv_args;
+
+/* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */
+int vdb_conv(const vdb_conv_args* a, void* stream);
+
+/* ---- FBank ----------------------------------------------------------------------
+ * A plan holds the device tables of one FBank configuration (the GGUF
+ * voicedetect.fbank.* keys, src/model_loader.cpp:126-136): Povey window, FFT
+ * twiddles and the triangular mel filters. Only n_fft = 512 is supported. */
+typedef struct vdb_fbank_plan vdb_fbank_plan;
+vdb_fbank_plan* vdb_fbank_plan_create(int sample_rate, int n_mels, int n_fft, int win, int hop,
+                                      float preemph, float low_freq, float high_freq);
+void vdb_fbank_plan_destroy(vdb_fbank_plan* plan);
+int vdb_fbank_plan_n_mels(const vdb_fbank_plan* plan);
+
+/* Log-mel features of `batch` clips (16 kHz mono f32, concatenated in device
+ * memory at offsets[b] with n_samples[b] samples; both arrays device int64 /
+ * int32). Clip b yields T_b = 1 + (n_b - win)/hop frames (0 when n_b < win);
+ * frame t < min(T_b, t_max) is written to feats[(b*t_max + t)*n_mels + m]
+ * (device f32, time-major). No CMN here: see vdb_cmn_stem. */
+int vdb_fbank(const vdb_fbank_plan* plan, const float* pcm, const long long* offsets,
+              const int* n_samples, int batch, int t_max, float* feats, void* stream);
+
+/* Per-utterance CMN + the ResNet stem conv (3x3, 1 -> oc, pad 1) + bias + ReLU.
+ * feats: device f32 [batch][t_max][n_mels] from vdb_fbank; frames: device int32
+ * [batch] valid frame counts (T_b); stem_w: device f32 [oc][9] with tap kt*3+kf;
+ * stem_b: device f32 [oc]. mean_scratch: device f32 [batch][n_mels] working
+ * memory (the per-clip CMN means). Output y: G(batch, t_max, n_mels, oc) f16. */
+int vdb_cmn_stem(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                 int cmn, const float* stem_w, const float* stem_b, int oc,
+                 float* mean_scratch, void* y, void* stream);
+
+/* Temporal statistics pooling + embedding FC + L2 normalisation, one CTA per clip.
+ * x: G(batch, t, f, c) f16 final backbone activation; tvalid: device int32 [batch]
+ * valid time extent. pooled[c*f + h] = mean, pooled[c*f*... + c*f + h] = std
+ * (unbiased, + var_eps inside the sqrt); emb = seg_w (f32 [emb_dim][2*c*f]) *
+ * pooled + seg_b - mean_vec (mean_vec may be NULL); then L2-normalised when
+ * l2 != 0. emb_out: device f32 [batch][emb_dim]; prenorm_out (may be NULL)
+ * receives the embedding before normalisation. */
+int vdb_pool_embed(const void* x, const int* tvalid, int batch, int t, int f, int c,
+                   const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
+                   float var_eps, int l2, float* emb_out, float* prenorm_out, void* stream);
+
+/* Top-k cosine search (no reference counterpart exists; the additive C ABI
+ * voicedetect_capi_identify calls it). q: device f32 [n_q][dim]; reg: device f32
+ * [n_reg][dim]; out_idx / out_score: device [n_q][k], descending score, equal
+ * scores ordered by the lower registry index; 0 < k <= 64, dim <= 1024. */
+int vdb_identify(const float* q, int n_q, const float* reg, int n_reg, int dim, int k,
+                 int* out_idx, float* out_score, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

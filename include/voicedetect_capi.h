@@ -1,0 +1,112 @@
+/* Flat C ABI of the B200 voice-detect engine (libvoicedetect_b200.so).
+ *
+ * Drop-in for the reference's frozen ABI, include/voicedetect_capi.h:31-89 of
+ * mudler/voice-detect.cpp (implementation src/voicedetect_capi.cpp:61-176): the
+ * same ten symbols with the same argument meaning, ownership and error
+ * behaviour, so a consumer that dlopens libvoicedetect.so (LocalAI via purego)
+ * can load this library instead. Additive entry points follow the reference's
+ * rule that new functions need no ABI bump (voicedetect_capi.h:25-30).
+ *
+ * Conventions (unchanged from the reference):
+ *  - status 0 = success, nonzero = error; the message is in
+ *    voicedetect_capi_last_error(ctx) until the next call on ctx;
+ *  - embed outputs are reset to NULL / 0 before any work; verify leaves its
+ *    outputs unchanged on error;
+ *  - returned vectors / strings are malloc'd and released with
+ *    voicedetect_capi_free_vec / voicedetect_capi_free_string;
+ *  - no C++ exception crosses the boundary.
+ * Threading: a context owns a CUDA stream, device buffers and a lock; calls on one
+ * context are serialised, calls on different contexts may run concurrently.
+ * The model is placed on the CUDA device that is current when voicedetect_capi_load
+ * is called.
+ */
+#ifndef VOICEDETECT_CAPI_H
+#define VOICEDETECT_CAPI_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct voicedetect_ctx voicedetect_ctx;
+
+/* ---- frozen v1 surface (reference include/voicedetect_capi.h) --------------- */
+
+/* ref :31 */ int voicedetect_capi_abi_version(void);
+/* ref :36 -- NULL on a missing/bad GGUF or when voicedetect.embedding_dim is absent */
+voicedetect_ctx* voicedetect_capi_load(const char* gguf_path);
+/* ref :39 -- safe on NULL */
+void voicedetect_capi_free(voicedetect_ctx* ctx);
+/* ref :45 -- "" for NULL ctx or no error */
+const char* voicedetect_capi_last_error(voicedetect_ctx* ctx);
+/* ref :49 */ void voicedetect_capi_free_string(char* s);
+/* ref :53 */ void voicedetect_capi_free_vec(float* v);
+/* ref :61 -- L2-normalised embedding of a WAV file */
+int voicedetect_capi_embed_path(voicedetect_ctx* ctx, const char* wav_path, float** out_vec,
+                                int* out_dim);
+/* ref :67 -- mono f32 PCM; linearly resampled to 16 kHz when sample_rate != 16000 */
+int voicedetect_capi_embed_pcm(voicedetect_ctx* ctx, const float* pcm, int n_samples,
+                               int sample_rate, float** out_vec, int* out_dim);
+/* ref :77 -- distance = 1 - cosine; verified = distance <= threshold */
+int voicedetect_capi_verify_paths(voicedetect_ctx* ctx, const char* a, const char* b,
+                                  float threshold, float* out_distance, int* out_verified);
+/* ref :88 -- the wav2vec2 analyze heads are outside this engine: always returns NULL
+ * with a last_error, as the reference does for a model without analyze heads
+ * (src/model.cpp:81-84). */
+char* voicedetect_capi_analyze_path_json(voicedetect_ctx* ctx, const char* wav_path);
+
+/* ---- additive entry points --------------------------------------------------- */
+
+/* Batched embed (the throughput path): n_clips mono f32 clips pcm[i] of
+ * n_samples[i] samples at sample_rate; writes n_clips * dim floats to the caller's
+ * `out` (row i = clip i, L2-normalised) and *out_dim = dim. */
+int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const float* const* pcm,
+                                     const int* n_samples, int n_clips, int sample_rate,
+                                     float* out, int* out_dim);
+
+/* Identify: cosine of each of n_q queries [n_q][dim] against n_reg registry rows
+ * [n_reg][dim]; writes the top-k registry indices (descending score, ties to the
+ * lower index) to out_idx [n_q][k] and their cosines to out_score [n_q][k].
+ * Host arrays. */
+int voicedetect_capi_identify(voicedetect_ctx* ctx, const float* queries, int n_q,
+                              const float* registry, int n_reg, int dim, int k, int* out_idx,
+                              float* out_score);
+
+/* Number of GPUs a context may use. This build drives one GPU per context (use
+ * one context per GPU, in a process or thread per GPU): n_gpus must be 1. */
+int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus);
+
+/* ---- B200-specific additive entry points --------------------------------------- */
+
+/* Device-resident batched embed: clip i is d_pcm + offsets[i] (16 kHz f32,
+ * n_samples[i] samples) in device memory; offsets / n_samples are host arrays;
+ * embeddings go to device memory d_out [n_clips][dim]. Asynchronous on `stream`
+ * (a cudaStream_t; NULL = the context's own stream). */
+int voicedetect_b200_embed_device(voicedetect_ctx* ctx, const float* d_pcm,
+                                  const long long* offsets, const int* n_samples, int n_clips,
+                                  float* d_out, void* stream);
+
+/* Bucketing policy: at most max_clips clips and max_frames padded FBank frames
+ * per batched pass (defaults 512 and 262144). */
+int voicedetect_b200_set_bucketing(voicedetect_ctx* ctx, int max_clips, long long max_frames);
+
+/* GPU kernels launched by the last embed call on ctx. */
+long long voicedetect_b200_last_launches(voicedetect_ctx* ctx);
+
+/* Embedding dimension of the loaded model (0 for NULL). */
+int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx);
+
+/* Synchronise the context's stream and report any kernel-side timeout. */
+int voicedetect_b200_sync(voicedetect_ctx* ctx);
+
+/* Conv-kernel profiling: while enabled, every tensor-core conv launch is bracketed
+ * by CUDA events on its own stream. profile_read synchronises and returns, since
+ * the previous read, the summed launch durations (ms), the algorithmic conv FLOPs
+ * over valid frames (2*OC*IC*k*k*F_out*valid frames), and the number of launches. */
+int voicedetect_b200_profile(voicedetect_ctx* ctx, int enable);
+int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_ms, double* conv_flops,
+                                  long long* conv_launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,93 @@
+"""Generate the committed golden fixtures in tests/golden/ (run where the
+reference checkout and torchaudio are available; the fixtures then travel with
+the repository).
+
+* fbank_torchaudio.npz -- three seeded synthetic clips (int16) and their
+  torchaudio.compliance.kaldi.fbank features with the reference's options
+  (povey window, preemph 0.97, dither 0, snip_edges, 80 mels) and per-utterance
+  CMN: the same golden source the reference's own parity suite uses
+  (scripts/gen_baseline.py:73-81 in the reference).
+* ref_conv_kat.npz -- outputs of the reference's OWN blocked conv kernels
+  (oracle/_ref/libvdref.so, src/directconv.cpp compiled unmodified) on the
+  shapes of the reference's tests/test_blocked.cpp:107-109,137-138,168-169, with
+  seeded U(-1, 1) inputs.
+* ref_resnet_tiny.npz -- pre-norm and L2 embeddings of a small seeded ResNet
+  (vd_synth.tiny_resnet_model) from the reference kernels + restated glue.
+
+Usage: python tests/golden/make_golden.py
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "voice-detect.cpp_b200"))
+
+import oracle  # noqa: E402
+import vd_synth  # noqa: E402
+
+CONV_KAT = [
+    # (W=time, H=freq, IC, OC, stride, bias_relu, k)
+    (20, 11, 32, 64, 1, False, 3),
+    (20, 11, 64, 128, 2, False, 3),
+    (7, 5, 16, 16, 1, False, 3),
+    (20, 11, 32, 64, 1, True, 3),
+    (20, 11, 64, 128, 2, True, 3),
+    (20, 11, 64, 128, 2, False, 1),
+    (15, 9, 32, 64, 2, False, 1),
+]
+
+
+def fbank_torchaudio(pcm: np.ndarray) -> np.ndarray:
+    import torch
+    import torchaudio
+    x = torch.from_numpy(pcm.astype(np.float64))[None]
+    f = torchaudio.compliance.kaldi.fbank(x, num_mel_bins=80, frame_length=25, frame_shift=10,
+                                          dither=0.0, window_type="povey", preemphasis_coefficient=0.97,
+                                          remove_dc_offset=True, snip_edges=True,
+                                          sample_frequency=16000, low_freq=20.0, high_freq=0.0,
+                                          energy_floor=0.0, use_energy=False)
+    f = f - f.mean(0, keepdim=True)
+    return f.numpy().T.astype(np.float32)  # [80, T]
+
+
+def conv_inputs(i: int, W, H, IC, OC, k):
+    rng = np.random.default_rng(1234 + i)
+    x = rng.uniform(-1, 1, (IC, H, W)).astype(np.float32)
+    w = rng.uniform(-1, 1, (OC, IC, k, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, OC).astype(np.float32)
+    return x, w, b
+
+
+def main() -> None:
+    clips = [vd_synth.make_clip(s, n) for s, n in ((11, 48000), (12, 16000 + 37), (13, 401))]
+    d = {}
+    for i, c in enumerate(clips):
+        d[f"clip{i}"] = c
+        d[f"fbank{i}"] = fbank_torchaudio(vd_synth.clip_f32(c))
+    np.savez_compressed(HERE / "fbank_torchaudio.npz", **d)
+
+    d = {}
+    for i, (W, H, IC, OC, s, br, k) in enumerate(CONV_KAT):
+        x, w, b = conv_inputs(i, W, H, IC, OC, k)
+        if k == 3:
+            y = oracle.ref_conv3x3(x, w, s, b if br else None, br)
+        else:
+            y = oracle.ref_conv1x1(x, w, s)
+        d[f"y{i}"] = y
+    np.savez_compressed(HERE / "ref_conv_kat.npz", **d)
+
+    m = vd_synth.tiny_resnet_model(5, n_mels=80)
+    pcm = vd_synth.clip_f32(vd_synth.make_clip(21, 24000))
+    feats = oracle.ref_fbank(pcm)
+    R = oracle.RefResNet34(m)
+    emb, pre = R.embed(feats)
+    np.savez_compressed(HERE / "ref_resnet_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
+    print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

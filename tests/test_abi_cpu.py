@@ -1,0 +1,78 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol that
+include/*.h declares, and the reference's NULL-safety / error conventions hold
+(src/voicedetect_capi.cpp:61-176; tests/test_smoke.cpp in the reference checks
+the version and ABI number)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+import vd_b200
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared_functions():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"//.*", "", text)
+        for m in re.finditer(r"\b((?:voicedetect|vdb)_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    L = C.CDLL(str(vd_b200.LIB_PATH))
+    names = _declared_functions()
+    assert len(names) >= 25
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_null_safety():
+    L = vd_b200.lib()
+    assert L.voicedetect_capi_abi_version() == 1
+    assert L.voicedetect_capi_last_error(None) == b""
+    L.voicedetect_capi_free(None)
+    L.voicedetect_capi_free_vec(None)
+    L.voicedetect_capi_free_string(None)
+    assert L.voicedetect_capi_load(None) is None
+    assert L.voicedetect_capi_load(b"/nonexistent/model.gguf") is None
+    # every model call on a NULL context reports an error, never crashes
+    p = C.POINTER(C.c_float)()
+    d = C.c_int(7)
+    assert L.voicedetect_capi_embed_path(None, b"x.wav", C.byref(p), C.byref(d)) == 1
+    assert not p and d.value == 0  # outputs reset before work
+    assert L.voicedetect_capi_verify_paths(None, b"a", b"b", 0.25, None, None) == 1
+    assert L.voicedetect_capi_analyze_path_json(None, b"a") is None
+    assert L.voicedetect_capi_set_devices(None, 1) == 1
+
+
+def test_load_rejects_corrupt_gguf(tmp_path):
+    import vd_synth
+    L = vd_b200.lib()
+    good = tmp_path / "m.gguf"
+    vd_synth.write_resnet_gguf(str(good), vd_synth.tiny_resnet_model(1, n_mels=16))
+    data = good.read_bytes()
+    bad_magic = tmp_path / "bad_magic.gguf"
+    bad_magic.write_bytes(b"XXXX" + data[4:])
+    truncated = tmp_path / "trunc.gguf"
+    truncated.write_bytes(data[: len(data) // 2])
+    empty = tmp_path / "empty.gguf"
+    empty.write_bytes(b"")
+    for p in (bad_magic, truncated, empty):
+        assert L.voicedetect_capi_load(str(p).encode()) is None
+
+
+def test_op_entry_points_reject_bad_arguments():
+    L = vd_b200.lib()
+    assert L.vdb_conv(None, None) != 0
+    assert b"NULL" in L.vdb_last_error()
+    a = vd_b200.ConvArgs(batch=1, t_out=4, f_out=4, oc=24, k0=3, stride0=1, ic0=32)
+    assert L.vdb_conv(C.byref(a), None) != 0  # oc not a multiple of 16
+    assert L.vdb_fbank_plan_create(16000, 80, 400, 400, 160, 0.97, 20.0, 0.0) is None
+    assert L.vdb_identify(None, 1, None, 1, 1, 1, None, None, None) != 0
+    assert L.vdb_grid_rows(2, 10, 8) == 2 * 12 * 10
+    assert L.vdb_phase_rows(2, 10, 8) == 4 * 2 * 7 * 6

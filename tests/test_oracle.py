@@ -1,0 +1,146 @@
+"""Pins the CPU oracle (oracle/vd_oracle.c) before anything is checked against it.
+
+* against the reference's own kernels compiled from its sources
+  (oracle/_ref/libvdref.so) on the shapes of the reference's model-free unit
+  test tests/test_blocked.cpp, and on FBank / full ResNet forwards;
+* against committed golden vectors (tests/golden/, made by make_golden.py):
+  torchaudio Kaldi FBank, and outputs of the reference kernels.
+Runs on CPU (no GPU needed).
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+import vd_synth
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+# reference gates: conv max|d| <= 1e-4 (tests/test_blocked.cpp:107), FBank
+# max|d| <= 1e-3 and cosine >= 0.9999 (tests/test_fbank.cpp:56-59)
+CONV_TOL = 1e-4
+FBANK_TOL = 1e-3
+
+
+def _cos(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    na, nb = np.linalg.norm(a), np.linalg.norm(b)
+    if na == 0.0 and nb == 0.0:  # e.g. a one-frame clip: CMN zeroes everything
+        return 1.0
+    return float(a @ b / (na * nb))
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not oracle.ref_available():
+        pytest.skip("reference kernels library not built")
+    return oracle
+
+
+def test_fbank_matches_torchaudio_golden():
+    g = np.load(GOLD / "fbank_torchaudio.npz")
+    for i in range(3):
+        pcm = vd_synth.clip_f32(g[f"clip{i}"])
+        want = g[f"fbank{i}"]
+        got = oracle.fbank(pcm)
+        assert got.shape == want.shape
+        assert np.abs(got - want).max() <= FBANK_TOL
+        assert _cos(got, want) >= 0.9999
+
+
+def test_fbank_matches_reference_kernel(ref):
+    for seed, n in ((1, 48000), (2, 16123), (3, 400), (4, 559)):
+        pcm = vd_synth.clip_f32(vd_synth.make_clip(seed, n))
+        a, b = oracle.fbank(pcm), ref.ref_fbank(pcm)
+        assert a.shape == b.shape
+        assert np.array_equal(a, b), np.abs(a - b).max()
+
+
+def test_fbank_no_frames():
+    pcm = np.zeros(399, np.float32)
+    assert oracle.fbank(pcm).shape == (80, 0)
+
+
+def test_conv_kat_golden():
+    """C restatement vs the reference kernels' outputs on test_blocked shapes."""
+    import importlib.util
+    g = np.load(GOLD / "ref_conv_kat.npz")
+    spec = importlib.util.spec_from_file_location("make_golden", GOLD / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    for i, (W, H, IC, OC, s, br, k) in enumerate(mg.CONV_KAT):
+        x, w, b = mg.conv_inputs(i, W, H, IC, OC, k)
+        y = oracle.conv2d(x, w, s, b if br else None, br)
+        want = g[f"y{i}"]
+        assert y.shape == want.shape
+        assert np.abs(y - want).max() <= CONV_TOL
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+def test_conv_matches_reference_kernel(ref, stride):
+    rng = np.random.default_rng(9)
+    for (W, H, IC, OC) in ((37, 13, 32, 32), (26, 10, 64, 64), (9, 7, 128, 256)):
+        x = rng.uniform(-1, 1, (IC, H, W)).astype(np.float32)
+        w = rng.uniform(-1, 1, (OC, IC, 3, 3)).astype(np.float32)
+        b = rng.uniform(-1, 1, OC).astype(np.float32)
+        assert np.array_equal(oracle.conv2d(x, w, stride, b, True),
+                              ref.ref_conv3x3(x, w, stride, b, True))
+        w1 = rng.uniform(-1, 1, (OC, IC, 1, 1)).astype(np.float32)
+        assert np.array_equal(oracle.conv2d(x, w1, stride, b), ref.ref_conv1x1(x, w1, stride, b))
+        if stride == 1:
+            wi = ref.ref_winograd3x3(x, w)
+            assert np.abs(wi - oracle.conv2d(x, w, 1)).max() <= CONV_TOL * max(1, np.abs(wi).max())
+
+
+def test_resnet_tiny_golden():
+    g = np.load(GOLD / "ref_resnet_tiny.npz")
+    m = vd_synth.tiny_resnet_model(5, n_mels=80)
+    feats = oracle.fbank(g["pcm"])
+    emb, pre = oracle.resnet34_embed(m, feats)
+    assert np.abs(pre - g["prenorm"]).max() <= 1e-3 * max(1.0, np.abs(g["prenorm"]).max())
+    assert _cos(emb, g["emb"]) >= 0.999999
+
+
+def test_resnet34_matches_reference_kernels(ref):
+    m = vd_synth.resnet34_model(3)
+    pcm = vd_synth.clip_f32(vd_synth.make_clip(77, 16000 + 160 * 13))
+    feats = oracle.fbank(pcm)
+    e0, p0 = oracle.resnet34_embed(m, feats)
+    e1, p1 = ref.RefResNet34(m).embed(feats)
+    assert np.array_equal(p0, p1)
+    assert np.array_equal(e0, e1)
+
+
+def test_q8_0_roundtrip_matches_gguf_dequant(tmp_path):
+    """The q8_0 model the oracle sees equals what a q8_0 GGUF carries."""
+    gguf = pytest.importorskip("gguf")
+    m = vd_synth.tiny_resnet_model(2, n_mels=16)
+    q = vd_synth.quantize_q8_0_model(m)
+    path = tmp_path / "q.gguf"
+    vd_synth.write_resnet_gguf(str(path), m, "q8_0")
+    r = gguf.GGUFReader(str(path))
+    t = {x.name: x for x in r.tensors}
+    w = t["blk1.conv1.weight"]
+    assert w.tensor_type == gguf.GGMLQuantizationType.Q8_0
+    deq = gguf.quants.dequantize(w.data, gguf.GGMLQuantizationType.Q8_0)
+    oc, ic = q["blocks"][1]["conv1_w"].shape[:2]
+    ohwi = deq.reshape(oc, 3, 3, ic)
+    assert np.array_equal(ohwi.transpose(0, 3, 1, 2), q["blocks"][1]["conv1_w"])
+
+
+def test_identify_oracle_ties():
+    reg = np.eye(4, dtype=np.float32)
+    reg = np.concatenate([reg, reg[:1]])  # row 4 duplicates row 0
+    q = np.array([[1, 0, 0, 0]], np.float32)
+    idx, sc = oracle.identify(q, reg, k=3)
+    assert idx[0, 0] == 0 and idx[0, 1] == 4
+    assert sc[0, 0] == pytest.approx(1.0) and sc[0, 1] == pytest.approx(1.0)
+
+
+def test_resample_linear():
+    x = np.arange(10, dtype=np.float32)
+    y = oracle.resample_linear(x, 8000, 16000)
+    assert len(y) == 20
+    assert y[0] == 0 and y[1] == pytest.approx(0.5) and y[-1] == 9

@@ -1,0 +1,379 @@
+// The flat C ABI (include/voicedetect_capi.h): same contract as the reference's
+// src/voicedetect_capi.cpp:61-176 -- int status, per-context last_error, malloc'd
+// outputs, outputs reset before work, nothing thrown across the boundary -- on
+// top of the B200 Engine.
+#include "voicedetect_capi.h"
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "engine.hpp"
+
+#define VOICEDETECT_CAPI_ABI_VERSION 1
+
+struct voicedetect_ctx {
+    std::unique_ptr<vdb::Engine> engine;
+    std::string last_error;
+    std::mutex mu;
+};
+
+namespace {
+
+float* dup_vec(const std::vector<float>& v) {
+    if (v.empty()) return nullptr;
+    float* buf = static_cast<float*>(std::malloc(v.size() * sizeof(float)));
+    if (!buf) return nullptr;
+    std::memcpy(buf, v.data(), v.size() * sizeof(float));
+    return buf;
+}
+
+int emit_embedding(voicedetect_ctx* ctx, const std::vector<float>& emb, float** out_vec,
+                   int* out_dim) {
+    float* buf = dup_vec(emb);
+    if (!buf) {
+        ctx->last_error = "out of memory";
+        return 1;
+    }
+    if (out_vec) *out_vec = buf;
+    else std::free(buf);
+    if (out_dim) *out_dim = (int)emb.size();
+    ctx->last_error.clear();
+    return 0;
+}
+
+// Embeds 16 kHz PCM through the engine; throws std::runtime_error on failure.
+std::vector<float> embed_16k(voicedetect_ctx* ctx, const std::vector<float>& pcm16k) {
+    std::string err;
+    const int D = ctx->engine->emb_dim();
+    std::vector<float> out((size_t)D);
+    const float* p = pcm16k.data();
+    const int n = (int)pcm16k.size();
+    if (ctx->engine->embed_host(&p, &n, 1, out.data(), err)) throw std::runtime_error(err);
+    return out;
+}
+
+std::vector<float> embed_path(voicedetect_ctx* ctx, const char* path) {
+    std::vector<float> mono;
+    int sr = 0;
+    std::string err;
+    if (!vdb::read_wav_mono(path, mono, sr, err)) throw std::runtime_error(err);
+    return embed_16k(ctx, vdb::resample_linear(mono, sr, 16000));
+}
+
+}  // namespace
+
+extern "C" int voicedetect_capi_abi_version(void) { return VOICEDETECT_CAPI_ABI_VERSION; }
+
+extern "C" voicedetect_ctx* voicedetect_capi_load(const char* gguf_path) {
+    if (!gguf_path) return nullptr;
+    try {
+        std::string err;
+        std::unique_ptr<vdb::Engine> e = vdb::Engine::load(gguf_path, err);
+        if (!e) {
+            std::fprintf(stderr, "[voicedetect] load failed: %s\n", err.c_str());
+            return nullptr;
+        }
+        auto* ctx = new (std::nothrow) voicedetect_ctx();
+        if (!ctx) return nullptr;
+        ctx->engine = std::move(e);
+        return ctx;
+    } catch (...) {
+        return nullptr;
+    }
+}
+
+extern "C" void voicedetect_capi_free(voicedetect_ctx* ctx) {
+    try {
+        delete ctx;
+    } catch (...) {
+    }
+}
+
+extern "C" const char* voicedetect_capi_last_error(voicedetect_ctx* ctx) {
+    if (!ctx) return "";
+    return ctx->last_error.c_str();
+}
+
+extern "C" void voicedetect_capi_free_string(char* s) { std::free(s); }
+
+extern "C" void voicedetect_capi_free_vec(float* v) { std::free(v); }
+
+extern "C" int voicedetect_capi_embed_path(voicedetect_ctx* ctx, const char* wav_path,
+                                           float** out_vec, int* out_dim) {
+    if (out_vec) *out_vec = nullptr;
+    if (out_dim) *out_dim = 0;
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!wav_path) { ctx->last_error = "wav_path is NULL"; return 1; }
+    try {
+        return emit_embedding(ctx, embed_path(ctx, wav_path), out_vec, out_dim);
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    } catch (...) {
+        ctx->last_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" int voicedetect_capi_embed_pcm(voicedetect_ctx* ctx, const float* pcm, int n_samples,
+                                          int sample_rate, float** out_vec, int* out_dim) {
+    if (out_vec) *out_vec = nullptr;
+    if (out_dim) *out_dim = 0;
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!pcm || n_samples < 0) { ctx->last_error = "invalid pcm buffer"; return 1; }
+    try {
+        std::vector<float> samples(pcm, pcm + n_samples);
+        if (sample_rate != 16000) samples = vdb::resample_linear(samples, sample_rate, 16000);
+        return emit_embedding(ctx, embed_16k(ctx, samples), out_vec, out_dim);
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    } catch (...) {
+        ctx->last_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" int voicedetect_capi_verify_paths(voicedetect_ctx* ctx, const char* a, const char* b,
+                                             float threshold, float* out_distance,
+                                             int* out_verified) {
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!a || !b) { ctx->last_error = "clip path is NULL"; return 1; }
+    try {
+        const std::vector<float> ea = embed_path(ctx, a);
+        const std::vector<float> eb = embed_path(ctx, b);
+        if (ea.size() != eb.size() || ea.empty())
+            throw std::runtime_error("voicedetect: embedding dimension mismatch in verify");
+        // src/model.cpp:65-78: f64 dot of the L2-normalised embeddings.
+        double dot = 0.0;
+        for (size_t i = 0; i < ea.size(); ++i) dot += (double)ea[i] * (double)eb[i];
+        const float distance = 1.0f - (float)dot;
+        if (out_distance) *out_distance = distance;
+        if (out_verified) *out_verified = distance <= threshold ? 1 : 0;
+        ctx->last_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    } catch (...) {
+        ctx->last_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" char* voicedetect_capi_analyze_path_json(voicedetect_ctx* ctx, const char* wav_path) {
+    if (!ctx) return nullptr;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return nullptr; }
+    if (!wav_path) { ctx->last_error = "wav_path is NULL"; return nullptr; }
+    ctx->last_error = "voicedetect: this model has no age/gender/emotion analyze heads";
+    return nullptr;
+}
+
+extern "C" int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const float* const* pcm,
+                                                const int* n_samples, int n_clips,
+                                                int sample_rate, float* out, int* out_dim) {
+    if (out_dim) *out_dim = 0;
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!pcm || !n_samples || !out || n_clips <= 0) {
+        ctx->last_error = "invalid batch arguments";
+        return 1;
+    }
+    try {
+        std::string err;
+        std::vector<std::vector<float>> res;
+        std::vector<const float*> ptrs((size_t)n_clips);
+        std::vector<int> ns((size_t)n_clips);
+        for (int i = 0; i < n_clips; ++i) {
+            if (!pcm[i] || n_samples[i] < 0) {
+                ctx->last_error = "invalid pcm buffer (clip " + std::to_string(i) + ")";
+                return 1;
+            }
+            if (sample_rate != 16000) {
+                res.emplace_back(vdb::resample_linear(
+                    std::vector<float>(pcm[i], pcm[i] + n_samples[i]), sample_rate, 16000));
+                ptrs[i] = res.back().data();
+                ns[i] = (int)res.back().size();
+            } else {
+                ptrs[i] = pcm[i];
+                ns[i] = n_samples[i];
+            }
+        }
+        if (ctx->engine->embed_host(ptrs.data(), ns.data(), n_clips, out, err)) {
+            ctx->last_error = err;
+            return 1;
+        }
+        if (out_dim) *out_dim = ctx->engine->emb_dim();
+        ctx->last_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    } catch (...) {
+        ctx->last_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" int voicedetect_capi_identify(voicedetect_ctx* ctx, const float* queries, int n_q,
+                                         const float* registry, int n_reg, int dim, int k,
+                                         int* out_idx, float* out_score) {
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!queries || !registry || !out_idx || !out_score || n_q <= 0 || n_reg <= 0 || dim <= 0 ||
+        k <= 0) {
+        ctx->last_error = "invalid identify arguments";
+        return 1;
+    }
+    cudaSetDevice(ctx->engine->device());
+    cudaStream_t st = ctx->engine->stream();
+    float *dq = nullptr, *dr = nullptr, *ds = nullptr;
+    int* di = nullptr;
+    const size_t qb = sizeof(float) * (size_t)n_q * dim, rb = sizeof(float) * (size_t)n_reg * dim;
+    const size_t ob = (size_t)n_q * k;
+    int rc = 1;
+    if (cudaMalloc(&dq, qb) == cudaSuccess && cudaMalloc(&dr, rb) == cudaSuccess &&
+        cudaMalloc(&ds, ob * sizeof(float)) == cudaSuccess &&
+        cudaMalloc(&di, ob * sizeof(int)) == cudaSuccess &&
+        cudaMemcpyAsync(dq, queries, qb, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+        cudaMemcpyAsync(dr, registry, rb, cudaMemcpyHostToDevice, st) == cudaSuccess) {
+        if (vdb_identify(dq, n_q, dr, n_reg, dim, k, di, ds, st) != 0) {
+            ctx->last_error = vdb_last_error();
+        } else if (cudaMemcpyAsync(out_idx, di, ob * sizeof(int), cudaMemcpyDeviceToHost, st) ==
+                       cudaSuccess &&
+                   cudaMemcpyAsync(out_score, ds, ob * sizeof(float), cudaMemcpyDeviceToHost,
+                                   st) == cudaSuccess &&
+                   cudaStreamSynchronize(st) == cudaSuccess) {
+            rc = 0;
+            ctx->last_error.clear();
+        } else {
+            ctx->last_error = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+        }
+    } else {
+        ctx->last_error = "device out of memory (identify)";
+    }
+    cudaStreamSynchronize(st);
+    cudaFree(dq);
+    cudaFree(dr);
+    cudaFree(ds);
+    cudaFree(di);
+    return rc;
+}
+
+extern "C" int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus) {
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (n_gpus != 1) {
+        ctx->last_error = "this build drives one GPU per context; create one context per GPU";
+        return 1;
+    }
+    ctx->last_error.clear();
+    return 0;
+}
+
+extern "C" int voicedetect_b200_embed_device(voicedetect_ctx* ctx, const float* d_pcm,
+                                             const long long* offsets, const int* n_samples,
+                                             int n_clips, float* d_out, void* stream) {
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!d_pcm || !offsets || !n_samples || !d_out || n_clips <= 0) {
+        ctx->last_error = "invalid batch arguments";
+        return 1;
+    }
+    try {
+        std::string err;
+        if (ctx->engine->embed_device(d_pcm, offsets, n_samples, n_clips, d_out,
+                                      static_cast<cudaStream_t>(stream), err)) {
+            ctx->last_error = err;
+            return 1;
+        }
+        ctx->last_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    } catch (...) {
+        ctx->last_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" int voicedetect_b200_set_bucketing(voicedetect_ctx* ctx, int max_clips,
+                                              long long max_frames) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (max_clips <= 0 || max_frames <= 0) {
+        ctx->last_error = "bucketing limits must be positive";
+        return 1;
+    }
+    ctx->engine->max_clips = max_clips;
+    ctx->engine->max_frames = max_frames;
+    return 0;
+}
+
+extern "C" long long voicedetect_b200_last_launches(voicedetect_ctx* ctx) {
+    return (ctx && ctx->engine) ? ctx->engine->last_launches : 0;
+}
+
+extern "C" int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx) {
+    return (ctx && ctx->engine) ? ctx->engine->emb_dim() : 0;
+}
+
+extern "C" int voicedetect_b200_profile(voicedetect_ctx* ctx, int enable) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->engine->set_profiling(enable != 0);
+    return 0;
+}
+
+extern "C" int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_ms,
+                                             double* conv_flops, long long* conv_launches) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    double ms = 0, fl = 0;
+    long long n = 0;
+    std::string err;
+    cudaSetDevice(ctx->engine->device());
+    if (ctx->engine->read_profile(ms, fl, n, err)) {
+        ctx->last_error = err;
+        return 1;
+    }
+    if (conv_ms) *conv_ms = ms;
+    if (conv_flops) *conv_flops = fl;
+    if (conv_launches) *conv_launches = n;
+    return 0;
+}
+
+extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    std::string err;
+    if (cudaSetDevice(ctx->engine->device()) != cudaSuccess ||
+        cudaStreamSynchronize(ctx->engine->stream()) != cudaSuccess) {
+        ctx->last_error = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+        return 1;
+    }
+    if (ctx->engine->check_device_error(err)) {
+        ctx->last_error = err;
+        return 1;
+    }
+    return 0;
+}

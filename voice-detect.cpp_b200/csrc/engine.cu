@@ -1,0 +1,736 @@
+// Engine implementation: GGUF -> device weights, bucketing, and the per-bucket
+// launch sequence. See engine.hpp for the overview.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+
+#include "gguf.hpp"
+#include "vdb_internal.h"
+
+namespace vdb {
+namespace {
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restrict__ out,
+                                  long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2half_rn(in[i]);
+}
+
+struct Loader {
+    const Gguf& g;
+    std::string& err;
+
+    // Conv weight as torch-order f32 [OC][IC][K][K]. f32/f16 tensors use the
+    // reference's ggml layout ne = [KW, KH, IC, OC] (src/encoder_resnet.cpp:16-20);
+    // q8_0 conv tensors (a new format: the reference never quantises 4-D weights)
+    // are stored OHWI, ne = [IC, KW, KH, OC], so the 32-element blocks run along IC.
+    bool conv(const std::string& name, std::vector<float>& w, int& oc, int& ic, int& k) {
+        const GgufTensor* t = g.tensor(name);
+        if (!t) {
+            err = "missing tensor '" + name + "'";
+            return false;
+        }
+        std::vector<float> raw;
+        if (!g.to_f32(*t, raw, err)) return false;
+        std::vector<int64_t> ne = t->ne;
+        while (ne.size() < 4) ne.push_back(1);
+        if (t->type == GGML_Q8_0) {
+            ic = (int)ne[0];
+            k = (int)ne[1];
+            oc = (int)ne[3];
+            if (ne[2] != ne[1]) {
+                err = "tensor '" + name + "': q8_0 conv weight must be [IC, K, K, OC]";
+                return false;
+            }
+            w.assign((size_t)oc * ic * k * k, 0.0f);
+            for (int o = 0; o < oc; ++o)
+                for (int kh = 0; kh < k; ++kh)
+                    for (int kw = 0; kw < k; ++kw)
+                        for (int i = 0; i < ic; ++i)
+                            w[(((size_t)o * ic + i) * k + kh) * k + kw] =
+                                raw[(((size_t)o * k + kh) * k + kw) * ic + i];
+        } else {
+            k = (int)ne[0];
+            ic = (int)ne[2];
+            oc = (int)ne[3];
+            if (ne[1] != ne[0]) {
+                err = "tensor '" + name + "': conv weight must be square [K, K, IC, OC]";
+                return false;
+            }
+            w = std::move(raw);
+        }
+        return true;
+    }
+
+    bool vec(const std::string& name, std::vector<float>& v, int expect) {
+        const GgufTensor* t = g.tensor(name);
+        if (!t) {
+            err = "missing tensor '" + name + "'";
+            return false;
+        }
+        if (!g.to_f32(*t, v, err)) return false;
+        if (expect >= 0 && (int)v.size() != expect) {
+            err = "tensor '" + name + "' has " + std::to_string(v.size()) + " elements, expected " +
+                  std::to_string(expect);
+            return false;
+        }
+        return true;
+    }
+};
+
+// torch [OC][IC][K][K] -> [OC][kt*K + kf][IC] with kt = kw (time), kf = kh (freq).
+std::vector<float> pack_taps(const std::vector<float>& w, int oc, int ic, int k) {
+    std::vector<float> out((size_t)oc * k * k * ic);
+    for (int o = 0; o < oc; ++o)
+        for (int kh = 0; kh < k; ++kh)
+            for (int kw = 0; kw < k; ++kw)
+                for (int i = 0; i < ic; ++i)
+                    out[((size_t)o * k * k + (size_t)kw * k + kh) * ic + i] =
+                        w[(((size_t)o * ic + i) * k + kh) * k + kw];
+    return out;
+}
+
+inline int frames_of(int n, int win, int hop) { return n >= win ? 1 + (n - win) / hop : 0; }
+inline int half_extent(int n) { return (n - 1) / 2 + 1; }
+
+}  // namespace
+
+Engine::~Engine() {
+    if (device_ >= 0) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    free_workspace();
+    for (void* p : weight_allocs_) cudaFree(p);
+    if (plan_) vdb_fbank_plan_destroy(plan_);
+    if (errword_) cudaFree(errword_);
+    for (cudaEvent_t& ev : stage_ev_)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : prof_ev_) cudaEventDestroy(ev);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::free_workspace() {
+    for (Level& L : levels_) {
+        for (void*& p : L.g) {
+            cudaFree(p);
+            p = nullptr;
+        }
+        cudaFree(L.p);
+        L.p = nullptr;
+        L.g_bytes = L.p_bytes = 0;
+    }
+    cudaFree(feats_);
+    feats_ = nullptr;
+    feats_bytes_ = 0;
+    cudaFree(mean_);
+    mean_ = nullptr;
+    mean_bytes_ = 0;
+    cudaFree(meta_);
+    meta_ = nullptr;
+    cudaFree(offs_);
+    offs_ = nullptr;
+    cudaFree(nsamp_);
+    nsamp_ = nullptr;
+    meta_cap_ = 0;
+    cudaFreeHost(h_stage_);
+    h_stage_ = nullptr;
+    h_stage_bytes_ = 0;
+    cudaFreeHost(h_pcm_);
+    h_pcm_ = nullptr;
+    h_pcm_bytes_ = 0;
+    cudaFree(d_pcm_);
+    d_pcm_ = nullptr;
+    d_pcm_bytes_ = 0;
+    cudaFreeHost(h_out_);
+    h_out_ = nullptr;
+    cudaFree(d_out_);
+    d_out_ = nullptr;
+    out_bytes_ = 0;
+}
+
+std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) {
+    Gguf g;
+    if (!g.load(path, err)) return nullptr;
+    std::unique_ptr<Engine> e(new Engine());
+    EngineConfig& c = e->cfg_;
+    // KV schema of src/model_loader.cpp:120-136 (same keys and defaults).
+    c.arch = g.str("voicedetect.arch");
+    c.emb_dim = (int)g.u32("voicedetect.embedding_dim");
+    c.l2 = g.boolean("voicedetect.l2_normalize", true);
+    c.sample_rate = (int)g.u32("voicedetect.fbank.sample_rate", 16000);
+    c.n_mels = (int)g.u32("voicedetect.fbank.n_mels", 80);
+    c.n_fft = (int)g.u32("voicedetect.fbank.n_fft", 512);
+    c.win = (int)g.u32("voicedetect.fbank.win_length", 400);
+    c.hop = (int)g.u32("voicedetect.fbank.hop_length", 160);
+    c.preemph = g.f32("voicedetect.fbank.preemph", 0.97f);
+    c.low_freq = g.f32("voicedetect.fbank.low_freq", 20.0f);
+    c.high_freq = g.f32("voicedetect.fbank.high_freq", 0.0f);
+    c.cmn = g.boolean("voicedetect.fbank.cmn", true);
+    if (c.emb_dim <= 0) {  // the reference's load() fails the same way (:213-214)
+        err = "GGUF has no voicedetect.embedding_dim";
+        return nullptr;
+    }
+    if (cudaGetDevice(&e->device_) != cudaSuccess) {
+        err = "no CUDA device";
+        return nullptr;
+    }
+    if (cudaStreamCreateWithFlags(&e->stream_, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->stage_ev_[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->stage_ev_[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&e->errword_, sizeof(int)) != cudaSuccess ||
+        cudaMemset(e->errword_, 0, sizeof(int)) != cudaSuccess) {
+        err = "CUDA stream/alloc failed";
+        return nullptr;
+    }
+    if (c.arch != "wespeaker_resnet34") return e;  // load succeeds; embed reports the arch
+
+    e->plan_ = vdb_fbank_plan_create(c.sample_rate, c.n_mels, c.n_fft, c.win, c.hop, c.preemph,
+                                     c.low_freq, c.high_freq);
+    if (!e->plan_) {
+        err = vdb_last_error();
+        return nullptr;
+    }
+    Loader L{g, err};
+    auto upload = [&](const std::vector<float>& v, float** dst) -> bool {
+        void* p = nullptr;
+        if (cudaMalloc(&p, v.size() * sizeof(float)) != cudaSuccess ||
+            cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) !=
+                cudaSuccess) {
+            err = "weight upload failed";
+            return false;
+        }
+        e->weight_allocs_.push_back(p);
+        *dst = static_cast<float*>(p);
+        return true;
+    };
+    auto upload_h = [&](const std::vector<float>& v, __half** dst) -> bool {
+        float* tmp = nullptr;
+        if (cudaMalloc(&tmp, v.size() * sizeof(float)) != cudaSuccess) {
+            err = "weight upload failed";
+            return false;
+        }
+        void* p = nullptr;
+        bool ok = cudaMalloc(&p, v.size() * sizeof(__half)) == cudaSuccess &&
+                  cudaMemcpy(tmp, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) ==
+                      cudaSuccess;
+        if (ok) {
+            const long long n = (long long)v.size();
+            f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(tmp, (__half*)p, n);
+            ok = cudaDeviceSynchronize() == cudaSuccess;
+        }
+        cudaFree(tmp);
+        if (!ok) {
+            err = "weight conversion failed";
+            if (p) cudaFree(p);
+            return false;
+        }
+        e->weight_allocs_.push_back(p);
+        *dst = static_cast<__half*>(p);
+        return true;
+    };
+
+    // ResNet manifest, src/model_loader.cpp:138-152.
+    const std::string pre = "voicedetect.resnet.";
+    const auto c1w = g.str_arr(pre + "conv1_weight"), c1b = g.str_arr(pre + "conv1_bias");
+    const auto c2w = g.str_arr(pre + "conv2_weight"), c2b = g.str_arr(pre + "conv2_bias");
+    const auto dw = g.str_arr(pre + "down_weight"), db = g.str_arr(pre + "down_bias");
+    const auto strides = g.i32_arr(pre + "stride");
+    const size_t nb = c1w.size();
+    if (nb == 0 || c1b.size() != nb || c2w.size() != nb || c2b.size() != nb ||
+        dw.size() != nb || db.size() != nb || strides.size() != nb) {
+        err = "inconsistent voicedetect.resnet.* block manifest";
+        return nullptr;
+    }
+    // stem
+    {
+        std::vector<float> w, b;
+        int oc, ic, k;
+        if (!L.conv(g.str(pre + "stem_weight"), w, oc, ic, k)) return nullptr;
+        if (ic != 1 || k != 3 || !(oc == 16 || oc == 32 || oc == 64)) {
+            err = "stem must be a 3x3 conv from 1 channel to 16/32/64";
+            return nullptr;
+        }
+        if (!L.vec(g.str(pre + "stem_bias"), b, oc)) return nullptr;
+        std::vector<float> sw((size_t)oc * 9);
+        for (int o = 0; o < oc; ++o)
+            for (int kh = 0; kh < 3; ++kh)
+                for (int kw = 0; kw < 3; ++kw) sw[(size_t)o * 9 + kw * 3 + kh] = w[(size_t)o * 9 + kh * 3 + kw];
+        e->stem_oc_ = oc;
+        if (!upload(sw, &e->stem_w_) || !upload(b, &e->stem_b_)) return nullptr;
+    }
+    int cin = e->stem_oc_;
+    int F = c.n_mels;
+    for (size_t i = 0; i < nb; ++i) {
+        ResBlockDev blk;
+        blk.stride = strides[i];
+        if (blk.stride != 1 && blk.stride != 2) {
+            err = "block stride must be 1 or 2";
+            return nullptr;
+        }
+        std::vector<float> w1, w2, b1, b2;
+        int oc, ic, k, oc2, ic2, k2;
+        if (!L.conv(c1w[i], w1, oc, ic, k) || !L.conv(c2w[i], w2, oc2, ic2, k2)) return nullptr;
+        if (k != 3 || k2 != 3 || ic != cin || ic2 != oc || oc2 != oc) {
+            err = "block " + std::to_string(i) + ": unexpected conv shapes";
+            return nullptr;
+        }
+        if (!L.vec(c1b[i], b1, oc) || !L.vec(c2b[i], b2, oc)) return nullptr;
+        blk.ic = ic;
+        blk.oc = oc;
+        if (!dw[i].empty()) {
+            std::vector<float> wd, bd;
+            int ocd, icd, kd;
+            if (!L.conv(dw[i], wd, ocd, icd, kd) || !L.vec(db[i], bd, oc)) return nullptr;
+            if (kd != 1 || ocd != oc || icd != ic) {
+                err = "block " + std::to_string(i) + ": bad downsample shape";
+                return nullptr;
+            }
+            for (int o = 0; o < oc; ++o) b2[o] += bd[o];  // both biases land in one epilogue
+            if (!upload_h(wd, &blk.wd)) return nullptr;
+        } else if (ic != oc || blk.stride != 1) {
+            err = "block " + std::to_string(i) + ": identity shortcut needs equal shapes";
+            return nullptr;
+        }
+        if (ic % 16 != 0 || oc % 16 != 0) {
+            err = "block channels must be multiples of 16";
+            return nullptr;
+        }
+        if (!upload_h(pack_taps(w1, oc, ic, 3), &blk.w1) || !upload(b1, &blk.b1) ||
+            !upload_h(pack_taps(w2, oc, oc, 3), &blk.w2) || !upload(b2, &blk.b2))
+            return nullptr;
+        e->blocks_.push_back(blk);
+        if (blk.stride == 2) F = half_extent(F);
+        cin = oc;
+    }
+    for (size_t i = 0; i < nb; ++i)
+        if (e->blocks_[i].stride == 2 && i == 0) {
+            err = "the first block may not be strided";
+            return nullptr;
+        }
+    // embedding head
+    {
+        std::vector<float> sw, sb, mv;
+        const GgufTensor* t = g.tensor(g.str(pre + "seg_weight"));
+        if (!t || t->ne.size() < 2) {
+            err = "missing or malformed seg_weight";
+            return nullptr;
+        }
+        const int P = (int)t->ne[0], D = (int)t->ne[1];
+        if (D != c.emb_dim || P != 2 * cin * F) {
+            err = "seg_weight shape does not match the backbone (" + std::to_string(P) + " vs " +
+                  std::to_string(2 * cin * F) + ")";
+            return nullptr;
+        }
+        if (!g.to_f32(*t, sw, err)) return nullptr;
+        if (!L.vec(g.str(pre + "seg_bias"), sb, D)) return nullptr;
+        e->pooled_ = P;
+        if (!upload(sw, &e->seg_w_) || !upload(sb, &e->seg_b_)) return nullptr;
+        const std::string mvn = g.str(pre + "mean_vec");
+        if (!mvn.empty()) {
+            if (!L.vec(mvn, mv, D) || !upload(mv, &e->mean_vec_)) return nullptr;
+        }
+        e->var_eps_ = g.f32(pre + "var_eps", 1e-8f);
+    }
+    // workspace levels: channels of the activation kept at each resolution level
+    e->levels_.clear();
+    e->levels_.push_back(Level{});
+    e->levels_[0].c = e->stem_oc_;
+    for (const ResBlockDev& b : e->blocks_) {
+        if (b.stride == 2) e->levels_.push_back(Level{});
+        e->levels_.back().c = std::max(e->levels_.back().c, b.oc);
+    }
+    return e;
+}
+
+bool Engine::supported(std::string& err) const {
+    if (cfg_.arch != "wespeaker_resnet34") {
+        err = "voicedetect: arch '" + cfg_.arch + "' is not implemented by the B200 engine";
+        return false;
+    }
+    return true;
+}
+
+int Engine::ensure_workspace(int B, int t_max, std::string& err) {
+    auto grow = [&](void** p, size_t& have, size_t need) -> bool {
+        if (need <= have) return true;
+        cudaDeviceSynchronize();  // the old buffer may still be read by queued work
+        cudaFree(*p);
+        *p = nullptr;
+        have = 0;
+        if (cudaMalloc(p, need) != cudaSuccess) {
+            err = "device out of memory (workspace)";
+            return false;
+        }
+        have = need;
+        return true;
+    };
+    int T = t_max, F = cfg_.n_mels;
+    for (size_t li = 0; li < levels_.size(); ++li) {
+        Level& L = levels_[li];
+        const size_t g = (size_t)vdb_grid_rows(B, T, F) * L.c * sizeof(__half);
+        size_t have = L.g_bytes;
+        for (int k = 0; k < 3; ++k) {
+            size_t h = have;
+            if (!grow(&L.g[k], h, g)) return 1;
+        }
+        L.g_bytes = std::max(L.g_bytes, g);
+        if (li + 1 < levels_.size()) {
+            const size_t pb = (size_t)vdb_phase_rows(B, T, F) * L.c * sizeof(__half);
+            if (!grow(&L.p, L.p_bytes, pb)) return 1;
+        }
+        T = half_extent(T);
+        F = half_extent(F);
+    }
+    if (!grow((void**)&feats_, feats_bytes_, (size_t)B * t_max * cfg_.n_mels * sizeof(float)))
+        return 1;
+    if (!grow((void**)&mean_, mean_bytes_, (size_t)B * cfg_.n_mels * sizeof(float))) return 1;
+    if (B > meta_cap_) {
+        cudaDeviceSynchronize();
+        stage_used_[0] = stage_used_[1] = false;
+        cudaFree(meta_);
+        cudaFree(offs_);
+        cudaFree(nsamp_);
+        cudaFreeHost(h_stage_);
+        meta_ = nullptr;
+        offs_ = nullptr;
+        nsamp_ = nullptr;
+        h_stage_ = nullptr;
+        const int cap = std::max(B, 64);
+        const size_t nlev = levels_.size();
+        // two staging slots so the host can fill bucket k+1 while bucket k copies
+        h_stage_bytes_ = (size_t)cap * (sizeof(long long) + sizeof(int) * (nlev + 3)) + 64;
+        if (cudaMalloc(&meta_, sizeof(int) * cap * (nlev + 2)) != cudaSuccess ||
+            cudaMalloc(&offs_, sizeof(long long) * cap) != cudaSuccess ||
+            cudaMalloc(&nsamp_, sizeof(int) * cap) != cudaSuccess ||
+            cudaMallocHost(&h_stage_, 2 * h_stage_bytes_) != cudaSuccess) {
+            err = "device out of memory (metadata)";
+            return 1;
+        }
+        meta_cap_ = cap;
+    }
+    return 0;
+}
+
+// One bucket of B clips: h_off/h_ns are device-pointer offsets and sample counts,
+// h_outrow the output row of each clip.
+int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_ns,
+                       const int* h_outrow, int B, cudaStream_t st, float* d_out,
+                       std::string& err) {
+    const size_t nlev = levels_.size();
+    int t_max = 0;
+    for (int b = 0; b < B; ++b) t_max = std::max(t_max, frames_of(h_ns[b], cfg_.win, cfg_.hop));
+    if (ensure_workspace(B, t_max, err)) return 1;
+    // Per-bucket metadata: [tvalid level 0..nlev-1][B], [outrow][B], then offsets, nsamp.
+    // A staging slot is only rewritten after the copies that last read it finished.
+    const int slot = stage_slot_;
+    stage_slot_ ^= 1;
+    if (stage_used_[slot]) VDB_CHECK_CUDA(cudaEventSynchronize(stage_ev_[slot]));
+    int* hm = reinterpret_cast<int*>(static_cast<char*>(h_stage_) + slot * h_stage_bytes_);
+    std::vector<long long> tv_sum(nlev, 0);
+    for (int b = 0; b < B; ++b) {
+        int tv = frames_of(h_ns[b], cfg_.win, cfg_.hop);
+        for (size_t l = 0; l < nlev; ++l) {
+            hm[l * B + b] = tv;
+            tv_sum[l] += tv;
+            tv = half_extent(tv);
+        }
+        hm[nlev * B + b] = h_outrow[b];
+    }
+    long long* ho = reinterpret_cast<long long*>(hm + (nlev + 1) * B + ((nlev + 1) * B) % 2);
+    int* hn = reinterpret_cast<int*>(ho + B);
+    std::memcpy(ho, h_off, sizeof(long long) * B);
+    std::memcpy(hn, h_ns, sizeof(int) * B);
+    VDB_CHECK_CUDA(cudaMemcpyAsync(meta_, hm, sizeof(int) * (nlev + 1) * B,
+                                   cudaMemcpyHostToDevice, st));
+    VDB_CHECK_CUDA(cudaMemcpyAsync(offs_, ho, sizeof(long long) * B, cudaMemcpyHostToDevice, st));
+    VDB_CHECK_CUDA(cudaMemcpyAsync(nsamp_, hn, sizeof(int) * B, cudaMemcpyHostToDevice, st));
+    VDB_CHECK_CUDA(cudaEventRecord(stage_ev_[slot], st));
+    stage_used_[slot] = true;
+    long long launches = 0;
+    // FBank -> CMN + stem
+    if (vdb_fbank(plan_, d_pcm, offs_, nsamp_, B, t_max, feats_, st)) {
+        err = vdb_last_error();
+        return 1;
+    }
+    if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
+                     stem_oc_, mean_, levels_[0].g[0], st)) {
+        err = vdb_last_error();
+        return 1;
+    }
+    launches += cfg_.cmn ? 3 : 2;
+    // Backbone.
+    int lev = 0, T = t_max, F = cfg_.n_mels;
+    int cur = 0;            // index of the G buffer holding the block input
+    bool cur_phase = false;  // block input is the level's PHASE buffer
+    for (size_t i = 0; i < blocks_.size(); ++i) {
+        const ResBlockDev& blk = blocks_[i];
+        const bool next_s2 = (i + 1 < blocks_.size()) && blocks_[i + 1].stride == 2;
+        Level& Lin = levels_[lev];
+        const void* x = cur_phase ? Lin.p : Lin.g[cur];
+        int To = T, Fo = F, lev_out = lev;
+        if (blk.stride == 2) {
+            To = half_extent(T);
+            Fo = half_extent(F);
+            lev_out = lev + 1;
+        }
+        Level& Lo = levels_[lev_out];
+        const int* tv_out = meta_ + (size_t)lev_out * B;
+        const int h_slot = (lev_out == lev) ? (cur + 1) % 3 : 0;
+        const int o_slot = (lev_out == lev) ? (cur + 2) % 3 : 1;
+        vdb_conv_args a{};
+        a.batch = B;
+        a.t_out = To;
+        a.f_out = Fo;
+        a.oc = blk.oc;
+        a.k0 = 3;
+        a.stride0 = blk.stride;
+        a.ic0 = blk.ic;
+        a.x0 = x;
+        a.w0 = blk.w1;
+        a.bias = blk.b1;
+        a.relu = 1;
+        a.tvalid = tv_out;
+        a.y = Lo.g[h_slot];
+        a.err = errword_;
+        // algorithmic FLOPs over valid output frames only (padding excluded)
+        const double valid_px = (double)Fo * (double)tv_sum[lev_out];
+        int pe = prof_begin(st);
+        if (vdb_conv(&a, st)) {
+            err = vdb_last_error();
+            return 1;
+        }
+        prof_end(pe, st, 2.0 * blk.oc * blk.ic * 9 * valid_px);
+        vdb_conv_args c2{};
+        c2.batch = B;
+        c2.t_out = To;
+        c2.f_out = Fo;
+        c2.oc = blk.oc;
+        c2.k0 = 3;
+        c2.stride0 = 1;
+        c2.ic0 = blk.oc;
+        c2.x0 = Lo.g[h_slot];
+        c2.w0 = blk.w2;
+        c2.bias = blk.b2;
+        c2.relu = 1;
+        c2.tvalid = tv_out;
+        c2.err = errword_;
+        if (blk.wd) {
+            c2.x1 = x;
+            c2.w1 = blk.wd;
+            c2.ic1 = blk.ic;
+            c2.stride1 = blk.stride;
+        } else {
+            c2.residual = x;
+        }
+        c2.y_phase = next_s2 ? 1 : 0;
+        c2.y = next_s2 ? Lo.p : Lo.g[o_slot];
+        pe = prof_begin(st);
+        if (vdb_conv(&c2, st)) {
+            err = vdb_last_error();
+            return 1;
+        }
+        prof_end(pe, st,
+                 2.0 * blk.oc * blk.oc * 9 * valid_px + (blk.wd ? 2.0 * blk.oc * blk.ic * valid_px : 0));
+        launches += 2;
+        lev = lev_out;
+        T = To;
+        F = Fo;
+        cur = o_slot;
+        cur_phase = next_s2;
+    }
+    const Level& Lf = levels_[lev];
+    if (pool_embed_launch(Lf.g[cur], meta_ + (size_t)lev * B, B, T, F, Lf.c, seg_w_, seg_b_,
+                          mean_vec_, cfg_.emb_dim, var_eps_, cfg_.l2 ? 1 : 0,
+                          meta_ + nlev * B, d_out, nullptr, st)) {
+        err = vdb_last_error();
+        return 1;
+    }
+    launches += 1;
+    last_launches += launches;
+    return 0;
+}
+
+int Engine::embed_device(const float* d_pcm, const long long* offsets, const int* nsamp, int n,
+                         float* d_out, cudaStream_t stream, std::string& err) {
+    if (!supported(err)) return 1;
+    if (n <= 0) {
+        err = "no clips";
+        return 1;
+    }
+    if (cudaSetDevice(device_) != cudaSuccess) {
+        err = "cudaSetDevice failed";
+        return 1;
+    }
+    cudaStream_t st = stream ? stream : stream_;
+    for (int i = 0; i < n; ++i)
+        if (frames_of(nsamp[i], cfg_.win, cfg_.hop) <= 0) {
+            // src/model.cpp:26-29
+            err = "voicedetect: FBank produced no frames (clip " + std::to_string(i) + ")";
+            return 1;
+        }
+    // Longest first; consecutive clips of similar length share a bucket.
+    std::vector<int> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return nsamp[a] > nsamp[b]; });
+    last_launches = 0;
+    std::vector<long long> bo;
+    std::vector<int> bn, br;
+    size_t i = 0;
+    while (i < order.size()) {
+        const int t0 = frames_of(nsamp[order[i]], cfg_.win, cfg_.hop);  // bucket's t_max
+        size_t j = i;
+        bo.clear();
+        bn.clear();
+        br.clear();
+        while (j < order.size() && (int)bo.size() < max_clips &&
+               (long long)(bo.size() + 1) * t0 <= std::max<long long>(max_frames, t0)) {
+            bo.push_back(offsets[order[j]]);
+            bn.push_back(nsamp[order[j]]);
+            br.push_back(order[j]);
+            ++j;
+        }
+        if (run_bucket(d_pcm, bo.data(), bn.data(), br.data(), (int)bo.size(), st, d_out, err))
+            return 1;
+        i = j;
+    }
+    return 0;
+}
+
+int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
+                       std::string& err) {
+    if (!supported(err)) return 1;
+    if (n <= 0) {
+        err = "no clips";
+        return 1;
+    }
+    if (cudaSetDevice(device_) != cudaSuccess) {
+        err = "cudaSetDevice failed";
+        return 1;
+    }
+    std::vector<long long> off(n);
+    long long total = 0;
+    for (int i = 0; i < n; ++i) {
+        if (nsamp[i] < 0) {
+            err = "negative sample count";
+            return 1;
+        }
+        off[i] = total;
+        total += nsamp[i];
+    }
+    const size_t pcm_bytes = std::max<size_t>((size_t)total * sizeof(float), 16);
+    if (pcm_bytes > h_pcm_bytes_) {
+        cudaFreeHost(h_pcm_);
+        cudaFree(d_pcm_);
+        h_pcm_ = nullptr;
+        d_pcm_ = nullptr;
+        h_pcm_bytes_ = d_pcm_bytes_ = 0;
+        if (cudaMallocHost(&h_pcm_, pcm_bytes) != cudaSuccess ||
+            cudaMalloc(&d_pcm_, pcm_bytes) != cudaSuccess) {
+            err = "out of memory (PCM staging)";
+            return 1;
+        }
+        h_pcm_bytes_ = d_pcm_bytes_ = pcm_bytes;
+    }
+    const size_t ob = (size_t)n * cfg_.emb_dim * sizeof(float);
+    if (ob > out_bytes_) {
+        cudaFreeHost(h_out_);
+        cudaFree(d_out_);
+        h_out_ = nullptr;
+        d_out_ = nullptr;
+        out_bytes_ = 0;
+        if (cudaMallocHost(&h_out_, ob) != cudaSuccess || cudaMalloc(&d_out_, ob) != cudaSuccess) {
+            err = "out of memory (output staging)";
+            return 1;
+        }
+        out_bytes_ = ob;
+    }
+    for (int i = 0; i < n; ++i)
+        if (nsamp[i] > 0) std::memcpy(h_pcm_ + off[i], pcm[i], sizeof(float) * nsamp[i]);
+    VDB_CHECK_CUDA(cudaMemcpyAsync(d_pcm_, h_pcm_, sizeof(float) * (size_t)total,
+                                   cudaMemcpyHostToDevice, stream_));
+    if (embed_device(d_pcm_, off.data(), nsamp, n, d_out_, stream_, err)) return 1;
+    VDB_CHECK_CUDA(cudaMemcpyAsync(h_out_, d_out_, ob, cudaMemcpyDeviceToHost, stream_));
+    VDB_CHECK_CUDA(cudaStreamSynchronize(stream_));
+    if (check_device_error(err)) return 1;
+    std::memcpy(out, h_out_, ob);
+    return 0;
+}
+
+int Engine::check_device_error(std::string& err) {
+    int h = 0;
+    if (cudaMemcpy(&h, errword_, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        err = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+        return 1;
+    }
+    if (h != 0) {
+        cudaMemset(errword_, 0, sizeof(int));
+        char buf[96];
+        std::snprintf(buf, sizeof(buf), "GPU kernel wait timed out (code 0x%x)", h);
+        err = buf;
+        return 1;
+    }
+    return 0;
+}
+
+void Engine::set_profiling(bool on) { profiling_ = on; }
+
+int Engine::prof_begin(cudaStream_t st) {
+    if (!profiling_) return -1;
+    if (prof_used_ + 2 > prof_ev_.size()) {
+        for (int i = 0; i < 64; ++i) {
+            cudaEvent_t ev;
+            if (cudaEventCreate(&ev) != cudaSuccess) return -1;
+            prof_ev_.push_back(ev);
+        }
+    }
+    const int idx = (int)prof_used_;
+    prof_used_ += 2;
+    cudaEventRecord(prof_ev_[idx], st);
+    return idx;
+}
+
+void Engine::prof_end(int idx, cudaStream_t st, double flops) {
+    if (idx < 0) return;
+    cudaEventRecord(prof_ev_[idx + 1], st);
+    prof_flops_ += flops;
+}
+
+int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_launches,
+                         std::string& err) {
+    conv_ms = 0.0;
+    conv_flops = prof_flops_;
+    conv_launches = (long long)(prof_used_ / 2);
+    for (size_t i = 0; i + 1 < prof_used_; i += 2) {
+        if (cudaEventSynchronize(prof_ev_[i + 1]) != cudaSuccess) {
+            err = "profile event failed";
+            return 1;
+        }
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]);
+        conv_ms += ms;
+    }
+    prof_used_ = 0;
+    prof_flops_ = 0.0;
+    return 0;
+}
+
+std::vector<float> resample_linear(const std::vector<float>& in, int in_sr, int out_sr) {
+    if (in_sr == out_sr || in.empty()) return in;
+    const double ratio = (double)out_sr / (double)in_sr;
+    const size_t n_out = (size_t)std::floor(in.size() * ratio);
+    std::vector<float> out(n_out);
+    for (size_t i = 0; i < n_out; ++i) {
+        const double src = i / ratio;
+        const size_t i0 = (size_t)src;
+        const double frac = src - i0;
+        const float a = in[i0];
+        const float b = (i0 + 1 < in.size()) ? in[i0 + 1] : a;
+        out[i] = (float)(a + (b - a) * frac);
+    }
+    return out;
+}
+
+}  // namespace vdb

@@ -1,0 +1,152 @@
+// The B200 embedding engine behind the C ABI: the counterpart of the reference's
+// vd::Model (src/model.hpp:18-56) + ResNet34Encoder (src/encoder_resnet.cpp) +
+// ModelLoader (src/model_loader.cpp), re-designed for batched GPU execution.
+//
+// A loaded Engine owns its weights on one device (packed once at load: conv
+// weights f16 [OC][taps][IC], stem and FC f32), an FBank plan, a CUDA stream and
+// a grow-only workspace. embed_* calls sort clips by length, cut them into
+// buckets (at most max_clips clips and max_frames padded frames each) and run
+// each bucket as one batched pass: FBank -> CMN+stem -> 32 tensor-core convs ->
+// TSTP+FC+L2. Ragged clips inside a bucket are exact: every conv masks rows past
+// each clip's valid length (see conv_tc.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "vdb_ops.h"
+
+namespace vdb {
+
+struct EngineConfig {
+    std::string arch;
+    int emb_dim = 0;
+    bool l2 = true;
+    int sample_rate = 16000, n_mels = 80, n_fft = 512, win = 400, hop = 160;
+    float preemph = 0.97f, low_freq = 20.0f, high_freq = 0.0f;
+    bool cmn = true;
+};
+
+struct ResBlockDev {
+    int ic = 0, oc = 0, stride = 1;
+    __half* w1 = nullptr;   // [oc][9][ic]
+    float* b1 = nullptr;
+    __half* w2 = nullptr;   // [oc][9][oc]
+    float* b2 = nullptr;    // conv2 bias (+ downsample bias when fused)
+    __half* wd = nullptr;   // [oc][ic] or nullptr (identity shortcut)
+};
+
+class Engine {
+public:
+    // Loads a GGUF on the current CUDA device. Returns nullptr and sets err on failure.
+    static std::unique_ptr<Engine> load(const std::string& path, std::string& err);
+    ~Engine();
+
+    const EngineConfig& config() const { return cfg_; }
+    int emb_dim() const { return cfg_.emb_dim; }
+    bool supported(std::string& err) const;
+
+    // Embeds n clips of 16 kHz f32 PCM already in device memory (clip i at
+    // d_pcm + offsets[i], nsamp[i] samples; offsets/nsamp are host arrays). Writes
+    // L2-normalised embeddings to d_out[i*emb_dim ...] (device). Asynchronous on
+    // `stream` (nullptr = the engine's stream). Returns 0 or sets err.
+    int embed_device(const float* d_pcm, const long long* offsets, const int* nsamp, int n,
+                     float* d_out, cudaStream_t stream, std::string& err);
+
+    // Host PCM in, host embeddings out (synchronous). pcm[i] has nsamp[i] samples.
+    int embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
+                   std::string& err);
+
+    // Reads and clears the device error word (kernel timeouts). Synchronises.
+    int check_device_error(std::string& err);
+
+    // Bucketing policy.
+    int max_clips = 512;
+    long long max_frames = 262144;
+
+    // Number of GPU kernels launched by the last embed call (for benchmarks).
+    long long last_launches = 0;
+
+    // Conv-kernel profiling: when enabled, every tensor-core conv launch is
+    // bracketed by CUDA events on its stream and its algorithmic FLOPs
+    // (2*OC*IC*k*k*F_out*sum of valid output frames) are accumulated.
+    void set_profiling(bool on);
+    // Synchronises, then returns totals since the last read and resets them.
+    int read_profile(double& conv_ms, double& conv_flops, long long& conv_launches,
+                     std::string& err);
+
+    cudaStream_t stream() const { return stream_; }
+    int device() const { return device_; }
+
+private:
+    Engine() = default;
+    int run_bucket(const float* d_pcm, const long long* h_off, const int* h_ns,
+                   const int* h_outrow, int B, cudaStream_t st, float* d_out, std::string& err);
+    int ensure_workspace(int B, int t_max, std::string& err);
+    void free_workspace();
+
+    EngineConfig cfg_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    vdb_fbank_plan* plan_ = nullptr;
+    // weights
+    int stem_oc_ = 0;
+    float* stem_w_ = nullptr;   // [oc][9], tap kt*3 + kf
+    float* stem_b_ = nullptr;
+    std::vector<ResBlockDev> blocks_;
+    float* seg_w_ = nullptr;    // [D][P]
+    float* seg_b_ = nullptr;
+    float* mean_vec_ = nullptr;
+    int pooled_ = 0;
+    float var_eps_ = 1e-8f;
+    std::vector<void*> weight_allocs_;
+    // workspace (grow-only)
+    struct Level {
+        int c = 0;
+        size_t g_bytes = 0, p_bytes = 0;
+        void* g[3] = {nullptr, nullptr, nullptr};
+        void* p = nullptr;
+    };
+    std::vector<Level> levels_;
+    float* feats_ = nullptr;
+    size_t feats_bytes_ = 0;
+    float* mean_ = nullptr;
+    size_t mean_bytes_ = 0;
+    int* meta_ = nullptr;         // device int32: frames, tvalid per level, out rows
+    long long* offs_ = nullptr;   // device int64 offsets
+    int* nsamp_ = nullptr;
+    int meta_cap_ = 0;
+    int* errword_ = nullptr;
+    // pinned staging for small per-bucket host->device metadata
+    void* h_stage_ = nullptr;
+    size_t h_stage_bytes_ = 0;   // bytes per slot (two slots)
+    int stage_slot_ = 0;
+    bool stage_used_[2] = {false, false};
+    cudaEvent_t stage_ev_[2] = {nullptr, nullptr};
+    // pinned staging for the host PCM path
+    float* h_pcm_ = nullptr;
+    size_t h_pcm_bytes_ = 0;
+    float* d_pcm_ = nullptr;
+    size_t d_pcm_bytes_ = 0;
+    float* h_out_ = nullptr;
+    float* d_out_ = nullptr;
+    size_t out_bytes_ = 0;
+    // profiling
+    bool profiling_ = false;
+    std::vector<cudaEvent_t> prof_ev_;  // pairs (start, stop)
+    size_t prof_used_ = 0;              // events in use
+    double prof_flops_ = 0.0;
+    int prof_begin(cudaStream_t st);    // returns event-pair index or -1
+    void prof_end(int idx, cudaStream_t st, double flops);
+};
+
+// Linear resampling, src/audio_io.cpp:9-23.
+std::vector<float> resample_linear(const std::vector<float>& in, int in_sr, int out_sr);
+// WAV decode to mono f32 (channels averaged) at the file's rate; false on error.
+bool read_wav_mono(const std::string& path, std::vector<float>& out, int& sample_rate,
+                   std::string& err);
+
+}  // namespace vdb

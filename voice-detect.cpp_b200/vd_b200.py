@@ -1,0 +1,358 @@
+"""ctypes binding of libvoicedetect_b200.so (the B200 engine's C ABI).
+
+Two ABI levels are exposed, mirroring the headers in include/:
+
+* the reference's flat model C ABI, ``voicedetect_capi_*`` (include/voicedetect_capi.h),
+  wrapped by :class:`Model`;
+* the op-level ABI, ``vdb_*`` (include/vdb_ops.h): the conv / FBank / pooling
+  kernels on device buffers, wrapped by :func:`conv` etc. The layout helpers
+  (:func:`to_grid`, :func:`to_phase`, :func:`from_grid`) build the GRID / PHASE
+  activation layouts that header defines, using torch on the device.
+
+There is no CPU fallback: importing works without a GPU, but every compute call
+goes to the CUDA library and raises if it is missing or fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libvoicedetect_b200.so"
+
+_lib: C.CDLL | None = None
+
+
+def build() -> None:
+    import subprocess
+    r = subprocess.run(["make", "-C", str(HERE), "-j8"], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("libvoicedetect_b200 build failed:\n" + r.stdout + r.stderr)
+
+
+class ConvArgs(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int), ("t_out", C.c_int), ("f_out", C.c_int), ("oc", C.c_int),
+        ("k0", C.c_int), ("stride0", C.c_int), ("ic0", C.c_int),
+        ("x0", C.c_void_p), ("w0", C.c_void_p),
+        ("stride1", C.c_int), ("ic1", C.c_int), ("x1", C.c_void_p), ("w1", C.c_void_p),
+        ("bias", C.c_void_p), ("residual", C.c_void_p), ("relu", C.c_int),
+        ("clamp_hi", C.c_float), ("tvalid", C.c_void_p), ("y", C.c_void_p),
+        ("y_phase", C.c_int), ("err", C.c_void_p),
+    ]
+
+
+def lib() -> C.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(f"{LIB_PATH} is missing; run `make -C {HERE}`")
+        L = C.CDLL(str(LIB_PATH))
+        L.vdb_last_error.restype = C.c_char_p
+        L.vdb_grid_rows.restype = C.c_longlong
+        L.vdb_grid_rows.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.vdb_phase_rows.restype = C.c_longlong
+        L.vdb_phase_rows.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.vdb_conv.restype = C.c_int
+        L.vdb_conv.argtypes = [C.POINTER(ConvArgs), C.c_void_p]
+        L.vdb_fbank_plan_create.restype = C.c_void_p
+        L.vdb_fbank_plan_create.argtypes = [C.c_int] * 5 + [C.c_float] * 3
+        L.vdb_fbank_plan_destroy.argtypes = [C.c_void_p]
+        L.vdb_fbank.restype = C.c_int
+        L.vdb_fbank.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_void_p, C.c_void_p]
+        L.vdb_cmn_stem.restype = C.c_int
+        L.vdb_cmn_stem.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                   C.c_void_p]
+        L.vdb_pool_embed.restype = C.c_int
+        L.vdb_pool_embed.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float,
+                                     C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.vdb_identify.restype = C.c_int
+        L.vdb_identify.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_void_p, C.c_void_p]
+        # model-level C ABI
+        L.voicedetect_capi_abi_version.restype = C.c_int
+        L.voicedetect_capi_load.restype = C.c_void_p
+        L.voicedetect_capi_load.argtypes = [C.c_char_p]
+        L.voicedetect_capi_free.argtypes = [C.c_void_p]
+        L.voicedetect_capi_last_error.restype = C.c_char_p
+        L.voicedetect_capi_last_error.argtypes = [C.c_void_p]
+        L.voicedetect_capi_free_string.argtypes = [C.c_void_p]
+        L.voicedetect_capi_free_vec.argtypes = [C.c_void_p]
+        L.voicedetect_capi_embed_path.restype = C.c_int
+        L.voicedetect_capi_embed_path.argtypes = [C.c_void_p, C.c_char_p,
+                                                  C.POINTER(C.POINTER(C.c_float)),
+                                                  C.POINTER(C.c_int)]
+        L.voicedetect_capi_embed_pcm.restype = C.c_int
+        L.voicedetect_capi_embed_pcm.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_int,
+                                                 C.c_int, C.POINTER(C.POINTER(C.c_float)),
+                                                 C.POINTER(C.c_int)]
+        L.voicedetect_capi_verify_paths.restype = C.c_int
+        L.voicedetect_capi_verify_paths.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p,
+                                                    C.c_float, C.POINTER(C.c_float),
+                                                    C.POINTER(C.c_int)]
+        L.voicedetect_capi_analyze_path_json.restype = C.c_void_p
+        L.voicedetect_capi_analyze_path_json.argtypes = [C.c_void_p, C.c_char_p]
+        L.voicedetect_capi_embed_pcm_batch.restype = C.c_int
+        L.voicedetect_capi_embed_pcm_batch.argtypes = [C.c_void_p,
+                                                       C.POINTER(C.POINTER(C.c_float)),
+                                                       C.POINTER(C.c_int), C.c_int, C.c_int,
+                                                       C.POINTER(C.c_float), C.POINTER(C.c_int)]
+        L.voicedetect_capi_identify.restype = C.c_int
+        L.voicedetect_capi_identify.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_int,
+                                                C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int,
+                                                C.POINTER(C.c_int), C.POINTER(C.c_float)]
+        L.voicedetect_capi_set_devices.restype = C.c_int
+        L.voicedetect_capi_set_devices.argtypes = [C.c_void_p, C.c_int]
+        L.voicedetect_b200_embed_device.restype = C.c_int
+        L.voicedetect_b200_embed_device.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.c_void_p, C.c_int, C.c_void_p,
+                                                    C.c_void_p]
+        L.voicedetect_b200_set_bucketing.restype = C.c_int
+        L.voicedetect_b200_set_bucketing.argtypes = [C.c_void_p, C.c_int, C.c_longlong]
+        L.voicedetect_b200_last_launches.restype = C.c_longlong
+        L.voicedetect_b200_last_launches.argtypes = [C.c_void_p]
+        L.voicedetect_b200_embedding_dim.restype = C.c_int
+        L.voicedetect_b200_embedding_dim.argtypes = [C.c_void_p]
+        L.voicedetect_b200_sync.restype = C.c_int
+        L.voicedetect_b200_sync.argtypes = [C.c_void_p]
+        L.voicedetect_b200_profile.restype = C.c_int
+        L.voicedetect_b200_profile.argtypes = [C.c_void_p, C.c_int]
+        L.voicedetect_b200_profile_read.restype = C.c_int
+        L.voicedetect_b200_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_double),
+                                                    C.POINTER(C.c_double),
+                                                    C.POINTER(C.c_longlong)]
+        _lib = L
+    return _lib
+
+
+class VoiceDetectError(RuntimeError):
+    pass
+
+
+class Model:
+    """A loaded speaker model behind the reference-compatible C ABI
+    (voicedetect_capi_*). Mirrors vd::Model (src/model.hpp): embed_path,
+    embed_pcm, verify_paths, plus the additive batch / identify calls."""
+
+    def __init__(self, gguf_path: str):
+        self._L = lib()
+        self.ctx = self._L.voicedetect_capi_load(str(gguf_path).encode())
+        if not self.ctx:
+            raise VoiceDetectError(f"voicedetect_capi_load failed for {gguf_path}")
+        self.dim = self._L.voicedetect_b200_embedding_dim(self.ctx)
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None):
+            self._L.voicedetect_capi_free(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return self._L.voicedetect_capi_last_error(self.ctx).decode()
+
+    def _vec(self, rc, p, d):
+        import numpy as np
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+        out = np.ctypeslib.as_array(p, shape=(d.value,)).copy()
+        self._L.voicedetect_capi_free_vec(C.cast(p, C.c_void_p))
+        return out
+
+    def embed_pcm(self, pcm, sample_rate: int = 16000):
+        import numpy as np
+        pcm = np.ascontiguousarray(pcm, dtype=np.float32)
+        p = C.POINTER(C.c_float)()
+        d = C.c_int(0)
+        rc = self._L.voicedetect_capi_embed_pcm(self.ctx, pcm.ctypes.data_as(C.POINTER(C.c_float)),
+                                                len(pcm), sample_rate, C.byref(p), C.byref(d))
+        return self._vec(rc, p, d)
+
+    def embed_path(self, path: str):
+        p = C.POINTER(C.c_float)()
+        d = C.c_int(0)
+        rc = self._L.voicedetect_capi_embed_path(self.ctx, str(path).encode(), C.byref(p),
+                                                 C.byref(d))
+        return self._vec(rc, p, d)
+
+    def verify_paths(self, a: str, b: str, threshold: float = 0.25):
+        dist = C.c_float(0)
+        ok = C.c_int(0)
+        rc = self._L.voicedetect_capi_verify_paths(self.ctx, str(a).encode(), str(b).encode(),
+                                                   threshold, C.byref(dist), C.byref(ok))
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+        return float(dist.value), bool(ok.value)
+
+    def embed_batch(self, clips, sample_rate: int = 16000):
+        import numpy as np
+        arrs = [np.ascontiguousarray(c, dtype=np.float32) for c in clips]
+        n = len(arrs)
+        ptrs = (C.POINTER(C.c_float) * n)(*[a.ctypes.data_as(C.POINTER(C.c_float)) for a in arrs])
+        ns = (C.c_int * n)(*[len(a) for a in arrs])
+        out = np.zeros((n, self.dim), np.float32)
+        d = C.c_int(0)
+        rc = self._L.voicedetect_capi_embed_pcm_batch(self.ctx, ptrs, ns, n, sample_rate,
+                                                      out.ctypes.data_as(C.POINTER(C.c_float)),
+                                                      C.byref(d))
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+        return out
+
+    def identify(self, queries, registry, k: int = 5):
+        import numpy as np
+        q = np.ascontiguousarray(queries, np.float32)
+        r = np.ascontiguousarray(registry, np.float32)
+        idx = np.zeros((q.shape[0], k), np.int32)
+        sc = np.zeros((q.shape[0], k), np.float32)
+        rc = self._L.voicedetect_capi_identify(self.ctx, q.ctypes.data_as(C.POINTER(C.c_float)),
+                                               q.shape[0], r.ctypes.data_as(C.POINTER(C.c_float)),
+                                               r.shape[0], q.shape[1], k,
+                                               idx.ctypes.data_as(C.POINTER(C.c_int)),
+                                               sc.ctypes.data_as(C.POINTER(C.c_float)))
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+        return idx, sc
+
+    def set_bucketing(self, max_clips: int, max_frames: int) -> None:
+        if self._L.voicedetect_b200_set_bucketing(self.ctx, max_clips, max_frames) != 0:
+            raise VoiceDetectError(self.last_error())
+
+    def embed_device(self, d_pcm, offsets, n_samples, d_out, stream=None) -> None:
+        """Device-resident batch: d_pcm / d_out torch CUDA tensors; offsets /
+        n_samples host int sequences."""
+        n = len(n_samples)
+        offs = (C.c_longlong * n)(*[int(o) for o in offsets])
+        ns = (C.c_int * n)(*[int(v) for v in n_samples])
+        rc = self._L.voicedetect_b200_embed_device(self.ctx, d_pcm.data_ptr(), offs, ns, n,
+                                                   d_out.data_ptr(),
+                                                   C.c_void_p(stream) if stream else None)
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+
+    def last_launches(self) -> int:
+        return int(self._L.voicedetect_b200_last_launches(self.ctx))
+
+    def sync(self) -> None:
+        if self._L.voicedetect_b200_sync(self.ctx) != 0:
+            raise VoiceDetectError(self.last_error())
+
+    def profile(self, enable: bool) -> None:
+        self._L.voicedetect_b200_profile(self.ctx, int(enable))
+
+    def profile_read(self):
+        """-> (conv_ms, conv_flops, conv_launches) since the previous read."""
+        ms, fl, n = C.c_double(0), C.c_double(0), C.c_longlong(0)
+        if self._L.voicedetect_b200_profile_read(self.ctx, C.byref(ms), C.byref(fl),
+                                                 C.byref(n)) != 0:
+            raise VoiceDetectError(self.last_error())
+        return ms.value, fl.value, n.value
+
+
+def last_error() -> str:
+    return lib().vdb_last_error().decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: {last_error()}")
+
+
+# ---------------------------------------------------------------------------
+# Layout helpers (torch, on device). x: (B, C, F, T) in torch NCHW terms with
+# H = freq, W = time, matching the reference's ggml [W=T, H=F, C, N].
+# ---------------------------------------------------------------------------
+def out_extent(n: int, stride: int) -> int:
+    return (n - 1) // stride + 1
+
+
+def to_grid(x, tvalid=None):
+    """(B, C, F, T) float -> GRID f16 tensor of shape (B*(T+2)*(F+2), C)."""
+    import torch
+    B, Cc, F, T = x.shape
+    g = torch.zeros(B, T + 2, F + 2, Cc, dtype=torch.float16, device=x.device)
+    g[:, 1:T + 1, 1:F + 1, :] = x.permute(0, 3, 2, 1).to(torch.float16)
+    if tvalid is not None:
+        for b, tv in enumerate(tvalid):
+            g[b, 1 + int(tv):, :, :] = 0
+    return g.reshape(B * (T + 2) * (F + 2), Cc).contiguous()
+
+
+def from_grid(g, B: int, C_: int, F: int, T: int):
+    """GRID (rows, C) -> (B, C, F, T) float32 (valid interior only)."""
+    x = g.reshape(B, T + 2, F + 2, C_)[:, 1:T + 1, 1:F + 1, :]
+    return x.permute(0, 3, 2, 1).float().contiguous()
+
+
+def to_phase(x, tvalid=None):
+    """(B, C, F, T) -> PHASE f16 tensor (4*B*(To+2)*(Fo+2), C) for a stride-2 consumer."""
+    import torch
+    B, Cc, F, T = x.shape
+    To, Fo = out_extent(T, 2), out_extent(F, 2)
+    pad = torch.zeros(B, T + 2, F + 2, Cc, dtype=torch.float16, device=x.device)
+    pad[:, 1:T + 1, 1:F + 1, :] = x.permute(0, 3, 2, 1).to(torch.float16)
+    if tvalid is not None:
+        for b, tv in enumerate(tvalid):
+            pad[b, 1 + int(tv):, :, :] = 0
+    out = torch.zeros(4, B, To + 2, Fo + 2, Cc, dtype=torch.float16, device=x.device)
+    for pt in range(2):
+        for pf in range(2):
+            src = pad[:, pt::2, pf::2, :]
+            nt, nf = src.shape[1], src.shape[2]
+            out[2 * pt + pf, :, 1:1 + nt, 1:1 + nf, :] = src
+    return out.reshape(-1, Cc).contiguous()
+
+
+def from_phase(p, B: int, C_: int, F: int, T: int):
+    """PHASE tensor of a (B, C, F, T) activation -> (B, C, F, T) float32."""
+    import torch
+    To, Fo = out_extent(T, 2), out_extent(F, 2)
+    pl = p.reshape(4, B, To + 2, Fo + 2, C_)
+    pad = torch.zeros(B, T + 2, F + 2, C_, dtype=p.dtype, device=p.device)
+    for pt in range(2):
+        for pf in range(2):
+            nt = len(range(pt, T + 2, 2))
+            nf = len(range(pf, F + 2, 2))
+            pad[:, pt::2, pf::2, :] = pl[2 * pt + pf, :, 1:1 + nt, 1:1 + nf, :]
+    return pad[:, 1:T + 1, 1:F + 1, :].permute(0, 3, 2, 1).float().contiguous()
+
+
+def pack_conv_weight(w):
+    """torch (OC, IC, KF, KT) -> f16 (OC, KT*KF, IC) (tap = kt*k + kf)."""
+    OC, IC, KF, KT = w.shape
+    return w.permute(0, 3, 2, 1).reshape(OC, KT * KF, IC).to(
+        __import__("torch").float16).contiguous()
+
+
+def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
+         x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
+         y=None, y_phase=False, err=None, stream=None):
+    """vdb_conv on device tensors. x0/x1/residual/y are f16 GRID or PHASE tensors,
+    w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,), tvalid int32 (B,)."""
+    import torch
+    if y is None:
+        rows = (lib().vdb_phase_rows(batch, t_out, f_out) if y_phase
+                else lib().vdb_grid_rows(batch, t_out, f_out))
+        y = torch.empty(rows, oc, dtype=torch.float16, device=x0.device)
+    a = ConvArgs(batch=batch, t_out=t_out, f_out=f_out, oc=oc, k0=k0, stride0=stride0,
+                 ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(),
+                 w0=w0.data_ptr(), stride1=stride1,
+                 ic1=(ic1 if ic1 is not None else (x1.shape[1] if x1 is not None else 0)),
+                 x1=x1.data_ptr() if x1 is not None else None,
+                 w1=w1.data_ptr() if w1 is not None else None, bias=bias.data_ptr(),
+                 residual=residual.data_ptr() if residual is not None else None,
+                 relu=int(relu), clamp_hi=float(clamp_hi), tvalid=tvalid.data_ptr(),
+                 y=y.data_ptr(), y_phase=int(y_phase),
+                 err=err.data_ptr() if err is not None else None)
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
+    return y
