@@ -236,7 +236,11 @@ def run_b200(args) -> int:
     n_max = (len(lengths) + world - 1) // world
     d_out = torch.zeros(n_max, model.dim, device=dev)
     gathered = torch.empty(world * n_max, model.dim, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    # One explicit (non-default) stream carries every kernel, the all-gather and the
+    # timing events; the engine launches on the stream it is given.
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    torch.cuda.synchronize()
 
     def step():
         model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
@@ -340,8 +344,82 @@ def run_b200(args) -> int:
     return 0
 
 
+# every distinct ResNet34 3x3 conv shape (stage entries carry the
+# fused 1x1 downsample in conv2), batch B, T = 300 frames, 80 mels.
+SWEEP_SHAPES = [  # (ic, oc, t_in, f_in, stride, fused_down)
+    (32, 32, 300, 80, 1, False), (32, 64, 300, 80, 2, False), (64, 64, 150, 40, 1, True),
+    (64, 64, 150, 40, 1, False), (64, 128, 150, 40, 2, False), (128, 128, 75, 20, 1, True),
+    (128, 128, 75, 20, 1, False), (128, 256, 75, 20, 2, False), (256, 256, 38, 10, 1, True),
+    (256, 256, 38, 10, 1, False)]
+
+
+def run_sweep(args) -> int:
+    """Per-shape vdb_conv timing (CUDA events, device-resident f16 inputs),
+    one JSON line per shape: algorithmic TFLOP/s over valid pixels."""
+    import torch
+    import vd_b200 as vd
+    torch.manual_seed(0)
+    B = args.op_sweep
+    L = vd.lib()
+    out = []
+    for ic, oc, T, F, s, down in SWEEP_SHAPES:
+        To, Fo = vd.out_extent(T, s), vd.out_extent(F, s)
+        icc = oc if down else ic
+        rows = L.vdb_phase_rows(B, T, F) if s == 2 else L.vdb_grid_rows(B, T, F)
+        x = torch.empty(rows, icc, dtype=torch.float16, device="cuda").normal_().relu_()
+        w = (torch.randn(oc, 9, icc, device="cuda") * (2 / (9 * icc)) ** 0.5).half()
+        b = torch.zeros(oc, device="cuda")
+        tv = torch.full((B,), To, dtype=torch.int32, device="cuda")
+        kw = {}
+        if down:
+            x1 = torch.empty(L.vdb_phase_rows(B, 2 * To, 2 * Fo), ic // 2, dtype=torch.float16,
+                             device="cuda").normal_().relu_()
+            kw = dict(x1=x1, w1=(torch.randn(oc, ic // 2, device="cuda") * 0.1).half(),
+                      stride1=2)
+        y = torch.empty(L.vdb_grid_rows(B, To, Fo), oc, dtype=torch.float16, device="cuda")
+
+        def run():
+            vd.conv(x, w, b, tv, batch=B, t_out=To, f_out=Fo, oc=oc, k0=3,
+                    stride0=1 if down else s, ic0=icc, relu=True, y=y,
+                    tile_m=args.sweep_tile_m, halo=args.sweep_halo, ksplit=args.sweep_ksplit,
+                    **kw)
+        try:
+            run()  # validates the requested tiling for this shape
+        except RuntimeError as e:
+            print(json.dumps({"shape": f"{icc}->{oc} s{s}", "skipped": str(e)}), flush=True)
+            continue
+        for _ in range(args.sweep_warmup):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.sweep_reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.sweep_reps
+        fl = 2.0 * oc * icc * 9 * To * Fo * B + (2.0 * oc * (ic // 2) * To * Fo * B if down else 0)
+        r = dict(shape=f"{icc}->{oc} s{s}{'+down' if down else ''} out {Fo}x{To}", batch=B,
+                 ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1),
+                 gflop=round(fl / 1e9, 2))
+        out.append(r)
+        print(json.dumps(r), flush=True)
+    tot_fl = sum(r["gflop"] for r in out)
+    tot_ms = sum(r["ms"] for r in out)
+    print(json.dumps({"sweep_total": {"gflop": round(tot_fl, 1), "ms": round(tot_ms, 3),
+                                      "tflops": round(tot_fl / tot_ms, 1)}}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op-sweep", type=int, default=0, metavar="B",
+                    help="time every distinct ResNet34 conv shape at batch B and exit")
+    ap.add_argument("--sweep-reps", type=int, default=20)
+    ap.add_argument("--sweep-warmup", type=int, default=3)
+    ap.add_argument("--sweep-tile-m", type=int, default=0, help="0 auto, 128 or 256")
+    ap.add_argument("--sweep-halo", type=int, default=0, help="0 auto, 1 force, -1 never")
+    ap.add_argument("--sweep-ksplit", type=int, default=0, help="0 auto, else 1..16")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -351,6 +429,8 @@ def main() -> int:
     ap.add_argument("--ref-clips", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.op_sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -75,6 +75,12 @@ typedef struct vdb_conv_args {
     void* y;                /* device f16 output */
     int y_phase;            /* 0: y is G(B, t_out, f_out, oc); 1: y is P(B, t_out, f_out, oc) */
     int* err;               /* device int32 error word (may be NULL): kernel timeouts */
+    /* tiling (0 = automatic) */
+    int tile_m;             /* output rows per CTA tile: 0, 128 or 256 */
+    int halo;               /* 0 auto, 1 force, -1 never: one input halo per channel block
+                               feeding all nine taps (stride-1 3x3, weights resident) */
+    int ksplit;             /* 0 auto, else 1..16 independent partial accumulators per
+                               128-row block, summed in the epilogue */
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */

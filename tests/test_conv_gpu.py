@@ -53,6 +53,25 @@ def _h(t):
     return t.half().float()
 
 
+def valid_tilings(IC, OC, k, stride):
+    """Every explicit (tile_m, halo, ksplit) the kernel accepts for this layer."""
+    bn = OC if OC <= 256 else OC // ((OC + 255) // 256)
+    kb = 64 if IC % 64 == 0 else (32 if IC % 32 == 0 else 16)
+    ks = kb // 16
+    halo_ok = k == 3 and stride == 1 and OC <= 256 and 9 * IC * bn * 2 <= 96 * 1024
+    out = []
+    for tile_m in (128, 256):
+        nmb = tile_m // 128
+        for J in (1, 2, 4, 8):
+            if nmb * J * bn > 512:
+                continue
+            if J <= ks:
+                out.append((tile_m, -1, J))
+            if halo_ok:
+                out.append((tile_m, 1, J))
+    return out
+
+
 CASES = [
     # name, B, IC, OC, F, T, k, stride, fused_down, residual, tvalid_frac
     ("gemm1x1", 2, 64, 64, 8, 12, 1, 1, False, False, None),
@@ -102,23 +121,28 @@ def test_conv_vs_reference(cuda_lib, case):
 
     xin = vd.to_phase(x.to(dev), tvalid_in) if stride == 2 else vd.to_grid(x.to(dev), tvalid_in)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    y = vd.conv(xin, vd.pack_conv_weight(w.to(dev)), bias.float().to(dev), tv_dev, batch=B,
-                t_out=To, f_out=Fo, oc=OC, k0=k, stride0=stride, ic0=IC, relu=True, err=err,
-                **kw)
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0, f"kernel error word {err.item():#x}"
-    got = vd.from_grid(y, B, OC, Fo, To).cpu()
     small = B * OC * Fo * To * IC * k * k < 2e7
     ref = _ref_conv(x, w, bias, stride, x1=x1, w1=w1, stride1=stride, residual=residual,
                     relu=True, tvalid_out=tvalid_out, use_oracle=small)
-    rel = float((got - ref).norm() / max(ref.norm(), 1e-12))
-    assert rel <= REL_L2_TOL, f"{name}: rel-L2 {rel:.3e}"
-    # borders and masked rows are exactly zero
-    gfull = y.reshape(B, To + 2, Fo + 2, OC).float().cpu()
-    assert torch.all(gfull[:, 0] == 0) and torch.all(gfull[:, :, 0] == 0)
-    assert torch.all(gfull[:, :, Fo + 1] == 0)
-    for b, t in enumerate(tvalid_out):
-        assert torch.all(gfull[b, 1 + t:] == 0)
+    # every tiling the kernel offers: automatic, 128/256-row tiles, and the
+    # shared-halo feed where the layer qualifies (stride 1, 3x3, resident weights)
+    configs = [(0, 0, 0)] + valid_tilings(IC, OC, k, stride)
+    wp = vd.pack_conv_weight(w.to(dev))
+    for tile_m, halo, ksplit in configs:
+        y = vd.conv(xin, wp, bias.float().to(dev), tv_dev, batch=B, t_out=To, f_out=Fo, oc=OC,
+                    k0=k, stride0=stride, ic0=IC, relu=True, err=err, tile_m=tile_m, halo=halo,
+                    ksplit=ksplit, **kw)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0, f"kernel error word {err.item():#x}"
+        got = vd.from_grid(y, B, OC, Fo, To).cpu()
+        rel = float((got - ref).norm() / max(ref.norm(), 1e-12))
+        assert rel <= REL_L2_TOL, f"{name} tile_m={tile_m} halo={halo} ksplit={ksplit}: rel-L2 {rel:.3e}"
+        # borders and masked rows are exactly zero
+        gfull = y.reshape(B, To + 2, Fo + 2, OC).float().cpu()
+        assert torch.all(gfull[:, 0] == 0) and torch.all(gfull[:, :, 0] == 0)
+        assert torch.all(gfull[:, :, Fo + 1] == 0)
+        for b, t in enumerate(tvalid_out):
+            assert torch.all(gfull[b, 1 + t:] == 0)
 
 
 def test_conv_phase_output(cuda_lib):

@@ -146,7 +146,9 @@ def test_device_path_matches_host_path(resnet):
     flat = torch.from_numpy(np.concatenate(clips)).cuda()
     offs = np.cumsum([0] + lens[:-1])
     out = torch.empty(len(clips), 256, device="cuda")
-    model.embed_device(flat, offs, lens, out, torch.cuda.current_stream().cuda_stream)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    model.embed_device(flat, offs, lens, out, s.cuda_stream)
     torch.cuda.synchronize()
     dev = out.cpu().numpy()
     assert np.allclose(dev, host, atol=1e-6)

@@ -6,24 +6,37 @@
 // GEMM view. Rows (M) are the pixels of the output's zero-bordered grid
 // (vdb_ops.h, GRID layout), columns (N) the output channels, and K runs over
 // (tap, input channel). Because every activation carries a one-pixel zero border
-// and is stored row-major over (time, freq), the A tile of tap (kt, kf) for 128
-// consecutive output rows is 128 consecutive input rows shifted by a constant:
+// and is stored row-major over (time, freq), the A operand of tap (kt, kf) for BM
+// consecutive output rows is BM consecutive input rows shifted by a constant:
 //   stride 1: off = (kt-1)*(F+2) + (kf-1) in the same grid;
 //   stride 2: the input is stored phase-split (PHASE layout), and the tap reads
 //             plane 2*(kt&1) + (kf&1) at off = (kt>>1)*(F+2) + (kf>>1).
-// So every A tile is ONE rectangular TMA box (channels x 128 rows); the border
-// zeros and TMA's out-of-bounds zero fill provide the convolution padding. Rows
-// that fall on the grid border, or past a clip's valid length, are computed and
-// then written as zeros, which keeps the next layer's padding exact under
-// length-bucketed batching (ragged clips in one batch).
+// The border zeros and TMA's out-of-bounds zero fill provide the padding. Rows on
+// the grid border, or past a clip's valid length, are computed and then written
+// as zeros, which keeps the next layer's padding exact under length-bucketed
+// batching (ragged clips in one batch).
 //
-// Kernel structure (persistent, one CTA per SM, 8 warps):
-//   warp 0 lane 0 : TMA producer, S-stage smem ring (A tile + B tile per stage)
-//   warp 1 lane 0 : tcgen05.mma issuer (M=128, N=BN, K=16 per instruction) into
-//                   a double-buffered f32 TMEM accumulator; also owns TMEM alloc
-//   warps 4..7    : epilogue: tcgen05.ld -> + bias [+ residual] -> ReLU/clamp ->
+// Two ways to feed a K segment:
+//   TAP  : one TMA box (KB channels x BM rows) per (tap, channel block) plus the
+//          matching weight box (KB x BN). Used for stride-2 and wide layers,
+//          where the weights dominate the traffic.
+//   HALO : for stride-1 3x3 layers with few channels, one TMA load per channel
+//          block brings the BM + 2*(F+2) + 2 input rows all nine taps need; the
+//          nine MMAs read it through row-shifted shared-memory descriptors (the
+//          tcgen05 swizzle is a function of the absolute shared-memory address,
+//          so a descriptor may start at any 128 B row of a TMA-written tile). The
+//          weights of all taps stay resident in shared memory for the whole
+//          kernel. A traffic drops from 9*BM to BM + 2*(F+2) + 2 rows per block.
+//
+// Kernel structure (persistent, one CTA per SM, 12 warps):
+//   warp 0 lane 0 : TMA producer, S-stage shared-memory ring
+//   warp 1 lane 0 : tcgen05.mma issuer (M=128 per instruction, BM/128 row
+//                   blocks, N=BN, K=16) into a double-buffered f32 TMEM
+//                   accumulator; warp 1 also owns the TMEM allocation
+//   warps 4..11   : epilogue, two warps per TMEM lane quadrant splitting the
+//                   columns: tcgen05.ld -> + bias [+ residual] -> ReLU/clamp ->
 //                   valid-pixel mask -> f16 store (plain or phase-split layout)
-// A second, optional K segment (a 1x1 conv on another input) accumulates into the
+// An optional second K segment (a 1x1 conv on another input) accumulates into the
 // same TMEM tile: that is how the BasicBlock downsample shortcut is fused into
 // conv2 (reference: blocked_conv1x1 + blocked_add_relu, src/encoder_resnet.cpp:68-72).
 #include <cuda_fp16.h>
@@ -39,55 +52,66 @@
 namespace vdb {
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kThreads = 256;
+constexpr int kMB = 128;           // rows per MMA instruction
+constexpr int kThreads = 384;      // 12 warps
+constexpr int kEpiWarp0 = 4;
+constexpr int kEpiThreads = 256;
 constexpr int kMaxStages = 8;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemMax = 232448;   // 227 KB opt-in dynamic shared memory
+constexpr int kMaxBatch = 8192;
+
+enum SegMode : int { SEG_TAP = 0, SEG_HALO = 1 };
 
 struct SegDev {
+    int mode;
     int n_taps;
     int ic;
-    int kb;      // channels per K block: 64 / 32 / 16 (128 / 64 / 32 B rows)
-    int n_kb;    // ic / kb
-    int kcols;   // B matrix K extent = n_taps * ic
-    uint32_t bytes;  // TMA bytes per k-iteration (A + B)
+    int kb;          // channels per K block: 64 / 32 / 16 (128 / 64 / 32 B rows)
+    int n_kb;        // ic / kb
+    uint32_t bytes;  // TMA bytes per stage
     int plane[9];
-    int off[9];
+    int off[9];      // TAP: global row offset per tap; HALO: row offset inside the halo
+    int halo_back;   // HALO: rows before m0 covered by the halo
+    int n_box, box_rows;  // HALO: TMA boxes per stage and their height
+    uint32_t bres;   // HALO: resident weights, byte offset from the smem base
 };
 
 struct ConvDev {
-    int M;          // output grid rows
-    int n_mt, n_nt, BN;
+    int M;             // output grid rows
+    int n_mt, n_nt, BN, BM, n_mblk, n_acc;
+    int J;             // independent partial accumulators per row block (K split)
     int n_seg;
     SegDev seg[2];
-    uint32_t stage_bytes, a_region, n_stages, tmem_cols;
+    uint32_t stage0, stage_bytes, a_region, n_stages, tmem_cols, bres_bytes;
+    uint32_t bias_off, tv_off, bar_off;
     const float* bias;
     const __half* residual;
     __half* y;
     int y_phase;
-    int Hp, Wp, T, F;   // output grid: Hp = T+2, Wp = F+2
-    int Hq, Wq;         // phase-split output: consumer grid
+    int Hp, Wp, T, F;  // output grid: Hp = T+2, Wp = F+2
+    int Hq, Wq;        // phase-split output: consumer grid
     long long plane_rows;
     const int* tvalid;
+    int batch;
     int relu;
     float clamp_hi;
     int oc;
     int* err;
 };
 
-// True when rows [m0, m0+128) contain at least one pixel inside a clip's valid
+// True when rows [m0, m0+BM) contain at least one pixel inside a clip's valid
 // time range (conservative: border columns of those rows count). Every role
 // evaluates it identically, so skipped tiles never touch the pipeline.
-__device__ __forceinline__ bool tile_live(const ConvDev& p, int m0) {
+__device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m0) {
     const int img = p.Hp * p.Wp;
-    const int mend = min(m0 + kBM, p.M);
+    const int mend = min(m0 + p.BM, p.M);
     for (int b = m0 / img; b * img < mend; ++b) {
         const int r0 = max(m0 - b * img, 0);
         const int r1 = min(mend - b * img, img);
-        const int tv = p.tvalid[b];
-        if (tv <= 0) continue;
+        const int t = tv[b];
+        if (t <= 0) continue;
         const int lo = p.Wp + 1;
-        const int hi = p.Wp * tv + p.F + 1;
+        const int hi = p.Wp * t + p.F + 1;
         if (r0 < hi && r1 > lo) return true;
     }
     return false;
@@ -97,29 +121,81 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)bits16));
 }
 
-// One epilogue chunk of NC (32 or 16) accumulator columns for this thread's row:
-// TMEM -> + bias [+ residual] -> ReLU / clamp -> mask -> f16 store. The TMEM load
-// is warp-collective, so every lane executes it whenever the tile is live.
-template <int NC>
-__device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, bool in_range, bool valid,
-                                          uint32_t taddr, int ch0, const __half* rrow,
-                                          __half* yrow) {
-    uint32_t v[NC];
-    if (live) {
-        if constexpr (NC == 32) tmem_ld_32x32b_x32(taddr, v);
-        else tmem_ld_32x32b_x16(taddr, v);
+struct RowInfo {
+    bool in_range, valid;
+    long long dst;
+};
+
+__device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int m, bool live) {
+    RowInfo ri{false, false, (long long)m};
+    if (m >= p.M) return ri;
+    ri.in_range = true;
+    const int img = p.Hp * p.Wp;
+    const int b = m / img;
+    const int r = m - b * img;
+    const int tp = r / p.Wp;
+    const int fp = r - tp * p.Wp;
+    ri.valid = live && tp >= 1 && tp <= tv[b] && fp >= 1 && fp <= p.F;
+    if (p.y_phase) {
+        const int q = ((tp & 1) << 1) | (fp & 1);
+        ri.dst = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
+                 (fp >> 1) + 1;
     }
-    if (!in_range) return;
-    float f[NC];
-    if (valid) {
+    return ri;
+}
+
+template <int NC>
+__device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8]) {
 #pragma unroll
-        for (int i = 0; i < NC; ++i) f[i] = __uint_as_float(v[i]) + __ldg(p.bias + ch0 + i);
-        if (rrow) {
-            const uint4* rp = reinterpret_cast<const uint4*>(rrow);
+    for (int j = 0; j < NC / 8; ++j) r[j] = __ldg(reinterpret_cast<const uint4*>(rrow) + j);
+}
+
+// One epilogue chunk of NC (32 or 16) accumulator columns for this thread's row:
+// TMEM (sum of the J partial accumulators) -> + bias [+ residual] -> ReLU / clamp
+// -> mask -> f16 store. The TMEM loads are warp-collective, so every lane executes
+// them whenever the tile is live.
+template <int NC, int J>
+__device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri,
+                                          uint32_t taddr, const float* sbias, bool has_res,
+                                          const uint4 (&res)[NC / 8], __half* yrow) {
+    float f[NC];
+#pragma unroll
+    for (int i = 0; i < NC; ++i) f[i] = 0.0f;
+    if (live) {
+        if constexpr (NC == 32) {
+#pragma unroll 1
+            for (int j = 0; j < J; ++j) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(taddr + (uint32_t)(j * p.BN), v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) f[i] += __uint_as_float(v[i]);
+            }
+        } else {
+            // 16-column chunks: partials in pairs, one wait per pair
+#pragma unroll
+            for (int j = 0; j < J; j += 2) {
+                uint32_t v[16], w[16];
+                if (j + 1 < J) {
+                    tmem_ld_32x32b_x16_pair(taddr + (uint32_t)(j * p.BN),
+                                            taddr + (uint32_t)((j + 1) * p.BN), v, w);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) f[i] += __uint_as_float(v[i]) + __uint_as_float(w[i]);
+                } else {
+                    tmem_ld_32x32b_x16(taddr + (uint32_t)(j * p.BN), v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) f[i] += __uint_as_float(v[i]);
+                }
+            }
+        }
+    }
+    if (!ri.in_range) return;
+    if (ri.valid) {
+#pragma unroll
+        for (int i = 0; i < NC; ++i) f[i] += sbias[i];
+        if (has_res) {
 #pragma unroll
             for (int j = 0; j < NC / 8; ++j) {
-                const uint4 q = __ldg(rp + j);
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+                const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     f[j * 8 + 2 * h] += h2f(w[h] & 0xFFFFu);
@@ -155,6 +231,95 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, bool in_r
     }
 }
 
+// Epilogue of one (tile, row block) for this thread: columns [c_lo, c_hi) of the
+// tile in chunks of NC, with the residual of the next chunk loaded before the
+// current one is finished.
+template <int NC, int J>
+__device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowInfo& ri, int m,
+                                         int n0, int c_lo, int c_hi, uint32_t tbase,
+                                         const float* sbias) {
+    const bool has_res = p.residual != nullptr && ri.valid;
+    const __half* rrow = has_res ? p.residual + (long long)m * p.oc + n0 : nullptr;
+    __half* yrow = p.y + ri.dst * p.oc + n0;
+    uint4 res[NC / 8];
+    if (has_res) load_res<NC>(rrow + c_lo, res);
+    for (int c = c_lo; c < c_hi; c += NC) {
+        uint4 cur[NC / 8];
+#pragma unroll
+        for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
+        if (has_res && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
+        epi_chunk<NC, J>(p, live, ri, tbase + (uint32_t)c, sbias + n0 + c, has_res, cur,
+                         yrow + c);
+    }
+}
+
+// ---- MMA issue schedules ---------------------------------------------------
+// The single issuing thread is on the critical path (a tcgen05.mma every ~60
+// cycles at best), so each stage is one fully unrolled, branch-free sequence with
+// descriptors derived by integer adds in 16-byte units from a per-stage base.
+// Partial accumulator (mb, j) sits at TMEM column (mb*J + j)*BN of the tile, and
+// consecutive MMAs rotate over the NMB*J partials so none waits on its
+// predecessor. `first` marks the tile's first stage: the first MMA into each
+// partial overwrites instead of accumulating.
+
+// HALO stage: nine taps of a 3x3 stride-1 conv read one shared input halo through
+// row-shifted descriptors; tap (kt, kf) starts kt*wp_units + kf*rb16 in.
+template <int KS, int NMB, int J>
+__device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
+                                           uint32_t wp_units, uint32_t rb16, uint64_t b_desc,
+                                           uint32_t b_tap_units, uint32_t idesc, bool first) {
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+        const uint64_t at = a_desc + (uint64_t)((tap / 3) * wp_units + (tap % 3) * rb16);
+        const uint64_t bt = b_desc + (uint64_t)(tap * b_tap_units);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+            const int q = tap * KS + k;
+            const int j = q % J;
+#pragma unroll
+            for (int mb = 0; mb < NMB; ++mb)
+                umma_f16(d_tile + (uint32_t)(mb * J + j) * bn,
+                         at + (uint64_t)(mb * 128 * rb16) + 2 * k, bt + 2 * k, idesc,
+                         (first && q < J) ? 0u : 1u);
+        }
+    }
+}
+
+// TAP stage: one (tap, channel block) A tile and its weight tile, rotating over
+// JU = min(J, KS) partials. When this is the tile's first segment the host
+// guarantees J <= KS, so the first stage initialises every partial.
+template <int KS, int NMB, int J>
+__device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
+                                          uint32_t rb16, uint64_t b_desc, uint32_t idesc,
+                                          bool first) {
+    constexpr int JU = J < KS ? J : KS;
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+        const int j = k % JU;
+#pragma unroll
+        for (int mb = 0; mb < NMB; ++mb)
+            umma_f16(d_tile + (uint32_t)(mb * J + j) * bn, a_desc + (uint64_t)(mb * 128 * rb16) + 2 * k,
+                     b_desc + 2 * k, idesc, (first && k < JU) ? 0u : 1u);
+    }
+}
+
+template <int NMB, int J>
+__device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
+                                            uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
+                                            uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
+                                            bool first) {
+    if (halo) {
+        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
+        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
+        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
+    } else {
+        if (ks == 4) issue_tap<4, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else if (ks == 2) issue_tap<2, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else issue_tap<1, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+    }
+}
+
+template <int NMB, int J>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -164,17 +329,21 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const uint32_t base = (raw_u32 + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - raw_u32);
     const uint32_t S = p.n_stages;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * p.stage_bytes);
-    const uint32_t bar_full = smem_u32(bars);
+    float* sbias = reinterpret_cast<float*>(smem + p.bias_off);
+    int* stv = reinterpret_cast<int*>(smem + p.tv_off);
+    const uint32_t bar_full = base + p.bar_off;
     const uint32_t bar_empty = bar_full + 8 * S;
     const uint32_t bar_tfull = bar_empty + 8 * S;
     const uint32_t bar_tempty = bar_tfull + 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+    const uint32_t bar_bres = bar_tempty + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.bar_off + 8 * (2 * S + 5));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
+    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias[i];
+    for (int i = threadIdx.x; i < p.batch; i += blockDim.x) stv[i] = p.tvalid[i];
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(bar_full + 8 * s, 1);
@@ -182,8 +351,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_tfull + 8 * a, 1);
-            mbar_init(bar_tempty + 8 * a, 128);
+            mbar_init(bar_tempty + 8 * a, kEpiThreads);
         }
+        mbar_init(bar_bres, 1);
         *abort_flag = 0;
         fence_barrier_init();
         fence_proxy_async_smem();
@@ -203,50 +373,66 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const uint32_t tmem_base = *tmem_slot;
 
     const int n_tiles = p.n_mt * p.n_nt;
-    const uint32_t idesc = umma_idesc_f16(kBM, p.BN);
+    const uint32_t idesc = umma_idesc_f16(kMB, p.BN);
+    const uint32_t acc_cols = (uint32_t)(NMB * J * p.BN);
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
+            // Resident weights of HALO segments: every (tap, channel block) box once.
+            if (p.bres_bytes) {
+                mbar_arrive_expect_tx(bar_bres, p.bres_bytes);
+                for (int sg = 0; sg < p.n_seg; ++sg) {
+                    const SegDev& s = p.seg[sg];
+                    if (s.mode != SEG_HALO) continue;
+                    const CUtensorMap* tb = sg ? &tmB1 : &tmB0;
+                    const uint32_t box = (uint32_t)p.BN * s.kb * 2;
+                    for (int tap = 0; tap < s.n_taps; ++tap)
+                        for (int kbi = 0; kbi < s.n_kb; ++kbi)
+                            tma_load_2d(base + s.bres + (uint32_t)(tap * s.n_kb + kbi) * box, tb,
+                                        bar_bres, tap * s.ic + kbi * s.kb, 0);
+                }
+            }
             uint32_t stage = 0, phase = 0;
             bool ok = true;
-            int inflight = 0;  // stages issued and not yet confirmed consumed
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
-                const int m0 = mt * kBM, n0 = nt * p.BN;
-                if (!tile_live(p, m0)) continue;
+                const int m0 = mt * p.BM, n0 = nt * p.BN;
+                if (!tile_live(p, stv, m0)) continue;
                 for (int sg = 0; sg < p.n_seg && ok; ++sg) {
                     const SegDev& s = p.seg[sg];
                     const CUtensorMap* ta = sg ? &tmA1 : &tmA0;
                     const CUtensorMap* tb = sg ? &tmB1 : &tmB0;
-                    for (int tap = 0; tap < s.n_taps && ok; ++tap) {
-                        for (int kbi = 0; kbi < s.n_kb; ++kbi) {
-                            if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, p.err,
-                                           VDB_ERR_TIMEOUT_EMPTY, abort_flag)) {
-                                ok = false;
-                                break;
-                            }
-                            const uint32_t fb = bar_full + 8 * stage;
-                            const uint32_t sa = base + stage * p.stage_bytes;
-                            mbar_arrive_expect_tx(fb, s.bytes);
+                    const int iters = s.mode == SEG_HALO ? s.n_kb : s.n_taps * s.n_kb;
+                    for (int it = 0; it < iters; ++it) {
+                        if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1, p.err,
+                                       VDB_ERR_TIMEOUT_EMPTY, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = bar_full + 8 * stage;
+                        const uint32_t sa = base + p.stage0 + stage * p.stage_bytes;
+                        mbar_arrive_expect_tx(fb, s.bytes);
+                        if (s.mode == SEG_HALO) {
+                            const uint32_t box_bytes = (uint32_t)s.box_rows * s.kb * 2;
+                            for (int bx = 0; bx < s.n_box; ++bx)
+                                tma_load_3d(sa + bx * box_bytes, ta, fb, it * s.kb,
+                                            m0 - s.halo_back + bx * s.box_rows, 0);
+                        } else {
+                            const int tap = it / s.n_kb, kbi = it - tap * s.n_kb;
                             tma_load_3d(sa, ta, fb, kbi * s.kb, m0 + s.off[tap], s.plane[tap]);
                             tma_load_2d(sa + p.a_region, tb, fb, tap * s.ic + kbi * s.kb, n0);
-                            inflight = min(inflight + 1, (int)S);
-                            if (++stage == S) {
-                                stage = 0;
-                                phase ^= 1;
-                            }
+                        }
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
                         }
                     }
                 }
             }
             if (!ok) {
                 // Let copies already issued land before the CTA can exit.
-                for (int i = 0; i < inflight; ++i) {
-                    stage = (stage + S - 1) % S;
-                    mbar_wait_drain(bar_full + 8 * stage, 0, 50000000ull);
-                    mbar_wait_drain(bar_full + 8 * stage, 1, 1000ull);
-                }
+                for (uint32_t i = 0; i < S; ++i) mbar_wait_drain(bar_full + 8 * i, phase, 20000000ull);
             }
         }
     } else if (warp == 1) {
@@ -254,25 +440,33 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             // ---------------- MMA issuer ----------------
             uint32_t stage = 0, phase = 0;
             uint32_t acc = 0, acc_phase = 0;
-            bool ok = true;
-            bool issued = false;
+            bool ok = true, issued = false;
+            if (p.bres_bytes &&
+                !mbar_wait(bar_bres, 0, p.err, VDB_ERR_TIMEOUT_FULL, abort_flag))
+                ok = false;
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                 const int mt = tile / p.n_nt;
-                const int m0 = mt * kBM;
-                if (!tile_live(p, m0)) continue;
+                if (!tile_live(p, stv, mt * p.BM)) continue;
                 if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1, p.err,
                                VDB_ERR_TIMEOUT_TEMPTY, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * (uint32_t)p.BN;
-                uint32_t first = 1;
+                const uint32_t d_tile = tmem_base + acc * acc_cols;
+                bool first = true;
                 for (int sg = 0; sg < p.n_seg && ok; ++sg) {
                     const SegDev& s = p.seg[sg];
+                    const bool halo = s.mode == SEG_HALO;
                     const int row_bytes = s.kb * 2;
+                    const uint32_t rb16 = (uint32_t)s.kb / 8;  // a row in 16-byte units
                     const int ksteps = s.kb / 16;
-                    const int iters = s.n_taps * s.n_kb;
+                    const int iters = halo ? s.n_kb : s.n_taps * s.n_kb;
+                    const uint64_t a_desc0 = umma_sdesc(base + p.stage0, row_bytes);
+                    const uint64_t bres_desc = umma_sdesc(base + s.bres, row_bytes);
+                    const uint32_t wp_units = (uint32_t)p.Wp * rb16;
+                    const uint32_t b_kb_units = (uint32_t)p.BN * rb16;
+                    const uint32_t b_tap_units = (uint32_t)s.n_kb * b_kb_units;
                     for (int it = 0; it < iters; ++it) {
                         if (!mbar_wait(bar_full + 8 * stage, phase, p.err, VDB_ERR_TIMEOUT_FULL,
                                        abort_flag)) {
@@ -280,14 +474,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t sa = base + stage * p.stage_bytes;
-                        const uint64_t ad = umma_sdesc(sa, row_bytes);
-                        const uint64_t bd = umma_sdesc(sa + p.a_region, row_bytes);
-                        for (int k = 0; k < ksteps; ++k) {
-                            // advance 16 f16 = 32 B along K: +2 in the (addr >> 4) field
-                            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, first ? 0u : 1u);
-                            first = 0;
-                        }
+                        const uint64_t a_desc = a_desc0 + (uint64_t)(stage * (p.stage_bytes >> 4));
+                        const uint64_t b_desc = halo ? bres_desc + (uint64_t)(it * b_kb_units)
+                                                     : a_desc + (uint64_t)(p.a_region >> 4);
+                        issue_stage<NMB, J>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc, wp_units,
+                                            rb16, b_desc, b_tap_units, idesc, first);
+                        first = false;
                         umma_commit(bar_empty + 8 * stage);
                         issued = true;
                         if (++stage == S) {
@@ -298,64 +490,55 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 }
                 if (!ok) break;
                 umma_commit(bar_tfull + 8 * acc);
-                if (++acc == 2) {
+                if (p.n_acc == 2 && ++acc == 2) {
                     acc = 0;
+                    acc_phase ^= 1;
+                } else if (p.n_acc == 1) {
                     acc_phase ^= 1;
                 }
             }
             if (!ok && issued) {
                 // Make sure no MMA is still writing TMEM before teardown.
                 const uint32_t last = (stage + S - 1) % S;
-                mbar_wait_drain(bar_empty + 8 * last, 0, 50000000ull);
-                mbar_wait_drain(bar_empty + 8 * last, 1, 1000ull);
+                mbar_wait_drain(bar_empty + 8 * last, phase ^ (stage == 0 ? 1u : 0u), 20000000ull);
             }
         }
-    } else if (warp >= 4) {
+    } else if (warp >= kEpiWarp0) {
         // ---------------- epilogue ----------------
-        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int ew = warp - kEpiWarp0;
+        const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+        const int half = ew >> 2;         // column half of the tile
+        const bool split = p.BN % 32 == 0;  // halves stay multiples of 16 columns
+        const int c_lo = split ? half * (p.BN / 2) : 0;
+        const int c_hi = split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0);
         uint32_t acc = 0, acc_phase = 0;
-        const int img = p.Hp * p.Wp;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
-            const int m0 = mt * kBM, n0 = nt * p.BN;
-            const bool live = tile_live(p, m0);
-            const int m = m0 + quad * 32 + lane;
-            bool valid = false;
-            long long dst = m;
-            if (m < p.M) {
-                const int b = m / img;
-                const int r = m - b * img;
-                const int tp = r / p.Wp;
-                const int fp = r - tp * p.Wp;
-                valid = live && tp >= 1 && tp <= p.tvalid[b] && fp >= 1 && fp <= p.F;
-                if (p.y_phase) {
-                    const int q = ((tp & 1) << 1) | (fp & 1);
-                    dst = (long long)q * p.plane_rows +
-                          ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq + (fp >> 1) + 1;
-                }
-            }
-            __half* yrow = p.y + dst * p.oc + n0;
-            const __half* rrow =
-                (p.residual && m < p.M) ? p.residual + (long long)m * p.oc + n0 : nullptr;
+            const int m0 = mt * p.BM, n0 = nt * p.BN;
+            const bool live = tile_live(p, stv, m0);
             if (live) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag))
                     break;
                 tc_fence_after();
             }
-            const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * (uint32_t)p.BN;
-            int c0 = 0;
-            for (; c0 + 32 <= p.BN; c0 += 32)
-                epi_chunk<32>(p, live, m < p.M, valid, trow + (uint32_t)c0, n0 + c0,
-                              rrow ? rrow + c0 : nullptr, yrow + c0);
-            if (c0 < p.BN)
-                epi_chunk<16>(p, live, m < p.M, valid, trow + (uint32_t)c0, n0 + c0,
-                              rrow ? rrow + c0 : nullptr, yrow + c0);
+            for (int mb = 0; mb < NMB; ++mb) {
+                const int m = m0 + mb * kMB + quad * 32 + lane;
+                const RowInfo ri = row_info(p, stv, m, live);
+                const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) +
+                                       acc * acc_cols + (uint32_t)(mb * J * p.BN);
+                if ((c_hi - c_lo) % 32 == 0)
+                    epi_rows<32, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias);
+                else
+                    epi_rows<16, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias);
+            }
             if (live) {
                 tc_fence_before();
                 mbar_arrive(bar_tempty + 8 * acc);
-                if (++acc == 2) {
+                if (p.n_acc == 2 && ++acc == 2) {
                     acc = 0;
+                    acc_phase ^= 1;
+                } else if (p.n_acc == 1) {
                     acc_phase ^= 1;
                 }
             }
@@ -376,16 +559,16 @@ CUtensorMapSwizzle swizzle_for(int kb) {
                     : (kb == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-bool make_map_a(CUtensorMap* m, const void* ptr, int C, long long rows, int planes, int kb) {
+bool make_map_a(CUtensorMap* m, const void* ptr, int C, long long rows, int planes, int kb,
+                int box_rows) {
     cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)rows, (cuuint64_t)planes};
     cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)rows * C * 2};
-    cuuint32_t box[3] = {(cuuint32_t)kb, (cuuint32_t)kBM, 1};
+    cuuint32_t box[3] = {(cuuint32_t)kb, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = encode_tiled_fn()(
-        m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-        CU_TENSOR_MAP_INTERLEAVE_NONE,
-        swizzle_for(kb),
-        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_tiled_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   swizzle_for(kb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -394,21 +577,18 @@ bool make_map_b(CUtensorMap* m, const void* ptr, int kcols, int oc, int bn, int 
     cuuint64_t strides[1] = {(cuuint64_t)kcols * 2};
     cuuint32_t box[2] = {(cuuint32_t)kb, (cuuint32_t)bn};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_tiled_fn()(
-        m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-        CU_TENSOR_MAP_INTERLEAVE_NONE,
-        swizzle_for(kb),
-        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_tiled_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   swizzle_for(kb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
-bool fill_seg(SegDev& s, int k, int stride, int ic, int Wp_out, int bn) {
+void fill_taps(SegDev& s, int k, int stride, int ic, int Wp_out) {
     s.ic = ic;
     s.kb = (ic % 64 == 0) ? 64 : ((ic % 32 == 0) ? 32 : 16);
     s.n_kb = ic / s.kb;
     s.n_taps = k * k;
-    s.kcols = s.n_taps * ic;
-    s.bytes = (uint32_t)(kBM + bn) * (uint32_t)s.kb * 2u;
     for (int kt = 0; kt < k; ++kt)
         for (int kf = 0; kf < k; ++kf) {
             const int tap = kt * k + kf;
@@ -425,8 +605,9 @@ bool fill_seg(SegDev& s, int k, int stride, int ic, int Wp_out, int bn) {
                 s.off[tap] = (kt >> 1) * Wp_out + (kf >> 1);
             }
         }
-    return true;
 }
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 }  // namespace
 }  // namespace vdb
@@ -447,12 +628,12 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: NULL args");
         return 1;
     }
-    if (a->batch <= 0 || a->t_out <= 0 || a->f_out <= 0) {
-        set_error("vdb_conv: empty output");
+    if (a->batch <= 0 || a->batch > kMaxBatch || a->t_out <= 0 || a->f_out <= 0) {
+        set_error("vdb_conv: batch must be in [1, 8192] and the output non-empty");
         return 1;
     }
-    if (a->oc % 16 != 0 || a->oc <= 0) {
-        set_error("vdb_conv: oc must be a positive multiple of 16");
+    if (a->oc % 16 != 0 || a->oc <= 0 || a->oc > 1024) {
+        set_error("vdb_conv: oc must be a positive multiple of 16 (<= 1024)");
         return 1;
     }
     if (a->ic0 % 16 != 0 || a->ic0 <= 0 || (a->x1 && (a->ic1 % 16 != 0 || a->ic1 <= 0))) {
@@ -468,6 +649,10 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: NULL buffer");
         return 1;
     }
+    if (!(a->tile_m == 0 || a->tile_m == 128 || a->tile_m == 256)) {
+        set_error("vdb_conv: tile_m must be 0 (auto), 128 or 256");
+        return 1;
+    }
     const int n_nt = (a->oc + 255) / 256;
     const int BN = a->oc / n_nt;
     if (BN % 16 != 0 || BN * n_nt != a->oc) {
@@ -477,23 +662,99 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     ConvDev p{};
     const int Hp = a->t_out + 2, Wp = a->f_out + 2;
     p.M = (int)vdb_grid_rows(a->batch, a->t_out, a->f_out);
-    p.n_mt = (p.M + kBM - 1) / kBM;
     p.n_nt = n_nt;
     p.BN = BN;
     p.n_seg = a->x1 ? 2 : 1;
-    fill_seg(p.seg[0], a->k0, a->stride0, a->ic0, Wp, BN);
-    if (a->x1) fill_seg(p.seg[1], 1, a->stride1, a->ic1, Wp, BN);
-    int kbmax = p.seg[0].kb;
-    if (a->x1) kbmax = std::max(kbmax, p.seg[1].kb);
-    p.a_region = (uint32_t)kBM * kbmax * 2;
-    p.stage_bytes = p.a_region + (uint32_t)BN * kbmax * 2;
-    p.n_stages = std::min<uint32_t>(kMaxStages, kSmemBudget / p.stage_bytes);
-    if (p.n_stages < 2) {
-        set_error("vdb_conv: stage does not fit in shared memory");
+    fill_taps(p.seg[0], a->k0, a->stride0, a->ic0, Wp);
+    if (a->x1) fill_taps(p.seg[1], 1, a->stride1, a->ic1, Wp);
+
+    // HALO for stride-1 3x3 segments whose weights fit in shared memory.
+    const uint32_t w_bytes0 = (uint32_t)9 * a->ic0 * BN * 2;
+    const bool halo_ok = a->k0 == 3 && a->stride0 == 1 && n_nt == 1 && w_bytes0 <= 96 * 1024;
+    const bool halo = a->halo == 0 ? halo_ok : (a->halo > 0 && halo_ok);
+    if (a->halo > 0 && !halo_ok) {
+        set_error("vdb_conv: HALO mode needs a stride-1 3x3 conv with oc <= 256 and weights <= 96 KB");
         return 1;
     }
+    // Tiling. A tcgen05.mma that accumulates into the same TMEM tile as the one
+    // before it waits for it (~180 cycles per MMA on B200), while independent
+    // accumulators overlap down to ~60 cycles per MMA. So the tile carries
+    // n_mblk * J independent f32 accumulators (row blocks x K-split partials,
+    // summed in the epilogue), double-buffered when TMEM's 512 columns allow.
+    // tile_m = 256 also halves the weight traffic per output row.
+    int BM = a->tile_m;
+    if (BM == 0) BM = 256;
+    if ((BM / kMB) * BN > 512) BM = kMB;
+    const int nmb = BM / kMB;
+    const int ks0 = p.seg[0].kb / 16;  // MMA K-steps per stage of segment 0
+    // Measured on the ResNet34 shapes (batch 64): two 128-row blocks already give
+    // the issuer two independent chains, and extra K partials cost more in the
+    // epilogue than they save, so the automatic choice is J = 1.
+    int J = a->ksplit;
+    if (J == 0) J = 1;
+    if (!(J == 1 || J == 2 || J == 4 || J == 8) || nmb * J * BN > 512) {
+        set_error("vdb_conv: ksplit must be 1, 2, 4 or 8 and tile_m/128 * ksplit * N <= 512");
+        return 1;
+    }
+    if (!halo && J > ks0) {
+        set_error("vdb_conv: ksplit may not exceed the K-steps per stage (channel block / 16)");
+        return 1;
+    }
+    p.BM = BM;
+    p.n_mblk = BM / kMB;
+    p.J = J;
+    p.n_acc = (2 * p.n_mblk * J * BN <= 512) ? 2 : 1;
+    p.n_mt = (p.M + BM - 1) / BM;
+
+    uint32_t off = 0;
+    p.bres_bytes = 0;
+    uint32_t a_bytes = 0, b_bytes = 0;
+    for (int sg = 0; sg < p.n_seg; ++sg) {
+        SegDev& s = p.seg[sg];
+        const uint32_t row_bytes = (uint32_t)s.kb * 2;
+        if (sg == 0 && halo) {
+            s.mode = SEG_HALO;
+            const int H = BM + 2 * Wp + 2;
+            s.halo_back = Wp + 1;
+            s.n_box = (H + 255) / 256;
+            s.box_rows = round_up((H + s.n_box - 1) / s.n_box, 8);
+            for (int t = 0; t < 9; ++t) s.off[t] = (t / 3) * Wp + (t % 3);  // kt*Wp + kf
+            s.bytes = (uint32_t)s.n_box * s.box_rows * row_bytes;
+            s.bres = off;
+            const uint32_t w = (uint32_t)9 * s.n_kb * BN * row_bytes;
+            off += w;
+            p.bres_bytes += w;
+            a_bytes = std::max(a_bytes, s.bytes);
+        } else {
+            s.mode = SEG_TAP;
+            s.bytes = (uint32_t)(BM + BN) * row_bytes;
+            a_bytes = std::max(a_bytes, (uint32_t)BM * row_bytes);
+            b_bytes = std::max(b_bytes, (uint32_t)BN * row_bytes);
+        }
+    }
+    off = (uint32_t)round_up((int)off, 1024);
+    p.stage0 = off;
+    p.a_region = (uint32_t)round_up((int)a_bytes, 1024);
+    p.stage_bytes = p.a_region + (uint32_t)round_up((int)b_bytes, 1024);
+    const uint32_t tail = (uint32_t)round_up(a->oc * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
+                          8 * (2 * kMaxStages + 5) + 16;
+    const int budget = kSmemMax - 1024 - (int)off - (int)tail;
+    p.n_stages = (uint32_t)std::min<int>(kMaxStages, budget / (int)p.stage_bytes);
+    if (p.n_stages < 2) {
+        set_error("vdb_conv: tile does not fit in shared memory");
+        return 1;
+    }
+    off += p.n_stages * p.stage_bytes;
+    p.bias_off = off;
+    off += (uint32_t)round_up(a->oc * 4, 16);
+    p.tv_off = off;
+    off += (uint32_t)round_up(a->batch * 4, 16);
+    p.bar_off = (uint32_t)round_up((int)off, 8);
+    off = p.bar_off + 8 * (2 * p.n_stages + 5) + 16;
+    const size_t smem = (size_t)off + 1024;
+
     uint32_t cols = 32;
-    while (cols < 2u * (uint32_t)BN) cols <<= 1;
+    while (cols < (uint32_t)(p.n_acc * p.n_mblk * J * BN)) cols <<= 1;
     p.tmem_cols = cols;
     p.bias = a->bias;
     p.residual = static_cast<const __half*>(a->residual);
@@ -507,6 +768,7 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     p.Wq = (a->f_out - 1) / 2 + 1 + 2;
     p.plane_rows = (long long)a->batch * p.Hq * p.Wq;
     p.tvalid = a->tvalid;
+    p.batch = a->batch;
     p.relu = a->relu;
     p.clamp_hi = a->clamp_hi;
     p.oc = a->oc;
@@ -515,43 +777,47 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     // Input row extents: stride 1 reads G(B, t_out, f_out); stride 2 reads the
     // 4 planes of a PHASE tensor, each shaped like the output grid.
     const long long rows_out = p.M;
-    CUtensorMap tmA0, tmB0, tmA1, tmB1;
-    if (!make_map_a(&tmA0, a->x0, a->ic0, rows_out, a->stride0 == 2 ? 4 : 1, p.seg[0].kb) ||
-        !make_map_b(&tmB0, a->w0, p.seg[0].kcols, a->oc, BN, p.seg[0].kb)) {
-        set_error("vdb_conv: cuTensorMapEncodeTiled failed (segment 0)");
-        return 1;
-    }
-    if (a->x1) {
-        if (!make_map_a(&tmA1, a->x1, a->ic1, rows_out, a->stride1 == 2 ? 4 : 1,
-                        p.seg[1].kb) ||
-            !make_map_b(&tmB1, a->w1, p.seg[1].kcols, a->oc, BN, p.seg[1].kb)) {
-            set_error("vdb_conv: cuTensorMapEncodeTiled failed (segment 1)");
+    CUtensorMap tm[4];
+    for (int sg = 0; sg < p.n_seg; ++sg) {
+        const SegDev& s = p.seg[sg];
+        const void* x = sg ? a->x1 : a->x0;
+        const void* w = sg ? a->w1 : a->w0;
+        const int stride = sg ? a->stride1 : a->stride0;
+        const int box_rows = s.mode == SEG_HALO ? s.box_rows : BM;
+        if (!make_map_a(&tm[2 * sg], x, s.ic, rows_out, stride == 2 ? 4 : 1, s.kb, box_rows) ||
+            !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, BN, s.kb)) {
+            set_error("vdb_conv: cuTensorMapEncodeTiled failed");
             return 1;
         }
-    } else {
-        tmA1 = tmA0;
-        tmB1 = tmB0;
     }
-    // stages + 1 KB alignment slack + barriers (2S + 4) * 8 B + TMEM slot / abort flag
-    const size_t smem = (size_t)p.n_stages * p.stage_bytes + 1024 + (2 * p.n_stages + 4) * 8 + 16;
-    static bool attr_set = false;
-    if (!attr_set) {
-        VDB_CHECK_CUDA(cudaFuncSetAttribute(conv_tc_kernel,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            227 * 1024));
-        attr_set = true;
+    if (p.n_seg == 1) {
+        tm[2] = tm[0];
+        tm[3] = tm[1];
     }
-    // TMEM: more than 256 columns per CTA must not share an SM with another CTA.
-    size_t smem_launch = smem;
-    if (p.tmem_cols > 256) smem_launch = std::max<size_t>(smem, 120 * 1024);
-    int occ = 1;
-    VDB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, conv_tc_kernel, kThreads,
-                                                                  smem_launch));
-    occ = std::max(1, std::min(occ, (int)(512 / p.tmem_cols)));
+    // One CTA per SM: more than 256 TMEM columns, or most of shared memory.
+    const size_t smem_launch = std::max<size_t>(smem, 120 * 1024);
     const int n_tiles = p.n_mt * p.n_nt;
-    const int grid = std::max(1, std::min(n_tiles, num_sms() * occ));
-    conv_tc_kernel<<<grid, kThreads, smem_launch, static_cast<cudaStream_t>(stream)>>>(
-        tmA0, tmB0, tmA1, tmB1, p);
-    VDB_CHECK_CUDA(cudaGetLastError());
-    return 0;
+    const int grid = std::max(1, std::min(n_tiles, num_sms()));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto launch = [&](auto kern) -> int {
+        VDB_CHECK_CUDA(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        kern<<<grid, kThreads, smem_launch, st>>>(tm[0], tm[1], tm[2], tm[3], p);
+        VDB_CHECK_CUDA(cudaGetLastError());
+        return 0;
+    };
+    const int key = p.n_mblk * 100 + J;
+    switch (key) {
+        case 101: return launch(conv_tc_kernel<1, 1>);
+        case 102: return launch(conv_tc_kernel<1, 2>);
+        case 104: return launch(conv_tc_kernel<1, 4>);
+        case 108: return launch(conv_tc_kernel<1, 8>);
+        case 201: return launch(conv_tc_kernel<2, 1>);
+        case 202: return launch(conv_tc_kernel<2, 2>);
+        case 204: return launch(conv_tc_kernel<2, 4>);
+        case 208: return launch(conv_tc_kernel<2, 8>);
+        default:
+            set_error("vdb_conv: ksplit must be 1, 2, 4 or 8");
+            return 1;
+    }
 }

@@ -39,7 +39,8 @@ class ConvArgs(C.Structure):
         ("stride1", C.c_int), ("ic1", C.c_int), ("x1", C.c_void_p), ("w1", C.c_void_p),
         ("bias", C.c_void_p), ("residual", C.c_void_p), ("relu", C.c_int),
         ("clamp_hi", C.c_float), ("tvalid", C.c_void_p), ("y", C.c_void_p),
-        ("y_phase", C.c_int), ("err", C.c_void_p),
+        ("y_phase", C.c_int), ("err", C.c_void_p), ("tile_m", C.c_int), ("halo", C.c_int),
+        ("ksplit", C.c_int),
     ]
 
 
@@ -335,7 +336,7 @@ def pack_conv_weight(w):
 
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
-         y=None, y_phase=False, err=None, stream=None):
+         y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0):
     """vdb_conv on device tensors. x0/x1/residual/y are f16 GRID or PHASE tensors,
     w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,), tvalid int32 (B,)."""
     import torch
@@ -352,7 +353,8 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  residual=residual.data_ptr() if residual is not None else None,
                  relu=int(relu), clamp_hi=float(clamp_hi), tvalid=tvalid.data_ptr(),
                  y=y.data_ptr(), y_phase=int(y_phase),
-                 err=err.data_ptr() if err is not None else None)
+                 err=err.data_ptr() if err is not None else None, tile_m=tile_m, halo=halo,
+                 ksplit=ksplit)
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
