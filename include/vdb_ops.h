@@ -113,6 +113,25 @@ int vdb_cmn_stem(const float* feats, const int* frames, int batch, int t_max, in
                  int cmn, const float* stem_w, const float* stem_b, int oc,
                  float* mean_scratch, void* y, void* stream);
 
+/* The same CMN + stem as vdb_cmn_stem, for callers that cannot allocate device
+ * memory: no counterpart exists in the reference. A streaming audio callback must
+ * not call cudaMalloc/cudaFree (they can stall the whole device for an unbounded
+ * time), and a host that manages all device memory through its own pool does not
+ * let a library allocate behind its back. This entry point allocates nothing: the
+ * per-clip CMN means go to a fixed array inside the library (65536 floats,
+ * 256 KB, held on every GPU that loads the library until the process exits).
+ *   - batch * n_mels must be <= 65536; larger calls fail with a clear error
+ *     (use vdb_cmn_stem with caller-provided memory instead).
+ *   - The first call on each device looks up the array's device address; make
+ *     that first call before any stream capture.
+ *   - Every call uses the same array, and each call overwrites every entry it
+ *     reads, so nothing carries over between calls. Calls whose kernels overlap
+ *     on the GPU (concurrent streams, or threads sharing a device) race on the
+ *     array: serialise them. */
+int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                         int cmn, const float* stem_w, const float* stem_b, int oc, void* y,
+                         void* stream);
+
 /* Temporal statistics pooling + embedding FC + L2 normalisation, one CTA per clip.
  * x: G(batch, t, f, c) f16 final backbone activation; tvalid: device int32 [batch]
  * valid time extent. pooled[c*f + h] = mean, pooled[c*f*... + c*f + h] = std

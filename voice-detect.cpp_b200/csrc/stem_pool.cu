@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <mutex>
+#include <string>
 
 #include "vdb_internal.h"
 #include "vdb_ops.h"
@@ -237,6 +239,87 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
             set_error("vdb_cmn_stem: stem channels must be 16, 32 or 64");
             return 1;
     }
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+// ---- CMN + stem without any allocation ---------------------------------------
+// vdb_cmn_stem needs working memory for the per-clip CMN means and asks the caller
+// for it. Some callers cannot provide or allocate it: a streaming audio callback
+// must not call cudaMalloc/cudaFree (they can synchronise the whole device and
+// take unbounded time), and a host that owns all device memory through its own
+// pool does not allow a library to allocate behind its back. For them the means
+// live in this fixed array, compiled into the library, which every GPU that loads
+// the library holds until the process exits.
+namespace {
+constexpr int kNoAllocMaxMeans = 65536;  // batch * n_mels (256 KB of f32)
+static __device__ __align__(256) float g_cmn_means[kNoAllocMaxMeans];
+constexpr int kMaxDevices = 64;
+std::once_flag g_means_once[kMaxDevices];
+float* g_means_addr[kMaxDevices] = {};
+cudaError_t g_means_status[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int batch, int t_max,
+                                    int n_mels, int cmn, const float* stem_w,
+                                    const float* stem_b, int oc, void* y, void* stream) {
+    if (!feats || !frames || !stem_w || !stem_b || !y) {
+        set_error("vdb_cmn_stem_noalloc: NULL argument");
+        return 1;
+    }
+    if (batch <= 0 || t_max <= 0 || n_mels <= 0 || n_mels > 128) {
+        set_error("vdb_cmn_stem_noalloc: bad shape");
+        return 1;
+    }
+    if ((long long)batch * n_mels > kNoAllocMaxMeans) {
+        set_error("vdb_cmn_stem_noalloc: batch * n_mels = " +
+                  std::to_string((long long)batch * n_mels) +
+                  " exceeds the built-in limit of 65536 (use vdb_cmn_stem with caller memory)");
+        return 1;
+    }
+    if (!(oc == 16 || oc == 32 || oc == 64)) {
+        set_error("vdb_cmn_stem_noalloc: stem channels must be 16, 32 or 64");
+        return 1;
+    }
+    int dev = 0;
+    VDB_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("vdb_cmn_stem_noalloc: device ordinal out of range");
+        return 1;
+    }
+    // First call on this device (with it current): look up the array's device
+    // address. A host-side reference to g_cmn_means is not a device address.
+    std::call_once(g_means_once[dev], [dev] {
+        void* p = nullptr;
+        g_means_status[dev] = cudaGetSymbolAddress(&p, g_cmn_means);
+        g_means_addr[dev] = static_cast<float*>(p);
+    });
+    if (g_means_status[dev] != cudaSuccess || !g_means_addr[dev]) {
+        set_error(std::string("vdb_cmn_stem_noalloc: cudaGetSymbolAddress failed: ") +
+                  cudaGetErrorString(g_means_status[dev]));
+        return 1;
+    }
+    float* means = g_means_addr[dev];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The mean kernel writes every entry the stem kernel reads, so the array's
+    // previous contents never leak into a result.
+    if (cmn) {
+        cmn_mean_kernel<<<batch, dim3(128, 4), 0, st>>>(feats, frames, t_max, n_mels, means);
+        VDB_CHECK_CUDA(cudaGetLastError());
+    }
+    const long long rows = vdb_grid_rows(batch, t_max, n_mels);
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((rows + threads - 1) / threads);
+    __half* yh = static_cast<__half*>(y);
+    if (oc == 16)
+        stem_kernel<16><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
+                                                    cmn, stem_w, stem_b, yh);
+    else if (oc == 32)
+        stem_kernel<32><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
+                                                    cmn, stem_w, stem_b, yh);
+    else
+        stem_kernel<64><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
+                                                    cmn, stem_w, stem_b, yh);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }
