@@ -42,6 +42,9 @@ CLIPS_PER_GPU = 8192
 POOL = 64            # distinct synthetic sources the clips are cut from
 SEED = 20261201
 METRIC = "utterance-sec/sec ResNet34 embed"
+# DRAM bytes (read + write) per algorithmic conv FLOP, measured with ncu on this
+# workload at the same bucket sizes (see profiles/launches__bench_c4_512clips.md).
+CONV_DRAM_BYTES_PER_FLOP = 4.55e-3
 UNIT = "utterance-sec/sec"
 
 
@@ -72,6 +75,30 @@ def lpt_shard(lengths: np.ndarray, world: int) -> list[list[int]]:
         load[r] += lengths[i]
         cnt[r] += 1
     return shards
+
+
+def gather_embeddings(local, gathered, world: int) -> None:
+    """The path's only collective: every rank's [n_max, D] embeddings into
+    `gathered` [world * n_max, D], rank-major (NCCL on GPUs, gloo on CPU)."""
+    import torch.distributed as dist
+    if world == 1:
+        gathered.copy_(local)
+    elif dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(gathered, local)
+    else:
+        dist.all_gather(list(gathered.chunk(world)), local)
+
+
+def restore_order(gathered, shards: list[list[int]], n_max: int):
+    """Rank-major gathered rows -> rows in original clip order."""
+    import torch
+    idx = torch.tensor([i for s in shards for i in s], dtype=torch.long)
+    rows = torch.tensor([r * n_max + k for r, s in enumerate(shards) for k in range(len(s))],
+                        dtype=torch.long)
+    out = torch.empty((len(idx), gathered.shape[1]), dtype=gathered.dtype,
+                      device=gathered.device)
+    out[idx.to(out.device)] = gathered[rows.to(out.device)]
+    return out
 
 
 def clip_of(pool, idx: int, n: int) -> np.ndarray:
@@ -244,10 +271,7 @@ def run_b200(args) -> int:
 
     def step():
         model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, d_out)
-        else:
-            gathered.copy_(d_out)
+        gather_embeddings(d_out, gathered, world)
 
     for _ in range(args.warmup):
         step()
@@ -319,7 +343,12 @@ def run_b200(args) -> int:
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
                      if peaks else "fallback 1.4 PFLOP/s sustained",
-                     "traffic": None, "conv_launches": conv_n,
+                     "traffic": (CONV_DRAM_BYTES_PER_FLOP * conv_flops / conv_n) if conv_n else None,
+                     "traffic_unit": "bytes per conv launch (dram read+write)",
+                     "traffic_source": "ncu capture summarised in "
+                                       "profiles/launches__bench_c4_512clips.md, scaled by "
+                                       "this run's FLOPs per launch",
+                     "conv_launches": conv_n,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "clocks": clk,
