@@ -67,7 +67,7 @@ typedef struct vdb_conv_args {
     const void* x1;
     const void* w1;     /* device f16 [oc][ic1] */
     /* epilogue: y = act(acc + bias [+ residual]) at valid pixels, 0 elsewhere */
-    const float* bias;      /* device f32 [oc] (sum of both segments' biases) */
+    const float* bias;      /* device f32 [oc] (sum of both segments' biases), or NULL */
     const void* residual;   /* device f16 G(B, t_out, f_out, oc) or NULL */
     int relu;               /* 1: max(0, .) */
     float clamp_hi;         /* > 0: min(., clamp_hi) after ReLU (Hardtanh(0, hi)) */
@@ -81,6 +81,18 @@ typedef struct vdb_conv_args {
                                feeding all nine taps (stride-1 3x3, weights resident) */
     int ksplit;             /* 0 auto, else 1..16 independent partial accumulators per
                                128-row block, summed in the epilogue */
+    /* channel slices and extra epilogue inputs / outputs (all 0 / NULL = off) */
+    int ldx0, ldx1;         /* row pitch (elements) of x0 / x1 when they are channel
+                               slices of wider tensors (0 = ic0 / ic1); the pointer then
+                               points at the slice's first channel (16-byte aligned) */
+    int ldy;                /* row pitch of y (0 = oc): y may be a channel slice */
+    void* y2;               /* optional second output, P(B, t_out, f_out, oc) layout */
+    int ldr;                /* row pitch of residual (0 = oc) */
+    const void* residual2;  /* second epilogue input (GRID, pitch ldr2) for act = 2 */
+    int ldr2;
+    int act;                /* 0: [+residual] -> ReLU/clamp flags; 1: SiLU;
+                               2: attentional fusion (x + ds) + tanh(acc + bias) * (x - ds)
+                               with x = residual, ds = residual2 */
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */
@@ -142,6 +154,13 @@ int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int batch, int t
 int vdb_pool_embed(const void* x, const int* tvalid, int batch, int t, int f, int c,
                    const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
                    float var_eps, int l2, float* emb_out, float* prenorm_out, void* stream);
+
+/* y = a + b over `rows` rows of C f16 channels, each operand with its own row
+ * pitch in elements (channel slices allowed; pitches and C multiples of 8, pointers
+ * 16-byte aligned). The Res2Net chunk fusion sp + x_i (ggml_add in
+ * src/encoder_eres2net.cpp:126) on GRID tensors, borders included. */
+int vdb_add(const void* a, int lda, const void* b, int ldb, void* y, int ldy, long long rows,
+            int C, void* stream);
 
 /* Top-k cosine search (no reference counterpart exists; the additive C ABI
  * voicedetect_capi_identify calls it). q: device f32 [n_q][dim]; reg: device f32

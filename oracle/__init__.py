@@ -319,6 +319,90 @@ class RefResNet34:
         return emb, pre
 
 
+# ---------------------------------------------------------------------------
+# ERes2Net end to end
+# ---------------------------------------------------------------------------
+class ERes2NetDesc(C.Structure):
+    _fields_ = [
+        ("n_convs", C.c_int), ("w", C.POINTER(_f32p)), ("b", C.POINTER(_f32p)),
+        ("ic", _i32p), ("oc", _i32p), ("k", _i32p), ("stride", _i32p),
+        ("num_blocks", C.c_int * 4), ("m_channels", C.c_int), ("scale", C.c_int),
+        ("relu_clamp", C.c_float), ("seg_w", _f32p), ("seg_b", _f32p), ("emb_dim", C.c_int),
+        ("pooled_dim", C.c_int), ("var_eps", C.c_float), ("l2_normalize", C.c_int),
+    ]
+
+
+class _EDescHolder:
+    def __init__(self, m: dict):
+        self.keep = []
+
+        def f(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a, np.float32)
+            self.keep.append(a)
+            return _fp(a)
+
+        cv = m["convs"]
+        n = len(cv)
+        self.w = (_f32p * n)(*[f(c["w"]) for c in cv])
+        self.b = (_f32p * n)(*[f(c["b"]) for c in cv])
+        self.ic = (C.c_int * n)(*[c["w"].shape[1] for c in cv])
+        self.oc = (C.c_int * n)(*[c["w"].shape[0] for c in cv])
+        self.k = (C.c_int * n)(*[c["w"].shape[2] for c in cv])
+        self.st = (C.c_int * n)(*[c["stride"] for c in cv])
+        seg_w = m["seg_w"]
+        self.desc = ERes2NetDesc(
+            n_convs=n, w=self.w, b=self.b, ic=self.ic, oc=self.oc, k=self.k, stride=self.st,
+            num_blocks=(C.c_int * 4)(*m["num_blocks"]), m_channels=m["m_channels"],
+            scale=m["scale"], relu_clamp=float(m["relu_clamp"]), seg_w=f(seg_w),
+            seg_b=f(m["seg_b"]), emb_dim=seg_w.shape[0], pooled_dim=seg_w.shape[1],
+            var_eps=float(m["var_eps"]), l2_normalize=int(m.get("l2_normalize", True)))
+
+
+def eres2net_embed(model: dict, feats: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """C restatement of ERes2NetEncoder::forward_capture -> (embedding, pre_norm)."""
+    h = _EDescHolder(model)
+    L = lib()
+    L.vdo_eres2net_forward.restype = C.c_int
+    L.vdo_eres2net_forward.argtypes = [C.POINTER(ERes2NetDesc), _f32p, C.c_int, C.c_int, _f32p,
+                                       _f32p]
+    feats = np.ascontiguousarray(feats, np.float32)
+    n_mels, T = feats.shape
+    D = h.desc.emb_dim
+    emb = np.zeros(D, np.float32)
+    pre = np.zeros(D, np.float32)
+    rc = L.vdo_eres2net_forward(C.byref(h.desc), _fp(feats), T, n_mels, _fp(emb), _fp(pre))
+    if rc != 0:
+        raise RuntimeError(f"vdo_eres2net_forward rc={rc}")
+    return emb, pre
+
+
+class RefERes2Net:
+    """The reference's blocked conv kernels + restated ERes2Net glue."""
+
+    def __init__(self, model: dict):
+        self._h = _EDescHolder(model)
+        L = ref_lib()
+        L.vdref_eres2net_new.restype = C.c_void_p
+        L.vdref_eres2net_new.argtypes = [C.POINTER(ERes2NetDesc)]
+        L.vdref_eres2net_forward.restype = C.c_int
+        L.vdref_eres2net_forward.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int, _f32p, _f32p]
+        self.emb_dim = self._h.desc.emb_dim
+        self.handle = L.vdref_eres2net_new(C.byref(self._h.desc))
+
+    def embed(self, feats: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        feats = np.ascontiguousarray(feats, np.float32)
+        n_mels, T = feats.shape
+        emb = np.zeros(self.emb_dim, np.float32)
+        pre = np.zeros(self.emb_dim, np.float32)
+        rc = ref_lib().vdref_eres2net_forward(self.handle, _fp(feats), T, n_mels, _fp(emb),
+                                              _fp(pre))
+        if rc != 0:
+            raise RuntimeError(f"vdref_eres2net_forward rc={rc}")
+        return emb, pre
+
+
 def resample_linear(pcm: np.ndarray, in_sr: int, out_sr: int = 16000) -> np.ndarray:
     pcm = np.ascontiguousarray(pcm, np.float32)
     n_out = lib().vdo_resample_linear(_fp(pcm), len(pcm), in_sr, out_sr, None, 0)

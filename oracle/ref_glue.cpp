@@ -286,3 +286,207 @@ int vdref_resnet34_forward(void* handle, const float* feats, int T, int n_mels, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// ERes2Net forward on the reference kernels: the stem through directconv_conv3x3
+// + bias + ReLU, every body conv through the blocked island ops
+// (blocked_conv1x1 / blocked_conv3x3 with fused bias, src/encoder_eres2net.cpp:44-50).
+// The elementwise glue (clamp, split, concat, add, SiLU, tanh, AFF mix) and the
+// tail are restated from src/encoder_eres2net.cpp:60-264.
+// ---------------------------------------------------------------------------
+struct RefERes2Net {
+    vd_eres2net_desc d{};
+    std::vector<float*> w, b;
+    std::vector<int> ic, oc, k, st;
+    float* seg_w = nullptr;
+    float* seg_b = nullptr;
+};
+
+struct RAct {
+    std::vector<float> v;
+    int C = 0, H = 0, W = 0;
+    size_t hw() const { return (size_t)H * W; }
+};
+
+struct REnc {
+    RefERes2Net* m;
+    int idx = 0;
+
+    RAct conv(const RAct& x) {
+        const int i = idx++;
+        const int k = m->k[i], s = m->st[i], OC = m->oc[i];
+        Ctx ctx;
+        ggml_tensor* xt = shim_wrap_f32(ctx.c, const_cast<float*>(x.v.data()), x.W, x.H, x.C, 1);
+        ggml_tensor* wt = shim_wrap_f32(ctx.c, m->w[i], k, k, x.C, OC);
+        ggml_tensor* bt = m->b[i] ? shim_wrap_f32(ctx.c, m->b[i], OC, 1, 1, 1) : nullptr;
+        ggml_tensor* xb = vd::blocked_reorder_in(ctx.c, xt);
+        ggml_tensor* yb = (k == 1) ? vd::blocked_conv1x1(ctx.c, wt, xb, s, bt, false)
+                                   : vd::blocked_conv3x3(ctx.c, wt, xb, (k - 1) / 2, s, bt, false);
+        ggml_tensor* yt = vd::blocked_reorder_out(ctx.c, yb, OC);
+        RAct y;
+        y.C = OC;
+        y.W = (int)yt->ne[0];
+        y.H = (int)yt->ne[1];
+        y.v.assign((const float*)yt->data, (const float*)yt->data + ggml_nelements(yt));
+        return y;
+    }
+    void clamp(RAct& a) {
+        const float hi = m->d.relu_clamp;
+        for (float& v : a.v) v = v < 0.0f ? 0.0f : (v > hi ? hi : v);
+    }
+    RAct aff(const RAct& x, const RAct& ds) {
+        RAct cat;
+        cat.C = x.C + ds.C;
+        cat.H = x.H;
+        cat.W = x.W;
+        cat.v = x.v;
+        cat.v.insert(cat.v.end(), ds.v.begin(), ds.v.end());
+        RAct z = conv(cat);
+        for (float& v : z.v) v = v / (1.0f + std::exp(-v));
+        RAct z2 = conv(z);
+        RAct out = x;
+        for (size_t i = 0; i < out.v.size(); ++i) {
+            const float att = std::tanh(z2.v[i]);
+            out.v[i] = (x.v[i] + ds.v[i]) + att * (x.v[i] - ds.v[i]);
+        }
+        return out;
+    }
+    RAct block(const RAct& x, int planes, int stride, bool is_aff, int& in_planes) {
+        const int scale = m->d.scale;
+        RAct out = conv(x);
+        clamp(out);
+        const int width = out.C / scale;
+        const size_t hw = out.hw();
+        RAct accum;
+        accum.C = out.C;
+        accum.H = out.H;
+        accum.W = out.W;
+        accum.v.assign(out.v.size(), 0.0f);
+        RAct sp;
+        for (int i = 0; i < scale; ++i) {
+            RAct chunk;
+            chunk.C = width;
+            chunk.H = out.H;
+            chunk.W = out.W;
+            chunk.v.assign(out.v.begin() + (size_t)i * width * hw,
+                           out.v.begin() + (size_t)(i + 1) * width * hw);
+            RAct cur;
+            if (i == 0) cur = chunk;
+            else if (is_aff) cur = aff(sp, chunk);
+            else {
+                cur = chunk;
+                for (size_t j = 0; j < cur.v.size(); ++j) cur.v[j] = sp.v[j] + chunk.v[j];
+            }
+            RAct cv = conv(cur);
+            clamp(cv);
+            std::copy(cv.v.begin(), cv.v.end(), accum.v.begin() + (size_t)i * width * hw);
+            sp = cv;
+        }
+        RAct o3 = conv(accum);
+        if (stride != 1 || in_planes != 2 * planes) {
+            RAct r = conv(x);
+            for (size_t j = 0; j < o3.v.size(); ++j) o3.v[j] += r.v[j];
+        } else {
+            for (size_t j = 0; j < o3.v.size(); ++j) o3.v[j] += x.v[j];
+        }
+        in_planes = 2 * planes;
+        clamp(o3);
+        return o3;
+    }
+    RAct layer(RAct x, int planes, int n, int stride, bool is_aff, int& in_planes) {
+        for (int bi = 0; bi < n; ++bi) x = block(x, planes, bi == 0 ? stride : 1, is_aff, in_planes);
+        return x;
+    }
+};
+
+extern "C" {
+
+void* vdref_eres2net_new(const vd_eres2net_desc* d) {
+    RefERes2Net* m = new RefERes2Net();
+    m->d = *d;
+    for (int i = 0; i < d->n_convs; ++i) {
+        m->ic.push_back(d->ic[i]);
+        m->oc.push_back(d->oc[i]);
+        m->k.push_back(d->k[i]);
+        m->st.push_back(d->stride[i]);
+        m->w.push_back(stable_copy(d->w[i], (size_t)d->oc[i] * d->ic[i] * d->k[i] * d->k[i]));
+        m->b.push_back(d->b[i] ? stable_copy(d->b[i], (size_t)d->oc[i]) : nullptr);
+    }
+    m->seg_w = stable_copy(d->seg_w, (size_t)d->emb_dim * d->pooled_dim);
+    m->seg_b = stable_copy(d->seg_b, (size_t)d->emb_dim);
+    return m;
+}
+
+int vdref_eres2net_forward(void* handle, const float* feats, int T, int n_mels, float* emb,
+                           float* prenorm) {
+    RefERes2Net* m = (RefERes2Net*)handle;
+    REnc e{m};
+    const int M = m->d.m_channels;
+    // stem: directconv_conv3x3 -> + bias -> ReLU (:203)
+    RAct h;
+    {
+        Ctx ctx;
+        ggml_tensor* x = shim_wrap_f32(ctx.c, const_cast<float*>(feats), T, n_mels, 1, 1);
+        ggml_tensor* sw = shim_wrap_f32(ctx.c, m->w[0], 3, 3, 1, m->oc[0]);
+        ggml_tensor* y = vd::directconv_conv3x3(ctx.c, sw, x, 1);
+        add_bias_relu_nchw((float*)y->data, T, n_mels, m->oc[0], m->b[0], true);
+        h.C = m->oc[0];
+        h.H = n_mels;
+        h.W = T;
+        h.v.assign((const float*)y->data, (const float*)y->data + ggml_nelements(y));
+        e.idx = 1;
+    }
+    int in_planes = M;
+    const int* nb = m->d.num_blocks;
+    RAct o1 = e.layer(h, M, nb[0], 1, false, in_planes);
+    RAct o2 = e.layer(o1, 2 * M, nb[1], 2, false, in_planes);
+    RAct o1d = e.conv(o1);
+    RAct f12 = e.aff(o2, o1d);
+    RAct o3 = e.layer(o2, 4 * M, nb[2], 2, true, in_planes);
+    RAct f12d = e.conv(f12);
+    RAct f123 = e.aff(o3, f12d);
+    RAct o4 = e.layer(o3, 8 * M, nb[3], 2, true, in_planes);
+    RAct f123d = e.conv(f123);
+    RAct f = e.aff(o4, f123d);
+    if (e.idx != m->d.n_convs) return 4;
+    // TSTP + seg FC + L2 (:228-262), same restatement as the ResNet tail
+    const int C = f.C, Hp = f.H, Wp = f.W, HC = Hp * C;
+    if (2 * HC != m->d.pooled_dim) return 3;
+    std::vector<float> pooled((size_t)2 * HC);
+    for (int c = 0; c < C; ++c)
+        for (int hh = 0; hh < Hp; ++hh) {
+            const float* row = f.v.data() + ((size_t)c * Hp + hh) * Wp;
+            double s = 0.0;
+            for (int w = 0; w < Wp; ++w) s += row[w];
+            const float mean = (float)(s / Wp);
+            double s2 = 0.0;
+            for (int w = 0; w < Wp; ++w) {
+                const float dv = row[w] - mean;
+                s2 += (double)(dv * dv);
+            }
+            float var = (float)(s2 / Wp);
+            if (Wp > 1) var = var * ((float)Wp / (float)(Wp - 1));
+            pooled[(size_t)c * Hp + hh] = mean;
+            pooled[(size_t)HC + (size_t)c * Hp + hh] = std::sqrt(var + m->d.var_eps);
+        }
+    const int D = m->d.emb_dim;
+    std::vector<float> out((size_t)D);
+    for (int j = 0; j < D; ++j) {
+        const float* wr = m->seg_w + (size_t)j * m->d.pooled_dim;
+        double acc = 0.0;
+        for (int i = 0; i < m->d.pooled_dim; ++i) acc += (double)wr[i] * (double)pooled[i];
+        out[j] = (float)acc + m->seg_b[j];
+    }
+    if (prenorm) std::memcpy(prenorm, out.data(), out.size() * sizeof(float));
+    if (m->d.l2_normalize) {
+        double n2 = 0.0;
+        for (float v : out) n2 += (double)v * (double)v;
+        const double nrm = std::sqrt(n2);
+        if (nrm > 0.0)
+            for (float& v : out) v = (float)((double)v / nrm);
+    }
+    std::memcpy(emb, out.data(), out.size() * sizeof(float));
+    return 0;
+}
+
+}  // extern "C"

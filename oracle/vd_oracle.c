@@ -313,3 +313,206 @@ void vdo_identify(const float* q, int n_q, const float* reg, int n_reg, int dim,
     }
     free(rn);
 }
+
+/* ---- ERes2Net, src/encoder_eres2net.cpp:36-264 ------------------------------ */
+
+typedef struct {
+    float* d;
+    int C, H, W;
+} Act;
+
+static Act act_new(int C, int H, int W) {
+    Act a;
+    a.C = C; a.H = H; a.W = W;
+    a.d = (float*)calloc((size_t)C * H * W, sizeof(float));
+    return a;
+}
+
+typedef struct {
+    const vd_eres2net_desc* d;
+    int idx;
+} ECtx;
+
+/* next_conv (:36-54): conv i with its stride, pad (k-1)/2, optional bias. */
+static Act e_next_conv(ECtx* e, const Act* x) {
+    const int i = e->idx++;
+    const vd_eres2net_desc* d = e->d;
+    const int k = d->k[i], s = d->stride[i], pad = (k - 1) / 2;
+    Act y = act_new(d->oc[i], (x->H + 2 * pad - k) / s + 1, (x->W + 2 * pad - k) / s + 1);
+    vdo_conv2d(x->d, x->W, x->H, x->C, d->w[i], d->oc[i], k, s, pad, d->b[i], 0, y.d);
+    return y;
+}
+
+/* hclamp = ggml_clamp(x, 0, hi) (:60-62) */
+static void e_clamp(Act* a, float hi) {
+    const size_t n = (size_t)a->C * a->H * a->W;
+    for (size_t i = 0; i < n; ++i) {
+        float v = a->d[i];
+        v = v < 0.0f ? 0.0f : v;
+        a->d[i] = v > hi ? hi : v;
+    }
+}
+
+/* AFF (:91-101): z = conv(concat(x, ds)) -> SiLU -> conv -> tanh;
+ * out = (x + ds) + tanh(z) * (x - ds). */
+static Act e_aff(ECtx* e, const Act* x, const Act* ds) {
+    const size_t hw = (size_t)x->H * x->W;
+    Act cat = act_new(x->C + ds->C, x->H, x->W);
+    memcpy(cat.d, x->d, sizeof(float) * x->C * hw);
+    memcpy(cat.d + (size_t)x->C * hw, ds->d, sizeof(float) * ds->C * hw);
+    Act z = e_next_conv(e, &cat);
+    free(cat.d);
+    const size_t nz = (size_t)z.C * hw;
+    for (size_t i = 0; i < nz; ++i) z.d[i] = z.d[i] / (1.0f + expf(-z.d[i]));  /* ggml_silu */
+    Act z2 = e_next_conv(e, &z);
+    free(z.d);
+    const size_t n = (size_t)x->C * hw;
+    Act out = act_new(x->C, x->H, x->W);
+    for (size_t i = 0; i < n; ++i) {
+        const float att = tanhf(z2.d[i]);
+        const float sum = x->d[i] + ds->d[i];
+        const float diff = x->d[i] - ds->d[i];
+        out.d[i] = sum + att * diff;
+    }
+    free(z2.d);
+    return out;
+}
+
+/* res2net_block (:111-137) */
+static Act e_block(ECtx* e, const Act* x, int planes, int stride, int is_aff, int* in_planes) {
+    const float hi = e->d->relu_clamp;
+    const int scale = e->d->scale;
+    Act out = e_next_conv(e, x);
+    e_clamp(&out, hi);
+    const int width = out.C / scale;
+    const size_t hw = (size_t)out.H * out.W;
+    Act accum = act_new(out.C, out.H, out.W);
+    Act sp = {NULL, 0, 0, 0};
+    for (int i = 0; i < scale; ++i) {
+        Act chunk = {out.d + (size_t)i * width * hw, width, out.H, out.W};
+        Act cur;
+        int own = 0;
+        if (i == 0) {
+            cur = chunk;
+        } else if (is_aff) {
+            cur = e_aff(e, &sp, &chunk);
+            own = 1;
+        } else {
+            cur = act_new(width, out.H, out.W);
+            for (size_t j = 0; j < (size_t)width * hw; ++j) cur.d[j] = sp.d[j] + chunk.d[j];
+            own = 1;
+        }
+        Act cv = e_next_conv(e, &cur);
+        e_clamp(&cv, hi);
+        if (own) free(cur.d);
+        memcpy(accum.d + (size_t)i * width * hw, cv.d, sizeof(float) * width * hw);
+        if (sp.d) free(sp.d);
+        sp = cv;
+    }
+    if (sp.d) free(sp.d);
+    free(out.d);
+    Act o3 = e_next_conv(e, &accum);
+    free(accum.d);
+    const size_t n = (size_t)o3.C * o3.H * o3.W;
+    if (stride != 1 || *in_planes != 2 * planes) {
+        Act r = e_next_conv(e, x);
+        for (size_t j = 0; j < n; ++j) o3.d[j] += r.d[j];
+        free(r.d);
+    } else {
+        for (size_t j = 0; j < n; ++j) o3.d[j] += x->d[j];
+    }
+    *in_planes = 2 * planes;
+    e_clamp(&o3, hi);
+    return o3;
+}
+
+static Act e_layer(ECtx* e, Act x, int planes, int n, int stride, int is_aff, int* in_planes,
+                   int free_input) {
+    for (int b = 0; b < n; ++b) {
+        Act y = e_block(e, &x, planes, b == 0 ? stride : 1, is_aff, in_planes);
+        if (b > 0 || free_input) free(x.d);
+        x = y;
+    }
+    return x;
+}
+
+/* TSTP + FC + L2 over a [C][H][W] activation (shared by both encoders). */
+static int tail_embed(const Act* a, const float* seg_w, const float* seg_b,
+                      const float* mean_vec, int emb_dim, int pooled_dim, float var_eps,
+                      int l2, float* emb, float* prenorm) {
+    const int C = a->C, H = a->H, W = a->W, HC = H * C;
+    if (2 * HC != pooled_dim) return 3;
+    float* pooled = (float*)malloc(sizeof(float) * 2 * (size_t)HC);
+    for (int c = 0; c < C; ++c)
+        for (int hh = 0; hh < H; ++hh) {
+            const float* row = a->d + ((size_t)c * H + hh) * W;
+            double s1 = 0.0;
+            for (int w = 0; w < W; ++w) s1 += row[w];
+            const float mean = (float)(s1 / W);
+            double s2 = 0.0;
+            for (int w = 0; w < W; ++w) {
+                const float dv = row[w] - mean;
+                s2 += (double)(dv * dv);
+            }
+            float var = (float)(s2 / W);
+            if (W > 1) var = var * ((float)W / (float)(W - 1));
+            pooled[(size_t)c * H + hh] = mean;
+            pooled[(size_t)HC + (size_t)c * H + hh] = sqrtf(var + var_eps);
+        }
+    for (int j = 0; j < emb_dim; ++j) {
+        const float* wr = seg_w + (size_t)j * pooled_dim;
+        double acc = 0.0;
+        for (int i = 0; i < pooled_dim; ++i) acc += (double)wr[i] * (double)pooled[i];
+        float v = (float)acc + seg_b[j];
+        if (mean_vec) v -= mean_vec[j];
+        emb[j] = v;
+    }
+    if (prenorm) memcpy(prenorm, emb, sizeof(float) * emb_dim);
+    if (l2) {
+        double n2 = 0.0;
+        for (int j = 0; j < emb_dim; ++j) n2 += (double)emb[j] * (double)emb[j];
+        const double nrm = sqrt(n2);
+        if (nrm > 0.0)
+            for (int j = 0; j < emb_dim; ++j) emb[j] = (float)((double)emb[j] / nrm);
+    }
+    free(pooled);
+    return 0;
+}
+
+/* ERes2NetEncoder::forward_capture (:147-264) */
+int vdo_eres2net_forward(const vd_eres2net_desc* d, const float* feats, int T, int n_mels,
+                         float* emb, float* prenorm) {
+    ECtx e = {d, 0};
+    const int M = d->m_channels;
+    Act x = {(float*)feats, 1, n_mels, T};
+    Act h = e_next_conv(&e, &x);  /* stem -> plain ReLU (:203) */
+    for (size_t i = 0; i < (size_t)h.C * h.H * h.W; ++i) h.d[i] = h.d[i] > 0.0f ? h.d[i] : 0.0f;
+    int in_planes = M;
+    Act o1 = e_layer(&e, h, M, d->num_blocks[0], 1, 0, &in_planes, 1);
+    Act o2 = e_layer(&e, o1, 2 * M, d->num_blocks[1], 2, 0, &in_planes, 0);
+    Act o1d = e_next_conv(&e, &o1);  /* layer1_downsample */
+    free(o1.d);
+    Act f12 = e_aff(&e, &o2, &o1d);
+    free(o1d.d);
+    Act o3 = e_layer(&e, o2, 4 * M, d->num_blocks[2], 2, 1, &in_planes, 0);
+    free(o2.d);
+    Act f12d = e_next_conv(&e, &f12);  /* layer2_downsample */
+    free(f12.d);
+    Act f123 = e_aff(&e, &o3, &f12d);
+    free(f12d.d);
+    Act o4 = e_layer(&e, o3, 8 * M, d->num_blocks[3], 2, 1, &in_planes, 0);
+    free(o3.d);
+    Act f123d = e_next_conv(&e, &f123);  /* layer3_downsample */
+    free(f123.d);
+    Act f1234 = e_aff(&e, &o4, &f123d);
+    free(o4.d);
+    free(f123d.d);
+    if (e.idx != d->n_convs) {
+        free(f1234.d);
+        return 4;  /* manifest does not match the topology */
+    }
+    const int rc = tail_embed(&f1234, d->seg_w, d->seg_b, NULL, d->emb_dim, d->pooled_dim,
+                              d->var_eps, d->l2_normalize, emb, prenorm);
+    free(f1234.d);
+    return rc;
+}

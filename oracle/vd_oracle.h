@@ -46,7 +46,32 @@ typedef struct {
     int l2_normalize;
 } vd_resnet_desc;
 
+/* ERes2Net: the flat conv list in forward-execution order (the GGUF manifest,
+ * src/model_loader.hpp:68-80). Conv i has torch weight (oc, ic, k, k) in w[i]
+ * (ggml [k,k,ic,oc]), bias b[i] or NULL, stride[i]; padding is (k-1)/2. */
+typedef struct {
+    int n_convs;
+    const float* const* w;
+    const float* const* b;
+    const int* ic;
+    const int* oc;
+    const int* k;
+    const int* stride;
+    int num_blocks[4];
+    int m_channels;
+    int scale;
+    float relu_clamp;
+    const float* seg_w; /* [emb_dim][pooled_dim] */
+    const float* seg_b;
+    int emb_dim;
+    int pooled_dim;
+    float var_eps;
+    int l2_normalize;
+} vd_eres2net_desc;
+
 /* ---- vd_oracle.c (C restatement) ---------------------------------------- */
+int vdo_eres2net_forward(const vd_eres2net_desc* d, const float* feats, int T, int n_mels,
+                         float* emb, float* prenorm);
 int vdo_fbank(const float* pcm, int n, int sample_rate, int n_mels, int n_fft, int win,
               int hop, float preemph, float low_freq, float high_freq, int cmn,
               float* out, long out_cap, int* out_T);

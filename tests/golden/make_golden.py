@@ -13,6 +13,8 @@ the repository).
   seeded U(-1, 1) inputs.
 * ref_resnet_tiny.npz -- pre-norm and L2 embeddings of a small seeded ResNet
   (vd_synth.tiny_resnet_model) from the reference kernels + restated glue.
+* ref_eres2net_tiny.npz -- the same for a small seeded ERes2Net
+  (vd_synth.tiny_eres2net_model: every block kind, AFF and cross-stage fusion).
 
 Usage: python tests/golden/make_golden.py
 """
@@ -86,6 +88,12 @@ def main() -> None:
     R = oracle.RefResNet34(m)
     emb, pre = R.embed(feats)
     np.savez_compressed(HERE / "ref_resnet_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
+
+    m = vd_synth.tiny_eres2net_model(6, n_mels=80)
+    pcm = vd_synth.clip_f32(vd_synth.make_clip(22, 20000))
+    feats = oracle.ref_fbank(pcm)
+    emb, pre = oracle.RefERes2Net(m).embed(feats)
+    np.savez_compressed(HERE / "ref_eres2net_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -167,3 +167,140 @@ def test_conv_phase_output(cuda_lib):
     plain = vd.from_grid(y_plain, B, OC, F, T)
     back = vd.from_phase(y_ph, B, OC, F, T)
     assert torch.equal(plain.cpu(), back.cpu())
+
+
+def _rand_act(g, B, C_, F, T, tv):
+    import torch
+    x = _h(torch.relu(torch.randn(B, C_, F, T, generator=g)))
+    for b, t in enumerate(tv):
+        x[b, :, :, t:] = 0
+    return x
+
+
+def _rel(got, ref):
+    return float((got - ref).norm() / max(ref.norm(), 1e-12))
+
+
+@pytest.mark.parametrize("k,stride", [(3, 1), (1, 1), (3, 2)])
+def test_conv_channel_slices(cuda_lib, k, stride):
+    """x0, residual and y as channel slices of wider GRID/PHASE tensors (the Res2Net
+    width split and the channel concat, src/encoder_eres2net.cpp:108-135): results
+    match the dense call, and channels outside the output slice are untouched."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(31)
+    B, CW, F, T = 2, 96, 20, 23
+    c0, IC, OC, o0 = 32, 32, 32, 64  # input slice [32, 64), output slice [64, 96)
+    tv = [23, 14]
+    To, Fo = vd.out_extent(T, stride), vd.out_extent(F, stride)
+    tvo = [vd.out_extent(t, stride) for t in tv]
+    xw = _rand_act(g, B, CW, F, T, tv)
+    w = _h(torch.randn(OC, IC, k, k, generator=g) * (2.0 / (IC * k * k)) ** 0.5)
+    bias = torch.randn(OC, generator=g) * 0.1
+    res_w = _rand_act(g, B, CW, Fo, To, tvo)
+    tvd = torch.tensor(tvo, dtype=torch.int32, device="cuda")
+    to_l = vd.to_phase if stride == 2 else vd.to_grid
+    xin = to_l(xw.cuda(), tv)
+    rin = vd.to_grid(res_w.cuda(), tvo)
+    wp = vd.pack_conv_weight(w.cuda())
+    sentinel = 3.0
+    yw = torch.full((vd.lib().vdb_grid_rows(B, To, Fo), CW), sentinel, dtype=torch.float16,
+                    device="cuda")
+    vd.conv(xin[:, c0:c0 + IC], wp, bias.cuda(), tvd, batch=B, t_out=To, f_out=Fo, oc=OC, k0=k,
+            stride0=stride, ic0=IC, residual=rin[:, o0:o0 + OC], relu=True,
+            y=yw[:, o0:o0 + OC])
+    torch.cuda.synchronize()
+    ref = _ref_conv(xw[:, c0:c0 + IC], w, bias, stride, residual=res_w[:, o0:o0 + OC],
+                    relu=True, tvalid_out=tvo)
+    got = vd.from_grid(yw[:, o0:o0 + OC].contiguous(), B, OC, Fo, To).cpu()
+    assert _rel(got, ref) <= REL_L2_TOL
+    assert torch.all(yw[:, :o0].float() == sentinel)
+
+
+def test_conv_dual_output(cuda_lib):
+    """y2 receives the PHASE layout of the same values y gets in GRID layout."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(32)
+    B, IC, OC, F, T = 2, 64, 128, 40, 33
+    tv = [33, 18]
+    x = _rand_act(g, B, IC, F, T, tv)
+    w = _h(torch.randn(OC, IC, 3, 3, generator=g) * 0.05)
+    bias = torch.randn(OC, generator=g) * 0.1
+    tvd = torch.tensor(tv, dtype=torch.int32, device="cuda")
+    xin = vd.to_grid(x.cuda(), tv)
+    wp = vd.pack_conv_weight(w.cuda())
+    y2 = torch.zeros(vd.lib().vdb_phase_rows(B, T, F), OC, dtype=torch.float16, device="cuda")
+    y = vd.conv(xin, wp, bias.cuda(), tvd, batch=B, t_out=T, f_out=F, oc=OC, relu=True, y2=y2)
+    torch.cuda.synchronize()
+    plain = vd.from_grid(y, B, OC, F, T).cpu()
+    assert torch.equal(plain, vd.from_phase(y2, B, OC, F, T).cpu())
+    ref = _ref_conv(x, w, bias, 1, relu=True, tvalid_out=tv)
+    assert _rel(plain, ref) <= REL_L2_TOL
+
+
+def test_conv_silu_no_bias(cuda_lib):
+    """act=1: SiLU(conv) with no bias (the AFF local_att first conv + SiLU,
+    src/encoder_eres2net.cpp:64-67, with bias=NULL accepted)."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(33)
+    B, IC, OC, F, T = 2, 128, 32, 10, 19
+    tv = [19, 7]
+    x = _h(torch.randn(B, IC, F, T, generator=g))
+    for b, t in enumerate(tv):
+        x[b, :, :, t:] = 0
+    w = _h(torch.randn(OC, IC, 1, 1, generator=g) * (1.0 / IC) ** 0.5)
+    tvd = torch.tensor(tv, dtype=torch.int32, device="cuda")
+    y = vd.conv(vd.to_grid(x.cuda(), tv), vd.pack_conv_weight(w.cuda()), None, tvd, batch=B,
+                t_out=T, f_out=F, oc=OC, k0=1, act=1)
+    torch.cuda.synchronize()
+    lin = _ref_conv(x, w, torch.zeros(OC), 1)
+    ref = lin * torch.sigmoid(lin)
+    for b, t in enumerate(tv):
+        ref[b, :, :, t:] = 0
+    assert _rel(vd.from_grid(y, B, OC, F, T).cpu(), ref) <= REL_L2_TOL
+
+
+def test_conv_attentional_fusion(cuda_lib):
+    """act=2: (x + ds) + tanh(conv(z) + b) * (x - ds), the AFF output
+    (src/encoder_eres2net.cpp:69-75), with x / ds / y as channel slices."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(34)
+    B, IC, OC, F, T = 2, 32, 128, 10, 17
+    tv = [17, 9]
+    z = _h(torch.randn(B, IC, F, T, generator=g))
+    for b, t in enumerate(tv):
+        z[b, :, :, t:] = 0
+    xw = _rand_act(g, B, 2 * OC, F, T, tv)   # x in channels [0, OC), ds in [OC, 2 OC)
+    w = _h(torch.randn(OC, IC, 1, 1, generator=g) * (1.0 / IC) ** 0.5)
+    bias = torch.randn(OC, generator=g) * 0.1
+    tvd = torch.tensor(tv, dtype=torch.int32, device="cuda")
+    xg = vd.to_grid(xw.cuda(), tv)
+    y = vd.conv(vd.to_grid(z.cuda(), tv), vd.pack_conv_weight(w.cuda()), bias.cuda(), tvd,
+                batch=B, t_out=T, f_out=F, oc=OC, k0=1, residual=xg[:, :OC],
+                residual2=xg[:, OC:], act=2)
+    torch.cuda.synchronize()
+    att = torch.tanh(_ref_conv(z, w, bias, 1))
+    xa, ds = xw[:, :OC], xw[:, OC:]
+    ref = (xa + ds) + att * (xa - ds)
+    for b, t in enumerate(tv):
+        ref[b, :, :, t:] = 0
+    assert _rel(vd.from_grid(y, B, OC, F, T).cpu(), ref) <= REL_L2_TOL
+
+
+def test_add_slices(cuda_lib):
+    """vdb_add on channel slices is exact f16(a + b) and leaves other channels alone."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(35)
+    rows = 1000
+    a = torch.randn(rows, 64, generator=g).half().cuda()
+    b = torch.randn(rows, 48, generator=g).half().cuda()
+    y = torch.full((rows, 80), 7.0, dtype=torch.float16, device="cuda")
+    vd.add(a[:, 16:48], b[:, 8:40], y[:, 40:72])
+    torch.cuda.synchronize()
+    ref = (a[:, 16:48].float() + b[:, 8:40].float()).half()
+    assert torch.equal(y[:, 40:72], ref)
+    assert torch.all(y[:, :40] == 7.0) and torch.all(y[:, 72:] == 7.0)

@@ -113,6 +113,37 @@ def test_resnet34_matches_reference_kernels(ref):
     assert np.array_equal(e0, e1)
 
 
+def test_eres2net_tiny_golden():
+    g = np.load(GOLD / "ref_eres2net_tiny.npz")
+    m = vd_synth.tiny_eres2net_model(6, n_mels=80)
+    feats = oracle.fbank(g["pcm"])
+    emb, pre = oracle.eres2net_embed(m, feats)
+    assert pre.shape == (512,)
+    assert np.abs(pre - g["prenorm"]).max() <= 1e-3 * max(1.0, np.abs(g["prenorm"]).max())
+    assert _cos(emb, g["emb"]) >= 0.999999
+
+
+def test_eres2net_matches_reference_kernels(ref):
+    """Restated ERes2Net glue + C conv vs the same glue on the reference's blocked
+    conv kernels: bit-identical (same accumulation order)."""
+    m = vd_synth.tiny_eres2net_model(8, n_mels=80)
+    pcm = vd_synth.clip_f32(vd_synth.make_clip(78, 16000 + 160 * 9))
+    feats = oracle.fbank(pcm)
+    e0, p0 = oracle.eres2net_embed(m, feats)
+    e1, p1 = ref.RefERes2Net(m).embed(feats)
+    assert np.array_equal(p0, p1)
+    assert np.array_equal(e0, e1)
+
+
+def test_eres2net_conv_manifest():
+    """The full ERes2Net-base manifest has 96 convs, stem included, in forward-execution
+    order (src/model_loader.hpp:68-80) and a 2*512*10 pooled vector at 80 mels."""
+    m = vd_synth.eres2net_model(0)
+    assert len(m["convs"]) == 96
+    assert m["seg_w"].shape == (512, 2 * 512 * 10)
+    assert sum(c["b"] is None for c in m["convs"]) == 3  # the cross-stage downsamples
+
+
 def test_q8_0_roundtrip_matches_gguf_dequant(tmp_path):
     """The q8_0 model the oracle sees equals what a q8_0 GGUF carries."""
     gguf = pytest.importorskip("gguf")

@@ -84,9 +84,13 @@ struct ConvDev {
     SegDev seg[2];
     uint32_t stage0, stage_bytes, a_region, n_stages, tmem_cols, bres_bytes;
     uint32_t bias_off, tv_off, bar_off;
-    const float* bias;
+    const float* bias;       // may be null (no bias)
     const __half* residual;
+    const __half* residual2;
+    int ldr, ldr2, ldy;      // row pitches (elements)
+    int act;                 // 0 ReLU/clamp flags, 1 SiLU, 2 attentional fusion
     __half* y;
+    __half* y2;              // optional PHASE-layout second output
     int y_phase;
     int Hp, Wp, T, F;  // output grid: Hp = T+2, Wp = F+2
     int Hq, Wq;        // phase-split output: consumer grid
@@ -123,11 +127,12 @@ __device__ __forceinline__ float h2f(uint32_t bits16) {
 
 struct RowInfo {
     bool in_range, valid;
-    long long dst;
+    long long dst;    // row of y
+    long long dst2;   // row of the PHASE-layout output (y2, or y when y_phase)
 };
 
 __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int m, bool live) {
-    RowInfo ri{false, false, (long long)m};
+    RowInfo ri{false, false, (long long)m, 0};
     if (m >= p.M) return ri;
     ri.in_range = true;
     const int img = p.Hp * p.Wp;
@@ -136,11 +141,10 @@ __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int
     const int tp = r / p.Wp;
     const int fp = r - tp * p.Wp;
     ri.valid = live && tp >= 1 && tp <= tv[b] && fp >= 1 && fp <= p.F;
-    if (p.y_phase) {
-        const int q = ((tp & 1) << 1) | (fp & 1);
-        ri.dst = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
-                 (fp >> 1) + 1;
-    }
+    const int q = ((tp & 1) << 1) | (fp & 1);
+    ri.dst2 = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
+              (fp >> 1) + 1;
+    if (p.y_phase) ri.dst = ri.dst2;
     return ri;
 }
 
@@ -157,7 +161,8 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
 template <int NC, int J>
 __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri,
                                           uint32_t taddr, const float* sbias, bool has_res,
-                                          const uint4 (&res)[NC / 8], __half* yrow) {
+                                          const uint4 (&res)[NC / 8], const __half* r2ptr,
+                                          __half* yrow, __half* y2row) {
     float f[NC];
 #pragma unroll
     for (int i = 0; i < NC; ++i) f[i] = 0.0f;
@@ -190,44 +195,73 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
     }
     if (!ri.in_range) return;
     if (ri.valid) {
+        if (sbias) {
 #pragma unroll
-        for (int i = 0; i < NC; ++i) f[i] += sbias[i];
-        if (has_res) {
+            for (int i = 0; i < NC; ++i) f[i] += sbias[i];
+        }
+        if (p.act == 2) {
+            // attentional fusion: (x + ds) + tanh(z) * (x - ds), x = residual, ds = residual2
 #pragma unroll
             for (int j = 0; j < NC / 8; ++j) {
-                const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
+                const uint4 d4 = __ldg(reinterpret_cast<const uint4*>(r2ptr) + j);
+                const uint32_t wx[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
+                const uint32_t wd[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    f[j * 8 + 2 * h] += h2f(w[h] & 0xFFFFu);
-                    f[j * 8 + 2 * h + 1] += h2f(w[h] >> 16);
+                for (int h = 0; h < 8; ++h) {
+                    const float x = h2f((h & 1) ? (wx[h >> 1] >> 16) : (wx[h >> 1] & 0xFFFFu));
+                    const float d = h2f((h & 1) ? (wd[h >> 1] >> 16) : (wd[h >> 1] & 0xFFFFu));
+                    const float att = tanhf(f[j * 8 + h]);
+                    f[j * 8 + h] = (x + d) + att * (x - d);
                 }
             }
-        }
-        if (p.relu) {
+        } else {
+            if (has_res) {
 #pragma unroll
-            for (int i = 0; i < NC; ++i) f[i] = fmaxf(f[i], 0.0f);
-        }
-        if (p.clamp_hi > 0.0f) {
+                for (int j = 0; j < NC / 8; ++j) {
+                    const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
 #pragma unroll
-            for (int i = 0; i < NC; ++i) f[i] = fminf(f[i], p.clamp_hi);
+                    for (int h = 0; h < 4; ++h) {
+                        f[j * 8 + 2 * h] += h2f(w[h] & 0xFFFFu);
+                        f[j * 8 + 2 * h + 1] += h2f(w[h] >> 16);
+                    }
+                }
+            }
+            if (p.act == 1) {
+#pragma unroll
+                for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
+            }
+            if (p.relu) {
+#pragma unroll
+                for (int i = 0; i < NC; ++i) f[i] = fmaxf(f[i], 0.0f);
+            }
+            if (p.clamp_hi > 0.0f) {
+#pragma unroll
+                for (int i = 0; i < NC; ++i) f[i] = fminf(f[i], p.clamp_hi);
+            }
         }
     } else {
 #pragma unroll
         for (int i = 0; i < NC; ++i) f[i] = 0.0f;
     }
-    uint4* yp = reinterpret_cast<uint4*>(yrow);
+    uint4 out[NC / 8];
 #pragma unroll
     for (int j = 0; j < NC / 8; ++j) {
-        uint4 q;
         __half2 h0 = __floats2half2_rn(f[j * 8 + 0], f[j * 8 + 1]);
         __half2 h1 = __floats2half2_rn(f[j * 8 + 2], f[j * 8 + 3]);
         __half2 h2 = __floats2half2_rn(f[j * 8 + 4], f[j * 8 + 5]);
         __half2 h3 = __floats2half2_rn(f[j * 8 + 6], f[j * 8 + 7]);
-        q.x = *reinterpret_cast<uint32_t*>(&h0);
-        q.y = *reinterpret_cast<uint32_t*>(&h1);
-        q.z = *reinterpret_cast<uint32_t*>(&h2);
-        q.w = *reinterpret_cast<uint32_t*>(&h3);
-        yp[j] = q;
+        out[j].x = *reinterpret_cast<uint32_t*>(&h0);
+        out[j].y = *reinterpret_cast<uint32_t*>(&h1);
+        out[j].z = *reinterpret_cast<uint32_t*>(&h2);
+        out[j].w = *reinterpret_cast<uint32_t*>(&h3);
+    }
+    uint4* yp = reinterpret_cast<uint4*>(yrow);
+#pragma unroll
+    for (int j = 0; j < NC / 8; ++j) yp[j] = out[j];
+    if (y2row) {
+        uint4* y2p = reinterpret_cast<uint4*>(y2row);
+#pragma unroll
+        for (int j = 0; j < NC / 8; ++j) y2p[j] = out[j];
     }
 }
 
@@ -239,8 +273,11 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
                                          int n0, int c_lo, int c_hi, uint32_t tbase,
                                          const float* sbias) {
     const bool has_res = p.residual != nullptr && ri.valid;
-    const __half* rrow = has_res ? p.residual + (long long)m * p.oc + n0 : nullptr;
-    __half* yrow = p.y + ri.dst * p.oc + n0;
+    const bool has_res2 = p.residual2 != nullptr && ri.valid;
+    const __half* rrow = has_res ? p.residual + (long long)m * p.ldr + n0 : nullptr;
+    const __half* r2row = has_res2 ? p.residual2 + (long long)m * p.ldr2 + n0 : nullptr;
+    __half* yrow = p.y + ri.dst * p.ldy + n0;
+    __half* y2row = (p.y2 && ri.in_range) ? p.y2 + ri.dst2 * p.oc + n0 : nullptr;
     uint4 res[NC / 8];
     if (has_res) load_res<NC>(rrow + c_lo, res);
     for (int c = c_lo; c < c_hi; c += NC) {
@@ -248,8 +285,9 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
         if (has_res && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
-        epi_chunk<NC, J>(p, live, ri, tbase + (uint32_t)c, sbias + n0 + c, has_res, cur,
-                         yrow + c);
+        epi_chunk<NC, J>(p, live, ri, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
+                         has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
+                         y2row ? y2row + c : nullptr);
     }
 }
 
@@ -342,7 +380,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias[i];
+    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias ? p.bias[i] : 0.0f;
     for (int i = threadIdx.x; i < p.batch; i += blockDim.x) stv[i] = p.tvalid[i];
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -559,10 +597,12 @@ CUtensorMapSwizzle swizzle_for(int kb) {
                     : (kb == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-bool make_map_a(CUtensorMap* m, const void* ptr, int C, long long rows, int planes, int kb,
-                int box_rows) {
+// A operand view: C channels of rows with pitch ld elements (ld > C when the
+// tensor is a channel slice of a wider one), in 1 or 4 planes.
+bool make_map_a(CUtensorMap* m, const void* ptr, int C, int ld, long long rows, int planes,
+                int kb, int box_rows) {
     cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)rows, (cuuint64_t)planes};
-    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)rows * C * 2};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)rows * ld * 2};
     cuuint32_t box[3] = {(cuuint32_t)kb, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode_tiled_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr),
@@ -645,8 +685,25 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: unsupported kernel/stride");
         return 1;
     }
-    if (!a->x0 || !a->w0 || !a->bias || !a->tvalid || !a->y || (a->x1 && !a->w1)) {
+    if (!a->x0 || !a->w0 || !a->tvalid || !a->y || (a->x1 && !a->w1)) {
         set_error("vdb_conv: NULL buffer");
+        return 1;
+    }
+    if ((a->ldx0 && a->ldx0 < a->ic0) || (a->x1 && a->ldx1 && a->ldx1 < a->ic1) ||
+        (a->ldy && a->ldy < a->oc) || (a->ldr && a->ldr < a->oc) || (a->ldr2 && a->ldr2 < a->oc) ||
+        (a->ldx0 | a->ldx1 | a->ldy | a->ldr | a->ldr2) % 8 != 0) {
+        set_error("vdb_conv: row pitches must be >= the channel count and multiples of 8");
+        return 1;
+    }
+    auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+    if (misaligned(a->x0) || (a->x1 && misaligned(a->x1)) || misaligned(a->y) ||
+        (a->y2 && misaligned(a->y2)) || (a->residual && misaligned(a->residual)) ||
+        (a->residual2 && misaligned(a->residual2))) {
+        set_error("vdb_conv: activation pointers must be 16-byte aligned");
+        return 1;
+    }
+    if (a->act < 0 || a->act > 2 || (a->act == 2 && (!a->residual || !a->residual2))) {
+        set_error("vdb_conv: act must be 0, 1 or 2 (2 needs residual and residual2)");
         return 1;
     }
     if (!(a->tile_m == 0 || a->tile_m == 128 || a->tile_m == 256)) {
@@ -758,7 +815,13 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     p.tmem_cols = cols;
     p.bias = a->bias;
     p.residual = static_cast<const __half*>(a->residual);
+    p.residual2 = static_cast<const __half*>(a->residual2);
+    p.ldr = a->ldr ? a->ldr : a->oc;
+    p.ldr2 = a->ldr2 ? a->ldr2 : a->oc;
+    p.ldy = a->ldy ? a->ldy : a->oc;
+    p.act = a->act;
     p.y = static_cast<__half*>(a->y);
+    p.y2 = static_cast<__half*>(a->y2);
     p.y_phase = a->y_phase;
     p.Hp = Hp;
     p.Wp = Wp;
@@ -784,7 +847,9 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         const void* w = sg ? a->w1 : a->w0;
         const int stride = sg ? a->stride1 : a->stride0;
         const int box_rows = s.mode == SEG_HALO ? s.box_rows : BM;
-        if (!make_map_a(&tm[2 * sg], x, s.ic, rows_out, stride == 2 ? 4 : 1, s.kb, box_rows) ||
+        const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
+        if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, stride == 2 ? 4 : 1, s.kb,
+                        box_rows) ||
             !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, BN, s.kb)) {
             set_error("vdb_conv: cuTensorMapEncodeTiled failed");
             return 1;

@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <algorithm>
+#include <cstdint>
 #include <mutex>
 #include <string>
 
@@ -239,6 +241,50 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
             set_error("vdb_cmn_stem: stem channels must be 16, 32 or 64");
             return 1;
     }
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+namespace vdb {
+namespace {
+__global__ void add_slices_kernel(const uint4* __restrict__ a, int lda8, const uint4* __restrict__ b,
+                                  int ldb8, uint4* __restrict__ y, int ldy8, long long rows,
+                                  int c8) {
+    const long long n = rows * c8;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / c8;
+        const int c = (int)(i - r * c8);
+        const uint4 va = a[r * lda8 + c], vb = b[r * ldb8 + c];
+        uint4 o;
+        const __half2* ha = reinterpret_cast<const __half2*>(&va);
+        const __half2* hb = reinterpret_cast<const __half2*>(&vb);
+        __half2* ho = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 fa = __half22float2(ha[k]), fb = __half22float2(hb[k]);
+            ho[k] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+        }
+        y[r * ldy8 + c] = o;
+    }
+}
+}  // namespace
+}  // namespace vdb
+
+extern "C" int vdb_add(const void* a, int lda, const void* b, int ldb, void* y, int ldy,
+                       long long rows, int C, void* stream) {
+    auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+    if (!a || !b || !y || rows <= 0 || C <= 0 || C % 8 || lda % 8 || ldb % 8 || ldy % 8 ||
+        lda < C || ldb < C || ldy < C || mis(a) || mis(b) || mis(y)) {
+        set_error("vdb_add: bad arguments (NULL, pitch < C, or not multiples of 8 / 16 B)");
+        return 1;
+    }
+    const long long n = rows * (C / 8);
+    const int threads = 256;
+    const int blocks = (int)std::min<long long>((n + threads - 1) / threads, 148LL * 16);
+    add_slices_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(a), lda / 8, static_cast<const uint4*>(b), ldb / 8,
+        static_cast<uint4*>(y), ldy / 8, rows, C / 8);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }

@@ -40,7 +40,9 @@ class ConvArgs(C.Structure):
         ("bias", C.c_void_p), ("residual", C.c_void_p), ("relu", C.c_int),
         ("clamp_hi", C.c_float), ("tvalid", C.c_void_p), ("y", C.c_void_p),
         ("y_phase", C.c_int), ("err", C.c_void_p), ("tile_m", C.c_int), ("halo", C.c_int),
-        ("ksplit", C.c_int),
+        ("ksplit", C.c_int), ("ldx0", C.c_int), ("ldx1", C.c_int), ("ldy", C.c_int),
+        ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
+        ("act", C.c_int),
     ]
 
 
@@ -76,6 +78,9 @@ def lib() -> C.CDLL:
         L.vdb_pool_embed.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float,
                                      C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.vdb_add.restype = C.c_int
+        L.vdb_add.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                              C.c_longlong, C.c_int, C.c_void_p]
         L.vdb_identify.restype = C.c_int
         L.vdb_identify.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_void_p]
@@ -338,11 +343,25 @@ def pack_conv_weight(w):
         __import__("torch").float16).contiguous()
 
 
+def _ld(t):
+    """Row pitch in elements of a 2-D (rows, C) tensor or channel-slice view of one."""
+    return int(t.stride(0)) if t is not None and t.dim() == 2 else 0
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
-         y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0):
-    """vdb_conv on device tensors. x0/x1/residual/y are f16 GRID or PHASE tensors,
-    w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,), tvalid int32 (B,)."""
+         y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
+         y2=None, residual2=None, act=0):
+    """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
+    tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
+    the row pitch is taken from the view's stride); y2 is an extra PHASE output,
+    w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,) or None, tvalid int32 (B,).
+    act: 0 = [+residual] then relu/clamp, 1 = SiLU, 2 = attentional fusion
+    (residual + residual2) + tanh(acc + bias) * (residual - residual2)."""
     import torch
     if y is None:
         rows = (lib().vdb_phase_rows(batch, t_out, f_out) if y_phase
@@ -352,13 +371,24 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(),
                  w0=w0.data_ptr(), stride1=stride1,
                  ic1=(ic1 if ic1 is not None else (x1.shape[1] if x1 is not None else 0)),
-                 x1=x1.data_ptr() if x1 is not None else None,
-                 w1=w1.data_ptr() if w1 is not None else None, bias=bias.data_ptr(),
-                 residual=residual.data_ptr() if residual is not None else None,
+                 x1=_ptr(x1), w1=_ptr(w1), bias=_ptr(bias), residual=_ptr(residual),
                  relu=int(relu), clamp_hi=float(clamp_hi), tvalid=tvalid.data_ptr(),
-                 y=y.data_ptr(), y_phase=int(y_phase),
-                 err=err.data_ptr() if err is not None else None, tile_m=tile_m, halo=halo,
-                 ksplit=ksplit)
+                 y=y.data_ptr(), y_phase=int(y_phase), err=_ptr(err), tile_m=tile_m,
+                 halo=halo, ksplit=ksplit, ldx0=_ld(x0), ldx1=_ld(x1), ldy=_ld(y),
+                 y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
+                 ldr2=_ld(residual2), act=int(act))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
+    return y
+
+
+def add(a, b, y=None, stream=None):
+    """vdb_add: y = a + b on (rows, C) f16 tensors or channel-slice views."""
+    import torch
+    rows, Cc = a.shape
+    if y is None:
+        y = torch.empty(rows, Cc, dtype=torch.float16, device=a.device)
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    _check(lib().vdb_add(a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), y.data_ptr(), _ld(y),
+                         rows, Cc, C.c_void_p(s)), "vdb_add")
     return y

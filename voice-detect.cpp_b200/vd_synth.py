@@ -165,6 +165,139 @@ def f16_model(m: dict) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# ERes2Net weights
+# ---------------------------------------------------------------------------
+def eres2net_model(seed: int = 0, n_mels: int = N_MELS, m_channels: int = 32,
+                   num_blocks=(3, 4, 6, 3), base_width: int = 32, scale: int = 2,
+                   emb_dim: int = 512) -> dict:
+    """Synthetic 3D-Speaker ERes2Net with BatchNorm folded into every conv, as a
+    flat conv list in the reference's forward-EXECUTION order
+    (src/encoder_eres2net.cpp:147-226; manifest src/model_loader.hpp:68-80):
+
+      stem 3x3 1->M (+b, ReLU)
+      layer1..layer4 of Res2Net blocks (expansion 2), each block:
+        conv1 1x1 (block stride) in->w*scale, then per chunk i: [AFF la1, la2 when
+        i > 0 and the layer fuses with AFF] conv3x3 w->w, then conv3 1x1
+        w*scale->2P, then the 1x1 shortcut (block stride) when shape changes
+      after layer2: layer1_downsample 3x3 s2 (no bias) + AFF(o2, .)
+      after layer3: layer2_downsample + AFF; after layer4: layer3_downsample + AFF
+    AFF(C): la1 1x1 2C->C/4 (+b) -> SiLU -> la2 1x1 C/4->C (+b) -> tanh.
+    Layers 3 and 4 fuse their chunks with AFF, layers 1 and 2 add them."""
+    rng = np.random.default_rng(seed)
+    convs: list[dict] = []
+
+    def conv(ic, oc, k, stride=1, bias=True):
+        w, b = _folded_conv(rng, oc, ic, k)
+        convs.append({"w": w, "b": b if bias else None, "stride": stride})
+
+    def aff(c):
+        conv(2 * c, c // 4, 1)
+        conv(c // 4, c, 1)
+
+    conv(1, m_channels, 3)  # stem
+    in_planes = m_channels
+    f = n_mels
+    planes_list = [m_channels, 2 * m_channels, 4 * m_channels, 8 * m_channels]
+    for li, (planes, n) in enumerate(zip(planes_list, num_blocks)):
+        is_aff = li >= 2
+        for bi in range(n):
+            stride = 2 if (li > 0 and bi == 0) else 1
+            width = int(np.floor(planes * base_width / 64.0))
+            conv(in_planes, width * scale, 1, stride)
+            for i in range(scale):
+                if i > 0 and is_aff:
+                    aff(width)
+                conv(width, width, 3)
+            conv(width * scale, 2 * planes, 1)
+            if stride != 1 or in_planes != 2 * planes:
+                conv(in_planes, 2 * planes, 1, stride)
+            in_planes = 2 * planes
+        if li > 0:
+            f = (f + 2 - 3) // 2 + 1
+            # cross-stage fusion after layers 2, 3, 4: downsample the previous fused
+            # feature (3x3 s2, BN-less) and AFF it into this layer's output
+            conv(planes, 2 * planes, 3, 2, bias=False)
+            aff(2 * planes)
+    c_last = 2 * planes_list[-1]
+    pooled = 2 * c_last * f
+    return {
+        "arch": "eres2net", "convs": convs, "m_channels": m_channels, "scale": scale,
+        "num_blocks": list(num_blocks), "relu_clamp": 20.0, "var_eps": 1e-8,
+        "seg_w": (rng.standard_normal((emb_dim, pooled)) / np.sqrt(pooled)).astype(np.float32),
+        "seg_b": rng.normal(0.0, 0.01, emb_dim).astype(np.float32),
+        "l2_normalize": True, "n_mels": n_mels,
+    }
+
+
+def tiny_eres2net_model(seed: int = 0, n_mels: int = 16) -> dict:
+    """Same topology rules, one block per layer and a short front, for CPU tests."""
+    return eres2net_model(seed, n_mels=n_mels, num_blocks=(1, 1, 2, 1))
+
+
+def quantize_model_f16(m: dict) -> dict:
+    """Round every ERes2Net weight (not the biases) through f16."""
+    q = dict(m)
+    q["convs"] = [dict(c, w=c["w"].astype(np.float16).astype(np.float32)) for c in m["convs"]]
+    q["seg_w"] = m["seg_w"].astype(np.float16).astype(np.float32)
+    return q
+
+
+def write_eres2net_gguf(path: str, m: dict, dtype: str = "f32") -> None:
+    """Write an eres2net GGUF with the reference's KV schema
+    (voicedetect.eres2net.*, src/model_loader.cpp:153-165). dtype: f32 | f16
+    (weights only; biases and the IC=1 stem stay f32)."""
+    import gguf
+
+    w = gguf.GGUFWriter(path, arch="voicedetect")
+    w.add_string("voicedetect.arch", "eres2net")
+    w.add_uint32("voicedetect.embedding_dim", int(m["seg_w"].shape[0]))
+    w.add_bool("voicedetect.l2_normalize", bool(m.get("l2_normalize", True)))
+    w.add_uint32("voicedetect.fbank.sample_rate", 16000)
+    w.add_uint32("voicedetect.fbank.n_mels", int(m.get("n_mels", N_MELS)))
+    w.add_uint32("voicedetect.fbank.n_fft", 512)
+    w.add_uint32("voicedetect.fbank.win_length", 400)
+    w.add_uint32("voicedetect.fbank.hop_length", 160)
+    w.add_float32("voicedetect.fbank.preemph", 0.97)
+    w.add_float32("voicedetect.fbank.low_freq", 20.0)
+    w.add_float32("voicedetect.fbank.high_freq", 0.0)
+    w.add_bool("voicedetect.fbank.cmn", True)
+    wn, bn, st = [], [], []
+    tensors = []
+    for i, c in enumerate(m["convs"]):
+        wn.append(f"conv{i}.weight")
+        tensors.append((wn[-1], c["w"], "conv"))
+        if c["b"] is not None:
+            bn.append(f"conv{i}.bias")
+            tensors.append((bn[-1], c["b"], "bias"))
+        else:
+            bn.append("")
+        st.append(int(c["stride"]))
+    w.add_array("voicedetect.eres2net.conv_weight", wn)
+    w.add_array("voicedetect.eres2net.conv_bias", bn)
+    w.add_array("voicedetect.eres2net.conv_stride", st)
+    w.add_array("voicedetect.eres2net.num_blocks", [int(v) for v in m["num_blocks"]])
+    w.add_uint32("voicedetect.eres2net.m_channels", int(m["m_channels"]))
+    w.add_uint32("voicedetect.eres2net.scale", int(m["scale"]))
+    w.add_string("voicedetect.eres2net.seg_weight", "seg.weight")
+    w.add_string("voicedetect.eres2net.seg_bias", "seg.bias")
+    w.add_float32("voicedetect.eres2net.relu_clamp", float(m["relu_clamp"]))
+    w.add_float32("voicedetect.eres2net.var_eps", float(m["var_eps"]))
+    tensors.append(("seg.weight", m["seg_w"], "fc"))
+    tensors.append(("seg.bias", m["seg_b"], "bias"))
+    for name, arr, kind in tensors:
+        arr = np.ascontiguousarray(arr, np.float32)
+        if dtype == "f16" and kind != "bias" and not (kind == "conv" and arr.shape[1] == 1
+                                                       and arr.shape[2] == 3):
+            w.add_tensor(name, arr.astype(np.float16))
+        else:
+            w.add_tensor(name, arr)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+# ---------------------------------------------------------------------------
 # GGUF writer (reference KV schema)
 # ---------------------------------------------------------------------------
 def write_resnet_gguf(path: str, m: dict, dtype: str = "f32") -> None:
