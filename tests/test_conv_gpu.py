@@ -83,6 +83,8 @@ CASES = [
     ("s1_32_32_res", 3, 32, 32, 80, 30, 3, 1, False, True, [30, 17, 5]),
     ("s2_32_64_down", 3, 32, 64, 80, 31, 3, 2, True, False, [31, 20, 9]),
     ("oc512_split", 1, 64, 512, 6, 9, 3, 1, False, False, None),
+    ("s2_1x1", 2, 64, 128, 20, 31, 1, 2, False, False, [31, 12]),
+    ("s2_1x1_down", 2, 32, 64, 20, 31, 1, 2, True, False, [31, 12]),
 ]
 
 

@@ -121,6 +121,11 @@ void Engine::free_workspace() {
         L.p = nullptr;
         L.g_bytes = L.p_bytes = 0;
     }
+    for (EBuf& eb : ebufs_) {
+        cudaFree(eb.p);
+        eb.p = nullptr;
+        eb.bytes = 0;
+    }
     cudaFree(feats_);
     feats_ = nullptr;
     feats_bytes_ = 0;
@@ -184,7 +189,8 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         err = "CUDA stream/alloc failed";
         return nullptr;
     }
-    if (c.arch != "wespeaker_resnet34") return e;  // load succeeds; embed reports the arch
+    // load succeeds for other archs; embed then reports the arch as not implemented
+    if (c.arch != "wespeaker_resnet34" && c.arch != "eres2net") return e;
 
     e->plan_ = vdb_fbank_plan_create(c.sample_rate, c.n_mels, c.n_fft, c.win, c.hop, c.preemph,
                                      c.low_freq, c.high_freq);
@@ -192,43 +198,16 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         err = vdb_last_error();
         return nullptr;
     }
+    if (c.arch == "eres2net") {
+        if (!e->load_eres2net(g, err)) return nullptr;
+        return e;
+    }
     Loader L{g, err};
     auto upload = [&](const std::vector<float>& v, float** dst) -> bool {
-        void* p = nullptr;
-        if (cudaMalloc(&p, v.size() * sizeof(float)) != cudaSuccess ||
-            cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) !=
-                cudaSuccess) {
-            err = "weight upload failed";
-            return false;
-        }
-        e->weight_allocs_.push_back(p);
-        *dst = static_cast<float*>(p);
-        return true;
+        return e->upload_f32(v, dst, err);
     };
     auto upload_h = [&](const std::vector<float>& v, __half** dst) -> bool {
-        float* tmp = nullptr;
-        if (cudaMalloc(&tmp, v.size() * sizeof(float)) != cudaSuccess) {
-            err = "weight upload failed";
-            return false;
-        }
-        void* p = nullptr;
-        bool ok = cudaMalloc(&p, v.size() * sizeof(__half)) == cudaSuccess &&
-                  cudaMemcpy(tmp, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) ==
-                      cudaSuccess;
-        if (ok) {
-            const long long n = (long long)v.size();
-            f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(tmp, (__half*)p, n);
-            ok = cudaDeviceSynchronize() == cudaSuccess;
-        }
-        cudaFree(tmp);
-        if (!ok) {
-            err = "weight conversion failed";
-            if (p) cudaFree(p);
-            return false;
-        }
-        e->weight_allocs_.push_back(p);
-        *dst = static_cast<__half*>(p);
-        return true;
+        return e->upload_f16(v, dst, err);
     };
 
     // ResNet manifest, src/model_loader.cpp:138-152.
@@ -344,8 +323,399 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
     return e;
 }
 
+bool Engine::upload_f32(const std::vector<float>& v, float** dst, std::string& err) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, v.size() * sizeof(float)) != cudaSuccess ||
+        cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+        if (p) cudaFree(p);
+        err = "weight upload failed";
+        return false;
+    }
+    weight_allocs_.push_back(p);
+    *dst = static_cast<float*>(p);
+    return true;
+}
+
+bool Engine::upload_f16(const std::vector<float>& v, __half** dst, std::string& err) {
+    float* tmp = nullptr;
+    if (cudaMalloc(&tmp, v.size() * sizeof(float)) != cudaSuccess) {
+        err = "weight upload failed";
+        return false;
+    }
+    void* p = nullptr;
+    bool ok = cudaMalloc(&p, v.size() * sizeof(__half)) == cudaSuccess &&
+              cudaMemcpy(tmp, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice) ==
+                  cudaSuccess;
+    if (ok) {
+        const long long n = (long long)v.size();
+        f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256>>>(tmp, (__half*)p, n);
+        ok = cudaDeviceSynchronize() == cudaSuccess;
+    }
+    cudaFree(tmp);
+    if (!ok) {
+        err = "weight conversion failed";
+        if (p) cudaFree(p);
+        return false;
+    }
+    weight_allocs_.push_back(p);
+    *dst = static_cast<__half*>(p);
+    return true;
+}
+
+// ERes2Net manifest (src/model_loader.cpp:153-165) compiled into a step plan by
+// replaying the reference forward with a running conv index:
+//   stem 3x3 + ReLU                                   (encoder_eres2net.cpp:196)
+//   layer1..4 of Res2Net blocks                       (:111-145, :200-218)
+//   cross-stage downsample + AFF after layers 2, 3, 4 (:206-218)
+// Layouts: a tensor read by a stride-2 conv is written in the PHASE layout (the
+// last block of layers 1-3 and the fused features f12 / f123); o2 and o3 are read
+// both ways and get both (y + y2). AFF's channel concat becomes the two input
+// segments of the local_att conv1 (x with W[:, :C], ds with W[:, C:]); the
+// Res2Net split / concat are channel offsets into the conv1 and accumulator
+// buffers.
+bool Engine::load_eres2net(const Gguf& g, std::string& err) {
+    const std::string pre = "voicedetect.eres2net.";
+    const auto wn = g.str_arr(pre + "conv_weight"), bn = g.str_arr(pre + "conv_bias");
+    const auto sn = g.i32_arr(pre + "conv_stride"), nb = g.i32_arr(pre + "num_blocks");
+    const int M = (int)g.u32(pre + "m_channels");
+    const int S = (int)g.u32(pre + "scale", 2);
+    const float hi = g.f32(pre + "relu_clamp", 20.0f);
+    var_eps_ = g.f32(pre + "var_eps", 1e-8f);
+    if (wn.empty() || bn.size() != wn.size() || sn.size() != wn.size() || nb.size() != 4 ||
+        M <= 0 || S < 1) {
+        err = "inconsistent voicedetect.eres2net.* manifest";
+        return false;
+    }
+    for (int v : nb)
+        if (v < 1) {
+            err = "eres2net: every layer needs at least one block";
+            return false;
+        }
+    Loader L{g, err};
+    struct MC {
+        std::vector<float> w, b;
+        int oc = 0, ic = 0, k = 0;
+    };
+    size_t idx = 0;
+    auto take = [&](MC& m, int k, int ic, int stride) -> bool {
+        if (idx >= wn.size()) {
+            err = "eres2net manifest has fewer convs than the topology needs";
+            return false;
+        }
+        const size_t i = idx++;
+        if (!L.conv(wn[i], m.w, m.oc, m.ic, m.k)) return false;
+        if (m.k != k || m.ic != ic || sn[i] != stride) {
+            err = "eres2net conv " + std::to_string(i) + " ('" + wn[i] + "'): expected " +
+                  std::to_string(k) + "x" + std::to_string(k) + " stride " +
+                  std::to_string(stride) + " from " + std::to_string(ic) + " channels, got " +
+                  std::to_string(m.k) + "x" + std::to_string(m.k) + " stride " +
+                  std::to_string(sn[i]) + " from " + std::to_string(m.ic);
+            return false;
+        }
+        if (k > 1 || ic > 1) {
+            if (m.oc % 16 || m.ic % 16) {
+                err = "eres2net conv " + std::to_string(i) + ": channels must be multiples of 16";
+                return false;
+            }
+        }
+        m.b.clear();
+        if (!bn[i].empty() && !L.vec(bn[i], m.b, m.oc)) return false;
+        return true;
+    };
+    auto dev_w = [&](const MC& m, const __half** out) -> bool {
+        __half* p = nullptr;
+        if (!upload_f16(pack_taps(m.w, m.oc, m.ic, m.k), &p, err)) return false;
+        *out = p;
+        return true;
+    };
+    // bias of one conv, or the sum of two (both segments land in one epilogue)
+    auto dev_b = [&](const std::vector<float>& b0, const std::vector<float>& b1, int oc,
+                     const float** out) -> bool {
+        *out = nullptr;
+        if (b0.empty() && b1.empty()) return true;
+        std::vector<float> s((size_t)oc, 0.0f);
+        for (size_t i = 0; i < b0.size(); ++i) s[i] += b0[i];
+        for (size_t i = 0; i < b1.size(); ++i) s[i] += b1[i];
+        float* p = nullptr;
+        if (!upload_f32(s, &p, err)) return false;
+        *out = p;
+        return true;
+    };
+    enum Role { R_STEM, R_XA, R_XB, R_A, R_ACC, R_TM, R_Z, R_POUT, R_PF, R_GD, R_GF };
+    std::vector<std::pair<int, int>> keys;  // (level, role) of each buffer
+    auto buf = [&](int level, int role, int c, bool phase) -> int {
+        for (size_t i = 0; i < keys.size(); ++i)
+            if (keys[i].first == level && keys[i].second == role) {
+                ebufs_[i].c = std::max(ebufs_[i].c, c);
+                return (int)i;
+            }
+        EBuf b;
+        b.level = level;
+        b.c = c;
+        b.phase = phase;
+        ebufs_.push_back(b);
+        keys.emplace_back(level, role);
+        return (int)ebufs_.size() - 1;
+    };
+    auto conv_step = [&](int level, int oc, int k0, int stride0, int ic0, EOperand x0,
+                         const __half* w0) {
+        EStep st;
+        st.kind = 0;
+        st.level = level;
+        st.oc = oc;
+        st.k0 = k0;
+        st.stride0 = stride0;
+        st.ic0 = ic0;
+        st.x0 = x0;
+        st.w0 = w0;
+        st.flops_px = 2.0 * oc * ic0 * k0 * k0;
+        return st;
+    };
+
+    // stem: 3x3, 1 -> M, bias + plain ReLU
+    {
+        MC st;
+        if (!take(st, 3, 1, 1)) return false;
+        if (st.oc != M || !(M == 16 || M == 32 || M == 64)) {
+            err = "eres2net stem must be a 3x3 conv from 1 channel to m_channels (16/32/64)";
+            return false;
+        }
+        if (st.b.empty()) st.b.assign((size_t)M, 0.0f);
+        std::vector<float> sw((size_t)M * 9);
+        for (int o = 0; o < M; ++o)
+            for (int kh = 0; kh < 3; ++kh)
+                for (int kw = 0; kw < 3; ++kw)
+                    sw[(size_t)o * 9 + kw * 3 + kh] = st.w[(size_t)o * 9 + kh * 3 + kw];
+        stem_oc_ = M;
+        if (!upload_f32(sw, &stem_w_, err) || !upload_f32(st.b, &stem_b_, err)) return false;
+        e_stem_buf_ = buf(0, R_STEM, M, false);
+    }
+
+    // AFF(x, ds) over C channels at `level` -> out (src/encoder_eres2net.cpp:91-101)
+    auto emit_aff = [&](int level, EOperand x, EOperand ds, int C, EOperand out,
+                        bool out_phase) -> bool {
+        MC la1, la2;
+        if (!take(la1, 1, 2 * C, 1)) return false;
+        const int Cq = la1.oc;
+        if (!take(la2, 1, Cq, 1)) return false;
+        if (la2.oc != C) {
+            err = "eres2net AFF: local_att conv2 must map back to " + std::to_string(C);
+            return false;
+        }
+        std::vector<float> wa((size_t)Cq * C), wb((size_t)Cq * C);
+        for (int o = 0; o < Cq; ++o)
+            for (int i = 0; i < C; ++i) {
+                wa[(size_t)o * C + i] = la1.w[(size_t)o * 2 * C + i];
+                wb[(size_t)o * C + i] = la1.w[(size_t)o * 2 * C + C + i];
+            }
+        const int z = buf(level, R_Z, Cq, false);
+        __half *pa = nullptr, *pb = nullptr;
+        if (!upload_f16(wa, &pa, err) || !upload_f16(wb, &pb, err)) return false;
+        EStep s1 = conv_step(level, Cq, 1, 1, C, x, pa);
+        s1.ic1 = C;
+        s1.x1 = ds;
+        s1.stride1 = 1;
+        s1.w1 = pb;
+        s1.flops_px = 2.0 * Cq * 2 * C;
+        s1.act = 1;  // SiLU
+        s1.y = EOperand{z, 0};
+        if (!dev_b(la1.b, {}, Cq, &s1.bias)) return false;
+        esteps_.push_back(s1);
+        const __half* w2 = nullptr;
+        if (!dev_w(la2, &w2)) return false;
+        EStep s2 = conv_step(level, C, 1, 1, Cq, EOperand{z, 0}, w2);
+        if (!dev_b(la2.b, {}, C, &s2.bias)) return false;
+        s2.act = 2;  // (x + ds) + tanh(.) * (x - ds)
+        s2.res = x;
+        s2.res2 = ds;
+        s2.y = out;
+        s2.y_phase = out_phase ? 1 : 0;
+        esteps_.push_back(s2);
+        return true;
+    };
+
+    int in_planes = M;
+    // Res2Net block (src/encoder_eres2net.cpp:111-137). x: G (stride 1) or P (stride 2)
+    // at level lo - (s == 2); outputs: yg (G, may be absent) and / or yp (P).
+    auto emit_block = [&](EOperand x, int s, int lo, int planes, bool is_aff, EOperand yg,
+                          EOperand yp) -> bool {
+        MC c1;
+        if (!take(c1, 1, in_planes, s)) return false;
+        if (c1.oc % S || (c1.oc / S) % 16) {
+            err = "eres2net: conv1 width must split into scale chunks of a multiple of 16";
+            return false;
+        }
+        const int w = c1.oc / S;
+        const int A = buf(lo, R_A, c1.oc, false), Acc = buf(lo, R_ACC, c1.oc, false);
+        const int Tm = buf(lo, R_TM, w, false);
+        const __half* pw = nullptr;
+        if (!dev_w(c1, &pw)) return false;
+        EStep st = conv_step(lo, c1.oc, 1, s, in_planes, x, pw);
+        if (!dev_b(c1.b, {}, c1.oc, &st.bias)) return false;
+        st.relu = 1;
+        st.clamp_hi = hi;
+        st.y = EOperand{A, 0};
+        esteps_.push_back(st);
+        for (int i = 0; i < S; ++i) {
+            const EOperand chunk{A, i * w};
+            EOperand cur = chunk;
+            if (i > 0) {
+                const EOperand sp{Acc, (i - 1) * w};
+                if (is_aff) {
+                    if (!emit_aff(lo, sp, chunk, w, EOperand{Tm, 0}, false)) return false;
+                } else {
+                    EStep ad;
+                    ad.kind = 1;
+                    ad.level = lo;
+                    ad.oc = w;
+                    ad.x0 = sp;
+                    ad.x1 = chunk;
+                    ad.y = EOperand{Tm, 0};
+                    esteps_.push_back(ad);
+                }
+                cur = EOperand{Tm, 0};
+            }
+            MC cv;
+            if (!take(cv, 3, w, 1)) return false;
+            if (cv.oc != w) {
+                err = "eres2net: chunk conv must keep the width";
+                return false;
+            }
+            if (!dev_w(cv, &pw)) return false;
+            EStep sc = conv_step(lo, w, 3, 1, w, cur, pw);
+            if (!dev_b(cv.b, {}, w, &sc.bias)) return false;
+            sc.relu = 1;
+            sc.clamp_hi = hi;
+            sc.y = EOperand{Acc, i * w};
+            esteps_.push_back(sc);
+        }
+        MC c3;
+        if (!take(c3, 1, c1.oc, 1)) return false;
+        if (c3.oc != 2 * planes) {
+            err = "eres2net: conv3 must produce 2 * planes channels";
+            return false;
+        }
+        if (!dev_w(c3, &pw)) return false;
+        EStep s3 = conv_step(lo, c3.oc, 1, 1, c1.oc, EOperand{Acc, 0}, pw);
+        std::vector<float> sb;
+        if (s != 1 || in_planes != 2 * planes) {  // 1x1 shortcut, fused as input segment 1
+            MC sh;
+            if (!take(sh, 1, in_planes, s)) return false;
+            if (sh.oc != 2 * planes) {
+                err = "eres2net: shortcut must produce 2 * planes channels";
+                return false;
+            }
+            __half* p1 = nullptr;
+            if (!upload_f16(sh.w, &p1, err)) return false;
+            s3.x1 = x;
+            s3.ic1 = in_planes;
+            s3.stride1 = s;
+            s3.w1 = p1;
+            s3.flops_px += 2.0 * c3.oc * in_planes;
+            sb = sh.b;
+        } else {
+            s3.res = x;
+        }
+        if (!dev_b(c3.b, sb, c3.oc, &s3.bias)) return false;
+        s3.relu = 1;
+        s3.clamp_hi = hi;
+        if (yg.buf >= 0) {
+            s3.y = yg;
+            s3.y2 = yp;
+        } else {
+            s3.y = yp;
+            s3.y_phase = 1;
+        }
+        esteps_.push_back(s3);
+        in_planes = 2 * planes;
+        return true;
+    };
+
+    // body (src/encoder_eres2net.cpp:200-218)
+    EOperand x{e_stem_buf_, 0};
+    EOperand lay_g[4], lay_p[4], fused_p;
+    int lev = 0;
+    for (int l = 0; l < 4; ++l) {
+        const int planes = M << l;
+        if (l > 0) x = lay_p[l - 1];
+        for (int b = 0; b < nb[l]; ++b) {
+            const int s = (b == 0 && l > 0) ? 2 : 1;
+            const int lo = lev + (s == 2 ? 1 : 0);
+            const bool last = b == nb[l] - 1;
+            EOperand yg, yp;
+            if (!last || l > 0) {
+                // ping-pong: never the buffer holding x
+                const int ra = buf(lo, R_XA, 2 * planes, false);
+                const int rb = buf(lo, R_XB, 2 * planes, false);
+                yg = EOperand{x.buf == ra ? rb : ra, 0};
+            }
+            if (last && l < 3) yp = EOperand{buf(lo, R_POUT, 2 * planes, true), 0};
+            if (!emit_block(x, s, lo, planes, l >= 2, yg, yp)) return false;
+            x = yg;
+            lev = lo;
+        }
+        lay_p[l] = (l < 3) ? EOperand{buf(lev, R_POUT, 2 * planes, true), 0} : EOperand{};
+        lay_g[l] = x;
+        if (l >= 1) {
+            // previous-scale feature: o1 (P) for layer 2, then the fused f12 / f123 (P)
+            const EOperand src = (l == 1) ? lay_p[0] : fused_p;
+            MC d;
+            if (!take(d, 3, planes, 2)) return false;
+            if (d.oc != 2 * planes) {
+                err = "eres2net: cross-stage downsample must produce 2 * planes channels";
+                return false;
+            }
+            const __half* pd = nullptr;
+            if (!dev_w(d, &pd)) return false;
+            const int gd = buf(lev, R_GD, 2 * planes, false);
+            EStep sd = conv_step(lev, d.oc, 3, 2, planes, src, pd);
+            if (!dev_b(d.b, {}, d.oc, &sd.bias)) return false;
+            sd.y = EOperand{gd, 0};
+            esteps_.push_back(sd);
+            const bool final_stage = (l == 3);
+            const EOperand out = final_stage ? EOperand{buf(lev, R_GF, 2 * planes, false), 0}
+                                             : EOperand{buf(lev, R_PF, 2 * planes, true), 0};
+            if (!emit_aff(lev, lay_g[l], EOperand{gd, 0}, 2 * planes, out, !final_stage))
+                return false;
+            fused_p = out;
+            if (final_stage) {
+                e_out_buf_ = out.buf;
+                e_out_level_ = lev;
+            }
+        }
+    }
+    if (idx != wn.size()) {
+        err = "eres2net manifest has " + std::to_string(wn.size()) + " convs, the topology uses " +
+              std::to_string(idx);
+        return false;
+    }
+    // embedding head (src/encoder_eres2net.cpp:228-250)
+    int F = cfg_.n_mels;
+    for (int l = 0; l < e_out_level_; ++l) F = half_extent(F);
+    const int cl = ebufs_[e_out_buf_].c;
+    const GgufTensor* t = g.tensor(g.str(pre + "seg_weight"));
+    if (!t || t->ne.size() < 2) {
+        err = "missing or malformed eres2net seg_weight";
+        return false;
+    }
+    const int P = (int)t->ne[0], D = (int)t->ne[1];
+    if (D != cfg_.emb_dim || P != 2 * cl * F) {
+        err = "eres2net seg_weight shape does not match the backbone (" + std::to_string(P) +
+              " vs " + std::to_string(2 * cl * F) + ")";
+        return false;
+    }
+    std::vector<float> sw, sb;
+    if (!g.to_f32(*t, sw, err)) return false;
+    if (!L.vec(g.str(pre + "seg_bias"), sb, D)) return false;
+    pooled_ = P;
+    if (!upload_f32(sw, &seg_w_, err) || !upload_f32(sb, &seg_b_, err)) return false;
+    // metadata levels (valid lengths per resolution); activations live in ebufs_
+    levels_.assign((size_t)e_out_level_ + 1, Level{});
+    return true;
+}
+
 bool Engine::supported(std::string& err) const {
-    if (cfg_.arch != "wespeaker_resnet34") {
+    if (cfg_.arch != "wespeaker_resnet34" && cfg_.arch != "eres2net") {
         err = "voicedetect: arch '" + cfg_.arch + "' is not implemented by the B200 engine";
         return false;
     }
@@ -382,6 +752,16 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
         }
         T = half_extent(T);
         F = half_extent(F);
+    }
+    std::vector<int> lt(1, t_max), lf(1, cfg_.n_mels);
+    for (size_t l = 1; l < std::max<size_t>(levels_.size(), 1); ++l) {
+        lt.push_back(half_extent(lt.back()));
+        lf.push_back(half_extent(lf.back()));
+    }
+    for (EBuf& eb : ebufs_) {
+        const long long rows = eb.phase ? vdb_phase_rows(B, lt[eb.level], lf[eb.level])
+                                        : vdb_grid_rows(B, lt[eb.level], lf[eb.level]);
+        if (!grow(&eb.p, eb.bytes, (size_t)rows * eb.c * sizeof(__half))) return 1;
     }
     if (!grow((void**)&feats_, feats_bytes_, (size_t)B * t_max * cfg_.n_mels * sizeof(float)))
         return 1;
@@ -454,12 +834,18 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
         err = vdb_last_error();
         return 1;
     }
+    const bool eres = cfg_.arch == "eres2net";
     if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
-                     stem_oc_, mean_, levels_[0].g[0], st)) {
+                     stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0], st)) {
         err = vdb_last_error();
         return 1;
     }
     launches += cfg_.cmn ? 3 : 2;
+    if (eres) {
+        if (run_eres2net(B, t_max, tv_sum, st, d_out, launches, err)) return 1;
+        last_launches += launches;
+        return 0;
+    }
     // Backbone.
     int lev = 0, T = t_max, F = cfg_.n_mels;
     int cur = 0;            // index of the G buffer holding the block input
@@ -549,6 +935,85 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     }
     launches += 1;
     last_launches += launches;
+    return 0;
+}
+
+int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
+                         float* d_out, long long& launches, std::string& err) {
+    const size_t nlev = levels_.size();
+    std::vector<int> lt(1, t_max), lf(1, cfg_.n_mels);
+    for (size_t l = 1; l < nlev; ++l) {
+        lt.push_back(half_extent(lt.back()));
+        lf.push_back(half_extent(lf.back()));
+    }
+    auto ptr = [&](const EOperand& o) -> void* {
+        if (o.buf < 0) return nullptr;
+        return static_cast<__half*>(ebufs_[o.buf].p) + o.c0;
+    };
+    auto ld = [&](const EOperand& o) -> int { return o.buf < 0 ? 0 : ebufs_[o.buf].c; };
+    for (const EStep& s : esteps_) {
+        const int To = lt[s.level], Fo = lf[s.level];
+        if (s.kind == 1) {
+            if (vdb_add(ptr(s.x0), ld(s.x0), ptr(s.x1), ld(s.x1), ptr(s.y), ld(s.y),
+                        vdb_grid_rows(B, To, Fo), s.oc, st)) {
+                err = vdb_last_error();
+                return 1;
+            }
+            ++launches;
+            continue;
+        }
+        if (s.y2.buf >= 0 && ebufs_[s.y2.buf].c != s.oc) {
+            err = "eres2net plan: second output must be a dense tensor";
+            return 1;
+        }
+        vdb_conv_args a{};
+        a.batch = B;
+        a.t_out = To;
+        a.f_out = Fo;
+        a.oc = s.oc;
+        a.k0 = s.k0;
+        a.stride0 = s.stride0;
+        a.ic0 = s.ic0;
+        a.x0 = ptr(s.x0);
+        a.ldx0 = ld(s.x0);
+        a.w0 = s.w0;
+        if (s.x1.buf >= 0) {
+            a.x1 = ptr(s.x1);
+            a.ldx1 = ld(s.x1);
+            a.ic1 = s.ic1;
+            a.stride1 = s.stride1;
+            a.w1 = s.w1;
+        }
+        a.bias = s.bias;
+        a.residual = ptr(s.res);
+        a.ldr = ld(s.res);
+        a.residual2 = ptr(s.res2);
+        a.ldr2 = ld(s.res2);
+        a.relu = s.relu;
+        a.clamp_hi = s.clamp_hi;
+        a.act = s.act;
+        a.tvalid = meta_ + (size_t)s.level * B;
+        a.y = ptr(s.y);
+        a.ldy = ld(s.y);
+        a.y_phase = s.y_phase;
+        a.y2 = ptr(s.y2);
+        a.err = errword_;
+        const int pe = prof_begin(st);
+        if (vdb_conv(&a, st)) {
+            err = vdb_last_error();
+            return 1;
+        }
+        prof_end(pe, st, s.flops_px * (double)Fo * (double)tv_sum[s.level]);
+        ++launches;
+    }
+    const int lev = e_out_level_;
+    if (pool_embed_launch(ebufs_[e_out_buf_].p, meta_ + (size_t)lev * B, B, lt[lev], lf[lev],
+                          ebufs_[e_out_buf_].c, seg_w_, seg_b_, nullptr, cfg_.emb_dim, var_eps_,
+                          cfg_.l2 ? 1 : 0, meta_ + nlev * B, d_out, nullptr, st)) {
+        err = vdb_last_error();
+        return 1;
+    }
+    ++launches;
     return 0;
 }
 

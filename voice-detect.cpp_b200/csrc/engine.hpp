@@ -21,6 +21,8 @@
 
 namespace vdb {
 
+class Gguf;
+
 struct EngineConfig {
     std::string arch;
     int emb_dim = 0;
@@ -37,6 +39,35 @@ struct ResBlockDev {
     __half* w2 = nullptr;   // [oc][9][oc]
     float* b2 = nullptr;    // conv2 bias (+ downsample bias when fused)
     __half* wd = nullptr;   // [oc][ic] or nullptr (identity shortcut)
+};
+
+// ERes2Net runs from a plan compiled once at load from the conv manifest
+// (src/encoder_eres2net.cpp:147-226 replayed with a running conv index): a flat
+// list of conv / add steps over named activation buffers. An operand is a
+// buffer plus a channel offset, so the Res2Net split and concat are views.
+struct EOperand {
+    int buf = -1;
+    int c0 = 0;
+};
+
+struct EStep {
+    int kind = 0;    // 0: vdb_conv, 1: vdb_add (y = x0 + x1 over oc channels)
+    int level = 0;   // resolution level of the output
+    int oc = 0, k0 = 1, stride0 = 1, ic0 = 0, ic1 = 0, stride1 = 1;
+    EOperand x0, x1, res, res2, y, y2;
+    const __half* w0 = nullptr;
+    const __half* w1 = nullptr;
+    const float* bias = nullptr;
+    int relu = 0, act = 0, y_phase = 0;
+    float clamp_hi = 0.0f;
+    double flops_px = 0.0;   // algorithmic FLOPs per valid output pixel
+};
+
+struct EBuf {
+    int level = 0, c = 0;
+    bool phase = false;      // P layout (for a stride-2 consumer) instead of G
+    void* p = nullptr;
+    size_t bytes = 0;
 };
 
 class Engine {
@@ -85,8 +116,13 @@ private:
     Engine() = default;
     int run_bucket(const float* d_pcm, const long long* h_off, const int* h_ns,
                    const int* h_outrow, int B, cudaStream_t st, float* d_out, std::string& err);
+    int run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
+                     float* d_out, long long& launches, std::string& err);
     int ensure_workspace(int B, int t_max, std::string& err);
     void free_workspace();
+    bool load_eres2net(const Gguf& g, std::string& err);
+    bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
+    bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
 
     EngineConfig cfg_;
     int device_ = 0;
@@ -103,6 +139,10 @@ private:
     int pooled_ = 0;
     float var_eps_ = 1e-8f;
     std::vector<void*> weight_allocs_;
+    // ERes2Net plan
+    std::vector<EBuf> ebufs_;
+    std::vector<EStep> esteps_;
+    int e_stem_buf_ = -1, e_out_buf_ = -1, e_out_level_ = 0;
     // workspace (grow-only)
     struct Level {
         int c = 0;
