@@ -412,7 +412,7 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
                   std::to_string(sn[i]) + " from " + std::to_string(m.ic);
             return false;
         }
-        if (k > 1 || ic > 1) {
+        if (ic > 1) {  // every conv but the IC = 1 stem runs on the tensor-core kernel
             if (m.oc % 16 || m.ic % 16) {
                 err = "eres2net conv " + std::to_string(i) + ": channels must be multiples of 16";
                 return false;

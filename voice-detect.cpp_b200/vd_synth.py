@@ -169,7 +169,7 @@ def f16_model(m: dict) -> dict:
 # ---------------------------------------------------------------------------
 def eres2net_model(seed: int = 0, n_mels: int = N_MELS, m_channels: int = 32,
                    num_blocks=(3, 4, 6, 3), base_width: int = 32, scale: int = 2,
-                   emb_dim: int = 512) -> dict:
+                   emb_dim: int = 512, calibrate: bool = True) -> dict:
     """Synthetic 3D-Speaker ERes2Net with BatchNorm folded into every conv, as a
     flat conv list in the reference's forward-EXECUTION order
     (src/encoder_eres2net.cpp:147-226; manifest src/model_loader.hpp:68-80):
@@ -182,7 +182,14 @@ def eres2net_model(seed: int = 0, n_mels: int = N_MELS, m_channels: int = 32,
       after layer2: layer1_downsample 3x3 s2 (no bias) + AFF(o2, .)
       after layer3: layer2_downsample + AFF; after layer4: layer3_downsample + AFF
     AFF(C): la1 1x1 2C->C/4 (+b) -> SiLU -> la2 1x1 C/4->C (+b) -> tanh.
-    Layers 3 and 4 fuse their chunks with AFF, layers 1 and 2 add them."""
+    Layers 3 and 4 fuse their chunks with AFF, layers 1 and 2 add them.
+
+    calibrate=True (default) replaces the random BatchNorm statistics by the
+    statistics of each conv's actual output on a seeded calibration input, in
+    execution order, as a trained model's running statistics are (gamma 1, beta
+    N(0, 0.1)). With random statistics the 96-conv network is chaotic: rounding
+    its activations to f16 alone moves the embedding to cosine ~0.9994 against
+    f32, so no f16 implementation could meet a 0.9999 parity gate on it."""
     rng = np.random.default_rng(seed)
     convs: list[dict] = []
 
@@ -220,13 +227,86 @@ def eres2net_model(seed: int = 0, n_mels: int = N_MELS, m_channels: int = 32,
             aff(2 * planes)
     c_last = 2 * planes_list[-1]
     pooled = 2 * c_last * f
-    return {
+    m = {
         "arch": "eres2net", "convs": convs, "m_channels": m_channels, "scale": scale,
         "num_blocks": list(num_blocks), "relu_clamp": 20.0, "var_eps": 1e-8,
         "seg_w": (rng.standard_normal((emb_dim, pooled)) / np.sqrt(pooled)).astype(np.float32),
         "seg_b": rng.normal(0.0, 0.01, emb_dim).astype(np.float32),
         "l2_normalize": True, "n_mels": n_mels,
     }
+    if calibrate:
+        _calibrate_eres2net(m, np.random.default_rng(seed + 7919))
+    return m
+
+
+def _calibrate_eres2net(m: dict, rng, frames: int = 200) -> None:
+    """Re-fold every biased conv of `m` in place with BatchNorm statistics measured
+    on its own output: walks the ERes2Net forward (src/encoder_eres2net.cpp:111-226)
+    in float64 on a seeded N(0, 2^2) feature map, and for conv i (weights already
+    holding the random init) sets w <- w / sqrt(var + 1e-5), b <- beta - mean /
+    sqrt(var + 1e-5) from the per-channel mean / variance of w * x over all output
+    positions, beta ~ N(0, 0.1). BN-less convs (the cross-stage downsamples) keep
+    their weights."""
+    import torch
+    import torch.nn.functional as Fn
+
+    convs = m["convs"]
+    it = iter(range(len(convs)))
+    hi = float(m["relu_clamp"])
+    S = int(m["scale"])
+    M = int(m["m_channels"])
+    nb = m["num_blocks"]
+
+    def conv(x):
+        c = convs[next(it)]
+        w = torch.from_numpy(c["w"].astype(np.float64))
+        k = w.shape[-1]
+        y = Fn.conv2d(x, w, stride=c["stride"], padding=(k - 1) // 2)
+        if c["b"] is None:
+            return y
+        mu = y.mean((0, 2, 3))
+        sc = 1.0 / torch.sqrt(y.var((0, 2, 3)) + 1e-5)
+        beta = torch.from_numpy(rng.normal(0.0, 0.1, y.shape[1]))
+        c["w"] = (w * sc.view(-1, 1, 1, 1)).numpy().astype(np.float32)
+        c["b"] = (beta - mu * sc).numpy().astype(np.float32)
+        return (y - mu.view(1, -1, 1, 1)) * sc.view(1, -1, 1, 1) + beta.view(1, -1, 1, 1)
+
+    def aff(x, ds):
+        z = Fn.silu(conv(torch.cat([x, ds], 1)))
+        return (x + ds) + torch.tanh(conv(z)) * (x - ds)
+
+    in_planes = [M]
+
+    def block(x, planes, is_aff, stride):
+        out = conv(x).clamp(0, hi)
+        w = out.shape[1] // S
+        sp, acc = None, []
+        for i in range(S):
+            ch = out[:, i * w:(i + 1) * w]
+            cur = ch if i == 0 else (aff(sp, ch) if is_aff else sp + ch)
+            sp = conv(cur).clamp(0, hi)
+            acc.append(sp)
+        o = conv(torch.cat(acc, 1))
+        res = conv(x) if (stride != 1 or in_planes[0] != 2 * planes) else x
+        in_planes[0] = 2 * planes
+        return (o + res).clamp(0, hi)
+
+    def layer(x, planes, n, is_aff, stride):
+        for b in range(n):
+            x = block(x, planes, is_aff, stride if b == 0 else 1)
+        return x
+
+    with torch.no_grad():
+        feats = torch.from_numpy(rng.standard_normal((1, 1, int(m["n_mels"]), frames)) * 2.0)
+        h = torch.relu(conv(feats))
+        o1 = layer(h, M, nb[0], False, 1)
+        o2 = layer(o1, 2 * M, nb[1], False, 2)
+        f12 = aff(o2, conv(o1))
+        o3 = layer(o2, 4 * M, nb[2], True, 2)
+        f123 = aff(o3, conv(f12))
+        o4 = layer(o3, 8 * M, nb[3], True, 2)
+        aff(o4, conv(f123))
+    assert next(it, None) is None, "calibration walk did not use every conv"
 
 
 def tiny_eres2net_model(seed: int = 0, n_mels: int = 16) -> dict:
