@@ -373,6 +373,182 @@ def run_b200(args) -> int:
     return 0
 
 
+ERES_METRIC = "utterance-sec/sec ERes2Net-base embed"
+
+
+def cpu_reference_eres2net(m: dict, clips, threads: int):
+    """The reference's CPU conv kernels (src/directconv.cpp blocked island, as
+    src/encoder_eres2net.cpp routes them) + FBank on `clips`; returns
+    (audio_seconds, wall_seconds)."""
+    import oracle
+    oracle.ref_lib().vdref_set_threads(threads)
+    R = oracle.RefERes2Net(m)
+    R.embed(oracle.ref_fbank(clips[0][:32000]))  # weight packing outside the timing
+    t0 = time.perf_counter()
+    for c in clips:
+        R.embed(oracle.ref_fbank(c))
+    return sum(len(c) for c in clips) / SR, time.perf_counter() - t0
+
+
+def run_eres2net(args) -> int:
+    """ERes2Net-base (m_channels 32, blocks 3/4/6/3, scale 2, AFF),
+    f16 weights, a batch of `--eres-batch` 10 s clips (998 frames) per GPU and step.
+    N > 1 runs one such batch per rank and all-gathers the embeddings (weak)."""
+    import torch
+    import torch.distributed as dist
+    import vd_b200
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    if args.impl == "reference":
+        if rank == 0:
+            m = vd_synth.quantize_model_f16(vd_synth.eres2net_model(SEED))
+            pool = make_pool(4, 10.0)
+            threads = os.cpu_count() or 1
+            times, audio_tot = [], 0.0
+            for s in range(args.warmup + args.steps):
+                audio, wall = cpu_reference_eres2net(m, pool[:args.ref_eres_clips], threads)
+                if s >= args.warmup:
+                    times.append(wall)
+                    audio_tot += audio
+            value = audio_tot / sum(times)
+            print(json.dumps({
+                "impl": "reference", "metric": ERES_METRIC, "value": value, "unit": UNIT,
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": eres_config(args, world),
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
+                                 "kind": "reference",
+                                 "sample": f"{args.ref_eres_clips} x 10 s clips per step; "
+                                           "reference FBank + blocked directconv kernels "
+                                           "compiled unmodified, restated ERes2Net glue"},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    tmp = tempfile.mkdtemp(prefix="vdbench_")
+    m = vd_synth.eres2net_model(SEED)
+    gguf = os.path.join(tmp, "eres2net_f16.gguf")
+    vd_synth.write_eres2net_gguf(gguf, m, "f16")
+    model = vd_b200.Model(gguf)
+    B, n = args.eres_batch, 10 * SR
+    pool = make_pool(16, 10.0)
+    host_pcm = np.concatenate([pool[(rank * B + i) % len(pool)] for i in range(B)])
+    offs = np.arange(B, dtype=np.int64) * n
+    lens = [n] * B
+    d_pcm = torch.from_numpy(host_pcm).to(dev)
+    d_out = torch.zeros(B, model.dim, device=dev)
+    gathered = torch.empty(world * B, model.dim, device=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    torch.cuda.synchronize()
+
+    def step():
+        model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
+        gather_embeddings(d_out, gathered, world)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    model.profile(True)
+    model.profile_read()
+    launches = 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+        launches += model.last_launches()
+    end.record(stream)
+    torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(end)
+    conv_ms, conv_flops, conv_n = model.profile_read()
+    model.profile(False)
+    clk = clocks.stop()
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    audio_step = world * B * n / SR
+    value = audio_step * args.steps / (max_ms / 1e3)
+    clips = [host_pcm[i * n:(i + 1) * n] for i in range(B)]
+    model.embed_batch(clips[:8])
+    e2e_times = []
+    for _ in range(args.e2e_steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.embed_batch(clips)
+        e2e_times.append(time.perf_counter() - t0)
+    e_t = torch.tensor([sum(e2e_times) / len(e2e_times)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    achieved = conv_flops / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
+    result = {
+        "metric": ERES_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 (f32 accumulate)",
+        "data": "synthetic (seeded harmonic+pink-noise clips, calibrated random weights)",
+        "config": eres_config(args, world),
+        "e2e": {"value": audio_step / float(e_t.item()), "unit": UNIT,
+                "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
+                "api": "voicedetect_capi_embed_pcm_batch"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
+                     if peaks else "fallback 1.4 PFLOP/s sustained",
+                     "traffic": None, "conv_launches": conv_n,
+                     "conv_ms_per_step": conv_ms / args.steps,
+                     "conv_tflop_per_step": conv_flops / args.steps / 1e12},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        audio, wall = cpu_reference_eres2net(vd_synth.quantize_model_f16(m),
+                                             clips[:args.ref_eres_clips], threads)
+        result["cpu_baseline"] = {
+            "value": audio / wall, "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{args.ref_eres_clips} x 10 s clips of the same batch; reference FBank "
+                      "+ blocked directconv kernels compiled unmodified (oracle/_ref), "
+                      "restated ERes2Net glue, all host threads"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def eres_config(args, world):
+    return {"workload": f"BASELINE config 2: ERes2Net-base f16 embed, batch {args.eres_batch} "
+                        "x 10 s clips (998 frames) per GPU",
+            "model": "eres2net (m_channels 32, blocks 3/4/6/3, baseWidth 32, scale 2, AFF; "
+                     "synthetic weights, BN folded, f16)",
+            "global_batch": world * args.eres_batch, "seq_len": "10 s (998 frames)",
+            "parallelism": f"dp{world}", "l2_flush": "activations larger than L2"}
+
+
 # BASELINE config 1: every distinct ResNet34 3x3 conv shape (stage entries carry the
 # fused 1x1 downsample in conv2), batch B, T = 300 frames, 80 mels.
 SWEEP_SHAPES = [  # (ic, oc, t_in, f_in, stride, fused_down)
@@ -457,9 +633,16 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--ref-clips", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eres2net", action="store_true",
+                    help="BASELINE config 2 (ERes2Net-base f16, 10 s clips) instead of the "
+                         "ResNet34 headline workload")
+    ap.add_argument("--eres-batch", type=int, default=256)
+    ap.add_argument("--ref-eres-clips", type=int, default=8)
     args = ap.parse_args()
     if args.op_sweep:
         return run_sweep(args)
+    if args.eres2net:
+        return run_eres2net(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)
