@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstring>
 #include <numeric>
+#include <thread>
 
 #include "gguf.hpp"
 #include "vdb_internal.h"
@@ -108,6 +109,14 @@ Engine::~Engine() {
     for (cudaEvent_t& ev : stage_ev_)
         if (ev) cudaEventDestroy(ev);
     for (cudaEvent_t ev : prof_ev_) cudaEventDestroy(ev);
+    for (int s = 0; s < 2; ++s) {
+        if (h2d_ev_[s]) cudaEventDestroy(h2d_ev_[s]);
+        if (comp_ev_[s]) cudaEventDestroy(comp_ev_[s]);
+    }
+    if (copy_stream_) {
+        cudaStreamSynchronize(copy_stream_);
+        cudaStreamDestroy(copy_stream_);
+    }
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -142,12 +151,14 @@ void Engine::free_workspace() {
     cudaFreeHost(h_stage_);
     h_stage_ = nullptr;
     h_stage_bytes_ = 0;
-    cudaFreeHost(h_pcm_);
-    h_pcm_ = nullptr;
-    h_pcm_bytes_ = 0;
-    cudaFree(d_pcm_);
-    d_pcm_ = nullptr;
-    d_pcm_bytes_ = 0;
+    for (int s = 0; s < 2; ++s) {
+        cudaFreeHost(h_ring_[s]);
+        cudaFree(d_ring_[s]);
+        h_ring_[s] = nullptr;
+        d_ring_[s] = nullptr;
+        ring_used_[s] = false;
+    }
+    ring_bytes_ = 0;
     cudaFreeHost(h_out_);
     h_out_ = nullptr;
     cudaFree(d_out_);
@@ -184,6 +195,11 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
     if (cudaStreamCreateWithFlags(&e->stream_, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->stage_ev_[0], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&e->stage_ev_[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&e->copy_stream_, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->h2d_ev_[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->h2d_ev_[1], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->comp_ev_[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->comp_ev_[1], cudaEventDisableTiming) != cudaSuccess ||
         cudaMalloc(&e->errword_, sizeof(int)) != cudaSuccess ||
         cudaMemset(e->errword_, 0, sizeof(int)) != cudaSuccess) {
         err = "CUDA stream/alloc failed";
@@ -1035,33 +1051,73 @@ int Engine::embed_device(const float* d_pcm, const long long* offsets, const int
             err = "voicedetect: FBank produced no frames (clip " + std::to_string(i) + ")";
             return 1;
         }
+    std::vector<int> order;
+    std::vector<size_t> bk;
+    plan_buckets(nsamp, n, order, bk);
+    last_launches = 0;
+    std::vector<long long> bo;
+    std::vector<int> bn;
+    for (size_t k = 0; k + 1 < bk.size(); ++k) {
+        bo.clear();
+        bn.clear();
+        for (size_t j = bk[k]; j < bk[k + 1]; ++j) {
+            bo.push_back(offsets[order[j]]);
+            bn.push_back(nsamp[order[j]]);
+        }
+        if (run_bucket(d_pcm, bo.data(), bn.data(), order.data() + bk[k], (int)bo.size(), st,
+                       d_out, err))
+            return 1;
+    }
+    return 0;
+}
+
+void Engine::plan_buckets(const int* nsamp, int n, std::vector<int>& order,
+                          std::vector<size_t>& bk) const {
     // Longest first; consecutive clips of similar length share a bucket.
-    std::vector<int> order(n);
+    order.resize((size_t)n);
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(),
                      [&](int a, int b) { return nsamp[a] > nsamp[b]; });
-    last_launches = 0;
-    std::vector<long long> bo;
-    std::vector<int> bn, br;
+    bk.assign(1, 0);
     size_t i = 0;
     while (i < order.size()) {
         const int t0 = frames_of(nsamp[order[i]], cfg_.win, cfg_.hop);  // bucket's t_max
         size_t j = i;
-        bo.clear();
-        bn.clear();
-        br.clear();
-        while (j < order.size() && (int)bo.size() < max_clips &&
-               (long long)(bo.size() + 1) * t0 <= std::max<long long>(max_frames, t0)) {
-            bo.push_back(offsets[order[j]]);
-            bn.push_back(nsamp[order[j]]);
-            br.push_back(order[j]);
+        while (j < order.size() && (long long)(j - i) < max_clips &&
+               (long long)(j - i + 1) * t0 <= std::max<long long>(max_frames, t0))
             ++j;
-        }
-        if (run_bucket(d_pcm, bo.data(), bn.data(), br.data(), (int)bo.size(), st, d_out, err))
-            return 1;
+        bk.push_back(j);
         i = j;
     }
-    return 0;
+}
+
+// Copies clips into one pinned buffer, splitting the bytes over a few threads
+// when there are many (a single core's memcpy would not keep up with the GPU).
+static void gather_clips(float* dst, const float* const* pcm, const int* nsamp,
+                         const int* idx, int count) {
+    std::vector<size_t> off((size_t)count + 1, 0);
+    for (int k = 0; k < count; ++k) off[k + 1] = off[k] + (size_t)nsamp[idx[k]];
+    const size_t total = off[count];
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const int nt = (int)std::min<size_t>(std::min(8u, hw), 1 + total / (4u << 20));
+    auto work = [&](int t) {
+        // thread t copies the sample range [t*total/nt, (t+1)*total/nt)
+        const size_t lo = total * t / nt, hi = total * (t + 1) / nt;
+        int k = (int)(std::upper_bound(off.begin(), off.end(), lo) - off.begin()) - 1;
+        for (size_t pos = lo; pos < hi && k < count; ++k) {
+            const size_t a = std::max(pos, off[k]), b = std::min(hi, off[k + 1]);
+            if (b > a) std::memcpy(dst + a, pcm[idx[k]] + (a - off[k]), (b - a) * sizeof(float));
+            pos = b;
+        }
+    };
+    if (nt <= 1) {
+        work(0);
+        return;
+    }
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; ++t) th.emplace_back(work, t);
+    work(0);
+    for (std::thread& x : th) x.join();
 }
 
 int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
@@ -1075,32 +1131,47 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
         err = "cudaSetDevice failed";
         return 1;
     }
-    std::vector<long long> off(n);
-    long long total = 0;
     for (int i = 0; i < n; ++i) {
         if (nsamp[i] < 0) {
             err = "negative sample count";
             return 1;
         }
-        off[i] = total;
-        total += nsamp[i];
-    }
-    const size_t pcm_bytes = std::max<size_t>((size_t)total * sizeof(float), 16);
-    if (pcm_bytes > h_pcm_bytes_) {
-        cudaFreeHost(h_pcm_);
-        cudaFree(d_pcm_);
-        h_pcm_ = nullptr;
-        d_pcm_ = nullptr;
-        h_pcm_bytes_ = d_pcm_bytes_ = 0;
-        if (cudaMallocHost(&h_pcm_, pcm_bytes) != cudaSuccess ||
-            cudaMalloc(&d_pcm_, pcm_bytes) != cudaSuccess) {
-            err = "out of memory (PCM staging)";
+        if (frames_of(nsamp[i], cfg_.win, cfg_.hop) <= 0) {  // src/model.cpp:26-29
+            err = "voicedetect: FBank produced no frames (clip " + std::to_string(i) + ")";
             return 1;
         }
-        h_pcm_bytes_ = d_pcm_bytes_ = pcm_bytes;
+    }
+    std::vector<int> order;
+    std::vector<size_t> bk;
+    plan_buckets(nsamp, n, order, bk);
+    // ring slots hold the largest bucket the policy allows (and this call's largest)
+    size_t need = ((size_t)max_frames * cfg_.hop + (size_t)max_clips * cfg_.win) * sizeof(float);
+    for (size_t k = 0; k + 1 < bk.size(); ++k) {
+        size_t b = 0;
+        for (size_t j = bk[k]; j < bk[k + 1]; ++j) b += (size_t)nsamp[order[j]] * sizeof(float);
+        need = std::max(need, b);
+    }
+    if (need > ring_bytes_) {
+        VDB_CHECK_CUDA(cudaDeviceSynchronize());
+        for (int s = 0; s < 2; ++s) {
+            cudaFreeHost(h_ring_[s]);
+            cudaFree(d_ring_[s]);
+            h_ring_[s] = nullptr;
+            d_ring_[s] = nullptr;
+            ring_used_[s] = false;
+        }
+        ring_bytes_ = 0;
+        for (int s = 0; s < 2; ++s)
+            if (cudaMallocHost(&h_ring_[s], need) != cudaSuccess ||
+                cudaMalloc(&d_ring_[s], need) != cudaSuccess) {
+                err = "out of memory (PCM staging)";
+                return 1;
+            }
+        ring_bytes_ = need;
     }
     const size_t ob = (size_t)n * cfg_.emb_dim * sizeof(float);
     if (ob > out_bytes_) {
+        VDB_CHECK_CUDA(cudaDeviceSynchronize());
         cudaFreeHost(h_out_);
         cudaFree(d_out_);
         h_out_ = nullptr;
@@ -1112,11 +1183,37 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
         }
         out_bytes_ = ob;
     }
-    for (int i = 0; i < n; ++i)
-        if (nsamp[i] > 0) std::memcpy(h_pcm_ + off[i], pcm[i], sizeof(float) * nsamp[i]);
-    VDB_CHECK_CUDA(cudaMemcpyAsync(d_pcm_, h_pcm_, sizeof(float) * (size_t)total,
-                                   cudaMemcpyHostToDevice, stream_));
-    if (embed_device(d_pcm_, off.data(), nsamp, n, d_out_, stream_, err)) return 1;
+    last_launches = 0;
+    std::vector<long long> bo;
+    std::vector<int> bn;
+    for (size_t k = 0; k + 1 < bk.size(); ++k) {
+        const int s = (int)(k & 1);
+        const int cnt = (int)(bk[k + 1] - bk[k]);
+        const int* idx = order.data() + bk[k];
+        // the pinned slot is free once its previous H2D copy finished
+        if (ring_used_[s]) VDB_CHECK_CUDA(cudaEventSynchronize(h2d_ev_[s]));
+        gather_clips(h_ring_[s], pcm, nsamp, idx, cnt);
+        bo.assign((size_t)cnt, 0);
+        bn.assign((size_t)cnt, 0);
+        long long tot = 0;
+        for (int j = 0; j < cnt; ++j) {
+            bo[j] = tot;
+            bn[j] = nsamp[idx[j]];
+            tot += bn[j];
+        }
+        // the device slot is free once the bucket that last read it finished
+        if (ring_used_[s]) VDB_CHECK_CUDA(cudaStreamWaitEvent(copy_stream_, comp_ev_[s], 0));
+        VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot * sizeof(float),
+                                       cudaMemcpyHostToDevice, copy_stream_));
+        VDB_CHECK_CUDA(cudaEventRecord(h2d_ev_[s], copy_stream_));
+        VDB_CHECK_CUDA(cudaStreamWaitEvent(stream_, h2d_ev_[s], 0));
+        ring_used_[s] = true;
+        if (run_bucket(d_ring_[s], bo.data(), bn.data(), idx, cnt, stream_, d_out_, err)) {
+            cudaStreamSynchronize(stream_);
+            return 1;
+        }
+        VDB_CHECK_CUDA(cudaEventRecord(comp_ev_[s], stream_));
+    }
     VDB_CHECK_CUDA(cudaMemcpyAsync(h_out_, d_out_, ob, cudaMemcpyDeviceToHost, stream_));
     VDB_CHECK_CUDA(cudaStreamSynchronize(stream_));
     if (check_device_error(err)) return 1;

@@ -116,6 +116,10 @@ private:
     Engine() = default;
     int run_bucket(const float* d_pcm, const long long* h_off, const int* h_ns,
                    const int* h_outrow, int B, cudaStream_t st, float* d_out, std::string& err);
+    // Length-sorted buckets: clip indices longest first in `order`; bucket k is
+    // order[bk[k] .. bk[k+1]).
+    void plan_buckets(const int* nsamp, int n, std::vector<int>& order,
+                      std::vector<size_t>& bk) const;
     int run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
                      float* d_out, long long& launches, std::string& err);
     int ensure_workspace(int B, int t_max, std::string& err);
@@ -166,11 +170,16 @@ private:
     int stage_slot_ = 0;
     bool stage_used_[2] = {false, false};
     cudaEvent_t stage_ev_[2] = {nullptr, nullptr};
-    // pinned staging for the host PCM path
-    float* h_pcm_ = nullptr;
-    size_t h_pcm_bytes_ = 0;
-    float* d_pcm_ = nullptr;
-    size_t d_pcm_bytes_ = 0;
+    // Host PCM path: a two-slot ring of pinned host + device PCM buffers, each
+    // holding one bucket. The host gathers bucket k+1 into its pinned slot while
+    // the GPU runs bucket k; the H2D copy runs on copy_stream_ and overlaps compute.
+    cudaStream_t copy_stream_ = nullptr;
+    float* h_ring_[2] = {nullptr, nullptr};
+    float* d_ring_[2] = {nullptr, nullptr};
+    size_t ring_bytes_ = 0;
+    bool ring_used_[2] = {false, false};
+    cudaEvent_t h2d_ev_[2] = {nullptr, nullptr};    // slot's H2D copy finished
+    cudaEvent_t comp_ev_[2] = {nullptr, nullptr};   // slot's bucket compute finished
     float* h_out_ = nullptr;
     float* d_out_ = nullptr;
     size_t out_bytes_ = 0;

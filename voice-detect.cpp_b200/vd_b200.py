@@ -207,8 +207,10 @@ class Model:
         import numpy as np
         arrs = [np.ascontiguousarray(c, dtype=np.float32) for c in clips]
         n = len(arrs)
-        ptrs = (C.POINTER(C.c_float) * n)(*[a.ctypes.data_as(C.POINTER(C.c_float)) for a in arrs])
-        ns = (C.c_int * n)(*[len(a) for a in arrs])
+        addr = np.fromiter((a.__array_interface__["data"][0] for a in arrs), np.uint64, n)
+        lens = np.fromiter((len(a) for a in arrs), np.int32, n)
+        ptrs = addr.ctypes.data_as(C.POINTER(C.POINTER(C.c_float)))
+        ns = lens.ctypes.data_as(C.POINTER(C.c_int))
         out = np.zeros((n, self.dim), np.float32)
         d = C.c_int(0)
         rc = self._L.voicedetect_capi_embed_pcm_batch(self.ctx, ptrs, ns, n, sample_rate,
