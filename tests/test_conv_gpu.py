@@ -53,8 +53,10 @@ def _h(t):
     return t.half().float()
 
 
-def valid_tilings(IC, OC, k, stride):
-    """Every explicit (tile_m, halo, ksplit) the kernel accepts for this layer."""
+def valid_tilings(IC, OC, k, stride, two_segments=False):
+    """Every explicit (tile_m, halo, ksplit) the kernel accepts for this layer
+    (tall HALO tiles may still be refused when two stages do not fit in shared
+    memory; the test skips those)."""
     bn = OC if OC <= 256 else OC // ((OC + 255) // 256)
     kb = 64 if IC % 64 == 0 else (32 if IC % 32 == 0 else 16)
     ks = kb // 16
@@ -69,6 +71,10 @@ def valid_tilings(IC, OC, k, stride):
                 out.append((tile_m, -1, J))
             if halo_ok:
                 out.append((tile_m, 1, J))
+    if halo_ok and not two_segments:
+        for tile_m in (384, 512, 1024):
+            if tile_m // 128 * bn <= 512:
+                out.append((tile_m, 1, 1))
     return out
 
 
@@ -85,6 +91,10 @@ CASES = [
     ("oc512_split", 1, 64, 512, 6, 9, 3, 1, False, False, None),
     ("s2_1x1", 2, 64, 128, 20, 31, 1, 2, False, False, [31, 12]),
     ("s2_1x1_down", 2, 32, 64, 20, 31, 1, 2, True, False, [31, 12]),
+    # large enough for the automatic choice of tall HALO tiles (8 and 3 row blocks)
+    ("tall_32_32", 16, 32, 32, 80, 300, 3, 1, False, True,
+     [300, 299, 251, 200, 150, 100, 64, 33, 300, 17, 9, 5, 3, 2, 1, 280]),
+    ("tall_64_64", 48, 64, 64, 40, 150, 3, 1, False, False, None),
 ]
 
 
@@ -128,12 +138,17 @@ def test_conv_vs_reference(cuda_lib, case):
                     relu=True, tvalid_out=tvalid_out, use_oracle=small)
     # every tiling the kernel offers: automatic, 128/256-row tiles, and the
     # shared-halo feed where the layer qualifies (stride 1, 3x3, resident weights)
-    configs = [(0, 0, 0)] + valid_tilings(IC, OC, k, stride)
+    configs = [(0, 0, 0)] + valid_tilings(IC, OC, k, stride, two_segments=fused_down)
     wp = vd.pack_conv_weight(w.to(dev))
     for tile_m, halo, ksplit in configs:
-        y = vd.conv(xin, wp, bias.float().to(dev), tv_dev, batch=B, t_out=To, f_out=Fo, oc=OC,
-                    k0=k, stride0=stride, ic0=IC, relu=True, err=err, tile_m=tile_m, halo=halo,
-                    ksplit=ksplit, **kw)
+        try:
+            y = vd.conv(xin, wp, bias.float().to(dev), tv_dev, batch=B, t_out=To, f_out=Fo,
+                        oc=OC, k0=k, stride0=stride, ic0=IC, relu=True, err=err, tile_m=tile_m,
+                        halo=halo, ksplit=ksplit, **kw)
+        except RuntimeError as e:
+            if tile_m > 256 and "does not fit" in str(e):
+                continue
+            raise
         torch.cuda.synchronize()
         assert int(err.item()) == 0, f"kernel error word {err.item():#x}"
         got = vd.from_grid(y, B, OC, Fo, To).cpu()

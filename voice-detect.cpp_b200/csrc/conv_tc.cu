@@ -93,6 +93,9 @@ struct ConvDev {
     __half* y2;              // optional PHASE-layout second output
     int y_phase;
     int Hp, Wp, T, F;  // output grid: Hp = T+2, Wp = F+2
+    // n / (Hp*Wp) and n / Wp as (umulhi(n, mul) + n) >> sh, exact for 0 <= n < 2^31
+    uint32_t img_mul, wp_mul;
+    int img_sh, wp_sh;
     int Hq, Wq;        // phase-split output: consumer grid
     long long plane_rows;
     const int* tvalid;
@@ -103,13 +106,21 @@ struct ConvDev {
     int* err;
 };
 
+// Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", 1994): with l = ceil(log2 d) and
+// mul = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, mul) + n) >> l for every
+// 0 <= n < 2^31 (the sum then stays below 2^32).
+__device__ __forceinline__ int fdiv(int n, uint32_t mul, int sh) {
+    return (int)((__umulhi((uint32_t)n, mul) + (uint32_t)n) >> sh);
+}
+
 // True when rows [m0, m0+BM) contain at least one pixel inside a clip's valid
 // time range (conservative: border columns of those rows count). Every role
 // evaluates it identically, so skipped tiles never touch the pipeline.
 __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m0) {
     const int img = p.Hp * p.Wp;
     const int mend = min(m0 + p.BM, p.M);
-    for (int b = m0 / img; b * img < mend; ++b) {
+    for (int b = fdiv(m0, p.img_mul, p.img_sh); b * img < mend; ++b) {
         const int r0 = max(m0 - b * img, 0);
         const int r1 = min(mend - b * img, img);
         const int t = tv[b];
@@ -136,15 +147,17 @@ __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int
     if (m >= p.M) return ri;
     ri.in_range = true;
     const int img = p.Hp * p.Wp;
-    const int b = m / img;
+    const int b = fdiv(m, p.img_mul, p.img_sh);
     const int r = m - b * img;
-    const int tp = r / p.Wp;
+    const int tp = fdiv(r, p.wp_mul, p.wp_sh);
     const int fp = r - tp * p.Wp;
     ri.valid = live && tp >= 1 && tp <= tv[b] && fp >= 1 && fp <= p.F;
-    const int q = ((tp & 1) << 1) | (fp & 1);
-    ri.dst2 = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
-              (fp >> 1) + 1;
-    if (p.y_phase) ri.dst = ri.dst2;
+    if (p.y2 || p.y_phase) {
+        const int q = ((tp & 1) << 1) | (fp & 1);
+        ri.dst2 = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
+                  (fp >> 1) + 1;
+        if (p.y_phase) ri.dst = ri.dst2;
+    }
     return ri;
 }
 
@@ -545,10 +558,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         // ---------------- epilogue ----------------
         const int ew = warp - kEpiWarp0;
         const int quad = warp & 3;        // TMEM lane quadrant this warp may access
-        const int half = ew >> 2;         // column half of the tile
-        const bool split = p.BN % 32 == 0;  // halves stay multiples of 16 columns
+        const int half = ew >> 2;
+        // Several 128-row blocks: warp half h drains blocks h, h+2, ... over all
+        // columns, so each row's index math is done once. One block: the halves
+        // split the columns (multiples of 16), or the first half takes them all.
+        const bool mb_split = NMB >= 2;
+        const bool split = !mb_split && p.BN % 32 == 0;
         const int c_lo = split ? half * (p.BN / 2) : 0;
-        const int c_hi = split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0);
+        const int c_hi = mb_split ? p.BN : (split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0));
         uint32_t acc = 0, acc_phase = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
@@ -561,6 +578,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 tc_fence_after();
             }
             for (int mb = 0; mb < NMB; ++mb) {
+                if (mb_split && (mb & 1) != half) continue;
                 const int m = m0 + mb * kMB + quad * 32 + lane;
                 const RowInfo ri = row_info(p, stv, m, live);
                 const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) +
@@ -590,6 +608,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         tc_fence_after();
         tmem_dealloc(tmem_base, p.tmem_cols);
     }
+}
+
+// Host side of fdiv: the multiplier and shift for divisor d (1 <= d < 2^31).
+void magic_div(uint32_t d, uint32_t& mul, int& sh) {
+    int l = 0;
+    while ((1ull << l) < d) ++l;
+    mul = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+    sh = l;
 }
 
 CUtensorMapSwizzle swizzle_for(int kb) {
@@ -706,14 +732,19 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: act must be 0, 1 or 2 (2 needs residual and residual2)");
         return 1;
     }
-    if (!(a->tile_m == 0 || a->tile_m == 128 || a->tile_m == 256)) {
-        set_error("vdb_conv: tile_m must be 0 (auto), 128 or 256");
-        return 1;
-    }
     const int n_nt = (a->oc + 255) / 256;
     const int BN = a->oc / n_nt;
     if (BN % 16 != 0 || BN * n_nt != a->oc) {
         set_error("vdb_conv: oc does not split into tcgen05 N tiles");
+        return 1;
+    }
+    // Row indices (and the fdiv fast division) are 32-bit: keep every tensor's row
+    // count, plus one tile of slack, below 2^31.
+    const long long kMaxRows = (1LL << 31) - 1024;
+    if (vdb_grid_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
+        vdb_phase_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
+        vdb_grid_rows(a->batch, 2 * a->t_out, 2 * a->f_out) > kMaxRows) {
+        set_error("vdb_conv: tensor too large (more than 2^31 rows); split the batch");
         return 1;
     }
     ConvDev p{};
@@ -739,8 +770,44 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     // n_mblk * J independent f32 accumulators (row blocks x K-split partials,
     // summed in the epilogue), double-buffered when TMEM's 512 columns allow.
     // tile_m = 256 also halves the weight traffic per output row.
+    // HALO tiles may be taller (tile_m up to 1024 = 8 row blocks): with small N the
+    // issuer needs more independent accumulators than two, and more row blocks
+    // give them without K partials. The automatic choice takes the most row blocks
+    // that keep the accumulators double-buffered, two pipeline stages in shared
+    // memory and at least two tiles per SM.
     int BM = a->tile_m;
-    if (BM == 0) BM = 256;
+    if (BM == 0) {
+        BM = 256;
+        if (halo && a->ksplit <= 1 && !a->x1) {
+            const int Hs = Wp + 1;
+            const int w_res = 9 * a->ic0 * BN * 2;
+            const long long rows = vdb_grid_rows(a->batch, a->t_out, a->f_out);
+            const int tail = round_up(a->oc * 4, 16) + round_up(a->batch * 4, 16) +
+                             8 * (2 * kMaxStages + 5) + 16;
+            for (int cand : {8, 4, 3}) {
+                const int H = cand * kMB + 2 * Hs;
+                const int nbox = (H + 255) / 256;
+                const int box = round_up((H + nbox - 1) / nbox, 8);
+                const int kb = a->ic0 % 64 == 0 ? 64 : (a->ic0 % 32 == 0 ? 32 : 16);
+                const long long stage = round_up(nbox * box * kb * 2, 1024);
+                const long long fit = (kSmemMax - 1024 - round_up(w_res, 1024) - tail) / stage;
+                if (2 * cand * BN <= 512 && fit >= 2 &&
+                    (rows + cand * kMB - 1) / (cand * kMB) >= 2LL * num_sms()) {
+                    BM = cand * kMB;
+                    break;
+                }
+            }
+        }
+    }
+    if (!(BM == 128 || BM == 256 || BM == 384 || BM == 512 || BM == 1024)) {
+        set_error("vdb_conv: tile_m must be 0 (auto), 128, 256, 384, 512 or 1024");
+        return 1;
+    }
+    if (BM > 256 && (!halo || a->x1)) {
+        set_error("vdb_conv: tile_m above 256 needs the HALO feed (stride-1 3x3, resident weights) "
+                  "and no second input segment");
+        return 1;
+    }
     if ((BM / kMB) * BN > 512) BM = kMB;
     const int nmb = BM / kMB;
     const int ks0 = p.seg[0].kb / 16;  // MMA K-steps per stage of segment 0
@@ -825,6 +892,8 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     p.y_phase = a->y_phase;
     p.Hp = Hp;
     p.Wp = Wp;
+    magic_div((uint32_t)Hp * (uint32_t)Wp, p.img_mul, p.img_sh);
+    magic_div((uint32_t)Wp, p.wp_mul, p.wp_sh);
     p.T = a->t_out;
     p.F = a->f_out;
     p.Hq = (a->t_out - 1) / 2 + 1 + 2;
@@ -881,8 +950,11 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         case 202: return launch(conv_tc_kernel<2, 2>);
         case 204: return launch(conv_tc_kernel<2, 4>);
         case 208: return launch(conv_tc_kernel<2, 8>);
+        case 301: return launch(conv_tc_kernel<3, 1>);
+        case 401: return launch(conv_tc_kernel<4, 1>);
+        case 801: return launch(conv_tc_kernel<8, 1>);
         default:
-            set_error("vdb_conv: ksplit must be 1, 2, 4 or 8");
+            set_error("vdb_conv: ksplit must be 1, 2, 4 or 8 (1 for tile_m above 256)");
             return 1;
     }
 }

@@ -1053,7 +1053,7 @@ int Engine::embed_device(const float* d_pcm, const long long* offsets, const int
         }
     std::vector<int> order;
     std::vector<size_t> bk;
-    plan_buckets(nsamp, n, order, bk);
+    plan_buckets(nsamp, n, max_frames, order, bk);
     last_launches = 0;
     std::vector<long long> bo;
     std::vector<int> bn;
@@ -1071,7 +1071,7 @@ int Engine::embed_device(const float* d_pcm, const long long* offsets, const int
     return 0;
 }
 
-void Engine::plan_buckets(const int* nsamp, int n, std::vector<int>& order,
+void Engine::plan_buckets(const int* nsamp, int n, long long frame_cap, std::vector<int>& order,
                           std::vector<size_t>& bk) const {
     // Longest first; consecutive clips of similar length share a bucket.
     order.resize((size_t)n);
@@ -1084,7 +1084,7 @@ void Engine::plan_buckets(const int* nsamp, int n, std::vector<int>& order,
         const int t0 = frames_of(nsamp[order[i]], cfg_.win, cfg_.hop);  // bucket's t_max
         size_t j = i;
         while (j < order.size() && (long long)(j - i) < max_clips &&
-               (long long)(j - i + 1) * t0 <= std::max<long long>(max_frames, t0))
+               (long long)(j - i + 1) * t0 <= std::max<long long>(frame_cap, t0))
             ++j;
         bk.push_back(j);
         i = j;
@@ -1141,9 +1141,14 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
             return 1;
         }
     }
+    // At least ~4 buckets when the call is large enough, so that the host gather and
+    // the H2D copy of one bucket hide behind the compute of the previous one.
+    long long frames_total = 0;
+    for (int i = 0; i < n; ++i) frames_total += frames_of(nsamp[i], cfg_.win, cfg_.hop);
+    const long long cap = std::min<long long>(max_frames, std::max<long long>(frames_total / 4, 16384));
     std::vector<int> order;
     std::vector<size_t> bk;
-    plan_buckets(nsamp, n, order, bk);
+    plan_buckets(nsamp, n, cap, order, bk);
     // ring slots hold the largest bucket the policy allows (and this call's largest)
     size_t need = ((size_t)max_frames * cfg_.hop + (size_t)max_clips * cfg_.win) * sizeof(float);
     for (size_t k = 0; k + 1 < bk.size(); ++k) {

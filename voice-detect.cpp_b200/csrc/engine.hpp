@@ -118,7 +118,7 @@ private:
                    const int* h_outrow, int B, cudaStream_t st, float* d_out, std::string& err);
     // Length-sorted buckets: clip indices longest first in `order`; bucket k is
     // order[bk[k] .. bk[k+1]).
-    void plan_buckets(const int* nsamp, int n, std::vector<int>& order,
+    void plan_buckets(const int* nsamp, int n, long long frame_cap, std::vector<int>& order,
                       std::vector<size_t>& bk) const;
     int run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
                      float* d_out, long long& launches, std::string& err);
