@@ -71,7 +71,7 @@ def valid_tilings(IC, OC, k, stride, two_segments=False):
                 out.append((tile_m, -1, J))
             if halo_ok:
                 out.append((tile_m, 1, J))
-    if halo_ok and not two_segments:
+    if halo_ok:
         for tile_m in (384, 512, 1024):
             if tile_m // 128 * bn <= 512:
                 out.append((tile_m, 1, 1))
@@ -95,6 +95,9 @@ CASES = [
     ("tall_32_32", 16, 32, 32, 80, 300, 3, 1, False, True,
      [300, 299, 251, 200, 150, 100, 64, 33, 300, 17, 9, 5, 3, 2, 1, 280]),
     ("tall_64_64", 48, 64, 64, 40, 150, 3, 1, False, False, None),
+    # tall HALO tiles followed by a 1x1 segment (the identity-shortcut form)
+    ("tall_32_seg1", 16, 32, 32, 80, 300, 3, 1, True, False,
+     [300, 299, 251, 200, 150, 100, 64, 33, 300, 17, 9, 5, 3, 2, 1, 280]),
 ]
 
 

@@ -72,7 +72,7 @@ struct SegDev {
     int plane[9];
     int off[9];      // TAP: global row offset per tap; HALO: row offset inside the halo
     int halo_back;   // HALO: rows before m0 covered by the halo
-    int n_box, box_rows;  // HALO: TMA boxes per stage and their height
+    int n_box, box_rows;  // TMA A boxes per stage and their height (TAP: BM split in <= 256)
     uint32_t bres;   // HALO: resident weights, byte offset from the smem base
 };
 
@@ -207,13 +207,13 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         }
     }
     if (!ri.in_range) return;
-    if (ri.valid) {
-        if (sbias) {
+    if (sbias) {
 #pragma unroll
-            for (int i = 0; i < NC; ++i) f[i] += sbias[i];
-        }
-        if (p.act == 2) {
-            // attentional fusion: (x + ds) + tanh(z) * (x - ds), x = residual, ds = residual2
+        for (int i = 0; i < NC; ++i) f[i] += sbias[i];
+    }
+    if (p.act == 2) {
+        // attentional fusion: (x + ds) + tanh(z) * (x - ds), x = residual, ds = residual2
+        if (ri.valid) {
 #pragma unroll
             for (int j = 0; j < NC / 8; ++j) {
                 const uint4 d4 = __ldg(reinterpret_cast<const uint4*>(r2ptr) + j);
@@ -227,46 +227,46 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
                     f[j * 8 + h] = (x + d) + att * (x - d);
                 }
             }
-        } else {
-            if (has_res) {
-#pragma unroll
-                for (int j = 0; j < NC / 8; ++j) {
-                    const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        f[j * 8 + 2 * h] += h2f(w[h] & 0xFFFFu);
-                        f[j * 8 + 2 * h + 1] += h2f(w[h] >> 16);
-                    }
-                }
-            }
-            if (p.act == 1) {
-#pragma unroll
-                for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
-            }
-            if (p.relu) {
-#pragma unroll
-                for (int i = 0; i < NC; ++i) f[i] = fmaxf(f[i], 0.0f);
-            }
-            if (p.clamp_hi > 0.0f) {
-#pragma unroll
-                for (int i = 0; i < NC; ++i) f[i] = fminf(f[i], p.clamp_hi);
-            }
         }
     } else {
+        if (has_res) {
 #pragma unroll
-        for (int i = 0; i < NC; ++i) f[i] = 0.0f;
+            for (int j = 0; j < NC / 8; ++j) {
+                const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    f[j * 8 + 2 * h] += h2f(w[h] & 0xFFFFu);
+                    f[j * 8 + 2 * h + 1] += h2f(w[h] >> 16);
+                }
+            }
+        }
+        if (p.act == 1) {
+#pragma unroll
+            for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
+        }
     }
+    // Pack to f16 pairs, then ReLU / Hardtanh on the pairs: rounding to f16 is
+    // monotone and 0 and clamp_hi are exact in f16, so max / min after rounding
+    // equal rounding after max / min. Invalid pixels are zeroed with a bit mask.
+    const uint32_t keep = ri.valid ? 0xFFFFFFFFu : 0u;
+    const bool relu = p.act == 0 && p.relu;
+    const bool clamp = p.act == 0 && p.clamp_hi > 0.0f;
+    const __half2 zero2 = __float2half2_rn(0.0f);
+    const __half2 hi2 = __float2half2_rn(p.clamp_hi);
     uint4 out[NC / 8];
 #pragma unroll
     for (int j = 0; j < NC / 8; ++j) {
-        __half2 h0 = __floats2half2_rn(f[j * 8 + 0], f[j * 8 + 1]);
-        __half2 h1 = __floats2half2_rn(f[j * 8 + 2], f[j * 8 + 3]);
-        __half2 h2 = __floats2half2_rn(f[j * 8 + 4], f[j * 8 + 5]);
-        __half2 h3 = __floats2half2_rn(f[j * 8 + 6], f[j * 8 + 7]);
-        out[j].x = *reinterpret_cast<uint32_t*>(&h0);
-        out[j].y = *reinterpret_cast<uint32_t*>(&h1);
-        out[j].z = *reinterpret_cast<uint32_t*>(&h2);
-        out[j].w = *reinterpret_cast<uint32_t*>(&h3);
+        __half2 h[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            h[q] = __floats2half2_rn(f[j * 8 + 2 * q], f[j * 8 + 2 * q + 1]);
+            if (relu) h[q] = __hmax2(h[q], zero2);
+            if (clamp) h[q] = __hmin2(h[q], hi2);
+        }
+        out[j].x = *reinterpret_cast<uint32_t*>(&h[0]) & keep;
+        out[j].y = *reinterpret_cast<uint32_t*>(&h[1]) & keep;
+        out[j].z = *reinterpret_cast<uint32_t*>(&h[2]) & keep;
+        out[j].w = *reinterpret_cast<uint32_t*>(&h[3]) & keep;
     }
     uint4* yp = reinterpret_cast<uint4*>(yrow);
 #pragma unroll
@@ -471,7 +471,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                             m0 - s.halo_back + bx * s.box_rows, 0);
                         } else {
                             const int tap = it / s.n_kb, kbi = it - tap * s.n_kb;
-                            tma_load_3d(sa, ta, fb, kbi * s.kb, m0 + s.off[tap], s.plane[tap]);
+                            const uint32_t box_bytes = (uint32_t)s.box_rows * s.kb * 2;
+                            for (int bx = 0; bx < s.n_box; ++bx)
+                                tma_load_3d(sa + bx * box_bytes, ta, fb, kbi * s.kb,
+                                            m0 + s.off[tap] + bx * s.box_rows, s.plane[tap]);
                             tma_load_2d(sa + p.a_region, tb, fb, tap * s.ic + kbi * s.kb, n0);
                         }
                         if (++stage == S) {
@@ -778,7 +781,7 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     int BM = a->tile_m;
     if (BM == 0) {
         BM = 256;
-        if (halo && a->ksplit <= 1 && !a->x1) {
+        if (halo && a->ksplit <= 1) {
             const int Hs = Wp + 1;
             const int w_res = 9 * a->ic0 * BN * 2;
             const long long rows = vdb_grid_rows(a->batch, a->t_out, a->f_out);
@@ -789,9 +792,17 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
                 const int nbox = (H + 255) / 256;
                 const int box = round_up((H + nbox - 1) / nbox, 8);
                 const int kb = a->ic0 % 64 == 0 ? 64 : (a->ic0 % 32 == 0 ? 32 : 16);
-                const long long stage = round_up(nbox * box * kb * 2, 1024);
+                long long a_b = (long long)nbox * box * kb * 2, b_b = 0;
+                if (a->x1) {  // segment 1 stages hold its A rows and a weight tile
+                    const int kb1 = a->ic1 % 64 == 0 ? 64 : (a->ic1 % 32 == 0 ? 32 : 16);
+                    a_b = std::max<long long>(a_b, (long long)cand * kMB * kb1 * 2);
+                    b_b = (long long)BN * kb1 * 2;
+                }
+                const long long stage = round_up((int)a_b, 1024) + round_up((int)b_b, 1024);
                 const long long fit = (kSmemMax - 1024 - round_up(w_res, 1024) - tail) / stage;
-                if (2 * cand * BN <= 512 && fit >= 2 &&
+                // two tiles in flight: a tile takes 1 stage per channel block of each segment
+                const int per_tile = (a->ic0 / kb) + (a->x1 ? a->ic1 / (a->ic1 % 64 == 0 ? 64 : (a->ic1 % 32 == 0 ? 32 : 16)) : 0);
+                if (2 * cand * BN <= 512 && fit >= 2 * per_tile &&
                     (rows + cand * kMB - 1) / (cand * kMB) >= 2LL * num_sms()) {
                     BM = cand * kMB;
                     break;
@@ -803,9 +814,8 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: tile_m must be 0 (auto), 128, 256, 384, 512 or 1024");
         return 1;
     }
-    if (BM > 256 && (!halo || a->x1)) {
-        set_error("vdb_conv: tile_m above 256 needs the HALO feed (stride-1 3x3, resident weights) "
-                  "and no second input segment");
+    if (BM > 256 && !halo) {
+        set_error("vdb_conv: tile_m above 256 needs the HALO feed (stride-1 3x3, resident weights)");
         return 1;
     }
     if ((BM / kMB) * BN > 512) BM = kMB;
@@ -851,6 +861,8 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
             a_bytes = std::max(a_bytes, s.bytes);
         } else {
             s.mode = SEG_TAP;
+            s.n_box = (BM + 255) / 256;
+            s.box_rows = BM / s.n_box;
             s.bytes = (uint32_t)(BM + BN) * row_bytes;
             a_bytes = std::max(a_bytes, (uint32_t)BM * row_bytes);
             b_bytes = std::max(b_bytes, (uint32_t)BN * row_bytes);
@@ -915,7 +927,7 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         const void* x = sg ? a->x1 : a->x0;
         const void* w = sg ? a->w1 : a->w0;
         const int stride = sg ? a->stride1 : a->stride0;
-        const int box_rows = s.mode == SEG_HALO ? s.box_rows : BM;
+        const int box_rows = s.box_rows;
         const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
         if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, stride == 2 ? 4 : 1, s.kb,
                         box_rows) ||

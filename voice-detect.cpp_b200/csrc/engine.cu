@@ -287,6 +287,11 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         } else if (ic != oc || blk.stride != 1) {
             err = "block " + std::to_string(i) + ": identity shortcut needs equal shapes";
             return nullptr;
+        } else {
+            const __half* eye = e->identity(oc, err);
+            if (!eye) return nullptr;
+            blk.wd = const_cast<__half*>(eye);
+            blk.identity = true;
         }
         if (ic % 16 != 0 || oc % 16 != 0) {
             err = "block channels must be multiples of 16";
@@ -337,6 +342,17 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         e->levels_.back().c = std::max(e->levels_.back().c, b.oc);
     }
     return e;
+}
+
+const __half* Engine::identity(int c, std::string& err) {
+    for (const auto& id : identities_)
+        if (id.first == c) return id.second;
+    std::vector<float> eye((size_t)c * c, 0.0f);
+    for (int i = 0; i < c; ++i) eye[(size_t)i * c + i] = 1.0f;
+    __half* p = nullptr;
+    if (!upload_f16(eye, &p, err)) return nullptr;
+    identities_.emplace_back(c, p);
+    return p;
 }
 
 bool Engine::upload_f32(const std::vector<float>& v, float** dst, std::string& err) {
@@ -629,8 +645,13 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
             s3.w1 = p1;
             s3.flops_px += 2.0 * c3.oc * in_planes;
             sb = sh.b;
-        } else {
-            s3.res = x;
+        } else {  // identity shortcut on the tensor cores (exact; see identity())
+            const __half* eye = identity(in_planes, err);
+            if (!eye) return false;
+            s3.x1 = x;
+            s3.ic1 = in_planes;
+            s3.stride1 = 1;
+            s3.w1 = eye;
         }
         if (!dev_b(c3.b, sb, c3.oc, &s3.bias)) return false;
         s3.relu = 1;
@@ -918,14 +939,11 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
         c2.relu = 1;
         c2.tvalid = tv_out;
         c2.err = errword_;
-        if (blk.wd) {
-            c2.x1 = x;
-            c2.w1 = blk.wd;
-            c2.ic1 = blk.ic;
-            c2.stride1 = blk.stride;
-        } else {
-            c2.residual = x;
-        }
+        // 1x1 downsample, or the identity shortcut, as input segment 1
+        c2.x1 = x;
+        c2.w1 = blk.wd;
+        c2.ic1 = blk.ic;
+        c2.stride1 = blk.stride;
         c2.y_phase = next_s2 ? 1 : 0;
         c2.y = next_s2 ? Lo.p : Lo.g[o_slot];
         pe = prof_begin(st);
@@ -934,7 +952,8 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
             return 1;
         }
         prof_end(pe, st,
-                 2.0 * blk.oc * blk.oc * 9 * valid_px + (blk.wd ? 2.0 * blk.oc * blk.ic * valid_px : 0));
+                 2.0 * blk.oc * blk.oc * 9 * valid_px +
+                     (blk.identity ? 0.0 : 2.0 * blk.oc * blk.ic * valid_px));
         launches += 2;
         lev = lev_out;
         T = To;

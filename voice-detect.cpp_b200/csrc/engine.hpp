@@ -38,7 +38,8 @@ struct ResBlockDev {
     float* b1 = nullptr;
     __half* w2 = nullptr;   // [oc][9][oc]
     float* b2 = nullptr;    // conv2 bias (+ downsample bias when fused)
-    __half* wd = nullptr;   // [oc][ic] or nullptr (identity shortcut)
+    __half* wd = nullptr;   // [oc][ic], or the [oc][oc] identity for an identity shortcut
+    bool identity = false;
 };
 
 // ERes2Net runs from a plan compiled once at load from the conv manifest
@@ -127,6 +128,11 @@ private:
     bool load_eres2net(const Gguf& g, std::string& err);
     bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
     bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
+    // f16 identity [c][c]: an identity shortcut added on the tensor cores as a 1x1
+    // input segment of the conv that ends the block (x * 1.0 is exact, and the sum
+    // is accumulated in f32 like the epilogue add it replaces). One per width.
+    const __half* identity(int c, std::string& err);
+    std::vector<std::pair<int, __half*>> identities_;
 
     EngineConfig cfg_;
     int device_ = 0;
