@@ -294,6 +294,7 @@ def run_b200(args) -> int:
     torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(end)
     conv_ms, conv_flops, conv_n = model.profile_read()
+    stages = model.profile_stages()
     model.profile(False)
     clk = clocks.stop()
     model.sync()
@@ -351,6 +352,7 @@ def run_b200(args) -> int:
                      "conv_launches": conv_n,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
+        "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -479,6 +481,7 @@ def run_eres2net(args) -> int:
     torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(end)
     conv_ms, conv_flops, conv_n = model.profile_read()
+    stages = model.profile_stages()
     model.profile(False)
     clk = clocks.stop()
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
@@ -520,6 +523,7 @@ def run_eres2net(args) -> int:
                      "traffic": None, "conv_launches": conv_n,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
+        "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -152,7 +152,7 @@ def test_device_path_matches_host_path(resnet):
     torch.cuda.synchronize()
     dev = out.cpu().numpy()
     assert np.allclose(dev, host, atol=1e-6)
-    assert model.last_launches() == 36  # fbank + cmn + stem + 32 convs + pool
+    assert model.last_launches() == 38  # fbank + cmn + stem + 32 convs + TSTP, FC, finish
 
 
 def test_identify_matches_oracle(resnet):

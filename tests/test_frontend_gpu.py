@@ -84,12 +84,15 @@ def test_cmn_stem_matches_oracle(cuda_lib):
         assert np.all(got[i, :, :, T:] == 0)
 
 
-def test_pool_embed_matches_oracle(cuda_lib):
+@pytest.mark.parametrize("B,T,F,Cc,D", [(4, 38, 10, 256, 256), (70, 13, 10, 512, 512),
+                                         (37, 9, 5, 32, 192)])
+def test_pool_embed_matches_oracle(cuda_lib, B, T, F, Cc, D):
+    """TSTP + split-K FC + finish/L2 vs f64 numpy; the larger cases span several
+    32-clip FC tiles, several K splits and output widths that are not multiples of 64."""
     import torch
     L = cuda_lib.lib()
-    rng = np.random.default_rng(8)
-    B, T, F, Cc, D = 4, 38, 10, 256, 256
-    tv = [38, 20, 2, 1]
+    rng = np.random.default_rng(8 + B)
+    tv = [T, T // 2 + 1, 2, 1] + [int(v) for v in rng.integers(1, T + 1, B - 4)]
     # values exactly representable in f16, so the kernel and the f64 check see the same input
     x = (np.abs(rng.standard_normal((B, Cc, F, T))) * 5).astype(np.float16).astype(np.float32)
     for i, t in enumerate(tv):

@@ -362,6 +362,19 @@ extern "C" int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_
     return 0;
 }
 
+extern "C" int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* front_ms,
+                                               double* conv_ms, double* pool_ms,
+                                               double* other_ms) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    const double* v = ctx->engine->stage_ms;
+    if (front_ms) *front_ms = v[1];
+    if (conv_ms) *conv_ms = v[0];
+    if (pool_ms) *pool_ms = v[2];
+    if (other_ms) *other_ms = v[3];
+    return 0;
+}
+
 extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
     if (!ctx || !ctx->engine) return 1;
     std::lock_guard<std::mutex> lk(ctx->mu);

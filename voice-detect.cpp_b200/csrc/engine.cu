@@ -141,6 +141,9 @@ void Engine::free_workspace() {
     cudaFree(mean_);
     mean_ = nullptr;
     mean_bytes_ = 0;
+    cudaFree(pool_scratch_);
+    pool_scratch_ = nullptr;
+    pool_scratch_bytes_ = 0;
     cudaFree(meta_);
     meta_ = nullptr;
     cudaFree(offs_);
@@ -803,6 +806,13 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     if (!grow((void**)&feats_, feats_bytes_, (size_t)B * t_max * cfg_.n_mels * sizeof(float)))
         return 1;
     if (!grow((void**)&mean_, mean_bytes_, (size_t)B * cfg_.n_mels * sizeof(float))) return 1;
+    {
+        // pooling input: the last level's frequency extent and channels
+        const int lev = cfg_.arch == "eres2net" ? e_out_level_ : (int)levels_.size() - 1;
+        const int pc = cfg_.arch == "eres2net" ? ebufs_[e_out_buf_].c : levels_.back().c;
+        const size_t n = pool_embed_scratch_floats(B, lf[lev], pc, cfg_.emb_dim);
+        if (!grow((void**)&pool_scratch_, pool_scratch_bytes_, n * sizeof(float))) return 1;
+    }
     if (B > meta_cap_) {
         cudaDeviceSynchronize();
         stage_used_[0] = stage_used_[1] = false;
@@ -867,6 +877,7 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     stage_used_[slot] = true;
     long long launches = 0;
     // FBank -> CMN + stem
+    const int pf = prof_begin(st, 1);
     if (vdb_fbank(plan_, d_pcm, offs_, nsamp_, B, t_max, feats_, st)) {
         err = vdb_last_error();
         return 1;
@@ -877,6 +888,7 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
         err = vdb_last_error();
         return 1;
     }
+    prof_end(pf, st, 0.0);
     launches += cfg_.cmn ? 3 : 2;
     if (eres) {
         if (run_eres2net(B, t_max, tv_sum, st, d_out, launches, err)) return 1;
@@ -962,13 +974,15 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
         cur_phase = next_s2;
     }
     const Level& Lf = levels_[lev];
+    const int pp = prof_begin(st, 2);
     if (pool_embed_launch(Lf.g[cur], meta_ + (size_t)lev * B, B, T, F, Lf.c, seg_w_, seg_b_,
                           mean_vec_, cfg_.emb_dim, var_eps_, cfg_.l2 ? 1 : 0,
-                          meta_ + nlev * B, d_out, nullptr, st)) {
+                          meta_ + nlev * B, d_out, nullptr, pool_scratch_, st)) {
         err = vdb_last_error();
         return 1;
     }
-    launches += 1;
+    prof_end(pp, st, 0.0);
+    launches += 3;
     last_launches += launches;
     return 0;
 }
@@ -989,11 +1003,13 @@ int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum,
     for (const EStep& s : esteps_) {
         const int To = lt[s.level], Fo = lf[s.level];
         if (s.kind == 1) {
+            const int pa = prof_begin(st, 3);
             if (vdb_add(ptr(s.x0), ld(s.x0), ptr(s.x1), ld(s.x1), ptr(s.y), ld(s.y),
                         vdb_grid_rows(B, To, Fo), s.oc, st)) {
                 err = vdb_last_error();
                 return 1;
             }
+            prof_end(pa, st, 0.0);
             ++launches;
             continue;
         }
@@ -1042,13 +1058,15 @@ int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum,
         ++launches;
     }
     const int lev = e_out_level_;
+    const int pp = prof_begin(st, 2);
     if (pool_embed_launch(ebufs_[e_out_buf_].p, meta_ + (size_t)lev * B, B, lt[lev], lf[lev],
                           ebufs_[e_out_buf_].c, seg_w_, seg_b_, nullptr, cfg_.emb_dim, var_eps_,
-                          cfg_.l2 ? 1 : 0, meta_ + nlev * B, d_out, nullptr, st)) {
+                          cfg_.l2 ? 1 : 0, meta_ + nlev * B, d_out, nullptr, pool_scratch_, st)) {
         err = vdb_last_error();
         return 1;
     }
-    ++launches;
+    prof_end(pp, st, 0.0);
+    launches += 3;
     return 0;
 }
 
@@ -1263,7 +1281,7 @@ int Engine::check_device_error(std::string& err) {
 
 void Engine::set_profiling(bool on) { profiling_ = on; }
 
-int Engine::prof_begin(cudaStream_t st) {
+int Engine::prof_begin(cudaStream_t st, int stage) {
     if (!profiling_) return -1;
     if (prof_used_ + 2 > prof_ev_.size()) {
         for (int i = 0; i < 64; ++i) {
@@ -1274,6 +1292,8 @@ int Engine::prof_begin(cudaStream_t st) {
     }
     const int idx = (int)prof_used_;
     prof_used_ += 2;
+    prof_stage_.resize(prof_used_ / 2);
+    prof_stage_[idx / 2] = stage;
     cudaEventRecord(prof_ev_[idx], st);
     return idx;
 }
@@ -1281,14 +1301,15 @@ int Engine::prof_begin(cudaStream_t st) {
 void Engine::prof_end(int idx, cudaStream_t st, double flops) {
     if (idx < 0) return;
     cudaEventRecord(prof_ev_[idx + 1], st);
-    prof_flops_ += flops;
+    if (prof_stage_[idx / 2] == 0) prof_flops_ += flops;
 }
 
 int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_launches,
                          std::string& err) {
     conv_ms = 0.0;
     conv_flops = prof_flops_;
-    conv_launches = (long long)(prof_used_ / 2);
+    conv_launches = 0;
+    for (double& v : stage_ms) v = 0.0;
     for (size_t i = 0; i + 1 < prof_used_; i += 2) {
         if (cudaEventSynchronize(prof_ev_[i + 1]) != cudaSuccess) {
             err = "profile event failed";
@@ -1296,7 +1317,12 @@ int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_la
         }
         float ms = 0.0f;
         cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]);
-        conv_ms += ms;
+        const int stg = prof_stage_[i / 2];
+        stage_ms[stg] += ms;
+        if (stg == 0) {
+            conv_ms += ms;
+            ++conv_launches;
+        }
     }
     prof_used_ = 0;
     prof_flops_ = 0.0;

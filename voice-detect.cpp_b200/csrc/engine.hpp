@@ -165,6 +165,8 @@ private:
     size_t feats_bytes_ = 0;
     float* mean_ = nullptr;
     size_t mean_bytes_ = 0;
+    float* pool_scratch_ = nullptr;   // pooled vectors + FC partials of one bucket
+    size_t pool_scratch_bytes_ = 0;
     int* meta_ = nullptr;         // device int32: frames, tvalid per level, out rows
     long long* offs_ = nullptr;   // device int64 offsets
     int* nsamp_ = nullptr;
@@ -194,8 +196,15 @@ private:
     std::vector<cudaEvent_t> prof_ev_;  // pairs (start, stop)
     size_t prof_used_ = 0;              // events in use
     double prof_flops_ = 0.0;
-    int prof_begin(cudaStream_t st);    // returns event-pair index or -1
+    // Event pairs are tagged with a stage: 0 conv, 1 front (FBank + CMN + stem),
+    // 2 pooling (TSTP + FC + L2), 3 other (element-wise adds).
+    int prof_begin(cudaStream_t st, int stage = 0);  // returns event-pair index or -1
     void prof_end(int idx, cudaStream_t st, double flops);
+    std::vector<int> prof_stage_;
+public:
+    // Per-stage summed launch durations (ms) of the last read_profile call.
+    double stage_ms[4] = {0, 0, 0, 0};
+private:
 };
 
 // Linear resampling, src/audio_io.cpp:9-23.

@@ -20,6 +20,7 @@
 // sums run in f32 with twiddles and filter weights computed on the host in f64.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <string>
@@ -29,7 +30,7 @@
 #include "vdb_ops.h"
 
 struct vdb_fbank_plan {
-    int sample_rate, n_mels, n_fft, win, hop;
+    int sample_rate, n_mels, n_fft, win, hop, n_weights;
     float preemph;
     double* d_window;    // [win] Povey window (f64)
     float2* d_twiddle;   // [512] W512^m = (cos, -sin)(2*pi*m/512)
@@ -45,6 +46,7 @@ namespace {
 constexpr int kFFT = 512;
 constexpr int kFramesPerBlock = 8;
 constexpr int kMaxMels = 128;
+constexpr int kMaxWeights = 4096;  // filter weights kept in shared memory
 
 __device__ __forceinline__ void cmul(float& re, float& im, float2 w) {
     const float r = re * w.x - im * w.y;
@@ -57,26 +59,39 @@ __device__ __forceinline__ int bitrev5(int x) { return __brev(x) >> 27; }
 
 __global__ void __launch_bounds__(32 * kFramesPerBlock)
 fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offsets,
-             const int* __restrict__ nsamp, int t_max, int win, int hop, float preemph,
-             int n_mels, const double* __restrict__ window, const float2* __restrict__ twiddle,
-             const int* __restrict__ kstart, const int* __restrict__ klen,
-             const int* __restrict__ woff, const float* __restrict__ weights,
-             float* __restrict__ feats) {
+             const int* __restrict__ nsamp, int batch, int t_max, int win, int hop,
+             float preemph, int n_mels, const double* __restrict__ window,
+             const float2* __restrict__ twiddle, const int* __restrict__ kstart,
+             const int* __restrict__ klen, const int* __restrict__ woff,
+             const float* __restrict__ weights, int n_weights, float* __restrict__ feats) {
+    // Persistent blocks: the tables are staged in shared memory once per block,
+    // then each warp walks frames (b, t) of the flattened batch x t_max range.
     __shared__ float2 s_tw[kFFT];
     __shared__ double s_win[kFFT];
     __shared__ float s_ps[kFramesPerBlock][kFFT / 2 + 1];
+    __shared__ float s_w[kMaxWeights];
+    __shared__ int s_ks[kMaxMels], s_kl[kMaxMels], s_wo[kMaxMels];
     for (int i = threadIdx.x; i < kFFT; i += blockDim.x) {
         s_tw[i] = twiddle[i];
         s_win[i] = i < win ? window[i] : 0.0;
     }
+    for (int i = threadIdx.x; i < n_weights; i += blockDim.x) s_w[i] = weights[i];
+    for (int i = threadIdx.x; i < n_mels; i += blockDim.x) {
+        s_ks[i] = kstart[i];
+        s_kl[i] = klen[i];
+        s_wo[i] = woff[i];
+    }
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = blockIdx.y;
-    const int t = blockIdx.x * kFramesPerBlock + warp;
+    const long long n_frames = (long long)batch * t_max;
+    for (long long id = (long long)blockIdx.x * kFramesPerBlock + warp; id < n_frames;
+         id += (long long)gridDim.x * kFramesPerBlock) {
+    const int b = (int)(id / t_max);
+    const int t = (int)(id - (long long)b * t_max);
     const int n = nsamp[b];
     const int T = n >= win ? 1 + (n - win) / hop : 0;
-    if (t >= T || t >= t_max) return;
+    if (t >= T) continue;
     const float* x = pcm + offsets[b] + (long long)t * hop;
 
     float re[16], im[16];
@@ -172,10 +187,12 @@ fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offset
     __syncwarp();
     float* out = feats + ((long long)b * t_max + t) * n_mels;
     for (int m = lane; m < n_mels; m += 32) {
-        const int k0 = kstart[m], kl = klen[m], wo = woff[m];
+        const int k0 = s_ks[m], kl = s_kl[m], wo = s_wo[m];
         float e = 0.0f;
-        for (int i = 0; i < kl; ++i) e = fmaf(__ldg(weights + wo + i), ps[k0 + i], e);
+        for (int i = 0; i < kl; ++i) e = fmaf(s_w[wo + i], ps[k0 + i], e);
         out[m] = logf(fmaxf(e, FLT_EPSILON));
+    }
+    __syncwarp();  // ps is rewritten by this warp's next frame
     }
 }
 
@@ -243,6 +260,12 @@ extern "C" vdb_fbank_plan* vdb_fbank_plan_create(int sample_rate, int n_mels, in
     p->win = win;
     p->hop = hop;
     p->preemph = preemph;
+    p->n_weights = (int)wts.size();
+    if (p->n_weights > kMaxWeights) {
+        set_error("vdb_fbank_plan_create: mel filter bank too large");
+        delete p;
+        return nullptr;
+    }
     bool ok = cudaMalloc(&p->d_window, sizeof(double) * win) == cudaSuccess &&
               cudaMalloc(&p->d_twiddle, sizeof(float2) * kFFT) == cudaSuccess &&
               cudaMalloc(&p->d_kstart, sizeof(int) * n_mels) == cudaSuccess &&
@@ -294,10 +317,13 @@ extern "C" int vdb_fbank(const vdb_fbank_plan* p, const float* pcm, const long l
         set_error("vdb_fbank: empty batch");
         return 1;
     }
-    dim3 grid((t_max + kFramesPerBlock - 1) / kFramesPerBlock, batch);
+    const long long frames = (long long)batch * t_max;
+    const int grid = (int)std::min<long long>((frames + kFramesPerBlock - 1) / kFramesPerBlock,
+                                              (long long)num_sms() * 6);
     fbank_kernel<<<grid, 32 * kFramesPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
-        pcm, offsets, n_samples, t_max, p->win, p->hop, p->preemph, p->n_mels, p->d_window,
-        p->d_twiddle, p->d_kstart, p->d_klen, p->d_woff, p->d_weights, feats);
+        pcm, offsets, n_samples, batch, t_max, p->win, p->hop, p->preemph, p->n_mels,
+        p->d_window, p->d_twiddle, p->d_kstart, p->d_klen, p->d_woff, p->d_weights,
+        p->n_weights, feats);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }

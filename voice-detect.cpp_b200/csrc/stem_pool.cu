@@ -41,64 +41,82 @@ __global__ void cmn_mean_kernel(const float* __restrict__ feats, const int* __re
     }
 }
 
+// The stem, one block per (image, run of kStemRows padded time rows). The block
+// first stages the CMN'd features its rows read — kStemRows + 2 feature rows,
+// zero outside the clip and at the frequency borders — in shared memory, so the
+// nine taps need no bounds checks and CMN is applied once per input. Then each
+// thread computes 8 channels of one padded pixel per step (weights in registers)
+// and a warp stores 512 contiguous bytes; the block's output rows are contiguous.
+constexpr int kStemRows = 16;
+
 template <int OC>
 __global__ void __launch_bounds__(256)
 stem_kernel(const float* __restrict__ feats, const int* __restrict__ frames,
             const float* __restrict__ mean, int batch, int t_max, int n_mels, int cmn,
             const float* __restrict__ w, const float* __restrict__ bias, __half* __restrict__ y) {
-    __shared__ float sw[OC * 9];
-    __shared__ float sb[OC];
-    for (int i = threadIdx.x; i < OC * 9; i += blockDim.x) sw[i] = w[i];
-    for (int i = threadIdx.x; i < OC; i += blockDim.x) sb[i] = bias[i];
-    __syncthreads();
+    constexpr int G = OC / 8;
+    constexpr int PPB = 256 / G;  // pixels per block step
+    __shared__ float sx[(kStemRows + 2) * 130];
+    const int g = (int)threadIdx.x % G;
+    const int pl = (int)threadIdx.x / G;
     const int Wp = n_mels + 2, Hp = t_max + 2;
-    const long long rows = (long long)batch * Hp * Wp;
-    const long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= rows) return;
-    const int b = (int)(r / ((long long)Hp * Wp));
-    const int rr = (int)(r - (long long)b * Hp * Wp);
-    const int tp = rr / Wp, fp = rr - tp * Wp;
+    const int b = blockIdx.y;
+    const int tp0 = blockIdx.x * kStemRows;
     const int T = min(frames[b], t_max);
-    float acc[OC];
-#pragma unroll
-    for (int o = 0; o < OC; ++o) acc[o] = 0.0f;
-    const bool valid = tp >= 1 && tp <= T && fp >= 1 && fp <= n_mels;
-    if (valid) {
-        const int t = tp - 1, f = fp - 1;
-        const float* fb = feats + (long long)b * t_max * n_mels;
-        const float* mb = mean + (long long)b * n_mels;
-        // accumulate in the reference's kh (freq) -> kw (time) order
-#pragma unroll
-        for (int kf = 0; kf < 3; ++kf) {
-            const int ff = f + kf - 1;
-#pragma unroll
-            for (int kt = 0; kt < 3; ++kt) {
-                const int tt = t + kt - 1;
-                float xin = 0.0f;
-                if (ff >= 0 && ff < n_mels && tt >= 0 && tt < T) {
-                    xin = __ldg(fb + (long long)tt * n_mels + ff);
-                    if (cmn) xin = __fsub_rn(xin, __ldg(mb + ff));
-                }
-#pragma unroll
-                for (int o = 0; o < OC; ++o) acc[o] = fmaf(sw[o * 9 + kt * 3 + kf], xin, acc[o]);
-            }
+    const float* fb = feats + (long long)b * t_max * n_mels;
+    const float* mb = mean + (long long)b * n_mels;
+    // sx[i][j] = feature(row tp0 - 2 + i, mel j - 1) - mean, 0 outside the clip
+    for (int e = threadIdx.x; e < (kStemRows + 2) * Wp; e += blockDim.x) {
+        const int i = e / Wp, j = e - i * Wp;
+        const int tt = tp0 - 2 + i, ff = j - 1;
+        float v = 0.0f;
+        if (tt >= 0 && tt < T && ff >= 0 && ff < n_mels) {
+            v = __ldg(fb + (long long)tt * n_mels + ff);
+            if (cmn) v = __fsub_rn(v, __ldg(mb + ff));
         }
-#pragma unroll
-        for (int o = 0; o < OC; ++o) acc[o] = fmaxf(acc[o] + sb[o], 0.0f);
+        sx[e] = v;
     }
-    uint4* yp = reinterpret_cast<uint4*>(y + r * OC);
+    float wr[8][9], br[8];
 #pragma unroll
-    for (int j = 0; j < OC / 8; ++j) {
-        uint4 q;
-        __half2 h0 = __floats2half2_rn(acc[j * 8 + 0], acc[j * 8 + 1]);
-        __half2 h1 = __floats2half2_rn(acc[j * 8 + 2], acc[j * 8 + 3]);
-        __half2 h2 = __floats2half2_rn(acc[j * 8 + 4], acc[j * 8 + 5]);
-        __half2 h3 = __floats2half2_rn(acc[j * 8 + 6], acc[j * 8 + 7]);
-        q.x = *reinterpret_cast<uint32_t*>(&h0);
-        q.y = *reinterpret_cast<uint32_t*>(&h1);
-        q.z = *reinterpret_cast<uint32_t*>(&h2);
-        q.w = *reinterpret_cast<uint32_t*>(&h3);
-        yp[j] = q;
+    for (int o = 0; o < 8; ++o) {
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wr[o][k] = __ldg(w + (g * 8 + o) * 9 + k);
+        br[o] = __ldg(bias + g * 8 + o);
+    }
+    __syncthreads();
+    const int rows = min(kStemRows, Hp - tp0) * Wp;
+    uint4* yb = reinterpret_cast<uint4*>(y) + ((long long)b * Hp + tp0) * Wp * G;
+    for (int q = pl; q < rows; q += PPB) {
+        const int r = q / Wp, fp = q - r * Wp;
+        const int tp = tp0 + r;
+        float acc[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) acc[o] = 0.0f;
+        if (tp >= 1 && tp <= T && fp >= 1 && fp <= n_mels) {
+            const float* x0 = sx + r * Wp + fp - 1;  // tap (kt, kf) at x0[kt*Wp + kf]
+            // accumulate in the reference's kh (freq) -> kw (time) order
+#pragma unroll
+            for (int kf = 0; kf < 3; ++kf) {
+#pragma unroll
+                for (int kt = 0; kt < 3; ++kt) {
+                    const float xin = x0[kt * Wp + kf];
+#pragma unroll
+                    for (int o = 0; o < 8; ++o) acc[o] = fmaf(wr[o][kt * 3 + kf], xin, acc[o]);
+                }
+            }
+#pragma unroll
+            for (int o = 0; o < 8; ++o) acc[o] = fmaxf(acc[o] + br[o], 0.0f);
+        }
+        uint4 v;
+        __half2 h0 = __floats2half2_rn(acc[0], acc[1]);
+        __half2 h1 = __floats2half2_rn(acc[2], acc[3]);
+        __half2 h2 = __floats2half2_rn(acc[4], acc[5]);
+        __half2 h3 = __floats2half2_rn(acc[6], acc[7]);
+        v.x = *reinterpret_cast<uint32_t*>(&h0);
+        v.y = *reinterpret_cast<uint32_t*>(&h1);
+        v.z = *reinterpret_cast<uint32_t*>(&h2);
+        v.w = *reinterpret_cast<uint32_t*>(&h3);
+        yb[(long long)q * G + g] = v;
     }
 }
 
@@ -114,21 +132,17 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
     return t;
 }
 
-// One CTA per clip. Dynamic smem: pooled [2*c*f] + emb [emb_dim] floats.
+// TSTP, one CTA per clip: pooled[b][c*F + f] = mean, pooled[b][C*F + c*F + f] = std
+// over the clip's valid frames (two passes in f64, unbiased variance, eps inside
+// the sqrt), in the reference's C-outer / F-inner flattening.
 __global__ void __launch_bounds__(256)
-pool_embed_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, int T, int F,
-                  int C, const float* __restrict__ seg_w, const float* __restrict__ seg_b,
-                  const float* __restrict__ mean_vec, int D, float eps, int l2,
-                  const int* __restrict__ out_rows, float* __restrict__ emb_out,
-                  float* __restrict__ prenorm_out) {
-    extern __shared__ float sm[];
-    __shared__ double red[32];
+tstp_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, int T, int F, int C,
+            float eps, float* __restrict__ pooled) {
     const int b = blockIdx.x;
     const int HC = C * F;
-    float* pooled = sm;
-    float* emb = sm + 2 * HC;
     const int N = min(tvalid[b], T);
     const long long img_row0 = (long long)b * (T + 2) * (F + 2);
+    float* out = pooled + (long long)b * 2 * HC;
     for (int p = threadIdx.x; p < HC; p += blockDim.x) {
         const int c = p % C, f = p / C;
         const __half* col = x + (img_row0 + (F + 2) + f + 1) * C + c;  // (t=0, f)
@@ -143,23 +157,84 @@ pool_embed_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, 
         }
         float var = N > 0 ? (float)(s2 / N) : 0.0f;
         if (N > 1) var = var * ((float)N / (float)(N - 1));
-        pooled[c * F + f] = mean;
-        pooled[HC + c * F + f] = sqrtf(var + eps);
+        out[c * F + f] = mean;
+        out[HC + c * F + f] = sqrtf(var + eps);
     }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int P = 2 * HC;
-    for (int j = warp; j < D; j += nw) {
-        const float* wr = seg_w + (long long)j * P;
-        float a = 0.0f;
-        for (int i = lane; i < P; i += 32) a = fmaf(__ldg(wr + i), pooled[i], a);
+}
+
+// Embedding FC over a bucket as a split-K f32 GEMM: part[s][b][j] = sum over the
+// s-th K range of pooled[b][k] * W[j][k]. 32 clips x 64 outputs per CTA, K tiles
+// of 32 staged in shared memory, 8 outputs per thread. Each weight tile is read
+// once per 32 clips instead of once per clip.
+constexpr int kFcBM = 32, kFcBN = 64, kFcBK = 32;
+
+__global__ void __launch_bounds__(256)
+fc_partial_kernel(const float* __restrict__ pooled, const float* __restrict__ W, int B, int D,
+                  int P, int k_per_split, float* __restrict__ part) {
+    __shared__ float As[kFcBK][kFcBM + 1];
+    __shared__ float Ws[kFcBK][kFcBN + 1];
+    const int b0 = blockIdx.x * kFcBM, j0 = blockIdx.y * kFcBN;
+    const int k_lo = blockIdx.z * k_per_split, k_hi = min(P, k_lo + k_per_split);
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
+    float acc[2][4];
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) {
-            float v = a + seg_b[j];
-            if (mean_vec) v -= mean_vec[j];
-            emb[j] = v;
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = k_lo; k0 < k_hi; k0 += kFcBK) {
+        // A tile: 32 clips x 32 k (4 per thread); W tile: 64 outputs x 32 k (8 per thread)
+        for (int e = threadIdx.x; e < kFcBM * kFcBK; e += 256) {
+            const int r = e / kFcBK, k = e % kFcBK;
+            const int bb = b0 + r, kk = k0 + k;
+            As[k][r] = (bb < B && kk < k_hi) ? pooled[(long long)bb * P + kk] : 0.0f;
         }
+        for (int e = threadIdx.x; e < kFcBN * kFcBK; e += 256) {
+            const int r = e / kFcBK, k = e % kFcBK;
+            const int jj = j0 + r, kk = k0 + k;
+            Ws[k][r] = (jj < D && kk < k_hi) ? W[(long long)jj * P + kk] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kFcBK; ++k) {
+            const float a0 = As[k][ty], a1 = As[k][ty + 16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float w = Ws[k][tx + 16 * j];
+                acc[0][j] = fmaf(a0, w, acc[0][j]);
+                acc[1][j] = fmaf(a1, w, acc[1][j]);
+            }
+        }
+        __syncthreads();
+    }
+    float* out = part + (long long)blockIdx.z * B * D;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int bb = b0 + ty + 16 * i;
+        if (bb >= B) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int jj = j0 + tx + 16 * j;
+            if (jj < D) out[(long long)bb * D + jj] = acc[i][j];
+        }
+    }
+}
+
+// Sum the split-K partials in a fixed order, + bias - mean_vec, then the L2
+// normalisation the reference does on the host in double. One CTA per clip.
+__global__ void __launch_bounds__(256)
+fc_finish_kernel(const float* __restrict__ part, int n_split, int B, int D,
+                 const float* __restrict__ seg_b, const float* __restrict__ mean_vec, int l2,
+                 const int* __restrict__ out_rows, float* __restrict__ emb_out,
+                 float* __restrict__ prenorm_out) {
+    extern __shared__ float emb[];
+    __shared__ double red[32];
+    const int b = blockIdx.x;
+    for (int j = threadIdx.x; j < D; j += blockDim.x) {
+        float v = 0.0f;
+        for (int sp = 0; sp < n_split; ++sp) v += part[((long long)sp * B + b) * D + j];
+        v += seg_b[j];
+        if (mean_vec) v -= mean_vec[j];
+        emb[j] = v;
     }
     __syncthreads();
     double n2 = 0.0;
@@ -176,25 +251,42 @@ pool_embed_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, 
 
 }  // namespace
 
+size_t pool_embed_scratch_floats(int batch, int f, int c, int emb_dim) {
+    const int P = 2 * c * f;
+    const int n_split = pool_fc_splits(batch, P, emb_dim);
+    return (size_t)batch * P + (size_t)n_split * batch * emb_dim;
+}
+
+int pool_fc_splits(int batch, int P, int emb_dim) {
+    // enough CTAs to cover the SMs about twice, K ranges of at least 8 tiles
+    const int tiles = ((batch + kFcBM - 1) / kFcBM) * ((emb_dim + kFcBN - 1) / kFcBN);
+    int n = std::max(1, (2 * num_sms() + tiles - 1) / tiles);
+    n = std::min(n, std::max(1, P / (8 * kFcBK)));
+    return n;
+}
+
 int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f, int c,
                       const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
                       float var_eps, int l2, const int* out_rows, float* emb_out,
-                      float* prenorm_out, cudaStream_t stream) {
-    const size_t smem = sizeof(float) * ((size_t)2 * c * f + emb_dim);
-    if (smem > 200 * 1024) {
-        set_error("vdb_pool_embed: pooled vector too large");
+                      float* prenorm_out, float* scratch, cudaStream_t stream) {
+    const int P = 2 * c * f;
+    if ((size_t)emb_dim * sizeof(float) > 48 * 1024) {
+        set_error("vdb_pool_embed: embedding too large");
         return 1;
     }
-    static bool attr = false;
-    if (!attr) {
-        VDB_CHECK_CUDA(cudaFuncSetAttribute(pool_embed_kernel,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            200 * 1024));
-        attr = true;
-    }
-    pool_embed_kernel<<<batch, 256, smem, stream>>>(static_cast<const __half*>(x), tvalid, t, f,
-                                                    c, seg_w, seg_b, mean_vec, emb_dim, var_eps,
-                                                    l2, out_rows, emb_out, prenorm_out);
+    const int n_split = pool_fc_splits(batch, P, emb_dim);
+    const int k_per = ((P + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
+    float* pooled = scratch;
+    float* part = scratch + (size_t)batch * P;
+    tstp_kernel<<<batch, 256, 0, stream>>>(static_cast<const __half*>(x), tvalid, t, f, c, var_eps,
+                                           pooled);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    const dim3 grid((batch + kFcBM - 1) / kFcBM, (emb_dim + kFcBN - 1) / kFcBN,
+                    (P + k_per - 1) / k_per);
+    fc_partial_kernel<<<grid, 256, 0, stream>>>(pooled, seg_w, batch, emb_dim, P, k_per, part);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    fc_finish_kernel<<<batch, 256, emb_dim * sizeof(float), stream>>>(
+        part, (int)grid.z, batch, emb_dim, seg_b, mean_vec, l2, out_rows, emb_out, prenorm_out);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }
@@ -210,7 +302,8 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
         set_error("vdb_cmn_stem: NULL argument");
         return 1;
     }
-    if (batch <= 0 || t_max <= 0 || n_mels <= 0 || n_mels > 128) {
+    if (batch <= 0 || batch > 65535 || t_max <= 0 || t_max > (1 << 22) || n_mels <= 0 ||
+        n_mels > 128) {
         set_error("vdb_cmn_stem: bad shape");
         return 1;
     }
@@ -220,9 +313,8 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
                                                        mean_scratch);
         VDB_CHECK_CUDA(cudaGetLastError());
     }
-    const long long rows = vdb_grid_rows(batch, t_max, n_mels);
     const int threads = 256;
-    const unsigned blocks = (unsigned)((rows + threads - 1) / threads);
+    const dim3 blocks((unsigned)((t_max + 2 + kStemRows - 1) / kStemRows), (unsigned)batch);
     __half* yh = static_cast<__half*>(y);
     switch (oc) {
         case 16:
@@ -313,7 +405,8 @@ extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int b
         set_error("vdb_cmn_stem_noalloc: NULL argument");
         return 1;
     }
-    if (batch <= 0 || t_max <= 0 || n_mels <= 0 || n_mels > 128) {
+    if (batch <= 0 || batch > 65535 || t_max <= 0 || t_max > (1 << 22) || n_mels <= 0 ||
+        n_mels > 128) {
         set_error("vdb_cmn_stem_noalloc: bad shape");
         return 1;
     }
@@ -353,9 +446,8 @@ extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int b
         cmn_mean_kernel<<<batch, dim3(128, 4), 0, st>>>(feats, frames, t_max, n_mels, means);
         VDB_CHECK_CUDA(cudaGetLastError());
     }
-    const long long rows = vdb_grid_rows(batch, t_max, n_mels);
     const int threads = 256;
-    const unsigned blocks = (unsigned)((rows + threads - 1) / threads);
+    const dim3 blocks((unsigned)((t_max + 2 + kStemRows - 1) / kStemRows), (unsigned)batch);
     __half* yh = static_cast<__half*>(y);
     if (oc == 16)
         stem_kernel<16><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
@@ -382,6 +474,14 @@ extern "C" int vdb_pool_embed(const void* x, const int* tvalid, int batch, int t
         set_error("vdb_pool_embed: bad shape");
         return 1;
     }
-    return pool_embed_launch(x, tvalid, batch, t, f, c, seg_w, seg_b, mean_vec, emb_dim, var_eps,
-                             l2, nullptr, emb_out, prenorm_out, static_cast<cudaStream_t>(stream));
+    // stream-ordered working memory for the pooled vectors and the FC partials
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* scratch = nullptr;
+    VDB_CHECK_CUDA(cudaMallocAsync(&scratch,
+                                   sizeof(float) * pool_embed_scratch_floats(batch, f, c, emb_dim),
+                                   st));
+    const int rc = pool_embed_launch(x, tvalid, batch, t, f, c, seg_w, seg_b, mean_vec, emb_dim,
+                                     var_eps, l2, nullptr, emb_out, prenorm_out, scratch, st);
+    cudaFreeAsync(scratch, st);
+    return rc;
 }

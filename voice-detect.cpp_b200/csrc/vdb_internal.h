@@ -23,11 +23,15 @@ EncodeTiledFn encode_tiled_fn();
 int num_sms();
 
 // Pooling + FC + L2 launcher with an optional output-row map (row b of the batch
-// is written to out_rows[b]); vdb_pool_embed is the public wrapper.
+// is written to out_rows[b]); vdb_pool_embed is the public wrapper. `scratch`
+// holds pool_embed_scratch_floats(...) floats of device working memory (the
+// pooled vectors and the split-K FC partials).
+int pool_fc_splits(int batch, int P, int emb_dim);
+size_t pool_embed_scratch_floats(int batch, int f, int c, int emb_dim);
 int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f, int c,
                       const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
                       float var_eps, int l2, const int* out_rows, float* emb_out,
-                      float* prenorm_out, cudaStream_t stream);
+                      float* prenorm_out, float* scratch, cudaStream_t stream);
 
 }  // namespace vdb
 

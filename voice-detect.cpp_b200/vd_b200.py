@@ -133,6 +133,8 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_profile.restype = C.c_int
         L.voicedetect_b200_profile.argtypes = [C.c_void_p, C.c_int]
         L.voicedetect_b200_profile_read.restype = C.c_int
+        L.voicedetect_b200_profile_stages.restype = C.c_int
+        L.voicedetect_b200_profile_stages.argtypes = [C.c_void_p] + [C.POINTER(C.c_double)] * 4
         L.voicedetect_b200_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_double),
                                                     C.POINTER(C.c_double),
                                                     C.POINTER(C.c_longlong)]
@@ -268,6 +270,13 @@ class Model:
                                                  C.byref(n)) != 0:
             raise VoiceDetectError(self.last_error())
         return ms.value, fl.value, n.value
+
+    def profile_stages(self):
+        """-> {front, conv, pool, other}: ms per stage of the last profile_read."""
+        v = [C.c_double(0) for _ in range(4)]
+        if self._L.voicedetect_b200_profile_stages(self.ctx, *[C.byref(x) for x in v]) != 0:
+            raise VoiceDetectError(self.last_error())
+        return dict(zip(("front", "conv", "pool", "other"), (x.value for x in v)))
 
 
 def last_error() -> str:
