@@ -44,7 +44,7 @@ SEED = 20261201
 METRIC = "utterance-sec/sec ResNet34 embed"
 # DRAM bytes (read + write) per algorithmic conv FLOP, measured with ncu on this
 # workload at the same bucket sizes (see profiles/launches__bench_c4_512clips.md).
-CONV_DRAM_BYTES_PER_FLOP = 4.55e-3
+CONV_DRAM_BYTES_PER_FLOP = 4.45e-3
 UNIT = "utterance-sec/sec"
 
 
