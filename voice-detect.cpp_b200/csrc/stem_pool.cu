@@ -134,31 +134,61 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
 
 // TSTP, one CTA per clip: pooled[b][c*F + f] = mean, pooled[b][C*F + c*F + f] = std
 // over the clip's valid frames (two passes in f64, unbiased variance, eps inside
-// the sqrt), in the reference's C-outer / F-inner flattening.
-__global__ void __launch_bounds__(256)
+// the sqrt), in the reference's C-outer / F-inner flattening. Thread u owns 8
+// channels of one mel column (u = f * C/8 + c/8): a warp reads 512 contiguous bytes
+// per frame, and each channel's sums run over the frames in order, as before.
+__global__ void __launch_bounds__(1024)
 tstp_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, int T, int F, int C,
             float eps, float* __restrict__ pooled) {
     const int b = blockIdx.x;
     const int HC = C * F;
+    const int C8 = C / 8;
     const int N = min(tvalid[b], T);
     const long long img_row0 = (long long)b * (T + 2) * (F + 2);
     float* out = pooled + (long long)b * 2 * HC;
-    for (int p = threadIdx.x; p < HC; p += blockDim.x) {
-        const int c = p % C, f = p / C;
-        const __half* col = x + (img_row0 + (F + 2) + f + 1) * C + c;  // (t=0, f)
-        const long long tstride = (long long)(F + 2) * C;
-        double s = 0.0;
-        for (int t = 0; t < N; ++t) s += (double)__half2float(col[t * tstride]);
-        const float mean = N > 0 ? (float)(s / N) : 0.0f;
-        double s2 = 0.0;
+    const long long tstride = (long long)(F + 2) * C8;  // in 16-byte units
+    for (int u = threadIdx.x; u < F * C8; u += blockDim.x) {
+        const int f = u / C8, c0 = (u - f * C8) * 8;
+        const uint4* col = reinterpret_cast<const uint4*>(x + (img_row0 + (F + 2) + f + 1) * C + c0);
+        double s[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s[k] = 0.0;
+#pragma unroll 4
         for (int t = 0; t < N; ++t) {
-            const float d = __half2float(col[t * tstride]) - mean;
-            s2 += (double)(d * d);
+            const uint4 v = __ldg(col + t * tstride);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 p = __half22float2(h[k]);
+                s[2 * k] += (double)p.x;
+                s[2 * k + 1] += (double)p.y;
+            }
         }
-        float var = N > 0 ? (float)(s2 / N) : 0.0f;
-        if (N > 1) var = var * ((float)N / (float)(N - 1));
-        out[c * F + f] = mean;
-        out[HC + c * F + f] = sqrtf(var + eps);
+        float mean[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mean[k] = N > 0 ? (float)(s[k] / N) : 0.0f;
+        double s2[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s2[k] = 0.0;
+#pragma unroll 4
+        for (int t = 0; t < N; ++t) {
+            const uint4 v = __ldg(col + t * tstride);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 p = __half22float2(h[k]);
+                const float d0 = p.x - mean[2 * k], d1 = p.y - mean[2 * k + 1];
+                s2[2 * k] += (double)(d0 * d0);
+                s2[2 * k + 1] += (double)(d1 * d1);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float var = N > 0 ? (float)(s2[k] / N) : 0.0f;
+            if (N > 1) var = var * ((float)N / (float)(N - 1));
+            out[(c0 + k) * F + f] = mean[k];
+            out[HC + (c0 + k) * F + f] = sqrtf(var + eps);
+        }
     }
 }
 
@@ -278,8 +308,14 @@ int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f,
     const int k_per = ((P + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
     float* pooled = scratch;
     float* part = scratch + (size_t)batch * P;
-    tstp_kernel<<<batch, 256, 0, stream>>>(static_cast<const __half*>(x), tvalid, t, f, c, var_eps,
-                                           pooled);
+    if (c % 8 != 0) {
+        set_error("vdb_pool_embed: channels must be a multiple of 8");
+        return 1;
+    }
+    const int units = f * (c / 8);
+    const int tthreads = std::min(1024, (units + 31) / 32 * 32);
+    tstp_kernel<<<batch, tthreads, 0, stream>>>(static_cast<const __half*>(x), tvalid, t, f, c,
+                                                var_eps, pooled);
     VDB_CHECK_CUDA(cudaGetLastError());
     const dim3 grid((batch + kFcBM - 1) / kFcBM, (emb_dim + kFcBN - 1) / kFcBN,
                     (P + k_per - 1) / k_per);
