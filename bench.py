@@ -308,6 +308,37 @@ def run_b200(args) -> int:
         dist.all_reduce(tot_audio)
     value = float(tot_audio.item()) * args.steps / (max_ms / 1e3)
 
+    # Config 4's scoring stage, reported beside the embed metric: this rank's
+    # embeddings against a seeded registry of 100,000 unit-norm 256-d vectors, top-5
+    # (vdb_identify, f32), timed with CUDA events on the same stream.
+    ident = None
+    if args.registry > 0:
+        L = vd_b200.lib()
+        gen = torch.Generator(device=dev).manual_seed(SEED + 11)
+        reg = torch.randn(args.registry, model.dim, device=dev, generator=gen)
+        reg = reg / reg.norm(dim=1, keepdim=True)
+        top_i = torch.empty(n_local, 5, dtype=torch.int32, device=dev)
+        top_s = torch.empty(n_local, 5, device=dev)
+
+        def identify():
+            rc = L.vdb_identify(d_out.data_ptr(), n_local, reg.data_ptr(), args.registry,
+                                model.dim, 5, top_i.data_ptr(), top_s.data_ptr(),
+                                stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(vd_b200.last_error())
+        identify()
+        torch.cuda.synchronize()
+        i0, i1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        i0.record(stream)
+        for _ in range(3):
+            identify()
+        i1.record(stream)
+        torch.cuda.synchronize()
+        ims = i0.elapsed_time(i1) / 3
+        ident = {"queries_per_rank": n_local, "registry": args.registry, "dim": model.dim,
+                 "k": 5, "ms": ims, "tflops": 2.0 * n_local * args.registry * model.dim / ims / 1e9,
+                 "share_of_step": ims / (max_ms / args.steps)}
+
     # e2e through the public C ABI with host buffers (PCM in, embeddings out)
     clips = [host_pcm[offs[k]:offs[k] + lens[k]] for k in range(n_local)]
     model.embed_batch(clips[:64])
@@ -353,6 +384,7 @@ def run_b200(args) -> int:
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
+        "identify": ident,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -372,6 +404,53 @@ def run_b200(args) -> int:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_latency(args) -> int:
+    """one 3.0 s clip (T = 298), ResNet34 with f32 GGUF weights,
+    batch 1, through voicedetect_capi_embed_pcm (host PCM in, host embedding out).
+    Warm-up 3, then the median of 20 calls; the reference's own CPU kernels time the
+    same clip single-threaded and on all host threads."""
+    import vd_b200
+    tmp = tempfile.mkdtemp(prefix="vdbench_")
+    m = vd_synth.resnet34_model(SEED)
+    gguf = os.path.join(tmp, "resnet34_f32.gguf")
+    vd_synth.write_resnet_gguf(gguf, m, "f32")
+    model = vd_b200.Model(gguf)
+    pcm = vd_synth.clip_f32(vd_synth.make_clip(SEED, 48000))
+    for _ in range(3):
+        model.embed_pcm(pcm)
+    lat = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        model.embed_pcm(pcm)
+        lat.append(time.perf_counter() - t0)
+    med = statistics.median(lat)
+    out = {"metric": "config-0 latency (3.0 s clip, batch 1, ResNet34 f32 GGUF)",
+           "value": med * 1e3, "unit": "ms", "higher_is_better": False,
+           "utterance_sec_per_sec": 3.0 / med, "n_gpus": 1, "steps": 20, "warmup": 3,
+           "api": "voicedetect_capi_embed_pcm", "best_ms": min(lat) * 1e3}
+    model.close()
+    if not args.no_cpu_baseline:
+        import oracle
+        R = oracle.RefResNet34(m)
+        res = {}
+        for threads in (1, os.cpu_count() or 1):
+            oracle.ref_lib().vdref_set_threads(threads)
+            for _ in range(3):
+                R.embed(oracle.ref_fbank(pcm))
+            ts = []
+            for _ in range(20):
+                t0 = time.perf_counter()
+                R.embed(oracle.ref_fbank(pcm))
+                ts.append(time.perf_counter() - t0)
+            res[str(threads)] = statistics.median(ts) * 1e3
+        out["cpu_baseline"] = {"kind": "reference", "unit": "ms",
+                               "median_ms_by_threads": res,
+                               "sample": "the same clip; reference FBank + blocked directconv "
+                                         "kernels compiled unmodified (oracle/_ref)"}
+    print(json.dumps(out), flush=True)
     return 0
 
 
@@ -637,16 +716,22 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--ref-clips", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--registry", type=int, default=100000,
+                    help="identify registry rows for config 4's scoring stage (0 = skip)")
     ap.add_argument("--eres2net", action="store_true",
                     help="BASELINE config 2 (ERes2Net-base f16, 10 s clips) instead of the "
                          "ResNet34 headline workload")
     ap.add_argument("--eres-batch", type=int, default=256)
+    ap.add_argument("--latency", action="store_true",
+                    help="BASELINE config 0: single 3 s clip latency through the C ABI")
     ap.add_argument("--ref-eres-clips", type=int, default=8)
     args = ap.parse_args()
     if args.op_sweep:
         return run_sweep(args)
     if args.eres2net:
         return run_eres2net(args)
+    if args.latency:
+        return run_latency(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -168,3 +168,22 @@ def test_identify_matches_oracle(resnet):
     assert np.array_equal(idx, widx)
     assert np.allclose(sc, wsc, atol=1e-5)
     assert idx[0, 0] == 17 and idx[0, 1] == 500
+
+
+@pytest.mark.parametrize("n_reg,dim,k", [(70001, 64, 5), (3000, 256, 64), (257, 48, 1)])
+def test_identify_chunks_and_k(resnet, n_reg, dim, k):
+    """Registries larger than one score chunk (32,768 rows for few queries), the
+    largest k, k = 1, and sizes that are not multiples of the 128-row tiles, with
+    duplicate rows that must tie-break to the lower index."""
+    _, model = resnet
+    rng = np.random.default_rng(n_reg)
+    reg = rng.standard_normal((n_reg, dim)).astype(np.float32)
+    reg /= np.linalg.norm(reg, axis=1, keepdims=True)
+    reg[n_reg - 1] = reg[5]
+    reg[40000 % n_reg] = reg[6]
+    q = np.concatenate([reg[[5, 6]] + 0.001 * rng.standard_normal((2, dim)).astype(np.float32),
+                        rng.standard_normal((37, dim)).astype(np.float32)])
+    idx, sc = model.identify(q, reg, k=k)
+    widx, wsc = oracle.identify(q, reg, k=k)
+    assert np.array_equal(idx, widx)
+    assert np.allclose(sc, wsc, atol=1e-5)
