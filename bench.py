@@ -225,6 +225,30 @@ def config_dict(args, world):
             "parallelism": f"dp{world}", "l2_flush": "inputs larger than L2 (~5.8 GB PCM/GPU)"}
 
 
+def hbm_rooflines(stages: dict, steps: int, lens, peaks: dict) -> dict:
+    """HBM rooflines of the non-conv kernels of one step, from algorithmic bytes over
+    valid frames (padding excluded): FBank reads 4 B per f32 PCM sample and writes
+    80 x 4 B per frame; CMN + stem read the features twice (mean, then stem) and write
+    32 ch x 2 B per valid pixel; pooling reads the final 256 x 10 activation once
+    (f16, valid level-3 frames) and writes the 256 x 4 B embedding."""
+    peak = peaks.get("hbm_gbs") or 6650.0
+    frames = [1 + (n - 400) // 160 for n in lens]
+    half = lambda t: (t - 1) // 2 + 1
+    t3 = [half(half(half(t))) for t in frames]
+    alg = {"fbank": 4 * sum(lens) + 320 * sum(frames),
+           "stem": 2 * 320 * sum(frames) + 80 * 64 * sum(frames),
+           "pool": 256 * 10 * 2 * sum(t3) + 1024 * len(lens)}
+    out = {}
+    for k, by in alg.items():
+        ms = stages.get(k, 0.0) / steps
+        ach = by / (ms / 1e3) / 1e9 if ms > 0 else 0.0
+        out[k] = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                  "frac": ach / peak, "algorithmic_bytes": by, "ms_per_step": ms,
+                  "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks.get("hbm_gbs")
+                  else "fallback 6650 GB/s"}
+    return out
+
+
 def run_b200(args) -> int:
     import torch
     import torch.distributed as dist
@@ -384,6 +408,7 @@ def run_b200(args) -> int:
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
+        "rooflines_other": hbm_rooflines(stages, args.steps, lens, peaks),
         "identify": ident,
         "clocks": clk,
     }

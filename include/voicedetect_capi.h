@@ -105,10 +105,10 @@ int voicedetect_b200_sync(voicedetect_ctx* ctx);
 int voicedetect_b200_profile(voicedetect_ctx* ctx, int enable);
 int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_ms, double* conv_flops,
                                   long long* conv_launches);
-/* The same read's launch durations (ms) by stage: FBank + CMN + stem, the convs,
- * TSTP + FC + L2, and element-wise adds (ERes2Net). No reference counterpart. */
-int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* front_ms, double* conv_ms,
-                                    double* pool_ms, double* other_ms);
+/* The same read's summed launch durations (ms) by stage, written to ms[0 .. n-1] in
+ * the order: convs, FBank, CMN + stem, TSTP + FC + L2, element-wise adds (ERes2Net).
+ * No reference counterpart. */
+int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* ms, int n);
 
 #ifdef __cplusplus
 }

@@ -362,16 +362,13 @@ extern "C" int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_
     return 0;
 }
 
-extern "C" int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* front_ms,
-                                               double* conv_ms, double* pool_ms,
-                                               double* other_ms) {
-    if (!ctx || !ctx->engine) return 1;
+extern "C" int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* ms, int n) {
+    if (!ctx || !ctx->engine || !ms || n < 0) return 1;
     std::lock_guard<std::mutex> lk(ctx->mu);
+    // order: conv, FBank, CMN + stem, pooling, other
     const double* v = ctx->engine->stage_ms;
-    if (front_ms) *front_ms = v[1];
-    if (conv_ms) *conv_ms = v[0];
-    if (pool_ms) *pool_ms = v[2];
-    if (other_ms) *other_ms = v[3];
+    const double out[5] = {v[0], v[1], v[4], v[2], v[3]};
+    for (int i = 0; i < n && i < 5; ++i) ms[i] = out[i];
     return 0;
 }
 

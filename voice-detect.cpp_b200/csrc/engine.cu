@@ -882,13 +882,15 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
         err = vdb_last_error();
         return 1;
     }
+    prof_end(pf, st, 0.0);
+    const int ps = prof_begin(st, 4);
     const bool eres = cfg_.arch == "eres2net";
     if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
                      stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0], st)) {
         err = vdb_last_error();
         return 1;
     }
-    prof_end(pf, st, 0.0);
+    prof_end(ps, st, 0.0);
     launches += cfg_.cmn ? 3 : 2;
     if (eres) {
         if (run_eres2net(B, t_max, tv_sum, st, d_out, launches, err)) return 1;

@@ -196,14 +196,14 @@ private:
     std::vector<cudaEvent_t> prof_ev_;  // pairs (start, stop)
     size_t prof_used_ = 0;              // events in use
     double prof_flops_ = 0.0;
-    // Event pairs are tagged with a stage: 0 conv, 1 front (FBank + CMN + stem),
-    // 2 pooling (TSTP + FC + L2), 3 other (element-wise adds).
+    // Event pairs are tagged with a stage: 0 conv, 1 FBank, 2 pooling (TSTP + FC +
+    // L2), 3 other (element-wise adds), 4 CMN + stem.
     int prof_begin(cudaStream_t st, int stage = 0);  // returns event-pair index or -1
     void prof_end(int idx, cudaStream_t st, double flops);
     std::vector<int> prof_stage_;
 public:
     // Per-stage summed launch durations (ms) of the last read_profile call.
-    double stage_ms[4] = {0, 0, 0, 0};
+    double stage_ms[5] = {0, 0, 0, 0, 0};
 private:
 };
 

@@ -134,7 +134,7 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_profile.argtypes = [C.c_void_p, C.c_int]
         L.voicedetect_b200_profile_read.restype = C.c_int
         L.voicedetect_b200_profile_stages.restype = C.c_int
-        L.voicedetect_b200_profile_stages.argtypes = [C.c_void_p] + [C.POINTER(C.c_double)] * 4
+        L.voicedetect_b200_profile_stages.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.c_int]
         L.voicedetect_b200_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_double),
                                                     C.POINTER(C.c_double),
                                                     C.POINTER(C.c_longlong)]
@@ -272,11 +272,11 @@ class Model:
         return ms.value, fl.value, n.value
 
     def profile_stages(self):
-        """-> {front, conv, pool, other}: ms per stage of the last profile_read."""
-        v = [C.c_double(0) for _ in range(4)]
-        if self._L.voicedetect_b200_profile_stages(self.ctx, *[C.byref(x) for x in v]) != 0:
+        """-> {conv, fbank, stem, pool, other}: ms per stage of the last profile_read."""
+        v = (C.c_double * 5)()
+        if self._L.voicedetect_b200_profile_stages(self.ctx, v, 5) != 0:
             raise VoiceDetectError(self.last_error())
-        return dict(zip(("front", "conv", "pool", "other"), (x.value for x in v)))
+        return dict(zip(("conv", "fbank", "stem", "pool", "other"), list(v)))
 
 
 def last_error() -> str:
