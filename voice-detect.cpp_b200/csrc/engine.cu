@@ -1230,8 +1230,12 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
     last_launches = 0;
     std::vector<long long> bo;
     std::vector<int> bn;
-    for (size_t k = 0; k + 1 < bk.size(); ++k) {
-        const int s = (int)(k & 1);
+    // Buckets run shortest clips first: the first bucket's host gather and copy are
+    // the only ones nothing overlaps, so it should be the smallest.
+    const size_t nbk = bk.size() - 1;
+    for (size_t step = 0; step < nbk; ++step) {
+        const size_t k = nbk - 1 - step;
+        const int s = (int)(step & 1);
         const int cnt = (int)(bk[k + 1] - bk[k]);
         const int* idx = order.data() + bk[k];
         // the pinned slot is free once its previous H2D copy finished

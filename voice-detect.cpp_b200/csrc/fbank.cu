@@ -2,15 +2,17 @@
 // loop in the reference's FBank::compute (src/fbank.cpp:121-191; CMN, :194-201,
 // is fused into the stem kernel in stem.cu).
 //
-// One warp per frame. The frame's 512 FFT inputs are held 16 per lane at index
-// n = lane + 32*j, which is also the coalesced load order. The 512-point DFT is
-// split as 512 = 16 x 32 (n = n1 + 32*n2, k = k2 + 16*k1):
-//   1. 16-point DFT over each lane's registers (radix-2 DIF, unrolled);
-//   2. twiddle by W512^(lane*k2);
+// One warp per frame. The 512 real FFT inputs are packed as 256 complex values
+// z[n] = v[2n] + i v[2n+1] (the standard real-input trick), held 8 per lane at
+// n = lane + 32*j. The 256-point DFT is split as 256 = 8 x 32 (n = n1 + 32*n2,
+// k = k2 + 8*k1):
+//   1. 8-point DFT over each lane's registers (radix-2 DIF, unrolled);
+//   2. twiddle by W256^(lane*k2);
 //   3. 32-point DFT across the lanes of each register slot (radix-2 DIF with
 //      __shfl_xor_sync, 5 stages).
-// Lane l, slot r then holds X[bitrev4(r) + 16*bitrev5(l)]. Power bins 0..256
-// go through shared memory to the mel stage (one lane per filter), then
+// Z goes through shared memory, where each lane forms its bins of the real DFT,
+// X[k] = (Z[k] + conj Z[256-k])/2 + W512^k (Z[k] - conj Z[256-k])/2i, and the power
+// spectrum; the mel stage then reads bins 0..256 (one lane per filter), then
 // log(max(e, FLT_EPSILON)).
 //
 // Per-frame steps before the FFT follow the reference exactly, including its
@@ -68,7 +70,8 @@ fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offset
     // then each warp walks frames (b, t) of the flattened batch x t_max range.
     __shared__ float2 s_tw[kFFT];
     __shared__ double s_win[kFFT];
-    __shared__ float s_ps[kFramesPerBlock][kFFT / 2 + 1];
+    // per warp: the 256 complex Z[k] (2 KB), then the 257-bin power spectrum
+    __shared__ __align__(16) float s_ps[kFramesPerBlock][kFFT];
     __shared__ float s_w[kMaxWeights];
     __shared__ int s_ks[kMaxMels], s_kl[kMaxMels], s_wo[kMaxMels];
     for (int i = threadIdx.x; i < kFFT; i += blockDim.x) {
@@ -94,48 +97,51 @@ fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offset
     if (t >= T) continue;
     const float* x = pcm + offsets[b] + (long long)t * hop;
 
-    float re[16], im[16];
+    // The 512 real inputs are packed as 256 complex z[n] = v[2n] + i v[2n+1]; lane l
+    // holds n = l + 32j (j = 0..7), i.e. samples 2l + 64j and 2l + 1 + 64j.
+    float ev[8], od[8];
     double s = 0.0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int idx = lane + 32 * j;
-        const float v = idx < win ? __ldg(x + idx) : 0.0f;
-        re[j] = v;
-        s += (double)v;
+    for (int j = 0; j < 8; ++j) {
+        const int i0 = 2 * lane + 64 * j;
+        ev[j] = i0 < win ? __ldg(x + i0) : 0.0f;
+        od[j] = i0 + 1 < win ? __ldg(x + i0 + 1) : 0.0f;
+        s += (double)ev[j] + (double)od[j];
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float mean_f = (float)(s / win);
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-        if (lane + 32 * j < win) re[j] = __fsub_rn(re[j], mean_f);
-
-    // Pre-emphasis on the DC-removed frame: previous sample of index lane+32j is
-    // lane-1 in the same slot, or lane 31 of slot j-1 for lane 0.
-    float prev[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const float up = __shfl_up_sync(0xffffffffu, re[j], 1);
-        const float wrap = __shfl_sync(0xffffffffu, j > 0 ? re[j - 1] : 0.0f, 31);
-        prev[j] = lane > 0 ? up : (j > 0 ? wrap : re[0]);
+    for (int j = 0; j < 8; ++j) {
+        const int i0 = 2 * lane + 64 * j;
+        if (i0 < win) ev[j] = __fsub_rn(ev[j], mean_f);
+        if (i0 + 1 < win) od[j] = __fsub_rn(od[j], mean_f);
     }
+    // Pre-emphasis on the DC-removed frame. The odd sample's predecessor is the even
+    // sample in the same register; the even sample's is the odd sample of n - 1:
+    // lane - 1 in the same slot, or lane 31 of slot j - 1 for lane 0 (sample 0 uses
+    // itself, the reference's replicate rule).
+    float re[8], im[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int idx = lane + 32 * j;
-        float v = 0.0f;
-        if (idx < win) {
-            const float y = __fsub_rn(re[j], __fmul_rn(preemph, prev[j]));
-            v = (float)((double)y * s_win[idx]);
-        }
-        re[j] = v;
-        im[j] = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        const float up = __shfl_up_sync(0xffffffffu, od[j], 1);
+        const float wrap = __shfl_sync(0xffffffffu, j > 0 ? od[j - 1] : 0.0f, 31);
+        const float prev = lane > 0 ? up : (j > 0 ? wrap : ev[0]);
+        const int i0 = 2 * lane + 64 * j;
+        float ye = 0.0f, yo = 0.0f;
+        if (i0 < win) ye = (float)((double)__fsub_rn(ev[j], __fmul_rn(preemph, prev)) * s_win[i0]);
+        if (i0 + 1 < win)
+            yo = (float)((double)__fsub_rn(od[j], __fmul_rn(preemph, ev[j])) * s_win[i0 + 1]);
+        re[j] = ye;
+        im[j] = yo;
     }
 
-    // 1. 16-point DIF over the register slots (input order j, output bitrev4).
+    // 256-point DFT of z, 256 = 8 x 32 (n = n1 + 32 n2, k = k2 + 8 k1):
+    // 1. 8-point DIF over the register slots (output slot r holds k2 = bitrev3(r)).
 #pragma unroll
-    for (int h = 8; h >= 1; h >>= 1) {
+    for (int h = 4; h >= 1; h >>= 1) {
 #pragma unroll
-        for (int s0 = 0; s0 < 16; s0 += 2 * h) {
+        for (int s0 = 0; s0 < 8; s0 += 2 * h) {
 #pragma unroll
             for (int i = 0; i < h; ++i) {
                 const int a = s0 + i, c = s0 + i + h;
@@ -143,25 +149,25 @@ fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offset
                 re[a] = ur + vr;
                 im[a] = ui + vi;
                 float dr = ur - vr, di = ui - vi;
-                if (i != 0) cmul(dr, di, s_tw[i * (8 / h) * 32]);  // W16^(i*8/h)
+                if (i != 0) cmul(dr, di, s_tw[i * (4 / h) * 64]);  // W8^(i*4/h)
                 re[c] = dr;
                 im[c] = di;
             }
         }
     }
-    // 2. twiddle W512^(lane * k2), k2 = bitrev4(slot).
+    // 2. twiddle W256^(lane * k2) = W512^(2 * lane * k2).
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const int k2 = ((r & 1) << 3) | ((r & 2) << 1) | ((r & 4) >> 1) | ((r & 8) >> 3);
-        if (k2 != 0 && lane != 0) cmul(re[r], im[r], s_tw[(lane * k2) & (kFFT - 1)]);
+    for (int r = 0; r < 8; ++r) {
+        const int k2 = ((r & 1) << 2) | (r & 2) | ((r & 4) >> 2);
+        if (k2 != 0 && lane != 0) cmul(re[r], im[r], s_tw[(2 * lane * k2) & (kFFT - 1)]);
     }
-    // 3. 32-point DIF across lanes for every slot.
+    // 3. 32-point DIF across lanes for every slot (lane l ends with k1 = bitrev5(l)).
 #pragma unroll
     for (int h = 16; h >= 1; h >>= 1) {
         const bool upper = (lane & h) != 0;
         const float2 tw = s_tw[(lane & (h - 1)) * (256 / h)];  // W_{2h}^(lane mod h)
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
+        for (int r = 0; r < 8; ++r) {
             const float pr = __shfl_xor_sync(0xffffffffu, re[r], h);
             const float pi = __shfl_xor_sync(0xffffffffu, im[r], h);
             if (!upper) {
@@ -175,14 +181,39 @@ fbank_kernel(const float* __restrict__ pcm, const long long* __restrict__ offset
             }
         }
     }
-    // Power spectrum bins 0..256 into shared memory.
-    const int k1 = bitrev5(lane);
+    // Z[k] to shared memory, then the real-input split
+    // X[k] = A + W512^k B, A = (Z[k] + conj Z[256-k]) / 2, B = (Z[k] - conj Z[256-k]) / 2i,
+    // and the power spectrum |X[k]|^2 for k = 0..256.
+    float2* zs = reinterpret_cast<float2*>(s_ps[warp]);
+    {
+        const int k1 = bitrev5(lane);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int k2 = ((r & 1) << 2) | (r & 2) | ((r & 4) >> 2);
+            zs[k2 + 8 * k1] = make_float2(re[r], im[r]);
+        }
+    }
+    __syncwarp();
+    float pw[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        const int k = lane + 32 * m;
+        const float2 zk = zs[k], zc = zs[(256 - k) & 255];
+        const float ar = 0.5f * (zk.x + zc.x), ai = 0.5f * (zk.y - zc.y);
+        const float br = 0.5f * (zk.y + zc.y), bi = -0.5f * (zk.x - zc.x);
+        const float2 w = s_tw[k];
+        const float xr = ar + (w.x * br - w.y * bi);
+        const float xi = ai + (w.x * bi + w.y * br);
+        pw[m] = xr * xr + xi * xi;
+    }
+    const float2 z0 = zs[0];
+    __syncwarp();  // all Z reads done before the power spectrum overwrites the buffer
     float* ps = s_ps[warp];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-        const int k2 = ((r & 1) << 3) | ((r & 2) << 1) | ((r & 4) >> 1) | ((r & 8) >> 3);
-        const int k = k2 + 16 * k1;
-        if (k <= kFFT / 2) ps[k] = re[r] * re[r] + im[r] * im[r];
+    for (int m = 0; m < 8; ++m) ps[lane + 32 * m] = pw[m];
+    if (lane == 0) {
+        const float xn = z0.x - z0.y;  // X[256] = Re Z[0] - Im Z[0]
+        ps[256] = xn * xn;
     }
     __syncwarp();
     float* out = feats + ((long long)b * t_max + t) * n_mels;
