@@ -731,7 +731,8 @@ def main() -> int:
     ap.add_argument("--sweep-reps", type=int, default=20)
     ap.add_argument("--sweep-warmup", type=int, default=3)
     ap.add_argument("--sweep-tile-m", type=int, default=0, help="0 auto, 128 or 256")
-    ap.add_argument("--sweep-halo", type=int, default=0, help="0 auto, 1 force, -1 never")
+    ap.add_argument("--sweep-halo", type=int, default=0,
+                    help="0 auto, 1 resident-weight halo, 2 streamed-weight halo, -1 never")
     ap.add_argument("--sweep-ksplit", type=int, default=0, help="0 auto, else 1..16")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)

@@ -60,7 +60,8 @@ def valid_tilings(IC, OC, k, stride, two_segments=False):
     bn = OC if OC <= 256 else OC // ((OC + 255) // 256)
     kb = 64 if IC % 64 == 0 else (32 if IC % 32 == 0 else 16)
     ks = kb // 16
-    halo_ok = k == 3 and stride == 1 and OC <= 256 and 9 * IC * bn * 2 <= 96 * 1024
+    hs_ok = k == 3 and stride == 1 and OC <= 256
+    halo_ok = hs_ok and 9 * IC * bn * 2 <= 96 * 1024
     out = []
     for tile_m in (128, 256):
         nmb = tile_m // 128
@@ -69,6 +70,8 @@ def valid_tilings(IC, OC, k, stride, two_segments=False):
                 continue
             if J <= ks:
                 out.append((tile_m, -1, J))
+                if hs_ok:
+                    out.append((tile_m, 2, J))  # streamed-weights halo (two rings)
             if halo_ok:
                 out.append((tile_m, 1, J))
     if halo_ok:
