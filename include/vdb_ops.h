@@ -95,6 +95,14 @@ typedef struct vdb_conv_args {
     int act;                /* 0: [+residual] -> ReLU/clamp flags; 1: SiLU;
                                2: attentional fusion (x + ds) + tanh(acc + bias) * (x - ds)
                                with x = residual, ds = residual2 */
+    /* optional sum output (NULL = off): ysum = f16(y + addend) per element, 0 at
+       border / masked pixels; GRID layout of the output grid, row pitches ldsum /
+       ldaddend (0 = oc). The Res2Net `sp + chunk` of the next chunk, written by the
+       conv that produces sp (src/encoder_eres2net.cpp:126). */
+    void* ysum;
+    int ldsum;
+    const void* addend;
+    int ldaddend;
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */

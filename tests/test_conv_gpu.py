@@ -327,3 +327,31 @@ def test_add_slices(cuda_lib):
     ref = (a[:, 16:48].float() + b[:, 8:40].float()).half()
     assert torch.equal(y[:, 40:72], ref)
     assert torch.all(y[:, :40] == 7.0) and torch.all(y[:, 72:] == 7.0)
+
+
+def test_conv_sum_output(cuda_lib):
+    """ysum = f16(y + addend) from the epilogue, on channel slices, equal bit for bit to
+    a separate vdb_add of the stored y (the fused Res2Net `sp + chunk`)."""
+    import torch
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(36)
+    B, IC, OC, F, T = 2, 32, 32, 40, 27
+    tv = [27, 11]
+    x = _rand_act(g, B, IC, F, T, tv)
+    w = _h(torch.randn(OC, IC, 3, 3, generator=g) * 0.1)
+    bias = torch.randn(OC, generator=g) * 0.1
+    tvd = torch.tensor(tv, dtype=torch.int32, device="cuda")
+    xin = vd.to_grid(x.cuda(), tv)
+    wide = vd.to_grid(_rand_act(g, B, 3 * OC, F, T, tv).cuda(), tv)  # addend = channels [OC, 2 OC)
+    rows = vd.lib().vdb_grid_rows(B, T, F)
+    ys = torch.full((rows, 2 * OC), 5.0, dtype=torch.float16, device="cuda")
+    y = vd.conv(xin, vd.pack_conv_weight(w.cuda()), bias.cuda(), tvd, batch=B, t_out=T, f_out=F,
+                oc=OC, relu=True, clamp_hi=20.0, ysum=ys[:, OC:], addend=wide[:, OC:2 * OC])
+    ref = vd.add(y, wide[:, OC:2 * OC])
+    torch.cuda.synchronize()
+    assert torch.equal(ys[:, OC:], ref)
+    assert torch.all(ys[:, :OC] == 5.0)
+    g4 = ys[:, OC:].reshape(B, T + 2, F + 2, OC).float()
+    assert torch.all(g4[:, 0] == 0) and torch.all(g4[:, :, 0] == 0)
+    for b, t in enumerate(tv):
+        assert torch.all(g4[b, 1 + t:] == 0)

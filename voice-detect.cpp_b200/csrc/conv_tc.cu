@@ -101,6 +101,9 @@ struct ConvDev {
     int act;                 // 0 ReLU/clamp flags, 1 SiLU, 2 attentional fusion
     __half* y;
     __half* y2;              // optional PHASE-layout second output
+    __half* ysum;            // optional f16(y + addend) output (GRID rows, pitch ldsum)
+    const __half* addend;
+    int ldsum, ldadd;
     int y_phase;
     int Hp, Wp, T, F;  // output grid: Hp = T+2, Wp = F+2
     // n / (Hp*Wp) and n / Wp as (umulhi(n, mul) + n) >> sh, exact for 0 <= n < 2^31
@@ -185,7 +188,8 @@ template <int NC, int J>
 __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri,
                                           uint32_t taddr, const float* sbias, bool has_res,
                                           const uint4 (&res)[NC / 8], const __half* r2ptr,
-                                          __half* yrow, __half* y2row) {
+                                          __half* yrow, __half* y2row, __half* srow,
+                                          const __half* arow) {
     float f[NC];
 #pragma unroll
     for (int i = 0; i < NC; ++i) f[i] = 0.0f;
@@ -286,6 +290,26 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) y2p[j] = out[j];
     }
+    if (srow) {
+        // f16(y + addend) in f32, like a separate element-wise add of the stored y
+        uint4* sp = reinterpret_cast<uint4*>(srow);
+#pragma unroll
+        for (int j = 0; j < NC / 8; ++j) {
+            uint4 o = make_uint4(0u, 0u, 0u, 0u);
+            if (arow) {
+                const uint4 av = __ldg(reinterpret_cast<const uint4*>(arow) + j);
+                const __half2* ho = reinterpret_cast<const __half2*>(&out[j]);
+                const __half2* ha = reinterpret_cast<const __half2*>(&av);
+                __half2* hs = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 fo = __half22float2(ho[q]), fa = __half22float2(ha[q]);
+                    hs[q] = __floats2half2_rn(fo.x + fa.x, fo.y + fa.y);
+                }
+            }
+            sp[j] = o;
+        }
+    }
 }
 
 // Epilogue of one (tile, row block) for this thread: columns [c_lo, c_hi) of the
@@ -301,6 +325,8 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
     const __half* r2row = has_res2 ? p.residual2 + (long long)m * p.ldr2 + n0 : nullptr;
     __half* yrow = p.y + ri.dst * p.ldy + n0;
     __half* y2row = (p.y2 && ri.in_range) ? p.y2 + ri.dst2 * p.oc + n0 : nullptr;
+    __half* srow = (p.ysum && ri.in_range) ? p.ysum + (long long)m * p.ldsum + n0 : nullptr;
+    const __half* arow = (p.ysum && ri.valid) ? p.addend + (long long)m * p.ldadd + n0 : nullptr;
     uint4 res[NC / 8];
     if (has_res) load_res<NC>(rrow + c_lo, res);
     for (int c = c_lo; c < c_hi; c += NC) {
@@ -310,7 +336,8 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
         if (has_res && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
         epi_chunk<NC, J>(p, live, ri, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
                          has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
-                         y2row ? y2row + c : nullptr);
+                         y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
+                         arow ? arow + c : nullptr);
     }
 }
 
@@ -845,6 +872,13 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         return 1;
     }
     auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+    if (a->ysum && (!a->addend || (a->ldsum && a->ldsum < a->oc) ||
+                    (a->ldaddend && a->ldaddend < a->oc) || (a->ldsum | a->ldaddend) % 8 != 0 ||
+                    misaligned(a->ysum) || misaligned(a->addend))) {
+        set_error("vdb_conv: ysum needs addend, pitches >= oc and multiples of 8, 16-byte "
+                  "aligned pointers");
+        return 1;
+    }
     if (misaligned(a->x0) || (a->x1 && misaligned(a->x1)) || misaligned(a->y) ||
         (a->y2 && misaligned(a->y2)) || (a->residual && misaligned(a->residual)) ||
         (a->residual2 && misaligned(a->residual2))) {
@@ -1068,6 +1102,10 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     p.act = a->act;
     p.y = static_cast<__half*>(a->y);
     p.y2 = static_cast<__half*>(a->y2);
+    p.ysum = static_cast<__half*>(a->ysum);
+    p.addend = static_cast<const __half*>(a->addend);
+    p.ldsum = a->ldsum ? a->ldsum : a->oc;
+    p.ldadd = a->ldaddend ? a->ldaddend : a->oc;
     p.y_phase = a->y_phase;
     p.Hp = Hp;
     p.Wp = Wp;

@@ -598,16 +598,9 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
                 const EOperand sp{Acc, (i - 1) * w};
                 if (is_aff) {
                     if (!emit_aff(lo, sp, chunk, w, EOperand{Tm, 0}, false)) return false;
-                } else {
-                    EStep ad;
-                    ad.kind = 1;
-                    ad.level = lo;
-                    ad.oc = w;
-                    ad.x0 = sp;
-                    ad.x1 = chunk;
-                    ad.y = EOperand{Tm, 0};
-                    esteps_.push_back(ad);
                 }
+                // plain blocks: sp + chunk was written by the previous chunk conv's
+                // epilogue (its sum output), so there is no separate add
                 cur = EOperand{Tm, 0};
             }
             MC cv;
@@ -622,6 +615,10 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
             sc.relu = 1;
             sc.clamp_hi = hi;
             sc.y = EOperand{Acc, i * w};
+            if (!is_aff && i + 1 < S) {  // fused `sp + chunk` for the next chunk
+                sc.ysum = EOperand{Tm, 0};
+                sc.addend = EOperand{A, (i + 1) * w};
+            }
             esteps_.push_back(sc);
         }
         MC c3;
@@ -1050,6 +1047,10 @@ int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum,
         a.ldy = ld(s.y);
         a.y_phase = s.y_phase;
         a.y2 = ptr(s.y2);
+        a.ysum = ptr(s.ysum);
+        a.ldsum = ld(s.ysum);
+        a.addend = ptr(s.addend);
+        a.ldaddend = ld(s.addend);
         a.err = errword_;
         const int pe = prof_begin(st);
         if (vdb_conv(&a, st)) {

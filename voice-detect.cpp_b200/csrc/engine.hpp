@@ -55,7 +55,7 @@ struct EStep {
     int kind = 0;    // 0: vdb_conv, 1: vdb_add (y = x0 + x1 over oc channels)
     int level = 0;   // resolution level of the output
     int oc = 0, k0 = 1, stride0 = 1, ic0 = 0, ic1 = 0, stride1 = 1;
-    EOperand x0, x1, res, res2, y, y2;
+    EOperand x0, x1, res, res2, y, y2, ysum, addend;
     const __half* w0 = nullptr;
     const __half* w1 = nullptr;
     const float* bias = nullptr;

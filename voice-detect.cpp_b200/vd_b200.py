@@ -42,7 +42,8 @@ class ConvArgs(C.Structure):
         ("y_phase", C.c_int), ("err", C.c_void_p), ("tile_m", C.c_int), ("halo", C.c_int),
         ("ksplit", C.c_int), ("ldx0", C.c_int), ("ldx1", C.c_int), ("ldy", C.c_int),
         ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
-        ("act", C.c_int),
+        ("act", C.c_int), ("ysum", C.c_void_p), ("ldsum", C.c_int), ("addend", C.c_void_p),
+        ("ldaddend", C.c_int),
     ]
 
 
@@ -366,13 +367,14 @@ def _ptr(t):
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
          y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
-         y2=None, residual2=None, act=0):
+         y2=None, residual2=None, act=0, ysum=None, addend=None):
     """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
     tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
     the row pitch is taken from the view's stride); y2 is an extra PHASE output,
     w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,) or None, tvalid int32 (B,).
     act: 0 = [+residual] then relu/clamp, 1 = SiLU, 2 = attentional fusion
-    (residual + residual2) + tanh(acc + bias) * (residual - residual2)."""
+    (residual + residual2) + tanh(acc + bias) * (residual - residual2).
+    ysum / addend: optional second GRID output ysum = f16(y + addend)."""
     import torch
     if y is None:
         rows = (lib().vdb_phase_rows(batch, t_out, f_out) if y_phase
@@ -387,7 +389,8 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  y=y.data_ptr(), y_phase=int(y_phase), err=_ptr(err), tile_m=tile_m,
                  halo=halo, ksplit=ksplit, ldx0=_ld(x0), ldx1=_ld(x1), ldy=_ld(y),
                  y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
-                 ldr2=_ld(residual2), act=int(act))
+                 ldr2=_ld(residual2), act=int(act), ysum=_ptr(ysum), ldsum=_ld(ysum),
+                 addend=_ptr(addend), ldaddend=_ld(addend))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
