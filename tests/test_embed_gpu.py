@@ -187,3 +187,33 @@ def test_identify_chunks_and_k(resnet, n_reg, dim, k):
     widx, wsc = oracle.identify(q, reg, k=k)
     assert np.array_equal(idx, widx)
     assert np.allclose(sc, wsc, atol=1e-5)
+
+
+def test_repeated_shapes_replay_graphs(resnet):
+    """A bucket shape seen again is replayed from a captured CUDA graph: results stay
+    equal to the oracle, for new audio of the same lengths and for reordered clips
+    (the per-clip metadata is refreshed in device memory before every replay)."""
+    m, model = resnet
+    lens = [32000, 24000, 16000 + 160 * 3]
+    for rnd in range(4):
+        clips = [vd_synth.clip_f32(vd_synth.make_clip(500 + 10 * rnd + i, n))
+                 for i, n in enumerate(lens)]
+        if rnd == 3:
+            clips = clips[::-1]
+        got = model.embed_batch(clips)
+        for i, c in enumerate(clips):
+            assert _cos(got[i], _oracle_embed(m, c)) >= COS_TOL, (rnd, i)
+    # device path: same shapes four times
+    import torch
+    pcm = np.concatenate([vd_synth.clip_f32(vd_synth.make_clip(600 + i, n))
+                          for i, n in enumerate(lens)])
+    offs = np.cumsum([0] + lens[:-1]).astype(np.int64)
+    d_pcm = torch.from_numpy(pcm).cuda()
+    outs = []
+    for _ in range(4):
+        d_out = torch.zeros(len(lens), model.dim, device="cuda")
+        model.embed_device(d_pcm, offs, lens, d_out)
+        model.sync()
+        outs.append(d_out.cpu().numpy())
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])

@@ -1151,8 +1151,14 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     const int grid = std::max(1, std::min(n_tiles, num_sms()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto launch = [&](auto kern) -> int {
-        VDB_CHECK_CUDA(
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        // The shared-memory opt-in. While a stream is being captured into a CUDA graph
+        // it is skipped: the engine captures a bucket only after launching it plainly
+        // once, which set it.
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
+        if (cs == cudaStreamCaptureStatusNone)
+            VDB_CHECK_CUDA(
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
         kern<<<grid, kThreads, smem_launch, st>>>(tm[0], tm[1], tm[2], tm[3], p);
         VDB_CHECK_CUDA(cudaGetLastError());
         return 0;

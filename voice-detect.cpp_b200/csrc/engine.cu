@@ -102,6 +102,7 @@ inline int half_extent(int n) { return (n - 1) / 2 + 1; }
 Engine::~Engine() {
     if (device_ >= 0) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    clear_graphs();
     free_workspace();
     for (void* p : weight_allocs_) cudaFree(p);
     if (plan_) vdb_fbank_plan_destroy(plan_);
@@ -598,9 +599,19 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
                 const EOperand sp{Acc, (i - 1) * w};
                 if (is_aff) {
                     if (!emit_aff(lo, sp, chunk, w, EOperand{Tm, 0}, false)) return false;
+                } else {
+                    // A separate element-wise add: folding it into the previous chunk
+                    // conv's epilogue (the conv's ysum output) measured slower, since
+                    // the epilogue, not memory, bounds these convs.
+                    EStep ad;
+                    ad.kind = 1;
+                    ad.level = lo;
+                    ad.oc = w;
+                    ad.x0 = sp;
+                    ad.x1 = chunk;
+                    ad.y = EOperand{Tm, 0};
+                    esteps_.push_back(ad);
                 }
-                // plain blocks: sp + chunk was written by the previous chunk conv's
-                // epilogue (its sum output), so there is no separate add
                 cur = EOperand{Tm, 0};
             }
             MC cv;
@@ -615,10 +626,6 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
             sc.relu = 1;
             sc.clamp_hi = hi;
             sc.y = EOperand{Acc, i * w};
-            if (!is_aff && i + 1 < S) {  // fused `sp + chunk` for the next chunk
-                sc.ysum = EOperand{Tm, 0};
-                sc.addend = EOperand{A, (i + 1) * w};
-            }
             esteps_.push_back(sc);
         }
         MC c3;
@@ -763,6 +770,7 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     auto grow = [&](void** p, size_t& have, size_t need) -> bool {
         if (need <= have) return true;
         cudaDeviceSynchronize();  // the old buffer may still be read by queued work
+        clear_graphs();           // captured launches point at the old buffers
         cudaFree(*p);
         *p = nullptr;
         have = 0;
@@ -812,6 +820,7 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     }
     if (B > meta_cap_) {
         cudaDeviceSynchronize();
+        clear_graphs();
         stage_used_[0] = stage_used_[1] = false;
         cudaFree(meta_);
         cudaFree(offs_);
@@ -873,6 +882,64 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     VDB_CHECK_CUDA(cudaEventRecord(stage_ev_[slot], st));
     stage_used_[slot] = true;
     long long launches = 0;
+    if (!graphs_enabled_ || profiling_) {
+        if (launch_bucket(d_pcm, B, t_max, tv_sum, st, d_out, launches, err)) return 1;
+        last_launches += launches;
+        return 0;
+    }
+    GraphEntry* ge = nullptr;
+    for (GraphEntry& g : graphs_)
+        if (g.B == B && g.t_max == t_max && g.d_pcm == d_pcm && g.d_out == d_out && g.st == st)
+            ge = &g;
+    if (!ge) {
+        graphs_.push_back(GraphEntry{B, t_max, d_pcm, d_out, st, 0, nullptr, 0});
+        ge = &graphs_.back();
+    }
+    if (!ge->exec && ge->seen++ == 0) {
+        // first sight: plain launches (they also set every kernel attribute)
+        if (launch_bucket(d_pcm, B, t_max, tv_sum, st, d_out, launches, err)) return 1;
+        last_launches += launches;
+        return 0;
+    }
+    if (!ge->exec) {
+        cudaGraph_t graph = nullptr;
+        long long n = 0;
+        int rc = 1;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            rc = launch_bucket(d_pcm, B, t_max, tv_sum, st, d_out, n, err);
+            const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+            if (ce != cudaSuccess) rc = rc ? rc : 2;
+        }
+        cudaGraphExec_t exec = nullptr;
+        if (rc == 0 && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) rc = 2;
+        if (graph) cudaGraphDestroy(graph);
+        if (rc != 0) {
+            // capture not possible here: run plainly from now on
+            cudaGetLastError();
+            graphs_enabled_ = false;
+            clear_graphs();
+            if (launch_bucket(d_pcm, B, t_max, tv_sum, st, d_out, launches, err)) return 1;
+            last_launches += launches;
+            return 0;
+        }
+        ge->exec = exec;
+        ge->launches = n;
+    }
+    VDB_CHECK_CUDA(cudaGraphLaunch(ge->exec, st));
+    last_launches += ge->launches;
+    return 0;
+}
+
+void Engine::clear_graphs() {
+    for (GraphEntry& g : graphs_)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    graphs_.clear();
+}
+
+int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
+                          const std::vector<long long>& tv_sum, cudaStream_t st, float* d_out,
+                          long long& launches, std::string& err) {
+    const size_t nlev = levels_.size();
     // FBank -> CMN + stem
     const int pf = prof_begin(st, 1);
     if (vdb_fbank(plan_, d_pcm, offs_, nsamp_, B, t_max, feats_, st)) {
@@ -889,11 +956,7 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     }
     prof_end(ps, st, 0.0);
     launches += cfg_.cmn ? 3 : 2;
-    if (eres) {
-        if (run_eres2net(B, t_max, tv_sum, st, d_out, launches, err)) return 1;
-        last_launches += launches;
-        return 0;
-    }
+    if (eres) return run_eres2net(B, t_max, tv_sum, st, d_out, launches, err);
     // Backbone.
     int lev = 0, T = t_max, F = cfg_.n_mels;
     int cur = 0;            // index of the G buffer holding the block input
@@ -982,7 +1045,6 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     }
     prof_end(pp, st, 0.0);
     launches += 3;
-    last_launches += launches;
     return 0;
 }
 
@@ -1198,6 +1260,7 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
     }
     if (need > ring_bytes_) {
         VDB_CHECK_CUDA(cudaDeviceSynchronize());
+        clear_graphs();
         for (int s = 0; s < 2; ++s) {
             cudaFreeHost(h_ring_[s]);
             cudaFree(d_ring_[s]);
@@ -1217,6 +1280,7 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
     const size_t ob = (size_t)n * cfg_.emb_dim * sizeof(float);
     if (ob > out_bytes_) {
         VDB_CHECK_CUDA(cudaDeviceSynchronize());
+        clear_graphs();
         cudaFreeHost(h_out_);
         cudaFree(d_out_);
         h_out_ = nullptr;

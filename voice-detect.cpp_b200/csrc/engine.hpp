@@ -121,6 +121,10 @@ private:
     // order[bk[k] .. bk[k+1]).
     void plan_buckets(const int* nsamp, int n, long long frame_cap, std::vector<int>& order,
                       std::vector<size_t>& bk) const;
+    // Every kernel launch of one bucket (metadata already on the device).
+    int launch_bucket(const float* d_pcm, int B, int t_max, const std::vector<long long>& tv_sum,
+                      cudaStream_t st, float* d_out, long long& launches, std::string& err);
+    void clear_graphs();
     int run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
                      float* d_out, long long& launches, std::string& err);
     int ensure_workspace(int B, int t_max, std::string& err);
@@ -149,6 +153,21 @@ private:
     int pooled_ = 0;
     float var_eps_ = 1e-8f;
     std::vector<void*> weight_allocs_;
+    // CUDA graphs of a bucket's launch sequence, keyed by everything its kernel
+    // arguments depend on (the per-clip metadata lives in device buffers that are
+    // refreshed before each launch). A shape is captured the second time it is seen;
+    // any workspace growth drops them all.
+    struct GraphEntry {
+        int B, t_max;
+        const float* d_pcm;
+        float* d_out;
+        cudaStream_t st;
+        int seen;
+        cudaGraphExec_t exec;
+        long long launches;
+    };
+    std::vector<GraphEntry> graphs_;
+    bool graphs_enabled_ = true;
     // ERes2Net plan
     std::vector<EBuf> ebufs_;
     std::vector<EStep> esteps_;
