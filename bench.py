@@ -269,6 +269,8 @@ def run_b200(args) -> int:
     gguf = os.path.join(tmp, "resnet34_q8_0.gguf")
     vd_synth.write_resnet_gguf(gguf, m, "q8_0")
     model = vd_b200.Model(gguf)
+    if args.bucket_frames:
+        model.set_bucketing(args.bucket_clips, args.bucket_frames)
 
     pool = make_pool()
     lengths = global_lengths(world, args.clips_per_gpu)
@@ -742,6 +744,9 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--ref-clips", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--bucket-clips", type=int, default=512)
+    ap.add_argument("--bucket-frames", type=int, default=0,
+                    help="bucket size in padded frames (0 = the engine default, 262144)")
     ap.add_argument("--registry", type=int, default=100000,
                     help="identify registry rows for config 4's scoring stage (0 = skip)")
     ap.add_argument("--eres2net", action="store_true",
