@@ -71,8 +71,11 @@ int voicedetect_capi_identify(voicedetect_ctx* ctx, const float* queries, int n_
                               const float* registry, int n_reg, int dim, int k, int* out_idx,
                               float* out_score);
 
-/* Number of GPUs a context may use. This build drives one GPU per context (use
- * one context per GPU, in a process or thread per GPU): n_gpus must be 1. */
+/* Number of GPUs a context uses (1 <= n_gpus <= visible GPUs). For n_gpus > 1 the
+ * model is loaded on the next n_gpus - 1 devices (after the one current at load)
+ * and voicedetect_capi_embed_pcm_batch shards its clips over all of them (longest
+ * clips first to the least loaded GPU), one host thread per GPU. Other calls use
+ * the load device. */
 int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus);
 
 /* ---- B200-specific additive entry points --------------------------------------- */

@@ -9,7 +9,9 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <algorithm>
 #include <mutex>
+#include <thread>
 #include <new>
 #include <stdexcept>
 #include <string>
@@ -20,7 +22,11 @@
 #define VOICEDETECT_CAPI_ABI_VERSION 1
 
 struct voicedetect_ctx {
-    std::unique_ptr<vdb::Engine> engine;
+    std::unique_ptr<vdb::Engine> engine;  // on the device current at load time
+    // voicedetect_capi_set_devices(n > 1): the same model on n - 1 more GPUs; the
+    // batch call shards clips over all of them
+    std::vector<std::unique_ptr<vdb::Engine>> extra;
+    std::string path;
     std::string last_error;
     std::mutex mu;
 };
@@ -68,6 +74,57 @@ std::vector<float> embed_path(voicedetect_ctx* ctx, const char* path) {
     return embed_16k(ctx, vdb::resample_linear(mono, sr, 16000));
 }
 
+// The batch call on several GPUs: clips go to engines by LPT on sample count (the
+// longest clip to the least loaded GPU), each engine embeds its shard from its own
+// host thread, and rows are scattered back in the caller's order.
+int embed_sharded(voicedetect_ctx* ctx, const std::vector<const float*>& ptrs,
+                  const std::vector<int>& ns, float* out, std::string& err) {
+    std::vector<vdb::Engine*> eng{ctx->engine.get()};
+    for (auto& e : ctx->extra) eng.push_back(e.get());
+    const int G = (int)eng.size(), n = (int)ptrs.size(), D = ctx->engine->emb_dim();
+    std::vector<int> order(n);
+    for (int i = 0; i < n; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return ns[a] > ns[b]; });
+    std::vector<long long> load(G, 0);
+    std::vector<std::vector<int>> shard(G);
+    for (int i : order) {
+        int g = 0;
+        for (int k = 1; k < G; ++k)
+            if (load[k] < load[g]) g = k;
+        shard[g].push_back(i);
+        load[g] += ns[i];
+    }
+    std::vector<std::vector<float>> res(G);
+    std::vector<std::string> errs(G);
+    std::vector<int> rcs(G, 0);
+    std::vector<std::thread> th;
+    for (int g = 0; g < G; ++g) {
+        if (shard[g].empty()) continue;
+        th.emplace_back([&, g]() {
+            cudaSetDevice(eng[g]->device());
+            std::vector<const float*> p;
+            std::vector<int> c;
+            for (int i : shard[g]) {
+                p.push_back(ptrs[i]);
+                c.push_back(ns[i]);
+            }
+            res[g].resize((size_t)shard[g].size() * D);
+            rcs[g] = eng[g]->embed_host(p.data(), c.data(), (int)p.size(), res[g].data(), errs[g]);
+        });
+    }
+    for (auto& t : th) t.join();
+    cudaSetDevice(ctx->engine->device());
+    for (int g = 0; g < G; ++g)
+        if (rcs[g]) {
+            err = "GPU " + std::to_string(eng[g]->device()) + ": " + errs[g];
+            return 1;
+        }
+    for (int g = 0; g < G; ++g)
+        for (size_t j = 0; j < shard[g].size(); ++j)
+            std::memcpy(out + (size_t)shard[g][j] * D, res[g].data() + j * D, sizeof(float) * D);
+    return 0;
+}
+
 }  // namespace
 
 extern "C" int voicedetect_capi_abi_version(void) { return VOICEDETECT_CAPI_ABI_VERSION; }
@@ -84,6 +141,7 @@ extern "C" voicedetect_ctx* voicedetect_capi_load(const char* gguf_path) {
         auto* ctx = new (std::nothrow) voicedetect_ctx();
         if (!ctx) return nullptr;
         ctx->engine = std::move(e);
+        ctx->path = gguf_path;
         return ctx;
     } catch (...) {
         return nullptr;
@@ -215,7 +273,12 @@ extern "C" int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const floa
                 ns[i] = n_samples[i];
             }
         }
-        if (ctx->engine->embed_host(ptrs.data(), ns.data(), n_clips, out, err)) {
+        if (ctx->extra.empty()) {
+            if (ctx->engine->embed_host(ptrs.data(), ns.data(), n_clips, out, err)) {
+                ctx->last_error = err;
+                return 1;
+            }
+        } else if (embed_sharded(ctx, ptrs, ns, out, err)) {
             ctx->last_error = err;
             return 1;
         }
@@ -280,12 +343,42 @@ extern "C" int voicedetect_capi_identify(voicedetect_ctx* ctx, const float* quer
 extern "C" int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus) {
     if (!ctx) return 1;
     std::lock_guard<std::mutex> lk(ctx->mu);
-    if (n_gpus != 1) {
-        ctx->last_error = "this build drives one GPU per context; create one context per GPU";
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess) count = 0;
+    if (n_gpus < 1 || n_gpus > count) {
+        ctx->last_error = "n_gpus must be between 1 and the number of visible GPUs (" +
+                          std::to_string(count) + ")";
         return 1;
     }
-    ctx->last_error.clear();
-    return 0;
+    try {
+        // Devices d0, d0 + 1, ... (mod count), d0 = the load device. Engines beyond
+        // n_gpus are released; missing ones load the same GGUF on their device.
+        const int d0 = ctx->engine->device();
+        while ((int)ctx->extra.size() > n_gpus - 1) ctx->extra.pop_back();
+        for (int i = (int)ctx->extra.size() + 1; i < n_gpus; ++i) {
+            const int dev = (d0 + i) % count;
+            if (cudaSetDevice(dev) != cudaSuccess) {
+                ctx->last_error = "cudaSetDevice failed";
+                return 1;
+            }
+            std::string err;
+            std::unique_ptr<vdb::Engine> e = vdb::Engine::load(ctx->path, err);
+            if (!e) {
+                ctx->last_error = "load on GPU " + std::to_string(dev) + " failed: " + err;
+                return 1;
+            }
+            e->max_clips = ctx->engine->max_clips;
+            e->max_frames = ctx->engine->max_frames;
+            ctx->extra.push_back(std::move(e));
+        }
+        cudaSetDevice(d0);
+        ctx->last_error.clear();
+        return 0;
+    } catch (const std::exception& ex) {
+        ctx->last_error = ex.what();
+        return 1;
+    }
 }
 
 extern "C" int voicedetect_b200_embed_device(voicedetect_ctx* ctx, const float* d_pcm,
@@ -326,6 +419,10 @@ extern "C" int voicedetect_b200_set_bucketing(voicedetect_ctx* ctx, int max_clip
     }
     ctx->engine->max_clips = max_clips;
     ctx->engine->max_frames = max_frames;
+    for (auto& e : ctx->extra) {
+        e->max_clips = max_clips;
+        e->max_frames = max_frames;
+    }
     return 0;
 }
 

@@ -238,6 +238,11 @@ class Model:
             raise VoiceDetectError(self.last_error())
         return idx, sc
 
+    def set_devices(self, n_gpus: int) -> None:
+        """Use n_gpus GPUs (the batch call shards clips over them)."""
+        if self._L.voicedetect_capi_set_devices(self.ctx, n_gpus) != 0:
+            raise VoiceDetectError(self.last_error())
+
     def set_bucketing(self, max_clips: int, max_frames: int) -> None:
         if self._L.voicedetect_b200_set_bucketing(self.ctx, max_clips, max_frames) != 0:
             raise VoiceDetectError(self.last_error())
