@@ -108,6 +108,62 @@ typedef struct vdb_conv_args {
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */
 int vdb_conv(const vdb_conv_args* a, void* stream);
 
+/* ---- 1-D (TDNN) convs: the ECAPA-TDNN path ---------------------------------------
+ * Replaces the reference's conv1d_same + ReLU + bn1d_eval (+ tanh) graph pieces
+ * (src/encoder.cpp:65-151, tdnn_block :157-167, ASP :246-258), f32 im2col + mul_mat
+ * there, tensor-core implicit GEMM here.
+ *
+ * SEQ layout S(B, T, P, C): clip b owns rows [b*(T+2P), (b+1)*(T+2P)); frame t of
+ *   clip b (time-major, C channels contiguous) is row b*(T+2P) + P + t. Frames
+ *   t < tvalid[b] <= T are the clip's data. The P rows on either side of the valid
+ *   frames hold their reflection (frame -j = frame j, frame tv-1+j = frame tv-1-j,
+ *   1 <= j <= P: SpeechBrain's reflect padding at the clip's own length, which the
+ *   reference builds with get_rows, src/encoder.cpp:32-50) when the tensor feeds a
+ *   conv with k > 1; other rows are never read by a valid output.
+ * Weights: f16 [oc][k][ic], tap j at time offset (j - (k-1)/2) * dil (torch
+ *   w[oc][ic][j] -> W[oc][j][ic]). */
+long long vdb_seq_rows(int batch, int t, int pad);
+
+typedef struct vdb_conv1d_args {
+    int batch;              /* B */
+    int t;                  /* T: frame slots per clip (the bucket length) */
+    int pad;                /* P: padding rows on each side, >= (k0-1)/2 * dil0 */
+    int oc;                 /* output channels, multiple of 16, <= 4096 */
+    int k0, dil0;           /* segment 0: odd kernel size <= 9 and its dilation */
+    int ic0;                /* multiple of 16 */
+    const void* x0;         /* device f16 S(B, T, P, ic0) (or a channel slice, pitch ldx0) */
+    int ldx0;
+    const void* w0;         /* device f16 [oc][k0][ic0] */
+    int ic1;                /* segment 1 (x1 == NULL: off): a 1x1 on x1 into the same sums */
+    const void* x1;
+    int ldx1;
+    const void* w1;         /* device f16 [oc][ic1] */
+    const float* bias;      /* device f32 [oc] or NULL */
+    const float* clip_bias; /* device f32 [B][oc] added with the bias (act 3/4), or NULL */
+    const float* bn_scale;  /* act 3/4: device f32 [oc] */
+    const float* bn_shift;
+    int act;                /* 0: acc + bias [+ residual], then ReLU if relu;
+                               1: SiLU; 3: BN(ReLU(acc + bias + clip_bias)) with
+                               BN(v) = v * bn_scale + bn_shift; 4: tanh of act 3 */
+    int relu;
+    const void* residual;   /* act 0/1: device f16 S(B, T, P, oc), pitch ldr; or NULL */
+    int ldr;
+    const int* tvalid;      /* device int32 [B] */
+    void* y;                /* device S(B, T, P, oc): f16, or f32 when y_f32 */
+    int ldy;
+    int y_f32;
+    int reflect;            /* also write the P reflection rows on each side */
+    void* ysum;             /* optional f16 f16(y + addend), same rows (and reflections) */
+    int ldsum;
+    const void* addend;
+    int ldaddend;
+    int* err;               /* device error word or NULL */
+    int tile_m;             /* 0 auto, 128 or 256 */
+    int tile_n;             /* 0 auto (oc split in <= 256-column tiles), else a divisor of oc */
+} vdb_conv1d_args;
+
+int vdb_conv1d(const vdb_conv1d_args* a, void* stream);
+
 /* ---- FBank ----------------------------------------------------------------------
  * A plan holds the device tables of one FBank configuration (the GGUF
  * voicedetect.fbank.* keys, src/model_loader.cpp:126-136): Povey window, FFT

@@ -420,3 +420,7 @@ def identify(q: np.ndarray, reg: np.ndarray, k: int = 5) -> tuple[np.ndarray, np
     lib().vdo_identify(_fp(q), nq, _fp(reg), reg.shape[0], dim, k,
                        idx.ctypes.data_as(_i32p), _fp(sc))
     return idx, sc
+
+
+# ECAPA-TDNN: numpy restatement (oracle/ecapa.py)
+from .ecapa import ecapa_embed  # noqa: E402,F401

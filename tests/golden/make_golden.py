@@ -15,8 +15,13 @@ the repository).
   (vd_synth.tiny_resnet_model) from the reference kernels + restated glue.
 * ref_eres2net_tiny.npz -- the same for a small seeded ERes2Net
   (vd_synth.tiny_eres2net_model: every block kind, AFF and cross-stage fusion).
+* ref_ecapa_tiny.npz -- a small seeded ECAPA-TDNN (vd_synth.tiny_ecapa_model) on
+  two clips: torchaudio FBank features and the float64 torch forward
+  (vd_synth.ecapa_forward_torch: torch's reflect pad, conv1d, batch_norm,
+  softmax), independent of the numpy oracle it pins. The reference's own ECAPA
+  graph needs the absent ggml library, so no reference output exists for it.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py [name ...]   (default: every fixture)
 """
 import sys
 from pathlib import Path
@@ -64,7 +69,27 @@ def conv_inputs(i: int, W, H, IC, OC, k):
     return x, w, b
 
 
+def make_ecapa() -> None:
+    import torch
+    m = vd_synth.tiny_ecapa_model(7, n_mels=80)
+    d = {}
+    for i, (seed, n) in enumerate(((23, 28000), (24, 16000 + 160 * 9 + 55))):
+        pcm = vd_synth.clip_f32(vd_synth.make_clip(seed, n))
+        feats = fbank_torchaudio(pcm)
+        emb, pre = vd_synth.ecapa_forward_torch(m, torch.from_numpy(feats[None].astype(np.float64)))
+        d[f"pcm{i}"] = pcm
+        d[f"feats{i}"] = feats
+        d[f"emb{i}"] = emb[0].astype(np.float32)
+        d[f"prenorm{i}"] = pre[0].astype(np.float32)
+    np.savez_compressed(HERE / "ref_ecapa_tiny.npz", **d)
+
+
 def main() -> None:
+    if len(sys.argv) > 1:
+        for name in sys.argv[1:]:
+            {"ecapa": make_ecapa}[name]()
+        print("wrote", sys.argv[1:])
+        return
     clips = [vd_synth.make_clip(s, n) for s, n in ((11, 48000), (12, 16000 + 37), (13, 401))]
     d = {}
     for i, c in enumerate(clips):
@@ -94,6 +119,7 @@ def main() -> None:
     feats = oracle.ref_fbank(pcm)
     emb, pre = oracle.RefERes2Net(m).embed(feats)
     np.savez_compressed(HERE / "ref_eres2net_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
+    make_ecapa()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -175,3 +175,58 @@ def test_resample_linear():
     y = oracle.resample_linear(x, 8000, 16000)
     assert len(y) == 20
     assert y[0] == 0 and y[1] == pytest.approx(0.5) and y[-1] == 9
+
+
+def test_ecapa_tiny_golden():
+    """numpy ECAPA oracle (oracle/ecapa.py) vs the committed golden made by an
+    independent float64 torch formulation on torchaudio FBank features."""
+    g = np.load(GOLD / "ref_ecapa_tiny.npz")
+    m = vd_synth.tiny_ecapa_model(7, n_mels=80)
+    for i in range(2):
+        emb, pre = oracle.ecapa_embed(m, g[f"feats{i}"])
+        want = g[f"prenorm{i}"]
+        assert np.abs(pre - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+        assert _cos(emb, g[f"emb{i}"]) >= 0.999999
+        # through the oracle's own FBank (pinned to torchaudio at 1e-3 above)
+        emb2, _ = oracle.ecapa_embed(m, oracle.fbank(g[f"pcm{i}"]))
+        assert _cos(emb2, g[f"emb{i}"]) >= 0.99999
+
+
+def test_ecapa_reflect_index():
+    """reflect_pad_time's index list (src/encoder.cpp:36-44): no edge repeat, and
+    a clip must be longer than the padding."""
+    from oracle.ecapa import reflect_index
+    assert reflect_index(5, 4).tolist() == [4, 3, 2, 1, 0, 1, 2, 3, 4, 3, 2, 1, 0]
+    assert reflect_index(7, 2).tolist() == [2, 1, 0, 1, 2, 3, 4, 5, 6, 5, 4]
+    with pytest.raises(ValueError):
+        reflect_index(4, 4)
+
+
+def test_ecapa_gguf_layout(tmp_path):
+    """write_ecapa_gguf follows the reference converter: verbatim names, KV dims,
+    only the 1x1 MFA weight quantised and stored squeezed to 2-D."""
+    gguf = pytest.importorskip("gguf")
+    m = vd_synth.tiny_ecapa_model(2, n_mels=80)
+    path = tmp_path / "e.gguf"
+    vd_synth.write_ecapa_gguf(str(path), m, "f16")
+    r = gguf.GGUFReader(str(path))
+    t = {x.name: x for x in r.tensors}
+    assert set(t) == set(m["sd"])
+    assert t["mfa.conv.conv.weight"].tensor_type == gguf.GGMLQuantizationType.F16
+    assert list(t["mfa.conv.conv.weight"].shape) == [3 * 64, 96]  # ne = [IC, OC]
+    for name in ("fc.conv.weight", "asp.tdnn.conv.conv.weight", "blocks.1.tdnn1.conv.conv.weight",
+                 "blocks.1.se_block.conv1.conv.weight", "blocks.0.conv.conv.weight"):
+        assert t[name].tensor_type == gguf.GGMLQuantizationType.F32, name
+    assert list(t["blocks.0.conv.conv.weight"].shape) == [5, 80, 64]  # ne = [K, IC, OC]
+    kv = {f.name: f for f in r.fields.values()}
+    assert "voicedetect.ecapa.res2net_scale" in kv
+
+
+def test_ecapa_f16_weights_are_well_conditioned():
+    """The calibrated synthetic ECAPA is not chaotic: rounding its conv weights to
+    f16 moves the embedding far less than the 0.9999 gate."""
+    m = vd_synth.tiny_ecapa_model(3, n_mels=80)
+    feats = oracle.fbank(vd_synth.clip_f32(vd_synth.make_clip(31, 24000)))
+    a, _ = oracle.ecapa_embed(m, feats)
+    b, _ = oracle.ecapa_embed(vd_synth.f16_ecapa_model(m), feats)
+    assert _cos(a, b) >= 0.99999

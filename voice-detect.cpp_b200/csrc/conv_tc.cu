@@ -117,6 +117,14 @@ struct ConvDev {
     float clamp_hi;
     int oc;
     int* err;
+    // 1-D sequence geometry (seq != 0, vdb_conv1d): clip b owns rows
+    // [b*Hp, (b+1)*Hp) with Hp = T + 2*pad, frame t at row b*Hp + pad + t, Wp = 1.
+    // Only valid frames are stored; with `reflect` each stored row is also written
+    // to the padding rows that mirror it (reflect padding at the clip's own length).
+    int seq, pad, reflect, y_f32;
+    const float* clip_bias;  // act 3/4: f32 [batch][oc] added before the ReLU
+    const float* bn_scale;   // act 3/4: f32 [oc] per-channel affine after the ReLU
+    const float* bn_shift;
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -138,8 +146,8 @@ __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m
         const int r1 = min(mend - b * img, img);
         const int t = tv[b];
         if (t <= 0) continue;
-        const int lo = p.Wp + 1;
-        const int hi = p.Wp * t + p.F + 1;
+        const int lo = p.seq ? p.pad : p.Wp + 1;
+        const int hi = p.seq ? p.pad + t : p.Wp * t + p.F + 1;
         if (r0 < hi && r1 > lo) return true;
     }
     return false;
@@ -153,12 +161,30 @@ struct RowInfo {
     bool in_range, valid;
     long long dst;    // row of y
     long long dst2;   // row of the PHASE-layout output (y2, or y when y_phase)
+    int b;            // clip (1-D geometry)
+    long long refl[2];  // 1-D reflect: padding rows mirroring this row, or -1
 };
 
 __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int m, bool live) {
-    RowInfo ri{false, false, (long long)m, 0};
+    RowInfo ri{false, false, (long long)m, 0, 0, {-1, -1}};
     if (m >= p.M) return ri;
     ri.in_range = true;
+    if (p.seq) {
+        const int b = fdiv(m, p.img_mul, p.img_sh);
+        const int t = m - b * p.Hp - p.pad;
+        const int tvb = min(tv[b], p.T);  // a length past the slot never writes outside it
+        ri.b = b;
+        ri.valid = live && t >= 0 && t < tvb;
+        if (p.reflect && ri.valid) {
+            // frame -t mirrors frame t (1 <= t <= pad); frame 2*(tvb-1) - t mirrors
+            // frame t when it lands in [tvb, tvb + pad)
+            const long long row0 = (long long)b * p.Hp + p.pad;
+            if (t >= 1 && t <= p.pad) ri.refl[0] = row0 - t;
+            const int tr = 2 * (tvb - 1) - t;
+            if (tr >= tvb && tr < tvb + p.pad) ri.refl[1] = row0 + tr;
+        }
+        return ri;
+    }
     const int img = p.Hp * p.Wp;
     const int b = fdiv(m, p.img_mul, p.img_sh);
     const int r = m - b * img;
@@ -185,7 +211,7 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
 // -> mask -> f16 store. The TMEM loads are warp-collective, so every lane executes
 // them whenever the tile is live.
 template <int NC, int J>
-__device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri,
+__device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri, int col,
                                           uint32_t taddr, const float* sbias, bool has_res,
                                           const uint4 (&res)[NC / 8], const __half* r2ptr,
                                           __half* yrow, __half* y2row, __half* srow,
@@ -221,6 +247,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         }
     }
     if (!ri.in_range) return;
+    if (p.seq && !ri.valid) return;  // 1-D: padding rows hold reflections (or nothing used)
     if (sbias) {
 #pragma unroll
         for (int i = 0; i < NC; ++i) f[i] += sbias[i];
@@ -257,7 +284,46 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         if (p.act == 1) {
 #pragma unroll
             for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
+        } else if (p.act >= 3) {
+            // TDNN block: BatchNorm(ReLU(acc + bias [+ clip bias])), then tanh for act 4
+            const float4* sc = reinterpret_cast<const float4*>(p.bn_scale + col);
+            const float4* sh = reinterpret_cast<const float4*>(p.bn_shift + col);
+            const float4* cb = p.clip_bias ? reinterpret_cast<const float4*>(
+                                                 p.clip_bias + (long long)ri.b * p.oc + col)
+                                           : nullptr;
+#pragma unroll
+            for (int j = 0; j < NC / 4; ++j) {
+                const float4 s4 = __ldg(sc + j), h4 = __ldg(sh + j);
+                const float4 c4 = cb ? __ldg(cb + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                const float hv[4] = {h4.x, h4.y, h4.z, h4.w};
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float v = fmaxf(f[4 * j + q] + cv[q], 0.0f) * sv[q] + hv[q];
+                    if (p.act == 4) v = tanhf(v);
+                    f[4 * j + q] = v;
+                }
+            }
         }
+    }
+    if (p.y_f32) {
+        // f32 output (1-D geometry; no sum output): optional ReLU, valid rows only
+        if (p.relu) {
+#pragma unroll
+            for (int i = 0; i < NC; ++i) f[i] = fmaxf(f[i], 0.0f);
+        }
+        float* yf = reinterpret_cast<float*>(p.y);
+        const long long rows[3] = {ri.dst, ri.refl[0], ri.refl[1]};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            if (rows[k] < 0) continue;
+            float4* yp = reinterpret_cast<float4*>(yf + rows[k] * p.ldy + col);
+#pragma unroll
+            for (int j = 0; j < NC / 4; ++j)
+                yp[j] = make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+        }
+        return;
     }
     // Pack to f16 pairs, then ReLU / Hardtanh on the pairs: rounding to f16 is
     // monotone and 0 and clamp_hi are exact in f16, so max / min after rounding
@@ -290,6 +356,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) y2p[j] = out[j];
     }
+    uint4 so[NC / 8];
     if (srow) {
         // f16(y + addend) in f32, like a separate element-wise add of the stored y
         uint4* sp = reinterpret_cast<uint4*>(srow);
@@ -307,7 +374,22 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
                     hs[q] = __floats2half2_rn(fo.x + fa.x, fo.y + fa.y);
                 }
             }
+            so[j] = o;
             sp[j] = o;
+        }
+    }
+    if (p.seq && p.reflect) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (ri.refl[k] < 0) continue;
+            uint4* rp = reinterpret_cast<uint4*>(p.y + ri.refl[k] * p.ldy + col);
+#pragma unroll
+            for (int j = 0; j < NC / 8; ++j) rp[j] = out[j];
+            if (srow) {
+                uint4* rs = reinterpret_cast<uint4*>(p.ysum + ri.refl[k] * p.ldsum + col);
+#pragma unroll
+                for (int j = 0; j < NC / 8; ++j) rs[j] = so[j];
+            }
         }
     }
 }
@@ -334,7 +416,7 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
         if (has_res && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
-        epi_chunk<NC, J>(p, live, ri, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
+        epi_chunk<NC, J>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
                          has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
                          y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
                          arow ? arow + c : nullptr);
@@ -823,7 +905,29 @@ void fill_taps(SegDev& s, int k, int stride, int ic, int Wp_out) {
         }
 }
 
+// 1-D taps of a k-wide conv with dilation d: row offsets (j - (k-1)/2) * d.
+void fill_taps_1d(SegDev& s, int k, int dil, int ic) {
+    s.ic = ic;
+    s.kb = (ic % 64 == 0) ? 64 : ((ic % 32 == 0) ? 32 : 16);
+    s.n_kb = ic / s.kb;
+    s.n_taps = k;
+    for (int j = 0; j < k; ++j) {
+        s.plane[j] = 0;
+        s.off[j] = (j - (k - 1) / 2) * dil;
+    }
+}
+
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Extras of the 1-D sequence geometry (vdb_conv1d); nullptr for the 2-D grid.
+struct SeqArgs {
+    int pad, dil0, reflect, y_f32, tile_n;
+    const float* clip_bias;
+    const float* bn_scale;
+    const float* bn_shift;
+};
+
+int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream);
 
 }  // namespace
 }  // namespace vdb
@@ -844,20 +948,101 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: NULL args");
         return 1;
     }
+    return conv_impl(a, nullptr, stream);
+}
+
+extern "C" long long vdb_seq_rows(int batch, int t, int pad) {
+    return (long long)batch * (t + 2LL * pad);
+}
+
+extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
+    if (!c) {
+        set_error("vdb_conv1d: NULL args");
+        return 1;
+    }
+    if (c->pad < 0 || c->k0 < 1 || c->k0 > 9 || c->k0 % 2 == 0 || c->dil0 < 1 ||
+        (c->k0 - 1) / 2 * c->dil0 > c->pad) {
+        set_error("vdb_conv1d: k0 must be odd in [1, 9], dil0 >= 1 and (k0-1)/2 * dil0 <= pad");
+        return 1;
+    }
+    if (c->act != 0 && c->act != 1 && c->act != 3 && c->act != 4) {
+        set_error("vdb_conv1d: act must be 0, 1, 3 or 4");
+        return 1;
+    }
+    if (c->act >= 3 && (!c->bn_scale || !c->bn_shift)) {
+        set_error("vdb_conv1d: act 3/4 need bn_scale and bn_shift");
+        return 1;
+    }
+    if (c->clip_bias && c->act < 3) {
+        set_error("vdb_conv1d: clip_bias needs act 3 or 4");
+        return 1;
+    }
+    if (c->y_f32 && c->ysum) {
+        set_error("vdb_conv1d: an f32 output has no sum output");
+        return 1;
+    }
+    auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+    if ((c->bn_scale && misaligned(c->bn_scale)) || (c->bn_shift && misaligned(c->bn_shift)) ||
+        (c->clip_bias && misaligned(c->clip_bias))) {
+        set_error("vdb_conv1d: bn_scale / bn_shift / clip_bias must be 16-byte aligned");
+        return 1;
+    }
+    vdb_conv_args a{};
+    a.batch = c->batch;
+    a.t_out = c->t;
+    a.f_out = 1;
+    a.oc = c->oc;
+    a.k0 = c->k0;
+    a.stride0 = 1;
+    a.ic0 = c->ic0;
+    a.x0 = c->x0;
+    a.ldx0 = c->ldx0;
+    a.w0 = c->w0;
+    a.stride1 = 1;
+    a.ic1 = c->ic1;
+    a.x1 = c->x1;
+    a.ldx1 = c->ldx1;
+    a.w1 = c->w1;
+    a.bias = c->bias;
+    a.residual = c->residual;
+    a.ldr = c->ldr;
+    a.relu = c->relu;
+    a.tvalid = c->tvalid;
+    a.y = c->y;
+    a.ldy = c->ldy;
+    a.err = c->err;
+    a.tile_m = c->tile_m;
+    a.halo = -1;
+    a.act = c->act;
+    a.ysum = c->ysum;
+    a.ldsum = c->ldsum;
+    a.addend = c->addend;
+    a.ldaddend = c->ldaddend;
+    SeqArgs sq{c->pad, c->dil0, c->reflect ? 1 : 0, c->y_f32 ? 1 : 0, c->tile_n,
+               c->clip_bias, c->bn_scale, c->bn_shift};
+    return conv_impl(&a, &sq, stream);
+}
+
+namespace vdb {
+namespace {
+
+int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
+    const bool seq = sq != nullptr;
     if (a->batch <= 0 || a->batch > kMaxBatch || a->t_out <= 0 || a->f_out <= 0) {
         set_error("vdb_conv: batch must be in [1, 8192] and the output non-empty");
         return 1;
     }
-    if (a->oc % 16 != 0 || a->oc <= 0 || a->oc > 1024) {
-        set_error("vdb_conv: oc must be a positive multiple of 16 (<= 1024)");
+    const int oc_max = seq ? 4096 : 1024;
+    if (a->oc % 16 != 0 || a->oc <= 0 || a->oc > oc_max) {
+        set_error("vdb_conv: oc must be a positive multiple of 16 (<= 1024; <= 4096 for 1-D)");
         return 1;
     }
     if (a->ic0 % 16 != 0 || a->ic0 <= 0 || (a->x1 && (a->ic1 % 16 != 0 || a->ic1 <= 0))) {
         set_error("vdb_conv: input channels must be positive multiples of 16");
         return 1;
     }
-    if (!(a->k0 == 3 || a->k0 == 1) || !(a->stride0 == 1 || a->stride0 == 2) ||
-        (a->x1 && !(a->stride1 == 1 || a->stride1 == 2))) {
+    if (!seq && (!(a->k0 == 3 || a->k0 == 1) || !(a->stride0 == 1 || a->stride0 == 2) ||
+                 (a->x1 && !(a->stride1 == 1 || a->stride1 == 2)))) {
         set_error("vdb_conv: unsupported kernel/stride");
         return 1;
     }
@@ -885,11 +1070,22 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: activation pointers must be 16-byte aligned");
         return 1;
     }
-    if (a->act < 0 || a->act > 2 || (a->act == 2 && (!a->residual || !a->residual2))) {
+    if (!seq && (a->act < 0 || a->act > 2 || (a->act == 2 && (!a->residual || !a->residual2)))) {
         set_error("vdb_conv: act must be 0, 1 or 2 (2 needs residual and residual2)");
         return 1;
     }
-    const int n_nt = (a->oc + 255) / 256;
+    if (seq && (a->y2 || a->y_phase || a->residual2)) {
+        set_error("vdb_conv1d: no PHASE outputs or second residual in the 1-D geometry");
+        return 1;
+    }
+    int n_nt = (a->oc + 255) / 256;
+    if (seq && sq->tile_n) {
+        if (sq->tile_n % 16 != 0 || sq->tile_n > 256 || a->oc % sq->tile_n != 0) {
+            set_error("vdb_conv1d: tile_n must be a multiple of 16, <= 256, dividing oc");
+            return 1;
+        }
+        n_nt = a->oc / sq->tile_n;
+    }
     const int BN = a->oc / n_nt;
     if (BN % 16 != 0 || BN * n_nt != a->oc) {
         set_error("vdb_conv: oc does not split into tcgen05 N tiles");
@@ -898,20 +1094,28 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     // Row indices (and the fdiv fast division) are 32-bit: keep every tensor's row
     // count, plus one tile of slack, below 2^31.
     const long long kMaxRows = (1LL << 31) - 1024;
-    if (vdb_grid_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
-        vdb_phase_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
-        vdb_grid_rows(a->batch, 2 * a->t_out, 2 * a->f_out) > kMaxRows) {
+    if (seq ? vdb_seq_rows(a->batch, a->t_out, sq->pad) > kMaxRows
+            : (vdb_grid_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
+               vdb_phase_rows(a->batch, a->t_out, a->f_out) > kMaxRows ||
+               vdb_grid_rows(a->batch, 2 * a->t_out, 2 * a->f_out) > kMaxRows)) {
         set_error("vdb_conv: tensor too large (more than 2^31 rows); split the batch");
         return 1;
     }
     ConvDev p{};
-    const int Hp = a->t_out + 2, Wp = a->f_out + 2;
-    p.M = (int)vdb_grid_rows(a->batch, a->t_out, a->f_out);
+    const int Hp = seq ? a->t_out + 2 * sq->pad : a->t_out + 2;
+    const int Wp = seq ? 1 : a->f_out + 2;
+    p.M = seq ? (int)vdb_seq_rows(a->batch, a->t_out, sq->pad)
+              : (int)vdb_grid_rows(a->batch, a->t_out, a->f_out);
     p.n_nt = n_nt;
     p.BN = BN;
     p.n_seg = a->x1 ? 2 : 1;
-    fill_taps(p.seg[0], a->k0, a->stride0, a->ic0, Wp);
-    if (a->x1) fill_taps(p.seg[1], 1, a->stride1, a->ic1, Wp);
+    if (seq) {
+        fill_taps_1d(p.seg[0], a->k0, sq->dil0, a->ic0);
+        if (a->x1) fill_taps_1d(p.seg[1], 1, 1, a->ic1);
+    } else {
+        fill_taps(p.seg[0], a->k0, a->stride0, a->ic0, Wp);
+        if (a->x1) fill_taps(p.seg[1], 1, a->stride1, a->ic1, Wp);
+    }
 
     // HALO for stride-1 3x3 segments whose weights fit in shared memory.
     const uint32_t w_bytes0 = (uint32_t)9 * a->ic0 * BN * 2;
@@ -921,9 +1125,9 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     // by ~9x, but measured no faster than TAP on the ResNet34 shapes (the epilogue
     // and the MMA issue bound those convs, not the L2 feed), so auto does not pick
     // it. a->halo: 0 auto, 1 force HALO, 2 force HALO_S, -1 TAP.
-    const bool hs_ok = a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
+    const bool hs_ok = !seq && a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
     const bool halo_ok = hs_ok && w_bytes0 <= 96 * 1024;
-    if (a->halo < -1 || a->halo > 2) {
+    if (a->halo < -1 || a->halo > 2 || (seq && a->halo > 0)) {
         set_error("vdb_conv: halo must be -1, 0, 1 or 2");
         return 1;
     }
@@ -1122,6 +1326,16 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
     p.clamp_hi = a->clamp_hi;
     p.oc = a->oc;
     p.err = a->err;
+    if (seq) {
+        p.seq = 1;
+        p.pad = sq->pad;
+        p.reflect = sq->reflect;
+        p.y_f32 = sq->y_f32;
+        p.clip_bias = sq->clip_bias;
+        p.bn_scale = sq->bn_scale;
+        p.bn_shift = sq->bn_shift;
+        magic_div((uint32_t)Hp, p.img_mul, p.img_sh);
+    }
 
     // Input row extents: stride 1 reads G(B, t_out, f_out); stride 2 reads the
     // 4 planes of a PHASE tensor, each shaped like the output grid.
@@ -1134,7 +1348,7 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         const int stride = sg ? a->stride1 : a->stride0;
         const int box_rows = s.box_rows;
         const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
-        if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, stride == 2 ? 4 : 1, s.kb,
+        if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, (!seq && stride == 2) ? 4 : 1, s.kb,
                         box_rows) ||
             !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, BN, s.kb)) {
             set_error("vdb_conv: cuTensorMapEncodeTiled failed");
@@ -1181,3 +1395,6 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
             return 1;
     }
 }
+
+}  // namespace
+}  // namespace vdb

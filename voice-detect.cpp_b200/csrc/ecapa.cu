@@ -1,0 +1,342 @@
+// ECAPA-TDNN glue on the SEQ layout (vdb_ops.h): everything of the reference's
+// EcapaEncoder (src/encoder.cpp:157-340) that is not a conv. The convs themselves
+// (stem, TDNN 1x1s, dilated Res2Net convs, MFA, attention) run on the tensor cores
+// through vdb_conv1d with their ReLU -> BatchNorm (-> tanh) epilogues.
+//
+//   cmn_pack_seq_kernel   FBank CMN (src/fbank.cpp:194-201) + f16 pack into the
+//                         SEQ layout with the reflect padding the k=5 stem reads
+//                         (src/encoder.cpp:32-50)
+//   seq_mean_kernel       SE squeeze: per-clip mean over time (src/encoder.cpp:200)
+//   small_fc_kernel       SE excite 1x1s (ReLU / sigmoid, :201-207) and the
+//                         attention's global-context term (see the ASP note below)
+//   se_apply_kernel       x * gate + block input (:208, :229)
+//   seq_meanstd_kernel    ASP global statistics mean / sqrt(clamp(var, eps)) (:261-264)
+//   asp_pool_kernel       softmax over time + attention-weighted mean / std (:280-285)
+//
+// Every kernel reads only a clip's valid frames (t < tvalid[b]); rows outside them
+// are never used, so length-bucketed batches are exact.
+//
+// ASP note. The reference concatenates [x; mean; std] (3C channels) and runs the
+// attention TDNN's 1x1 conv over it (src/encoder.cpp:268-275). The mean / std
+// blocks are constant over time, so W * [x; m; s] = W_x * x + (W_m * m + W_s * s):
+// the second term is one [B, 2C] x [2C, att] product per clip (small_fc_kernel),
+// added as a per-clip bias in the tensor-core conv's epilogue before its ReLU.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "vdb_internal.h"
+#include "vdb_ops.h"
+
+namespace vdb {
+namespace {
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 t = __half22float2(h[q]);
+        f[2 * q] = t.x;
+        f[2 * q + 1] = t.y;
+    }
+}
+
+// One block per clip, blockDim (128, 4): thread x = mel bin (n_mels <= 128).
+// Writes frames -pad .. T+pad-1 of the clip (reflected at both ends).
+__global__ void cmn_pack_seq_kernel(const float* __restrict__ feats,
+                                    const int* __restrict__ frames, int t_max, int n_mels,
+                                    int cmn, int pad, __half* __restrict__ x) {
+    __shared__ double part[4][128];
+    __shared__ float mu[128];
+    const int b = blockIdx.x;
+    const int m = threadIdx.x, ty = threadIdx.y;
+    const int T = min(frames[b], t_max);
+    const float* fb = feats + (long long)b * t_max * n_mels;
+    double s = 0.0;
+    if (cmn && m < n_mels)
+        for (int t = ty; t < T; t += 4) s += (double)fb[(long long)t * n_mels + m];
+    part[ty][m] = s;
+    __syncthreads();
+    if (ty == 0 && m < n_mels)
+        mu[m] = (cmn && T > 0) ? (float)((part[0][m] + part[1][m] + part[2][m] + part[3][m]) / T)
+                               : 0.0f;
+    __syncthreads();
+    if (T <= 0 || m >= n_mels) return;
+    const long long row0 = (long long)b * (t_max + 2 * pad);
+    for (int tp = ty; tp < T + 2 * pad; tp += 4) {
+        int u = tp - pad;
+        if (u < 0) u = -u;
+        if (u >= T) u = 2 * (T - 1) - u;
+        u = min(max(u, 0), T - 1);  // clips shorter than pad + 1 frames are refused by the host
+        x[(row0 + tp) * n_mels + m] = __float2half_rn(fb[(long long)u * n_mels + m] - mu[m]);
+    }
+}
+
+// out[b][c] = mean over the valid frames of x (f32 sums). Block (b, 512 channels):
+// 64 channel groups of 8 x 4 time lanes.
+__global__ void seq_mean_kernel(const __half* __restrict__ x, int ldx,
+                                const int* __restrict__ tv, int T, int pad, int C,
+                                float* __restrict__ out) {
+    __shared__ float red[4][512];
+    const int b = blockIdx.x;
+    const int g = threadIdx.x & 63, ty = threadIdx.x >> 6;
+    const int c = blockIdx.y * 512 + g * 8;
+    const int tvb = min(tv[b], T);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c < C) {
+        const __half* xb = x + ((long long)b * (T + 2 * pad) + pad) * ldx + c;
+        for (int t = ty; t < tvb; t += 4) {
+            float f[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (long long)t * ldx)), f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += f[i];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[ty][g * 8 + i] = acc[i];
+    __syncthreads();
+    const int j = threadIdx.x;  // 256 threads, 512 sums: two each
+    for (int k = j; k < 512; k += 256) {
+        const int cc = blockIdx.y * 512 + k;
+        if (cc < C && tvb > 0)
+            out[(long long)b * C + cc] = (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb;
+    }
+}
+
+// out[b][n] = act(bias[n] + sum_k W[n][k] * in[b][k]); act 0 none, 1 ReLU,
+// 2 sigmoid. One warp per (n, 4 clips), lanes over k.
+__global__ void small_fc_kernel(const float* __restrict__ in, int ldin, int B, int K,
+                                const float* __restrict__ W, const float* __restrict__ bias, int N,
+                                int act, float* __restrict__ out, int ldout) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    const int b0 = blockIdx.y * 4;
+    if (n >= N) return;
+    float acc[4] = {0, 0, 0, 0};
+    const float* w = W + (long long)n * K;
+    for (int k = lane; k < K; k += 32) {
+        const float wv = __ldg(w + k);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (b0 + j < B) acc[j] += wv * __ldg(in + (long long)(b0 + j) * ldin + k);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    if (lane == 0) {
+        const float bv = bias ? bias[n] : 0.0f;
+        for (int j = 0; j < 4 && b0 + j < B; ++j) {
+            float v = acc[j] + bv;
+            if (act == 1) v = fmaxf(v, 0.0f);
+            else if (act == 2) v = 1.0f / (1.0f + expf(-v));
+            out[(long long)(b0 + j) * ldout + n] = v;
+        }
+    }
+}
+
+// y = h * gate[b] + res at the valid frames (8 channels per thread).
+__global__ void se_apply_kernel(const __half* __restrict__ h, int ldh,
+                                const float* __restrict__ gate, const __half* __restrict__ res,
+                                int ldr, const int* __restrict__ tv, int T, int pad, int C,
+                                long long rows, __half* __restrict__ y, int ldy) {
+    const int groups = C / 8;
+    const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= rows * groups) return;
+    const long long r = u / groups;
+    const int c = (int)(u - r * groups) * 8;
+    const int Hp = T + 2 * pad;
+    const int b = (int)(r / Hp);
+    const int t = (int)(r - (long long)b * Hp) - pad;
+    if (t < 0 || t >= tv[b]) return;
+    float fh[8], fr[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(h + r * ldh + c)), fh);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(res + r * ldr + c)), fr);
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + (long long)b * C + c));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + (long long)b * C + c + 4));
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    uint4 o;
+    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        oh[q] = __floats2half2_rn(fh[2 * q] * gv[2 * q] + fr[2 * q],
+                                  fh[2 * q + 1] * gv[2 * q + 1] + fr[2 * q + 1]);
+    *reinterpret_cast<uint4*>(y + r * ldy + c) = o;
+}
+
+// stats[b][c] = mean, stats[b][C + c] = sqrt(max(mean((x - mean)^2), eps)) over the
+// valid frames: two passes, like the reference's mean -> sub -> sqr -> mean.
+__global__ void seq_meanstd_kernel(const __half* __restrict__ x, int ldx,
+                                   const int* __restrict__ tv, int T, int pad, int C, float eps,
+                                   float* __restrict__ stats) {
+    __shared__ float red[4][512];
+    __shared__ float mean_s[512];
+    const int b = blockIdx.x;
+    const int g = threadIdx.x & 63, ty = threadIdx.x >> 6;
+    const int c = blockIdx.y * 512 + g * 8;
+    const int tvb = min(tv[b], T);
+    const __half* xb = x + ((long long)b * (T + 2 * pad) + pad) * ldx + c;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (c < C)
+        for (int t = ty; t < tvb; t += 4) {
+            float f[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (long long)t * ldx)), f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += f[i];
+        }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[ty][g * 8 + i] = acc[i];
+    __syncthreads();
+    for (int k = threadIdx.x; k < 512; k += 256)
+        mean_s[k] = tvb > 0 ? (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb : 0.0f;
+    __syncthreads();
+    float mv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        mv[i] = mean_s[g * 8 + i];
+        acc[i] = 0.0f;
+    }
+    if (c < C)
+        for (int t = ty; t < tvb; t += 4) {
+            float f[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (long long)t * ldx)), f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float d = f[i] - mv[i];
+                acc[i] += d * d;
+            }
+        }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[ty][g * 8 + i] = acc[i];
+    __syncthreads();
+    for (int k = threadIdx.x; k < 512; k += 256) {
+        const int cc = blockIdx.y * 512 + k;
+        if (cc >= C || tvb <= 0) continue;
+        const float var = (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb;
+        stats[(long long)b * 2 * C + cc] = mean_s[k];
+        stats[(long long)b * 2 * C + C + cc] = sqrtf(fmaxf(var, eps));
+    }
+}
+
+// Attentive statistics pooling of one clip's channels: a = softmax over the valid
+// frames of the logits, mu = sum a*x, sd = sqrt(max(sum a*(x - mu)^2, eps)).
+// Single pass per thread with the running maximum (online softmax) and a weighted
+// Welford update of mean and second moment, then a merge of the 4 time lanes.
+// Block (b, 64 channels): 64 channels x 4 time lanes.
+struct AspState {
+    float m, s, mu, m2;
+};
+
+__device__ __forceinline__ AspState asp_merge(const AspState& a, const AspState& b) {
+    if (b.s == 0.0f) return a;
+    if (a.s == 0.0f) return b;
+    const float m = fmaxf(a.m, b.m);
+    const float ea = expf(a.m - m), eb = expf(b.m - m);
+    const float sa = a.s * ea, sb = b.s * eb;
+    const float s = sa + sb;
+    const float d = b.mu - a.mu;
+    AspState r;
+    r.m = m;
+    r.s = s;
+    r.mu = a.mu + d * (sb / s);
+    r.m2 = a.m2 * ea + b.m2 * eb + d * d * (sa * sb / s);
+    return r;
+}
+
+__global__ void asp_pool_kernel(const float* __restrict__ logits, int ldl,
+                                const __half* __restrict__ x, int ldx, const int* __restrict__ tv,
+                                int T, int pad, int C, float eps, float* __restrict__ pooled) {
+    __shared__ AspState st[4][64];
+    const int b = blockIdx.x;
+    const int cl = threadIdx.x & 63, ty = threadIdx.x >> 6;
+    const int c = blockIdx.y * 64 + cl;
+    const int tvb = min(tv[b], T);
+    AspState a{-INFINITY, 0.0f, 0.0f, 0.0f};
+    if (c < C) {
+        const long long row0 = (long long)b * (T + 2 * pad) + pad;
+        for (int t = ty; t < tvb; t += 4) {
+            const float l = __ldg(logits + (row0 + t) * ldl + c);
+            const float xv = __half2float(x[(row0 + t) * ldx + c]);
+            if (l > a.m) {
+                const float r = expf(a.m - l);
+                a.s *= r;
+                a.m2 *= r;
+                a.m = l;
+            }
+            const float w = expf(l - a.m);
+            a.s += w;
+            const float d = xv - a.mu;
+            a.mu += d * (w / a.s);
+            a.m2 += w * d * (xv - a.mu);
+        }
+    }
+    st[ty][cl] = a;
+    __syncthreads();
+    if (ty == 0 && c < C) {
+        AspState r = st[0][cl];
+        for (int k = 1; k < 4; ++k) r = asp_merge(r, st[k][cl]);
+        const float var = r.s > 0.0f ? r.m2 / r.s : 0.0f;
+        pooled[(long long)b * 2 * C + c] = r.mu;
+        pooled[(long long)b * 2 * C + C + c] = sqrtf(fmaxf(var, eps));
+    }
+}
+
+}  // namespace
+
+int ecapa_cmn_pack(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                   int cmn, int pad, __half* x, cudaStream_t st) {
+    if (n_mels > 128) {
+        set_error("ecapa: n_mels must be <= 128");
+        return 1;
+    }
+    cmn_pack_seq_kernel<<<batch, dim3(128, 4), 0, st>>>(feats, frames, t_max, n_mels, cmn, pad, x);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int ecapa_seq_mean(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
+                   float* out, cudaStream_t st) {
+    const dim3 grid((unsigned)batch, (unsigned)((C + 511) / 512));
+    seq_mean_kernel<<<grid, 256, 0, st>>>(x, ldx, tv, T, pad, C, out);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int ecapa_small_fc(const float* in, int ldin, int batch, int K, const float* W,
+                   const float* bias, int N, int act, float* out, int ldout, cudaStream_t st) {
+    const dim3 grid((unsigned)((N + 7) / 8), (unsigned)((batch + 3) / 4));
+    small_fc_kernel<<<grid, 256, 0, st>>>(in, ldin, batch, K, W, bias, N, act, out, ldout);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int ecapa_se_apply(const __half* h, int ldh, const float* gate, const __half* res, int ldr,
+                   const int* tv, int batch, int T, int pad, int C, __half* y, int ldy,
+                   cudaStream_t st) {
+    const long long rows = vdb_seq_rows(batch, T, pad);
+    const long long units = rows * (C / 8);
+    se_apply_kernel<<<(unsigned)((units + 255) / 256), 256, 0, st>>>(h, ldh, gate, res, ldr, tv, T,
+                                                                    pad, C, rows, y, ldy);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
+                  float eps, float* stats, cudaStream_t st) {
+    const dim3 grid((unsigned)batch, (unsigned)((C + 511) / 512));
+    seq_meanstd_kernel<<<grid, 256, 0, st>>>(x, ldx, tv, T, pad, C, eps, stats);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const int* tv,
+                   int batch, int T, int pad, int C, float eps, float* pooled, cudaStream_t st) {
+    const dim3 grid((unsigned)batch, (unsigned)((C + 63) / 64));
+    asp_pool_kernel<<<grid, 256, 0, st>>>(logits, ldl, x, ldx, tv, T, pad, C, eps, pooled);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace vdb

@@ -145,6 +145,9 @@ void Engine::free_workspace() {
     cudaFree(pool_scratch_);
     pool_scratch_ = nullptr;
     pool_scratch_bytes_ = 0;
+    cudaFree(ecapa_ws_);
+    ecapa_ws_ = nullptr;
+    ecapa_ws_bytes_ = 0;
     cudaFree(meta_);
     meta_ = nullptr;
     cudaFree(offs_);
@@ -210,7 +213,7 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         return nullptr;
     }
     // load succeeds for other archs; embed then reports the arch as not implemented
-    if (c.arch != "wespeaker_resnet34" && c.arch != "eres2net") return e;
+    if (c.arch != "wespeaker_resnet34" && c.arch != "eres2net" && c.arch != "ecapa_tdnn") return e;
 
     e->plan_ = vdb_fbank_plan_create(c.sample_rate, c.n_mels, c.n_fft, c.win, c.hop, c.preemph,
                                      c.low_freq, c.high_freq);
@@ -220,6 +223,10 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
     }
     if (c.arch == "eres2net") {
         if (!e->load_eres2net(g, err)) return nullptr;
+        return e;
+    }
+    if (c.arch == "ecapa_tdnn") {
+        if (!e->load_ecapa(g, err)) return nullptr;
         return e;
     }
     Loader L{g, err};
@@ -759,7 +766,8 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
 }
 
 bool Engine::supported(std::string& err) const {
-    if (cfg_.arch != "wespeaker_resnet34" && cfg_.arch != "eres2net") {
+    if (cfg_.arch != "wespeaker_resnet34" && cfg_.arch != "eres2net" &&
+        cfg_.arch != "ecapa_tdnn") {
         err = "voicedetect: arch '" + cfg_.arch + "' is not implemented by the B200 engine";
         return false;
     }
@@ -811,7 +819,9 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     if (!grow((void**)&feats_, feats_bytes_, (size_t)B * t_max * cfg_.n_mels * sizeof(float)))
         return 1;
     if (!grow((void**)&mean_, mean_bytes_, (size_t)B * cfg_.n_mels * sizeof(float))) return 1;
-    {
+    if (cfg_.arch == "ecapa_tdnn") {
+        if (!grow(&ecapa_ws_, ecapa_ws_bytes_, ecapa_ws_bytes(B, t_max))) return 1;
+    } else {
         // pooling input: the last level's frequency extent and channels
         const int lev = cfg_.arch == "eres2net" ? e_out_level_ : (int)levels_.size() - 1;
         const int pc = cfg_.arch == "eres2net" ? ebufs_[e_out_buf_].c : levels_.back().c;
@@ -854,6 +864,18 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     const size_t nlev = levels_.size();
     int t_max = 0;
     for (int b = 0; b < B; ++b) t_max = std::max(t_max, frames_of(h_ns[b], cfg_.win, cfg_.hop));
+    if (cfg_.arch == "ecapa_tdnn") {
+        // reflect padding needs more frames than the widest conv reaches on either side
+        // (torch's reflect pad has the same precondition; the reference's index list
+        // would read outside the clip, src/encoder.cpp:36-44)
+        for (int b = 0; b < B; ++b)
+            if (frames_of(h_ns[b], cfg_.win, cfg_.hop) < ecapa_.pad + 1) {
+                err = "voicedetect: ECAPA-TDNN needs at least " + std::to_string(ecapa_.pad + 1) +
+                      " FBank frames per clip (" +
+                      std::to_string(cfg_.win + ecapa_.pad * cfg_.hop) + " samples at 16 kHz)";
+                return 1;
+            }
+    }
     if (ensure_workspace(B, t_max, err)) return 1;
     // Per-bucket metadata: [tvalid level 0..nlev-1][B], [outrow][B], then offsets, nsamp.
     // A staging slot is only rewritten after the copies that last read it finished.
@@ -949,6 +971,7 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
     prof_end(pf, st, 0.0);
     const int ps = prof_begin(st, 4);
     const bool eres = cfg_.arch == "eres2net";
+    if (cfg_.arch == "ecapa_tdnn") return run_ecapa(B, t_max, tv_sum, st, d_out, launches, err);
     if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
                      stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0], st)) {
         err = vdb_last_error();

@@ -64,6 +64,37 @@ struct EStep {
     double flops_px = 0.0;   // algorithmic FLOPs per valid output pixel
 };
 
+// ECAPA-TDNN (src/encoder.cpp). One TDNN conv: f16 weights [oc][k][ic], the conv
+// bias, and the eval BatchNorm after its ReLU folded to scale / shift (or none).
+struct TdnnDev {
+    int ic = 0, oc = 0, k = 1, dil = 1;
+    __half* w = nullptr;
+    float* b = nullptr;
+    float* scale = nullptr;
+    float* shift = nullptr;
+};
+
+struct EcapaBlockDev {
+    int dil = 1;                     // dilation of the Res2Net convs (block index + 1)
+    TdnnDev tdnn1, tdnn2;            // tdnn2.w: the columns reading group 0 ([C][C/scale])
+    __half* tdnn2_w_rest = nullptr;  // the columns reading groups 1.. ([C][C - C/scale])
+    std::vector<TdnnDev> groups;     // scale - 1 dilated convs, C/scale -> C/scale
+    int se = 0;                      // SE bottleneck
+    float* se_w1 = nullptr;          // [se][C]
+    float* se_b1 = nullptr;
+    float* se_w2 = nullptr;          // [C][se]
+    float* se_b2 = nullptr;
+};
+
+struct EcapaDev {
+    int C = 0, Cm = 0, att = 0, scale = 0, pad = 0;
+    TdnnDev stem, mfa, asp_tdnn, asp_conv;  // asp_tdnn.w: the columns reading x ([att][Cm])
+    float* asp_ctx_w = nullptr;             // [att][2*Cm]: the columns reading mean / std
+    std::vector<EcapaBlockDev> blocks;
+    float* fc_w = nullptr;                  // [emb][2*Cm], asp_bn folded in
+    float* fc_b = nullptr;
+};
+
 struct EBuf {
     int level = 0, c = 0;
     bool phase = false;      // P layout (for a stride-2 consumer) instead of G
@@ -130,6 +161,10 @@ private:
     int ensure_workspace(int B, int t_max, std::string& err);
     void free_workspace();
     bool load_eres2net(const Gguf& g, std::string& err);
+    bool load_ecapa(const Gguf& g, std::string& err);
+    int run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
+                  float* d_out, long long& launches, std::string& err);
+    size_t ecapa_ws_bytes(int B, int t_max) const;
     bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
     bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
     // f16 identity [c][c]: an identity shortcut added on the tensor cores as a 1x1
@@ -168,6 +203,10 @@ private:
     };
     std::vector<GraphEntry> graphs_;
     bool graphs_enabled_ = true;
+    // ECAPA-TDNN weights and its workspace (carved per bucket shape)
+    EcapaDev ecapa_;
+    void* ecapa_ws_ = nullptr;
+    size_t ecapa_ws_bytes_ = 0;
     // ERes2Net plan
     std::vector<EBuf> ebufs_;
     std::vector<EStep> esteps_;

@@ -295,17 +295,31 @@ int pool_fc_splits(int batch, int P, int emb_dim) {
     return n;
 }
 
-int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f, int c,
-                      const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
-                      float var_eps, int l2, const int* out_rows, float* emb_out,
-                      float* prenorm_out, float* scratch, cudaStream_t stream) {
-    const int P = 2 * c * f;
+int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
+                    const float* seg_b, const float* mean_vec, int emb_dim, int l2,
+                    const int* out_rows, float* emb_out, float* prenorm_out, float* part,
+                    cudaStream_t stream) {
     if ((size_t)emb_dim * sizeof(float) > 48 * 1024) {
         set_error("vdb_pool_embed: embedding too large");
         return 1;
     }
     const int n_split = pool_fc_splits(batch, P, emb_dim);
     const int k_per = ((P + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
+    const dim3 grid((batch + kFcBM - 1) / kFcBM, (emb_dim + kFcBN - 1) / kFcBN,
+                    (P + k_per - 1) / k_per);
+    fc_partial_kernel<<<grid, 256, 0, stream>>>(pooled, seg_w, batch, emb_dim, P, k_per, part);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    fc_finish_kernel<<<batch, 256, emb_dim * sizeof(float), stream>>>(
+        part, (int)grid.z, batch, emb_dim, seg_b, mean_vec, l2, out_rows, emb_out, prenorm_out);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f, int c,
+                      const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
+                      float var_eps, int l2, const int* out_rows, float* emb_out,
+                      float* prenorm_out, float* scratch, cudaStream_t stream) {
+    const int P = 2 * c * f;
     float* pooled = scratch;
     float* part = scratch + (size_t)batch * P;
     if (c % 8 != 0) {
@@ -317,14 +331,8 @@ int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f,
     tstp_kernel<<<batch, tthreads, 0, stream>>>(static_cast<const __half*>(x), tvalid, t, f, c,
                                                 var_eps, pooled);
     VDB_CHECK_CUDA(cudaGetLastError());
-    const dim3 grid((batch + kFcBM - 1) / kFcBM, (emb_dim + kFcBN - 1) / kFcBN,
-                    (P + k_per - 1) / k_per);
-    fc_partial_kernel<<<grid, 256, 0, stream>>>(pooled, seg_w, batch, emb_dim, P, k_per, part);
-    VDB_CHECK_CUDA(cudaGetLastError());
-    fc_finish_kernel<<<batch, 256, emb_dim * sizeof(float), stream>>>(
-        part, (int)grid.z, batch, emb_dim, seg_b, mean_vec, l2, out_rows, emb_out, prenorm_out);
-    VDB_CHECK_CUDA(cudaGetLastError());
-    return 0;
+    return fc_embed_launch(pooled, batch, P, seg_w, seg_b, mean_vec, emb_dim, l2, out_rows,
+                           emb_out, prenorm_out, part, stream);
 }
 
 }  // namespace vdb

@@ -1,6 +1,7 @@
 // Host-side helpers shared by the engine's .cu/.cpp files (not part of the ABI).
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -32,6 +33,30 @@ int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f,
                       const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
                       float var_eps, int l2, const int* out_rows, float* emb_out,
                       float* prenorm_out, float* scratch, cudaStream_t stream);
+// The embedding FC + bias - mean_vec + L2 of pool_embed_launch on pooled vectors
+// already in device memory (f32 [batch][P]); `part` holds
+// pool_fc_splits(batch, P, emb_dim) * batch * emb_dim floats.
+int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
+                    const float* seg_b, const float* mean_vec, int emb_dim, int l2,
+                    const int* out_rows, float* emb_out, float* prenorm_out, float* part,
+                    cudaStream_t stream);
+
+// ECAPA-TDNN glue kernels on the SEQ layout (ecapa.cu). tv: device int32 [batch]
+// valid frames; T and pad describe the SEQ tensors; ld* are row pitches.
+int ecapa_cmn_pack(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                   int cmn, int pad, __half* x, cudaStream_t st);
+int ecapa_seq_mean(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
+                   float* out, cudaStream_t st);
+// out[b][n] = act(bias[n] + W[n] . in[b]); act 0 none, 1 ReLU, 2 sigmoid
+int ecapa_small_fc(const float* in, int ldin, int batch, int K, const float* W,
+                   const float* bias, int N, int act, float* out, int ldout, cudaStream_t st);
+int ecapa_se_apply(const __half* h, int ldh, const float* gate, const __half* res, int ldr,
+                   const int* tv, int batch, int T, int pad, int C, __half* y, int ldy,
+                   cudaStream_t st);
+int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
+                  float eps, float* stats, cudaStream_t st);
+int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const int* tv,
+                   int batch, int T, int pad, int C, float eps, float* pooled, cudaStream_t st);
 
 }  // namespace vdb
 

@@ -47,6 +47,20 @@ class ConvArgs(C.Structure):
     ]
 
 
+class Conv1dArgs(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int), ("t", C.c_int), ("pad", C.c_int), ("oc", C.c_int),
+        ("k0", C.c_int), ("dil0", C.c_int), ("ic0", C.c_int), ("x0", C.c_void_p),
+        ("ldx0", C.c_int), ("w0", C.c_void_p), ("ic1", C.c_int), ("x1", C.c_void_p),
+        ("ldx1", C.c_int), ("w1", C.c_void_p), ("bias", C.c_void_p), ("clip_bias", C.c_void_p),
+        ("bn_scale", C.c_void_p), ("bn_shift", C.c_void_p), ("act", C.c_int), ("relu", C.c_int),
+        ("residual", C.c_void_p), ("ldr", C.c_int), ("tvalid", C.c_void_p), ("y", C.c_void_p),
+        ("ldy", C.c_int), ("y_f32", C.c_int), ("reflect", C.c_int), ("ysum", C.c_void_p),
+        ("ldsum", C.c_int), ("addend", C.c_void_p), ("ldaddend", C.c_int), ("err", C.c_void_p),
+        ("tile_m", C.c_int), ("tile_n", C.c_int),
+    ]
+
+
 def lib() -> C.CDLL:
     """Load the in-tree library (raises if it has not been built)."""
     global _lib
@@ -61,6 +75,10 @@ def lib() -> C.CDLL:
         L.vdb_phase_rows.argtypes = [C.c_int, C.c_int, C.c_int]
         L.vdb_conv.restype = C.c_int
         L.vdb_conv.argtypes = [C.POINTER(ConvArgs), C.c_void_p]
+        L.vdb_seq_rows.restype = C.c_longlong
+        L.vdb_seq_rows.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.vdb_conv1d.restype = C.c_int
+        L.vdb_conv1d.argtypes = [C.POINTER(Conv1dArgs), C.c_void_p]
         L.vdb_fbank_plan_create.restype = C.c_void_p
         L.vdb_fbank_plan_create.argtypes = [C.c_int] * 5 + [C.c_float] * 3
         L.vdb_fbank_plan_destroy.argtypes = [C.c_void_p]
@@ -398,6 +416,66 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  addend=_ptr(addend), ldaddend=_ld(addend))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
+    return y
+
+
+# ---------------------------------------------------------------------------
+# 1-D (TDNN) convs on the SEQ layout: x (B, C, T) <-> (B*(T+2*pad), C) f16 rows
+# ---------------------------------------------------------------------------
+def to_seq(x, pad: int, tvalid=None, reflect: bool = True):
+    """(B, C, T) float -> SEQ f16 (B*(T+2*pad), C). With reflect, the pad rows on
+    either side of each clip's valid frames hold their reflection; other rows 0."""
+    import torch
+    B, Cc, T = x.shape
+    s = torch.zeros(B, T + 2 * pad, Cc, dtype=torch.float16, device=x.device)
+    for b in range(B):
+        tv = T if tvalid is None else int(tvalid[b])
+        xb = x[b, :, :tv].t().to(torch.float16)
+        s[b, pad:pad + tv] = xb
+        if reflect:
+            for j in range(1, pad + 1):
+                if j < tv:
+                    s[b, pad - j] = xb[j]
+                    s[b, pad + tv - 1 + j] = xb[tv - 1 - j]
+    return s.reshape(B * (T + 2 * pad), Cc).contiguous()
+
+
+def from_seq(s, B: int, C_: int, T: int, pad: int):
+    """SEQ (rows, C) -> (B, C, T) float32 (frame slots 0..T-1)."""
+    return s.reshape(B, T + 2 * pad, C_)[:, pad:pad + T, :].permute(0, 2, 1).float().contiguous()
+
+
+def pack_conv1d_weight(w):
+    """torch (OC, IC, K) -> f16 (OC, K, IC)."""
+    return w.permute(0, 2, 1).to(__import__("torch").float16).contiguous()
+
+
+def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x1=None,
+           w1=None, ic1=None, bn_scale=None, bn_shift=None, clip_bias=None, act=0, relu=False,
+           residual=None, y=None, y_f32=False, reflect=False, ysum=None, addend=None, err=None,
+           stream=None, tile_m=0, tile_n=0):
+    """vdb_conv1d on device tensors: x0/x1/residual/y/ysum/addend are SEQ tensors
+    (rows, C) or channel-slice views of wider ones; w0 f16 (OC, K, IC), w1 f16
+    (OC, IC1); bias / bn_scale / bn_shift f32 (OC,); clip_bias f32 (B, OC).
+    act: 0 = acc + bias [+ residual] (then ReLU if relu), 1 = SiLU,
+    3 = BN(ReLU(acc + bias + clip_bias)), 4 = tanh of act 3."""
+    import torch
+    if y is None:
+        rows = lib().vdb_seq_rows(batch, t, pad)
+        y = torch.empty(rows, oc, dtype=torch.float32 if y_f32 else torch.float16,
+                        device=x0.device)
+    a = Conv1dArgs(batch=batch, t=t, pad=pad, oc=oc, k0=k0, dil0=dil0,
+                   ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(), ldx0=_ld(x0),
+                   w0=w0.data_ptr(),
+                   ic1=(ic1 if ic1 is not None else (x1.shape[1] if x1 is not None else 0)),
+                   x1=_ptr(x1), ldx1=_ld(x1), w1=_ptr(w1), bias=_ptr(bias),
+                   clip_bias=_ptr(clip_bias), bn_scale=_ptr(bn_scale), bn_shift=_ptr(bn_shift),
+                   act=int(act), relu=int(relu), residual=_ptr(residual), ldr=_ld(residual),
+                   tvalid=tvalid.data_ptr(), y=y.data_ptr(), ldy=_ld(y), y_f32=int(y_f32),
+                   reflect=int(reflect), ysum=_ptr(ysum), ldsum=_ld(ysum), addend=_ptr(addend),
+                   ldaddend=_ld(addend), err=_ptr(err), tile_m=tile_m, tile_n=tile_n)
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    _check(lib().vdb_conv1d(C.byref(a), C.c_void_p(s)), "vdb_conv1d")
     return y
 
 

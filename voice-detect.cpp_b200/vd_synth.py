@@ -465,3 +465,247 @@ def write_resnet_gguf(path: str, m: dict, dtype: str = "f32") -> None:
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
     w.close()
+
+
+# ---------------------------------------------------------------------------
+# ECAPA-TDNN (SpeechBrain layout, the reference's primary arch)
+# ---------------------------------------------------------------------------
+def ecapa_model(seed: int = 0, n_mels: int = N_MELS, channels: int = 1024, n_blocks: int = 3,
+                scale: int = 8, se_channels: int = 128, mfa_channels: int = 1536,
+                att_channels: int = 128, emb_dim: int = 192, calibrate: bool = True) -> dict:
+    """Synthetic SpeechBrain ECAPA-TDNN as a state dict with the verbatim tensor
+    names the reference reads (src/encoder.cpp:157-351, converter
+    scripts/convert_voicedetect_to_gguf.py):
+
+      blocks.0                      TDNNBlock k=5: Conv1d n_mels->C, ReLU, BatchNorm1d
+      blocks.i (i = 1..n_blocks)    SE-Res2Net: tdnn1 (1x1), res2net_block.blocks.j
+                                    (k=3, dilation i+1, C/scale channels, j < scale-1),
+                                    tdnn2 (1x1), se_block.conv1/conv2 (1x1, no BN)
+      mfa                           TDNNBlock 1x1 n_blocks*C -> mfa_channels
+      asp.tdnn / asp.conv           attention: 3*mfa -> att (TDNN), att -> mfa (Conv1d)
+      asp_bn.norm                   BatchNorm1d over 2*mfa
+      fc.conv                       Conv1d 1x1 2*mfa -> emb_dim
+
+    Conv weights are Kaiming-normal (std sqrt(2 / (IC*k))), biases N(0, 0.05),
+    BatchNorm gamma U(0.8, 1.2), beta N(0, 0.1). calibrate=True sets every
+    running mean / variance to the statistics of that BatchNorm's input on a
+    seeded calibration batch (a trained model's running statistics), like the
+    ERes2Net generator; without it the deep random network's activations drift
+    far from unit scale."""
+    rng = np.random.default_rng(seed)
+    sd: dict[str, np.ndarray] = {}
+
+    def conv(name, oc, ic, k):
+        sd[name + ".weight"] = (rng.standard_normal((oc, ic, k)) *
+                                np.sqrt(2.0 / (ic * k))).astype(np.float32)
+        sd[name + ".bias"] = rng.normal(0.0, 0.05, oc).astype(np.float32)
+
+    def bn(name, c):
+        sd[name + ".weight"] = rng.uniform(0.8, 1.2, c).astype(np.float32)
+        sd[name + ".bias"] = rng.normal(0.0, 0.1, c).astype(np.float32)
+        sd[name + ".running_mean"] = rng.normal(0.0, 0.1, c).astype(np.float32)
+        sd[name + ".running_var"] = rng.uniform(0.5, 1.5, c).astype(np.float32)
+
+    def tdnn(p, oc, ic, k):
+        conv(p + ".conv.conv", oc, ic, k)
+        bn(p + ".norm.norm", oc)
+
+    C = channels
+    w = C // scale
+    tdnn("blocks.0", C, n_mels, 5)
+    for i in range(1, n_blocks + 1):
+        p = f"blocks.{i}"
+        tdnn(p + ".tdnn1", C, C, 1)
+        for j in range(scale - 1):
+            tdnn(f"{p}.res2net_block.blocks.{j}", w, w, 3)
+        tdnn(p + ".tdnn2", C, C, 1)
+        conv(p + ".se_block.conv1.conv", se_channels, C, 1)
+        conv(p + ".se_block.conv2.conv", C, se_channels, 1)
+    tdnn("mfa", mfa_channels, n_blocks * C, 1)
+    tdnn("asp.tdnn", att_channels, 3 * mfa_channels, 1)
+    conv("asp.conv.conv", mfa_channels, att_channels, 1)
+    bn("asp_bn.norm", 2 * mfa_channels)
+    conv("fc.conv", emb_dim, 2 * mfa_channels, 1)
+    m = {"arch": "ecapa_tdnn", "sd": sd, "n_mels": n_mels, "emb_dim": emb_dim,
+         "channels": C, "n_blocks": n_blocks + 1, "scale": scale, "se_channels": se_channels,
+         "att_channels": att_channels, "l2_normalize": True}
+    if calibrate:
+        import torch
+        crng = np.random.default_rng(seed + 104729)
+        feats = torch.from_numpy(crng.standard_normal((8, n_mels, 160)) * 1.5)
+        ecapa_forward_torch(m, feats, calibrate=True)
+    return m
+
+
+def tiny_ecapa_model(seed: int = 0, n_mels: int = 16) -> dict:
+    """Narrow ECAPA (same topology rules) for CPU tests: C 64, scale 4, 3 blocks."""
+    return ecapa_model(seed, n_mels=n_mels, channels=64, scale=4, se_channels=16,
+                       mfa_channels=96, att_channels=32, emb_dim=32)
+
+
+def ecapa_forward_torch(m: dict, feats, calibrate: bool = False):
+    """ECAPA-TDNN forward in torch float64 with SpeechBrain semantics, written with
+    torch's own reflect padding, conv1d, batch_norm and softmax (an implementation
+    independent of the numpy oracle). feats: [N, n_mels, T] (CMN already applied).
+    Returns (embedding, pre-norm embedding), each [N, emb_dim].
+
+    calibrate=True first sets each BatchNorm's running statistics (in execution
+    order) to the mean / variance of its input over the batch and time, then
+    applies it; the updated arrays are written back into m["sd"]."""
+    import torch
+    import torch.nn.functional as Fn
+
+    sd = m["sd"]
+
+    def t(name):
+        return torch.from_numpy(sd[name].astype(np.float64))
+
+    def conv(x, p, dil=1):
+        wt = t(p + ".weight")
+        k = wt.shape[-1]
+        pad = (k - 1) // 2 * dil
+        if pad:
+            x = Fn.pad(x, (pad, pad), mode="reflect")
+        return Fn.conv1d(x, wt, t(p + ".bias"), dilation=dil)
+
+    def bn(x, p):
+        if calibrate:
+            dims = (0, 2) if x.dim() == 3 else (0,)
+            mu = x.mean(dims)
+            var = x.var(dims, unbiased=False).clamp_min(1e-2)
+            sd[p + ".running_mean"] = mu.numpy().astype(np.float32)
+            sd[p + ".running_var"] = var.numpy().astype(np.float32)
+        return Fn.batch_norm(x, t(p + ".running_mean"), t(p + ".running_var"), t(p + ".weight"),
+                             t(p + ".bias"), training=False, eps=1e-5)
+
+    def tdnn(x, p, dil=1):
+        return bn(torch.relu(conv(x, p + ".conv.conv", dil)), p + ".norm.norm")
+
+    def block(x, i):
+        p = f"blocks.{i}"
+        res = x
+        h = tdnn(x, p + ".tdnn1")
+        s = int(m["scale"])
+        parts = torch.chunk(h, s, dim=1)
+        ys = [parts[0]]
+        for j in range(1, s):
+            inp = parts[j] if j == 1 else parts[j] + ys[-1]
+            ys.append(tdnn(inp, f"{p}.res2net_block.blocks.{j - 1}", dil=i + 1))
+        h = tdnn(torch.cat(ys, 1), p + ".tdnn2")
+        g = h.mean(2, keepdim=True)
+        g = torch.relu(conv(g, p + ".se_block.conv1.conv"))
+        g = torch.sigmoid(conv(g, p + ".se_block.conv2.conv"))
+        return h * g + res
+
+    with torch.no_grad():
+        x = tdnn(feats.to(torch.float64), "blocks.0")
+        outs = []
+        for i in range(1, int(m["n_blocks"])):
+            x = block(x, i)
+            outs.append(x)
+        x = tdnn(torch.cat(outs, 1), "mfa")
+        T = x.shape[2]
+        mean = x.mean(2, keepdim=True)
+        std = ((x - mean) ** 2).mean(2, keepdim=True).clamp_min(1e-12).sqrt()
+        ctx = torch.cat([x, mean.expand(-1, -1, T), std.expand(-1, -1, T)], 1)
+        a = torch.tanh(tdnn(ctx, "asp.tdnn"))
+        a = torch.softmax(conv(a, "asp.conv.conv"), dim=2)
+        mu = (a * x).sum(2)
+        sdv = (a * (x - mu.unsqueeze(2)) ** 2).sum(2).clamp_min(1e-12).sqrt()
+        pooled = bn(torch.cat([mu, sdv], 1), "asp_bn.norm")
+        pre = conv(pooled.unsqueeze(2), "fc.conv").squeeze(2)
+        emb = pre / pre.norm(dim=1, keepdim=True)
+    return emb.numpy(), pre.numpy()
+
+
+def f16_ecapa_model(m: dict) -> dict:
+    """Round every ECAPA conv weight (not biases / BatchNorm) through f16."""
+    sd = {k: (v.astype(np.float16).astype(np.float32) if k.endswith("conv.weight") else v)
+          for k, v in m["sd"].items()}
+    return dict(m, sd=sd)
+
+
+_ECAPA_QUANT_EXCLUDE = ("fc.", "asp.")
+_ECAPA_QUANT_EXCLUDE_IN = (".se_block.", ".tdnn1.", ".tdnn2.")
+
+
+def _ecapa_quantizable(name: str, arr: np.ndarray) -> bool:
+    """The reference converter's quant_plan (scripts/convert_voicedetect_to_gguf.py:
+    allowlist '.conv.weight', exclusions fc / asp / se_block / tdnn1 / tdnn2,
+    kernel 1, both channel counts >= 32): only the MFA weight qualifies."""
+    if not name.endswith(".conv.weight") or arr.ndim != 3 or arr.shape[2] != 1:
+        return False
+    if name.startswith(_ECAPA_QUANT_EXCLUDE) or any(s in name for s in _ECAPA_QUANT_EXCLUDE_IN):
+        return False
+    return arr.shape[0] >= 32 and arr.shape[1] >= 32
+
+
+def write_ecapa_gguf(path: str, m: dict, dtype: str = "f32") -> None:
+    """Write an ecapa_tdnn GGUF with the reference's KV schema and verbatim tensor
+    names. dtype f32 | f16 | q8_0 applies where the reference converter quantises
+    (the 1x1 MFA weight, stored squeezed to 2-D [OC, IC]); every other tensor is f32."""
+    import gguf
+    from gguf import quants
+
+    w = gguf.GGUFWriter(path, arch="voicedetect")
+    w.add_string("voicedetect.arch", "ecapa_tdnn")
+    w.add_uint32("voicedetect.embedding_dim", int(m["emb_dim"]))
+    w.add_bool("voicedetect.l2_normalize", bool(m.get("l2_normalize", True)))
+    w.add_uint32("voicedetect.fbank.sample_rate", 16000)
+    w.add_uint32("voicedetect.fbank.n_mels", int(m["n_mels"]))
+    w.add_uint32("voicedetect.fbank.n_fft", 512)
+    w.add_uint32("voicedetect.fbank.win_length", 400)
+    w.add_uint32("voicedetect.fbank.hop_length", 160)
+    w.add_float32("voicedetect.fbank.preemph", 0.97)
+    w.add_float32("voicedetect.fbank.low_freq", 20.0)
+    w.add_float32("voicedetect.fbank.high_freq", 0.0)
+    w.add_bool("voicedetect.fbank.use_energy", False)
+    w.add_bool("voicedetect.fbank.cmn", True)
+    w.add_string("voicedetect.fbank.window", "povey")
+    w.add_uint32("voicedetect.ecapa.channels", int(m["channels"]))
+    w.add_uint32("voicedetect.ecapa.n_blocks", int(m["n_blocks"]))
+    w.add_uint32("voicedetect.ecapa.se_channels", int(m["se_channels"]))
+    w.add_uint32("voicedetect.ecapa.res2net_scale", int(m["scale"]))
+    w.add_uint32("voicedetect.ecapa.attention_channels", int(m["att_channels"]))
+    for name, arr in m["sd"].items():
+        arr = np.ascontiguousarray(arr, np.float32)
+        if dtype == "f32" or not _ecapa_quantizable(name, arr):
+            w.add_tensor(name, arr)
+            continue
+        a2 = np.ascontiguousarray(arr[:, :, 0])
+        if dtype == "f16":
+            w.add_tensor(name, a2.astype(np.float16))
+        elif dtype == "q8_0" and a2.shape[1] % 32 == 0:
+            qb = quants.quantize(a2, gguf.GGMLQuantizationType.Q8_0)
+            w.add_tensor(name, qb, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        elif dtype == "q8_0":
+            w.add_tensor(name, arr)
+        else:
+            raise ValueError(dtype)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+def quantized_ecapa_model(m: dict, dtype: str) -> dict:
+    """The model a dtype GGUF carries (quantised MFA weight round-tripped)."""
+    if dtype == "f32":
+        return m
+    import gguf
+    from gguf import quants
+
+    sd = dict(m["sd"])
+    for name, arr in m["sd"].items():
+        if not _ecapa_quantizable(name, arr):
+            continue
+        a2 = np.ascontiguousarray(arr[:, :, 0])
+        if dtype == "f16":
+            r = a2.astype(np.float16).astype(np.float32)
+        elif a2.shape[1] % 32 == 0:
+            qt = gguf.GGMLQuantizationType.Q8_0
+            r = quants.dequantize(quants.quantize(a2, qt), qt).reshape(a2.shape)
+        else:
+            r = a2
+        sd[name] = r[:, :, None].astype(np.float32)
+    return dict(m, sd=sd)
