@@ -482,6 +482,7 @@ def run_latency(args) -> int:
 
 
 ERES_METRIC = "utterance-sec/sec ERes2Net-base embed"
+ECAPA_METRIC = "utterance-sec/sec ECAPA-TDNN embed"
 
 
 def cpu_reference_eres2net(m: dict, clips, threads: int):
@@ -498,9 +499,78 @@ def cpu_reference_eres2net(m: dict, clips, threads: int):
     return sum(len(c) for c in clips) / SR, time.perf_counter() - t0
 
 
-def run_eres2net(args) -> int:
+def cpu_port_ecapa(m: dict, clips, threads: int):
+    """The numpy ECAPA oracle (oracle/ecapa.py, a restatement of src/encoder.cpp:
+    the reference's ECAPA graph needs the absent ggml library) + the oracle FBank on
+    `clips`, float32 matmuls on `threads` BLAS threads; (audio_seconds, wall_seconds)."""
+    import oracle
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    ctx = threadpool_limits(limits=threads) if threadpool_limits else None
+    try:
+        oracle.ecapa_embed(m, oracle.fbank(clips[0][:16000]))
+        t0 = time.perf_counter()
+        for c in clips:
+            oracle.ecapa_embed(m, oracle.fbank(c))
+        return sum(len(c) for c in clips) / SR, time.perf_counter() - t0
+    finally:
+        if ctx is not None:
+            ctx.unregister()
+
+
+class _Family:
+    """One fixed-batch benchmark config: BASELINE config 2 (ERes2Net) or 3 (ECAPA)."""
+
+    def __init__(self, name: str, args):
+        self.name = name
+        self.args = args
+        if name == "eres2net":
+            self.metric, self.seconds, self.batch = ERES_METRIC, 10, args.eres_batch
+            self.gguf_name, self.ref_clips = "eres2net_f16.gguf", args.ref_eres_clips
+        else:
+            self.metric, self.seconds, self.batch = ECAPA_METRIC, 4, args.ecapa_batch
+            self.gguf_name, self.ref_clips = "ecapa_f16.gguf", args.ref_ecapa_clips
+
+    def model(self):
+        return vd_synth.eres2net_model(SEED) if self.name == "eres2net" else \
+            vd_synth.ecapa_model(SEED)
+
+    def write(self, path, m):
+        if self.name == "eres2net":
+            vd_synth.write_eres2net_gguf(path, m, "f16")
+        else:
+            vd_synth.write_ecapa_gguf(path, m, "f16")
+
+    def weights_as_loaded(self, m):
+        return vd_synth.quantize_model_f16(m) if self.name == "eres2net" else \
+            vd_synth.quantized_ecapa_model(m, "f16")
+
+    def cpu(self, m, clips, threads):
+        """(audio_s, wall_s, kind, sample description)"""
+        if self.name == "eres2net":
+            audio, wall = cpu_reference_eres2net(m, clips, threads)
+            return audio, wall, "reference", (
+                f"{len(clips)} x 10 s clips per step; reference FBank + blocked directconv "
+                "kernels compiled unmodified (oracle/_ref), restated ERes2Net glue, all host "
+                "threads")
+        audio, wall = cpu_port_ecapa(m, clips, threads)
+        return audio, wall, "port", (
+            f"{len(clips)} x 4 s clips per step; numpy restatement of src/encoder.cpp "
+            "(float32 BLAS matmuls) + oracle FBank, all host threads")
+
+    def config(self, world):
+        if self.name == "eres2net":
+            return eres_config(self.args, world)
+        return ecapa_config(self.args, world)
+
+
+def run_eres2net(args, family: str = "eres2net") -> int:
     """ERes2Net-base (m_channels 32, blocks 3/4/6/3, scale 2, AFF),
     f16 weights, a batch of `--eres-batch` 10 s clips (998 frames) per GPU and step.
+    family "ecapa": BASELINE config 3, ECAPA-TDNN (C 1024, scale 8, MFA 1536, 192-d),
+    f16, a batch of `--ecapa-batch` 4 s clips (398 frames) per GPU and step.
     N > 1 runs one such batch per rank and all-gathers the embeddings (weak)."""
     import torch
     import torch.distributed as dist
@@ -515,29 +585,27 @@ def run_eres2net(args) -> int:
     else:
         torch.cuda.set_device(0)
     dev = torch.device("cuda", local if world > 1 else 0)
+    fam = _Family(family, args)
     if args.impl == "reference":
         if rank == 0:
-            m = vd_synth.quantize_model_f16(vd_synth.eres2net_model(SEED))
-            pool = make_pool(4, 10.0)
+            m = fam.weights_as_loaded(fam.model())
+            pool = make_pool(max(4, fam.ref_clips), float(fam.seconds))
             threads = os.cpu_count() or 1
-            times, audio_tot = [], 0.0
+            times, audio_tot, kind, sample = [], 0.0, "", ""
             for s in range(args.warmup + args.steps):
-                audio, wall = cpu_reference_eres2net(m, pool[:args.ref_eres_clips], threads)
+                audio, wall, kind, sample = fam.cpu(m, pool[:fam.ref_clips], threads)
                 if s >= args.warmup:
                     times.append(wall)
                     audio_tot += audio
             value = audio_tot / sum(times)
             print(json.dumps({
-                "impl": "reference", "metric": ERES_METRIC, "value": value, "unit": UNIT,
+                "impl": "reference", "metric": fam.metric, "value": value, "unit": UNIT,
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": eres_config(args, world),
+                "config": fam.config(world),
                 "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
-                                 "kind": "reference",
-                                 "sample": f"{args.ref_eres_clips} x 10 s clips per step; "
-                                           "reference FBank + blocked directconv kernels "
-                                           "compiled unmodified, restated ERes2Net glue"},
+                                 "kind": kind, "sample": sample},
                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}), flush=True)
         if world > 1:
@@ -546,12 +614,12 @@ def run_eres2net(args) -> int:
         return 0
 
     tmp = tempfile.mkdtemp(prefix="vdbench_")
-    m = vd_synth.eres2net_model(SEED)
-    gguf = os.path.join(tmp, "eres2net_f16.gguf")
-    vd_synth.write_eres2net_gguf(gguf, m, "f16")
+    m = fam.model()
+    gguf = os.path.join(tmp, fam.gguf_name)
+    fam.write(gguf, m)
     model = vd_b200.Model(gguf)
-    B, n = args.eres_batch, 10 * SR
-    pool = make_pool(16, 10.0)
+    B, n = fam.batch, fam.seconds * SR
+    pool = make_pool(16, float(fam.seconds))
     host_pcm = np.concatenate([pool[(rank * B + i) % len(pool)] for i in range(B)])
     offs = np.arange(B, dtype=np.int64) * n
     lens = [n] * B
@@ -612,12 +680,12 @@ def run_eres2net(args) -> int:
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
     achieved = conv_flops / (conv_ms / 1e3) / 1e12 if conv_ms > 0 else 0.0
     result = {
-        "metric": ERES_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": fam.metric, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 (f32 accumulate)",
         "data": "synthetic (seeded harmonic+pink-noise clips, calibrated random weights)",
-        "config": eres_config(args, world),
+        "config": fam.config(world),
         "e2e": {"value": audio_step / float(e_t.item()), "unit": UNIT,
                 "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch"},
@@ -634,13 +702,10 @@ def run_eres2net(args) -> int:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        audio, wall = cpu_reference_eres2net(vd_synth.quantize_model_f16(m),
-                                             clips[:args.ref_eres_clips], threads)
-        result["cpu_baseline"] = {
-            "value": audio / wall, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"{args.ref_eres_clips} x 10 s clips of the same batch; reference FBank "
-                      "+ blocked directconv kernels compiled unmodified (oracle/_ref), "
-                      "restated ERes2Net glue, all host threads"}
+        audio, wall, kind, sample = fam.cpu(fam.weights_as_loaded(m), clips[:fam.ref_clips],
+                                            threads)
+        result["cpu_baseline"] = {"value": audio / wall, "unit": UNIT, "cores": threads,
+                                  "kind": kind, "sample": sample + " (clips of the same batch)"}
     if rank == 0:
         print(json.dumps(result), flush=True)
     model.close()
@@ -648,6 +713,15 @@ def run_eres2net(args) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def ecapa_config(args, world):
+    return {"workload": f"BASELINE config 3: ECAPA-TDNN f16 embed, batch {args.ecapa_batch} "
+                        "x 4 s clips (398 frames) per GPU",
+            "model": "ecapa_tdnn (C 1024, k5 stem, 3 SE-Res2 blocks k3 dil 2/3/4 scale 8, "
+                     "SE 128, MFA 1536, ASP att 128, 192-d; synthetic calibrated weights, f16)",
+            "global_batch": world * args.ecapa_batch, "seq_len": "4 s (398 frames)",
+            "parallelism": f"dp{world}", "l2_flush": "activations larger than L2"}
 
 
 def eres_config(args, world):
@@ -756,11 +830,17 @@ def main() -> int:
     ap.add_argument("--latency", action="store_true",
                     help="BASELINE config 0: single 3 s clip latency through the C ABI")
     ap.add_argument("--ref-eres-clips", type=int, default=8)
+    ap.add_argument("--ecapa", action="store_true",
+                    help="BASELINE config 3: ECAPA-TDNN f16, batch of 4 s clips")
+    ap.add_argument("--ecapa-batch", type=int, default=512)
+    ap.add_argument("--ref-ecapa-clips", type=int, default=32)
     args = ap.parse_args()
     if args.op_sweep:
         return run_sweep(args)
     if args.eres2net:
         return run_eres2net(args)
+    if args.ecapa:
+        return run_eres2net(args, "ecapa")
     if args.latency:
         return run_latency(args)
     if args.impl == "reference":

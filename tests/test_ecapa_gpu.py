@@ -240,3 +240,19 @@ def test_ecapa_q8_0_mfa(tmp_path_factory, cuda_lib):
         assert _cos(model.embed_pcm(pcm), _oracle(mq, pcm)) >= COS_TOL
     finally:
         model.close()
+
+
+def test_ecapa_profile_counts_convs(ecapa_f16):
+    """Profiling brackets every tensor-core conv of a bucket (stem, 3 x (tdnn1 + 7
+    Res2Net convs + tdnn2), MFA, the two attention convs) and leaves no error behind."""
+    _, model = ecapa_f16
+    clips = [vd_synth.clip_f32(vd_synth.make_clip(600 + i, 64000)) for i in range(4)]
+    model.profile(True)
+    model.profile_read()
+    model.embed_batch(clips)
+    ms, flops, n = model.profile_read()
+    stages = model.profile_stages()
+    model.profile(False)
+    assert n == 31 and ms > 0 and flops > 0
+    assert stages["conv"] > 0 and stages["pool"] > 0
+    assert model.embed_batch(clips).shape == (4, 192)

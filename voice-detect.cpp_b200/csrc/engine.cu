@@ -969,9 +969,9 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         return 1;
     }
     prof_end(pf, st, 0.0);
+    if (cfg_.arch == "ecapa_tdnn") return run_ecapa(B, t_max, tv_sum, st, d_out, launches, err);
     const int ps = prof_begin(st, 4);
     const bool eres = cfg_.arch == "eres2net";
-    if (cfg_.arch == "ecapa_tdnn") return run_ecapa(B, t_max, tv_sum, st, d_out, launches, err);
     if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
                      stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0], st)) {
         err = vdb_last_error();
@@ -1410,7 +1410,13 @@ int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_la
             return 1;
         }
         float ms = 0.0f;
-        cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]);
+        if (cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]) != cudaSuccess) {
+            cudaGetLastError();  // do not leave the error for an unrelated later check
+            err = "profile event pair " + std::to_string(i / 2) + " was not recorded";
+            prof_used_ = 0;
+            prof_flops_ = 0.0;
+            return 1;
+        }
         const int stg = prof_stage_[i / 2];
         stage_ms[stg] += ms;
         if (stg == 0) {
