@@ -94,6 +94,7 @@ struct ConvDev {
     int two_ring, ra, rb;
     uint32_t a_stride, b_stride, b_ring0;
     uint32_t bias_off, tv_off, bar_off;
+    uint32_t ss_off;         // act 3/4: bn_scale then bn_shift in shared memory (0: none)
     const float* bias;       // may be null (no bias)
     const __half* residual;
     const __half* residual2;
@@ -210,12 +211,15 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
 // TMEM (sum of the J partial accumulators) -> + bias [+ residual] -> ReLU / clamp
 // -> mask -> f16 store. The TMEM loads are warp-collective, so every lane executes
 // them whenever the tile is live.
+// `res` holds this chunk's residual when has_res, else its addend when add_in_res
+// (both prefetched one chunk ahead by epi_rows); sss is the shared-memory copy of
+// bn_scale (sss[0, oc)) and bn_shift (sss[oc, 2*oc)) for act 3/4.
 template <int NC, int J>
 __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri, int col,
-                                          uint32_t taddr, const float* sbias, bool has_res,
-                                          const uint4 (&res)[NC / 8], const __half* r2ptr,
-                                          __half* yrow, __half* y2row, __half* srow,
-                                          const __half* arow) {
+                                          uint32_t taddr, const float* sbias, const float* sss,
+                                          bool has_res, const uint4 (&res)[NC / 8],
+                                          const __half* r2ptr, __half* yrow, __half* y2row,
+                                          __half* srow, const __half* arow, bool add_in_res) {
     float f[NC];
 #pragma unroll
     for (int i = 0; i < NC; ++i) f[i] = 0.0f;
@@ -286,14 +290,14 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
             for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
         } else if (p.act >= 3) {
             // TDNN block: BatchNorm(ReLU(acc + bias [+ clip bias])), then tanh for act 4
-            const float4* sc = reinterpret_cast<const float4*>(p.bn_scale + col);
-            const float4* sh = reinterpret_cast<const float4*>(p.bn_shift + col);
+            const float4* sc = reinterpret_cast<const float4*>(sss + col);
+            const float4* sh = reinterpret_cast<const float4*>(sss + p.oc + col);
             const float4* cb = p.clip_bias ? reinterpret_cast<const float4*>(
                                                  p.clip_bias + (long long)ri.b * p.oc + col)
                                            : nullptr;
 #pragma unroll
             for (int j = 0; j < NC / 4; ++j) {
-                const float4 s4 = __ldg(sc + j), h4 = __ldg(sh + j);
+                const float4 s4 = sc[j], h4 = sh[j];
                 const float4 c4 = cb ? __ldg(cb + j) : make_float4(0.f, 0.f, 0.f, 0.f);
                 const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
                 const float hv[4] = {h4.x, h4.y, h4.z, h4.w};
@@ -364,7 +368,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         for (int j = 0; j < NC / 8; ++j) {
             uint4 o = make_uint4(0u, 0u, 0u, 0u);
             if (arow) {
-                const uint4 av = __ldg(reinterpret_cast<const uint4*>(arow) + j);
+                const uint4 av = add_in_res ? res[j] : __ldg(reinterpret_cast<const uint4*>(arow) + j);
                 const __half2* ho = reinterpret_cast<const __half2*>(&out[j]);
                 const __half2* ha = reinterpret_cast<const __half2*>(&av);
                 __half2* hs = reinterpret_cast<__half2*>(&o);
@@ -400,7 +404,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 template <int NC, int J>
 __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowInfo& ri, int m,
                                          int n0, int c_lo, int c_hi, uint32_t tbase,
-                                         const float* sbias) {
+                                         const float* sbias, const float* sss) {
     const bool has_res = p.residual != nullptr && ri.valid;
     const bool has_res2 = p.residual2 != nullptr && ri.valid;
     const __half* rrow = has_res ? p.residual + (long long)m * p.ldr + n0 : nullptr;
@@ -409,17 +413,20 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
     __half* y2row = (p.y2 && ri.in_range) ? p.y2 + ri.dst2 * p.oc + n0 : nullptr;
     __half* srow = (p.ysum && ri.in_range) ? p.ysum + (long long)m * p.ldsum + n0 : nullptr;
     const __half* arow = (p.ysum && ri.valid) ? p.addend + (long long)m * p.ldadd + n0 : nullptr;
+    // The prefetch registers carry the residual, or else the sum output's addend.
+    const bool add_in_res = !has_res && arow != nullptr;
+    const __half* prow = has_res ? rrow : (add_in_res ? arow : nullptr);
     uint4 res[NC / 8];
-    if (has_res) load_res<NC>(rrow + c_lo, res);
+    if (prow) load_res<NC>(prow + c_lo, res);
     for (int c = c_lo; c < c_hi; c += NC) {
         uint4 cur[NC / 8];
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
-        if (has_res && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
+        if (prow && c + NC < c_hi) load_res<NC>(prow + c + NC, res);
         epi_chunk<NC, J>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
-                         has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
+                         sss, has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
                          y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
-                         arow ? arow + c : nullptr);
+                         arow ? arow + c : nullptr, add_in_res);
     }
 }
 
@@ -501,6 +508,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const uint32_t S = p.n_stages;
     float* sbias = reinterpret_cast<float*>(smem + p.bias_off);
     int* stv = reinterpret_cast<int*>(smem + p.tv_off);
+    float* sss = p.ss_off ? reinterpret_cast<float*>(smem + p.ss_off) : nullptr;
     const uint32_t bar_full = base + p.bar_off;
     const uint32_t bar_empty = bar_full + 8 * S;
     const uint32_t bar_tfull = bar_empty + 8 * S;
@@ -513,6 +521,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int lane = threadIdx.x & 31;
 
     for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias ? p.bias[i] : 0.0f;
+    if (sss)
+        for (int i = threadIdx.x; i < p.oc; i += blockDim.x) {
+            sss[i] = p.bn_scale[i];
+            sss[p.oc + i] = p.bn_shift[i];
+        }
     for (int i = threadIdx.x; i < p.batch; i += blockDim.x) stv[i] = p.tvalid[i];
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -816,9 +829,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) +
                                        acc * acc_cols + (uint32_t)(mb * J * p.BN);
                 if ((c_hi - c_lo) % 32 == 0)
-                    epi_rows<32, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias);
+                    epi_rows<32, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
                 else
-                    epi_rows<16, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias);
+                    epi_rows<16, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
             }
             if (live) {
                 tc_fence_before();
@@ -1150,6 +1163,10 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // that keep the accumulators double-buffered, two pipeline stages in shared
     // memory and at least two tiles per SM.
     int BM = a->tile_m;
+    // 1-D convs with 256-column tiles: 128-row tiles keep two accumulators in TMEM so
+    // the epilogue of one tile overlaps the MMAs of the next (measured 10-20% faster
+    // on the ECAPA 1024- and 1536-channel convs than 256-row single-buffered tiles).
+    if (BM == 0 && seq) BM = BN > 128 ? 128 : 256;
     if (BM == 0) {
         BM = 256;
         if (halo && a->ksplit <= 1) {
@@ -1255,8 +1272,10 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     p.stage0 = off;
     p.a_region = (uint32_t)round_up((int)a_bytes, 1024);
     p.stage_bytes = p.a_region + (uint32_t)round_up((int)b_bytes, 1024);
+    const bool has_bn = seq && sq->bn_scale != nullptr;
+    const uint32_t ss_bytes = has_bn ? 2u * (uint32_t)round_up(a->oc * 4, 16) : 0u;
     const uint32_t tail = (uint32_t)round_up(a->oc * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
-                          8 * (2 * kMaxStages + 5) + 16;
+                          ss_bytes + 8 * (2 * kMaxStages + 5) + 16;
     const int budget = kSmemMax - 1024 - (int)off - (int)tail;
     p.two_ring = two_ring ? 1 : 0;
     if (two_ring) {
@@ -1290,6 +1309,8 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     off += (uint32_t)round_up(a->oc * 4, 16);
     p.tv_off = off;
     off += (uint32_t)round_up(a->batch * 4, 16);
+    p.ss_off = has_bn ? off : 0u;
+    off += ss_bytes;
     p.bar_off = (uint32_t)round_up((int)off, 8);
     off = p.bar_off + 8 * (2 * p.n_stages + 5) + 16;
     const size_t smem = (size_t)off + 1024;
