@@ -46,6 +46,7 @@ METRIC = "utterance-sec/sec ResNet34 embed"
 # workload at the same bucket sizes (see profiles/launches__bench_c4_512clips.md).
 CONV_DRAM_BYTES_PER_FLOP = 4.45e-3
 UNIT = "utterance-sec/sec"
+E2E_WARMUP = 2  # untimed public-API calls before the e2e timing (see run_b200)
 
 
 def log(*a):
@@ -367,7 +368,10 @@ def run_b200(args) -> int:
 
     # e2e through the public C ABI with host buffers (PCM in, embeddings out)
     clips = [host_pcm[offs[k]:offs[k] + lens[k]] for k in range(n_local)]
-    model.embed_batch(clips[:64])
+    # steady state: bucket shapes seen once per call are launched plainly on their
+    # first sight and captured as CUDA graphs on their second, so two warm-up calls
+    for _ in range(E2E_WARMUP):
+        model.embed_batch(clips)
     if world > 1:
         dist.barrier()
     e2e_times = []
@@ -395,7 +399,8 @@ def run_b200(args) -> int:
         "config": config_dict(args, world),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * total,
                 "d2h_bytes_per_step": 4 * n_local * model.dim,
-                "api": "voicedetect_capi_embed_pcm_batch"},
+                "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": E2E_WARMUP,
+                "timed_calls": args.e2e_steps},
         "gpu_launches": launches,  # our kernels only (the NCCL all-gather is not counted)
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -665,7 +670,8 @@ def run_eres2net(args, family: str = "eres2net") -> int:
     audio_step = world * B * n / SR
     value = audio_step * args.steps / (max_ms / 1e3)
     clips = [host_pcm[i * n:(i + 1) * n] for i in range(B)]
-    model.embed_batch(clips[:8])
+    # one warm-up call: its equal-shape buckets are launched, captured and replayed
+    model.embed_batch(clips)
     e2e_times = []
     for _ in range(args.e2e_steps):
         torch.cuda.synchronize()
@@ -688,7 +694,8 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         "config": fam.config(world),
         "e2e": {"value": audio_step / float(e_t.item()), "unit": UNIT,
                 "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
-                "api": "voicedetect_capi_embed_pcm_batch"},
+                "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": 1,
+                "timed_calls": args.e2e_steps},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

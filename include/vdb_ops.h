@@ -160,6 +160,10 @@ typedef struct vdb_conv1d_args {
     int* err;               /* device error word or NULL */
     int tile_m;             /* 0 auto, 128 or 256 */
     int tile_n;             /* 0 auto (oc split in <= 256-column tiles), else a divisor of oc */
+    int pair;               /* 1: two SMs (a cluster of 2, tcgen05 cta_group::2) share each
+                               256-row tile, each loading half of the tile's weight columns
+                               (oc tiles multiples of 32, tile_m 0 or 256); 0 / -1: one CTA
+                               per tile */
 } vdb_conv1d_args;
 
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);

@@ -62,10 +62,15 @@ CASES = {
 }
 
 
+@pytest.mark.parametrize("pair", [1, 0], ids=["pair", "single"])
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_conv1d_matches_torch(cuda_lib, name):
+def test_conv1d_matches_torch(cuda_lib, name, pair):
+    """pair 1: two-SM cta_group::2 tiles (where the tiling allows them), 0: one CTA
+    per tile."""
     import torch
     B, T, pad, ic, oc, k, dil, act, two_seg, use_cb, use_sum, y_f32, tm, tn = CASES[name]
+    if pair and tm not in (0, 256):
+        pytest.skip("a CTA pair computes 256-row tiles")
     vd = cuda_lib
     g = torch.Generator().manual_seed(hash(name) % 1000)
     tv = [T] + [max(pad + 1, T - 7 * i - 3) for i in range(1, B)]
@@ -113,7 +118,7 @@ def test_conv1d_matches_torch(cuda_lib, name):
     y = torch.zeros(rows, oc, dtype=torch.float32 if y_f32 else torch.float16, device=dev)
     vd.conv1d(xs, vd.pack_conv1d_weight(w).to(dev), b.to(dev), tvd, batch=B, t=T, pad=pad,
               oc=oc, k0=k, dil0=dil, act=act, y=y, y_f32=y_f32, reflect=not y_f32,
-              tile_m=tm, tile_n=tn, **kw)
+              tile_m=tm, tile_n=tn, pair=pair, **kw)
     torch.cuda.synchronize()
     ys = y.float().cpu().reshape(B, T + 2 * pad, oc)
     for i, t in enumerate(tv):
@@ -131,6 +136,18 @@ def test_conv1d_matches_torch(cuda_lib, name):
             assert torch.equal(ss[i, pad:pad + t], want), (name, i)
             for j in range(1, pad + 1):
                 assert torch.equal(ss[i, pad - j], ss[i, pad + j])
+
+
+def test_conv1d_pair_rejects_odd_tiles(cuda_lib):
+    import torch
+    vd = cuda_lib
+    dev = torch.device("cuda")
+    B, T, pad = 1, 20, 1
+    xs = torch.zeros(vd.lib().vdb_seq_rows(B, T, pad), 32, dtype=torch.float16, device=dev)
+    w = torch.zeros(48, 1, 32, dtype=torch.float16, device=dev)
+    tvd = torch.tensor([T], dtype=torch.int32, device=dev)
+    with pytest.raises(RuntimeError, match="pair"):
+        vd.conv1d(xs, w, None, tvd, batch=B, t=T, pad=pad, oc=48, pair=1)
 
 
 def test_conv1d_rejects_reach_beyond_pad(cuda_lib):

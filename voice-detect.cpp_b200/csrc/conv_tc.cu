@@ -465,7 +465,7 @@ __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_
 // TAP stage: one (tap, channel block) A tile and its weight tile, rotating over
 // JU = min(J, KS) partials. When this is the tile's first segment the host
 // guarantees J <= KS, so the first stage initialises every partial.
-template <int KS, int NMB, int J>
+template <int KS, int NMB, int J, bool PAIR>
 __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                           uint32_t rb16, uint64_t b_desc, uint32_t idesc,
                                           bool first) {
@@ -474,29 +474,41 @@ __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t
     for (int k = 0; k < KS; ++k) {
         const int j = k % JU;
 #pragma unroll
-        for (int mb = 0; mb < NMB; ++mb)
-            umma_f16(d_tile + (uint32_t)(mb * J + j) * bn, a_desc + (uint64_t)(mb * 128 * rb16) + 2 * k,
-                     b_desc + 2 * k, idesc, (first && k < JU) ? 0u : 1u);
+        for (int mb = 0; mb < NMB; ++mb) {
+            if constexpr (PAIR)
+                umma_f16_pair(d_tile + (uint32_t)(mb * J + j) * bn,
+                              a_desc + (uint64_t)(mb * 128 * rb16) + 2 * k, b_desc + 2 * k, idesc,
+                              (first && k < JU) ? 0u : 1u);
+            else
+                umma_f16(d_tile + (uint32_t)(mb * J + j) * bn,
+                         a_desc + (uint64_t)(mb * 128 * rb16) + 2 * k, b_desc + 2 * k, idesc,
+                         (first && k < JU) ? 0u : 1u);
+        }
     }
 }
 
-template <int NMB, int J>
+template <int NMB, int J, bool PAIR>
 __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
                                             uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
                                             uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
                                             bool first) {
-    if (halo) {
+    if (!PAIR && halo) {
         if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
         else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
         else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
     } else {
-        if (ks == 4) issue_tap<4, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
-        else if (ks == 2) issue_tap<2, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
-        else issue_tap<1, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        if (ks == 4) issue_tap<4, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else if (ks == 2) issue_tap<2, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else issue_tap<1, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
     }
 }
 
-template <int NMB, int J>
+// PAIR: the CTA is one half of a cta_group::2 pair (cluster of 2, TAP feeds only,
+// NMB = J = 1). The pair computes a 256-row tile: each CTA loads its own 128 A rows
+// and half of the tile's weight columns; the even CTA issues the pair MMAs and its
+// commits arrive in both CTAs; every load of the pair completes on the even CTA's
+// full barrier, and both CTAs' epilogue warps release the even CTA's accumulator.
+template <int NMB, int J, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -519,6 +531,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the MMA-issuing CTA
+    const int cta0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ncta = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias ? p.bias[i] : 0.0f;
     if (sss)
@@ -534,7 +549,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_tfull + 8 * a, 1);
-            mbar_init(bar_tempty + 8 * a, kEpiThreads);
+            mbar_init(bar_tempty + 8 * a, PAIR ? 2 * (kEpiThreads / 32) : kEpiThreads);
         }
         mbar_init(bar_bres, 1);
         *abort_flag = 0;
@@ -549,14 +564,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             tma_prefetch_desc(&tmB1);
         }
     }
-    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
+    if (warp == 1) {
+        if constexpr (PAIR) tmem_alloc_pair(smem_u32(tmem_slot), p.tmem_cols);
+        else tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
+    }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any signal
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     const int n_tiles = p.n_mt * p.n_nt;
-    const uint32_t idesc = umma_idesc_f16(kMB, p.BN);
+    const uint32_t idesc = umma_idesc_f16(PAIR ? 2 * kMB : kMB, p.BN);
     const uint32_t acc_cols = (uint32_t)(NMB * J * p.BN);
 
     if (warp == 0) {
@@ -634,10 +653,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         mbar_wait_drain(bar_full + 8 * i, i < (uint32_t)p.ra ? pa : pb, 20000000ull);
                 }
             }
-            for (int tile = blockIdx.x; tile < n_tiles && ok && !p.two_ring; tile += gridDim.x) {
+            for (int tile = cta0; tile < n_tiles && ok && !p.two_ring; tile += ncta) {
                 const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
                 const int m0 = mt * p.BM, n0 = nt * p.BN;
                 if (!tile_live(p, stv, m0)) continue;
+                // this CTA's A rows and weight rows (a pair splits both in halves)
+                [[maybe_unused]] const int am0 = m0 + (int)rank * kMB;
+                [[maybe_unused]] const int bn0 = n0 + (int)rank * (p.BN / 2);
                 for (int sg = 0; sg < p.n_seg && ok; ++sg) {
                     const SegDev& s = p.seg[sg];
                     const CUtensorMap* ta = sg ? &tmA1 : &tmA0;
@@ -651,6 +673,19 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         }
                         const uint32_t fb = bar_full + 8 * stage;
                         const uint32_t sa = base + p.stage0 + stage * p.stage_bytes;
+                        if constexpr (PAIR) {
+                            // both CTAs' bytes complete on the even CTA's barrier
+                            const uint32_t fl = mapa_shared(fb, 0);
+                            if (rank == 0) mbar_arrive_expect_tx(fb, 2 * s.bytes);
+                            const int tap = it / s.n_kb, kbi = it - tap * s.n_kb;
+                            tma_load_3d_pair(sa, ta, fl, kbi * s.kb, am0 + s.off[tap], s.plane[tap]);
+                            tma_load_2d_pair(sa + p.a_region, tb, fl, tap * s.ic + kbi * s.kb, bn0);
+                            if (++stage == S) {
+                                stage = 0;
+                                phase ^= 1;
+                            }
+                            continue;
+                        }
                         mbar_arrive_expect_tx(fb, s.bytes);
                         if (s.mode == SEG_HALO) {
                             const uint32_t box_bytes = (uint32_t)s.box_rows * s.kb * 2;
@@ -678,7 +713,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer ----------------
             uint32_t stage = 0, phase = 0;
             uint32_t acc = 0, acc_phase = 0;
@@ -687,7 +722,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             if (p.bres_bytes &&
                 !mbar_wait(bar_bres, 0, p.err, VDB_ERR_TIMEOUT_FULL, abort_flag))
                 ok = false;
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            for (int tile = cta0; tile < n_tiles && ok; tile += ncta) {
                 const int mt = tile / p.n_nt;
                 if (!tile_live(p, stv, mt * p.BM)) continue;
                 if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1, p.err,
@@ -735,7 +770,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                                  : 0ull);
                                 const uint64_t b_desc =
                                     umma_sdesc(base + p.b_ring0 + sb * p.b_stride, row_bytes);
-                                issue_stage<NMB, J>(false, ksteps, d_tile, (uint32_t)p.BN, a_desc,
+                                issue_stage<NMB, J, false>(false, ksteps, d_tile, (uint32_t)p.BN, a_desc,
                                                     wp_units, rb16, b_desc, b_tap_units, idesc,
                                                     first);
                                 first = false;
@@ -765,10 +800,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         const uint64_t a_desc = a_desc0 + (uint64_t)(stage * (p.stage_bytes >> 4));
                         const uint64_t b_desc = halo ? bres_desc + (uint64_t)(it * b_kb_units)
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
-                        issue_stage<NMB, J>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc, wp_units,
-                                            rb16, b_desc, b_tap_units, idesc, first);
+                        issue_stage<NMB, J, PAIR>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc,
+                                                  wp_units, rb16, b_desc, b_tap_units, idesc, first);
                         first = false;
-                        umma_commit(bar_empty + 8 * stage);
+                        if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
+                        else umma_commit(bar_empty + 8 * stage);
                         issued = true;
                         if (++stage == S) {
                             stage = 0;
@@ -777,7 +813,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                     }
                 }
                 if (!ok) break;
-                umma_commit(bar_tfull + 8 * acc);
+                if constexpr (PAIR) umma_commit_pair(bar_tfull + 8 * acc, 0x3);
+                else umma_commit(bar_tfull + 8 * acc);
                 if (p.n_acc == 2 && ++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
@@ -812,10 +849,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         const int c_lo = split ? half * (p.BN / 2) : 0;
         const int c_hi = mb_split ? p.BN : (split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0));
         uint32_t acc = 0, acc_phase = 0;
-        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        for (int tile = cta0; tile < n_tiles; tile += ncta) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
-            const int m0 = mt * p.BM, n0 = nt * p.BN;
-            const bool live = tile_live(p, stv, m0);
+            const int m0 = mt * p.BM + (int)rank * kMB, n0 = nt * p.BN;
+            const bool live = tile_live(p, stv, mt * p.BM);
             if (live) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag))
@@ -835,7 +872,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             }
             if (live) {
                 tc_fence_before();
-                mbar_arrive(bar_tempty + 8 * acc);
+                if constexpr (PAIR) {
+                    // one arrival per warp on the MMA-issuing CTA's barrier
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+                } else {
+                    mbar_arrive(bar_tempty + 8 * acc);
+                }
                 if (p.n_acc == 2 && ++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
@@ -847,11 +890,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     }
 
     tc_fence_before();
-    __syncthreads();
+    // A pair's MMAs read both CTAs' shared memory and write both TMEMs: neither CTA
+    // releases either until the whole pair is done.
+    if constexpr (PAIR) cluster_sync();
+    else __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, p.tmem_cols);
+        else tmem_dealloc(tmem_base, p.tmem_cols);
     }
 }
 
@@ -934,7 +981,7 @@ int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 // Extras of the 1-D sequence geometry (vdb_conv1d); nullptr for the 2-D grid.
 struct SeqArgs {
-    int pad, dil0, reflect, y_f32, tile_n;
+    int pad, dil0, reflect, y_f32, tile_n, pair;
     const float* clip_bias;
     const float* bn_scale;
     const float* bn_shift;
@@ -1031,7 +1078,7 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
     a.ldsum = c->ldsum;
     a.addend = c->addend;
     a.ldaddend = c->ldaddend;
-    SeqArgs sq{c->pad, c->dil0, c->reflect ? 1 : 0, c->y_f32 ? 1 : 0, c->tile_n,
+    SeqArgs sq{c->pad, c->dil0, c->reflect ? 1 : 0, c->y_f32 ? 1 : 0, c->tile_n, c->pair,
                c->clip_bias, c->bn_scale, c->bn_shift};
     return conv_impl(&a, &sq, stream);
 }
@@ -1222,10 +1269,25 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         set_error("vdb_conv: ksplit may not exceed the K-steps per stage (channel block / 16)");
         return 1;
     }
+    // CTA pairs (cta_group::2, 1-D convs): a 256-row tile per pair, each CTA loading
+    // its 128 rows and half the weight columns, so a CTA moves 1.5x fewer bytes per
+    // MMA than a 128 x BN tile of its own. Measured on the ECAPA shapes (B200, batch
+    // 512 x 398 frames) it only pays off for the 80-channel k=5 stem (16-channel K
+    // blocks: 528 -> 444 us); the 1024/1536-channel 1x1 convs run at the same speed
+    // and the 128-channel ones slower, so it is opt-in. sq->pair: 1 on, 0 / -1 off.
+    const bool pair = seq && sq->pair == 1 && !halo && !two_ring && J == 1 && BN % 32 == 0 &&
+                      (a->tile_m == 0 || a->tile_m == 256) && num_sms() >= 2;
+    if (seq && sq->pair == 1 && !pair) {
+        set_error("vdb_conv1d: a CTA pair needs oc tiles that are multiples of 32 and tile_m 0 or 256");
+        return 1;
+    }
+    if (pair) BM = 2 * kMB;
     p.BM = BM;
-    p.n_mblk = BM / kMB;
+    p.n_mblk = pair ? 1 : BM / kMB;
     p.J = J;
     p.n_acc = (2 * p.n_mblk * J * BN <= 512) ? 2 : 1;
+    const int cta_rows = pair ? kMB : BM;   // A rows one CTA loads per stage
+    const int cta_bn = pair ? BN / 2 : BN;  // weight rows one CTA loads per stage
     p.n_mt = (p.M + BM - 1) / BM;
 
     uint32_t off = 0;
@@ -1259,13 +1321,13 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             a_bytes = std::max(a_bytes, s.bytes);
         } else {
             s.mode = SEG_TAP;
-            s.n_box = (BM + 255) / 256;
-            s.box_rows = BM / s.n_box;
-            s.bytes = (uint32_t)(BM + BN) * row_bytes;
-            s.a_bytes = (uint32_t)BM * row_bytes;
-            s.b_bytes = (uint32_t)BN * row_bytes;
-            a_bytes = std::max(a_bytes, (uint32_t)BM * row_bytes);
-            b_bytes = std::max(b_bytes, (uint32_t)BN * row_bytes);
+            s.n_box = (cta_rows + 255) / 256;
+            s.box_rows = cta_rows / s.n_box;
+            s.bytes = (uint32_t)(cta_rows + cta_bn) * row_bytes;
+            s.a_bytes = (uint32_t)cta_rows * row_bytes;
+            s.b_bytes = (uint32_t)cta_bn * row_bytes;
+            a_bytes = std::max(a_bytes, (uint32_t)cta_rows * row_bytes);
+            b_bytes = std::max(b_bytes, (uint32_t)cta_bn * row_bytes);
         }
     }
     off = (uint32_t)round_up((int)off, 1024);
@@ -1371,7 +1433,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
         if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, (!seq && stride == 2) ? 4 : 1, s.kb,
                         box_rows) ||
-            !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, BN, s.kb)) {
+            !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, cta_bn, s.kb)) {
             set_error("vdb_conv: cuTensorMapEncodeTiled failed");
             return 1;
         }
@@ -1383,7 +1445,8 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // One CTA per SM: more than 256 TMEM columns, or most of shared memory.
     const size_t smem_launch = std::max<size_t>(smem, 120 * 1024);
     const int n_tiles = p.n_mt * p.n_nt;
-    const int grid = std::max(1, std::min(n_tiles, num_sms()));
+    const int grid = pair ? 2 * std::max(1, std::min(n_tiles, num_sms() / 2))
+                          : std::max(1, std::min(n_tiles, num_sms()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto launch = [&](auto kern) -> int {
         // The shared-memory opt-in. While a stream is being captured into a CUDA graph
@@ -1398,19 +1461,41 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         VDB_CHECK_CUDA(cudaGetLastError());
         return 0;
     };
+    if (pair) {
+        auto kern = conv_tc_kernel<1, 1, true>;
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
+        if (cs == cudaStreamCaptureStatusNone)
+            VDB_CHECK_CUDA(
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem_launch;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
+        return 0;
+    }
     const int key = p.n_mblk * 100 + J;
     switch (key) {
-        case 101: return launch(conv_tc_kernel<1, 1>);
-        case 102: return launch(conv_tc_kernel<1, 2>);
-        case 104: return launch(conv_tc_kernel<1, 4>);
-        case 108: return launch(conv_tc_kernel<1, 8>);
-        case 201: return launch(conv_tc_kernel<2, 1>);
-        case 202: return launch(conv_tc_kernel<2, 2>);
-        case 204: return launch(conv_tc_kernel<2, 4>);
-        case 208: return launch(conv_tc_kernel<2, 8>);
-        case 301: return launch(conv_tc_kernel<3, 1>);
-        case 401: return launch(conv_tc_kernel<4, 1>);
-        case 801: return launch(conv_tc_kernel<8, 1>);
+        case 101: return launch(conv_tc_kernel<1, 1, false>);
+        case 102: return launch(conv_tc_kernel<1, 2, false>);
+        case 104: return launch(conv_tc_kernel<1, 4, false>);
+        case 108: return launch(conv_tc_kernel<1, 8, false>);
+        case 201: return launch(conv_tc_kernel<2, 1, false>);
+        case 202: return launch(conv_tc_kernel<2, 2, false>);
+        case 204: return launch(conv_tc_kernel<2, 4, false>);
+        case 208: return launch(conv_tc_kernel<2, 8, false>);
+        case 301: return launch(conv_tc_kernel<3, 1, false>);
+        case 401: return launch(conv_tc_kernel<4, 1, false>);
+        case 801: return launch(conv_tc_kernel<8, 1, false>);
         default:
             set_error("vdb_conv: ksplit must be 1, 2, 4 or 8 (1 for tile_m above 256)");
             return 1;

@@ -7,8 +7,6 @@
 //                         SEQ layout with the reflect padding the k=5 stem reads
 //                         (src/encoder.cpp:32-50)
 //   seq_mean_kernel       SE squeeze: per-clip mean over time (src/encoder.cpp:200)
-//   small_fc_kernel       SE excite 1x1s (ReLU / sigmoid, :201-207) and the
-//                         attention's global-context term (see the ASP note below)
 //   se_apply_kernel       x * gate + block input (:208, :229)
 //   seq_meanstd_kernel    ASP global statistics mean / sqrt(clamp(var, eps)) (:261-264)
 //   asp_pool_kernel       softmax over time + attention-weighted mean / std (:280-285)
@@ -19,7 +17,7 @@
 // ASP note. The reference concatenates [x; mean; std] (3C channels) and runs the
 // attention TDNN's 1x1 conv over it (src/encoder.cpp:268-275). The mean / std
 // blocks are constant over time, so W * [x; m; s] = W_x * x + (W_m * m + W_s * s):
-// the second term is one [B, 2C] x [2C, att] product per clip (small_fc_kernel),
+// the second term is one [B, 2C] x [2C, att] product per clip (small_gemm_launch),
 // added as a per-clip bias in the tensor-core conv's epilogue before its ReLU.
 #include <cuda_fp16.h>
 
@@ -101,38 +99,6 @@ __global__ void seq_mean_kernel(const __half* __restrict__ x, int ldx,
         const int cc = blockIdx.y * 512 + k;
         if (cc < C && tvb > 0)
             out[(long long)b * C + cc] = (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb;
-    }
-}
-
-// out[b][n] = act(bias[n] + sum_k W[n][k] * in[b][k]); act 0 none, 1 ReLU,
-// 2 sigmoid. One warp per (n, 4 clips), lanes over k.
-__global__ void small_fc_kernel(const float* __restrict__ in, int ldin, int B, int K,
-                                const float* __restrict__ W, const float* __restrict__ bias, int N,
-                                int act, float* __restrict__ out, int ldout) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x * 8 + warp;
-    const int b0 = blockIdx.y * 4;
-    if (n >= N) return;
-    float acc[4] = {0, 0, 0, 0};
-    const float* w = W + (long long)n * K;
-    for (int k = lane; k < K; k += 32) {
-        const float wv = __ldg(w + k);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (b0 + j < B) acc[j] += wv * __ldg(in + (long long)(b0 + j) * ldin + k);
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
-    if (lane == 0) {
-        const float bv = bias ? bias[n] : 0.0f;
-        for (int j = 0; j < 4 && b0 + j < B; ++j) {
-            float v = acc[j] + bv;
-            if (act == 1) v = fmaxf(v, 0.0f);
-            else if (act == 2) v = 1.0f / (1.0f + expf(-v));
-            out[(long long)(b0 + j) * ldout + n] = v;
-        }
     }
 }
 
@@ -222,65 +188,75 @@ __global__ void seq_meanstd_kernel(const __half* __restrict__ x, int ldx,
 
 // Attentive statistics pooling of one clip's channels: a = softmax over the valid
 // frames of the logits, mu = sum a*x, sd = sqrt(max(sum a*(x - mu)^2, eps)).
-// Single pass per thread with the running maximum (online softmax) and a weighted
-// Welford update of mean and second moment, then a merge of the 4 time lanes.
-// Block (b, 64 channels): 64 channels x 4 time lanes.
-struct AspState {
-    float m, s, mu, m2;
+// One pass: each thread keeps, for its channels, the running maximum m of the
+// logits and S = sum w, A = sum w*d, Q = sum w*d^2 with w = exp(l - m) and
+// d = x - g, g the channel's global mean (the shift keeps Q/S - (A/S)^2 well
+// conditioned); a new maximum rescales S, A, Q by exp(m_old - m_new). Then
+// mu = g + A/S, var = Q/S - (A/S)^2. The four time lanes of a channel are merged
+// the same way. Block (b, 128 channels): 64 channel pairs x 4 time lanes.
+struct AspAcc {
+    float m, s, a, q;
 };
 
-__device__ __forceinline__ AspState asp_merge(const AspState& a, const AspState& b) {
-    if (b.s == 0.0f) return a;
-    if (a.s == 0.0f) return b;
-    const float m = fmaxf(a.m, b.m);
-    const float ea = expf(a.m - m), eb = expf(b.m - m);
-    const float sa = a.s * ea, sb = b.s * eb;
-    const float s = sa + sb;
-    const float d = b.mu - a.mu;
-    AspState r;
-    r.m = m;
-    r.s = s;
-    r.mu = a.mu + d * (sb / s);
-    r.m2 = a.m2 * ea + b.m2 * eb + d * d * (sa * sb / s);
-    return r;
+__device__ __forceinline__ void asp_update(AspAcc& st, float l, float d) {
+    if (l > st.m) {
+        const float r = __expf(st.m - l);  // 0 for the first frame (m = -inf)
+        st.s *= r;
+        st.a *= r;
+        st.q *= r;
+        st.m = l;
+    }
+    const float w = __expf(l - st.m);
+    st.s += w;
+    st.a = fmaf(w, d, st.a);
+    st.q = fmaf(w * d, d, st.q);
 }
 
-__global__ void asp_pool_kernel(const float* __restrict__ logits, int ldl,
-                                const __half* __restrict__ x, int ldx, const int* __restrict__ tv,
-                                int T, int pad, int C, float eps, float* __restrict__ pooled) {
-    __shared__ AspState st[4][64];
+__global__ void __launch_bounds__(256)
+asp_pool_kernel(const float* __restrict__ logits, int ldl, const __half* __restrict__ x, int ldx,
+                const float* __restrict__ stats, const int* __restrict__ tv, int T, int pad,
+                int C, float eps, float* __restrict__ pooled) {
+    __shared__ AspAcc sm[4][128];
     const int b = blockIdx.x;
-    const int cl = threadIdx.x & 63, ty = threadIdx.x >> 6;
-    const int c = blockIdx.y * 64 + cl;
+    const int cp = threadIdx.x & 63, ty = threadIdx.x >> 6;
+    const int c = blockIdx.y * 128 + 2 * cp;
     const int tvb = min(tv[b], T);
-    AspState a{-INFINITY, 0.0f, 0.0f, 0.0f};
+    AspAcc u{-INFINITY, 0.0f, 0.0f, 0.0f}, v{-INFINITY, 0.0f, 0.0f, 0.0f};
     if (c < C) {
+        const float g0 = stats[(long long)b * 2 * C + c], g1 = stats[(long long)b * 2 * C + c + 1];
         const long long row0 = (long long)b * (T + 2 * pad) + pad;
+#pragma unroll 4
         for (int t = ty; t < tvb; t += 4) {
-            const float l = __ldg(logits + (row0 + t) * ldl + c);
-            const float xv = __half2float(x[(row0 + t) * ldx + c]);
-            if (l > a.m) {
-                const float r = expf(a.m - l);
-                a.s *= r;
-                a.m2 *= r;
-                a.m = l;
-            }
-            const float w = expf(l - a.m);
-            a.s += w;
-            const float d = xv - a.mu;
-            a.mu += d * (w / a.s);
-            a.m2 += w * d * (xv - a.mu);
+            const float2 l = __ldg(reinterpret_cast<const float2*>(logits + (row0 + t) * ldl + c));
+            const float2 xv = __half22float2(
+                *reinterpret_cast<const __half2*>(x + (row0 + t) * ldx + c));
+            asp_update(u, l.x, xv.x - g0);
+            asp_update(v, l.y, xv.y - g1);
         }
     }
-    st[ty][cl] = a;
+    sm[ty][2 * cp] = u;
+    sm[ty][2 * cp + 1] = v;
     __syncthreads();
-    if (ty == 0 && c < C) {
-        AspState r = st[0][cl];
-        for (int k = 1; k < 4; ++k) r = asp_merge(r, st[k][cl]);
-        const float var = r.s > 0.0f ? r.m2 / r.s : 0.0f;
-        pooled[(long long)b * 2 * C + c] = r.mu;
-        pooled[(long long)b * 2 * C + C + c] = sqrtf(fmaxf(var, eps));
+    if (threadIdx.x >= 128) return;
+    const int cl = threadIdx.x, cc = blockIdx.y * 128 + cl;
+    if (cc >= C) return;
+    float m = -INFINITY;
+    for (int k = 0; k < 4; ++k)
+        if (sm[k][cl].s > 0.0f) m = fmaxf(m, sm[k][cl].m);
+    float S = 0.0f, A = 0.0f, Q = 0.0f;
+    for (int k = 0; k < 4; ++k) {
+        const AspAcc& e = sm[k][cl];
+        if (e.s <= 0.0f) continue;
+        const float r = __expf(e.m - m);
+        S += e.s * r;
+        A += e.a * r;
+        Q += e.q * r;
     }
+    const float g = stats[(long long)b * 2 * C + cc];
+    const float mean_d = S > 0.0f ? A / S : 0.0f;
+    const float var = S > 0.0f ? fmaxf(Q / S - mean_d * mean_d, 0.0f) : 0.0f;
+    pooled[(long long)b * 2 * C + cc] = g + mean_d;
+    pooled[(long long)b * 2 * C + C + cc] = sqrtf(fmaxf(var, eps));
 }
 
 }  // namespace
@@ -304,14 +280,6 @@ int ecapa_seq_mean(const __half* x, int ldx, const int* tv, int batch, int T, in
     return 0;
 }
 
-int ecapa_small_fc(const float* in, int ldin, int batch, int K, const float* W,
-                   const float* bias, int N, int act, float* out, int ldout, cudaStream_t st) {
-    const dim3 grid((unsigned)((N + 7) / 8), (unsigned)((batch + 3) / 4));
-    small_fc_kernel<<<grid, 256, 0, st>>>(in, ldin, batch, K, W, bias, N, act, out, ldout);
-    VDB_CHECK_CUDA(cudaGetLastError());
-    return 0;
-}
-
 int ecapa_se_apply(const __half* h, int ldh, const float* gate, const __half* res, int ldr,
                    const int* tv, int batch, int T, int pad, int C, __half* y, int ldy,
                    cudaStream_t st) {
@@ -331,10 +299,15 @@ int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int
     return 0;
 }
 
-int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const int* tv,
-                   int batch, int T, int pad, int C, float eps, float* pooled, cudaStream_t st) {
-    const dim3 grid((unsigned)batch, (unsigned)((C + 63) / 64));
-    asp_pool_kernel<<<grid, 256, 0, st>>>(logits, ldl, x, ldx, tv, T, pad, C, eps, pooled);
+int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const float* stats,
+                   const int* tv, int batch, int T, int pad, int C, float eps, float* pooled,
+                   cudaStream_t st) {
+    if (C % 2 != 0 || ldl % 2 != 0 || ldx % 2 != 0) {
+        set_error("ecapa: attentive pooling needs an even channel count and pitches");
+        return 1;
+    }
+    const dim3 grid((unsigned)batch, (unsigned)((C + 127) / 128));
+    asp_pool_kernel<<<grid, 256, 0, st>>>(logits, ldl, x, ldx, stats, tv, T, pad, C, eps, pooled);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }

@@ -165,6 +165,7 @@ private:
     int run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
                   float* d_out, long long& launches, std::string& err);
     size_t ecapa_ws_bytes(int B, int t_max) const;
+    size_t ecapa_gemm_scratch(int B) const;
     bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
     bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
     // f16 identity [c][c]: an identity shortcut added on the tensor cores as a 1x1

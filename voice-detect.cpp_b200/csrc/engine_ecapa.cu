@@ -278,6 +278,16 @@ bool Engine::load_ecapa(const Gguf& g, std::string& err) {
     return true;
 }
 
+// split-K partials of the per-clip FCs (SE squeeze / excite, attention context)
+size_t Engine::ecapa_gemm_scratch(int B) const {
+    const EcapaDev& E = ecapa_;
+    size_t n = small_gemm_scratch_floats(B, 2 * E.Cm, E.att);
+    for (const EcapaBlockDev& b : E.blocks)
+        n = std::max({n, small_gemm_scratch_floats(B, E.C, b.se),
+                      small_gemm_scratch_floats(B, b.se, E.C)});
+    return n;
+}
+
 size_t Engine::ecapa_ws_bytes(int B, int t_max) const {
     const EcapaDev& E = ecapa_;
     const size_t R = (size_t)vdb_seq_rows(B, t_max, E.pad);
@@ -297,6 +307,7 @@ size_t Engine::ecapa_ws_bytes(int B, int t_max) const {
     n += 2 * align256((size_t)B * E.C * f) + align256((size_t)B * se * f);  // SE
     n += 2 * align256((size_t)B * 2 * E.Cm * f) + align256((size_t)B * E.att * f);
     n += align256((size_t)pool_fc_splits(B, 2 * E.Cm, cfg_.emb_dim) * B * cfg_.emb_dim * f);
+    n += align256(ecapa_gemm_scratch(B) * f);
     return n;
 }
 
@@ -337,6 +348,7 @@ int Engine::run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cu
     float* cb = (float*)take((size_t)B * att * f);
     float* part = (float*)take((size_t)pool_fc_splits(B, 2 * Cm, cfg_.emb_dim) * B *
                                cfg_.emb_dim * f);
+    float* gpart = (float*)take(ecapa_gemm_scratch(B) * f);
 
     auto fail = [&]() -> int {
         err = vdb_last_error();
@@ -379,10 +391,13 @@ int Engine::run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cu
     if (ecapa_cmn_pack(feats_, tv, B, T, cfg_.n_mels, cfg_.cmn ? 1 : 0, P, x0, st)) return fail();
     prof_end(pc, st, 0.0);
     ++launches;
-    // block0
-    if (launch(conv(E.stem, x0, cfg_.n_mels, a0, C, 3, 0),
-               2.0 * C * cfg_.n_mels * E.stem.k * frames))
-        return 1;
+    // block0 (a CTA-pair tiling: its narrow K blocks make it feed-bound, and halving
+    // each CTA's weight loads measured ~16% faster)
+    {
+        vdb_conv1d_args a = conv(E.stem, x0, cfg_.n_mels, a0, C, 3, 0);
+        a.pair = 1;
+        if (launch(a, 2.0 * C * cfg_.n_mels * E.stem.k * frames)) return 1;
+    }
     const __half* in = a0;
     int ld_in = C;
     for (int bi = 0; bi < nb; ++bi) {
@@ -414,13 +429,13 @@ int Engine::run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cu
         // SE (:196-209) + residual (:229), written into the block's MFA input slice
         const int ps = prof_begin(st, 3);
         if (ecapa_seq_mean(hb, C, tv, B, T, P, C, se_s, st) ||
-            ecapa_small_fc(se_s, C, B, C, blk.se_w1, blk.se_b1, blk.se, 1, se_z, blk.se, st) ||
-            ecapa_small_fc(se_z, blk.se, B, blk.se, blk.se_w2, blk.se_b2, C, 2, se_g, C, st) ||
+            small_gemm_launch(se_s, B, C, blk.se_w1, blk.se, blk.se_b1, 1, se_z, gpart, st) ||
+            small_gemm_launch(se_z, B, blk.se, blk.se_w2, C, blk.se_b2, 2, se_g, gpart, st) ||
             ecapa_se_apply(hb, C, se_g, in, ld_in, tv, B, T, P, C, cat + (size_t)bi * C, nb * C,
                            st))
             return fail();
         prof_end(ps, st, 0.0);
-        launches += 4;
+        launches += 6;  // mean, 2 x (split-K GEMM + finish), apply
         in = cat + (size_t)bi * C;
         ld_in = nb * C;
     }
@@ -429,10 +444,10 @@ int Engine::run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cu
     // ASP (:246-285)
     const int pa = prof_begin(st, 2);
     if (ecapa_meanstd(mf, Cm, tv, B, T, P, Cm, kAspEps, stats, st) ||
-        ecapa_small_fc(stats, 2 * Cm, B, 2 * Cm, E.asp_ctx_w, E.asp_tdnn.b, att, 0, cb, att, st))
+        small_gemm_launch(stats, B, 2 * Cm, E.asp_ctx_w, att, E.asp_tdnn.b, 0, cb, gpart, st))
         return fail();
     prof_end(pa, st, 0.0);
-    launches += 2;
+    launches += 3;  // mean / std, split-K GEMM + finish
     {
         vdb_conv1d_args a = conv(E.asp_tdnn, mf, Cm, at, att, 4, 0);
         a.bias = nullptr;  // the conv bias is inside the per-clip context bias
@@ -445,7 +460,7 @@ int Engine::run_ecapa(int B, int t_max, const std::vector<long long>& tv_sum, cu
         if (launch(a, 2.0 * Cm * att * frames)) return 1;
     }
     const int pp = prof_begin(st, 2);
-    if (ecapa_asp_pool(lg, Cm, mf, Cm, tv, B, T, P, Cm, kAspEps, pooled, st)) return fail();
+    if (ecapa_asp_pool(lg, Cm, mf, Cm, stats, tv, B, T, P, Cm, kAspEps, pooled, st)) return fail();
     // head: fc (asp_bn folded) + host-side-equivalent L2 (:339-372)
     if (fc_embed_launch(pooled, B, 2 * Cm, E.fc_w, E.fc_b, nullptr, cfg_.emb_dim,
                         cfg_.l2 ? 1 : 0, meta_ + (size_t)levels_.size() * B, d_out, nullptr, part,

@@ -315,6 +315,42 @@ int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
     return 0;
 }
 
+namespace {
+
+// out[i] = act(sum of the split-K partials + bias[i % N]); act 0 none, 1 ReLU, 2 sigmoid.
+__global__ void bias_act_finish_kernel(const float* __restrict__ part, int n_split, long long BN,
+                                       int N, const float* __restrict__ bias, int act,
+                                       float* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= BN) return;
+    float v = 0.0f;
+    for (int sp = 0; sp < n_split; ++sp) v += part[(long long)sp * BN + i];
+    if (bias) v += bias[i % N];
+    if (act == 1) v = fmaxf(v, 0.0f);
+    else if (act == 2) v = 1.0f / (1.0f + expf(-v));
+    out[i] = v;
+}
+
+}  // namespace
+
+size_t small_gemm_scratch_floats(int batch, int K, int N) {
+    return (size_t)pool_fc_splits(batch, K, N) * batch * N;
+}
+
+int small_gemm_launch(const float* in, int batch, int K, const float* W, int N, const float* bias,
+                      int act, float* out, float* part, cudaStream_t stream) {
+    const int n_split = pool_fc_splits(batch, K, N);
+    const int k_per = ((K + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
+    const dim3 grid((batch + kFcBM - 1) / kFcBM, (N + kFcBN - 1) / kFcBN, (K + k_per - 1) / k_per);
+    fc_partial_kernel<<<grid, 256, 0, stream>>>(in, W, batch, N, K, k_per, part);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    const long long BN = (long long)batch * N;
+    bias_act_finish_kernel<<<(unsigned)((BN + 255) / 256), 256, 0, stream>>>(part, (int)grid.z, BN, N,
+                                                                             bias, act, out);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
 int pool_embed_launch(const void* x, const int* tvalid, int batch, int t, int f, int c,
                       const float* seg_w, const float* seg_b, const float* mean_vec, int emb_dim,
                       float var_eps, int l2, const int* out_rows, float* emb_out,

@@ -47,16 +47,21 @@ int ecapa_cmn_pack(const float* feats, const int* frames, int batch, int t_max, 
                    int cmn, int pad, __half* x, cudaStream_t st);
 int ecapa_seq_mean(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
                    float* out, cudaStream_t st);
-// out[b][n] = act(bias[n] + W[n] . in[b]); act 0 none, 1 ReLU, 2 sigmoid
-int ecapa_small_fc(const float* in, int ldin, int batch, int K, const float* W,
-                   const float* bias, int N, int act, float* out, int ldout, cudaStream_t st);
+// out[b][n] = act(bias[n] + W[n] . in[b]) for f32 in [batch][K], W [N][K], out [batch][N]
+// (dense); act 0 none, 1 ReLU, 2 sigmoid. A tiled split-K GEMM (the embedding FC's
+// kernel) plus a finish pass; `part` holds small_gemm_scratch_floats(batch, K, N).
+size_t small_gemm_scratch_floats(int batch, int K, int N);
+int small_gemm_launch(const float* in, int batch, int K, const float* W, int N, const float* bias,
+                      int act, float* out, float* part, cudaStream_t stream);
 int ecapa_se_apply(const __half* h, int ldh, const float* gate, const __half* res, int ldr,
                    const int* tv, int batch, int T, int pad, int C, __half* y, int ldy,
                    cudaStream_t st);
 int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
                   float eps, float* stats, cudaStream_t st);
-int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const int* tv,
-                   int batch, int T, int pad, int C, float eps, float* pooled, cudaStream_t st);
+// stats: [batch][2C] global mean | std of x (ecapa_meanstd), the shift of the moments
+int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const float* stats,
+                   const int* tv, int batch, int T, int pad, int C, float eps, float* pooled,
+                   cudaStream_t st);
 
 }  // namespace vdb
 

@@ -57,7 +57,7 @@ class Conv1dArgs(C.Structure):
         ("residual", C.c_void_p), ("ldr", C.c_int), ("tvalid", C.c_void_p), ("y", C.c_void_p),
         ("ldy", C.c_int), ("y_f32", C.c_int), ("reflect", C.c_int), ("ysum", C.c_void_p),
         ("ldsum", C.c_int), ("addend", C.c_void_p), ("ldaddend", C.c_int), ("err", C.c_void_p),
-        ("tile_m", C.c_int), ("tile_n", C.c_int),
+        ("tile_m", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int),
     ]
 
 
@@ -453,7 +453,7 @@ def pack_conv1d_weight(w):
 def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x1=None,
            w1=None, ic1=None, bn_scale=None, bn_shift=None, clip_bias=None, act=0, relu=False,
            residual=None, y=None, y_f32=False, reflect=False, ysum=None, addend=None, err=None,
-           stream=None, tile_m=0, tile_n=0):
+           stream=None, tile_m=0, tile_n=0, pair=0):
     """vdb_conv1d on device tensors: x0/x1/residual/y/ysum/addend are SEQ tensors
     (rows, C) or channel-slice views of wider ones; w0 f16 (OC, K, IC), w1 f16
     (OC, IC1); bias / bn_scale / bn_shift f32 (OC,); clip_bias f32 (B, OC).
@@ -473,7 +473,8 @@ def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x
                    act=int(act), relu=int(relu), residual=_ptr(residual), ldr=_ld(residual),
                    tvalid=tvalid.data_ptr(), y=y.data_ptr(), ldy=_ld(y), y_f32=int(y_f32),
                    reflect=int(reflect), ysum=_ptr(ysum), ldsum=_ld(ysum), addend=_ptr(addend),
-                   ldaddend=_ld(addend), err=_ptr(err), tile_m=tile_m, tile_n=tile_n)
+                   ldaddend=_ld(addend), err=_ptr(err), tile_m=tile_m, tile_n=tile_n,
+                   pair=pair)
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv1d(C.byref(a), C.c_void_p(s)), "vdb_conv1d")
     return y
