@@ -139,6 +139,7 @@ __device__ __forceinline__ int fdiv(int n, uint32_t mul, int sh) {
 // True when rows [m0, m0+BM) contain at least one pixel inside a clip's valid
 // time range (conservative: border columns of those rows count). Every role
 // evaluates it identically, so skipped tiles never touch the pipeline.
+template <bool SEQ>
 __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m0) {
     const int img = p.Hp * p.Wp;
     const int mend = min(m0 + p.BM, p.M);
@@ -147,8 +148,8 @@ __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m
         const int r1 = min(mend - b * img, img);
         const int t = tv[b];
         if (t <= 0) continue;
-        const int lo = p.seq ? p.pad : p.Wp + 1;
-        const int hi = p.seq ? p.pad + t : p.Wp * t + p.F + 1;
+        const int lo = SEQ ? p.pad : p.Wp + 1;
+        const int hi = SEQ ? p.pad + t : p.Wp * t + p.F + 1;
         if (r0 < hi && r1 > lo) return true;
     }
     return false;
@@ -166,11 +167,12 @@ struct RowInfo {
     long long refl[2];  // 1-D reflect: padding rows mirroring this row, or -1
 };
 
+template <bool SEQ>
 __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int m, bool live) {
     RowInfo ri{false, false, (long long)m, 0, 0, {-1, -1}};
     if (m >= p.M) return ri;
     ri.in_range = true;
-    if (p.seq) {
+    if constexpr (SEQ) {
         const int b = fdiv(m, p.img_mul, p.img_sh);
         const int t = m - b * p.Hp - p.pad;
         const int tvb = min(tv[b], p.T);  // a length past the slot never writes outside it
@@ -214,7 +216,7 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
 // `res` holds this chunk's residual when has_res, else its addend when add_in_res
 // (both prefetched one chunk ahead by epi_rows); sss is the shared-memory copy of
 // bn_scale (sss[0, oc)) and bn_shift (sss[oc, 2*oc)) for act 3/4.
-template <int NC, int J>
+template <int NC, int J, bool SEQ>
 __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri, int col,
                                           uint32_t taddr, const float* sbias, const float* sss,
                                           bool has_res, const uint4 (&res)[NC / 8],
@@ -251,7 +253,9 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         }
     }
     if (!ri.in_range) return;
-    if (p.seq && !ri.valid) return;  // 1-D: padding rows hold reflections (or nothing used)
+    if constexpr (SEQ) {
+        if (!ri.valid) return;  // 1-D: padding rows hold reflections (or nothing used)
+    }
     if (sbias) {
 #pragma unroll
         for (int i = 0; i < NC; ++i) f[i] += sbias[i];
@@ -288,7 +292,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         if (p.act == 1) {
 #pragma unroll
             for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
-        } else if (p.act >= 3) {
+        } else if (SEQ && p.act >= 3) {
             // TDNN block: BatchNorm(ReLU(acc + bias [+ clip bias])), then tanh for act 4
             const float4* sc = reinterpret_cast<const float4*>(sss + col);
             const float4* sh = reinterpret_cast<const float4*>(sss + p.oc + col);
@@ -311,7 +315,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
             }
         }
     }
-    if (p.y_f32) {
+    if (SEQ && p.y_f32) {
         // f32 output (1-D geometry; no sum output): optional ReLU, valid rows only
         if (p.relu) {
 #pragma unroll
@@ -382,7 +386,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
             sp[j] = o;
         }
     }
-    if (p.seq && p.reflect) {
+    if (SEQ && p.reflect) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             if (ri.refl[k] < 0) continue;
@@ -401,7 +405,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 // Epilogue of one (tile, row block) for this thread: columns [c_lo, c_hi) of the
 // tile in chunks of NC, with the residual of the next chunk loaded before the
 // current one is finished.
-template <int NC, int J>
+template <int NC, int J, bool SEQ>
 __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowInfo& ri, int m,
                                          int n0, int c_lo, int c_hi, uint32_t tbase,
                                          const float* sbias, const float* sss) {
@@ -423,7 +427,7 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
         if (prow && c + NC < c_hi) load_res<NC>(prow + c + NC, res);
-        epi_chunk<NC, J>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
+        epi_chunk<NC, J, SEQ>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
                          sss, has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
                          y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
                          arow ? arow + c : nullptr, add_in_res);
@@ -503,12 +507,24 @@ __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, 
     }
 }
 
+// Persistent tile loop bounds. Read from the special registers at each loop rather
+// than held in kernel-lifetime variables: keeping them live across the roles cost
+// the epilogue-bound 2-D convs up to 15% (register pressure in the epilogue).
+template <bool PAIR>
+__device__ __forceinline__ int first_tile() {
+    return PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+}
+template <bool PAIR>
+__device__ __forceinline__ int tile_stride() {
+    return PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+}
+
 // PAIR: the CTA is one half of a cta_group::2 pair (cluster of 2, TAP feeds only,
 // NMB = J = 1). The pair computes a 256-row tile: each CTA loads its own 128 A rows
 // and half of the tile's weight columns; the even CTA issues the pair MMAs and its
 // commits arrive in both CTAs; every load of the pair completes on the even CTA's
 // full barrier, and both CTAs' epilogue warps release the even CTA's accumulator.
-template <int NMB, int J, bool PAIR>
+template <int NMB, int J, bool PAIR, bool SEQ>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -520,7 +536,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const uint32_t S = p.n_stages;
     float* sbias = reinterpret_cast<float*>(smem + p.bias_off);
     int* stv = reinterpret_cast<int*>(smem + p.tv_off);
-    float* sss = p.ss_off ? reinterpret_cast<float*>(smem + p.ss_off) : nullptr;
+    float* sss = (SEQ && p.ss_off) ? reinterpret_cast<float*>(smem + p.ss_off) : nullptr;
     const uint32_t bar_full = base + p.bar_off;
     const uint32_t bar_empty = bar_full + 8 * S;
     const uint32_t bar_tfull = bar_empty + 8 * S;
@@ -532,8 +548,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the MMA-issuing CTA
-    const int cta0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int ncta = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias ? p.bias[i] : 0.0f;
     if (sss)
@@ -604,7 +618,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                     const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
                     const int m0 = mt * p.BM, n0 = nt * p.BN;
-                    if (!tile_live(p, stv, m0)) continue;
+                    if (!tile_live<SEQ>(p, stv, m0)) continue;
                     for (int sg = 0; sg < p.n_seg && ok; ++sg) {
                         const SegDev& s = p.seg[sg];
                         const CUtensorMap* ta = sg ? &tmA1 : &tmA0;
@@ -653,10 +667,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         mbar_wait_drain(bar_full + 8 * i, i < (uint32_t)p.ra ? pa : pb, 20000000ull);
                 }
             }
-            for (int tile = cta0; tile < n_tiles && ok && !p.two_ring; tile += ncta) {
+            for (int tile = first_tile<PAIR>(); tile < n_tiles && ok && !p.two_ring; tile += tile_stride<PAIR>()) {
                 const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
                 const int m0 = mt * p.BM, n0 = nt * p.BN;
-                if (!tile_live(p, stv, m0)) continue;
+                if (!tile_live<SEQ>(p, stv, m0)) continue;
                 // this CTA's A rows and weight rows (a pair splits both in halves)
                 [[maybe_unused]] const int am0 = m0 + (int)rank * kMB;
                 [[maybe_unused]] const int bn0 = n0 + (int)rank * (p.BN / 2);
@@ -722,9 +736,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             if (p.bres_bytes &&
                 !mbar_wait(bar_bres, 0, p.err, VDB_ERR_TIMEOUT_FULL, abort_flag))
                 ok = false;
-            for (int tile = cta0; tile < n_tiles && ok; tile += ncta) {
+            for (int tile = first_tile<PAIR>(); tile < n_tiles && ok; tile += tile_stride<PAIR>()) {
                 const int mt = tile / p.n_nt;
-                if (!tile_live(p, stv, mt * p.BM)) continue;
+                if (!tile_live<SEQ>(p, stv, mt * p.BM)) continue;
                 if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1, p.err,
                                VDB_ERR_TIMEOUT_TEMPTY, abort_flag)) {
                     ok = false;
@@ -849,10 +863,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         const int c_lo = split ? half * (p.BN / 2) : 0;
         const int c_hi = mb_split ? p.BN : (split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0));
         uint32_t acc = 0, acc_phase = 0;
-        for (int tile = cta0; tile < n_tiles; tile += ncta) {
+        for (int tile = first_tile<PAIR>(); tile < n_tiles; tile += tile_stride<PAIR>()) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
             const int m0 = mt * p.BM + (int)rank * kMB, n0 = nt * p.BN;
-            const bool live = tile_live(p, stv, mt * p.BM);
+            const bool live = tile_live<SEQ>(p, stv, mt * p.BM);
             if (live) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag))
@@ -862,13 +876,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             for (int mb = 0; mb < NMB; ++mb) {
                 if (mb_split && (mb & 1) != half) continue;
                 const int m = m0 + mb * kMB + quad * 32 + lane;
-                const RowInfo ri = row_info(p, stv, m, live);
                 const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) +
                                        acc * acc_cols + (uint32_t)(mb * J * p.BN);
+                const RowInfo ri = row_info<SEQ>(p, stv, m, live);
                 if ((c_hi - c_lo) % 32 == 0)
-                    epi_rows<32, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<32, J, SEQ>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
                 else
-                    epi_rows<16, J>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<16, J, SEQ>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
             }
             if (live) {
                 tc_fence_before();
@@ -1462,7 +1476,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         return 0;
     };
     if (pair) {
-        auto kern = conv_tc_kernel<1, 1, true>;
+        auto kern = conv_tc_kernel<1, 1, true, true>;
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
         if (cs == cudaStreamCaptureStatusNone)
@@ -1483,19 +1497,27 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
         return 0;
     }
+    if (seq) {
+        if (J != 1 || p.n_mblk > 2) {
+            set_error("vdb_conv1d: 1-D tiles are 128 or 256 rows with one accumulator");
+            return 1;
+        }
+        return p.n_mblk == 2 ? launch(conv_tc_kernel<2, 1, false, true>)
+                             : launch(conv_tc_kernel<1, 1, false, true>);
+    }
     const int key = p.n_mblk * 100 + J;
     switch (key) {
-        case 101: return launch(conv_tc_kernel<1, 1, false>);
-        case 102: return launch(conv_tc_kernel<1, 2, false>);
-        case 104: return launch(conv_tc_kernel<1, 4, false>);
-        case 108: return launch(conv_tc_kernel<1, 8, false>);
-        case 201: return launch(conv_tc_kernel<2, 1, false>);
-        case 202: return launch(conv_tc_kernel<2, 2, false>);
-        case 204: return launch(conv_tc_kernel<2, 4, false>);
-        case 208: return launch(conv_tc_kernel<2, 8, false>);
-        case 301: return launch(conv_tc_kernel<3, 1, false>);
-        case 401: return launch(conv_tc_kernel<4, 1, false>);
-        case 801: return launch(conv_tc_kernel<8, 1, false>);
+        case 101: return launch(conv_tc_kernel<1, 1, false, false>);
+        case 102: return launch(conv_tc_kernel<1, 2, false, false>);
+        case 104: return launch(conv_tc_kernel<1, 4, false, false>);
+        case 108: return launch(conv_tc_kernel<1, 8, false, false>);
+        case 201: return launch(conv_tc_kernel<2, 1, false, false>);
+        case 202: return launch(conv_tc_kernel<2, 2, false, false>);
+        case 204: return launch(conv_tc_kernel<2, 4, false, false>);
+        case 208: return launch(conv_tc_kernel<2, 8, false, false>);
+        case 301: return launch(conv_tc_kernel<3, 1, false, false>);
+        case 401: return launch(conv_tc_kernel<4, 1, false, false>);
+        case 801: return launch(conv_tc_kernel<8, 1, false, false>);
         default:
             set_error("vdb_conv: ksplit must be 1, 2, 4 or 8 (1 for tile_m above 256)");
             return 1;
