@@ -193,57 +193,64 @@ tstp_kernel(const __half* __restrict__ x, const int* __restrict__ tvalid, int T,
 }
 
 // Embedding FC over a bucket as a split-K f32 GEMM: part[s][b][j] = sum over the
-// s-th K range of pooled[b][k] * W[j][k]. 32 clips x 64 outputs per CTA, K tiles
-// of 32 staged in shared memory, 8 outputs per thread. Each weight tile is read
-// once per 32 clips instead of once per clip.
-constexpr int kFcBM = 32, kFcBN = 64, kFcBK = 32;
+// s-th K range of pooled[b][k] * W[j][k]. 64 clips x 64 outputs per CTA, K tiles
+// of 16 staged k-major in shared memory with float4 global loads, 4 x 4 outputs per
+// thread read as two float4s per k (16 FMAs per 2 shared loads). Each weight tile
+// is read once per 64 clips instead of once per clip. K must be a multiple of 4
+// (16-byte rows); k_per_split a multiple of kFcBK.
+constexpr int kFcBM = 64, kFcBN = 64, kFcBK = 16;
 
 __global__ void __launch_bounds__(256)
 fc_partial_kernel(const float* __restrict__ pooled, const float* __restrict__ W, int B, int D,
                   int P, int k_per_split, float* __restrict__ part) {
-    __shared__ float As[kFcBK][kFcBM + 1];
-    __shared__ float Ws[kFcBK][kFcBN + 1];
+    __shared__ __align__(16) float As[kFcBK][kFcBM + 4];
+    __shared__ __align__(16) float Ws[kFcBK][kFcBN + 4];
     const int b0 = blockIdx.x * kFcBM, j0 = blockIdx.y * kFcBN;
     const int k_lo = blockIdx.z * k_per_split, k_hi = min(P, k_lo + k_per_split);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads
-    float acc[2][4];
+    const int lr = threadIdx.x >> 2, lk = (threadIdx.x & 3) * 4;  // loader: row, k quad
+    float acc[4][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
     for (int k0 = k_lo; k0 < k_hi; k0 += kFcBK) {
-        // A tile: 32 clips x 32 k (4 per thread); W tile: 64 outputs x 32 k (8 per thread)
-        for (int e = threadIdx.x; e < kFcBM * kFcBK; e += 256) {
-            const int r = e / kFcBK, k = e % kFcBK;
-            const int bb = b0 + r, kk = k0 + k;
-            As[k][r] = (bb < B && kk < k_hi) ? pooled[(long long)bb * P + kk] : 0.0f;
-        }
-        for (int e = threadIdx.x; e < kFcBN * kFcBK; e += 256) {
-            const int r = e / kFcBK, k = e % kFcBK;
-            const int jj = j0 + r, kk = k0 + k;
-            Ws[k][r] = (jj < D && kk < k_hi) ? W[(long long)jj * P + kk] : 0.0f;
-        }
+        const int kk = k0 + lk;  // k_hi - k0 is a multiple of 4, so a quad is all in or out
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), w = a;
+        if (b0 + lr < B && kk < k_hi)
+            a = __ldg(reinterpret_cast<const float4*>(pooled + (long long)(b0 + lr) * P + kk));
+        if (j0 + lr < D && kk < k_hi)
+            w = __ldg(reinterpret_cast<const float4*>(W + (long long)(j0 + lr) * P + kk));
+        As[lk][lr] = a.x;
+        As[lk + 1][lr] = a.y;
+        As[lk + 2][lr] = a.z;
+        As[lk + 3][lr] = a.w;
+        Ws[lk][lr] = w.x;
+        Ws[lk + 1][lr] = w.y;
+        Ws[lk + 2][lr] = w.z;
+        Ws[lk + 3][lr] = w.w;
         __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < kFcBK; ++k) {
-            const float a0 = As[k][ty], a1 = As[k][ty + 16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float w = Ws[k][tx + 16 * j];
-                acc[0][j] = fmaf(a0, w, acc[0][j]);
-                acc[1][j] = fmaf(a1, w, acc[1][j]);
-            }
+        for (int k = 0; k < kFcBK; ++k) {
+            const float4 av = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
+            const float a4[4] = {av.x, av.y, av.z, av.w};
+            const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a4[i], w4[j], acc[i][j]);
         }
         __syncthreads();
     }
     float* out = part + (long long)blockIdx.z * B * D;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int bb = b0 + ty + 16 * i;
+    for (int i = 0; i < 4; ++i) {
+        const int bb = b0 + ty * 4 + i;
         if (bb >= B) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int jj = j0 + tx + 16 * j;
+            const int jj = j0 + tx * 4 + j;
             if (jj < D) out[(long long)bb * D + jj] = acc[i][j];
         }
     }
@@ -295,6 +302,16 @@ int pool_fc_splits(int batch, int P, int emb_dim) {
     return n;
 }
 
+namespace {
+bool fc_shape_ok(int K) {
+    if (K % 4 != 0) {
+        set_error("FC: the input length must be a multiple of 4");
+        return false;
+    }
+    return true;
+}
+}  // namespace
+
 int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
                     const float* seg_b, const float* mean_vec, int emb_dim, int l2,
                     const int* out_rows, float* emb_out, float* prenorm_out, float* part,
@@ -303,6 +320,7 @@ int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
         set_error("vdb_pool_embed: embedding too large");
         return 1;
     }
+    if (!fc_shape_ok(P)) return 1;
     const int n_split = pool_fc_splits(batch, P, emb_dim);
     const int k_per = ((P + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
     const dim3 grid((batch + kFcBM - 1) / kFcBM, (emb_dim + kFcBN - 1) / kFcBN,
@@ -339,6 +357,7 @@ size_t small_gemm_scratch_floats(int batch, int K, int N) {
 
 int small_gemm_launch(const float* in, int batch, int K, const float* W, int N, const float* bias,
                       int act, float* out, float* part, cudaStream_t stream) {
+    if (!fc_shape_ok(K)) return 1;
     const int n_split = pool_fc_splits(batch, K, N);
     const int k_per = ((K + n_split - 1) / n_split + kFcBK - 1) / kFcBK * kFcBK;
     const dim3 grid((batch + kFcBM - 1) / kFcBM, (N + kFcBN - 1) / kFcBN, (K + k_per - 1) / k_per);
