@@ -58,6 +58,26 @@ def make_pool(n: int = POOL, seconds: float = 20.0) -> list[np.ndarray]:
     return [vd_synth.clip_f32(vd_synth.make_clip(SEED + i, n_s)) for i in range(n)]
 
 
+def timed_calls(call, warmup: int, steps: int, dev, world: int) -> float:
+    """Mean wall seconds of `steps` calls after `warmup` untimed ones (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        call()
+    if world > 1:
+        dist.barrier()
+    ts = []
+    for _ in range(steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        call()
+        ts.append(time.perf_counter() - t0)
+    t = torch.tensor([sum(ts) / len(ts)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def global_lengths(world: int, per_gpu: int) -> np.ndarray:
     return vd_synth.clip_lengths(SEED, world * per_gpu, 2.0, 20.0)
 
@@ -370,20 +390,17 @@ def run_b200(args) -> int:
     clips = [host_pcm[offs[k]:offs[k] + lens[k]] for k in range(n_local)]
     # steady state: bucket shapes seen once per call are launched plainly on their
     # first sight and captured as CUDA graphs on their second, so two warm-up calls
-    for _ in range(E2E_WARMUP):
-        model.embed_batch(clips)
-    if world > 1:
-        dist.barrier()
-    e2e_times = []
-    for _ in range(args.e2e_steps):
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        model.embed_batch(clips)
-        e2e_times.append(time.perf_counter() - t0)
-    e_t = torch.tensor([sum(e2e_times) / len(e2e_times)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
-    e2e_value = float(tot_audio.item()) / float(e_t.item())
+    e_sec = timed_calls(lambda: model.embed_batch(clips), E2E_WARMUP, args.e2e_steps, dev, world)
+    e2e_value = float(tot_audio.item()) / e_sec
+    # the same shard as int16 (the generator's samples; f32 = int16 / 32768 exactly)
+    # through voicedetect_b200_embed_s16_batch: half the PCIe bytes, converted on the GPU
+    clips16 = [np.round(c * 32768.0).astype(np.int16) for c in clips]
+    s_sec = timed_calls(lambda: model.embed_batch_s16(clips16), E2E_WARMUP, args.e2e_steps, dev,
+                        world)
+    e2e_s16 = {"value": float(tot_audio.item()) / s_sec, "unit": UNIT,
+               "h2d_bytes_per_step": 2 * total, "d2h_bytes_per_step": 4 * n_local * model.dim,
+               "api": "voicedetect_b200_embed_s16_batch", "warmup_calls": E2E_WARMUP,
+               "timed_calls": args.e2e_steps}
 
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -401,6 +418,7 @@ def run_b200(args) -> int:
                 "d2h_bytes_per_step": 4 * n_local * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": E2E_WARMUP,
                 "timed_calls": args.e2e_steps},
+        "e2e_s16": e2e_s16,
         "gpu_launches": launches,  # our kernels only (the NCCL all-gather is not counted)
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -671,16 +689,9 @@ def run_eres2net(args, family: str = "eres2net") -> int:
     value = audio_step * args.steps / (max_ms / 1e3)
     clips = [host_pcm[i * n:(i + 1) * n] for i in range(B)]
     # one warm-up call: its equal-shape buckets are launched, captured and replayed
-    model.embed_batch(clips)
-    e2e_times = []
-    for _ in range(args.e2e_steps):
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        model.embed_batch(clips)
-        e2e_times.append(time.perf_counter() - t0)
-    e_t = torch.tensor([sum(e2e_times) / len(e2e_times)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e_sec = timed_calls(lambda: model.embed_batch(clips), 1, args.e2e_steps, dev, world)
+    clips16 = [np.round(c * 32768.0).astype(np.int16) for c in clips]
+    s_sec = timed_calls(lambda: model.embed_batch_s16(clips16), 1, args.e2e_steps, dev, world)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
@@ -692,10 +703,14 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         "dtype": "f16 (f32 accumulate)",
         "data": "synthetic (seeded harmonic+pink-noise clips, calibrated random weights)",
         "config": fam.config(world),
-        "e2e": {"value": audio_step / float(e_t.item()), "unit": UNIT,
+        "e2e": {"value": audio_step / e_sec, "unit": UNIT,
                 "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": 1,
                 "timed_calls": args.e2e_steps},
+        "e2e_s16": {"value": audio_step / s_sec, "unit": UNIT,
+                    "h2d_bytes_per_step": 2 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
+                    "api": "voicedetect_b200_embed_s16_batch", "warmup_calls": 1,
+                    "timed_calls": args.e2e_steps},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

@@ -168,6 +168,19 @@ typedef struct vdb_conv1d_args {
 
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);
 
+/* ---- Audio ingest ----------------------------------------------------------------
+ * Device-side replacement for the reference's host audio path (drwav's int16 -> f32
+ * scaling and vd::resample_linear, src/audio_io.cpp:9-23): `batch` mono clips, clip b
+ * at element offset in_off[b] of `in` with n_in[b] samples at in_sr Hz (in_type 0: f32,
+ * 1: int16 scaled by 2^-15), written as n_out[b] = vdb_resampled_length(n_in[b], in_sr,
+ * out_sr) f32 samples at out_sr Hz to out + out_off[b]. Linear interpolation with the
+ * reference's exact arithmetic (bitwise equal to the host computation). in_off, n_in,
+ * out_off, n_out: device arrays; max_out >= every n_out[b]. */
+long long vdb_resampled_length(long long n_in, int in_sr, int out_sr);
+int vdb_pcm_ingest(const void* in, int in_type, const long long* in_off, const int* n_in,
+                   int batch, int in_sr, int out_sr, const long long* out_off, const int* n_out,
+                   int max_out, float* out, void* stream);
+
 /* ---- FBank ----------------------------------------------------------------------
  * A plan holds the device tables of one FBank configuration (the GGUF
  * voicedetect.fbank.* keys, src/model_loader.cpp:126-136): Povey window, FFT

@@ -23,6 +23,8 @@
 #ifndef VOICEDETECT_CAPI_H
 #define VOICEDETECT_CAPI_H
 
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -87,6 +89,17 @@ int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus);
 int voicedetect_b200_embed_device(voicedetect_ctx* ctx, const float* d_pcm,
                                   const long long* offsets, const int* n_samples, int n_clips,
                                   float* d_out, void* stream);
+
+/* Batch embed of int16 mono clips (the samples a WAV file holds; value / 32768 is
+ * the f32 the reference's drwav decode produces) at any sample rate: the int16
+ * samples cross PCIe (half the bytes of f32) and are converted and, at rates other
+ * than 16 kHz, linearly resampled on the GPU with the reference's resample_linear
+ * arithmetic (src/audio_io.cpp:9-23; bitwise equal to the host result). Otherwise as
+ * voicedetect_capi_embed_pcm_batch: out [n_clips][dim], status 0 / nonzero with
+ * last_error. No reference counterpart (the reference decodes WAV to f32 on the host). */
+int voicedetect_b200_embed_s16_batch(voicedetect_ctx* ctx, const int16_t* const* pcm,
+                                     const int* n_samples, int n_clips, int sample_rate,
+                                     float* out, int* out_dim);
 
 /* Bucketing policy: at most max_clips clips and max_frames padded FBank frames
  * per batched pass (defaults 512 and 262144). */

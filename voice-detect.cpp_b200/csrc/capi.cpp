@@ -77,8 +77,10 @@ std::vector<float> embed_path(voicedetect_ctx* ctx, const char* path) {
 // The batch call on several GPUs: clips go to engines by LPT on sample count (the
 // longest clip to the least loaded GPU), each engine embeds its shard from its own
 // host thread, and rows are scattered back in the caller's order.
-int embed_sharded(voicedetect_ctx* ctx, const std::vector<const float*>& ptrs,
-                  const std::vector<int>& ns, float* out, std::string& err) {
+// ptrs / ns: raw mono clips of element type `type` (0 f32, 1 int16) at sample_rate.
+int embed_sharded(voicedetect_ctx* ctx, const std::vector<const void*>& ptrs,
+                  const std::vector<int>& ns, int type, int sample_rate, float* out,
+                  std::string& err) {
     std::vector<vdb::Engine*> eng{ctx->engine.get()};
     for (auto& e : ctx->extra) eng.push_back(e.get());
     const int G = (int)eng.size(), n = (int)ptrs.size(), D = ctx->engine->emb_dim();
@@ -102,14 +104,15 @@ int embed_sharded(voicedetect_ctx* ctx, const std::vector<const float*>& ptrs,
         if (shard[g].empty()) continue;
         th.emplace_back([&, g]() {
             cudaSetDevice(eng[g]->device());
-            std::vector<const float*> p;
+            std::vector<const void*> p;
             std::vector<int> c;
             for (int i : shard[g]) {
                 p.push_back(ptrs[i]);
                 c.push_back(ns[i]);
             }
             res[g].resize((size_t)shard[g].size() * D);
-            rcs[g] = eng[g]->embed_host(p.data(), c.data(), (int)p.size(), res[g].data(), errs[g]);
+            rcs[g] = eng[g]->embed_host_raw(p.data(), type, c.data(), (int)p.size(), sample_rate,
+                                            res[g].data(), errs[g]);
         });
     }
     for (auto& t : th) t.join();
@@ -242,6 +245,53 @@ extern "C" char* voicedetect_capi_analyze_path_json(voicedetect_ctx* ctx, const 
     return nullptr;
 }
 
+// Batch of raw mono clips through the context's engine(s).
+static int embed_raw_batch(voicedetect_ctx* ctx, const void* const* pcm, int type,
+                           const int* n_samples, int n_clips, int sample_rate, float* out,
+                           std::string& err) {
+    std::vector<const void*> ptrs((size_t)n_clips);
+    std::vector<int> ns((size_t)n_clips);
+    for (int i = 0; i < n_clips; ++i) {
+        if (!pcm[i] || n_samples[i] < 0) {
+            err = "invalid pcm buffer (clip " + std::to_string(i) + ")";
+            return 1;
+        }
+        ptrs[i] = pcm[i];
+        ns[i] = n_samples[i];
+    }
+    if (ctx->extra.empty())
+        return ctx->engine->embed_host_raw(ptrs.data(), type, ns.data(), n_clips, sample_rate,
+                                           out, err);
+    return embed_sharded(ctx, ptrs, ns, type, sample_rate, out, err);
+}
+
+extern "C" int voicedetect_b200_embed_s16_batch(voicedetect_ctx* ctx, const int16_t* const* pcm,
+                                                const int* n_samples, int n_clips,
+                                                int sample_rate, float* out, int* out_dim) {
+    if (out_dim) *out_dim = 0;
+    if (!ctx) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
+    if (!pcm || !n_samples || !out || n_clips <= 0 || sample_rate <= 0) {
+        ctx->last_error = "invalid batch arguments";
+        return 1;
+    }
+    try {
+        std::string err;
+        if (embed_raw_batch(ctx, reinterpret_cast<const void* const*>(pcm), 1, n_samples,
+                            n_clips, sample_rate, out, err)) {
+            ctx->last_error = err;
+            return 1;
+        }
+        if (out_dim) *out_dim = ctx->engine->emb_dim();
+        ctx->last_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        ctx->last_error = e.what();
+        return 1;
+    }
+}
+
 extern "C" int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const float* const* pcm,
                                                 const int* n_samples, int n_clips,
                                                 int sample_rate, float* out, int* out_dim) {
@@ -253,32 +303,16 @@ extern "C" int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const floa
         ctx->last_error = "invalid batch arguments";
         return 1;
     }
+    if (sample_rate <= 0) {
+        ctx->last_error = "invalid sample rate";
+        return 1;
+    }
     try {
         std::string err;
-        std::vector<std::vector<float>> res;
-        std::vector<const float*> ptrs((size_t)n_clips);
-        std::vector<int> ns((size_t)n_clips);
-        for (int i = 0; i < n_clips; ++i) {
-            if (!pcm[i] || n_samples[i] < 0) {
-                ctx->last_error = "invalid pcm buffer (clip " + std::to_string(i) + ")";
-                return 1;
-            }
-            if (sample_rate != 16000) {
-                res.emplace_back(vdb::resample_linear(
-                    std::vector<float>(pcm[i], pcm[i] + n_samples[i]), sample_rate, 16000));
-                ptrs[i] = res.back().data();
-                ns[i] = (int)res.back().size();
-            } else {
-                ptrs[i] = pcm[i];
-                ns[i] = n_samples[i];
-            }
-        }
-        if (ctx->extra.empty()) {
-            if (ctx->engine->embed_host(ptrs.data(), ns.data(), n_clips, out, err)) {
-                ctx->last_error = err;
-                return 1;
-            }
-        } else if (embed_sharded(ctx, ptrs, ns, out, err)) {
+        // other rates are resampled on the device (vdb_pcm_ingest, the reference's
+        // resample_linear arithmetic)
+        if (embed_raw_batch(ctx, reinterpret_cast<const void* const*>(pcm), 0, n_samples,
+                            n_clips, sample_rate, out, err)) {
             ctx->last_error = err;
             return 1;
         }

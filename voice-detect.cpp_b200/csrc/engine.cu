@@ -3,6 +3,7 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstring>
 #include <numeric>
@@ -166,6 +167,16 @@ void Engine::free_workspace() {
         ring_used_[s] = false;
     }
     ring_bytes_ = 0;
+    for (int s = 0; s < 2; ++s) {
+        cudaFree(d_conv_[s]);
+        cudaFreeHost(h_imeta_[s]);
+        cudaFree(d_imeta_[s]);
+        d_conv_[s] = nullptr;
+        h_imeta_[s] = nullptr;
+        d_imeta_[s] = nullptr;
+    }
+    conv_bytes_ = 0;
+    imeta_cap_ = 0;
     cudaFreeHost(h_out_);
     h_out_ = nullptr;
     cudaFree(d_out_);
@@ -1218,20 +1229,24 @@ void Engine::plan_buckets(const int* nsamp, int n, long long frame_cap, std::vec
 
 // Copies clips into one pinned buffer, splitting the bytes over a few threads
 // when there are many (a single core's memcpy would not keep up with the GPU).
-static void gather_clips(float* dst, const float* const* pcm, const int* nsamp,
+// Gather `count` clips (elements of `esz` bytes; clip idx[k] has nsamp[idx[k]]
+// elements at pcm[idx[k]]) back to back into dst, with up to 8 threads splitting the
+// byte range.
+static void gather_clips(char* dst, const void* const* pcm, const int* nsamp, size_t esz,
                          const int* idx, int count) {
     std::vector<size_t> off((size_t)count + 1, 0);
-    for (int k = 0; k < count; ++k) off[k + 1] = off[k] + (size_t)nsamp[idx[k]];
+    for (int k = 0; k < count; ++k) off[k + 1] = off[k] + (size_t)nsamp[idx[k]] * esz;
     const size_t total = off[count];
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const int nt = (int)std::min<size_t>(std::min(8u, hw), 1 + total / (4u << 20));
+    const int nt = (int)std::min<size_t>(std::min(8u, hw), 1 + total / (16u << 20));
     auto work = [&](int t) {
-        // thread t copies the sample range [t*total/nt, (t+1)*total/nt)
+        // thread t copies the byte range [t*total/nt, (t+1)*total/nt)
         const size_t lo = total * t / nt, hi = total * (t + 1) / nt;
         int k = (int)(std::upper_bound(off.begin(), off.end(), lo) - off.begin()) - 1;
         for (size_t pos = lo; pos < hi && k < count; ++k) {
             const size_t a = std::max(pos, off[k]), b = std::min(hi, off[k + 1]);
-            if (b > a) std::memcpy(dst + a, pcm[idx[k]] + (a - off[k]), (b - a) * sizeof(float));
+            if (b > a)
+                std::memcpy(dst + a, static_cast<const char*>(pcm[idx[k]]) + (a - off[k]), b - a);
             pos = b;
         }
     };
@@ -1247,21 +1262,42 @@ static void gather_clips(float* dst, const float* const* pcm, const int* nsamp,
 
 int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
                        std::string& err) {
+    return embed_host_raw(reinterpret_cast<const void* const*>(pcm), 0, nsamp, n, 16000, out,
+                          err);
+}
+
+int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, int n,
+                           int sample_rate, float* out, std::string& err) {
     if (!supported(err)) return 1;
     if (n <= 0) {
         err = "no clips";
+        return 1;
+    }
+    if ((type != 0 && type != 1) || sample_rate <= 0) {
+        err = "invalid PCM type or sample rate";
         return 1;
     }
     if (cudaSetDevice(device_) != cudaSuccess) {
         err = "cudaSetDevice failed";
         return 1;
     }
+    const size_t esz = type == 1 ? sizeof(int16_t) : sizeof(float);
+    // int16 or a rate other than 16 kHz: the raw samples cross PCIe and a kernel
+    // converts / resamples them on the device (src/audio_io.cpp:9-23 semantics)
+    const bool convert = type != 0 || sample_rate != 16000;
+    std::vector<int> ns((size_t)n);
     for (int i = 0; i < n; ++i) {
-        if (nsamp[i] < 0) {
+        if (n_in[i] < 0) {
             err = "negative sample count";
             return 1;
         }
-        if (frames_of(nsamp[i], cfg_.win, cfg_.hop) <= 0) {  // src/model.cpp:26-29
+        const long long n16 = convert ? vdb_resampled_length(n_in[i], sample_rate, 16000) : n_in[i];
+        if (n16 > INT32_MAX) {
+            err = "clip too long";
+            return 1;
+        }
+        ns[i] = (int)n16;
+        if (frames_of(ns[i], cfg_.win, cfg_.hop) <= 0) {  // src/model.cpp:26-29
             err = "voicedetect: FBank produced no frames (clip " + std::to_string(i) + ")";
             return 1;
         }
@@ -1269,18 +1305,26 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
     // At least ~4 buckets when the call is large enough, so that the host gather and
     // the H2D copy of one bucket hide behind the compute of the previous one.
     long long frames_total = 0;
-    for (int i = 0; i < n; ++i) frames_total += frames_of(nsamp[i], cfg_.win, cfg_.hop);
+    for (int i = 0; i < n; ++i) frames_total += frames_of(ns[i], cfg_.win, cfg_.hop);
     const long long cap = std::min<long long>(max_frames, std::max<long long>(frames_total / 4, 16384));
     std::vector<int> order;
     std::vector<size_t> bk;
-    plan_buckets(nsamp, n, cap, order, bk);
+    plan_buckets(ns.data(), n, cap, order, bk);
     // ring slots hold the largest bucket the policy allows (and this call's largest)
-    size_t need = ((size_t)max_frames * cfg_.hop + (size_t)max_clips * cfg_.win) * sizeof(float);
+    size_t need = convert ? 0 : ((size_t)max_frames * cfg_.hop + (size_t)max_clips * cfg_.win) * sizeof(float);
+    size_t need_conv = 0;
+    int max_cnt = 0;
     for (size_t k = 0; k + 1 < bk.size(); ++k) {
-        size_t b = 0;
-        for (size_t j = bk[k]; j < bk[k + 1]; ++j) b += (size_t)nsamp[order[j]] * sizeof(float);
+        size_t b = 0, c = 0;
+        for (size_t j = bk[k]; j < bk[k + 1]; ++j) {
+            b += (size_t)n_in[order[j]] * esz;
+            c += (size_t)ns[order[j]] * sizeof(float);
+        }
         need = std::max(need, b);
+        need_conv = std::max(need_conv, c);
+        max_cnt = std::max(max_cnt, (int)(bk[k + 1] - bk[k]));
     }
+    need = std::max<size_t>(need, 16);
     if (need > ring_bytes_) {
         VDB_CHECK_CUDA(cudaDeviceSynchronize());
         clear_graphs();
@@ -1299,6 +1343,32 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
                 return 1;
             }
         ring_bytes_ = need;
+    }
+    if (convert && (need_conv > conv_bytes_ || max_cnt > imeta_cap_)) {
+        VDB_CHECK_CUDA(cudaDeviceSynchronize());
+        clear_graphs();  // captured buckets read the old converted-PCM buffers
+        for (int s = 0; s < 2; ++s) {
+            cudaFree(d_conv_[s]);
+            cudaFreeHost(h_imeta_[s]);
+            cudaFree(d_imeta_[s]);
+            d_conv_[s] = nullptr;
+            h_imeta_[s] = nullptr;
+            d_imeta_[s] = nullptr;
+            ring_used_[s] = false;
+        }
+        conv_bytes_ = 0;
+        imeta_cap_ = 0;
+        const int cap_c = std::max(max_cnt, max_clips);
+        const size_t mb = (size_t)cap_c * (2 * sizeof(long long) + 2 * sizeof(int));
+        for (int s = 0; s < 2; ++s)
+            if (cudaMalloc(&d_conv_[s], std::max(need_conv, conv_bytes_)) != cudaSuccess ||
+                cudaMallocHost(&h_imeta_[s], mb) != cudaSuccess ||
+                cudaMalloc(&d_imeta_[s], mb) != cudaSuccess) {
+                err = "out of memory (PCM conversion)";
+                return 1;
+            }
+        conv_bytes_ = need_conv;
+        imeta_cap_ = cap_c;
     }
     const size_t ob = (size_t)n * cfg_.emb_dim * sizeof(float);
     if (ob > out_bytes_) {
@@ -1328,23 +1398,52 @@ int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* 
         const int* idx = order.data() + bk[k];
         // the pinned slot is free once its previous H2D copy finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaEventSynchronize(h2d_ev_[s]));
-        gather_clips(h_ring_[s], pcm, nsamp, idx, cnt);
+        gather_clips(reinterpret_cast<char*>(h_ring_[s]), pcm, n_in, esz, idx, cnt);
         bo.assign((size_t)cnt, 0);
         bn.assign((size_t)cnt, 0);
-        long long tot = 0;
+        long long tot = 0, tot_in = 0;
+        int max_out = 0;
+        // conversion metadata: [in_off][out_off] (int64), [n_in][n_out] (int32)
+        long long* mi = convert ? static_cast<long long*>(h_imeta_[s]) : nullptr;
         for (int j = 0; j < cnt; ++j) {
             bo[j] = tot;
-            bn[j] = nsamp[idx[j]];
+            bn[j] = ns[idx[j]];
+            if (convert) {
+                mi[j] = tot_in;
+                mi[imeta_cap_ + j] = tot;
+                int* mn = reinterpret_cast<int*>(mi + 2 * imeta_cap_);
+                mn[j] = n_in[idx[j]];
+                mn[imeta_cap_ + j] = bn[j];
+            }
             tot += bn[j];
+            tot_in += n_in[idx[j]];
+            max_out = std::max(max_out, bn[j]);
         }
         // the device slot is free once the bucket that last read it finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaStreamWaitEvent(copy_stream_, comp_ev_[s], 0));
-        VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot * sizeof(float),
+        VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot_in * esz,
                                        cudaMemcpyHostToDevice, copy_stream_));
+        if (convert)
+            VDB_CHECK_CUDA(cudaMemcpyAsync(d_imeta_[s], h_imeta_[s],
+                                           (size_t)imeta_cap_ * (2 * sizeof(long long) + 2 * sizeof(int)),
+                                           cudaMemcpyHostToDevice, copy_stream_));
         VDB_CHECK_CUDA(cudaEventRecord(h2d_ev_[s], copy_stream_));
         VDB_CHECK_CUDA(cudaStreamWaitEvent(stream_, h2d_ev_[s], 0));
         ring_used_[s] = true;
-        if (run_bucket(d_ring_[s], bo.data(), bn.data(), idx, cnt, stream_, d_out_, err)) {
+        const float* d_pcm = reinterpret_cast<const float*>(d_ring_[s]);
+        if (convert) {
+            long long* dm = static_cast<long long*>(d_imeta_[s]);
+            const int* dn = reinterpret_cast<const int*>(dm + 2 * imeta_cap_);
+            if (vdb_pcm_ingest(d_ring_[s], type, dm, dn, cnt, sample_rate, 16000, dm + imeta_cap_,
+                               dn + imeta_cap_, max_out, d_conv_[s], stream_)) {
+                err = vdb_last_error();
+                cudaStreamSynchronize(stream_);
+                return 1;
+            }
+            ++last_launches;
+            d_pcm = d_conv_[s];
+        }
+        if (run_bucket(d_pcm, bo.data(), bn.data(), idx, cnt, stream_, d_out_, err)) {
             cudaStreamSynchronize(stream_);
             return 1;
         }

@@ -122,6 +122,11 @@ public:
     // Host PCM in, host embeddings out (synchronous). pcm[i] has nsamp[i] samples.
     int embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
                    std::string& err);
+    // Host mono PCM of element type `type` (0 f32, 1 int16 scaled by 2^-15) at
+    // `sample_rate`: the raw samples are copied to the device and converted /
+    // linearly resampled to f32 16 kHz there (vdb_pcm_ingest) before the buckets run.
+    int embed_host_raw(const void* const* pcm, int type, const int* nsamp, int n,
+                       int sample_rate, float* out, std::string& err);
 
     // Reads and clears the device error word (kernel timeouts). Synchronises.
     int check_device_error(std::string& err);
@@ -241,9 +246,16 @@ private:
     // holding one bucket. The host gathers bucket k+1 into its pinned slot while
     // the GPU runs bucket k; the H2D copy runs on copy_stream_ and overlaps compute.
     cudaStream_t copy_stream_ = nullptr;
-    float* h_ring_[2] = {nullptr, nullptr};
-    float* d_ring_[2] = {nullptr, nullptr};
+    void* h_ring_[2] = {nullptr, nullptr};   // raw PCM of one bucket (f32 or int16)
+    void* d_ring_[2] = {nullptr, nullptr};
     size_t ring_bytes_ = 0;
+    // device conversion of raw PCM (int16 / other rates): f32 16 kHz output per slot
+    // and the per-clip offsets / lengths the ingest kernel reads
+    float* d_conv_[2] = {nullptr, nullptr};
+    size_t conv_bytes_ = 0;
+    void* h_imeta_[2] = {nullptr, nullptr};
+    void* d_imeta_[2] = {nullptr, nullptr};
+    int imeta_cap_ = 0;
     bool ring_used_[2] = {false, false};
     cudaEvent_t h2d_ev_[2] = {nullptr, nullptr};    // slot's H2D copy finished
     cudaEvent_t comp_ev_[2] = {nullptr, nullptr};   // slot's bucket compute finished

@@ -131,6 +131,17 @@ def lib() -> C.CDLL:
                                                        C.POINTER(C.POINTER(C.c_float)),
                                                        C.POINTER(C.c_int), C.c_int, C.c_int,
                                                        C.POINTER(C.c_float), C.POINTER(C.c_int)]
+        L.voicedetect_b200_embed_s16_batch.restype = C.c_int
+        L.voicedetect_b200_embed_s16_batch.argtypes = [C.c_void_p,
+                                                       C.POINTER(C.POINTER(C.c_int16)),
+                                                       C.POINTER(C.c_int), C.c_int, C.c_int,
+                                                       C.POINTER(C.c_float), C.POINTER(C.c_int)]
+        L.vdb_resampled_length.restype = C.c_longlong
+        L.vdb_resampled_length.argtypes = [C.c_longlong, C.c_int, C.c_int]
+        L.vdb_pcm_ingest.restype = C.c_int
+        L.vdb_pcm_ingest.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                     C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                     C.c_void_p, C.c_void_p]
         L.voicedetect_capi_identify.restype = C.c_int
         L.voicedetect_capi_identify.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.c_int,
                                                 C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int,
@@ -235,6 +246,25 @@ class Model:
         out = np.zeros((n, self.dim), np.float32)
         d = C.c_int(0)
         rc = self._L.voicedetect_capi_embed_pcm_batch(self.ctx, ptrs, ns, n, sample_rate,
+                                                      out.ctypes.data_as(C.POINTER(C.c_float)),
+                                                      C.byref(d))
+        if rc != 0:
+            raise VoiceDetectError(self.last_error())
+        return out
+
+    def embed_batch_s16(self, clips, sample_rate: int = 16000):
+        """int16 mono clips (voicedetect_b200_embed_s16_batch): converted and, at other
+        rates, resampled on the GPU."""
+        import numpy as np
+        arrs = [np.ascontiguousarray(c, dtype=np.int16) for c in clips]
+        n = len(arrs)
+        addr = np.fromiter((a.__array_interface__["data"][0] for a in arrs), np.uint64, n)
+        lens = np.fromiter((len(a) for a in arrs), np.int32, n)
+        ptrs = addr.ctypes.data_as(C.POINTER(C.POINTER(C.c_int16)))
+        ns = lens.ctypes.data_as(C.POINTER(C.c_int))
+        out = np.zeros((n, self.dim), np.float32)
+        d = C.c_int(0)
+        rc = self._L.voicedetect_b200_embed_s16_batch(self.ctx, ptrs, ns, n, sample_rate,
                                                       out.ctypes.data_as(C.POINTER(C.c_float)),
                                                       C.byref(d))
         if rc != 0:
@@ -478,6 +508,29 @@ def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv1d(C.byref(a), C.c_void_p(s)), "vdb_conv1d")
     return y
+
+
+def pcm_ingest(clips, sample_rate: int, out_rate: int = 16000):
+    """vdb_pcm_ingest on device tensors: list of 1-D int16 or f32 torch tensors (one
+    dtype) -> list of f32 tensors at out_rate."""
+    import torch
+    dev = clips[0].device
+    s16 = clips[0].dtype == torch.int16
+    n_in = [int(c.numel()) for c in clips]
+    n_out = [int(lib().vdb_resampled_length(n, sample_rate, out_rate)) for n in n_in]
+    cat = torch.cat(clips)
+    in_off = torch.tensor([0] + list(__import__("itertools").accumulate(n_in))[:-1],
+                          dtype=torch.int64, device=dev)
+    out_off_l = [0] + list(__import__("itertools").accumulate(n_out))[:-1]
+    out = torch.zeros(max(sum(n_out), 1), dtype=torch.float32, device=dev)
+    a = torch.tensor(n_in, dtype=torch.int32, device=dev)
+    b = torch.tensor(n_out, dtype=torch.int32, device=dev)
+    oo = torch.tensor(out_off_l, dtype=torch.int64, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    _check(lib().vdb_pcm_ingest(cat.data_ptr(), 1 if s16 else 0, in_off.data_ptr(), a.data_ptr(),
+                                len(clips), sample_rate, out_rate, oo.data_ptr(), b.data_ptr(),
+                                max(n_out), out.data_ptr(), C.c_void_p(s)), "vdb_pcm_ingest")
+    return [out[o:o + n] for o, n in zip(out_off_l, n_out)]
 
 
 def add(a, b, y=None, stream=None):
