@@ -424,3 +424,6 @@ def identify(q: np.ndarray, reg: np.ndarray, k: int = 5) -> tuple[np.ndarray, np
 
 # ECAPA-TDNN: numpy restatement (oracle/ecapa.py)
 from .ecapa import ecapa_embed  # noqa: E402,F401
+
+# CAM++: numpy restatement (oracle/campplus.py)
+from .campplus import campplus_embed  # noqa: E402,F401

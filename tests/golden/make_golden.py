@@ -20,6 +20,9 @@ the repository).
   (vd_synth.ecapa_forward_torch: torch's reflect pad, conv1d, batch_norm,
   softmax), independent of the numpy oracle it pins. The reference's own ECAPA
   graph needs the absent ggml library, so no reference output exists for it.
+* ref_campplus_tiny.npz -- the same for a small seeded CAM++ (vd_synth.tiny_campplus_model,
+  every layer kind; one clip longer than one 100-frame context segment) from
+  vd_synth.campplus_forward_torch.
 
 Usage: python tests/golden/make_golden.py [name ...]   (default: every fixture)
 """
@@ -84,10 +87,25 @@ def make_ecapa() -> None:
     np.savez_compressed(HERE / "ref_ecapa_tiny.npz", **d)
 
 
+def make_campplus() -> None:
+    import torch
+    m = vd_synth.tiny_campplus_model(9, n_mels=80)
+    d = {}
+    for i, (seed, n) in enumerate(((25, 24000), (26, 16000 + 160 * 230 + 61))):
+        pcm = vd_synth.clip_f32(vd_synth.make_clip(seed, n))
+        feats = fbank_torchaudio(pcm)
+        emb, pre = vd_synth.campplus_forward_torch(m, torch.from_numpy(feats[None].astype(np.float64)))
+        d[f"pcm{i}"] = pcm
+        d[f"feats{i}"] = feats
+        d[f"emb{i}"] = emb[0].astype(np.float32)
+        d[f"prenorm{i}"] = pre[0].astype(np.float32)
+    np.savez_compressed(HERE / "ref_campplus_tiny.npz", **d)
+
+
 def main() -> None:
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:
-            {"ecapa": make_ecapa}[name]()
+            {"ecapa": make_ecapa, "campplus": make_campplus}[name]()
         print("wrote", sys.argv[1:])
         return
     clips = [vd_synth.make_clip(s, n) for s, n in ((11, 48000), (12, 16000 + 37), (13, 401))]
@@ -120,6 +138,7 @@ def main() -> None:
     emb, pre = oracle.RefERes2Net(m).embed(feats)
     np.savez_compressed(HERE / "ref_eres2net_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
     make_ecapa()
+    make_campplus()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -230,3 +230,34 @@ def test_ecapa_f16_weights_are_well_conditioned():
     a, _ = oracle.ecapa_embed(m, feats)
     b, _ = oracle.ecapa_embed(vd_synth.f16_ecapa_model(m), feats)
     assert _cos(a, b) >= 0.99999
+
+
+def test_campplus_tiny_golden():
+    """numpy CAM++ oracle (oracle/campplus.py) vs the committed golden made by an
+    independent float64 torch formulation on torchaudio FBank features (one clip
+    spans two 100-frame context segments)."""
+    g = np.load(GOLD / "ref_campplus_tiny.npz")
+    m = vd_synth.tiny_campplus_model(9, n_mels=80)
+    for i in range(2):
+        emb, pre = oracle.campplus_embed(m, g[f"feats{i}"])
+        want = g[f"prenorm{i}"]
+        assert np.abs(pre - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+        assert _cos(emb, g[f"emb{i}"]) >= 0.999999
+        emb2, _ = oracle.campplus_embed(m, oracle.fbank(g[f"pcm{i}"]))
+        assert _cos(emb2, g[f"emb{i}"]) >= 0.99999
+
+
+def test_campplus_manifest_and_gguf(tmp_path):
+    """The full CAM++ manifest: 225 convs and 55 runtime BatchNorms in execution
+    order (the converter's assertion, scripts/convert_voicedetect_to_gguf.py), written
+    with the reference's voicedetect.campplus.* keys."""
+    gguf = pytest.importorskip("gguf")
+    m = vd_synth.campplus_model(0, calibrate=False)
+    assert len(m["convs"]) == 225 and len(m["bns"]) == 55
+    assert m["convs"][-1]["w"].shape == (192, 1024, 1)
+    path = tmp_path / "c.gguf"
+    vd_synth.write_campplus_gguf(str(path), m, "f16")
+    r = gguf.GGUFReader(str(path))
+    kv = {f.name for f in r.fields.values()}
+    assert {"voicedetect.campplus.conv_weight", "voicedetect.campplus.bn_prefix",
+            "voicedetect.campplus.emb_bn_mean"} <= kv

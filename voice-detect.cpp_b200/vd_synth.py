@@ -709,3 +709,254 @@ def quantized_ecapa_model(m: dict, dtype: str) -> dict:
             r = a2
         sd[name] = r[:, :, None].astype(np.float32)
     return dict(m, sd=sd)
+
+
+# ---------------------------------------------------------------------------
+# CAM++ (3D-Speaker D-TDNN with context-aware masking)
+# ---------------------------------------------------------------------------
+CAMPP_LAYERS = (12, 24, 16)
+CAMPP_DIL = (1, 2, 2)
+
+
+def campplus_model(seed: int = 0, n_mels: int = N_MELS, m_channels: int = 32,
+                   init_channels: int = 128, growth: int = 32, bn_size: int = 4,
+                   layers=CAMPP_LAYERS, emb_dim: int = 192, calibrate: bool = True) -> dict:
+    """Synthetic 3D-Speaker CAM++ as the reference's manifest sees it
+    (src/model_loader.hpp:82-98, src/encoder_campplus.cpp:148-300): a flat list of
+    convs in forward-EXECUTION order and a list of the runtime (affine) BatchNorms:
+
+      FCM (12 convs, BatchNorm folded, freq-axis strides): stem 3x3 1->M; two stages
+        of [BasicResBlock s2 (conv1, conv2, 1x1 shortcut), BasicResBlock s1 (conv1,
+        conv2)]; conv2 3x3 s2. Freq 80 -> 10, channels M x 10.
+      TDNN: Conv1d k=5 stride 2 pad 2 (BN folded) -> ReLU.
+      3 CAMDenseTDNN blocks (layers 12 / 24 / 16, dilation 1 / 2 / 2), each layer:
+        BN (runtime) -> ReLU -> 1x1 conv to bn_size*growth (BN folded) -> ReLU -> CAM:
+        linear_local k=3 dilated (no bias), linear1 1x1 (bias) -> ReLU, linear2 1x1
+        (bias) -> sigmoid, on the mean + 100-frame segment context; the layer output
+        (growth channels) is concatenated to the block input.
+      Transits: BN (runtime) -> ReLU -> 1x1 conv halving the channels (no bias; the
+        last one has the output BN folded in, a bias, and a ReLU after it).
+      Head: stats pooling (mean, unbiased std), 1x1 dense 2C -> emb (no bias),
+        affine-free BN.
+
+    Weights are Kaiming-normal; with calibrate=True every BatchNorm (folded or
+    runtime) takes the statistics of its input on a seeded calibration batch, as a
+    trained model's running statistics are (see ecapa_model)."""
+    rng = np.random.default_rng(seed)
+    convs: list[dict] = []
+    bns: list[dict] = []
+
+    def conv(oc, ic, k, two_d=False, bias=True, **meta):
+        shape = (oc, ic, k, k) if two_d else (oc, ic, k)
+        w = (rng.standard_normal(shape) * np.sqrt(2.0 / (ic * k * (k if two_d else 1)))).astype(np.float32)
+        b = rng.normal(0.0, 0.05, oc).astype(np.float32) if bias else None
+        convs.append(dict(w=w, b=b, fold=bias and meta.pop("fold", True), **meta))
+
+    def bn(c):
+        bns.append({"weight": rng.uniform(0.8, 1.2, c).astype(np.float32),
+                    "bias": rng.normal(0.0, 0.1, c).astype(np.float32),
+                    "running_mean": rng.normal(0.0, 0.1, c).astype(np.float32),
+                    "running_var": rng.uniform(0.5, 1.5, c).astype(np.float32)})
+
+    M = m_channels
+    conv(M, 1, 3, True)                                     # FCM stem
+    for _ in range(2):                                      # layer1, layer2
+        conv(M, M, 3, True), conv(M, M, 3, True), conv(M, M, 1, True)   # s2 block + shortcut
+        conv(M, M, 3, True), conv(M, M, 3, True)                         # s1 block
+    conv(M, M, 3, True)                                     # FCM conv2 (s2)
+    f = n_mels
+    for _ in range(3):
+        f = (f - 1) // 2 + 1
+    conv(init_channels, M * f, 5)                           # TDNN
+    C = init_channels
+    bnc = bn_size * growth
+    for bi, nl in enumerate(layers):
+        for _ in range(nl):
+            bn(C)                                           # nonlinear1
+            conv(bnc, C, 1)                                 # linear1 (+ folded BN)
+            conv(growth, bnc, 3, bias=False)                # CAM linear_local
+            conv(bnc // 2, bnc, 1, fold=False)              # CAM linear1 (genuine bias)
+            conv(growth, bnc // 2, 1, fold=False)           # CAM linear2 (genuine bias)
+            C += growth
+        bn(C)                                               # transit nonlinear
+        conv(C // 2, C, 1, bias=(bi == 2))                  # transit (last: + out BN)
+        C //= 2
+    conv(emb_dim, 2 * C, 1, bias=False)                     # dense head
+    m = {"arch": "campplus", "convs": convs, "bns": bns, "n_mels": n_mels, "emb_dim": emb_dim,
+         "emb_bn_mean": rng.normal(0.0, 0.1, emb_dim).astype(np.float32),
+         "emb_bn_var": rng.uniform(0.5, 1.5, emb_dim).astype(np.float32),
+         "bn_eps": 1e-5, "l2_normalize": True, "layers": list(layers)}
+    assert len(convs) == 12 + 1 + 4 * sum(layers) + 3 + 1
+    if calibrate:
+        import torch
+        crng = np.random.default_rng(seed + 15485863)
+        feats = torch.from_numpy(crng.standard_normal((6, n_mels, 240)) * 1.5)
+        campplus_forward_torch(m, feats, calibrate=True)
+    return m
+
+
+def tiny_campplus_model(seed: int = 0, n_mels: int = 80) -> dict:
+    """Narrow CAM++ for CPU tests: same topology rules, 2 / 3 / 2 dense layers."""
+    return campplus_model(seed, n_mels=n_mels, m_channels=16, init_channels=64, growth=16,
+                          bn_size=2, layers=(2, 3, 2), emb_dim=48)
+
+
+def campplus_forward_torch(m: dict, feats, calibrate: bool = False):
+    """CAM++ forward in torch float64 with the reference's semantics, written with
+    torch's own conv1d / conv2d / batch_norm (an implementation independent of the
+    numpy oracle). feats [N, n_mels, T] (CMN applied). Returns (emb, pre-norm) [N, D].
+    calibrate=True folds measured BatchNorm statistics into the BN-folded convs and
+    sets the runtime BatchNorms' running statistics, in execution order."""
+    import torch
+    import torch.nn.functional as Fn
+
+    convs, bns = m["convs"], m["bns"]
+    ci = [0]
+    bi = [0]
+    eps = float(m["bn_eps"])
+
+    def t(a):
+        return torch.from_numpy(np.asarray(a, np.float64))
+
+    def fold(c, y, dims):
+        # calibrated BatchNorm folded into a biased conv: w *= s, b = beta - mu * s
+        mu = y.mean(dims)
+        s = 1.0 / torch.sqrt(y.var(dims, unbiased=False) + 1e-5)
+        beta = t(np.random.default_rng(len(c["w"].ravel())).normal(0.0, 0.1, y.shape[1]))
+        shp = (-1,) + (1,) * (c["w"].ndim - 1)
+        c["w"] = (t(c["w"]) * s.view(shp)).numpy().astype(np.float32)
+        c["b"] = (beta - mu * s).numpy().astype(np.float32)
+
+    def conv2d(x, stride_f):
+        c = convs[ci[0]]
+        ci[0] += 1
+        k = c["w"].shape[-1]
+        pad = (k - 1) // 2
+        if calibrate and c["b"] is not None and c["fold"]:
+            y = Fn.conv2d(x, t(c["w"]), None, stride=(stride_f, 1), padding=pad)
+            fold(c, y, (0, 2, 3))
+        return Fn.conv2d(x, t(c["w"]), None if c["b"] is None else t(c["b"]),
+                         stride=(stride_f, 1), padding=pad)
+
+    def conv1d(x, stride=1, pad=0, dil=1):
+        c = convs[ci[0]]
+        ci[0] += 1
+        if calibrate and c["b"] is not None and c["fold"]:
+            y = Fn.conv1d(x, t(c["w"]), None, stride=stride, padding=pad, dilation=dil)
+            fold(c, y, (0, 2))
+        return Fn.conv1d(x, t(c["w"]), None if c["b"] is None else t(c["b"]),
+                         stride=stride, padding=pad, dilation=dil)
+
+    def bn(x):
+        p = bns[bi[0]]
+        bi[0] += 1
+        if calibrate:
+            p["running_mean"] = x.mean((0, 2)).numpy().astype(np.float32)
+            p["running_var"] = x.var((0, 2), unbiased=False).clamp_min(1e-2).numpy().astype(np.float32)
+        return Fn.batch_norm(x, t(p["running_mean"]), t(p["running_var"]), t(p["weight"]),
+                             t(p["bias"]), training=False, eps=eps)
+
+    def block(x, stride):
+        out = torch.relu(conv2d(x, stride))
+        out = conv2d(out, 1)
+        sc = conv2d(x, stride) if stride != 1 else x
+        return torch.relu(out + sc)
+
+    with torch.no_grad():
+        x = feats.to(torch.float64).unsqueeze(1)            # [N, 1, F, T]
+        h = torch.relu(conv2d(x, 1))
+        h = block(h, 2)
+        h = block(h, 1)
+        h = block(h, 2)
+        h = block(h, 1)
+        h = torch.relu(conv2d(h, 2))
+        N, Cc, Fq, T = h.shape
+        h = h.reshape(N, Cc * Fq, T)                         # channel = c * F' + f
+        h = torch.relu(conv1d(h, stride=2, pad=2))
+        Tp = h.shape[-1]
+        seg = torch.arange(Tp) // 100
+        nseg = (Tp + 99) // 100
+        for blk, (nl, dil) in enumerate(zip(m["layers"], CAMPP_DIL)):
+            for _ in range(nl):
+                a = torch.relu(bn(h))
+                cc = torch.relu(conv1d(a))
+                y = conv1d(cc, pad=dil, dil=dil)
+                # context: global mean + 100-frame segment means (each divided by 100)
+                segs = torch.stack([cc[:, :, s * 100:(s + 1) * 100].sum(-1) / 100.0
+                                    for s in range(nseg)], -1)           # [N, C, nseg]
+                ctx = cc.mean(-1, keepdim=True) + segs[:, :, seg]
+                mk = torch.sigmoid(conv1d(torch.relu(conv1d(ctx))))
+                h = torch.cat([h, y * mk], 1)
+            tr = conv1d(torch.relu(bn(h)))
+            h = torch.relu(tr) if blk == 2 else tr
+        mean = h.mean(-1)
+        std = h.std(-1, unbiased=True) if Tp > 1 else torch.zeros_like(mean)
+        stats = torch.cat([mean, std], 1).unsqueeze(-1)
+        e = conv1d(stats).squeeze(-1)
+        if calibrate:
+            m["emb_bn_mean"] = e.mean(0).numpy().astype(np.float32)
+            m["emb_bn_var"] = e.var(0, unbiased=False).clamp_min(1e-2).numpy().astype(np.float32)
+        pre = (e - t(m["emb_bn_mean"])) / torch.sqrt(t(m["emb_bn_var"]) + eps)
+        emb = pre / pre.norm(dim=1, keepdim=True)
+    assert ci[0] == len(convs) and bi[0] == len(bns)
+    return emb.numpy(), pre.numpy()
+
+
+def write_campplus_gguf(path: str, m: dict, dtype: str = "f32") -> None:
+    """campplus GGUF with the reference's manifest keys (voicedetect.campplus.*,
+    src/model_loader.cpp:165-172). dtype f32 | f16 (conv weights)."""
+    import gguf
+
+    w = gguf.GGUFWriter(path, arch="voicedetect")
+    w.add_string("voicedetect.arch", "campplus")
+    w.add_uint32("voicedetect.embedding_dim", int(m["emb_dim"]))
+    w.add_bool("voicedetect.l2_normalize", bool(m.get("l2_normalize", True)))
+    w.add_uint32("voicedetect.fbank.sample_rate", 16000)
+    w.add_uint32("voicedetect.fbank.n_mels", int(m["n_mels"]))
+    w.add_uint32("voicedetect.fbank.n_fft", 512)
+    w.add_uint32("voicedetect.fbank.win_length", 400)
+    w.add_uint32("voicedetect.fbank.hop_length", 160)
+    w.add_float32("voicedetect.fbank.preemph", 0.97)
+    w.add_float32("voicedetect.fbank.low_freq", 20.0)
+    w.add_float32("voicedetect.fbank.high_freq", 0.0)
+    w.add_bool("voicedetect.fbank.cmn", True)
+    wn, bn_ = [], []
+    tensors = []
+    for i, c in enumerate(m["convs"]):
+        wn.append(f"conv{i}.weight")
+        tensors.append((wn[-1], c["w"], "conv"))
+        if c["b"] is not None:
+            bn_.append(f"conv{i}.bias")
+            tensors.append((bn_[-1], c["b"], "bias"))
+        else:
+            bn_.append("")
+    pre = []
+    for j, b in enumerate(m["bns"]):
+        pre.append(f"bn{j}")
+        for k in ("weight", "bias", "running_mean", "running_var"):
+            tensors.append((f"bn{j}.{k}", b[k], "bias"))
+    tensors.append(("emb_bn.running_mean", m["emb_bn_mean"], "bias"))
+    tensors.append(("emb_bn.running_var", m["emb_bn_var"], "bias"))
+    w.add_array("voicedetect.campplus.conv_weight", wn)
+    w.add_array("voicedetect.campplus.conv_bias", bn_)
+    w.add_array("voicedetect.campplus.bn_prefix", pre)
+    w.add_string("voicedetect.campplus.emb_bn_mean", "emb_bn.running_mean")
+    w.add_string("voicedetect.campplus.emb_bn_var", "emb_bn.running_var")
+    w.add_float32("voicedetect.campplus.bn_eps", float(m["bn_eps"]))
+    for name, arr, kind in tensors:
+        arr = np.ascontiguousarray(arr, np.float32)
+        if dtype == "f16" and kind == "conv" and arr.shape[1] > 1:
+            w.add_tensor(name, arr.astype(np.float16))
+        else:
+            w.add_tensor(name, arr)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+def f16_campplus_model(m: dict) -> dict:
+    """The weights an f16 GGUF carries (conv weights with IC > 1 rounded)."""
+    convs = [dict(c, w=c["w"].astype(np.float16).astype(np.float32)) if c["w"].shape[1] > 1
+             else c for c in m["convs"]]
+    return dict(m, convs=convs)
