@@ -31,6 +31,11 @@
  *   position (tp, fp) of image b sits in plane q at row
  *   (b*(To+2) + (tp>>1) + 1)*(Fo+2) + (fp>>1) + 1. Slots no position maps to
  *   are never read by a valid output.
+ * FPHASE FP(B, T, F, C): the same data split into the 2 frequency phases for a
+ *   consumer that strides 2 along frequency only (CAM++'s FCM, Conv2d stride (2, 1)),
+ *   output extents (T, Fo = (F-1)/2+1). Plane q = fp&1 is a G(B, T, Fo, C)-shaped
+ *   block; padded position (tp, fp) of image b sits in plane q at row
+ *   (b*(T+2) + tp)*(Fo+2) + (fp>>1) + 1.
  * Weights: f16 [OC][k*k][IC] with tap index kt*k + kf (kt = time tap = the
  *   reference's kw, kf = freq tap = the reference's kh), i.e. torch
  *   w[oc][ic][kf][kt] -> W[oc][kt*k + kf][ic].
@@ -56,13 +61,14 @@ typedef struct vdb_conv_args {
     /* segment 0: the conv itself */
     int k0;             /* kernel size: 3 (pad 1) or 1 (pad 0) */
     int stride0;        /* 1: x0 is G(B, t_out, f_out, ic0); 2: x0 is P(B, t_in, f_in, ic0)
-                           whose stride-2 output extents are (t_out, f_out) */
+                           whose stride-2 output extents are (t_out, f_out); 3 (stride 2 on
+                           the frequency axis only): x0 is FP(B, t_out, f_in, ic0) */
     int ic0;            /* input channels, multiple of 16 */
     const void* x0;     /* device f16 */
     const void* w0;     /* device f16 [oc][k0*k0][ic0] */
     /* segment 1 (optional, x1 == NULL to disable): a 1x1 conv accumulated into the
        same outputs (the fused BasicBlock downsample shortcut) */
-    int stride1;        /* 1: x1 is G(B, t_out, f_out, ic1); 2: x1 is P(...) */
+    int stride1;        /* 1: x1 is G(B, t_out, f_out, ic1); 2: x1 is P(...); 3: FP(...) */
     int ic1;
     const void* x1;
     const void* w1;     /* device f16 [oc][ic1] */
@@ -73,7 +79,10 @@ typedef struct vdb_conv_args {
     float clamp_hi;         /* > 0: min(., clamp_hi) after ReLU (Hardtanh(0, hi)) */
     const int* tvalid;      /* device int32 [B]: valid time extent of the output */
     void* y;                /* device f16 output */
-    int y_phase;            /* 0: y is G(B, t_out, f_out, oc); 1: y is P(B, t_out, f_out, oc) */
+    int y_phase;            /* 0: y is G(B, t_out, f_out, oc); 1: y is P(B, t_out, f_out, oc);
+                               2: y is FP(B, t_out, f_out, oc); 3: y is
+                               TS(B, (t_out-1)/2+1, y_pad, f_out*oc) (pixel (t, f) channel c
+                               at channel f*oc + c; grid border pixels are not stored) */
     int* err;               /* device int32 error word (may be NULL): kernel timeouts */
     /* tiling (0 = automatic) */
     int tile_m;             /* output rows per CTA tile: 0, 128 or 256 */
@@ -103,6 +112,7 @@ typedef struct vdb_conv_args {
     int ldsum;
     const void* addend;
     int ldaddend;
+    int y_pad;              /* y_phase 3: padding rows P of the 1-D consumer's slots */
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */
@@ -120,6 +130,12 @@ int vdb_conv(const vdb_conv_args* a, void* stream);
  *   1 <= j <= P: SpeechBrain's reflect padding at the clip's own length, which the
  *   reference builds with get_rows, src/encoder.cpp:32-50) when the tensor feeds a
  *   conv with k > 1; other rows are never read by a valid output.
+ * With reflect = 2 the tensor is zero-padded instead: every row of the clip slots
+ *   is stored, 0 outside the valid frames.
+ * TPHASE TS(B, T, P, C): the input of a time-stride-2 conv whose output is
+ *   S(B, T, P, *): two S(B, T, P, C) planes (contiguous, plane-major), input frame u
+ *   of clip b in plane u&1 at row b*(T+2P) + P + (u>>1). Rows no frame maps to must
+ *   hold 0 (the producer's caller clears the planes).
  * Weights: f16 [oc][k][ic], tap j at time offset (j - (k-1)/2) * dil (torch
  *   w[oc][ic][j] -> W[oc][j][ic]). */
 long long vdb_seq_rows(int batch, int t, int pad);
@@ -144,7 +160,8 @@ typedef struct vdb_conv1d_args {
     const float* bn_shift;
     int act;                /* 0: acc + bias [+ residual], then ReLU if relu;
                                1: SiLU; 3: BN(ReLU(acc + bias + clip_bias)) with
-                               BN(v) = v * bn_scale + bn_shift; 4: tanh of act 3 */
+                               BN(v) = v * bn_scale + bn_shift; 4: tanh of act 3;
+                               5: (acc + bias) * gate[b][t / gate_seg][col] */
     int relu;
     const void* residual;   /* act 0/1: device f16 S(B, T, P, oc), pitch ldr; or NULL */
     int ldr;
@@ -152,7 +169,9 @@ typedef struct vdb_conv1d_args {
     void* y;                /* device S(B, T, P, oc): f16, or f32 when y_f32 */
     int ldy;
     int y_f32;
-    int reflect;            /* also write the P reflection rows on each side */
+    int reflect;            /* 1: also write the P reflection rows on each side;
+                               2: zero padding (every slot row stored, 0 outside the
+                               valid frames); 0: valid frames only */
     void* ysum;             /* optional f16 f16(y + addend), same rows (and reflections) */
     int ldsum;
     const void* addend;
@@ -164,6 +183,11 @@ typedef struct vdb_conv1d_args {
                                256-row tile, each loading half of the tile's weight columns
                                (oc tiles multiples of 32, tile_m 0 or 256); 0 / -1: one CTA
                                per tile */
+    int stride0;            /* 0 / 1: stride 1; 2: time stride 2, x0 is TS(B, T, P, ic0)
+                               (output frame o reads input frames 2o + (j - (k-1)/2)*dil) */
+    const float* gate;      /* act 5: device f32 [B][gate_nseg][oc], 16-byte aligned */
+    int gate_seg;           /* act 5: frames per gate segment */
+    int gate_nseg;          /* act 5: segments per clip in `gate` (>= ceil(T / gate_seg)) */
 } vdb_conv1d_args;
 
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);

@@ -105,12 +105,13 @@ struct ConvDev {
     __half* ysum;            // optional f16(y + addend) output (GRID rows, pitch ldsum)
     const __half* addend;
     int ldsum, ldadd;
-    int y_phase;
+    int y_phase;       // 0 GRID, 1 PHASE, 2 FPHASE, 3 TPHASE (see row_info)
     int Hp, Wp, T, F;  // output grid: Hp = T+2, Wp = F+2
     // n / (Hp*Wp) and n / Wp as (umulhi(n, mul) + n) >> sh, exact for 0 <= n < 2^31
     uint32_t img_mul, wp_mul;
     int img_sh, wp_sh;
-    int Hq, Wq;        // phase-split output: consumer grid
+    int Hq, Wq;        // phase-split output: consumer grid (TPHASE: rows per clip, F)
+    int ypad;          // TPHASE: padding rows of the consumer's sequence slots
     long long plane_rows;
     const int* tvalid;
     int batch;
@@ -126,6 +127,10 @@ struct ConvDev {
     const float* clip_bias;  // act 3/4: f32 [batch][oc] added before the ReLU
     const float* bn_scale;   // act 3/4: f32 [oc] per-channel affine after the ReLU
     const float* bn_shift;
+    // act 5: y = (acc + bias) * gate[(b*gate_nseg + t/gate_seg)*oc + col] (a per-clip,
+    // per-segment channel gate: the CAM++ context attention)
+    const float* gate;
+    int gate_seg, gate_nseg;
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -164,12 +169,13 @@ struct RowInfo {
     long long dst;    // row of y
     long long dst2;   // row of the PHASE-layout output (y2, or y when y_phase)
     int b;            // clip (1-D geometry)
+    int t;            // frame within the clip (1-D geometry)
     long long refl[2];  // 1-D reflect: padding rows mirroring this row, or -1
 };
 
 template <bool SEQ>
 __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int m, bool live) {
-    RowInfo ri{false, false, (long long)m, 0, 0, {-1, -1}};
+    RowInfo ri{false, false, (long long)m, 0, 0, 0, {-1, -1}};
     if (m >= p.M) return ri;
     ri.in_range = true;
     if constexpr (SEQ) {
@@ -177,8 +183,9 @@ __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int
         const int t = m - b * p.Hp - p.pad;
         const int tvb = min(tv[b], p.T);  // a length past the slot never writes outside it
         ri.b = b;
+        ri.t = t;
         ri.valid = live && t >= 0 && t < tvb;
-        if (p.reflect && ri.valid) {
+        if (p.reflect == 1 && ri.valid) {
             // frame -t mirrors frame t (1 <= t <= pad); frame 2*(tvb-1) - t mirrors
             // frame t when it lands in [tvb, tvb + pad)
             const long long row0 = (long long)b * p.Hp + p.pad;
@@ -194,11 +201,29 @@ __device__ __forceinline__ RowInfo row_info(const ConvDev& p, const int* tv, int
     const int tp = fdiv(r, p.wp_mul, p.wp_sh);
     const int fp = r - tp * p.Wp;
     ri.valid = live && tp >= 1 && tp <= tv[b] && fp >= 1 && fp <= p.F;
-    if (p.y2 || p.y_phase) {
+    if (p.y2 || p.y_phase == 1) {
+        // PHASE: the 4 (time, freq) stride-2 planes of the padded grid
         const int q = ((tp & 1) << 1) | (fp & 1);
         ri.dst2 = (long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
                   (fp >> 1) + 1;
         if (p.y_phase) ri.dst = ri.dst2;
+    } else if (p.y_phase == 2) {
+        // FPHASE: the 2 frequency stride-2 planes, time rows unchanged
+        ri.dst2 = (long long)(fp & 1) * p.plane_rows + ((long long)b * p.Hq + tp) * p.Wq +
+                  (fp >> 1) + 1;
+        ri.dst = ri.dst2;
+    } else if (p.y_phase == 3) {
+        // TPHASE: frame t of pixel (t, f) to plane t&1, sequence row t>>1 of a
+        // time-stride-2 1-D consumer, channels f*oc .. f*oc+oc-1 of that row. The grid
+        // border has no slot there: those rows store nothing.
+        if (tp >= 1 && tp <= p.T && fp >= 1 && fp <= p.F) {
+            const int t = tp - 1;
+            ri.dst2 = (long long)(t & 1) * p.plane_rows +
+                      ((long long)b * p.Hq + p.ypad + (t >> 1)) * p.F + (fp - 1);
+            ri.dst = ri.dst2;
+        } else {
+            ri.in_range = false;
+        }
     }
     return ri;
 }
@@ -254,7 +279,10 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
     }
     if (!ri.in_range) return;
     if constexpr (SEQ) {
-        if (!ri.valid) return;  // 1-D: padding rows hold reflections (or nothing used)
+        // 1-D: padding rows hold reflections (or nothing used), unless the tensor is
+        // zero-padded (reflect 2): then every row of the slots is stored, 0 outside
+        // the valid frames
+        if (!ri.valid && p.reflect != 2) return;
     }
     if (sbias) {
 #pragma unroll
@@ -292,7 +320,20 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         if (p.act == 1) {
 #pragma unroll
             for (int i = 0; i < NC; ++i) f[i] = f[i] / (1.0f + expf(-f[i]));  // SiLU
-        } else if (SEQ && p.act >= 3) {
+        } else if (SEQ && p.act == 5) {
+            if (ri.valid) {
+                const float4* g = reinterpret_cast<const float4*>(
+                    p.gate + ((long long)ri.b * p.gate_nseg + ri.t / p.gate_seg) * p.oc + col);
+#pragma unroll
+                for (int j = 0; j < NC / 4; ++j) {
+                    const float4 g4 = __ldg(g + j);
+                    f[4 * j] *= g4.x;
+                    f[4 * j + 1] *= g4.y;
+                    f[4 * j + 2] *= g4.z;
+                    f[4 * j + 3] *= g4.w;
+                }
+            }
+        } else if (SEQ && (p.act == 3 || p.act == 4)) {
             // TDNN block: BatchNorm(ReLU(acc + bias [+ clip bias])), then tanh for act 4
             const float4* sc = reinterpret_cast<const float4*>(sss + col);
             const float4* sh = reinterpret_cast<const float4*>(sss + p.oc + col);
@@ -386,7 +427,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
             sp[j] = o;
         }
     }
-    if (SEQ && p.reflect) {
+    if (SEQ && p.reflect == 1) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             if (ri.refl[k] < 0) continue;
@@ -966,12 +1007,18 @@ void fill_taps(SegDev& s, int k, int stride, int ic, int Wp_out) {
             const int tap = kt * k + kf;
             if (k == 1) {
                 // 1x1: stride 1 reads the same grid row; stride 2 reads padded
-                // position (2t+1, 2f+1) = plane 3 at the output's own row.
-                s.plane[tap] = (stride == 2) ? 3 : 0;
+                // position (2t+1, 2f+1) = plane 3 at the output's own row; the
+                // frequency-only stride 3 reads (t+1, 2f+1) = plane 1 of FPHASE.
+                s.plane[tap] = (stride == 2) ? 3 : (stride == 3 ? 1 : 0);
                 s.off[tap] = 0;
             } else if (stride == 1) {
                 s.plane[tap] = 0;
                 s.off[tap] = (kt - 1) * Wp_out + (kf - 1);
+            } else if (stride == 3) {
+                // FPHASE: padded input (to + kt, 2*fo + kf) is plane kf&1 at the
+                // output's row shifted by kt - 1 time rows and kf>>1 columns
+                s.plane[tap] = kf & 1;
+                s.off[tap] = (kt - 1) * Wp_out + (kf >> 1);
             } else {
                 s.plane[tap] = ((kt & 1) << 1) | (kf & 1);
                 s.off[tap] = (kt >> 1) * Wp_out + (kf >> 1);
@@ -979,15 +1026,19 @@ void fill_taps(SegDev& s, int k, int stride, int ic, int Wp_out) {
         }
 }
 
-// 1-D taps of a k-wide conv with dilation d: row offsets (j - (k-1)/2) * d.
-void fill_taps_1d(SegDev& s, int k, int dil, int ic) {
+// 1-D taps of a k-wide conv with dilation d: row offsets (j - (k-1)/2) * d. With
+// stride 2 the input is TPHASE (frame u of the input for output frame o is
+// 2*o + u): tap offset u = (j - (k-1)/2) * d reads plane u & 1 at row offset
+// floor(u / 2).
+void fill_taps_1d(SegDev& s, int k, int dil, int ic, int stride = 1) {
     s.ic = ic;
     s.kb = (ic % 64 == 0) ? 64 : ((ic % 32 == 0) ? 32 : 16);
     s.n_kb = ic / s.kb;
     s.n_taps = k;
     for (int j = 0; j < k; ++j) {
-        s.plane[j] = 0;
-        s.off[j] = (j - (k - 1) / 2) * dil;
+        const int u = (j - (k - 1) / 2) * dil;
+        s.plane[j] = stride == 2 ? (u & 1) : 0;
+        s.off[j] = stride == 2 ? (u >> 1) : u;  // arithmetic shift: floor division
     }
 }
 
@@ -995,7 +1046,9 @@ int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 // Extras of the 1-D sequence geometry (vdb_conv1d); nullptr for the 2-D grid.
 struct SeqArgs {
-    int pad, dil0, reflect, y_f32, tile_n, pair;
+    int pad, dil0, reflect, y_f32, tile_n, pair, stride0;
+    const float* gate;
+    int gate_seg, gate_nseg;
     const float* clip_bias;
     const float* bn_scale;
     const float* bn_shift;
@@ -1039,15 +1092,34 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
         set_error("vdb_conv1d: k0 must be odd in [1, 9], dil0 >= 1 and (k0-1)/2 * dil0 <= pad");
         return 1;
     }
-    if (c->act != 0 && c->act != 1 && c->act != 3 && c->act != 4) {
-        set_error("vdb_conv1d: act must be 0, 1, 3 or 4");
+    if (c->act != 0 && c->act != 1 && c->act != 3 && c->act != 4 && c->act != 5) {
+        set_error("vdb_conv1d: act must be 0, 1, 3, 4 or 5");
         return 1;
     }
-    if (c->act >= 3 && (!c->bn_scale || !c->bn_shift)) {
+    if (c->act == 5 && (!c->gate || c->gate_seg < 1 || c->gate_nseg < 1 ||
+                        (c->t - 1) / c->gate_seg >= c->gate_nseg ||
+                        (reinterpret_cast<uintptr_t>(c->gate) & 15u) != 0)) {
+        set_error("vdb_conv1d: act 5 needs a 16-byte aligned gate [batch][gate_nseg][oc] with "
+                  "gate_seg >= 1 and gate_nseg * gate_seg >= t");
+        return 1;
+    }
+    if (c->reflect < 0 || c->reflect > 2 || c->stride0 < 0 || c->stride0 > 2) {
+        set_error("vdb_conv1d: reflect must be 0, 1 or 2 and stride0 0, 1 or 2");
+        return 1;
+    }
+    if (c->stride0 == 2 && c->x1) {
+        set_error("vdb_conv1d: a stride-2 conv takes one input segment");
+        return 1;
+    }
+    if (c->reflect == 2 && c->y_f32) {
+        set_error("vdb_conv1d: zero padding (reflect 2) needs the f16 output");
+        return 1;
+    }
+    if ((c->act == 3 || c->act == 4) && (!c->bn_scale || !c->bn_shift)) {
         set_error("vdb_conv1d: act 3/4 need bn_scale and bn_shift");
         return 1;
     }
-    if (c->clip_bias && c->act < 3) {
+    if (c->clip_bias && c->act != 3 && c->act != 4) {
         set_error("vdb_conv1d: clip_bias needs act 3 or 4");
         return 1;
     }
@@ -1092,7 +1164,8 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
     a.ldsum = c->ldsum;
     a.addend = c->addend;
     a.ldaddend = c->ldaddend;
-    SeqArgs sq{c->pad, c->dil0, c->reflect ? 1 : 0, c->y_f32 ? 1 : 0, c->tile_n, c->pair,
+    SeqArgs sq{c->pad,  c->dil0,     c->reflect,   c->y_f32 ? 1 : 0, c->tile_n,
+               c->pair, c->stride0 == 2 ? 2 : 1, c->gate,    c->gate_seg, c->gate_nseg,
                c->clip_bias, c->bn_scale, c->bn_shift};
     return conv_impl(&a, &sq, stream);
 }
@@ -1115,9 +1188,14 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         set_error("vdb_conv: input channels must be positive multiples of 16");
         return 1;
     }
-    if (!seq && (!(a->k0 == 3 || a->k0 == 1) || !(a->stride0 == 1 || a->stride0 == 2) ||
-                 (a->x1 && !(a->stride1 == 1 || a->stride1 == 2)))) {
+    if (!seq && (!(a->k0 == 3 || a->k0 == 1) || a->stride0 < 1 || a->stride0 > 3 ||
+                 (a->x1 && (a->stride1 < 1 || a->stride1 > 3)))) {
         set_error("vdb_conv: unsupported kernel/stride");
+        return 1;
+    }
+    if (!seq && (a->y_phase < 0 || a->y_phase > 3 || (a->y2 && a->y_phase > 1) ||
+                 (a->y_phase == 3 && (a->y_pad < 1 || a->y_pad > 64)))) {
+        set_error("vdb_conv: y_phase must be 0..3 (y2 only with 0 / 1; 3 needs y_pad in [1, 64])");
         return 1;
     }
     if (!a->x0 || !a->w0 || !a->tvalid || !a->y || (a->x1 && !a->w1)) {
@@ -1184,7 +1262,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     p.BN = BN;
     p.n_seg = a->x1 ? 2 : 1;
     if (seq) {
-        fill_taps_1d(p.seg[0], a->k0, sq->dil0, a->ic0);
+        fill_taps_1d(p.seg[0], a->k0, sq->dil0, a->ic0, sq->stride0);
         if (a->x1) fill_taps_1d(p.seg[1], 1, 1, a->ic1);
     } else {
         fill_taps(p.seg[0], a->k0, a->stride0, a->ic0, Wp);
@@ -1414,8 +1492,17 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     magic_div((uint32_t)Wp, p.wp_mul, p.wp_sh);
     p.T = a->t_out;
     p.F = a->f_out;
-    p.Hq = (a->t_out - 1) / 2 + 1 + 2;
-    p.Wq = (a->f_out - 1) / 2 + 1 + 2;
+    if (a->y_phase == 2) {         // FPHASE for a frequency-stride-2 consumer
+        p.Hq = a->t_out + 2;
+        p.Wq = (a->f_out - 1) / 2 + 1 + 2;
+    } else if (a->y_phase == 3) {  // TPHASE for a time-stride-2 1-D consumer
+        p.ypad = a->y_pad;
+        p.Hq = (a->t_out - 1) / 2 + 1 + 2 * a->y_pad;
+        p.Wq = a->f_out;
+    } else {                       // PHASE
+        p.Hq = (a->t_out - 1) / 2 + 1 + 2;
+        p.Wq = (a->f_out - 1) / 2 + 1 + 2;
+    }
     p.plane_rows = (long long)a->batch * p.Hq * p.Wq;
     p.tvalid = a->tvalid;
     p.batch = a->batch;
@@ -1431,6 +1518,9 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         p.clip_bias = sq->clip_bias;
         p.bn_scale = sq->bn_scale;
         p.bn_shift = sq->bn_shift;
+        p.gate = sq->gate;
+        p.gate_seg = sq->gate_seg;
+        p.gate_nseg = sq->gate_nseg;
         magic_div((uint32_t)Hp, p.img_mul, p.img_sh);
     }
 
@@ -1445,8 +1535,10 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         const int stride = sg ? a->stride1 : a->stride0;
         const int box_rows = s.box_rows;
         const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
-        if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, (!seq && stride == 2) ? 4 : 1, s.kb,
-                        box_rows) ||
+        // planes: PHASE 4, FPHASE 2 (2-D stride 3), TPHASE 2 (1-D stride 2)
+        const int planes = seq ? ((sg == 0 && sq->stride0 == 2) ? 2 : 1)
+                               : (stride == 2 ? 4 : (stride == 3 ? 2 : 1));
+        if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, planes, s.kb, box_rows) ||
             !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, cta_bn, s.kb)) {
             set_error("vdb_conv: cuTensorMapEncodeTiled failed");
             return 1;

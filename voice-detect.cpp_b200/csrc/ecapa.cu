@@ -8,7 +8,9 @@
 //                         (src/encoder.cpp:32-50)
 //   seq_mean_kernel       SE squeeze: per-clip mean over time (src/encoder.cpp:200)
 //   se_apply_kernel       x * gate + block input (:208, :229)
-//   seq_meanstd_kernel    ASP global statistics mean / sqrt(clamp(var, eps)) (:261-264)
+//   seq_meanstd_kernel    ASP global statistics mean / sqrt(clamp(var, eps)) (:261-264);
+//                         with `unbiased`, CAM++'s statistics pooling (mean, std with
+//                         the T/(T-1) correction, no floor: src/encoder_campplus.cpp:283-292)
 //   asp_pool_kernel       softmax over time + attention-weighted mean / std (:280-285)
 //
 // Every kernel reads only a clip's valid frames (t < tvalid[b]); rows outside them
@@ -135,7 +137,7 @@ __global__ void se_apply_kernel(const __half* __restrict__ h, int ldh,
 // valid frames: two passes, like the reference's mean -> sub -> sqr -> mean.
 __global__ void seq_meanstd_kernel(const __half* __restrict__ x, int ldx,
                                    const int* __restrict__ tv, int T, int pad, int C, float eps,
-                                   float* __restrict__ stats) {
+                                   int unbiased, float* __restrict__ stats) {
     __shared__ float red[4][512];
     __shared__ float mean_s[512];
     const int b = blockIdx.x;
@@ -180,7 +182,8 @@ __global__ void seq_meanstd_kernel(const __half* __restrict__ x, int ldx,
     for (int k = threadIdx.x; k < 512; k += 256) {
         const int cc = blockIdx.y * 512 + k;
         if (cc >= C || tvb <= 0) continue;
-        const float var = (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb;
+        float var = (red[0][k] + red[1][k] + red[2][k] + red[3][k]) / tvb;
+        if (unbiased && tvb > 1) var *= (float)tvb / (float)(tvb - 1);
         stats[(long long)b * 2 * C + cc] = mean_s[k];
         stats[(long long)b * 2 * C + C + cc] = sqrtf(fmaxf(var, eps));
     }
@@ -294,7 +297,15 @@ int ecapa_se_apply(const __half* h, int ldh, const float* gate, const __half* re
 int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int pad, int C,
                   float eps, float* stats, cudaStream_t st) {
     const dim3 grid((unsigned)batch, (unsigned)((C + 511) / 512));
-    seq_meanstd_kernel<<<grid, 256, 0, st>>>(x, ldx, tv, T, pad, C, eps, stats);
+    seq_meanstd_kernel<<<grid, 256, 0, st>>>(x, ldx, tv, T, pad, C, eps, 0, stats);
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int seq_meanstd_unbiased(const __half* x, int ldx, const int* tv, int batch, int T, int pad,
+                         int C, float* stats, cudaStream_t st) {
+    const dim3 grid((unsigned)batch, (unsigned)((C + 511) / 512));
+    seq_meanstd_kernel<<<grid, 256, 0, st>>>(x, ldx, tv, T, pad, C, 0.0f, 1, stats);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }

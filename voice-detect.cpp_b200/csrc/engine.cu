@@ -224,7 +224,9 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
         return nullptr;
     }
     // load succeeds for other archs; embed then reports the arch as not implemented
-    if (c.arch != "wespeaker_resnet34" && c.arch != "eres2net" && c.arch != "ecapa_tdnn") return e;
+    if (c.arch != "wespeaker_resnet34" && c.arch != "eres2net" && c.arch != "ecapa_tdnn" &&
+        c.arch != "campplus")
+        return e;
 
     e->plan_ = vdb_fbank_plan_create(c.sample_rate, c.n_mels, c.n_fft, c.win, c.hop, c.preemph,
                                      c.low_freq, c.high_freq);
@@ -238,6 +240,10 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
     }
     if (c.arch == "ecapa_tdnn") {
         if (!e->load_ecapa(g, err)) return nullptr;
+        return e;
+    }
+    if (c.arch == "campplus") {
+        if (!e->load_campplus(g, err) || !e->identity(e->campp_.M, err)) return nullptr;
         return e;
     }
     Loader L{g, err};
@@ -778,7 +784,7 @@ bool Engine::load_eres2net(const Gguf& g, std::string& err) {
 
 bool Engine::supported(std::string& err) const {
     if (cfg_.arch != "wespeaker_resnet34" && cfg_.arch != "eres2net" &&
-        cfg_.arch != "ecapa_tdnn") {
+        cfg_.arch != "ecapa_tdnn" && cfg_.arch != "campplus") {
         err = "voicedetect: arch '" + cfg_.arch + "' is not implemented by the B200 engine";
         return false;
     }
@@ -832,6 +838,8 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     if (!grow((void**)&mean_, mean_bytes_, (size_t)B * cfg_.n_mels * sizeof(float))) return 1;
     if (cfg_.arch == "ecapa_tdnn") {
         if (!grow(&ecapa_ws_, ecapa_ws_bytes_, ecapa_ws_bytes(B, t_max))) return 1;
+    } else if (cfg_.arch == "campplus") {
+        if (!grow(&ecapa_ws_, ecapa_ws_bytes_, campp_ws_bytes(B, t_max))) return 1;
     } else {
         // pooling input: the last level's frequency extent and channels
         const int lev = cfg_.arch == "eres2net" ? e_out_level_ : (int)levels_.size() - 1;
@@ -981,6 +989,7 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
     }
     prof_end(pf, st, 0.0);
     if (cfg_.arch == "ecapa_tdnn") return run_ecapa(B, t_max, tv_sum, st, d_out, launches, err);
+    if (cfg_.arch == "campplus") return run_campplus(B, t_max, tv_sum, st, d_out, launches, err);
     const int ps = prof_begin(st, 4);
     const bool eres = cfg_.arch == "eres2net";
     if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,

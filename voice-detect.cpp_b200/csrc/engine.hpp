@@ -95,6 +95,52 @@ struct EcapaDev {
     float* fc_b = nullptr;
 };
 
+// CAM++ (src/encoder_campplus.cpp). FCM 2-D convs: f16 [oc][kt*k + kf][ic] + bias
+// (BN folded; the stride-2 block's conv2 bias includes its shortcut's).
+struct Fcm2dDev {
+    int ic = 0, oc = 0, k = 3;
+    __half* w = nullptr;
+    float* b = nullptr;
+};
+
+struct CamppStageDev {
+    Fcm2dDev c1, c2, c3, c4;    // stride-2 block conv1 / conv2, stride-1 block conv1 / conv2
+    __half* sc_w = nullptr;     // stride-2 block 1x1 shortcut [oc][ic]
+};
+
+struct CamppLayerDev {
+    int c_in = 0;
+    float* bn_scale = nullptr;  // nonlinear1 BN over c_in channels
+    float* bn_shift = nullptr;
+    TdnnDev lin1;               // 1x1 c_in -> bnc, bias, ReLU
+    TdnnDev local;              // k=3 dilated bnc -> growth, no bias, * CAM gate
+    float* cam_w1 = nullptr;    // [cam_m][bnc]
+    float* cam_b1 = nullptr;
+    float* cam_w2 = nullptr;    // [growth][cam_m]
+    float* cam_b2 = nullptr;
+};
+
+struct CamppBlockDev {
+    int dil = 1, c0 = 0, cmax = 0;
+    std::vector<CamppLayerDev> layers;
+    float* tr_scale = nullptr;  // transit BN over cmax
+    float* tr_shift = nullptr;
+    TdnnDev transit;            // 1x1 cmax -> cmax/2
+};
+
+struct CamppDev {
+    int M = 0, f_out = 0, bnc = 0, growth = 0, cam_m = 0, c_out = 0;
+    int pad = 2;                // SEQ padding rows at the TDNN rate (>= the widest dilation)
+    float* stem_w = nullptr;    // [M][9], tap kt*3 + kf
+    float* stem_b = nullptr;
+    CamppStageDev stages[2];
+    Fcm2dDev fcm_out;           // FCM conv2 (freq stride 2)
+    TdnnDev tdnn;               // k=5 time stride 2, columns f*M + c
+    std::vector<CamppBlockDev> blocks;
+    float* fc_w = nullptr;      // [emb][2*c_out], output BN folded
+    float* fc_b = nullptr;
+};
+
 struct EBuf {
     int level = 0, c = 0;
     bool phase = false;      // P layout (for a stride-2 consumer) instead of G
@@ -171,6 +217,10 @@ private:
                   float* d_out, long long& launches, std::string& err);
     size_t ecapa_ws_bytes(int B, int t_max) const;
     size_t ecapa_gemm_scratch(int B) const;
+    bool load_campplus(const Gguf& g, std::string& err);
+    int run_campplus(int B, int t_max, const std::vector<long long>& tv_sum, cudaStream_t st,
+                     float* d_out, long long& launches, std::string& err);
+    size_t campp_ws_bytes(int B, int t_max) const;
     bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
     bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
     // f16 identity [c][c]: an identity shortcut added on the tensor cores as a 1x1
@@ -209,7 +259,8 @@ private:
     };
     std::vector<GraphEntry> graphs_;
     bool graphs_enabled_ = true;
-    // ECAPA-TDNN weights and its workspace (carved per bucket shape)
+    // ECAPA-TDNN / CAM++ weights; their workspace (ecapa_ws_) is carved per bucket shape
+    CamppDev campp_;
     EcapaDev ecapa_;
     void* ecapa_ws_ = nullptr;
     size_t ecapa_ws_bytes_ = 0;

@@ -53,7 +53,8 @@ template <int OC>
 __global__ void __launch_bounds__(256)
 stem_kernel(const float* __restrict__ feats, const int* __restrict__ frames,
             const float* __restrict__ mean, int batch, int t_max, int n_mels, int cmn,
-            const float* __restrict__ w, const float* __restrict__ bias, __half* __restrict__ y) {
+            const float* __restrict__ w, const float* __restrict__ bias, __half* __restrict__ y,
+            int fphase) {
     constexpr int G = OC / 8;
     constexpr int PPB = 256 / G;  // pixels per block step
     __shared__ float sx[(kStemRows + 2) * 130];
@@ -116,7 +117,15 @@ stem_kernel(const float* __restrict__ feats, const int* __restrict__ frames,
         v.y = *reinterpret_cast<uint32_t*>(&h1);
         v.z = *reinterpret_cast<uint32_t*>(&h2);
         v.w = *reinterpret_cast<uint32_t*>(&h3);
-        yb[(long long)q * G + g] = v;
+        if (fphase) {
+            // FPHASE output for a frequency-stride-2 consumer (vdb_ops.h)
+            const int Wq = (n_mels - 1) / 2 + 1 + 2;
+            const long long dst = (long long)(fp & 1) * batch * Hp * Wq +
+                                  ((long long)b * Hp + tp) * Wq + (fp >> 1) + 1;
+            reinterpret_cast<uint4*>(y)[dst * G + g] = v;
+        } else {
+            yb[(long long)q * G + g] = v;
+        }
     }
 }
 
@@ -397,6 +406,13 @@ using namespace vdb;
 extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, int t_max,
                             int n_mels, int cmn, const float* stem_w, const float* stem_b,
                             int oc, float* mean_scratch, void* y, void* stream) {
+    return vdb::cmn_stem_launch(feats, frames, batch, t_max, n_mels, cmn, stem_w, stem_b, oc,
+                                mean_scratch, y, 0, static_cast<cudaStream_t>(stream));
+}
+
+int vdb::cmn_stem_launch(const float* feats, const int* frames, int batch, int t_max,
+                         int n_mels, int cmn, const float* stem_w, const float* stem_b, int oc,
+                         float* mean_scratch, void* y, int fphase, cudaStream_t stream) {
     if (!feats || !frames || !stem_w || !stem_b || !y || (cmn && !mean_scratch)) {
         set_error("vdb_cmn_stem: NULL argument");
         return 1;
@@ -406,7 +422,7 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
         set_error("vdb_cmn_stem: bad shape");
         return 1;
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaStream_t st = stream;
     if (cmn) {
         cmn_mean_kernel<<<batch, dim3(128, 4), 0, st>>>(feats, frames, t_max, n_mels,
                                                        mean_scratch);
@@ -418,15 +434,15 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
     switch (oc) {
         case 16:
             stem_kernel<16><<<blocks, threads, 0, st>>>(feats, frames, mean_scratch, batch, t_max,
-                                                        n_mels, cmn, stem_w, stem_b, yh);
+                                                        n_mels, cmn, stem_w, stem_b, yh, fphase);
             break;
         case 32:
             stem_kernel<32><<<blocks, threads, 0, st>>>(feats, frames, mean_scratch, batch, t_max,
-                                                        n_mels, cmn, stem_w, stem_b, yh);
+                                                        n_mels, cmn, stem_w, stem_b, yh, fphase);
             break;
         case 64:
             stem_kernel<64><<<blocks, threads, 0, st>>>(feats, frames, mean_scratch, batch, t_max,
-                                                        n_mels, cmn, stem_w, stem_b, yh);
+                                                        n_mels, cmn, stem_w, stem_b, yh, fphase);
             break;
         default:
             set_error("vdb_cmn_stem: stem channels must be 16, 32 or 64");
@@ -550,13 +566,13 @@ extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int b
     __half* yh = static_cast<__half*>(y);
     if (oc == 16)
         stem_kernel<16><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
-                                                    cmn, stem_w, stem_b, yh);
+                                                    cmn, stem_w, stem_b, yh, 0);
     else if (oc == 32)
         stem_kernel<32><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
-                                                    cmn, stem_w, stem_b, yh);
+                                                    cmn, stem_w, stem_b, yh, 0);
     else
         stem_kernel<64><<<blocks, threads, 0, st>>>(feats, frames, means, batch, t_max, n_mels,
-                                                    cmn, stem_w, stem_b, yh);
+                                                    cmn, stem_w, stem_b, yh, 0);
     VDB_CHECK_CUDA(cudaGetLastError());
     return 0;
 }

@@ -41,6 +41,12 @@ int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
                     const int* out_rows, float* emb_out, float* prenorm_out, float* part,
                     cudaStream_t stream);
 
+// CMN + stem of vdb_cmn_stem with the output in GRID (fphase 0) or FPHASE (fphase 1,
+// for a frequency-stride-2 consumer: CAM++'s FCM) layout.
+int cmn_stem_launch(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                    int cmn, const float* stem_w, const float* stem_b, int oc,
+                    float* mean_scratch, void* y, int fphase, cudaStream_t stream);
+
 // ECAPA-TDNN glue kernels on the SEQ layout (ecapa.cu). tv: device int32 [batch]
 // valid frames; T and pad describe the SEQ tensors; ld* are row pitches.
 int ecapa_cmn_pack(const float* feats, const int* frames, int batch, int t_max, int n_mels,
@@ -62,6 +68,19 @@ int ecapa_meanstd(const __half* x, int ldx, const int* tv, int batch, int T, int
 int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const float* stats,
                    const int* tv, int batch, int T, int pad, int C, float eps, float* pooled,
                    cudaStream_t st);
+
+// CAM++ (campplus.cu): mean / std pooling with the unbiased variance and no floor
+// (ecapa.cu's kernel), BN + ReLU of a channel prefix over `rows` SEQ rows, and the
+// CAM gate [batch][nseg_max][G] = sigmoid(w2 . ReLU(w1 . ctx + b1) + b2) per 100-frame
+// segment (w1 [M][C], w2 [G][M] f32).
+int seq_meanstd_unbiased(const __half* x, int ldx, const int* tv, int batch, int T, int pad,
+                         int C, float* stats, cudaStream_t st);
+int campp_bn_relu(const __half* h, int ldh, int C, const float* scale, const float* shift,
+                  long long rows, __half* a, int lda, cudaStream_t st);
+size_t campp_gate_smem(int C, int M, int nseg_max);
+int campp_cam_gate(const __half* cc, int ldc, const int* tv, int batch, int T, int pad, int C,
+                   int seg, int nseg_max, const float* w1, const float* b1, int M,
+                   const float* w2, const float* b2, int G, float* gate, cudaStream_t st);
 
 }  // namespace vdb
 

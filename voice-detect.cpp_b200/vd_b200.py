@@ -43,7 +43,7 @@ class ConvArgs(C.Structure):
         ("ksplit", C.c_int), ("ldx0", C.c_int), ("ldx1", C.c_int), ("ldy", C.c_int),
         ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
         ("act", C.c_int), ("ysum", C.c_void_p), ("ldsum", C.c_int), ("addend", C.c_void_p),
-        ("ldaddend", C.c_int),
+        ("ldaddend", C.c_int), ("y_pad", C.c_int),
     ]
 
 
@@ -57,7 +57,8 @@ class Conv1dArgs(C.Structure):
         ("residual", C.c_void_p), ("ldr", C.c_int), ("tvalid", C.c_void_p), ("y", C.c_void_p),
         ("ldy", C.c_int), ("y_f32", C.c_int), ("reflect", C.c_int), ("ysum", C.c_void_p),
         ("ldsum", C.c_int), ("addend", C.c_void_p), ("ldaddend", C.c_int), ("err", C.c_void_p),
-        ("tile_m", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int),
+        ("tile_m", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int), ("stride0", C.c_int),
+        ("gate", C.c_void_p), ("gate_seg", C.c_int), ("gate_nseg", C.c_int),
     ]
 
 
@@ -401,6 +402,62 @@ def from_phase(p, B: int, C_: int, F: int, T: int):
     return pad[:, 1:T + 1, 1:F + 1, :].permute(0, 3, 2, 1).float().contiguous()
 
 
+def to_fphase(x, tvalid=None):
+    """(B, C, F, T) -> FPHASE f16 tensor (2*B*(T+2)*(Fo+2), C) for a consumer that
+    strides 2 along frequency only."""
+    import torch
+    B, Cc, F, T = x.shape
+    Fo = out_extent(F, 2)
+    pad = torch.zeros(B, T + 2, F + 2, Cc, dtype=torch.float16, device=x.device)
+    pad[:, 1:T + 1, 1:F + 1, :] = x.permute(0, 3, 2, 1).to(torch.float16)
+    if tvalid is not None:
+        for b, tv in enumerate(tvalid):
+            pad[b, 1 + int(tv):, :, :] = 0
+    out = torch.zeros(2, B, T + 2, Fo + 2, Cc, dtype=torch.float16, device=x.device)
+    for pf in range(2):
+        src = pad[:, :, pf::2, :]
+        out[pf, :, :, 1:1 + src.shape[2], :] = src
+    return out.reshape(-1, Cc).contiguous()
+
+
+def from_fphase(p, B: int, C_: int, F: int, T: int):
+    """FPHASE tensor of a (B, C, F, T) activation -> (B, C, F, T) float32."""
+    import torch
+    Fo = out_extent(F, 2)
+    pl = p.reshape(2, B, T + 2, Fo + 2, C_)
+    pad = torch.zeros(B, T + 2, F + 2, C_, dtype=p.dtype, device=p.device)
+    for pf in range(2):
+        nf = len(range(pf, F + 2, 2))
+        pad[:, :, pf::2, :] = pl[pf, :, :, 1:1 + nf, :]
+    return pad[:, 1:T + 1, 1:F + 1, :].permute(0, 3, 2, 1).float().contiguous()
+
+
+def from_tphase(tp, B: int, C_: int, T: int, pad: int):
+    """TPHASE (2*B*(To+2*pad), C) of a T-frame sequence -> (B, C, T) float32."""
+    To = out_extent(T, 2)
+    pl = tp.reshape(2, B, To + 2 * pad, C_)
+    out = pl.new_zeros(B, T, C_)
+    out[:, 0::2] = pl[0, :, pad:pad + len(range(0, T, 2))]
+    out[:, 1::2] = pl[1, :, pad:pad + len(range(1, T, 2))]
+    return out.permute(0, 2, 1).float().contiguous()
+
+
+def to_tphase(x, pad: int, tvalid=None):
+    """(B, C, T) float -> TPHASE f16 (2*B*(To+2*pad), C), To = (T-1)//2+1, zero
+    outside each clip's valid frames."""
+    import torch
+    B, Cc, T = x.shape
+    To = out_extent(T, 2)
+    out = torch.zeros(2, B, To + 2 * pad, Cc, dtype=torch.float16, device=x.device)
+    for b in range(B):
+        tv = T if tvalid is None else int(tvalid[b])
+        xb = x[b, :, :tv].t().to(torch.float16)
+        ev, od = xb[0::2], xb[1::2]
+        out[0, b, pad:pad + ev.shape[0]] = ev
+        out[1, b, pad:pad + od.shape[0]] = od
+    return out.reshape(-1, Cc).contiguous()
+
+
 def pack_conv_weight(w):
     """torch (OC, IC, KF, KT) -> f16 (OC, KT*KF, IC) (tap = kt*k + kf)."""
     OC, IC, KF, KT = w.shape
@@ -420,19 +477,30 @@ def _ptr(t):
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
          y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
-         y2=None, residual2=None, act=0, ysum=None, addend=None):
+         y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0):
     """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
     tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
     the row pitch is taken from the view's stride); y2 is an extra PHASE output,
     w0 f16 (OC, k*k, IC), w1 f16 (OC, IC1), bias f32 (OC,) or None, tvalid int32 (B,).
     act: 0 = [+residual] then relu/clamp, 1 = SiLU, 2 = attentional fusion
     (residual + residual2) + tanh(acc + bias) * (residual - residual2).
-    ysum / addend: optional second GRID output ysum = f16(y + addend)."""
+    ysum / addend: optional second GRID output ysum = f16(y + addend).
+    stride 3 / y_phase 2: the frequency-only stride-2 input / output (FPHASE);
+    y_phase 3: a TPHASE output for a time-stride-2 1-D consumer with y_pad padding
+    rows, shaped (2*B*(To+2*y_pad), f_out*oc)."""
     import torch
     if y is None:
-        rows = (lib().vdb_phase_rows(batch, t_out, f_out) if y_phase
-                else lib().vdb_grid_rows(batch, t_out, f_out))
-        y = torch.empty(rows, oc, dtype=torch.float16, device=x0.device)
+        yp = int(y_phase)
+        if yp == 3:
+            To = out_extent(t_out, 2)
+            y = torch.zeros(2 * batch * (To + 2 * y_pad), f_out * oc, dtype=torch.float16,
+                            device=x0.device)
+        else:
+            rows = (lib().vdb_phase_rows(batch, t_out, f_out) if yp == 1
+                    else 2 * batch * (t_out + 2) * (out_extent(f_out, 2) + 2) if yp == 2
+                    else lib().vdb_grid_rows(batch, t_out, f_out))
+            y = torch.empty(rows, oc, dtype=torch.float16, device=x0.device)
+    ldy = 0 if int(y_phase) == 3 else _ld(y)
     a = ConvArgs(batch=batch, t_out=t_out, f_out=f_out, oc=oc, k0=k0, stride0=stride0,
                  ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(),
                  w0=w0.data_ptr(), stride1=stride1,
@@ -440,10 +508,10 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  x1=_ptr(x1), w1=_ptr(w1), bias=_ptr(bias), residual=_ptr(residual),
                  relu=int(relu), clamp_hi=float(clamp_hi), tvalid=tvalid.data_ptr(),
                  y=y.data_ptr(), y_phase=int(y_phase), err=_ptr(err), tile_m=tile_m,
-                 halo=halo, ksplit=ksplit, ldx0=_ld(x0), ldx1=_ld(x1), ldy=_ld(y),
+                 halo=halo, ksplit=ksplit, ldx0=_ld(x0), ldx1=_ld(x1), ldy=ldy,
                  y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
                  ldr2=_ld(residual2), act=int(act), ysum=_ptr(ysum), ldsum=_ld(ysum),
-                 addend=_ptr(addend), ldaddend=_ld(addend))
+                 addend=_ptr(addend), ldaddend=_ld(addend), y_pad=int(y_pad))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
@@ -483,12 +551,15 @@ def pack_conv1d_weight(w):
 def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x1=None,
            w1=None, ic1=None, bn_scale=None, bn_shift=None, clip_bias=None, act=0, relu=False,
            residual=None, y=None, y_f32=False, reflect=False, ysum=None, addend=None, err=None,
-           stream=None, tile_m=0, tile_n=0, pair=0):
+           stream=None, tile_m=0, tile_n=0, pair=0, stride0=1, gate=None, gate_seg=0,
+           gate_nseg=0):
     """vdb_conv1d on device tensors: x0/x1/residual/y/ysum/addend are SEQ tensors
     (rows, C) or channel-slice views of wider ones; w0 f16 (OC, K, IC), w1 f16
     (OC, IC1); bias / bn_scale / bn_shift f32 (OC,); clip_bias f32 (B, OC).
     act: 0 = acc + bias [+ residual] (then ReLU if relu), 1 = SiLU,
-    3 = BN(ReLU(acc + bias + clip_bias)), 4 = tanh of act 3."""
+    3 = BN(ReLU(acc + bias + clip_bias)), 4 = tanh of act 3, 5 = (acc + bias) *
+    gate[b, t // gate_seg] with gate f32 (B, gate_nseg, OC). reflect: 0 / False valid
+    frames only, 1 / True reflection rows, 2 zero padding. stride0 2: x0 is TPHASE."""
     import torch
     if y is None:
         rows = lib().vdb_seq_rows(batch, t, pad)
@@ -504,7 +575,8 @@ def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x
                    tvalid=tvalid.data_ptr(), y=y.data_ptr(), ldy=_ld(y), y_f32=int(y_f32),
                    reflect=int(reflect), ysum=_ptr(ysum), ldsum=_ld(ysum), addend=_ptr(addend),
                    ldaddend=_ld(addend), err=_ptr(err), tile_m=tile_m, tile_n=tile_n,
-                   pair=pair)
+                   pair=pair, stride0=int(stride0), gate=_ptr(gate), gate_seg=int(gate_seg),
+                   gate_nseg=int(gate_nseg))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv1d(C.byref(a), C.c_void_p(s)), "vdb_conv1d")
     return y
