@@ -506,6 +506,7 @@ def run_latency(args) -> int:
 
 ERES_METRIC = "utterance-sec/sec ERes2Net-base embed"
 ECAPA_METRIC = "utterance-sec/sec ECAPA-TDNN embed"
+CAMPP_METRIC = "utterance-sec/sec CAM++ embed"
 
 
 def cpu_reference_eres2net(m: dict, clips, threads: int):
@@ -522,21 +523,24 @@ def cpu_reference_eres2net(m: dict, clips, threads: int):
     return sum(len(c) for c in clips) / SR, time.perf_counter() - t0
 
 
-def cpu_port_ecapa(m: dict, clips, threads: int):
+def cpu_port_ecapa(m: dict, clips, threads: int, embed=None):
     """The numpy ECAPA oracle (oracle/ecapa.py, a restatement of src/encoder.cpp:
     the reference's ECAPA graph needs the absent ggml library) + the oracle FBank on
-    `clips`, float32 matmuls on `threads` BLAS threads; (audio_seconds, wall_seconds)."""
+    `clips`, float32 matmuls on `threads` BLAS threads; (audio_seconds, wall_seconds).
+    `embed` swaps in another numpy encoder (the CAM++ one, oracle/campplus.py)."""
     import oracle
+    if embed is None:
+        embed = oracle.ecapa_embed
     try:
         from threadpoolctl import threadpool_limits
     except ImportError:  # pragma: no cover
         threadpool_limits = None
     ctx = threadpool_limits(limits=threads) if threadpool_limits else None
     try:
-        oracle.ecapa_embed(m, oracle.fbank(clips[0][:16000]))
+        embed(m, oracle.fbank(clips[0][:16000]))
         t0 = time.perf_counter()
         for c in clips:
-            oracle.ecapa_embed(m, oracle.fbank(c))
+            embed(m, oracle.fbank(c))
         return sum(len(c) for c in clips) / SR, time.perf_counter() - t0
     finally:
         if ctx is not None:
@@ -544,7 +548,8 @@ def cpu_port_ecapa(m: dict, clips, threads: int):
 
 
 class _Family:
-    """One fixed-batch benchmark config: BASELINE config 2 (ERes2Net) or 3 (ECAPA)."""
+    """One fixed-batch benchmark config: BASELINE config 2 (ERes2Net), 3 (ECAPA), or
+    CAM++ (the reference topology, no BASELINE config of its own)."""
 
     def __init__(self, name: str, args):
         self.name = name
@@ -552,23 +557,34 @@ class _Family:
         if name == "eres2net":
             self.metric, self.seconds, self.batch = ERES_METRIC, 10, args.eres_batch
             self.gguf_name, self.ref_clips = "eres2net_f16.gguf", args.ref_eres_clips
+        elif name == "campplus":
+            self.metric, self.seconds, self.batch = CAMPP_METRIC, 4, args.campplus_batch
+            self.gguf_name, self.ref_clips = "campplus_f16.gguf", args.ref_ecapa_clips
         else:
             self.metric, self.seconds, self.batch = ECAPA_METRIC, 4, args.ecapa_batch
             self.gguf_name, self.ref_clips = "ecapa_f16.gguf", args.ref_ecapa_clips
 
     def model(self):
-        return vd_synth.eres2net_model(SEED) if self.name == "eres2net" else \
-            vd_synth.ecapa_model(SEED)
+        if self.name == "eres2net":
+            return vd_synth.eres2net_model(SEED)
+        if self.name == "campplus":
+            return vd_synth.campplus_model(SEED)
+        return vd_synth.ecapa_model(SEED)
 
     def write(self, path, m):
         if self.name == "eres2net":
             vd_synth.write_eres2net_gguf(path, m, "f16")
+        elif self.name == "campplus":
+            vd_synth.write_campplus_gguf(path, m, "f16")
         else:
             vd_synth.write_ecapa_gguf(path, m, "f16")
 
     def weights_as_loaded(self, m):
-        return vd_synth.quantize_model_f16(m) if self.name == "eres2net" else \
-            vd_synth.quantized_ecapa_model(m, "f16")
+        if self.name == "eres2net":
+            return vd_synth.quantize_model_f16(m)
+        if self.name == "campplus":
+            return vd_synth.f16_campplus_model(m)
+        return vd_synth.quantized_ecapa_model(m, "f16")
 
     def cpu(self, m, clips, threads):
         """(audio_s, wall_s, kind, sample description)"""
@@ -578,6 +594,12 @@ class _Family:
                 f"{len(clips)} x 10 s clips per step; reference FBank + blocked directconv "
                 "kernels compiled unmodified (oracle/_ref), restated ERes2Net glue, all host "
                 "threads")
+        if self.name == "campplus":
+            import oracle
+            audio, wall = cpu_port_ecapa(m, clips, threads, oracle.campplus_embed)
+            return audio, wall, "port", (
+                f"{len(clips)} x 4 s clips per step; numpy restatement of "
+                "src/encoder_campplus.cpp (float32 BLAS matmuls) + oracle FBank, all host threads")
         audio, wall = cpu_port_ecapa(m, clips, threads)
         return audio, wall, "port", (
             f"{len(clips)} x 4 s clips per step; numpy restatement of src/encoder.cpp "
@@ -586,6 +608,8 @@ class _Family:
     def config(self, world):
         if self.name == "eres2net":
             return eres_config(self.args, world)
+        if self.name == "campplus":
+            return campplus_config(self.args, world)
         return ecapa_config(self.args, world)
 
 
@@ -746,6 +770,16 @@ def ecapa_config(args, world):
             "parallelism": f"dp{world}", "l2_flush": "activations larger than L2"}
 
 
+def campplus_config(args, world):
+    return {"workload": f"CAM++ f16 embed, batch {args.campplus_batch} x 4 s clips "
+                        "(398 frames) per GPU",
+            "model": "campplus (FCM 32 ch, TDNN 320->128 k5 s2, dense blocks 12/24/16 growth "
+                     "32 bottleneck 128 dil 1/2/2, transits 256/512/512, stats, 192-d; "
+                     "synthetic calibrated weights, f16)",
+            "global_batch": world * args.campplus_batch, "seq_len": "4 s (398 frames)",
+            "parallelism": f"dp{world}", "l2_flush": "activations larger than L2"}
+
+
 def eres_config(args, world):
     return {"workload": f"BASELINE config 2: ERes2Net-base f16 embed, batch {args.eres_batch} "
                         "x 10 s clips (998 frames) per GPU",
@@ -856,6 +890,9 @@ def main() -> int:
                     help="BASELINE config 3: ECAPA-TDNN f16, batch of 4 s clips")
     ap.add_argument("--ecapa-batch", type=int, default=512)
     ap.add_argument("--ref-ecapa-clips", type=int, default=32)
+    ap.add_argument("--campplus", action="store_true",
+                    help="CAM++ (reference topology) f16, batch of 4 s clips")
+    ap.add_argument("--campplus-batch", type=int, default=512)
     args = ap.parse_args()
     if args.op_sweep:
         return run_sweep(args)
@@ -863,6 +900,8 @@ def main() -> int:
         return run_eres2net(args)
     if args.ecapa:
         return run_eres2net(args, "ecapa")
+    if args.campplus:
+        return run_eres2net(args, "campplus")
     if args.latency:
         return run_latency(args)
     if args.impl == "reference":
