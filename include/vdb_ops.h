@@ -188,6 +188,12 @@ typedef struct vdb_conv1d_args {
     const float* gate;      /* act 5: device f32 [B][gate_nseg][oc], 16-byte aligned */
     int gate_seg;           /* act 5: frames per gate segment */
     int gate_nseg;          /* act 5: segments per clip in `gate` (>= ceil(T / gate_seg)) */
+    const float* x_scale;   /* optional input prologue (1x1, one segment, no CTA pair): the
+                               conv reads max(x0 * x_scale[c] + x_shift[c], 0) rounded to
+                               f16 (scale and shift rounded to f16 first) instead of x0 (a
+                               BatchNorm + ReLU on its input); device f32 [ic0], 16-byte
+                               aligned, or NULL */
+    const float* x_shift;
 } vdb_conv1d_args;
 
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);

@@ -6,7 +6,9 @@ float32 convs on ragged batches, gate rel-L2 <= 1e-3:
     with the fused 1x1 shortcut as a second segment and an FPHASE output (y_phase 2);
   * the FCM's last conv writing the TDNN's time-phase input (y_phase 3);
   * the TDNN conv with time stride 2 over that input, zero-padded output (reflect 2);
-  * the CAM layer's dilated conv with the per-segment gate in its epilogue (act 5).
+  * the CAM layer's dilated conv with the per-segment gate in its epilogue (act 5);
+  * the dense layers' 1x1 convs with the BatchNorm + ReLU of their input applied to
+    the A tiles in shared memory (the input prologue).
 
 End to end through the C ABI: PCM -> FBank -> CMN -> FCM -> TDNN -> dense blocks
 -> statistics pooling -> dense head -> L2 against the numpy oracle
@@ -165,6 +167,37 @@ def test_cam_gate_conv(cuda_lib, dil):
         assert torch.count_nonzero(ys[i, P + t:, 96:]) == 0
         assert torch.count_nonzero(ys[i, :P, 96:]) == 0
         assert torch.all(ys[i, :, :96] == 3.0)
+
+
+@pytest.mark.parametrize("ic,ld", [(192, 256), (160, 160), (48, 64), (992, 1024)])
+def test_conv1x1_bn_relu_prologue(cuda_lib, ic, ld):
+    """Dense-layer 1x1 conv reading the first `ic` channels of a wider feature tensor
+    with BN + ReLU applied to its A tiles in shared memory (64 / 32 / 16-channel K
+    blocks, i.e. every TMA swizzle width). The prologue rounds scale and shift to f16
+    and computes one f16 fused multiply-add with ReLU; the reference here is f32."""
+    import torch
+    import torch.nn.functional as Fn
+    vd = cuda_lib
+    g = torch.Generator().manual_seed(ic)
+    B, T, P, oc = 3, 70, 2, 128
+    tv = [T, 51, 3]
+    x = _mask_t(torch.randn(B, ld, T, generator=g), tv).half().float()
+    sc = torch.rand(ic, generator=g) + 0.5
+    sh = torch.randn(ic, generator=g) * 0.3
+    w = (torch.randn(oc, ic, 1, generator=g) * (2.0 / ic) ** 0.5).half().float()
+    b = torch.randn(oc, generator=g) * 0.1
+    a = torch.relu(x[:, :ic] * sc[None, :, None] + sh[None, :, None])
+    dev = torch.device("cuda")
+    tvd = torch.tensor(tv, dtype=torch.int32, device=dev)
+    xs = vd.to_seq(x, P, tv, reflect=False).to(dev)
+    y = vd.conv1d(xs[:, :ic], vd.pack_conv1d_weight(w).to(dev), b.to(dev), tvd, batch=B, t=T,
+                  pad=P, oc=oc, relu=True, reflect=2, x_scale=sc.to(dev), x_shift=sh.to(dev))
+    torch.cuda.synchronize()
+    ys = y.float().cpu().reshape(B, T + 2 * P, oc)
+    for i, t in enumerate(tv):
+        r = torch.relu(Fn.conv1d(a[i:i + 1, :, :t], w, b))[0]
+        assert _rel(ys[i, P:P + t].t(), r) <= REL_TOL, i
+        assert torch.count_nonzero(ys[i, P + t:]) == 0
 
 
 def test_conv1d_gate_needs_segments(cuda_lib):

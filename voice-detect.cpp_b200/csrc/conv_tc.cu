@@ -131,6 +131,13 @@ struct ConvDev {
     // per-segment channel gate: the CAM++ context attention)
     const float* gate;
     int gate_seg, gate_nseg;
+    // 1-D input prologue (xform != 0, 1x1 single-segment TAP convs): warps 2-3 rewrite
+    // each landed A tile in shared memory as f16(max(x * x_scale[c] + x_shift[c], 0))
+    // per input channel c before the MMAs read it (a BatchNorm + ReLU on the conv's
+    // input, applied on the fly instead of in a separate pass over the tensor)
+    int xform;
+    const float* x_scale;
+    const float* x_shift;
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -583,7 +590,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const uint32_t bar_tfull = bar_empty + 8 * S;
     const uint32_t bar_tempty = bar_tfull + 16;
     const uint32_t bar_bres = bar_tempty + 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.bar_off + 8 * (2 * S + 5));
+    const uint32_t bar_xfull = bar_bres + 8;  // [S]: stage transformed (xform)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + p.bar_off + 8 * (3 * S + 5));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -601,6 +609,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
+            mbar_init(bar_xfull + 8 * s, 2);  // one arrival per transform warp
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(bar_tfull + 8 * a, 1);
@@ -845,8 +854,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         }
                         continue;
                     }
+                    // with the input prologue, a stage is ready once both transform
+                    // warps have rewritten it (they wait for its TMA bytes themselves)
+                    const uint32_t ready = p.xform ? bar_xfull : bar_full;
                     for (int it = 0; it < iters; ++it) {
-                        if (!mbar_wait(bar_full + 8 * stage, phase, p.err, VDB_ERR_TIMEOUT_FULL,
+                        if (!mbar_wait(ready + 8 * stage, phase, p.err, VDB_ERR_TIMEOUT_FULL,
                                        abort_flag)) {
                             ok = false;
                             break;
@@ -888,6 +900,67 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                     const uint32_t last = (stage + S - 1) % S;
                     mbar_wait_drain(bar_empty + 8 * last, phase ^ (stage == 0 ? 1u : 0u),
                                     20000000ull);
+                }
+            }
+        }
+    } else if (warp == 2 || warp == 3) {
+        if constexpr (SEQ && !PAIR) {
+            if (p.xform) {
+                // ---------------- input prologue (BN + ReLU of the A tiles) ----------
+                // Thread t owns the 16-byte chunks at byte offsets t*16 + 1024*k of each
+                // A tile. The tile is 1024-byte aligned and the TMA swizzle XORs the
+                // chunk index within a row with address bits [7, 10), so every chunk a
+                // thread owns holds the same 8 input channels: chunk ((t ^ (t >> 3)) &
+                // (row chunks - 1)) of the row.
+                const SegDev& s = p.seg[0];
+                const int t = (int)threadIdx.x - 64;
+                const uint32_t rowbytes = (uint32_t)s.kb * 2;
+                const uint32_t o0 = (uint32_t)t * 16u;
+                const int lchunk = (int)(((o0 >> 4) ^ (o0 >> 7)) & (rowbytes / 16 - 1));
+                const uint32_t a_bytes = (uint32_t)(s.n_box * s.box_rows) * rowbytes;
+                uint32_t stage = 0, phase = 0;
+                bool ok = true;
+                for (int tile = first_tile<false>(); tile < n_tiles && ok;
+                     tile += tile_stride<false>()) {
+                    const int mt = tile / p.n_nt;
+                    if (!tile_live<SEQ>(p, stv, mt * p.BM)) continue;
+                    for (int it = 0; it < s.n_kb; ++it) {
+                        if (!mbar_wait(bar_full + 8 * stage, phase, p.err, VDB_ERR_TIMEOUT_XFORM,
+                                       abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        const int c0 = it * s.kb + lchunk * 8;
+                        const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.x_scale + c0));
+                        const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.x_scale + c0 + 4));
+                        const float4 h0 = __ldg(reinterpret_cast<const float4*>(p.x_shift + c0));
+                        const float4 h1 = __ldg(reinterpret_cast<const float4*>(p.x_shift + c0 + 4));
+                        // f16x2 fused multiply-add with ReLU (one rounding of the exact
+                        // x*scale + shift, with scale and shift rounded to f16): a third of
+                        // the instructions of the f32 form, which two warps could not
+                        // issue as fast as the tensor cores consume the tiles
+                        const __half2 sc[4] = {__floats2half2_rn(s0.x, s0.y), __floats2half2_rn(s0.z, s0.w),
+                                               __floats2half2_rn(s1.x, s1.y), __floats2half2_rn(s1.z, s1.w)};
+                        const __half2 sh[4] = {__floats2half2_rn(h0.x, h0.y), __floats2half2_rn(h0.z, h0.w),
+                                               __floats2half2_rn(h1.x, h1.y), __floats2half2_rn(h1.z, h1.w)};
+                        uint8_t* a = smem + p.stage0 + stage * p.stage_bytes;
+#pragma unroll 4
+                        for (uint32_t o = o0; o < a_bytes; o += 1024u) {
+                            uint4 v = *reinterpret_cast<const uint4*>(a + o);
+                            __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) hv[q] = __hfma2_relu(hv[q], sc[q], sh[q]);
+                            *reinterpret_cast<uint4*>(a + o) = v;
+                        }
+                        // generic-proxy writes -> visible to the tensor cores' async proxy
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(bar_xfull + 8 * stage);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
                 }
             }
         }
@@ -1049,6 +1122,8 @@ struct SeqArgs {
     int pad, dil0, reflect, y_f32, tile_n, pair, stride0;
     const float* gate;
     int gate_seg, gate_nseg;
+    const float* x_scale;
+    const float* x_shift;
     const float* clip_bias;
     const float* bn_scale;
     const float* bn_shift;
@@ -1111,6 +1186,12 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
         set_error("vdb_conv1d: a stride-2 conv takes one input segment");
         return 1;
     }
+    if (!c->x_scale != !c->x_shift ||
+        (c->x_scale && ((reinterpret_cast<uintptr_t>(c->x_scale) & 15u) != 0 ||
+                        (reinterpret_cast<uintptr_t>(c->x_shift) & 15u) != 0))) {
+        set_error("vdb_conv1d: x_scale and x_shift go together, 16-byte aligned");
+        return 1;
+    }
     if (c->reflect == 2 && c->y_f32) {
         set_error("vdb_conv1d: zero padding (reflect 2) needs the f16 output");
         return 1;
@@ -1166,7 +1247,7 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
     a.ldaddend = c->ldaddend;
     SeqArgs sq{c->pad,  c->dil0,     c->reflect,   c->y_f32 ? 1 : 0, c->tile_n,
                c->pair, c->stride0 == 2 ? 2 : 1, c->gate,    c->gate_seg, c->gate_nseg,
-               c->clip_bias, c->bn_scale, c->bn_shift};
+               c->x_scale, c->x_shift, c->clip_bias, c->bn_scale, c->bn_shift};
     return conv_impl(&a, &sq, stream);
 }
 
@@ -1313,7 +1394,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             const int w_res = 9 * a->ic0 * BN * 2;
             const long long rows = vdb_grid_rows(a->batch, a->t_out, a->f_out);
             const int tail = round_up(a->oc * 4, 16) + round_up(a->batch * 4, 16) +
-                             8 * (2 * kMaxStages + 5) + 16;
+                             8 * (3 * kMaxStages + 5) + 16;
             for (int cand : {8, 4, 3}) {
                 const int H = cand * kMB + 2 * Hs;
                 const int nbox = (H + 255) / 256;
@@ -1429,7 +1510,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const bool has_bn = seq && sq->bn_scale != nullptr;
     const uint32_t ss_bytes = has_bn ? 2u * (uint32_t)round_up(a->oc * 4, 16) : 0u;
     const uint32_t tail = (uint32_t)round_up(a->oc * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
-                          ss_bytes + 8 * (2 * kMaxStages + 5) + 16;
+                          ss_bytes + 8 * (3 * kMaxStages + 5) + 16;
     const int budget = kSmemMax - 1024 - (int)off - (int)tail;
     p.two_ring = two_ring ? 1 : 0;
     if (two_ring) {
@@ -1466,7 +1547,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     p.ss_off = has_bn ? off : 0u;
     off += ss_bytes;
     p.bar_off = (uint32_t)round_up((int)off, 8);
-    off = p.bar_off + 8 * (2 * p.n_stages + 5) + 16;
+    off = p.bar_off + 8 * (3 * p.n_stages + 5) + 16;
     const size_t smem = (size_t)off + 1024;
 
     uint32_t cols = 32;
@@ -1521,6 +1602,16 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         p.gate = sq->gate;
         p.gate_seg = sq->gate_seg;
         p.gate_nseg = sq->gate_nseg;
+        if (sq->x_scale) {
+            if (a->k0 != 1 || a->x1 || pair || p.seg[0].mode != SEG_TAP) {
+                set_error("vdb_conv1d: the input BN + ReLU prologue needs a single-segment "
+                          "1x1 conv without CTA pairs");
+                return 1;
+            }
+            p.xform = 1;
+            p.x_scale = sq->x_scale;
+            p.x_shift = sq->x_shift;
+        }
         magic_div((uint32_t)Hp, p.img_mul, p.img_sh);
     }
 

@@ -18,10 +18,11 @@
 //   writing the next stage's FPHASE input -> FCM conv2 (freq stride 2) writing the
 //   TDNN's time-phase input directly (channel f*M + c; the TDNN weight's columns are
 //   permuted to match the reference's c*F + f order) -> TDNN (k=5, time stride 2) ->
-//   3 dense blocks, per layer: BN + ReLU of the concatenated features (one pass),
-//   1x1 conv + bias + ReLU, CAM gate (context means -> 2 FCs -> sigmoid per
-//   100-frame segment), k=3 dilated conv whose epilogue multiplies by the gate and
-//   stores into the features' next 32 channels; transit BN + ReLU + 1x1 ->
+//   3 dense blocks, per layer: 1x1 conv over the concatenated features with their
+//   BN + ReLU applied to each A tile in shared memory (the conv's input prologue) +
+//   bias + ReLU, CAM gate (segment sums; context -> 2 FCs -> sigmoid per 100-frame
+//   segment), k=3 dilated conv whose epilogue multiplies by the gate and stores into
+//   the features' next 32 channels; transit (BN + ReLU prologue, 1x1) ->
 //   statistics pooling (mean, unbiased std) -> dense head (output BN folded) -> L2.
 #include <cuda_fp16.h>
 
@@ -389,8 +390,8 @@ size_t Engine::campp_ws_bytes(int B, int t_max) const {
     n += align256(2 * (size_t)B * (T + 2) * (F3 + 2) * M * h);            // conv2 FPHASE
     n += align256(2 * R * F3 * M * h);                                    // TDNN TPHASE input
     n += 2 * align256(R * cmax * h);                                      // dense features
-    n += align256(R * cmax * h);                                          // BN + ReLU
     n += align256(R * E.bnc * h);                                         // CAM input
+    n += align256((size_t)B * nseg * E.bnc * f);                          // segment sums
     n += align256((size_t)B * nseg * E.growth * f);                       // CAM gate
     n += align256((size_t)B * 2 * E.c_out * f);                           // statistics
     n += align256((size_t)pool_fc_splits(B, 2 * E.c_out, cfg_.emb_dim) * B * cfg_.emb_dim * f);
@@ -426,8 +427,8 @@ int Engine::run_campplus(int B, int t_max, const std::vector<long long>& tv_sum,
     const size_t ts_bytes = 2 * R * F3 * M * h;
     __half* ts = (__half*)take(ts_bytes);
     __half* hb[2] = {(__half*)take(R * cmax * h), (__half*)take(R * cmax * h)};
-    __half* ab = (__half*)take(R * cmax * h);
     __half* cc = (__half*)take(R * E.bnc * h);
+    float* segsum = (float*)take((size_t)B * nseg * E.bnc * f);
     float* gate = (float*)take((size_t)B * nseg * E.growth * f);
     float* stats = (float*)take((size_t)B * 2 * E.c_out * f);
     float* part = (float*)take((size_t)pool_fc_splits(B, 2 * E.c_out, cfg_.emb_dim) * B *
@@ -559,22 +560,21 @@ int Engine::run_campplus(int B, int t_max, const std::vector<long long>& tv_sum,
         const int ld = Bk.cmax;
         int C = Bk.c0;
         for (const CamppLayerDev& L : Bk.layers) {
-            const int pg = prof_begin(st, 3);
-            if (campp_bn_relu(hcur, ld, C, L.bn_scale, L.bn_shift, (long long)R, ab, C, st))
-                return fail();
-            prof_end(pg, st, 0.0);
-            ++launches;
+            // nonlinear1 (BN + ReLU of the first C channels) as the 1x1 conv's input
+            // prologue, then + bias, ReLU
             {
-                vdb_conv1d_args a = conv1(L.lin1, ab, C, cc, E.bnc);
+                vdb_conv1d_args a = conv1(L.lin1, hcur, ld, cc, E.bnc);
+                a.x_scale = L.bn_scale;
+                a.x_shift = L.bn_shift;
                 a.relu = 1;
                 if (run1d(a, 2.0 * E.bnc * C * qframes)) return 1;
             }
             const int pc = prof_begin(st, 3);
             if (campp_cam_gate(cc, E.bnc, tq, B, Tq, P, E.bnc, kSeg, nseg, L.cam_w1, L.cam_b1,
-                               E.cam_m, L.cam_w2, L.cam_b2, E.growth, gate, st))
+                               E.cam_m, L.cam_w2, L.cam_b2, E.growth, segsum, gate, st))
                 return fail();
             prof_end(pc, st, 0.0);
-            ++launches;
+            launches += 2;
             {
                 vdb_conv1d_args a = conv1(L.local, cc, E.bnc, hcur + C, ld);
                 a.act = 5;
@@ -585,15 +585,13 @@ int Engine::run_campplus(int B, int t_max, const std::vector<long long>& tv_sum,
             }
             C += E.growth;
         }
-        // transit into the next block's features (or the pooling input)
-        const int pg = prof_begin(st, 3);
-        if (campp_bn_relu(hcur, ld, C, Bk.tr_scale, Bk.tr_shift, (long long)R, ab, C, st))
-            return fail();
-        prof_end(pg, st, 0.0);
-        ++launches;
+        // transit (BN + ReLU prologue, 1x1) into the next block's features (or the
+        // pooling input)
         hi ^= 1;
         const int ldn = bi + 1 < E.blocks.size() ? E.blocks[bi + 1].cmax : Bk.transit.oc;
-        vdb_conv1d_args a = conv1(Bk.transit, ab, C, hb[hi], ldn);
+        vdb_conv1d_args a = conv1(Bk.transit, hcur, ld, hb[hi], ldn);
+        a.x_scale = Bk.tr_scale;
+        a.x_shift = Bk.tr_shift;
         a.relu = bi + 1 == E.blocks.size() ? 1 : 0;
         if (run1d(a, 2.0 * Bk.transit.oc * C * qframes)) return 1;
     }

@@ -17,6 +17,7 @@ enum : int {
     VDB_ERR_TIMEOUT_TFULL = 0x103,  // epilogue waited too long for an accumulator
     VDB_ERR_TIMEOUT_TEMPTY = 0x104, // MMA waited too long for a drained accumulator
     VDB_ERR_TIMEOUT_DRAIN = 0x105,  // teardown drain gave up
+    VDB_ERR_TIMEOUT_XFORM = 0x106,  // input-transform warps waited too long for a TMA stage
 };
 
 // Wall-clock bound on any single barrier wait inside a kernel.

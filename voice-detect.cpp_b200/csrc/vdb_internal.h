@@ -70,17 +70,16 @@ int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const
                    cudaStream_t st);
 
 // CAM++ (campplus.cu): mean / std pooling with the unbiased variance and no floor
-// (ecapa.cu's kernel), BN + ReLU of a channel prefix over `rows` SEQ rows, and the
-// CAM gate [batch][nseg_max][G] = sigmoid(w2 . ReLU(w1 . ctx + b1) + b2) per 100-frame
-// segment (w1 [M][C], w2 [G][M] f32).
+// (ecapa.cu's kernel) and the CAM gate [batch][nseg_max][G] =
+// sigmoid(w2 . ReLU(w1 . ctx + b1) + b2) per 100-frame segment (w1 [M][C], w2 [G][M]
+// f32); segsum: f32 scratch [batch][nseg_max][C].
 int seq_meanstd_unbiased(const __half* x, int ldx, const int* tv, int batch, int T, int pad,
                          int C, float* stats, cudaStream_t st);
-int campp_bn_relu(const __half* h, int ldh, int C, const float* scale, const float* shift,
-                  long long rows, __half* a, int lda, cudaStream_t st);
-size_t campp_gate_smem(int C, int M, int nseg_max);
+size_t campp_gate_smem(int C, int M, int G, int nseg_max);
 int campp_cam_gate(const __half* cc, int ldc, const int* tv, int batch, int T, int pad, int C,
                    int seg, int nseg_max, const float* w1, const float* b1, int M,
-                   const float* w2, const float* b2, int G, float* gate, cudaStream_t st);
+                   const float* w2, const float* b2, int G, float* segsum, float* gate,
+                   cudaStream_t st);
 
 }  // namespace vdb
 
