@@ -47,10 +47,13 @@ def _mask_t(x, tv):
     return x
 
 
+@pytest.mark.parametrize("halo,tile_m", [(0, 0), (-1, 0), (1, 512)],
+                         ids=["auto", "tap", "halo512"])
 @pytest.mark.parametrize("F,T", [(80, 37), (41, 29)])
-def test_conv2d_freq_stride(cuda_lib, F, T):
-    """Block 0 of an FCM stage: conv1 3x3 stride (2, 1) from FPHASE; conv2 3x3 + the
-    1x1 stride-(2, 1) shortcut (second K segment) -> ReLU, stored as FPHASE."""
+def test_conv2d_freq_stride(cuda_lib, F, T, halo, tile_m):
+    """Block 0 of an FCM stage: conv1 3x3 stride (2, 1) from FPHASE (fed per tap, or
+    by one halo per frequency plane with the weights resident); conv2 3x3 + the 1x1
+    stride-(2, 1) shortcut (second K segment) -> ReLU, stored as FPHASE."""
     import torch
     import torch.nn.functional as Fn
     vd = cuda_lib
@@ -72,7 +75,7 @@ def test_conv2d_freq_stride(cuda_lib, F, T):
     tvd = torch.tensor(tv, dtype=torch.int32, device=dev)
     xf = vd.to_fphase(x, tv).to(dev)
     y1 = vd.conv(xf, vd.pack_conv_weight(w1).to(dev), b1.to(dev), tvd, batch=B, t_out=T,
-                 f_out=Fo, oc=C, k0=3, stride0=3, relu=True)
+                 f_out=Fo, oc=C, k0=3, stride0=3, relu=True, halo=halo, tile_m=tile_m)
     got1 = vd.from_grid(y1, B, C, Fo, T).cpu()
     assert _rel(got1, r1) <= REL_TOL
     y2 = vd.conv(y1, vd.pack_conv_weight(w2).to(dev), b2.to(dev), tvd, batch=B, t_out=T,
@@ -83,7 +86,7 @@ def test_conv2d_freq_stride(cuda_lib, F, T):
     # the FPHASE output feeds the next stage's stride-(2, 1) conv
     Fq = vd.out_extent(Fo, 2)
     y3 = vd.conv(y2, vd.pack_conv_weight(w1).to(dev), b1.to(dev), tvd, batch=B, t_out=T,
-                 f_out=Fq, oc=C, k0=3, stride0=3, relu=True)
+                 f_out=Fq, oc=C, k0=3, stride0=3, relu=True, halo=halo, tile_m=tile_m)
     r3 = _mask_t(torch.relu(Fn.conv2d(vd.from_fphase(y2, B, C, Fo, T).cpu(), w1, b1,
                                       stride=(2, 1), padding=1)), tv)
     assert _rel(vd.from_grid(y3, B, C, Fq, T).cpu(), r3) <= REL_TOL

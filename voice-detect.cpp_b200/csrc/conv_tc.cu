@@ -76,6 +76,7 @@ struct SegDev {
     int plane[9];
     int off[9];      // TAP: global row offset per tap; HALO: row offset inside the halo
     int halo_back;   // HALO: rows before m0 covered by the halo
+    uint32_t plane_bytes;  // HALO over FPHASE (stride 3): offset of the plane-1 halo, else 0
     int n_box, box_rows;  // TMA A boxes per stage and their height (TAP: BM split in <= 256)
     uint32_t bres;   // HALO: resident weights, byte offset from the smem base
     uint32_t a_bytes, b_bytes;  // two-ring pipeline: A bytes per channel block, weight bytes per tap
@@ -493,13 +494,19 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 
 // HALO stage: nine taps of a 3x3 stride-1 conv read one shared input halo through
 // row-shifted descriptors; tap (kt, kf) starts kt*wp_units + kf*rb16 in.
+// plane_units != 0: the halo is FPHASE (a frequency-stride-2 input), two planes
+// plane_units apart; tap (kt, kf) reads plane kf&1 at kt rows of Wp and kf>>1 rows in.
 template <int KS, int NMB, int J>
 __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                            uint32_t wp_units, uint32_t rb16, uint64_t b_desc,
-                                           uint32_t b_tap_units, uint32_t idesc, bool first) {
+                                           uint32_t b_tap_units, uint32_t idesc, bool first,
+                                           uint32_t plane_units) {
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
-        const uint64_t at = a_desc + (uint64_t)((tap / 3) * wp_units + (tap % 3) * rb16);
+        const int kf = tap % 3;
+        const uint32_t col = plane_units ? (uint32_t)(kf & 1) * plane_units + (uint32_t)(kf >> 1) * rb16
+                                         : (uint32_t)kf * rb16;
+        const uint64_t at = a_desc + (uint64_t)((tap / 3) * wp_units + col);
         const uint64_t bt = b_desc + (uint64_t)(tap * b_tap_units);
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
@@ -543,11 +550,11 @@ template <int NMB, int J, bool PAIR>
 __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
                                             uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
                                             uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
-                                            bool first) {
+                                            bool first, uint32_t plane_units = 0) {
     if (!PAIR && halo) {
-        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
-        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
-        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first);
+        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
+        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
+        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
     } else {
         if (ks == 4) issue_tap<4, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
         else if (ks == 2) issue_tap<2, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
@@ -756,6 +763,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                             for (int bx = 0; bx < s.n_box; ++bx)
                                 tma_load_3d(sa + bx * box_bytes, ta, fb, it * s.kb,
                                             m0 - s.halo_back + bx * s.box_rows, 0);
+                            if (s.plane_bytes)  // FPHASE: the odd-frequency plane's halo
+                                for (int bx = 0; bx < s.n_box; ++bx)
+                                    tma_load_3d(sa + s.plane_bytes + bx * box_bytes, ta, fb,
+                                                it * s.kb, m0 - s.halo_back + bx * s.box_rows, 1);
                         } else {
                             const int tap = it / s.n_kb, kbi = it - tap * s.n_kb;
                             const uint32_t box_bytes = (uint32_t)s.box_rows * s.kb * 2;
@@ -868,7 +879,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         const uint64_t b_desc = halo ? bres_desc + (uint64_t)(it * b_kb_units)
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
                         issue_stage<NMB, J, PAIR>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc,
-                                                  wp_units, rb16, b_desc, b_tap_units, idesc, first);
+                                                  wp_units, rb16, b_desc, b_tap_units, idesc, first,
+                                                  s.plane_bytes >> 4);
                         first = false;
                         if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
                         else umma_commit(bar_empty + 8 * stage);
@@ -1358,8 +1370,11 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // by ~9x, but measured no faster than TAP on the ResNet34 shapes (the epilogue
     // and the MMA issue bound those convs, not the L2 feed), so auto does not pick
     // it. a->halo: 0 auto, 1 force HALO, 2 force HALO_S, -1 TAP.
+    // The resident-weight HALO also feeds the frequency-stride-2 conv over FPHASE
+    // (stride 3): one halo per plane, the 9 taps as row shifts inside them.
     const bool hs_ok = !seq && a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
-    const bool halo_ok = hs_ok && w_bytes0 <= 96 * 1024;
+    const bool fph = !seq && a->k0 == 3 && a->stride0 == 3;
+    const bool halo_ok = (hs_ok || (fph && n_nt == 1)) && w_bytes0 <= 96 * 1024;
     if (a->halo < -1 || a->halo > 2 || (seq && a->halo > 0)) {
         set_error("vdb_conv: halo must be -1, 0, 1 or 2");
         return 1;
@@ -1367,8 +1382,9 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const bool halo = a->halo == 0 ? halo_ok : (a->halo == 1 && halo_ok);
     const bool two_ring = a->halo == 2 && hs_ok;
     if ((a->halo == 1 && !halo_ok) || (a->halo == 2 && !hs_ok)) {
-        set_error("vdb_conv: HALO modes need a stride-1 3x3 conv with oc <= 256 (and weights "
-                  "<= 96 KB for the resident HALO)");
+        set_error("vdb_conv: HALO modes need a 3x3 conv with oc <= 256, stride 1 (or the "
+                  "frequency-only stride 3 for the resident HALO) and weights <= 96 KB for "
+                  "the resident HALO");
         return 1;
     }
     // Tiling. A tcgen05.mma that accumulates into the same TMEM tile as the one
@@ -1390,17 +1406,18 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     if (BM == 0) {
         BM = 256;
         if (halo && a->ksplit <= 1) {
-            const int Hs = Wp + 1;
+            const int Hs = fph ? Wp : Wp + 1;
             const int w_res = 9 * a->ic0 * BN * 2;
             const long long rows = vdb_grid_rows(a->batch, a->t_out, a->f_out);
             const int tail = round_up(a->oc * 4, 16) + round_up(a->batch * 4, 16) +
                              8 * (3 * kMaxStages + 5) + 16;
             for (int cand : {8, 4, 3}) {
-                const int H = cand * kMB + 2 * Hs;
+                const int H = cand * kMB + 2 * Hs + (fph ? 1 : 0);
                 const int nbox = (H + 255) / 256;
                 const int box = round_up((H + nbox - 1) / nbox, 8);
                 const int kb = a->ic0 % 64 == 0 ? 64 : (a->ic0 % 32 == 0 ? 32 : 16);
                 long long a_b = (long long)nbox * box * kb * 2, b_b = 0;
+                if (fph) a_b += round_up((int)a_b, 1024);  // the second plane's halo
                 if (a->x1) {  // segment 1 stages hold its A rows and a weight tile
                     const int kb1 = a->ic1 % 64 == 0 ? 64 : (a->ic1 % 32 == 0 ? 32 : 16);
                     a_b = std::max<long long>(a_b, (long long)cand * kMB * kb1 * 2);
@@ -1481,17 +1498,21 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             s.bytes = s.a_bytes;
         } else if (sg == 0 && halo) {
             s.mode = SEG_HALO;
-            const int H = BM + 2 * Wp + 2;
-            s.halo_back = Wp + 1;
+            // stride 1: taps at kt*Wp + kf rows into a halo from m0 - (Wp + 1); FPHASE:
+            // taps at kt*Wp + (kf>>1) rows into plane kf&1's halo from m0 - Wp
+            const int H = fph ? BM + 2 * Wp + 1 : BM + 2 * Wp + 2;
+            s.halo_back = fph ? Wp : Wp + 1;
             s.n_box = (H + 255) / 256;
             s.box_rows = round_up((H + s.n_box - 1) / s.n_box, 8);
             for (int t = 0; t < 9; ++t) s.off[t] = (t / 3) * Wp + (t % 3);  // kt*Wp + kf
-            s.bytes = (uint32_t)s.n_box * s.box_rows * row_bytes;
+            const uint32_t one = (uint32_t)s.n_box * s.box_rows * row_bytes;
+            s.plane_bytes = fph ? (uint32_t)round_up((int)one, 1024) : 0u;
+            s.bytes = fph ? 2 * one : one;
             s.bres = off;
             const uint32_t w = (uint32_t)9 * s.n_kb * BN * row_bytes;
             off += w;
             p.bres_bytes += w;
-            a_bytes = std::max(a_bytes, s.bytes);
+            a_bytes = std::max(a_bytes, s.plane_bytes + one);
         } else {
             s.mode = SEG_TAP;
             s.n_box = (cta_rows + 255) / 256;
