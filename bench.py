@@ -270,6 +270,27 @@ def hbm_rooflines(stages: dict, steps: int, lens, peaks: dict) -> dict:
     return out
 
 
+def profiled_steps(model, step, steps: int):
+    """Per-launch CUDA-event profile of min(steps, 2) extra steps, after the timed
+    region: the events bracket every launch and the profiled steps run their launches
+    plainly (no graph replay), so they are kept out of the timed steps. Returns the
+    conv milliseconds, FLOPs and launches and the per-stage milliseconds, scaled to
+    `steps` steps, and the number of steps profiled."""
+    import torch
+    n = max(1, min(steps, 2))
+    model.profile(True)
+    model.profile_read()
+    for _ in range(n):
+        step()
+    torch.cuda.synchronize()
+    conv_ms, conv_flops, conv_n = model.profile_read()
+    stages = model.profile_stages()
+    model.profile(False)
+    f = steps / n
+    return (conv_ms * f, conv_flops * f, int(round(conv_n * f)),
+            {k: v * f for k, v in stages.items()}, n)
+
+
 def run_b200(args) -> int:
     import torch
     import torch.distributed as dist
@@ -328,8 +349,6 @@ def run_b200(args) -> int:
         dist.barrier()
     clocks = ClockSampler(dev.index)
     clocks.start()
-    model.profile(True)
-    model.profile_read()
     launches = 0
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -340,10 +359,8 @@ def run_b200(args) -> int:
     end.record(stream)
     torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(end)
-    conv_ms, conv_flops, conv_n = model.profile_read()
-    stages = model.profile_stages()
-    model.profile(False)
     clk = clocks.stop()
+    conv_ms, conv_flops, conv_n, stages, prof_steps = profiled_steps(model, step, args.steps)
     model.sync()
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -429,7 +446,7 @@ def run_b200(args) -> int:
                      "traffic_source": "ncu capture summarised in "
                                        "profiles/launches__bench_c4_512clips.md, scaled by "
                                        "this run's FLOPs per launch",
-                     "conv_launches": conv_n,
+                     "conv_launches": conv_n, "profiled_steps": prof_steps,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
@@ -689,8 +706,6 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         dist.barrier()
     clocks = ClockSampler(dev.index)
     clocks.start()
-    model.profile(True)
-    model.profile_read()
     launches = 0
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -701,10 +716,8 @@ def run_eres2net(args, family: str = "eres2net") -> int:
     end.record(stream)
     torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(end)
-    conv_ms, conv_flops, conv_n = model.profile_read()
-    stages = model.profile_stages()
-    model.profile(False)
     clk = clocks.stop()
+    conv_ms, conv_flops, conv_n, stages, prof_steps = profiled_steps(model, step, args.steps)
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -740,7 +753,7 @@ def run_eres2net(args, family: str = "eres2net") -> int:
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
                      if peaks else "fallback 1.4 PFLOP/s sustained",
-                     "traffic": None, "conv_launches": conv_n,
+                     "traffic": None, "conv_launches": conv_n, "profiled_steps": prof_steps,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},

@@ -501,11 +501,14 @@ __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_
                                            uint32_t wp_units, uint32_t rb16, uint64_t b_desc,
                                            uint32_t b_tap_units, uint32_t idesc, bool first,
                                            uint32_t plane_units) {
+    // column offsets of kf = 1, 2 (kf = 0 is 0), chosen once: the loop below is the
+    // issue-bound inner loop of the small-channel convs
+    const uint32_t col1 = plane_units ? plane_units : rb16;
+    const uint32_t col2 = plane_units ? rb16 : 2 * rb16;
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
         const int kf = tap % 3;
-        const uint32_t col = plane_units ? (uint32_t)(kf & 1) * plane_units + (uint32_t)(kf >> 1) * rb16
-                                         : (uint32_t)kf * rb16;
+        const uint32_t col = kf == 0 ? 0u : (kf == 1 ? col1 : col2);
         const uint64_t at = a_desc + (uint64_t)((tap / 3) * wp_units + col);
         const uint64_t bt = b_desc + (uint64_t)(tap * b_tap_units);
 #pragma unroll

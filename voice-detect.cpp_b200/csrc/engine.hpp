@@ -114,9 +114,9 @@ struct CamppLayerDev {
     float* bn_shift = nullptr;
     TdnnDev lin1;               // 1x1 c_in -> bnc, bias, ReLU
     TdnnDev local;              // k=3 dilated bnc -> growth, no bias, * CAM gate
-    float* cam_w1 = nullptr;    // [cam_m][bnc]
+    float* cam_w1 = nullptr;    // transposed: [bnc][cam_m]
     float* cam_b1 = nullptr;
-    float* cam_w2 = nullptr;    // [growth][cam_m]
+    float* cam_w2 = nullptr;    // transposed: [cam_m][growth]
     float* cam_b2 = nullptr;
 };
 

@@ -20,8 +20,8 @@
 //   permuted to match the reference's c*F + f order) -> TDNN (k=5, time stride 2) ->
 //   3 dense blocks, per layer: 1x1 conv over the concatenated features with their
 //   BN + ReLU applied to each A tile in shared memory (the conv's input prologue) +
-//   bias + ReLU, CAM gate (segment sums; context -> 2 FCs -> sigmoid per 100-frame
-//   segment), k=3 dilated conv whose epilogue multiplies by the gate and stores into
+//   bias + ReLU, CAM gate (one kernel per layer: segment sums -> context -> 2 FCs
+//   -> sigmoid per 100-frame segment), k=3 dilated conv whose epilogue multiplies by the gate and stores into
 //   the features' next 32 channels; transit (BN + ReLU prologue, 1x1) ->
 //   statistics pooling (mean, unbiased std) -> dense head (output BN folded) -> L2.
 #include <cuda_fp16.h>
@@ -314,8 +314,17 @@ bool Engine::load_campplus(const Gguf& g, std::string& err) {
             if (!tdnn_dev(l1, L.lin1, 1) || !tdnn_dev(lo, L.local, B.dil)) return false;
             std::vector<float> mb1 = m1.b.empty() ? std::vector<float>(m1.oc, 0.0f) : m1.b;
             std::vector<float> mb2 = m2.b.empty() ? std::vector<float>(m2.oc, 0.0f) : m2.b;
-            if (!upload_f32(m1.w, &L.cam_w1, err) || !upload_f32(mb1, &L.cam_b1, err) ||
-                !upload_f32(m2.w, &L.cam_w2, err) || !upload_f32(mb2, &L.cam_b2, err))
+            // CAM FCs stored transposed ([in][out]) for the gate kernel
+            auto transpose = [](const std::vector<float>& w, int rows, int cols) {
+                std::vector<float> t(w.size());
+                for (int r = 0; r < rows; ++r)
+                    for (int c = 0; c < cols; ++c) t[(size_t)c * rows + r] = w[(size_t)r * cols + c];
+                return t;
+            };
+            if (!upload_f32(transpose(m1.w, m1.oc, m1.ic), &L.cam_w1, err) ||
+                !upload_f32(mb1, &L.cam_b1, err) ||
+                !upload_f32(transpose(m2.w, m2.oc, m2.ic), &L.cam_w2, err) ||
+                !upload_f32(mb2, &L.cam_b2, err))
                 return false;
             B.layers.push_back(L);
             C += E.growth;
@@ -391,7 +400,6 @@ size_t Engine::campp_ws_bytes(int B, int t_max) const {
     n += align256(2 * R * F3 * M * h);                                    // TDNN TPHASE input
     n += 2 * align256(R * cmax * h);                                      // dense features
     n += align256(R * E.bnc * h);                                         // CAM input
-    n += align256((size_t)B * nseg * E.bnc * f);                          // segment sums
     n += align256((size_t)B * nseg * E.growth * f);                       // CAM gate
     n += align256((size_t)B * 2 * E.c_out * f);                           // statistics
     n += align256((size_t)pool_fc_splits(B, 2 * E.c_out, cfg_.emb_dim) * B * cfg_.emb_dim * f);
@@ -428,7 +436,6 @@ int Engine::run_campplus(int B, int t_max, const std::vector<long long>& tv_sum,
     __half* ts = (__half*)take(ts_bytes);
     __half* hb[2] = {(__half*)take(R * cmax * h), (__half*)take(R * cmax * h)};
     __half* cc = (__half*)take(R * E.bnc * h);
-    float* segsum = (float*)take((size_t)B * nseg * E.bnc * f);
     float* gate = (float*)take((size_t)B * nseg * E.growth * f);
     float* stats = (float*)take((size_t)B * 2 * E.c_out * f);
     float* part = (float*)take((size_t)pool_fc_splits(B, 2 * E.c_out, cfg_.emb_dim) * B *
@@ -571,10 +578,10 @@ int Engine::run_campplus(int B, int t_max, const std::vector<long long>& tv_sum,
             }
             const int pc = prof_begin(st, 3);
             if (campp_cam_gate(cc, E.bnc, tq, B, Tq, P, E.bnc, kSeg, nseg, L.cam_w1, L.cam_b1,
-                               E.cam_m, L.cam_w2, L.cam_b2, E.growth, segsum, gate, st))
+                               E.cam_m, L.cam_w2, L.cam_b2, E.growth, gate, st))
                 return fail();
             prof_end(pc, st, 0.0);
-            launches += 2;
+            ++launches;
             {
                 vdb_conv1d_args a = conv1(L.local, cc, E.bnc, hcur + C, ld);
                 a.act = 5;
