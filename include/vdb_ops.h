@@ -195,6 +195,10 @@ typedef struct vdb_conv1d_args {
                                BatchNorm + ReLU on its input); device f32 [ic0], 16-byte
                                aligned, or NULL */
     const float* x_shift;
+    int halo;               /* feed of a k > 1 stride-1 single-segment conv: 0 auto (the halo
+                               for outputs of <= 64 columns), -1 one A tile per tap, 1 one
+                               input halo of tile + (k-1)*dil rows per channel block feeding
+                               every tap, weights resident (<= 96 KB) */
 } vdb_conv1d_args;
 
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);

@@ -139,10 +139,12 @@ def test_fcm_to_tdnn_time_phase(cuda_lib):
         assert torch.all(ys[i, :, oc:] == 7.0)
 
 
+@pytest.mark.parametrize("halo", [0, -1], ids=["halo", "tap"])
 @pytest.mark.parametrize("dil", [1, 2])
-def test_cam_gate_conv(cuda_lib, dil):
+def test_cam_gate_conv(cuda_lib, dil, halo):
     """CAM layer: linear_local (k=3, dilation, no bias, zero padding) times the
-    per-(clip, segment) gate, stored zero-padded into a channel slice."""
+    per-(clip, segment) gate, stored zero-padded into a channel slice; fed by one
+    input halo per channel block (the automatic choice) or one tile per tap."""
     import torch
     import torch.nn.functional as Fn
     vd = cuda_lib
@@ -160,7 +162,7 @@ def test_cam_gate_conv(cuda_lib, dil):
     h = torch.full((rows, 96 + oc), 3.0, dtype=torch.float16, device=dev)
     vd.conv1d(xs, vd.pack_conv1d_weight(w).to(dev), None, tvd, batch=B, t=T, pad=P, oc=oc,
               k0=3, dil0=dil, act=5, gate=gate.to(dev), gate_seg=seg, gate_nseg=nseg,
-              y=h[:, 96:], reflect=2)
+              y=h[:, 96:], reflect=2, halo=halo)
     torch.cuda.synchronize()
     ys = h.float().cpu().reshape(B, T + 2 * P, 96 + oc)
     for i, t in enumerate(tv):

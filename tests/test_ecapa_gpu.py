@@ -66,7 +66,7 @@ CASES = {
 @pytest.mark.parametrize("name", sorted(CASES))
 def test_conv1d_matches_torch(cuda_lib, name, pair):
     """pair 1: two-SM cta_group::2 tiles (where the tiling allows them), 0: one CTA
-    per tile."""
+    per tile, multi-tap convs fed by one input halo per channel block."""
     import torch
     B, T, pad, ic, oc, k, dil, act, two_seg, use_cb, use_sum, y_f32, tm, tn = CASES[name]
     if pair and tm not in (0, 256):
@@ -116,9 +116,12 @@ def test_conv1d_matches_torch(cuda_lib, name, pair):
         ysum = torch.zeros(rows, oc, dtype=torch.float16, device=dev)
         kw.update(ysum=ysum, addend=vd.to_seq(add, pad, tv).to(dev))
     y = torch.zeros(rows, oc, dtype=torch.float32 if y_f32 else torch.float16, device=dev)
+    # pair 0 on a multi-tap single-segment conv also exercises the 1-D halo feed
+    halo = 1 if (not pair and k > 1 and not two_seg and tn == 0
+                 and k * ic * oc * 2 <= 96 * 1024) else 0
     vd.conv1d(xs, vd.pack_conv1d_weight(w).to(dev), b.to(dev), tvd, batch=B, t=T, pad=pad,
               oc=oc, k0=k, dil0=dil, act=act, y=y, y_f32=y_f32, reflect=not y_f32,
-              tile_m=tm, tile_n=tn, pair=pair, **kw)
+              tile_m=tm, tile_n=tn, pair=pair, halo=halo, **kw)
     torch.cuda.synchronize()
     ys = y.float().cpu().reshape(B, T + 2 * pad, oc)
     for i, t in enumerate(tv):

@@ -77,6 +77,7 @@ struct SegDev {
     int off[9];      // TAP: global row offset per tap; HALO: row offset inside the halo
     int halo_back;   // HALO: rows before m0 covered by the halo
     uint32_t plane_bytes;  // HALO over FPHASE (stride 3): offset of the plane-1 halo, else 0
+    int dil;         // 1-D: tap j reads j*dil rows into a HALO (taps at (j - (k-1)/2)*dil)
     int n_box, box_rows;  // TMA A boxes per stage and their height (TAP: BM split in <= 256)
     uint32_t bres;   // HALO: resident weights, byte offset from the smem base
     uint32_t a_bytes, b_bytes;  // two-ring pipeline: A bytes per channel block, weight bytes per tap
@@ -549,12 +550,40 @@ __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t
     }
 }
 
+// 1-D HALO: n_taps taps, tap j starting j*dil rows (dil_units = dil*rb16) into the
+// halo, which begins (k-1)/2*dil rows before the tile.
+template <int KS, int NMB, int J>
+__device__ __forceinline__ void issue_halo1d(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
+                                             uint32_t rb16, uint64_t b_desc, uint32_t b_tap_units,
+                                             uint32_t idesc, bool first, int n_taps,
+                                             uint32_t dil_units) {
+    for (int tap = 0; tap < n_taps; ++tap) {
+        const uint64_t at = a_desc + (uint64_t)(tap * dil_units);
+        const uint64_t bt = b_desc + (uint64_t)(tap * b_tap_units);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+            const int q = tap * KS + k;
+            const int j = q % J;
+#pragma unroll
+            for (int mb = 0; mb < NMB; ++mb)
+                umma_f16(d_tile + (uint32_t)(mb * J + j) * bn,
+                         at + (uint64_t)(mb * 128 * rb16) + 2 * k, bt + 2 * k, idesc,
+                         (first && q < J) ? 0u : 1u);
+        }
+    }
+}
+
 template <int NMB, int J, bool PAIR>
 __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
                                             uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
                                             uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
-                                            bool first, uint32_t plane_units = 0) {
-    if (!PAIR && halo) {
+                                            bool first, uint32_t plane_units = 0,
+                                            int taps1d = 0, uint32_t dil_units = 0) {
+    if (!PAIR && halo && taps1d) {
+        if (ks == 4) issue_halo1d<4, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+        else if (ks == 2) issue_halo1d<2, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+        else issue_halo1d<1, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+    } else if (!PAIR && halo) {
         if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
         else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
         else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
@@ -883,7 +912,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
                         issue_stage<NMB, J, PAIR>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc,
                                                   wp_units, rb16, b_desc, b_tap_units, idesc, first,
-                                                  s.plane_bytes >> 4);
+                                                  s.plane_bytes >> 4, SEQ ? s.n_taps : 0,
+                                                  SEQ ? (uint32_t)s.dil * rb16 : 0u);
                         first = false;
                         if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
                         else umma_commit(bar_empty + 8 * stage);
@@ -1123,6 +1153,7 @@ void fill_taps_1d(SegDev& s, int k, int dil, int ic, int stride = 1) {
     s.kb = (ic % 64 == 0) ? 64 : ((ic % 32 == 0) ? 32 : 16);
     s.n_kb = ic / s.kb;
     s.n_taps = k;
+    s.dil = dil;
     for (int j = 0; j < k; ++j) {
         const int u = (j - (k - 1) / 2) * dil;
         s.plane[j] = stride == 2 ? (u & 1) : 0;
@@ -1193,6 +1224,10 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
                   "gate_seg >= 1 and gate_nseg * gate_seg >= t");
         return 1;
     }
+    if (c->halo < -1 || c->halo > 1) {
+        set_error("vdb_conv1d: halo must be -1 (per-tap tiles), 0 (auto) or 1 (one halo)");
+        return 1;
+    }
     if (c->reflect < 0 || c->reflect > 2 || c->stride0 < 0 || c->stride0 > 2) {
         set_error("vdb_conv1d: reflect must be 0, 1 or 2 and stride0 0, 1 or 2");
         return 1;
@@ -1254,7 +1289,7 @@ extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
     a.ldy = c->ldy;
     a.err = c->err;
     a.tile_m = c->tile_m;
-    a.halo = -1;
+    a.halo = c->halo;
     a.act = c->act;
     a.ysum = c->ysum;
     a.ldsum = c->ldsum;
@@ -1377,12 +1412,19 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // (stride 3): one halo per plane, the 9 taps as row shifts inside them.
     const bool hs_ok = !seq && a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
     const bool fph = !seq && a->k0 == 3 && a->stride0 == 3;
-    const bool halo_ok = (hs_ok || (fph && n_nt == 1)) && w_bytes0 <= 96 * 1024;
-    if (a->halo < -1 || a->halo > 2 || (seq && a->halo > 0)) {
+    // 1-D: one halo of tile + 2*reach rows per channel block feeds every tap (weights
+    // resident); automatic for narrow outputs (<= 64 columns: CAM++'s 32-column k=3
+    // convs), where the per-tap stages cost more than their MMAs.
+    const bool seq_halo_ok = seq && a->k0 > 1 && sq->stride0 == 1 && !a->x1 && n_nt == 1 &&
+                             !sq->x_scale && sq->pair != 1 &&
+                             (uint32_t)a->k0 * a->ic0 * BN * 2 <= 96 * 1024;
+    const bool halo_ok = seq ? seq_halo_ok
+                             : (hs_ok || (fph && n_nt == 1)) && w_bytes0 <= 96 * 1024;
+    if (a->halo < -1 || a->halo > 2 || (seq && a->halo > 1)) {
         set_error("vdb_conv: halo must be -1, 0, 1 or 2");
         return 1;
     }
-    const bool halo = a->halo == 0 ? halo_ok : (a->halo == 1 && halo_ok);
+    const bool halo = a->halo == 0 ? halo_ok && (!seq || BN <= 64) : (a->halo == 1 && halo_ok);
     const bool two_ring = a->halo == 2 && hs_ok;
     if ((a->halo == 1 && !halo_ok) || (a->halo == 2 && !hs_ok)) {
         set_error("vdb_conv: HALO modes need a 3x3 conv with oc <= 256, stride 1 (or the "
@@ -1503,8 +1545,9 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             s.mode = SEG_HALO;
             // stride 1: taps at kt*Wp + kf rows into a halo from m0 - (Wp + 1); FPHASE:
             // taps at kt*Wp + (kf>>1) rows into plane kf&1's halo from m0 - Wp
-            const int H = fph ? BM + 2 * Wp + 1 : BM + 2 * Wp + 2;
-            s.halo_back = fph ? Wp : Wp + 1;
+            const int reach = seq ? (a->k0 - 1) / 2 * sq->dil0 : 0;
+            const int H = seq ? BM + 2 * reach : (fph ? BM + 2 * Wp + 1 : BM + 2 * Wp + 2);
+            s.halo_back = seq ? reach : (fph ? Wp : Wp + 1);
             s.n_box = (H + 255) / 256;
             s.box_rows = round_up((H + s.n_box - 1) / s.n_box, 8);
             for (int t = 0; t < 9; ++t) s.off[t] = (t / 3) * Wp + (t % 3);  // kt*Wp + kf
@@ -1512,7 +1555,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             s.plane_bytes = fph ? (uint32_t)round_up((int)one, 1024) : 0u;
             s.bytes = fph ? 2 * one : one;
             s.bres = off;
-            const uint32_t w = (uint32_t)9 * s.n_kb * BN * row_bytes;
+            const uint32_t w = (uint32_t)s.n_taps * s.n_kb * BN * row_bytes;
             off += w;
             p.bres_bytes += w;
             a_bytes = std::max(a_bytes, s.plane_bytes + one);

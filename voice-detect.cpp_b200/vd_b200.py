@@ -59,7 +59,7 @@ class Conv1dArgs(C.Structure):
         ("ldsum", C.c_int), ("addend", C.c_void_p), ("ldaddend", C.c_int), ("err", C.c_void_p),
         ("tile_m", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int), ("stride0", C.c_int),
         ("gate", C.c_void_p), ("gate_seg", C.c_int), ("gate_nseg", C.c_int),
-        ("x_scale", C.c_void_p), ("x_shift", C.c_void_p),
+        ("x_scale", C.c_void_p), ("x_shift", C.c_void_p), ("halo", C.c_int),
     ]
 
 
@@ -553,7 +553,7 @@ def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x
            w1=None, ic1=None, bn_scale=None, bn_shift=None, clip_bias=None, act=0, relu=False,
            residual=None, y=None, y_f32=False, reflect=False, ysum=None, addend=None, err=None,
            stream=None, tile_m=0, tile_n=0, pair=0, stride0=1, gate=None, gate_seg=0,
-           gate_nseg=0, x_scale=None, x_shift=None):
+           gate_nseg=0, x_scale=None, x_shift=None, halo=0):
     """vdb_conv1d on device tensors: x0/x1/residual/y/ysum/addend are SEQ tensors
     (rows, C) or channel-slice views of wider ones; w0 f16 (OC, K, IC), w1 f16
     (OC, IC1); bias / bn_scale / bn_shift f32 (OC,); clip_bias f32 (B, OC).
@@ -578,7 +578,8 @@ def conv1d(x0, w0, bias, tvalid, *, batch, t, pad, oc, k0=1, dil0=1, ic0=None, x
                    reflect=int(reflect), ysum=_ptr(ysum), ldsum=_ld(ysum), addend=_ptr(addend),
                    ldaddend=_ld(addend), err=_ptr(err), tile_m=tile_m, tile_n=tile_n,
                    pair=pair, stride0=int(stride0), gate=_ptr(gate), gate_seg=int(gate_seg),
-                   gate_nseg=int(gate_nseg), x_scale=_ptr(x_scale), x_shift=_ptr(x_shift))
+                   gate_nseg=int(gate_nseg), x_scale=_ptr(x_scale), x_shift=_ptr(x_shift),
+                   halo=int(halo))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv1d(C.byref(a), C.c_void_p(s)), "vdb_conv1d")
     return y
