@@ -30,21 +30,36 @@ namespace {
 //    tvalid) + sum[s] / seg_len;
 // 3. hidden = ReLU(w1 . context + b1), gate = sigmoid(w2 . hidden + b2) per segment,
 //    one thread per output with the weights stored transposed (w1t [C][M], w2t
-//    [M][G]): a warp's 32 outputs read 128 contiguous bytes per input, from L1/L2.
-// Shared memory: ctx [nseg_max][C], hid [nseg_max][M], red [2048].
+//    [M][G]) and copied to shared memory first with 16-byte loads all in flight at
+//    once (the block's chain of dependent memory round trips is what bounds it): a
+//    warp's 32 outputs then read consecutive banks per input, the input a broadcast.
+// Shared memory: w1t [C][M], w2t [M][G], ctx [nseg_max][C], hid [nseg_max][M],
+// red [2048].
 __global__ void __launch_bounds__(256)
 cam_gate_kernel(const __half* __restrict__ cc, int ldc, const int* __restrict__ tv, int T,
-                int pad, int C, int seg, int nseg_max, const float* __restrict__ w1t,
-                const float* __restrict__ b1, int M, const float* __restrict__ w2t,
+                int pad, int C, int seg, int nseg_max, const float* __restrict__ w1t_g,
+                const float* __restrict__ b1, int M, const float* __restrict__ w2t_g,
                 const float* __restrict__ b2, int G, float* __restrict__ gate) {
     extern __shared__ float sm[];
     const int b = blockIdx.x;
     const int tvb = min(tv[b], T);
     const int nseg = (tvb + seg - 1) / seg;
-    float* ctx = sm;
+    float* w1t = sm;
+    float* w2t = w1t + C * M;
+    float* ctx = w2t + M * G;
     float* hid = ctx + (size_t)nseg_max * C;
     float* red = hid + (size_t)nseg_max * M;
     const int tid = threadIdx.x;
+    {
+        const float4* a = reinterpret_cast<const float4*>(w1t_g);
+        float4* d = reinterpret_cast<float4*>(w1t);
+#pragma unroll 8
+        for (int i = tid; i < C * M / 4; i += 256) d[i] = __ldg(a + i);
+        const float4* a2 = reinterpret_cast<const float4*>(w2t_g);
+        float4* d2 = reinterpret_cast<float4*>(w2t);
+#pragma unroll 4
+        for (int i = tid; i < M * G / 4; i += 256) d2[i] = __ldg(a2 + i);
+    }
     const int groups = C / 8, lanes = 256 / groups;
     const int g = tid % groups, ln = tid / groups;
     const __half* xb = cc + ((long long)b * (T + 2 * pad) + pad) * ldc + g * 8;
@@ -94,7 +109,7 @@ cam_gate_kernel(const __half* __restrict__ cc, int ldc, const int* __restrict__ 
         const float* x = ctx + r * C;
         float v = 0.0f;
 #pragma unroll 16
-        for (int c = 0; c < C; ++c) v = fmaf(__ldg(w1t + (size_t)c * M + j), x[c], v);
+        for (int c = 0; c < C; ++c) v = fmaf(w1t[c * M + j], x[c], v);
         hid[u] = fmaxf(v + __ldg(b1 + j), 0.0f);
     }
     __syncthreads();
@@ -103,27 +118,27 @@ cam_gate_kernel(const __half* __restrict__ cc, int ldc, const int* __restrict__ 
         const float* x = hid + r * M;
         float v = 0.0f;
 #pragma unroll 16
-        for (int j = 0; j < M; ++j) v = fmaf(__ldg(w2t + (size_t)j * G + k), x[j], v);
+        for (int j = 0; j < M; ++j) v = fmaf(w2t[j * G + k], x[j], v);
         gate[((long long)b * nseg_max + r) * G + k] = 1.0f / (1.0f + expf(-(v + __ldg(b2 + k))));
     }
 }
 
 }  // namespace
 
-size_t campp_gate_smem(int C, int M, int nseg_max) {
-    return ((size_t)nseg_max * (C + M) + 2048) * sizeof(float);
+size_t campp_gate_smem(int C, int M, int G, int nseg_max) {
+    return ((size_t)C * M + (size_t)M * G + (size_t)nseg_max * (C + M) + 2048) * sizeof(float);
 }
 
 int campp_cam_gate(const __half* cc, int ldc, const int* tv, int batch, int T, int pad, int C,
                    int seg, int nseg_max, const float* w1t, const float* b1, int M,
                    const float* w2t, const float* b2, int G, float* gate, cudaStream_t st) {
     if (C % 8 != 0 || C > 2048 || 256 % (C / 8) != 0 || ldc % 8 != 0 || seg < 1 ||
-        (long long)nseg_max * seg < T) {
+        (long long)nseg_max * seg < T || (C * M) % 4 != 0 || (M * G) % 4 != 0) {
         set_error("campplus: CAM context needs C a multiple of 8 dividing 2048 and "
                   "nseg_max * seg >= T");
         return 1;
     }
-    const size_t smem = campp_gate_smem(C, M, nseg_max);
+    const size_t smem = campp_gate_smem(C, M, G, nseg_max);
     if (smem > 200 * 1024) {
         set_error("campplus: clip too long for the CAM gate kernel (" +
                   std::to_string(nseg_max) + " context segments)");

@@ -75,7 +75,7 @@ int ecapa_asp_pool(const float* logits, int ldl, const __half* x, int ldx, const
 // transposed: w1t f32 [C][M], w2t f32 [M][G].
 int seq_meanstd_unbiased(const __half* x, int ldx, const int* tv, int batch, int T, int pad,
                          int C, float* stats, cudaStream_t st);
-size_t campp_gate_smem(int C, int M, int nseg_max);
+size_t campp_gate_smem(int C, int M, int G, int nseg_max);
 int campp_cam_gate(const __half* cc, int ldc, const int* tv, int batch, int T, int pad, int C,
                    int seg, int nseg_max, const float* w1t, const float* b1, int M,
                    const float* w2t, const float* b2, int G, float* gate, cudaStream_t st);
