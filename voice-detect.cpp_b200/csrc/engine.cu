@@ -1236,18 +1236,19 @@ void Engine::plan_buckets(const int* nsamp, int n, long long frame_cap, std::vec
     }
 }
 
-// Copies clips into one pinned buffer, splitting the bytes over a few threads
-// when there are many (a single core's memcpy would not keep up with the GPU).
+// Copies clips into one pinned buffer, splitting the bytes over threads (one per
+// 4 MB, at most 16 and the host's cores): one core's memcpy moves ~5 GB/s, and with
+// 8 MB per thread the gather of a 128-clip bucket of 4 s clips took longer than its
+// compute, which bounded the host-PCM path at half the device rate.
 // Gather `count` clips (elements of `esz` bytes; clip idx[k] has nsamp[idx[k]]
-// elements at pcm[idx[k]]) back to back into dst, with up to 8 threads splitting the
-// byte range.
+// elements at pcm[idx[k]]) back to back into dst.
 static void gather_clips(char* dst, const void* const* pcm, const int* nsamp, size_t esz,
                          const int* idx, int count) {
     std::vector<size_t> off((size_t)count + 1, 0);
     for (int k = 0; k < count; ++k) off[k + 1] = off[k] + (size_t)nsamp[idx[k]] * esz;
     const size_t total = off[count];
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const int nt = (int)std::min<size_t>(std::min(8u, hw), 1 + total / (16u << 20));
+    const int nt = (int)std::min<size_t>(std::min(16u, hw), 1 + total / (4u << 20));
     auto work = [&](int t) {
         // thread t copies the byte range [t*total/nt, (t+1)*total/nt)
         const size_t lo = total * t / nt, hi = total * (t + 1) / nt;
@@ -1311,11 +1312,14 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
             return 1;
         }
     }
-    // At least ~4 buckets when the call is large enough, so that the host gather and
-    // the H2D copy of one bucket hide behind the compute of the previous one.
+    // At least 2 buckets when the call is large enough, so that the host gather and
+    // the H2D copy of one bucket hide behind the compute of the other. Not more: a
+    // bucket too small to fill the GPU costs more device time than the overlap saves
+    // (CAM++, 512 x 4 s clips: one 128-clip bucket 3.5 ms of device time against 8.9 ms
+    // for all 512 at once, so four of them made the call slower than no split).
     long long frames_total = 0;
     for (int i = 0; i < n; ++i) frames_total += frames_of(ns[i], cfg_.win, cfg_.hop);
-    const long long cap = std::min<long long>(max_frames, std::max<long long>(frames_total / 4, 16384));
+    const long long cap = std::min<long long>(max_frames, std::max<long long>(frames_total / 2, 16384));
     std::vector<int> order;
     std::vector<size_t> bk;
     plan_buckets(ns.data(), n, cap, order, bk);
