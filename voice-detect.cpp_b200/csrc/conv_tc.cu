@@ -676,6 +676,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above reads only data that existed before the previous kernel on the
+    // stream started (weights, bias, BN scale / shift, per-clip lengths), so the next
+    // conv may run up to this point while this one finishes (its CTAs take SMs as ours
+    // leave); nothing below starts before the previous kernel has completed.
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    pdl_wait();
 
     const int n_tiles = p.n_mt * p.n_nt;
     const uint32_t idesc = umma_idesc_f16(PAIR ? 2 * kMB : kMB, p.BN);
@@ -1721,8 +1727,19 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         if (cs == cudaStreamCaptureStatusNone)
             VDB_CHECK_CUDA(
                 cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
-        kern<<<grid, kThreads, smem_launch, st>>>(tm[0], tm[1], tm[2], tm[3], p);
-        VDB_CHECK_CUDA(cudaGetLastError());
+        // programmatic stream serialization: the prologue (barriers, TMEM, bias and
+        // lengths in shared memory) overlaps the previous conv's last tiles
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem_launch;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
         return 0;
     };
     if (pair) {
@@ -1737,13 +1754,15 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem_launch;
         cfg.stream = st;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 2;
         VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
         return 0;
     }

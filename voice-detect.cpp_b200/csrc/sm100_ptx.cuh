@@ -37,6 +37,15 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch (a kernel launched with programmatic stream
+// serialization may start before the previous kernel on its stream has finished):
+// pdl_wait blocks until that kernel has completed and its memory is visible (a no-op
+// without the launch attribute); pdl_launch_dependents lets the next such kernel start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
