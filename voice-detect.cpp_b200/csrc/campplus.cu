@@ -15,6 +15,7 @@
 #include <cmath>
 #include <string>
 
+#include "sm100_ptx.cuh"
 #include "vdb_internal.h"
 #include "vdb_ops.h"
 
@@ -41,6 +42,10 @@ cam_gate_kernel(const __half* __restrict__ cc, int ldc, const int* __restrict__ 
                 const float* __restrict__ b1, int M, const float* __restrict__ w2t_g,
                 const float* __restrict__ b2, int G, float* __restrict__ gate) {
     extern __shared__ float sm[];
+    // launched with programmatic stream serialization: the gate conv that follows may
+    // start its prologue now; every read below waits for the bottleneck conv
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x;
     const int tvb = min(tv[b], T);
     const int nseg = (tvb + seg - 1) / seg;
@@ -150,9 +155,18 @@ int campp_cam_gate(const __half* cc, int ldc, const int* tv, int batch, int T, i
         VDB_CHECK_CUDA(cudaFuncSetAttribute(cam_gate_kernel,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             200 * 1024));
-    cam_gate_kernel<<<batch, 256, smem, st>>>(cc, ldc, tv, T, pad, C, seg, nseg_max, w1t, b1, M,
-                                              w2t, b2, G, gate);
-    VDB_CHECK_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)batch);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, cam_gate_kernel, cc, ldc, tv, T, pad, C, seg, nseg_max,
+                                      w1t, b1, M, w2t, b2, G, gate));
     return 0;
 }
 
