@@ -114,6 +114,9 @@ typedef struct vdb_conv_args {
     const void* addend;
     int ldaddend;
     int y_pad;              /* y_phase 3: padding rows P of the 1-D consumer's slots */
+    int tile_n;             /* 0 auto (oc in <= 256-column tiles), else output columns per
+                               tile: a multiple of 16 dividing oc (the HALO feeds need one
+                               tile) */
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */

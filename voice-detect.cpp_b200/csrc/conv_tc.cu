@@ -1368,12 +1368,13 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         return 1;
     }
     int n_nt = (a->oc + 255) / 256;
-    if (seq && sq->tile_n) {
-        if (sq->tile_n % 16 != 0 || sq->tile_n > 256 || a->oc % sq->tile_n != 0) {
-            set_error("vdb_conv1d: tile_n must be a multiple of 16, <= 256, dividing oc");
+    const int tile_n = seq ? sq->tile_n : a->tile_n;
+    if (tile_n) {
+        if (tile_n % 16 != 0 || tile_n > 256 || a->oc % tile_n != 0) {
+            set_error("vdb_conv: tile_n must be a multiple of 16, <= 256, dividing oc");
             return 1;
         }
-        n_nt = a->oc / sq->tile_n;
+        n_nt = a->oc / tile_n;
     }
     const int BN = a->oc / n_nt;
     if (BN % 16 != 0 || BN * n_nt != a->oc) {
