@@ -86,7 +86,7 @@ typedef struct vdb_conv_args {
     int* err;               /* device int32 error word (may be NULL): kernel timeouts */
     /* tiling (0 = automatic) */
     int tile_m;             /* output rows per CTA tile: 0, 128 or 256 */
-    int halo;               /* feed of a stride-1 3x3 (mode 1 also of a stride-3 one): 0 auto,
+    int halo;               /* feed of a stride-1 3x3 (mode 1 also of stride-2 / 3 ones): 0 auto,
                                -1 never (one A tile per tap),
                                1 one input halo per channel block feeding all nine taps with
                                the weights resident (<= 96 KB), 2 the same halo with the

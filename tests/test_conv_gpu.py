@@ -61,7 +61,8 @@ def valid_tilings(IC, OC, k, stride, two_segments=False):
     kb = 64 if IC % 64 == 0 else (32 if IC % 32 == 0 else 16)
     ks = kb // 16
     hs_ok = k == 3 and stride == 1 and OC <= 256
-    halo_ok = hs_ok and 9 * IC * bn * 2 <= 96 * 1024
+    # the resident-weight halo also feeds stride-2 3x3 convs (one halo per PHASE plane)
+    halo_ok = k == 3 and stride in (1, 2) and OC <= 256 and 9 * IC * bn * 2 <= 96 * 1024
     out = []
     for tile_m in (128, 256):
         nmb = tile_m // 128
@@ -143,7 +144,7 @@ def test_conv_vs_reference(cuda_lib, case):
     ref = _ref_conv(x, w, bias, stride, x1=x1, w1=w1, stride1=stride, residual=residual,
                     relu=True, tvalid_out=tvalid_out, use_oracle=small)
     # every tiling the kernel offers: automatic, 128/256-row tiles, and the
-    # shared-halo feed where the layer qualifies (stride 1, 3x3, resident weights)
+    # shared-halo feed where the layer qualifies (3x3 stride 1 or 2, resident weights)
     configs = [(0, 0, 0)] + valid_tilings(IC, OC, k, stride, two_segments=fused_down)
     wp = vd.pack_conv_weight(w.to(dev))
     for tile_m, halo, ksplit in configs:

@@ -76,7 +76,9 @@ struct SegDev {
     int plane[9];
     int off[9];      // TAP: global row offset per tap; HALO: row offset inside the halo
     int halo_back;   // HALO: rows before m0 covered by the halo
-    uint32_t plane_bytes;  // HALO over FPHASE (stride 3): offset of the plane-1 halo, else 0
+    uint32_t plane_bytes;  // HALO over FPHASE / PHASE: bytes between the planes' halos, else 0
+    int halo_planes;       // HALO: planes loaded per channel block (1, FPHASE 2, PHASE 4)
+    int halo_mode;         // HALO tap geometry: 0 stride 1, 1 FPHASE, 2 PHASE
     int dil;         // 1-D: tap j reads j*dil rows into a HALO (taps at (j - (k-1)/2)*dil)
     int n_box, box_rows;  // TMA A boxes per stage and their height (TAP: BM split in <= 256)
     uint32_t bres;   // HALO: resident weights, byte offset from the smem base
@@ -495,22 +497,35 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 
 // HALO stage: nine taps of a 3x3 stride-1 conv read one shared input halo through
 // row-shifted descriptors; tap (kt, kf) starts kt*wp_units + kf*rb16 in.
-// plane_units != 0: the halo is FPHASE (a frequency-stride-2 input), two planes
-// plane_units apart; tap (kt, kf) reads plane kf&1 at kt rows of Wp and kf>>1 rows in.
+// Tap (kt, kf) of a halo starts row(kt) + col(kf) 16-byte units in, by mode:
+//   0 stride 1: kt*Wp + kf rows;
+//   1 FPHASE (frequency-stride-2 input, 2 planes plane_units apart): plane kf&1,
+//     kt*Wp + (kf>>1) rows;
+//   2 PHASE (stride-2 input, 4 planes): plane 2*(kt&1) + (kf&1), (kt>>1)*Wp + (kf>>1)
+//     rows.
 template <int KS, int NMB, int J>
 __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                            uint32_t wp_units, uint32_t rb16, uint64_t b_desc,
                                            uint32_t b_tap_units, uint32_t idesc, bool first,
-                                           uint32_t plane_units) {
-    // column offsets of kf = 1, 2 (kf = 0 is 0), chosen once: the loop below is the
+                                           int hmode, uint32_t plane_units) {
+    // offsets of kt, kf = 1, 2 (0 for 0), chosen once: the loop below is the
     // issue-bound inner loop of the small-channel convs
-    const uint32_t col1 = plane_units ? plane_units : rb16;
-    const uint32_t col2 = plane_units ? rb16 : 2 * rb16;
+    uint32_t row1 = wp_units, row2 = 2 * wp_units, col1 = rb16, col2 = 2 * rb16;
+    if (hmode == 1) {
+        col1 = plane_units;
+        col2 = rb16;
+    } else if (hmode == 2) {
+        row1 = 2 * plane_units;
+        row2 = wp_units;
+        col1 = plane_units;
+        col2 = rb16;
+    }
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
-        const int kf = tap % 3;
+        const int kt = tap / 3, kf = tap % 3;
+        const uint32_t row = kt == 0 ? 0u : (kt == 1 ? row1 : row2);
         const uint32_t col = kf == 0 ? 0u : (kf == 1 ? col1 : col2);
-        const uint64_t at = a_desc + (uint64_t)((tap / 3) * wp_units + col);
+        const uint64_t at = a_desc + (uint64_t)(row + col);
         const uint64_t bt = b_desc + (uint64_t)(tap * b_tap_units);
 #pragma unroll
         for (int k = 0; k < KS; ++k) {
@@ -577,16 +592,16 @@ template <int NMB, int J, bool PAIR>
 __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
                                             uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
                                             uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
-                                            bool first, uint32_t plane_units = 0,
+                                            bool first, int hmode = 0, uint32_t plane_units = 0,
                                             int taps1d = 0, uint32_t dil_units = 0) {
     if (!PAIR && halo && taps1d) {
         if (ks == 4) issue_halo1d<4, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
         else if (ks == 2) issue_halo1d<2, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
         else issue_halo1d<1, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
     } else if (!PAIR && halo) {
-        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
-        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
-        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, plane_units);
+        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
+        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
+        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
     } else {
         if (ks == 4) issue_tap<4, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
         else if (ks == 2) issue_tap<2, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
@@ -801,10 +816,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                             for (int bx = 0; bx < s.n_box; ++bx)
                                 tma_load_3d(sa + bx * box_bytes, ta, fb, it * s.kb,
                                             m0 - s.halo_back + bx * s.box_rows, 0);
-                            if (s.plane_bytes)  // FPHASE: the odd-frequency plane's halo
+                            // FPHASE / PHASE: the other planes' halos
+                            for (int q = 1; q < s.halo_planes; ++q)
                                 for (int bx = 0; bx < s.n_box; ++bx)
-                                    tma_load_3d(sa + s.plane_bytes + bx * box_bytes, ta, fb,
-                                                it * s.kb, m0 - s.halo_back + bx * s.box_rows, 1);
+                                    tma_load_3d(sa + q * s.plane_bytes + bx * box_bytes, ta, fb,
+                                                it * s.kb, m0 - s.halo_back + bx * s.box_rows, q);
                         } else {
                             const int tap = it / s.n_kb, kbi = it - tap * s.n_kb;
                             const uint32_t box_bytes = (uint32_t)s.box_rows * s.kb * 2;
@@ -918,7 +934,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
                         issue_stage<NMB, J, PAIR>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc,
                                                   wp_units, rb16, b_desc, b_tap_units, idesc, first,
-                                                  s.plane_bytes >> 4, SEQ ? s.n_taps : 0,
+                                                  s.halo_mode, s.plane_bytes >> 4,
+                                                  SEQ ? s.n_taps : 0,
                                                   SEQ ? (uint32_t)s.dil * rb16 : 0u);
                         first = false;
                         if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
@@ -1419,6 +1436,8 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // (stride 3): one halo per plane, the 9 taps as row shifts inside them.
     const bool hs_ok = !seq && a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
     const bool fph = !seq && a->k0 == 3 && a->stride0 == 3;
+    const bool ph2 = !seq && a->k0 == 3 && a->stride0 == 2;  // PHASE: 4 plane halos
+    const int hplanes = ph2 ? 4 : (fph ? 2 : 1);
     // 1-D: one halo of tile + 2*reach rows per channel block feeds every tap (weights
     // resident); automatic for narrow outputs (<= 64 columns: CAM++'s 32-column k=3
     // convs), where the per-tap stages cost more than their MMAs.
@@ -1426,7 +1445,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
                              !sq->x_scale && sq->pair != 1 &&
                              (uint32_t)a->k0 * a->ic0 * BN * 2 <= 96 * 1024;
     const bool halo_ok = seq ? seq_halo_ok
-                             : (hs_ok || (fph && n_nt == 1)) && w_bytes0 <= 96 * 1024;
+                             : (hs_ok || ((fph || ph2) && n_nt == 1)) && w_bytes0 <= 96 * 1024;
     if (a->halo < -1 || a->halo > 2 || (seq && a->halo > 1)) {
         set_error("vdb_conv: halo must be -1, 0, 1 or 2");
         return 1;
@@ -1434,9 +1453,9 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const bool halo = a->halo == 0 ? halo_ok && (!seq || BN <= 64) : (a->halo == 1 && halo_ok);
     const bool two_ring = a->halo == 2 && hs_ok;
     if ((a->halo == 1 && !halo_ok) || (a->halo == 2 && !hs_ok)) {
-        set_error("vdb_conv: HALO modes need a 3x3 conv with oc <= 256, stride 1 (or the "
-                  "frequency-only stride 3 for the resident HALO) and weights <= 96 KB for "
-                  "the resident HALO");
+        set_error("vdb_conv: HALO modes need a 3x3 conv with oc <= 256, stride 1 (or stride "
+                  "2 / the frequency-only stride 3 for the resident HALO) and weights <= 96 KB "
+                  "for the resident HALO");
         return 1;
     }
     // Tiling. A tcgen05.mma that accumulates into the same TMEM tile as the one
@@ -1464,12 +1483,12 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             const int tail = round_up(a->oc * 4, 16) + round_up(a->batch * 4, 16) +
                              8 * (3 * kMaxStages + 5) + 16;
             for (int cand : {8, 4, 3}) {
-                const int H = cand * kMB + 2 * Hs + (fph ? 1 : 0);
+                const int H = ph2 ? cand * kMB + Wp + 1 : cand * kMB + 2 * Hs + (fph ? 1 : 0);
                 const int nbox = (H + 255) / 256;
                 const int box = round_up((H + nbox - 1) / nbox, 8);
                 const int kb = a->ic0 % 64 == 0 ? 64 : (a->ic0 % 32 == 0 ? 32 : 16);
                 long long a_b = (long long)nbox * box * kb * 2, b_b = 0;
-                if (fph) a_b += round_up((int)a_b, 1024);  // the second plane's halo
+                a_b += (long long)(hplanes - 1) * round_up((int)a_b, 1024);  // other planes
                 if (a->x1) {  // segment 1 stages hold its A rows and a weight tile
                     const int kb1 = a->ic1 % 64 == 0 ? 64 : (a->ic1 % 32 == 0 ? 32 : 16);
                     a_b = std::max<long long>(a_b, (long long)cand * kMB * kb1 * 2);
@@ -1553,19 +1572,24 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             // stride 1: taps at kt*Wp + kf rows into a halo from m0 - (Wp + 1); FPHASE:
             // taps at kt*Wp + (kf>>1) rows into plane kf&1's halo from m0 - Wp
             const int reach = seq ? (a->k0 - 1) / 2 * sq->dil0 : 0;
-            const int H = seq ? BM + 2 * reach : (fph ? BM + 2 * Wp + 1 : BM + 2 * Wp + 2);
-            s.halo_back = seq ? reach : (fph ? Wp : Wp + 1);
+            // PHASE: taps at (kt>>1)*Wp + (kf>>1) rows into plane 2(kt&1)+(kf&1)'s
+            // halo from m0
+            const int H = seq ? BM + 2 * reach
+                              : (ph2 ? BM + Wp + 1 : (fph ? BM + 2 * Wp + 1 : BM + 2 * Wp + 2));
+            s.halo_back = seq ? reach : (ph2 ? 0 : (fph ? Wp : Wp + 1));
             s.n_box = (H + 255) / 256;
             s.box_rows = round_up((H + s.n_box - 1) / s.n_box, 8);
             for (int t = 0; t < 9; ++t) s.off[t] = (t / 3) * Wp + (t % 3);  // kt*Wp + kf
             const uint32_t one = (uint32_t)s.n_box * s.box_rows * row_bytes;
-            s.plane_bytes = fph ? (uint32_t)round_up((int)one, 1024) : 0u;
-            s.bytes = fph ? 2 * one : one;
+            s.halo_planes = seq ? 1 : hplanes;
+            s.halo_mode = seq ? 0 : (ph2 ? 2 : (fph ? 1 : 0));
+            s.plane_bytes = s.halo_planes > 1 ? (uint32_t)round_up((int)one, 1024) : 0u;
+            s.bytes = (uint32_t)s.halo_planes * one;
             s.bres = off;
             const uint32_t w = (uint32_t)s.n_taps * s.n_kb * BN * row_bytes;
             off += w;
             p.bres_bytes += w;
-            a_bytes = std::max(a_bytes, s.plane_bytes + one);
+            a_bytes = std::max(a_bytes, (uint32_t)(s.halo_planes - 1) * s.plane_bytes + one);
         } else {
             s.mode = SEG_TAP;
             s.n_box = (cta_rows + 255) / 256;
