@@ -1,5 +1,10 @@
 #include "gguf.hpp"
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <cstdio>
 #include <cstring>
 
@@ -102,28 +107,46 @@ bool ggml_row_bytes(uint32_t type, int64_t n0, size_t& bytes) {
 
 }  // namespace
 
+Gguf::~Gguf() {
+    if (map_) munmap(map_, map_len_);
+}
+
 bool Gguf::load(const std::string& path, std::string& err) {
-    FILE* f = std::fopen(path.c_str(), "rb");
-    if (!f) {
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) {
         err = "cannot open GGUF: " + path;
         return false;
     }
-    std::fseek(f, 0, SEEK_END);
-    const long sz = std::ftell(f);
-    std::fseek(f, 0, SEEK_SET);
-    if (sz < 24) {
-        std::fclose(f);
+    struct stat st {};
+    if (fstat(fd, &st) != 0 || st.st_size < 24) {
+        ::close(fd);
         err = "GGUF too small: " + path;
         return false;
     }
-    buf_.resize((size_t)sz);
-    const size_t got = std::fread(buf_.data(), 1, buf_.size(), f);
-    std::fclose(f);
-    if (got != buf_.size()) {
-        err = "short read: " + path;
-        return false;
+    const size_t sz = (size_t)st.st_size;
+    void* m = mmap(nullptr, sz, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (m != MAP_FAILED) {
+        map_ = m;
+        map_len_ = sz;
+        data_ = static_cast<const uint8_t*>(m);
+    } else {
+        buf_.resize(sz);
+        size_t got = 0;
+        while (got < sz) {
+            const ssize_t r = ::read(fd, buf_.data() + got, sz - got);
+            if (r <= 0) break;
+            got += (size_t)r;
+        }
+        if (got != sz) {
+            ::close(fd);
+            err = "short read: " + path;
+            return false;
+        }
+        data_ = buf_.data();
     }
-    Cursor c{buf_.data(), buf_.data() + buf_.size()};
+    ::close(fd);
+    size_ = sz;
+    Cursor c{data_, data_ + size_};
     const uint32_t magic = c.get<uint32_t>();
     if (magic != 0x46554747u) {  // "GGUF"
         err = "not a GGUF file (bad magic): " + path;
@@ -188,7 +211,7 @@ bool Gguf::load(const std::string& path, std::string& err) {
     uint64_t align = 32;
     auto it = kv_.find("general.alignment");
     if (it != kv_.end() && it->second.num > 0) align = (uint64_t)it->second.num;
-    const uint64_t pos = (uint64_t)(c.p - buf_.data());
+    const uint64_t pos = (uint64_t)(c.p - data_);
     const uint64_t data0 = (pos + align - 1) / align * align;
     for (GgufTensor& t : infos) {
         size_t row = 0;
@@ -204,11 +227,11 @@ bool Gguf::load(const std::string& path, std::string& err) {
         size_t nb = row;
         for (size_t d = 1; d < t.ne.size(); ++d) nb *= (size_t)t.ne[d];
         t.nbytes = nb;
-        if (data0 + t.offset + nb > buf_.size() || data0 + t.offset < data0) {
+        if (data0 + t.offset + nb > size_ || data0 + t.offset < data0) {
             err = "tensor '" + t.name + "' extends past the end of the file (truncated GGUF?)";
             return false;
         }
-        t.data = buf_.data() + data0 + t.offset;
+        t.data = data_ + data0 + t.offset;
         tensors_[t.name] = t;
     }
     return true;

@@ -46,7 +46,13 @@ struct GgufTensor {
 
 class Gguf {
 public:
-    // Returns false (and sets err) on a missing, truncated or malformed file.
+    Gguf() = default;
+    ~Gguf();
+    Gguf(const Gguf&) = delete;
+    Gguf& operator=(const Gguf&) = delete;
+    // Returns false (and sets err) on a missing, truncated or malformed file. The file
+    // is memory-mapped read-only (tensor data is read in place, never copied whole);
+    // where mapping fails it is read into memory instead.
     bool load(const std::string& path, std::string& err);
 
     bool has(const std::string& key) const { return kv_.count(key) != 0; }
@@ -65,7 +71,11 @@ public:
     size_t n_tensors() const { return tensors_.size(); }
 
 private:
-    std::vector<uint8_t> buf_;
+    std::vector<uint8_t> buf_;      // the file, when it could not be mapped
+    void* map_ = nullptr;           // the read-only mapping, or null
+    size_t map_len_ = 0;
+    const uint8_t* data_ = nullptr;  // file bytes (mapping or buf_)
+    size_t size_ = 0;
     uint32_t version_ = 0;
     std::map<std::string, GgufValue> kv_;
     std::map<std::string, GgufTensor> tensors_;
