@@ -296,3 +296,20 @@ def test_campplus_small_model_f32(tmp_path_factory, cuda_lib):
             assert _cos(got[i], _oracle(m, c)) >= COS_TOL, i
     finally:
         model.close()
+
+
+def test_campplus_q8_0(tmp_path_factory, cuda_lib):
+    """q8_0 GGUF: the 1x1 Conv1d weights quantised (squeezed to [OC, IC], the
+    converter's rule for rank <= 3 weights), dequantised at load."""
+    m = vd_synth.campplus_model(5, m_channels=16, init_channels=64, growth=32, bn_size=2,
+                                layers=(2, 2, 2), emb_dim=48)
+    model = _model(tmp_path_factory, cuda_lib, m, "q8_0", "campplus_q8.gguf")
+    try:
+        mq = vd_synth.q8_campplus_model(m)
+        clips = [vd_synth.clip_f32(vd_synth.make_clip(800 + i, n))
+                 for i, n in enumerate([40000, 12000])]
+        got = model.embed_batch(clips)
+        for i, c in enumerate(clips):
+            assert _cos(got[i], _oracle(mq, c)) >= COS_TOL, i
+    finally:
+        model.close()

@@ -904,8 +904,11 @@ def campplus_forward_torch(m: dict, feats, calibrate: bool = False):
 
 def write_campplus_gguf(path: str, m: dict, dtype: str = "f32") -> None:
     """campplus GGUF with the reference's manifest keys (voicedetect.campplus.*,
-    src/model_loader.cpp:165-172). dtype f32 | f16 (conv weights)."""
+    src/model_loader.cpp:165-172). dtype f32 | f16 (conv weights) | q8_0 (the 1x1
+    Conv1d weights whose input width is a multiple of 32 squeezed to [OC, IC] and
+    quantised, the converter's rule for rank <= 3 weights; the other convs f16)."""
     import gguf
+    from gguf import quants
 
     w = gguf.GGUFWriter(path, arch="voicedetect")
     w.add_string("voicedetect.arch", "campplus")
@@ -945,7 +948,10 @@ def write_campplus_gguf(path: str, m: dict, dtype: str = "f32") -> None:
     w.add_float32("voicedetect.campplus.bn_eps", float(m["bn_eps"]))
     for name, arr, kind in tensors:
         arr = np.ascontiguousarray(arr, np.float32)
-        if dtype == "f16" and kind == "conv" and arr.shape[1] > 1:
+        if dtype == "q8_0" and kind == "conv" and _campplus_q8(arr):
+            qb = quants.quantize(np.ascontiguousarray(arr[:, :, 0]), gguf.GGMLQuantizationType.Q8_0)
+            w.add_tensor(name, qb, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        elif dtype in ("f16", "q8_0") and kind == "conv" and arr.shape[1] > 1:
             w.add_tensor(name, arr.astype(np.float16))
         else:
             w.add_tensor(name, arr)
@@ -959,4 +965,29 @@ def f16_campplus_model(m: dict) -> dict:
     """The weights an f16 GGUF carries (conv weights with IC > 1 rounded)."""
     convs = [dict(c, w=c["w"].astype(np.float16).astype(np.float32)) if c["w"].shape[1] > 1
              else c for c in m["convs"]]
+    return dict(m, convs=convs)
+
+
+def _campplus_q8(w: np.ndarray) -> bool:
+    """A 1x1 Conv1d weight [OC, IC, 1] whose rows split into q8_0 blocks of 32."""
+    return w.ndim == 3 and w.shape[2] == 1 and w.shape[1] % 32 == 0
+
+
+def q8_campplus_model(m: dict) -> dict:
+    """The weights a q8_0 GGUF carries: quantisable 1x1 convs round-tripped through
+    q8_0, the other convs with IC > 1 through f16."""
+    import gguf
+    from gguf import quants
+    qt = gguf.GGMLQuantizationType.Q8_0
+    convs = []
+    for c in m["convs"]:
+        w = c["w"]
+        if _campplus_q8(w):
+            a2 = np.ascontiguousarray(w[:, :, 0], np.float32)
+            r = quants.dequantize(quants.quantize(a2, qt), qt).reshape(a2.shape)
+            convs.append(dict(c, w=r[:, :, None].astype(np.float32)))
+        elif w.shape[1] > 1:
+            convs.append(dict(c, w=w.astype(np.float16).astype(np.float32)))
+        else:
+            convs.append(c)
     return dict(m, convs=convs)
