@@ -119,7 +119,14 @@ typedef struct vdb_conv_args {
                                tile) */
 } vdb_conv_args;
 
-/* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate). */
+/* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate).
+ * Launch ordering: vdb_conv and vdb_conv1d launch with programmatic stream
+ * serialization, so a conv may start while the kernel launched just before it on
+ * `stream` is still running. Before it waits for that kernel, the conv reads only
+ * `bias`, `bn_scale` / `bn_shift` and `tvalid`: these must not be written by the
+ * kernel launched immediately before the conv on the same stream (a copy, an event
+ * from another stream, or any earlier kernel is fine). Every other input, the
+ * weights included, is read after that kernel has completed. */
 int vdb_conv(const vdb_conv_args* a, void* stream);
 
 /* ---- 1-D (TDNN) convs: the ECAPA-TDNN path ---------------------------------------
@@ -204,6 +211,7 @@ typedef struct vdb_conv1d_args {
                                every tap, weights resident (<= 96 KB) */
 } vdb_conv1d_args;
 
+/* Same launch ordering rule as vdb_conv. */
 int vdb_conv1d(const vdb_conv1d_args* a, void* stream);
 
 /* ---- Audio ingest ----------------------------------------------------------------
