@@ -42,8 +42,9 @@ CLIPS_PER_GPU = 8192
 POOL = 64            # distinct synthetic sources the clips are cut from
 SEED = 20261201
 METRIC = "utterance-sec/sec ResNet34 embed"
-# DRAM bytes (read + write) per algorithmic conv FLOP, measured with ncu on this
-# workload at the same bucket sizes (see profiles/launches__bench_c4_512clips.md).
+# DRAM bytes (read + write) per algorithmic conv FLOP, measured with ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum over every conv launch) on this
+# workload at the same bucket sizes: 344.6 GB over 77.4 TFLOP.
 CONV_DRAM_BYTES_PER_FLOP = 4.45e-3
 UNIT = "utterance-sec/sec"
 E2E_WARMUP = 2  # untimed public-API calls before the e2e timing (see run_b200)
