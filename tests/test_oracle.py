@@ -261,3 +261,19 @@ def test_campplus_manifest_and_gguf(tmp_path):
     kv = {f.name for f in r.fields.values()}
     assert {"voicedetect.campplus.conv_weight", "voicedetect.campplus.bn_prefix",
             "voicedetect.campplus.emb_bn_mean"} <= kv
+
+
+@pytest.mark.parametrize("T", [1, 3, 199, 201])
+def test_campplus_oracle_edge_lengths(T):
+    """CAM++ oracle vs the float64 torch formulation at the lengths where the forward
+    changes shape: one TDNN frame (no std correction), exactly one 100-frame context
+    segment, and one frame into a second segment."""
+    m = vd_synth.tiny_campplus_model(9, n_mels=80)
+    rng = np.random.default_rng(T)
+    feats = (rng.standard_normal((80, T)) * 1.5).astype(np.float32)
+    emb, pre = oracle.campplus_embed(m, feats)
+    torch = pytest.importorskip("torch")
+    temb, tpre = vd_synth.campplus_forward_torch(
+        m, torch.from_numpy(feats[None].astype(np.float64)))
+    assert np.abs(pre - tpre[0]).max() <= 1e-4 * max(1.0, np.abs(tpre[0]).max())
+    assert _cos(emb, temb[0]) >= 0.999999
