@@ -6,8 +6,10 @@ Two ABI levels are exposed, mirroring the headers in include/:
   wrapped by :class:`Model`;
 * the op-level ABI, ``vdb_*`` (include/vdb_ops.h): the conv / FBank / pooling
   kernels on device buffers, wrapped by :func:`conv` etc. The layout helpers
-  (:func:`to_grid`, :func:`to_phase`, :func:`from_grid`) build the GRID / PHASE
-  activation layouts that header defines, using torch on the device.
+  (:func:`to_grid` / :func:`from_grid`, :func:`to_phase` / :func:`from_phase`,
+  :func:`to_fphase` / :func:`from_fphase`, :func:`to_seq` / :func:`from_seq`,
+  :func:`to_tphase` / :func:`from_tphase`) build and read the GRID / PHASE / FPHASE /
+  SEQ / TPHASE activation layouts that header defines, with torch (on any device).
 
 There is no CPU fallback: importing works without a GPU, but every compute call
 goes to the CUDA library and raises if it is missing or fails.
