@@ -62,7 +62,9 @@ def test_load_rejects_corrupt_gguf(tmp_path):
     truncated.write_bytes(data[: len(data) // 2])
     empty = tmp_path / "empty.gguf"
     empty.write_bytes(b"")
-    for p in (bad_magic, truncated, empty):
+    missing = tmp_path / "missing.gguf"
+    # a directory cannot be mapped or read: the loader's plain-read fallback must fail
+    for p in (bad_magic, truncated, empty, missing, tmp_path):
         assert L.voicedetect_capi_load(str(p).encode()) is None
 
 
