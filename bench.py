@@ -292,6 +292,40 @@ def profiled_steps(model, step, steps: int):
             {k: v * f for k, v in stages.items()}, n)
 
 
+def bench_parity(m: dict, host_pcm, offs, lens, d_out, rank: int, world: int, dev) -> dict:
+    """Cosine of 4 timed embeddings of this rank against the reference kernels
+    (oracle/_ref: src/fbank.cpp + blocked src/directconv.cpp ResNet34, restated tail)
+    on the dequantised q8_0 weights; min over the 4 clips and over ranks."""
+    import torch
+    import torch.distributed as dist
+    import oracle
+    n = len(lens)
+    rng = np.random.default_rng(SEED + 100 + rank)
+    order = np.argsort(lens)
+    pick = sorted({int(order[-1]), int(order[0])} |
+                  {int(i) for i in rng.choice(n, 2, replace=False)})
+    got = d_out[:n].cpu().numpy()
+    mq = vd_synth.quantize_q8_0_model(m)
+    if oracle.ref_available():
+        R = oracle.RefResNet34(mq)
+        ref = lambda pcm: R.embed(oracle.ref_fbank(pcm))[0]  # noqa: E731
+        kind = "reference kernels (oracle/_ref), dequantised q8_0 weights"
+    else:
+        ref = lambda pcm: oracle.resnet34_embed(mq, oracle.fbank(pcm))[0]  # noqa: E731
+        kind = "C restatement (oracle/vd_oracle.c), dequantised q8_0 weights"
+    coss = []
+    for i in pick:
+        want = ref(host_pcm[offs[i]:offs[i] + lens[i]]).astype(np.float64)
+        g = got[i].astype(np.float64)
+        coss.append(float(g @ want / (np.linalg.norm(g) * np.linalg.norm(want))))
+    t = torch.tensor([min(coss)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return {"min_cos": float(t.item()), "clips_per_rank": len(pick), "gate": 0.9999,
+            "oracle": kind,
+            "clip_seconds": [round(lens[i] / SR, 2) for i in pick]}
+
+
 def run_b200(args) -> int:
     import torch
     import torch.distributed as dist
@@ -373,6 +407,11 @@ def run_b200(args) -> int:
         dist.all_reduce(tot_audio)
     value = float(tot_audio.item()) * args.steps / (max_ms / 1e3)
 
+    # Self-check after the timed region: 4 of this rank's timed embeddings (its longest
+    # and shortest clip and two drawn at random) against the reference's own kernels
+    # (oracle/_ref) on the dequantised q8_0 weights; the minimum cosine over ranks.
+    parity = bench_parity(m, host_pcm, offs, lens, d_out, rank, world, dev)
+
     # Config 4's scoring stage, reported beside the embed metric: this rank's
     # embeddings against a seeded registry of 100,000 unit-norm 256-d vectors, top-5
     # (vdb_identify, f32), timed with CUDA events on the same stream.
@@ -453,6 +492,7 @@ def run_b200(args) -> int:
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
         "rooflines_other": hbm_rooflines(stages, args.steps, lens, peaks),
         "identify": ident,
+        "parity": parity,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

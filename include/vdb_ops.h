@@ -264,7 +264,8 @@ int vdb_cmn_stem(const float* feats, const int* frames, int batch, int t_max, in
  *   - batch * n_mels must be <= 65536; larger calls fail with a clear error
  *     (use vdb_cmn_stem with caller-provided memory instead).
  *   - The first call on each device looks up the array's device address; make
- *     that first call before any stream capture.
+ *     that first call before any stream capture. A lookup that fails is not
+ *     remembered: the call returns an error and the next call tries again.
  *   - Every call uses the same array, and each call overwrites every entry it
  *     reads, so nothing carries over between calls. Calls whose kernels overlap
  *     on the GPU (concurrent streams, or threads sharing a device) race on the

@@ -101,6 +101,20 @@ int voicedetect_b200_embed_s16_batch(voicedetect_ctx* ctx, const int16_t* const*
                                      const int* n_samples, int n_clips, int sample_rate,
                                      float* out, int* out_dim);
 
+/* The audio front door of embed_path / verify_paths on its own (reference
+ * vd::load_audio_16k_mono, src/audio_io.cpp:25-38): decodes a WAV file (PCM u8 /
+ * s16 / s24 / s32, IEEE float 32 / 64, mono or multi-channel), averages the
+ * channels in f64 and linearly resamples to 16 kHz (src/audio_io.cpp:9-23).
+ * *out_pcm receives a malloc'd buffer of *out_n samples (free it with
+ * voicedetect_capi_free_vec); both are reset before work. Needs no context or GPU.
+ * Status 0 / nonzero; a failure's message is returned by
+ * voicedetect_b200_audio_error(). */
+int voicedetect_b200_load_audio_16k_mono(const char* wav_path, float** out_pcm, int* out_n);
+
+/* The message of this thread's last failed voicedetect_b200_load_audio_16k_mono
+ * ("" after a success). */
+const char* voicedetect_b200_audio_error(void);
+
 /* Bucketing policy: at most max_clips clips and max_frames padded FBank frames
  * per batched pass (defaults 512 and 262144). */
 int voicedetect_b200_set_bucketing(voicedetect_ctx* ctx, int max_clips, long long max_frames);

@@ -129,6 +129,12 @@ def ref_lib() -> C.CDLL:
         L.vdref_resnet34_new.argtypes = [C.POINTER(ResNetDesc)]
         L.vdref_resnet34_forward.restype = C.c_int
         L.vdref_resnet34_forward.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int, _f32p, _f32p]
+        L.vdref_resample_linear.restype = C.c_long
+        L.vdref_resample_linear.argtypes = [_f32p, C.c_long, C.c_int, C.c_int, _f32p, C.c_long]
+        L.vdref_load_audio_16k_mono.restype = C.c_long
+        L.vdref_load_audio_16k_mono.argtypes = [C.c_char_p, _f32p, C.c_long]
+        L.vdref_drwav_decode_f32.restype = C.c_long
+        L.vdref_drwav_decode_f32.argtypes = [C.c_char_p, _f32p, C.c_long, _i32p, _i32p]
         n = int(os.environ.get("VD_ORACLE_THREADS", "0")) or (os.cpu_count() or 1)
         L.vdref_set_threads(n)
         _lib_ref = L
@@ -409,6 +415,43 @@ def resample_linear(pcm: np.ndarray, in_sr: int, out_sr: int = 16000) -> np.ndar
     out = np.zeros(max(n_out, 0), np.float32)
     lib().vdo_resample_linear(_fp(pcm), len(pcm), in_sr, out_sr, _fp(out), len(out))
     return out
+
+
+def ref_resample_linear(pcm: np.ndarray, in_sr: int, out_sr: int = 16000) -> np.ndarray:
+    """The reference's own vd::resample_linear (src/audio_io.cpp:9-23), compiled."""
+    L = ref_lib()
+    pcm = np.ascontiguousarray(pcm, np.float32)
+    n_out = L.vdref_resample_linear(_fp(pcm), len(pcm), in_sr, out_sr, None, 0)
+    out = np.zeros(max(n_out, 0), np.float32)
+    L.vdref_resample_linear(_fp(pcm), len(pcm), in_sr, out_sr, _fp(out), len(out))
+    return out
+
+
+def ref_load_audio_16k_mono(path) -> np.ndarray:
+    """The reference's own vd::load_audio_16k_mono (src/audio_io.cpp:25-38): dr_wav
+    decode, f64 channel average, resample to 16 kHz."""
+    L = ref_lib()
+    p = str(path).encode()
+    n = L.vdref_load_audio_16k_mono(p, None, 0)
+    if n < 0:
+        raise RuntimeError(f"reference could not decode {path}")
+    out = np.zeros(n, np.float32)
+    L.vdref_load_audio_16k_mono(p, _fp(out), n)
+    return out
+
+
+def ref_drwav_decode(path) -> tuple[np.ndarray, int]:
+    """dr_wav's f32 decode (the reference's vendored third_party/dr_wav.h):
+    [frames, channels] float32 and the sample rate."""
+    L = ref_lib()
+    p = str(path).encode()
+    ch, sr = C.c_int(0), C.c_int(0)
+    frames = L.vdref_drwav_decode_f32(p, None, 0, C.byref(ch), C.byref(sr))
+    if frames < 0:
+        raise RuntimeError(f"dr_wav could not decode {path}")
+    out = np.zeros(frames * ch.value, np.float32)
+    L.vdref_drwav_decode_f32(p, _fp(out), len(out), C.byref(ch), C.byref(sr))
+    return out.reshape(frames, ch.value), sr.value
 
 
 def identify(q: np.ndarray, reg: np.ndarray, k: int = 5) -> tuple[np.ndarray, np.ndarray]:

@@ -23,6 +23,11 @@ the repository).
 * ref_campplus_tiny.npz -- the same for a small seeded CAM++ (vd_synth.tiny_campplus_model,
   every layer kind; one clip longer than one 100-frame context segment) from
   vd_synth.campplus_forward_torch.
+* fixtures_ref.npz -- the reference's real-audio fixtures (fixtures/*.wav, copied
+  from its tests/fixtures): per clip the reference's own decode + resample
+  (vd::load_audio_16k_mono, src/audio_io.cpp:25-38, compiled into oracle/_ref), the
+  reference's own post-CMN FBank of those samples (src/fbank.cpp compiled) and
+  torchaudio's Kaldi FBank of the same samples.
 
 Usage: python tests/golden/make_golden.py [name ...]   (default: every fixture)
 """
@@ -102,10 +107,23 @@ def make_campplus() -> None:
     np.savez_compressed(HERE / "ref_campplus_tiny.npz", **d)
 
 
+FIXTURES = ("clip_a", "clip_b_same", "clip_c_diff")
+
+
+def make_fixtures() -> None:
+    d = {}
+    for name in FIXTURES:
+        pcm = oracle.ref_load_audio_16k_mono(HERE / "fixtures" / f"{name}.wav")
+        d[f"{name}_pcm"] = pcm
+        d[f"{name}_ref_fbank"] = oracle.ref_fbank(pcm)
+        d[f"{name}_ta_fbank"] = fbank_torchaudio(pcm)
+    np.savez_compressed(HERE / "fixtures_ref.npz", **d)
+
+
 def main() -> None:
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:
-            {"ecapa": make_ecapa, "campplus": make_campplus}[name]()
+            {"ecapa": make_ecapa, "campplus": make_campplus, "fixtures": make_fixtures}[name]()
         print("wrote", sys.argv[1:])
         return
     clips = [vd_synth.make_clip(s, n) for s, n in ((11, 48000), (12, 16000 + 37), (13, 401))]
@@ -139,6 +157,7 @@ def main() -> None:
     np.savez_compressed(HERE / "ref_eres2net_tiny.npz", pcm=pcm, emb=emb, prenorm=pre)
     make_ecapa()
     make_campplus()
+    make_fixtures()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -78,3 +78,70 @@ def test_op_entry_points_reject_bad_arguments():
     assert L.vdb_identify(None, 1, None, 1, 1, 1, None, None, None) != 0
     assert L.vdb_grid_rows(2, 10, 8) == 2 * 12 * 10
     assert L.vdb_phase_rows(2, 10, 8) == 4 * 2 * 7 * 6
+
+
+def _tensor_table_dims(data: bytes):
+    """Byte offsets of every tensor's dimension fields in a GGUF v2/v3 file
+    (the tensor-info table that follows the metadata)."""
+    import struct
+    pos = 8
+    n_t, n_kv = struct.unpack_from("<QQ", data, pos)
+    pos += 16
+    sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+
+    def skip_str(p):
+        (n,) = struct.unpack_from("<Q", data, p)
+        return p + 8 + n
+
+    def skip_val(p, t):
+        if t == 8:
+            return skip_str(p)
+        if t == 9:
+            at, n = struct.unpack_from("<IQ", data, p)
+            p += 12
+            for _ in range(n):
+                p = skip_val(p, at)
+            return p
+        return p + sizes[t]
+
+    for _ in range(n_kv):
+        pos = skip_str(pos)
+        (t,) = struct.unpack_from("<I", data, pos)
+        pos = skip_val(pos + 4, t)
+    out = []
+    for _ in range(n_t):
+        pos = skip_str(pos)
+        (nd,) = struct.unpack_from("<I", data, pos)
+        pos += 4
+        out.append((nd, pos))
+        pos += 8 * nd + 4 + 8
+    return out
+
+
+def test_load_rejects_overflowing_tensor_dimensions(tmp_path, capfd):
+    """A tensor whose dimensions multiply past 2^64 (so the byte count would wrap to
+    a small value) is refused at load instead of passing the bounds check."""
+    import struct
+
+    import vd_synth
+    L = vd_b200.lib()
+    good = tmp_path / "m.gguf"
+    vd_synth.write_resnet_gguf(str(good), vd_synth.tiny_resnet_model(1, n_mels=16))
+    data = bytearray(good.read_bytes())
+    dims = _tensor_table_dims(bytes(data))
+    nd, pos = next((nd, p) for nd, p in dims if nd == 4)
+    ne = list(struct.unpack_from("<4Q", data, pos))
+    # 2^62 * 2^2 * ... : every product wraps modulo 2^64
+    cases = [[ne[0], 1 << 62, 4, 1 << 33], [ne[0], ne[1], 1 << 40, 1 << 40],
+             [1 << 63, 1, 1, 1]]
+    for k, bad_ne in enumerate(cases):
+        bad = bytearray(data)
+        struct.pack_into("<4Q", bad, pos, *bad_ne)
+        p = tmp_path / f"overflow{k}.gguf"
+        p.write_bytes(bytes(bad))
+        assert L.voicedetect_capi_load(str(p).encode()) is None
+        err = capfd.readouterr().err
+        if bad_ne[0] >= 1 << 63:  # negative as int64
+            assert "non-positive dimension" in err, err
+        else:
+            assert "larger than the file" in err, err

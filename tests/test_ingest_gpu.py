@@ -1,8 +1,10 @@
 """Device-side audio ingest (vdb_pcm_ingest, voicedetect_b200_embed_s16_batch): int16
 or f32 mono PCM at any rate converted / linearly resampled to f32 16 kHz on the GPU,
 replacing the reference's host path (drwav s16 -> f32, resample_linear,
-src/audio_io.cpp:9-23). Gates: bitwise equality with the oracle's restatement of
-resample_linear, and embeddings bitwise equal to the f32 16 kHz path they replace."""
+src/audio_io.cpp:9-23). Gates: bitwise equality with the reference's own compiled
+resample_linear (oracle/_ref; the oracle's restatement where that library is absent,
+itself pinned bitwise to it in tests/test_audio_cpu.py), and embeddings bitwise equal
+to the f32 16 kHz path they replace."""
 import numpy as np
 import pytest
 
@@ -22,7 +24,8 @@ def test_ingest_matches_oracle_resample(cuda_lib, rate, dtype):
     rng = np.random.default_rng(rate)
     clips16 = [vd_synth.make_clip(700 + i, n) if n >= 64 else
                rng.integers(-32768, 32768, n).astype(np.int16) for i, n in enumerate(lens)]
-    want = [oracle.resample_linear(vd_synth.clip_f32(c), rate, 16000) for c in clips16]
+    resample = oracle.ref_resample_linear if oracle.ref_available() else oracle.resample_linear
+    want = [resample(vd_synth.clip_f32(c), rate, 16000) for c in clips16]
     dev = torch.device("cuda")
     if dtype == "s16":
         ins = [torch.from_numpy(c.astype(np.int16)).to(dev) for c in clips16]

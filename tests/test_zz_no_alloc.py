@@ -5,8 +5,10 @@ cudaMalloc, or a host that owns every device allocation through its own pool).
 It keeps the per-clip CMN means in a fixed array inside the library instead of
 caller-provided working memory. Checked through the C ABI against the existing
 entry point, vdb_cmn_stem, on two calls in a row with different inputs (so a
-stale array would show), and for its size limit. The file name sorts last so
-that a run stopping at the first failure has already run every other test.
+stale array would show), directly against the CPU oracle's CMN + stem conv at
+rel-L2 <= 1e-3 (with and without CMN, 16 / 32 / 64 stem channels), and for its
+size limit. The file name sorts last so that a run stopping at the first failure
+has already run every other test.
 """
 import numpy as np
 import pytest
@@ -24,17 +26,17 @@ def _inputs(seed, B, t_max, frames, M=80, OC=32):
     return feats, fr, w, b
 
 
-def _run_both(vd, feats, fr, w, b, B, t_max, M=80, OC=32):
+def _run_both(vd, feats, fr, w, b, B, t_max, M=80, OC=32, cmn=1):
     import torch
     L = vd.lib()
     rows = L.vdb_grid_rows(B, t_max, M)
     y_ref = torch.full((rows, OC), 7.0, dtype=torch.float16, device="cuda")
     y_new = torch.full((rows, OC), -7.0, dtype=torch.float16, device="cuda")
     scratch = torch.empty(B, M, device="cuda")
-    rc = L.vdb_cmn_stem(feats.data_ptr(), fr.data_ptr(), B, t_max, M, 1, w.data_ptr(),
+    rc = L.vdb_cmn_stem(feats.data_ptr(), fr.data_ptr(), B, t_max, M, cmn, w.data_ptr(),
                         b.data_ptr(), OC, scratch.data_ptr(), y_ref.data_ptr(), None)
     assert rc == 0, vd.last_error()
-    rc = L.vdb_cmn_stem_noalloc(feats.data_ptr(), fr.data_ptr(), B, t_max, M, 1, w.data_ptr(),
+    rc = L.vdb_cmn_stem_noalloc(feats.data_ptr(), fr.data_ptr(), B, t_max, M, cmn, w.data_ptr(),
                                 b.data_ptr(), OC, y_new.data_ptr(), None)
     assert rc == 0, vd.last_error()
     torch.cuda.synchronize()
@@ -53,6 +55,33 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda_lib):
     y_ref, y_new = _run_both(cuda_lib, feats, fr, w, b, 5, 23)
     rel = float((y_new.float() - y_ref.float()).norm() / y_ref.float().norm())
     assert rel <= 1e-3 and torch.equal(y_new, y_ref)
+
+
+@pytest.mark.parametrize("oc,cmn", [(16, 1), (32, 0), (64, 1)])
+def test_noalloc_matches_oracle(cuda_lib, oc, cmn):
+    """Against the CPU oracle directly: per-clip CMN over each clip's valid frames
+    (src/fbank.cpp:194-201, skipped when cmn = 0), then the 3x3 stem conv + bias +
+    ReLU (src/encoder_resnet.cpp:116-117), rel-L2 <= 1e-3 per clip, zeros past each
+    clip's valid length."""
+    import oracle
+    B, t_max, M = 4, 29, 80
+    frames = [29, 11, 1, 20]
+    feats, fr, w, b = _inputs(10 + oc + cmn, B, t_max, frames, M, oc)
+    _, y_new = _run_both(cuda_lib, feats, fr, w, b, B, t_max, M, oc, cmn)
+    got = cuda_lib.from_grid(y_new, B, oc, M, t_max).cpu().numpy()
+    x_all = feats.cpu().numpy()
+    # [oc][9] taps kt*3 + kf (kt = time, kf = freq) -> torch layout (oc, 1, freq, time)
+    w4 = w.cpu().numpy().reshape(oc, 3, 3).transpose(0, 2, 1)[:, None].copy()
+    bias = b.cpu().numpy()
+    for i, T in enumerate(frames):
+        x = x_all[i, :T, :].T.copy()  # [80, T] feat-major
+        if cmn:
+            x -= (x.astype(np.float64).sum(1, keepdims=True) / T).astype(np.float32)
+        want = oracle.conv2d(x[None], w4, 1, bias, True)
+        have = got[i, :, :, :T]
+        rel = np.linalg.norm(have - want) / max(np.linalg.norm(want), 1e-12)
+        assert rel <= 1e-3, (i, rel)
+        assert np.all(got[i, :, :, T:] == 0)
 
 
 def test_noalloc_rejects_oversized_batch(cuda_lib):

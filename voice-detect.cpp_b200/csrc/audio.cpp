@@ -1,8 +1,10 @@
 // WAV decoding for embed_path / verify_paths: RIFF/WAVE with PCM u8 / s16 / s24 /
-// s32, IEEE float 32/64, and WAVE_FORMAT_EXTENSIBLE wrapping those. Samples are
-// converted to f32 with the usual full-scale divisors (s16 / 32768, s24 / 2^23,
-// s32 / 2^31, u8 as (x - 128) / 128), channels are averaged in f64 as the
-// reference does after decoding (src/audio_io.cpp:25-38).
+// s32, IEEE float 32/64, and WAVE_FORMAT_EXTENSIBLE wrapping those. Samples become
+// f32 exactly as the reference's decoder (its vendored dr_wav, third_party/dr_wav.h)
+// converts them: s16 * 2^-15 and s24 * 2^-23 (exact scalings), s32 / 2^31 in f64,
+// u8 as u * f32(2/255) - 1 in f32, f64 rounded to f32. Channels are then averaged
+// in f64 as the reference does after decoding (src/audio_io.cpp:25-38). Checked
+// bitwise against the compiled reference for every encoding (tests/test_audio_cpu.py).
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -74,7 +76,9 @@ bool read_wav_mono(const std::string& path, std::vector<float>& out, int& sample
             if (fmt == 1 && bits == 16) {
                 v = (float)(int16_t)rd16(s) / 32768.0f;
             } else if (fmt == 1 && bits == 8) {
-                v = ((float)s[0] - 128.0f) / 128.0f;
+                // 0..255 -> 0..2 -> -1..1, two f32 roundings (no fused multiply-add)
+                const float scaled = (float)s[0] * (2.0f / 255.0f);
+                v = scaled - 1.0f;
             } else if (fmt == 1 && bits == 24) {
                 const int32_t x = (int32_t)((uint32_t)s[0] << 8 | (uint32_t)s[1] << 16 |
                                             (uint32_t)s[2] << 24) >> 8;

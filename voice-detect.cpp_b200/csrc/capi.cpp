@@ -33,30 +33,47 @@ struct voicedetect_ctx {
 
 namespace {
 
-float* dup_vec(const std::vector<float>& v) {
-    if (v.empty()) return nullptr;
-    float* buf = static_cast<float*>(std::malloc(v.size() * sizeof(float)));
-    if (!buf) return nullptr;
-    std::memcpy(buf, v.data(), v.size() * sizeof(float));
-    return buf;
-}
+// Restores the calling thread's current CUDA device when it leaves scope, so a host
+// application that manages its own device sees it unchanged after any ABI call.
+class DeviceRestore {
+public:
+    DeviceRestore() { ok_ = cudaGetDevice(&dev_) == cudaSuccess; }
+    ~DeviceRestore() {
+        if (ok_) cudaSetDevice(dev_);
+    }
+    DeviceRestore(const DeviceRestore&) = delete;
+    DeviceRestore& operator=(const DeviceRestore&) = delete;
 
-int emit_embedding(voicedetect_ctx* ctx, const std::vector<float>& emb, float** out_vec,
+private:
+    int dev_ = 0;
+    bool ok_ = false;
+};
+
+// Hands an embedding to the caller under the ABI's ownership rule: the vector is a
+// fresh malloc'd block that voicedetect_capi_free_vec releases; nothing is written
+// to the out-parameters unless the whole call succeeds.
+int give_embedding(voicedetect_ctx* ctx, const std::vector<float>& emb, float** out_vec,
                    int* out_dim) {
-    float* buf = dup_vec(emb);
-    if (!buf) {
+    const size_t bytes = emb.size() * sizeof(float);
+    float* block = bytes ? static_cast<float*>(std::malloc(bytes)) : nullptr;
+    if (bytes && !block) {
         ctx->last_error = "out of memory";
         return 1;
     }
-    if (out_vec) *out_vec = buf;
-    else std::free(buf);
-    if (out_dim) *out_dim = (int)emb.size();
+    if (bytes) std::memcpy(block, emb.data(), bytes);
+    if (out_vec) {
+        *out_vec = block;
+    } else {
+        std::free(block);  // caller asked only for the dimension
+    }
+    if (out_dim) *out_dim = static_cast<int>(emb.size());
     ctx->last_error.clear();
     return 0;
 }
 
 // Embeds 16 kHz PCM through the engine; throws std::runtime_error on failure.
 std::vector<float> embed_16k(voicedetect_ctx* ctx, const std::vector<float>& pcm16k) {
+    DeviceRestore keep_device;  // the engine switches to its own device
     std::string err;
     const int D = ctx->engine->emb_dim();
     std::vector<float> out((size_t)D);
@@ -103,20 +120,30 @@ int embed_sharded(voicedetect_ctx* ctx, const std::vector<const void*>& ptrs,
     for (int g = 0; g < G; ++g) {
         if (shard[g].empty()) continue;
         th.emplace_back([&, g]() {
-            cudaSetDevice(eng[g]->device());
-            std::vector<const void*> p;
-            std::vector<int> c;
-            for (int i : shard[g]) {
-                p.push_back(ptrs[i]);
-                c.push_back(ns[i]);
+            // an exception escaping a std::thread would terminate the host process:
+            // every failure of a shard becomes its status and message instead
+            try {
+                if (cudaSetDevice(eng[g]->device()) != cudaSuccess)
+                    throw std::runtime_error("cudaSetDevice failed");
+                std::vector<const void*> p;
+                std::vector<int> c;
+                for (int i : shard[g]) {
+                    p.push_back(ptrs[i]);
+                    c.push_back(ns[i]);
+                }
+                res[g].resize((size_t)shard[g].size() * D);
+                rcs[g] = eng[g]->embed_host_raw(p.data(), type, c.data(), (int)p.size(),
+                                                sample_rate, res[g].data(), errs[g]);
+            } catch (const std::exception& e) {
+                errs[g] = e.what();
+                rcs[g] = 1;
+            } catch (...) {
+                errs[g] = "unknown error";
+                rcs[g] = 1;
             }
-            res[g].resize((size_t)shard[g].size() * D);
-            rcs[g] = eng[g]->embed_host_raw(p.data(), type, c.data(), (int)p.size(), sample_rate,
-                                            res[g].data(), errs[g]);
         });
     }
     for (auto& t : th) t.join();
-    cudaSetDevice(ctx->engine->device());
     for (int g = 0; g < G; ++g)
         if (rcs[g]) {
             err = "GPU " + std::to_string(eng[g]->device()) + ": " + errs[g];
@@ -176,7 +203,7 @@ extern "C" int voicedetect_capi_embed_path(voicedetect_ctx* ctx, const char* wav
     if (!ctx->engine) { ctx->last_error = "context has no loaded model"; return 1; }
     if (!wav_path) { ctx->last_error = "wav_path is NULL"; return 1; }
     try {
-        return emit_embedding(ctx, embed_path(ctx, wav_path), out_vec, out_dim);
+        return give_embedding(ctx, embed_path(ctx, wav_path), out_vec, out_dim);
     } catch (const std::exception& e) {
         ctx->last_error = e.what();
         return 1;
@@ -197,7 +224,7 @@ extern "C" int voicedetect_capi_embed_pcm(voicedetect_ctx* ctx, const float* pcm
     try {
         std::vector<float> samples(pcm, pcm + n_samples);
         if (sample_rate != 16000) samples = vdb::resample_linear(samples, sample_rate, 16000);
-        return emit_embedding(ctx, embed_16k(ctx, samples), out_vec, out_dim);
+        return give_embedding(ctx, embed_16k(ctx, samples), out_vec, out_dim);
     } catch (const std::exception& e) {
         ctx->last_error = e.what();
         return 1;
@@ -259,6 +286,7 @@ static int embed_raw_batch(voicedetect_ctx* ctx, const void* const* pcm, int typ
         ptrs[i] = pcm[i];
         ns[i] = n_samples[i];
     }
+    DeviceRestore keep_device;
     if (ctx->extra.empty())
         return ctx->engine->embed_host_raw(ptrs.data(), type, ns.data(), n_clips, sample_rate,
                                            out, err);
@@ -339,6 +367,7 @@ extern "C" int voicedetect_capi_identify(voicedetect_ctx* ctx, const float* quer
         ctx->last_error = "invalid identify arguments";
         return 1;
     }
+    DeviceRestore keep_device;
     cudaSetDevice(ctx->engine->device());
     cudaStream_t st = ctx->engine->stream();
     float *dq = nullptr, *dr = nullptr, *ds = nullptr;
@@ -385,6 +414,7 @@ extern "C" int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus) {
                           std::to_string(count) + ")";
         return 1;
     }
+    DeviceRestore keep_device;
     try {
         // Devices d0, d0 + 1, ... (mod count), d0 = the load device. Engines beyond
         // n_gpus are released; missing ones load the same GGUF on their device.
@@ -406,7 +436,6 @@ extern "C" int voicedetect_capi_set_devices(voicedetect_ctx* ctx, int n_gpus) {
             e->max_frames = ctx->engine->max_frames;
             ctx->extra.push_back(std::move(e));
         }
-        cudaSetDevice(d0);
         ctx->last_error.clear();
         return 0;
     } catch (const std::exception& ex) {
@@ -426,6 +455,7 @@ extern "C" int voicedetect_b200_embed_device(voicedetect_ctx* ctx, const float* 
         return 1;
     }
     try {
+        DeviceRestore keep_device;
         std::string err;
         if (ctx->engine->embed_device(d_pcm, offsets, n_samples, n_clips, d_out,
                                       static_cast<cudaStream_t>(stream), err)) {
@@ -482,6 +512,7 @@ extern "C" int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_
     double ms = 0, fl = 0;
     long long n = 0;
     std::string err;
+    DeviceRestore keep_device;
     cudaSetDevice(ctx->engine->device());
     if (ctx->engine->read_profile(ms, fl, n, err)) {
         ctx->last_error = err;
@@ -507,6 +538,7 @@ extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
     if (!ctx || !ctx->engine) return 1;
     std::lock_guard<std::mutex> lk(ctx->mu);
     std::string err;
+    DeviceRestore keep_device;
     if (cudaSetDevice(ctx->engine->device()) != cudaSuccess ||
         cudaStreamSynchronize(ctx->engine->stream()) != cudaSuccess) {
         ctx->last_error = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
@@ -518,3 +550,49 @@ extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
     }
     return 0;
 }
+
+namespace {
+thread_local std::string g_audio_error;
+}
+
+extern "C" int voicedetect_b200_load_audio_16k_mono(const char* wav_path, float** out_pcm,
+                                                    int* out_n) {
+    if (out_pcm) *out_pcm = nullptr;
+    if (out_n) *out_n = 0;
+    if (!wav_path || !out_pcm || !out_n) {
+        g_audio_error = "wav_path, out_pcm and out_n must not be NULL";
+        return 1;
+    }
+    try {
+        std::vector<float> mono;
+        int sr = 0;
+        std::string err;
+        if (!vdb::read_wav_mono(wav_path, mono, sr, err)) {
+            g_audio_error = err;
+            return 1;
+        }
+        const std::vector<float> pcm = vdb::resample_linear(mono, sr, 16000);
+        if (pcm.size() > (size_t)INT32_MAX) {
+            g_audio_error = "audio too long";
+            return 1;
+        }
+        float* block = static_cast<float*>(std::malloc(pcm.empty() ? 1 : pcm.size() * sizeof(float)));
+        if (!block) {
+            g_audio_error = "out of memory";
+            return 1;
+        }
+        if (!pcm.empty()) std::memcpy(block, pcm.data(), pcm.size() * sizeof(float));
+        *out_pcm = block;
+        *out_n = (int)pcm.size();
+        g_audio_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        g_audio_error = e.what();
+        return 1;
+    } catch (...) {
+        g_audio_error = "unknown error";
+        return 1;
+    }
+}
+
+extern "C" const char* voicedetect_b200_audio_error(void) { return g_audio_error.c_str(); }

@@ -220,14 +220,32 @@ bool Gguf::load(const std::string& path, std::string& err) {
                 err = "tensor '" + t.name + "' has a non-positive dimension";
                 return false;
             }
+        // A tensor must fit in the file, so no dimension, element count or byte count
+        // can exceed the file size: checking that before every multiply keeps a crafted
+        // header from wrapping the product to a small value that passes the bounds check.
+        const uint64_t limit = (uint64_t)size_;
+        uint64_t elems = 1;
+        for (int64_t v : t.ne) {
+            if ((uint64_t)v > limit || elems > limit / (uint64_t)v) {
+                err = "tensor '" + t.name + "' is larger than the file (corrupt dimensions)";
+                return false;
+            }
+            elems *= (uint64_t)v;
+        }
         if (!ggml_row_bytes(t.type, t.ne[0], row)) {
             err = "tensor '" + t.name + "' has unsupported type " + std::to_string(t.type);
             return false;
         }
-        size_t nb = row;
-        for (size_t d = 1; d < t.ne.size(); ++d) nb *= (size_t)t.ne[d];
-        t.nbytes = nb;
-        if (data0 + t.offset + nb > size_ || data0 + t.offset < data0) {
+        uint64_t nb = row;
+        for (size_t d = 1; d < t.ne.size(); ++d) {
+            if (nb > limit / (uint64_t)t.ne[d]) {
+                err = "tensor '" + t.name + "' is larger than the file (corrupt dimensions)";
+                return false;
+            }
+            nb *= (uint64_t)t.ne[d];
+        }
+        t.nbytes = (size_t)nb;
+        if (t.offset > limit || data0 > limit - t.offset || nb > limit - (data0 + t.offset)) {
             err = "tensor '" + t.name + "' extends past the end of the file (truncated GGUF?)";
             return false;
         }

@@ -521,9 +521,26 @@ namespace {
 constexpr int kNoAllocMaxMeans = 65536;  // batch * n_mels (256 KB of f32)
 static __device__ __align__(256) float g_cmn_means[kNoAllocMaxMeans];
 constexpr int kMaxDevices = 64;
-std::once_flag g_means_once[kMaxDevices];
+// Per device: the array's device address once a lookup has succeeded (null until
+// then), guarded by that device's mutex. Only a success is kept, so a lookup that
+// failed (made during a stream capture, or a transient error) is tried again on the
+// next call instead of leaving the entry point unusable on that device.
+std::mutex g_means_mu[kMaxDevices];
 float* g_means_addr[kMaxDevices] = {};
-cudaError_t g_means_status[kMaxDevices] = {};
+
+// The device address of g_cmn_means on device `dev` (current), or null with the
+// error in `status`.
+float* means_address(int dev, cudaError_t& status) {
+    std::lock_guard<std::mutex> lk(g_means_mu[dev]);
+    status = cudaSuccess;
+    if (!g_means_addr[dev]) {
+        void* addr = nullptr;
+        status = cudaGetSymbolAddress(&addr, g_cmn_means);
+        if (status == cudaSuccess && addr) g_means_addr[dev] = static_cast<float*>(addr);
+        else cudaGetLastError();  // do not leave the failure as the sticky last error
+    }
+    return g_means_addr[dev];
+}
 }  // namespace
 
 extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int batch, int t_max,
@@ -554,19 +571,16 @@ extern "C" int vdb_cmn_stem_noalloc(const float* feats, const int* frames, int b
         set_error("vdb_cmn_stem_noalloc: device ordinal out of range");
         return 1;
     }
-    // First call on this device (with it current): look up the array's device
-    // address. A host-side reference to g_cmn_means is not a device address.
-    std::call_once(g_means_once[dev], [dev] {
-        void* p = nullptr;
-        g_means_status[dev] = cudaGetSymbolAddress(&p, g_cmn_means);
-        g_means_addr[dev] = static_cast<float*>(p);
-    });
-    if (g_means_status[dev] != cudaSuccess || !g_means_addr[dev]) {
-        set_error(std::string("vdb_cmn_stem_noalloc: cudaGetSymbolAddress failed: ") +
-                  cudaGetErrorString(g_means_status[dev]));
+    // First successful call on this device (with it current) looks up the array's
+    // device address. A host-side reference to g_cmn_means is not a device address.
+    cudaError_t status = cudaSuccess;
+    float* means = means_address(dev, status);
+    if (!means) {
+        set_error(std::string("vdb_cmn_stem_noalloc: cudaGetSymbolAddress failed (retried on "
+                              "the next call): ") +
+                  cudaGetErrorString(status));
         return 1;
     }
-    float* means = g_means_addr[dev];
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // The mean kernel writes every entry the stem kernel reads, so the array's
     // previous contents never leak into a result.

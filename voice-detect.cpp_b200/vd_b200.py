@@ -140,6 +140,11 @@ def lib() -> C.CDLL:
                                                        C.POINTER(C.POINTER(C.c_int16)),
                                                        C.POINTER(C.c_int), C.c_int, C.c_int,
                                                        C.POINTER(C.c_float), C.POINTER(C.c_int)]
+        L.voicedetect_b200_load_audio_16k_mono.restype = C.c_int
+        L.voicedetect_b200_load_audio_16k_mono.argtypes = [C.c_char_p,
+                                                           C.POINTER(C.POINTER(C.c_float)),
+                                                           C.POINTER(C.c_int)]
+        L.voicedetect_b200_audio_error.restype = C.c_char_p
         L.vdb_resampled_length.restype = C.c_longlong
         L.vdb_resampled_length.argtypes = [C.c_longlong, C.c_int, C.c_int]
         L.vdb_pcm_ingest.restype = C.c_int
@@ -621,3 +626,20 @@ def add(a, b, y=None, stream=None):
     _check(lib().vdb_add(a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), y.data_ptr(), _ld(y),
                          rows, Cc, C.c_void_p(s)), "vdb_add")
     return y
+
+
+def load_audio_16k_mono(path: str):
+    """Decode a WAV file and resample it to 16 kHz mono through the library's audio
+    front door (voicedetect_b200_load_audio_16k_mono; host code, no GPU needed).
+    Returns a float32 numpy array."""
+    import numpy as np
+    L = lib()
+    buf = C.POINTER(C.c_float)()
+    n = C.c_int(0)
+    if L.voicedetect_b200_load_audio_16k_mono(str(path).encode(), C.byref(buf), C.byref(n)) != 0:
+        raise RuntimeError(L.voicedetect_b200_audio_error().decode())
+    try:
+        return np.ctypeslib.as_array(buf, shape=(n.value,)).copy() if n.value else \
+            np.zeros(0, np.float32)
+    finally:
+        L.voicedetect_capi_free_vec(buf)
