@@ -881,7 +881,7 @@ def run_sweep(args) -> int:
             vd.conv(x, w, b, tv, batch=B, t_out=To, f_out=Fo, oc=oc, k0=3,
                     stride0=1 if down else s, ic0=icc, relu=True, y=y,
                     tile_m=args.sweep_tile_m, halo=args.sweep_halo, ksplit=args.sweep_ksplit,
-                    tile_n=args.sweep_tile_n, **kw)
+                    tile_n=args.sweep_tile_n, pair=args.sweep_pair, **kw)
         try:
             run()  # validates the requested tiling for this shape
         except RuntimeError as e:
@@ -922,6 +922,8 @@ def main() -> int:
     ap.add_argument("--sweep-ksplit", type=int, default=0, help="0 auto, else 1..16")
     ap.add_argument("--sweep-tile-n", type=int, default=0,
                     help="0 auto, else output columns per tile (divides oc)")
+    ap.add_argument("--sweep-pair", type=int, default=0,
+                    help="0 auto, 1 CTA pairs (cta_group::2), -1 off")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)

@@ -117,6 +117,9 @@ typedef struct vdb_conv_args {
     int tile_n;             /* 0 auto (oc in <= 256-column tiles), else output columns per
                                tile: a multiple of 16 dividing oc (the HALO feeds need one
                                tile) */
+    int pair;               /* CTA pairs (tcgen05 cta_group::2: two SMs share one 256-row
+                               tile, each holding half of the weight columns): 0 auto,
+                               1 on (one-tap-per-stage feed only), -1 off */
 } vdb_conv_args;
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate).

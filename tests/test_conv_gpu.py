@@ -79,6 +79,8 @@ def valid_tilings(IC, OC, k, stride, two_segments=False):
         for tile_m in (384, 512, 1024):
             if tile_m // 128 * bn <= 512:
                 out.append((tile_m, 1, 1))
+    if bn % 32 == 0:
+        out.append((256, -1, 1, 1))  # CTA pair (cta_group::2), one tap per stage
     return out
 
 
@@ -147,11 +149,13 @@ def test_conv_vs_reference(cuda_lib, case):
     # shared-halo feed where the layer qualifies (3x3 stride 1 or 2, resident weights)
     configs = [(0, 0, 0)] + valid_tilings(IC, OC, k, stride, two_segments=fused_down)
     wp = vd.pack_conv_weight(w.to(dev))
-    for tile_m, halo, ksplit in configs:
+    for cfg in configs:
+        tile_m, halo, ksplit = cfg[:3]
+        pair = cfg[3] if len(cfg) > 3 else 0
         try:
             y = vd.conv(xin, wp, bias.float().to(dev), tv_dev, batch=B, t_out=To, f_out=Fo,
                         oc=OC, k0=k, stride0=stride, ic0=IC, relu=True, err=err, tile_m=tile_m,
-                        halo=halo, ksplit=ksplit, **kw)
+                        halo=halo, ksplit=ksplit, pair=pair, **kw)
         except RuntimeError as e:
             if tile_m > 256 and "does not fit" in str(e):
                 continue
@@ -160,7 +164,8 @@ def test_conv_vs_reference(cuda_lib, case):
         assert int(err.item()) == 0, f"kernel error word {err.item():#x}"
         got = vd.from_grid(y, B, OC, Fo, To).cpu()
         rel = float((got - ref).norm() / max(ref.norm(), 1e-12))
-        assert rel <= REL_L2_TOL, f"{name} tile_m={tile_m} halo={halo} ksplit={ksplit}: rel-L2 {rel:.3e}"
+        assert rel <= REL_L2_TOL, \
+            f"{name} tile_m={tile_m} halo={halo} ksplit={ksplit} pair={pair}: rel-L2 {rel:.3e}"
         # borders and masked rows are exactly zero
         gfull = y.reshape(B, To + 2, Fo + 2, OC).float().cpu()
         assert torch.all(gfull[:, 0] == 0) and torch.all(gfull[:, :, 0] == 0)

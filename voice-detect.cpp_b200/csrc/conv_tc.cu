@@ -1536,10 +1536,20 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // 512 x 398 frames) it only pays off for the 80-channel k=5 stem (16-channel K
     // blocks: 528 -> 444 us); the 1024/1536-channel 1x1 convs run at the same speed
     // and the 128-channel ones slower, so it is opt-in. sq->pair: 1 on, 0 / -1 off.
-    const bool pair = seq && sq->pair == 1 && !halo && !two_ring && J == 1 && BN % 32 == 0 &&
-                      (a->tile_m == 0 || a->tile_m == 256) && num_sms() >= 2;
-    if (seq && sq->pair == 1 && !pair) {
-        set_error("vdb_conv1d: a CTA pair needs oc tiles that are multiples of 32 and tile_m 0 or 256");
+    // 2-D convs with 256-column tiles take pairs automatically: a 256-row, 256-column
+    // tile then needs 256 TMEM columns per CTA instead of 512, so the accumulator is
+    // double-buffered (the epilogue overlaps the next tile's MMAs), and each SM
+    // fetches half the weight operand per MMA (256 -> 256 convs 999 -> 1127 TFLOP/s,
+    // 128 -> 256 stride 2 745 -> 881 at batch 512 x 300 frames). With 128 columns it
+    // measured slower (916 -> 727 TFLOP/s on 128 -> 128).
+    const int want_pair = seq ? sq->pair : a->pair;
+    const bool auto_pair = want_pair == 0 && !seq && BN == 256 && a->tile_m == 0 &&
+                           a->ksplit <= 1;
+    const bool pair = (want_pair == 1 || auto_pair) && !halo && !two_ring && J == 1 &&
+                      BN % 32 == 0 && (a->tile_m == 0 || a->tile_m == 256) && num_sms() >= 2;
+    if (want_pair == 1 && !pair) {
+        set_error("vdb_conv: a CTA pair needs the one-tap-per-stage feed, oc tiles that are "
+                  "multiples of 32 and tile_m 0 or 256");
         return 1;
     }
     if (pair) BM = 2 * kMB;
@@ -1768,7 +1778,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         return 0;
     };
     if (pair) {
-        auto kern = conv_tc_kernel<1, 1, true, true>;
+        auto kern = seq ? conv_tc_kernel<1, 1, true, true> : conv_tc_kernel<1, 1, true, false>;
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
         if (cs == cudaStreamCaptureStatusNone)

@@ -45,7 +45,7 @@ class ConvArgs(C.Structure):
         ("ksplit", C.c_int), ("ldx0", C.c_int), ("ldx1", C.c_int), ("ldy", C.c_int),
         ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
         ("act", C.c_int), ("ysum", C.c_void_p), ("ldsum", C.c_int), ("addend", C.c_void_p),
-        ("ldaddend", C.c_int), ("y_pad", C.c_int), ("tile_n", C.c_int),
+        ("ldaddend", C.c_int), ("y_pad", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int),
     ]
 
 
@@ -485,7 +485,7 @@ def _ptr(t):
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
          y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
-         y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0, tile_n=0):
+         y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0, tile_n=0, pair=0):
     """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
     tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
     the row pitch is taken from the view's stride); y2 is an extra PHASE output,
@@ -520,7 +520,7 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
                  ldr2=_ld(residual2), act=int(act), ysum=_ptr(ysum), ldsum=_ld(ysum),
                  addend=_ptr(addend), ldaddend=_ld(addend), y_pad=int(y_pad),
-                 tile_n=int(tile_n))
+                 tile_n=int(tile_n), pair=int(pair))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
