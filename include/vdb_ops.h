@@ -298,7 +298,13 @@ int vdb_add(const void* a, int lda, const void* b, int ldb, void* y, int ldy, lo
 /* Top-k cosine search (no reference counterpart exists; the additive C ABI
  * voicedetect_capi_identify calls it). q: device f32 [n_q][dim]; reg: device f32
  * [n_reg][dim]; out_idx / out_score: device [n_q][k], descending score, equal
- * scores ordered by the lower registry index; 0 < k <= 64, dim <= 1024. */
+ * scores ordered by the lower registry index, -1 / -inf past n_reg; 0 < k <= 64,
+ * dim <= 1024. For dim <= 512 the candidates come from a tcgen05 f16 GEMM of the
+ * unit-normalised rows with the top-(k + 8) kept per query in its epilogue; those
+ * are rescored exactly (f64 dot over f64 norms) and the returned scores are exact
+ * cosines. A row of the exact top k can be missed only if more than k + 8 rows
+ * score within the f16 rounding of unit vectors (|error| <= 2^-10 per score,
+ * about 2e-3 between two scores) of it. Allocates stream-ordered workspace. */
 int vdb_identify(const float* q, int n_q, const float* reg, int n_reg, int dim, int k,
                  int* out_idx, float* out_score, void* stream);
 
