@@ -2,6 +2,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <mutex>
 #include <string>
 
@@ -41,6 +42,27 @@ EncodeTiledFn encode_tiled_fn() {
         return missing;
     }
     return fn;
+}
+
+void keep_async_pool() {
+    // Stream-ordered workspace (cudaMallocAsync) comes from the device's default
+    // memory pool, which by default returns freed memory to the driver at every
+    // synchronisation, so the next call pays a full allocation (about a millisecond
+    // for the 100 MB an identify call uses). Keep it cached instead: once per device,
+    // the pool's release threshold is raised to "never". It only affects this
+    // process's pool and ends with it.
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done[dev]) return;
+    cudaMemPool_t pool = nullptr;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess && pool) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    done[dev] = true;
 }
 
 int num_sms() {

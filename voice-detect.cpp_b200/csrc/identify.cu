@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <climits>
+#include <mutex>
 
 #include "sm100_ptx.cuh"
 #include "vdb_internal.h"
@@ -44,6 +45,16 @@ __device__ __forceinline__ bool better(float s, int i, float t, int j) {
     return s > t || (s == t && i < j);
 }
 
+// Order-preserving map of a float to an int (a < b  <=>  key(a) < key(b)), for
+// atomicMax on scores of either sign.
+__device__ __forceinline__ int score_key(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float key_score(int k) {
+    return __int_as_float(k >= 0 ? k : k ^ 0x7FFFFFFF);
+}
+
 // ---------------------------------------------------------------------------
 // 1. unit-norm f16 rows
 // ---------------------------------------------------------------------------
@@ -52,10 +63,11 @@ __device__ __forceinline__ bool better(float s, int i, float t, int j) {
 // |x| into nrm. Rows past n (up to the padded count) are written as zeros.
 __global__ void __launch_bounds__(256)
 normalize_rows_kernel(const float* __restrict__ x, int n, int n_pad, int dim, int dim_pad,
-                      __half* __restrict__ xh, double* __restrict__ nrm) {
+                      __half* __restrict__ xh, double* __restrict__ nrm, int* __restrict__ thr) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= n_pad) return;
+    if (thr && lane == 0) thr[row] = score_key(-INFINITY);
     __half* out = xh + (long long)row * dim_pad;
     if (row >= n) {
         for (int d = lane; d < dim_pad; d += 32) out[d] = __float2half_rn(0.0f);
@@ -81,19 +93,73 @@ constexpr int kRows = 128;           // registry rows per tile (MMA N) and queri
 constexpr int kKc = 64;              // dims per K chunk (128-byte swizzled rows)
 constexpr uint32_t kChunkBytes = kRows * kKc * 2;  // one 128 x 64 f16 box: 16 KB
 constexpr int kStages = 5;
+constexpr uint32_t kStageBytes = 8 * 32 * 17 * 4;  // 16 scores per epilogue thread, padded
 
 struct IdDev {
     int n_q, n_reg, n_rt;     // queries, registry rows, registry tiles of 128
     int n_kc;                 // K chunks of 64 dims
     int nrb;                  // query row blocks per item (2: 256 queries, 1: 128)
     int n_qb, n_sl;           // query blocks, registry slices
-    int L;                    // list length per query
+    int L;                    // candidates kept per query and item (the reservoir size)
     float* part_s;            // [n_sl][n_q_pad][L] f16-scored candidates
     int* part_i;
     int n_q_pad;
+    int* thr;                 // [n_q_pad] per-query lower bound on its L-th best f16
+                              // score, as an order-preserving int (atomicMax)
+    int seed;                 // 1: only raise thr (no candidate lists written)
     int* err;
 };
 
+
+// Candidate reservoir of one query: the LR best (score desc, index asc) of the values
+// admitted so far, unsorted, in registers; `mn` / `mi` / `mpos` are its worst entry
+// (lowest score, highest index among equal scores) once it is full.
+template <int LR>
+struct Reservoir {
+    float s[LR];
+    int i[LR];
+    int n;
+    float mn;
+    int mi, mpos;
+
+    __device__ __forceinline__ void reset() {
+        n = 0;
+        mn = -INFINITY;
+        mi = INT_MAX;
+        mpos = 0;
+#pragma unroll
+        for (int j = 0; j < LR; ++j) {
+            s[j] = -INFINITY;
+            i[j] = -1;
+        }
+    }
+    __device__ __forceinline__ void find_worst() {
+        mn = s[0];
+        mi = i[0];
+        mpos = 0;
+#pragma unroll
+        for (int j = 1; j < LR; ++j) {
+            const bool w = s[j] < mn || (s[j] == mn && i[j] > mi);
+            mn = w ? s[j] : mn;
+            mi = w ? i[j] : mi;
+            mpos = w ? j : mpos;
+        }
+    }
+    // Called only for v above the admission threshold: appends, or replaces the worst.
+    __device__ __forceinline__ void add(float v, int idx) {
+        const int slot = n < LR ? n : mpos;
+#pragma unroll
+        for (int j = 0; j < LR; ++j) {
+            const bool here = j == slot;
+            s[j] = here ? v : s[j];
+            i[j] = here ? idx : i[j];
+        }
+        if (n < LR) ++n;
+        if (n == LR) find_worst();
+    }
+};
+
+template <int LR>
 __global__ void __launch_bounds__(kThreads, 1)
 identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmR,
                    const __grid_constant__ IdDev p) {
@@ -103,7 +169,8 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint8_t* smem = smem_raw + (base - raw_u32);
     const uint32_t q_bytes = (uint32_t)p.nrb * p.n_kc * kChunkBytes;
     const uint32_t stage0 = q_bytes;
-    const uint32_t bar0 = stage0 + kStages * kChunkBytes;
+    const uint32_t stage_off = stage0 + kStages * kChunkBytes;  // epilogue value staging
+    const uint32_t bar0 = stage_off + kStageBytes;
     const uint32_t bar_full = base + bar0;
     const uint32_t bar_empty = bar_full + 8 * kStages;
     const uint32_t bar_tfull = bar_empty + 8 * kStages;
@@ -249,22 +316,33 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
         }
     } else if (warp >= 4) {
-        // ---------------- epilogue: running top-L per query ----------------
+        // ---------------- epilogue: the best LR candidates per query ----------------
+        // Thread = one query (TMEM lane). A value enters the reservoir when it beats
+        // the admission threshold: while the reservoir fills, the query's published
+        // lower bound (p.thr, raised by earlier items: any item's LR-th best is at most
+        // the query's overall L-th best), afterwards the reservoir's worst entry. A
+        // 32-value chunk in which no lane of the warp beats its threshold costs one max
+        // and one vote.
         const int ew = warp - 4;
         const int quad = warp & 3;       // TMEM lane quadrant this warp may read
         const int rb = ew >> 2;          // query row block
-        const int L = p.L;
-        float ls[kMaxL];
-        int li[kMaxL];
+        const bool active = rb < p.nrb;
+        float* my_stage = reinterpret_cast<float*>(smem + stage_off) + (ew * 32 + lane) * 17;
+        Reservoir<LR> res;
         uint32_t acc = 0, acc_phase = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             const int qb = item / p.n_sl, sl = item - qb * p.n_sl;
             const int t0 = (int)((long long)sl * p.n_rt / p.n_sl);
             const int t1 = (int)((long long)(sl + 1) * p.n_rt / p.n_sl);
-            const bool active = rb < p.nrb;
-            int n = 0;            // entries held (the list is sorted: best first)
-            float thr = -INFINITY;  // entry L-1's score once the list is full
+            const int q = (qb * p.nrb + rb) * kRows + quad * 32 + lane;
+            res.reset();
+            // the largest float below the bound: values equal to the bound still enter
+            float floor_s = -INFINITY;
+            if (active && q < p.n_q_pad) {
+                const float b = key_score(((volatile int*)p.thr)[q]);
+                floor_s = b > -INFINITY ? nextafterf(b, -INFINITY) : -INFINITY;
+            }
             for (int t = t0; t < t1; ++t) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag)) {
@@ -278,26 +356,39 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     const int r0 = t * kRows;
                     const int valid = min(kRows, p.n_reg - r0);
 #pragma unroll 1
-                    for (int cb = 0; cb < kRows; cb += 32) {
-                        uint32_t v[32];
+                    for (int cb = 0; cb < kRows; cb += 64) {
+                        // two 32-column loads in flight, one wait
+                        uint32_t v[2][32];
                         __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
-                        tmem_ld_32x32b_x32(taddr + (uint32_t)cb, v);
+                        tmem_ld_32x32b_x32_nowait(taddr + (uint32_t)cb, v[0]);
+                        tmem_ld_32x32b_x32_nowait(taddr + (uint32_t)cb + 32u, v[1]);
+                        tmem_wait_ld();
+                        float thr = res.n < LR ? floor_s : fmaxf(floor_s, res.mn);
+                        // strictly above: a later row with an equal score has a higher
+                        // index, so it never displaces an earlier one
+                        uint32_t mask[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const float s = __uint_as_float(v[i]);
-                            // strictly better than the current L-th: later rows with an
-                            // equal score have a higher index, so they never displace it
-                            if (s > thr && cb + i < valid) {
-                                int pos = n < L ? n : L - 1;
-                                while (pos > 0 && s > ls[pos - 1]) {
-                                    ls[pos] = ls[pos - 1];
-                                    li[pos] = li[pos - 1];
-                                    --pos;
+                        for (int i = 0; i < 64; ++i)
+                            mask[i >> 4] |= (__uint_as_float(v[i >> 5][i & 31]) > thr &&
+                                             cb + i < valid) ? (1u << (i & 15)) : 0u;
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            uint32_t m = mask[h];
+                            if (m == 0) continue;
+                            // the rare lanes with candidates walk them in a rolled loop (one
+                            // inlined insertion: an unrolled one per value made the
+                            // epilogue's hot code too large for the instruction cache)
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                my_stage[i] = __uint_as_float(v[h >> 1][(h & 1) * 16 + i]);
+#pragma unroll 1
+                            for (; m; m &= m - 1) {
+                                const int i = __ffs(m) - 1;
+                                const float sv = my_stage[i];
+                                if (sv > thr) {
+                                    res.add(sv, r0 + cb + h * 16 + i);
+                                    thr = res.n < LR ? floor_s : fmaxf(floor_s, res.mn);
                                 }
-                                ls[pos] = s;
-                                li[pos] = r0 + cb + i;
-                                if (n < L) ++n;
-                                if (n == L) thr = ls[L - 1];
                             }
                         }
                     }
@@ -308,15 +399,23 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     acc = 0;
                     acc_phase ^= 1;
                 }
-            }
-            if (!ok || !active) continue;
-            const int q = (qb * p.nrb + rb) * kRows + quad * 32 + lane;
-            if (q < p.n_q) {
-                const long long o = ((long long)sl * p.n_q_pad + q) * L;
-                for (int j = 0; j < L; ++j) {
-                    p.part_s[o + j] = j < n ? ls[j] : -INFINITY;
-                    p.part_i[o + j] = j < n ? li[j] : -1;
+                // every 4 tiles: share this item's LR-th best with the query's other
+                // items (running concurrently on other SMs) and take the best bound so far
+                if (active && q < p.n_q && ((t - t0) & 3) == 3) {
+                    if (res.n == LR) atomicMax(p.thr + q, score_key(res.mn));
+                    const float b = key_score(((volatile int*)p.thr)[q]);
+                    if (b > -INFINITY) floor_s = fmaxf(floor_s, nextafterf(b, -INFINITY));
                 }
+            }
+            if (!ok || !active || q >= p.n_q) continue;
+            // this item's LR-th best bounds the query's overall L-th best from below
+            if (res.n == LR) atomicMax(p.thr + q, score_key(res.mn));
+            if (p.seed) continue;
+            const long long o = ((long long)sl * p.n_q_pad + q) * LR;
+#pragma unroll
+            for (int j = 0; j < LR; ++j) {
+                p.part_s[o + j] = res.s[j];
+                p.part_i[o + j] = res.i[j];
             }
         }
     }
@@ -333,12 +432,12 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 // ---------------------------------------------------------------------------
 // 3. merge the slices' candidates, rescore exactly, emit the top k
 // ---------------------------------------------------------------------------
-// Warp per query. Candidates are ranked by (f16 score desc, index asc); the best L
-// are rescored as dot(q, r) / (|q| |r|) in f64 from the f32 inputs, and the top k
+// Warp per query over LS candidates per slice. Candidates are ranked by (f16 score
+// desc, index asc); the best L are rescored as dot(q, r) / (|q| |r|) in f64 from the f32 inputs, and the top k
 // of those by (exact score desc, index asc) are written (-1 / -inf past n_reg).
 __global__ void __launch_bounds__(256)
 merge_rescore_kernel(const float* __restrict__ part_s, const int* __restrict__ part_i, int n_sl,
-                     int n_q_pad, int L, const float* __restrict__ q,
+                     int n_q_pad, int LS, int L, const float* __restrict__ q,
                      const float* __restrict__ reg, int n_q, int dim,
                      const double* __restrict__ qn, const double* __restrict__ rn, int k,
                      int* __restrict__ out_idx, float* __restrict__ out_score) {
@@ -349,9 +448,9 @@ merge_rescore_kernel(const float* __restrict__ part_s, const int* __restrict__ p
     float ls[kMaxL];
     int li[kMaxL];
     int n = 0;
-    for (int e = lane; e < n_sl * L; e += 32) {
-        const int sl = e / L, j = e - sl * L;
-        const long long o = ((long long)sl * n_q_pad + qq) * L + j;
+    for (int e = lane; e < n_sl * LS; e += 32) {
+        const int sl = e / LS, j = e - sl * LS;
+        const long long o = ((long long)sl * n_q_pad + qq) * LS + j;
         const int i = part_i[o];
         if (i < 0) continue;
         const float s = part_s[o];
@@ -547,6 +646,7 @@ int identify_cuda_cores(const float* q, int n_q, const float* reg, int n_reg, in
     chunk = std::min<long long>(chunk, n_reg);
     float* work = nullptr;
     const size_t bytes = sizeof(float) * ((size_t)n_q + n_reg + (size_t)qc * chunk);
+    keep_async_pool();
     VDB_CHECK_CUDA(cudaMallocAsync(&work, bytes, st));
     float* qn = work;
     float* rn = qn + n_q;
@@ -611,7 +711,10 @@ extern "C" int vdb_identify(const float* q, int n_q, const float* reg, int n_reg
     p.n_rt = (n_reg + kRows - 1) / kRows;
     p.n_qb = (n_q + p.nrb * kRows - 1) / (p.nrb * kRows);
     p.n_q_pad = p.n_qb * p.nrb * kRows;
-    p.L = std::min(k + kExtra, kMaxL);
+    // reservoir per query and item: 16 entries for k <= 8 (registers), else 72
+    const int LR = k + kExtra <= 16 ? 16 : kMaxL;
+    const int L_pool = std::min(k + kExtra, LR);
+    p.L = LR;
     // Registry slices per query block: enough work items for every SM, choosing the
     // count whose last wave is fullest (an item = one query block x one slice).
     const int G = num_sms();
@@ -636,8 +739,10 @@ extern "C" int vdb_identify(const float* q, int n_q, const float* reg, int n_reg
     const size_t nrm_b = sizeof(double) * ((size_t)n_q + (size_t)n_reg);
     const size_t part_n = (size_t)p.n_sl * p.n_q_pad * p.L;
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
-    const size_t bytes = up(qh_b) + up(rh_b) + up(nrm_b) + up(part_n * 4) * 2;
+    const size_t thr_b = sizeof(int) * (size_t)p.n_q_pad;
+    const size_t bytes = up(qh_b) + up(rh_b) + up(nrm_b) + up(part_n * 4) * 2 + up(thr_b);
     uint8_t* work = nullptr;
+    keep_async_pool();
     VDB_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&work), bytes, st));
     __half* qh = reinterpret_cast<__half*>(work);
     __half* rh = reinterpret_cast<__half*>(work + up(qh_b));
@@ -645,13 +750,14 @@ extern "C" int vdb_identify(const float* q, int n_q, const float* reg, int n_reg
     double* rn = qn + n_q;
     p.part_s = reinterpret_cast<float*>(work + up(qh_b) + up(rh_b) + up(nrm_b));
     p.part_i = reinterpret_cast<int*>(work + up(qh_b) + up(rh_b) + up(nrm_b) + up(part_n * 4));
+    p.thr = reinterpret_cast<int*>(work + up(qh_b) + up(rh_b) + up(nrm_b) + 2 * up(part_n * 4));
     p.err = nullptr;
 
     int rc = 0;
     normalize_rows_kernel<<<(p.n_q_pad + 7) / 8, 256, 0, st>>>(q, n_q, p.n_q_pad, dim, dim_pad, qh,
-                                                                qn);
+                                                                qn, p.thr);
     normalize_rows_kernel<<<(int)((n_reg_pad + 7) / 8), 256, 0, st>>>(reg, n_reg, (int)n_reg_pad,
-                                                                      dim, dim_pad, rh, rn);
+                                                                      dim, dim_pad, rh, rn, nullptr);
     CUtensorMap tq, tr;
     if (!make_map_rows(&tq, qh, dim_pad, p.n_q_pad) || !make_map_rows(&tr, rh, dim_pad, n_reg_pad)) {
         set_error("vdb_identify: cuTensorMapEncodeTiled failed");
@@ -659,19 +765,48 @@ extern "C" int vdb_identify(const float* q, int n_q, const float* reg, int n_reg
     }
     if (!rc) {
         const uint32_t q_bytes = (uint32_t)p.nrb * p.n_kc * kChunkBytes;
-        const size_t smem = 1024 + q_bytes + kStages * kChunkBytes + 8 * (2 * kStages + 6) + 16;
-        cudaError_t e = cudaFuncSetAttribute(identify_tc_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        const size_t smem =
+            1024 + q_bytes + kStages * kChunkBytes + kStageBytes + 8 * (2 * kStages + 6) + 16;
+        auto kern = LR == 16 ? identify_tc_kernel<16> : identify_tc_kernel<kMaxL>;
+        cudaError_t e = cudaSuccess;
+        {
+            // the shared-memory opt-in, once per device and kernel (the size is fixed)
+            static std::mutex mu;
+            static bool set[64][2] = {};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            std::lock_guard<std::mutex> lk(mu);
+            const int kv = LR == 16 ? 0 : 1;
+            if (dev < 0 || dev >= 64 || !set[dev][kv]) {
+                e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(1024 + 2 * 4 * kChunkBytes + kStages * kChunkBytes +
+                                               kStageBytes + 8 * (2 * kStages + 6) + 16));
+                if (e == cudaSuccess && dev >= 0 && dev < 64) set[dev][kv] = true;
+            }
+        }
+        // Seed pass over the first 32 registry tiles (4096 rows, 8 slices of 4): raises
+        // every query's admission bound before the full pass, so the full pass's items
+        // start warm instead of admitting most values of their first tiles.
+        if (e == cudaSuccess && p.n_rt >= 64) {
+            IdDev ps = p;
+            ps.seed = 1;
+            ps.n_rt = 32;
+            ps.n_sl = 8;
+            // same reservoir size as the full pass: the bound must be an LR-th best
+            kern<<<std::min(ps.n_qb * ps.n_sl, G), kThreads, smem, st>>>(tq, tr, ps);
+            e = cudaGetLastError();
+        }
         const int items = p.n_qb * p.n_sl;
         const int grid = std::min(items, G);
         if (e == cudaSuccess) {
-            identify_tc_kernel<<<grid, kThreads, smem, st>>>(tq, tr, p);
+            kern<<<grid, kThreads, smem, st>>>(tq, tr, p);
             e = cudaGetLastError();
         }
         if (e == cudaSuccess) {
             merge_rescore_kernel<<<(n_q + 7) / 8, 256, 0, st>>>(p.part_s, p.part_i, p.n_sl,
-                                                                p.n_q_pad, p.L, q, reg, n_q, dim,
-                                                                qn, rn, k, out_idx, out_score);
+                                                                p.n_q_pad, p.L, L_pool, q, reg,
+                                                                n_q, dim, qn, rn, k, out_idx,
+                                                                out_score);
             e = cudaGetLastError();
         }
         if (e != cudaSuccess) {

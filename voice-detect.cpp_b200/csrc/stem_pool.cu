@@ -619,6 +619,7 @@ extern "C" int vdb_pool_embed(const void* x, const int* tvalid, int batch, int t
     // stream-ordered working memory for the pooled vectors and the FC partials
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* scratch = nullptr;
+    keep_async_pool();
     VDB_CHECK_CUDA(cudaMallocAsync(&scratch,
                                    sizeof(float) * pool_embed_scratch_floats(batch, f, c, emb_dim),
                                    st));

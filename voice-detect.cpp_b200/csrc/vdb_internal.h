@@ -23,6 +23,11 @@ EncodeTiledFn encode_tiled_fn();
 
 int num_sms();
 
+// Keeps memory freed by cudaFreeAsync cached in the current device's default pool
+// (once per device), so repeated calls with stream-ordered workspace do not pay a
+// fresh allocation each time.
+void keep_async_pool();
+
 // Pooling + FC + L2 launcher with an optional output-row map (row b of the batch
 // is written to out_rows[b]); vdb_pool_embed is the public wrapper. `scratch`
 // holds pool_embed_scratch_floats(...) floats of device working memory (the
