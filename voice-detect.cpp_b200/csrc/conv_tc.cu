@@ -252,7 +252,7 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
 // `res` holds this chunk's residual when has_res, else its addend when add_in_res
 // (both prefetched one chunk ahead by epi_rows); sss is the shared-memory copy of
 // bn_scale (sss[0, oc)) and bn_shift (sss[oc, 2*oc)) for act 3/4.
-template <int NC, int J, bool SEQ>
+template <int NC, int J, bool SEQ, bool PLAIN>
 __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const RowInfo& ri, int col,
                                           uint32_t taddr, const float* sbias, const float* sss,
                                           bool has_res, const uint4 (&res)[NC / 8],
@@ -289,6 +289,28 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         }
     }
     if (!ri.in_range) return;
+    if constexpr (PLAIN) {
+        // (acc + bias) -> ReLU -> valid-pixel mask -> f16: the ResNet BasicBlock convs
+        // (every other epilogue mode compiled out, so the hot code stays small)
+        const uint32_t keep = ri.valid ? 0xFFFFFFFFu : 0u;
+        const __half2 zero2 = __float2half2_rn(0.0f);
+        uint4* yp = reinterpret_cast<uint4*>(yrow);
+#pragma unroll
+        for (int j = 0; j < NC / 8; ++j) {
+            __half2 h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                h[q] = __floats2half2_rn(f[j * 8 + 2 * q] + sbias[j * 8 + 2 * q],
+                                         f[j * 8 + 2 * q + 1] + sbias[j * 8 + 2 * q + 1]);
+                if (p.relu) h[q] = __hmax2(h[q], zero2);
+            }
+            yp[j] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
+                               *reinterpret_cast<uint32_t*>(&h[1]) & keep,
+                               *reinterpret_cast<uint32_t*>(&h[2]) & keep,
+                               *reinterpret_cast<uint32_t*>(&h[3]) & keep);
+        }
+        return;
+    }
     if constexpr (SEQ) {
         // 1-D: padding rows hold reflections (or nothing used), unless the tensor is
         // zero-padded (reflect 2): then every row of the slots is stored, 0 outside
@@ -457,10 +479,19 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 // Epilogue of one (tile, row block) for this thread: columns [c_lo, c_hi) of the
 // tile in chunks of NC, with the residual of the next chunk loaded before the
 // current one is finished.
-template <int NC, int J, bool SEQ>
+template <int NC, int J, bool SEQ, bool PLAIN>
 __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowInfo& ri, int m,
                                          int n0, int c_lo, int c_hi, uint32_t tbase,
                                          const float* sbias, const float* sss) {
+    if constexpr (PLAIN) {
+        __half* yrow = p.y + ri.dst * p.ldy + n0;
+        const uint4 none[NC / 8] = {};
+        for (int c = c_lo; c < c_hi; c += NC)
+            epi_chunk<NC, J, SEQ, true>(p, live, ri, n0 + c, tbase + (uint32_t)c,
+                                        sbias + n0 + c, sss, false, none, nullptr, yrow + c,
+                                        nullptr, nullptr, nullptr, false);
+        return;
+    }
     const bool has_res = p.residual != nullptr && ri.valid;
     const bool has_res2 = p.residual2 != nullptr && ri.valid;
     const __half* rrow = has_res ? p.residual + (long long)m * p.ldr + n0 : nullptr;
@@ -479,7 +510,7 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
         if (prow && c + NC < c_hi) load_res<NC>(prow + c + NC, res);
-        epi_chunk<NC, J, SEQ>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
+        epi_chunk<NC, J, SEQ, false>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
                          sss, has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
                          y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
                          arow ? arow + c : nullptr, add_in_res);
@@ -626,7 +657,7 @@ __device__ __forceinline__ int tile_stride() {
 // and half of the tile's weight columns; the even CTA issues the pair MMAs and its
 // commits arrive in both CTAs; every load of the pair completes on the even CTA's
 // full barrier, and both CTAs' epilogue warps release the even CTA's accumulator.
-template <int NMB, int J, bool PAIR, bool SEQ>
+template <int NMB, int J, bool PAIR, bool SEQ, bool PLAIN = false>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -1062,9 +1093,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                        acc * acc_cols + (uint32_t)(mb * J * p.BN);
                 const RowInfo ri = row_info<SEQ>(p, stv, m, live);
                 if ((c_hi - c_lo) % 32 == 0)
-                    epi_rows<32, J, SEQ>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<32, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
                 else
-                    epi_rows<16, J, SEQ>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<16, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
             }
             if (live) {
                 tc_fence_before();
@@ -1777,8 +1808,13 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
         return 0;
     };
+    // The plain epilogue (bias, ReLU, mask, GRID / PHASE store): every ResNet34 conv.
+    const bool plain = !seq && a->act == 0 && !a->residual && !a->residual2 && !a->y2 &&
+                       !a->ysum && a->clamp_hi <= 0.0f && (a->y_phase == 0 || a->y_phase == 1);
     if (pair) {
-        auto kern = seq ? conv_tc_kernel<1, 1, true, true> : conv_tc_kernel<1, 1, true, false>;
+        auto kern = seq ? conv_tc_kernel<1, 1, true, true>
+                        : (plain ? conv_tc_kernel<1, 1, true, false, true>
+                                 : conv_tc_kernel<1, 1, true, false>);
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
         if (cs == cudaStreamCaptureStatusNone)
@@ -1810,6 +1846,16 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
                              : launch(conv_tc_kernel<1, 1, false, true>);
     }
     const int key = p.n_mblk * 100 + J;
+    if (plain) {
+        switch (key) {
+            case 101: return launch(conv_tc_kernel<1, 1, false, false, true>);
+            case 201: return launch(conv_tc_kernel<2, 1, false, false, true>);
+            case 301: return launch(conv_tc_kernel<3, 1, false, false, true>);
+            case 401: return launch(conv_tc_kernel<4, 1, false, false, true>);
+            case 801: return launch(conv_tc_kernel<8, 1, false, false, true>);
+            default: break;  // ksplit > 1: the general epilogue
+        }
+    }
     switch (key) {
         case 101: return launch(conv_tc_kernel<1, 1, false, false>);
         case 102: return launch(conv_tc_kernel<1, 2, false, false>);
