@@ -142,6 +142,7 @@ struct ConvDev {
     int xform;
     const float* x_scale;
     const float* x_shift;
+    int n_iss;               // MMA-issuing warps (2-D tiles of 2+ row blocks: 2)
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -534,7 +535,7 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 //     kt*Wp + (kf>>1) rows;
 //   2 PHASE (stride-2 input, 4 planes): plane 2*(kt&1) + (kf&1), (kt>>1)*Wp + (kf>>1)
 //     rows.
-template <int KS, int NMB, int J>
+template <int KS, int NMB, int J, int MB0 = 0, int MBS = 1>
 __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                            uint32_t wp_units, uint32_t rb16, uint64_t b_desc,
                                            uint32_t b_tap_units, uint32_t idesc, bool first,
@@ -563,7 +564,7 @@ __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_
             const int q = tap * KS + k;
             const int j = q % J;
 #pragma unroll
-            for (int mb = 0; mb < NMB; ++mb)
+            for (int mb = MB0; mb < NMB; mb += MBS)
                 umma_f16(d_tile + (uint32_t)(mb * J + j) * bn,
                          at + (uint64_t)(mb * 128 * rb16) + 2 * k, bt + 2 * k, idesc,
                          (first && q < J) ? 0u : 1u);
@@ -574,7 +575,7 @@ __device__ __forceinline__ void issue_halo(uint32_t d_tile, uint32_t bn, uint64_
 // TAP stage: one (tap, channel block) A tile and its weight tile, rotating over
 // JU = min(J, KS) partials. When this is the tile's first segment the host
 // guarantees J <= KS, so the first stage initialises every partial.
-template <int KS, int NMB, int J, bool PAIR>
+template <int KS, int NMB, int J, bool PAIR, int MB0 = 0, int MBS = 1>
 __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                           uint32_t rb16, uint64_t b_desc, uint32_t idesc,
                                           bool first) {
@@ -583,7 +584,7 @@ __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t
     for (int k = 0; k < KS; ++k) {
         const int j = k % JU;
 #pragma unroll
-        for (int mb = 0; mb < NMB; ++mb) {
+        for (int mb = MB0; mb < NMB; mb += MBS) {
             if constexpr (PAIR)
                 umma_f16_pair(d_tile + (uint32_t)(mb * J + j) * bn,
                               a_desc + (uint64_t)(mb * 128 * rb16) + 2 * k, b_desc + 2 * k, idesc,
@@ -598,7 +599,7 @@ __device__ __forceinline__ void issue_tap(uint32_t d_tile, uint32_t bn, uint64_t
 
 // 1-D HALO: n_taps taps, tap j starting j*dil rows (dil_units = dil*rb16) into the
 // halo, which begins (k-1)/2*dil rows before the tile.
-template <int KS, int NMB, int J>
+template <int KS, int NMB, int J, int MB0 = 0, int MBS = 1>
 __device__ __forceinline__ void issue_halo1d(uint32_t d_tile, uint32_t bn, uint64_t a_desc,
                                              uint32_t rb16, uint64_t b_desc, uint32_t b_tap_units,
                                              uint32_t idesc, bool first, int n_taps,
@@ -611,7 +612,7 @@ __device__ __forceinline__ void issue_halo1d(uint32_t d_tile, uint32_t bn, uint6
             const int q = tap * KS + k;
             const int j = q % J;
 #pragma unroll
-            for (int mb = 0; mb < NMB; ++mb)
+            for (int mb = MB0; mb < NMB; mb += MBS)
                 umma_f16(d_tile + (uint32_t)(mb * J + j) * bn,
                          at + (uint64_t)(mb * 128 * rb16) + 2 * k, bt + 2 * k, idesc,
                          (first && q < J) ? 0u : 1u);
@@ -619,25 +620,52 @@ __device__ __forceinline__ void issue_halo1d(uint32_t d_tile, uint32_t bn, uint6
     }
 }
 
-template <int NMB, int J, bool PAIR>
+template <int NMB, int J, bool PAIR, int MB0 = 0, int MBS = 1>
 __device__ __forceinline__ void issue_stage(bool halo, int ks, uint32_t d_tile, uint32_t bn,
                                             uint64_t a_desc, uint32_t wp_units, uint32_t rb16,
                                             uint64_t b_desc, uint32_t b_tap_units, uint32_t idesc,
                                             bool first, int hmode = 0, uint32_t plane_units = 0,
                                             int taps1d = 0, uint32_t dil_units = 0) {
     if (!PAIR && halo && taps1d) {
-        if (ks == 4) issue_halo1d<4, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
-        else if (ks == 2) issue_halo1d<2, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
-        else issue_halo1d<1, NMB, J>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+        if (ks == 4) issue_halo1d<4, NMB, J, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+        else if (ks == 2) issue_halo1d<2, NMB, J, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
+        else issue_halo1d<1, NMB, J, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, b_tap_units, idesc, first, taps1d, dil_units);
     } else if (!PAIR && halo) {
-        if (ks == 4) issue_halo<4, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
-        else if (ks == 2) issue_halo<2, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
-        else issue_halo<1, NMB, J>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
+        if (ks == 4) issue_halo<4, NMB, J, MB0, MBS>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
+        else if (ks == 2) issue_halo<2, NMB, J, MB0, MBS>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
+        else issue_halo<1, NMB, J, MB0, MBS>(d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units, idesc, first, hmode, plane_units);
     } else {
-        if (ks == 4) issue_tap<4, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
-        else if (ks == 2) issue_tap<2, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
-        else issue_tap<1, NMB, J, PAIR>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        if (ks == 4) issue_tap<4, NMB, J, PAIR, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else if (ks == 2) issue_tap<2, NMB, J, PAIR, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
+        else issue_tap<1, NMB, J, PAIR, MB0, MBS>(d_tile, bn, a_desc, rb16, b_desc, idesc, first);
     }
+}
+
+// The stage's MMAs for issuer `iss` of `n_iss`: with two issuing warps each takes
+// every second row block (compile-time start and stride, so each issuer's unrolled
+// sequence has the same shape as a single issuer's).
+template <int NMB, int J, bool PAIR, bool SEQ>
+__device__ __forceinline__ void issue_split(int n_iss, int iss, bool halo, int ks, uint32_t d_tile,
+                                            uint32_t bn, uint64_t a_desc, uint32_t wp_units,
+                                            uint32_t rb16, uint64_t b_desc, uint32_t b_tap_units,
+                                            uint32_t idesc, bool first, int hmode = 0,
+                                            uint32_t plane_units = 0, int taps1d = 0,
+                                            uint32_t dil_units = 0) {
+    if constexpr (NMB >= 2 && !PAIR && !SEQ) {
+        if (n_iss == 2) {
+            if (iss == 0)
+                issue_stage<NMB, J, PAIR, 0, 2>(halo, ks, d_tile, bn, a_desc, wp_units, rb16,
+                                                b_desc, b_tap_units, idesc, first, hmode,
+                                                plane_units, taps1d, dil_units);
+            else
+                issue_stage<NMB, J, PAIR, 1, 2>(halo, ks, d_tile, bn, a_desc, wp_units, rb16,
+                                                b_desc, b_tap_units, idesc, first, hmode,
+                                                plane_units, taps1d, dil_units);
+            return;
+        }
+    }
+    issue_stage<NMB, J, PAIR>(halo, ks, d_tile, bn, a_desc, wp_units, rb16, b_desc, b_tap_units,
+                              idesc, first, hmode, plane_units, taps1d, dil_units);
 }
 
 // Persistent tile loop bounds. Read from the special registers at each loop rather
@@ -691,13 +719,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         }
     for (int i = threadIdx.x; i < p.batch; i += blockDim.x) stv[i] = p.tvalid[i];
     if (threadIdx.x == 0) {
+        const uint32_t n_iss = (SEQ || PAIR) ? 1u : (uint32_t)p.n_iss;  // commits per phase
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, n_iss);
             mbar_init(bar_xfull + 8 * s, 2);  // one arrival per transform warp
         }
         for (int a = 0; a < 2; ++a) {
-            mbar_init(bar_tfull + 8 * a, 1);
+            mbar_init(bar_tfull + 8 * a, n_iss);
             mbar_init(bar_tempty + 8 * a, PAIR ? 2 * (kEpiThreads / 32) : kEpiThreads);
         }
         mbar_init(bar_bres, 1);
@@ -872,7 +901,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 for (uint32_t i = 0; i < S; ++i) mbar_wait_drain(bar_full + 8 * i, phase, 20000000ull);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || (!SEQ && !PAIR && warp == 2 && p.n_iss == 2)) {
+        // One MMA-issuing thread paces small-N tiles (an N = 32 MMA every ~57 cycles
+        // from one thread against the tensor pipe's 40): 2-D tiles of two or more row
+        // blocks split them over warps 1 and 2, each committing to every barrier.
+        const int n_iss = (SEQ || PAIR) ? 1 : p.n_iss;
+        const int iss = warp - 1;
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer ----------------
             uint32_t stage = 0, phase = 0;
@@ -930,9 +964,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                                  : 0ull);
                                 const uint64_t b_desc =
                                     umma_sdesc(base + p.b_ring0 + sb * p.b_stride, row_bytes);
-                                issue_stage<NMB, J, false>(false, ksteps, d_tile, (uint32_t)p.BN, a_desc,
-                                                    wp_units, rb16, b_desc, b_tap_units, idesc,
-                                                    first);
+                                issue_split<NMB, J, false, SEQ>(n_iss, iss, false, ksteps, d_tile,
+                                                                (uint32_t)p.BN, a_desc, wp_units,
+                                                                rb16, b_desc, b_tap_units, idesc,
+                                                                first);
                                 first = false;
                                 umma_commit(bar_empty + 8 * ib);
                                 issued = true;
@@ -963,11 +998,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         const uint64_t a_desc = a_desc0 + (uint64_t)(stage * (p.stage_bytes >> 4));
                         const uint64_t b_desc = halo ? bres_desc + (uint64_t)(it * b_kb_units)
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
-                        issue_stage<NMB, J, PAIR>(halo, ksteps, d_tile, (uint32_t)p.BN, a_desc,
-                                                  wp_units, rb16, b_desc, b_tap_units, idesc, first,
-                                                  s.halo_mode, s.plane_bytes >> 4,
-                                                  SEQ ? s.n_taps : 0,
-                                                  SEQ ? (uint32_t)s.dil * rb16 : 0u);
+                        issue_split<NMB, J, PAIR, SEQ>(n_iss, iss, halo, ksteps, d_tile,
+                                                       (uint32_t)p.BN, a_desc, wp_units, rb16,
+                                                       b_desc, b_tap_units, idesc, first,
+                                                       s.halo_mode, s.plane_bytes >> 4,
+                                                       SEQ ? s.n_taps : 0,
+                                                       SEQ ? (uint32_t)s.dil * rb16 : 0u);
                         first = false;
                         if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
                         else umma_commit(bar_empty + 8 * stage);
@@ -1586,6 +1622,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     if (pair) BM = 2 * kMB;
     p.BM = BM;
     p.n_mblk = pair ? 1 : BM / kMB;
+    p.n_iss = (!seq && !pair && p.n_mblk >= 2) ? 2 : 1;
     p.J = J;
     p.n_acc = (2 * p.n_mblk * J * BN <= 512) ? 2 : 1;
     const int cta_rows = pair ? kMB : BM;   // A rows one CTA loads per stage
