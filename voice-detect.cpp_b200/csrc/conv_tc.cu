@@ -1494,11 +1494,10 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // HALO for stride-1 3x3 segments whose weights fit in shared memory.
     const uint32_t w_bytes0 = (uint32_t)9 * a->ic0 * BN * 2;
     // Feed of segment 0: HALO (one A halo per channel block, resident weights) when
-    // the weights fit, else TAP. HALO_S (a->halo = 2: the halo with the weights
-    // streamed per tap through a second ring) cuts the A traffic of a stride-1 3x3
-    // by ~9x, but measured no faster than TAP on the ResNet34 shapes (the epilogue
-    // and the MMA issue bound those convs, not the L2 feed), so auto does not pick
-    // it. a->halo: 0 auto, 1 force HALO, 2 force HALO_S, -1 TAP.
+    // the weights fit; else, for stride-1 3x3 convs of up to 128 columns, HALO_S (the
+    // halo with the weights streamed per tap through a second ring: ~9x less A
+    // traffic than TAP); else TAP. a->halo: 0 auto, 1 force HALO, 2 force HALO_S,
+    // -1 TAP.
     // The resident-weight HALO also feeds the frequency-stride-2 conv over FPHASE
     // (stride 3): one halo per plane, the 9 taps as row shifts inside them.
     const bool hs_ok = !seq && a->k0 == 3 && a->stride0 == 1 && n_nt == 1;
@@ -1518,7 +1517,14 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         return 1;
     }
     const bool halo = a->halo == 0 ? halo_ok && (!seq || BN <= 64) : (a->halo == 1 && halo_ok);
-    const bool two_ring = a->halo == 2 && hs_ok;
+    // Stride-1 3x3 convs whose weights do not fit resident take the halo with streamed
+    // weights automatically up to 128 columns (ResNet34 128 -> 128 at batch 512 x 300
+    // frames: 972 -> 1074 TFLOP/s; with the fused downsample 956 -> 1035); 256-column
+    // tiles run as CTA pairs instead (1152 against 1082 for the streamed halo).
+    const bool auto_two_ring = a->halo == 0 && !seq && hs_ok && !halo_ok && BN <= 128 &&
+                               a->ksplit <= 1 && (a->tile_m == 0 || a->tile_m == 256) &&
+                               a->pair != 1;
+    const bool two_ring = (a->halo == 2 && hs_ok) || auto_two_ring;
     if ((a->halo == 1 && !halo_ok) || (a->halo == 2 && !hs_ok)) {
         set_error("vdb_conv: HALO modes need a 3x3 conv with oc <= 256, stride 1 (or stride "
                   "2 / the frequency-only stride 3 for the resident HALO) and weights <= 96 KB "
