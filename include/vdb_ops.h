@@ -120,7 +120,27 @@ typedef struct vdb_conv_args {
     int pair;               /* CTA pairs (tcgen05 cta_group::2: two SMs share one 256-row
                                tile, each holding half of the weight columns): 0 auto,
                                1 on (one-tap-per-stage feed only), -1 off */
+    int qpack;              /* 1: a ResNet stage-1 conv (3x3, stride 1, ic0 = oc = 32) over
+                               the QPACK layout: x0, y (y_phase 0) and residual are
+                               QP(B, t_out, f_out) rows of 128 channels (vdb_qpack_rows),
+                               w0 is the packed weight of vdb_qpack_pack_weights, residual
+                               (optional) is added before the ReLU, y_phase 1 writes the
+                               PHASE layout instead; no second segment */
 } vdb_conv_args;
+
+/* QPACK layout QP(B, T, F): the zero-bordered grid of G(B, T, F, 32) with four
+ * consecutive padded frequency pixels per row: row (b*(T+2) + t')*Wq + q holds
+ * pixels f' = 4q + j, j = 0..3, as channels j*32 .. j*32 + 31 (Wq = ceil((F+2)/4);
+ * the pixels past the padded grid are zero). A stage-1 conv then issues 18 tensor-core
+ * MMAs of N = 32..96 per 512 output pixels and 32 input channels instead of 36 of
+ * N = 32 (an N = 32 MMA is bound by fetching its A operand, not by its math). */
+long long vdb_qpack_rows(int batch, int t, int f);
+
+/* Packs a stage-1 conv weight for QPACK convs: w_taps device f16 [32][9][32] (the
+ * vdb_conv layout [oc][kt*3 + kf][ic]) -> out device f16 [3][384][32]: for time tap kt
+ * and input pixel shift u = -1..4 the rows (j, oc) for output pixel phases j with
+ * 0 <= u - j + 1 <= 2 hold W[oc][kt*3 + (u - j + 1)][:]. Asynchronous on `stream`. */
+int vdb_qpack_pack_weights(const void* w_taps, void* out, void* stream);
 
 /* Implicit-GEMM conv on tcgen05 tensor cores (f16 in, f32 accumulate).
  * Launch ordering: vdb_conv and vdb_conv1d launch with programmatic stream

@@ -361,3 +361,61 @@ def test_conv_sum_output(cuda_lib):
     assert torch.all(g4[:, 0] == 0) and torch.all(g4[:, :, 0] == 0)
     for b, t in enumerate(tv):
         assert torch.all(g4[b, 1 + t:] == 0)
+
+
+QPACK_CASES = [
+    # name, B, F, T, tvalid, residual, y_phase, tile_m
+    ("qp_ragged", 3, 80, 37, [37, 20, 5], False, 0, 0),
+    ("qp_res", 3, 80, 37, [37, 21, 1], True, 0, 0),
+    ("qp_phase", 2, 80, 31, [31, 12], True, 1, 0),
+    ("qp_tile128", 3, 80, 37, [37, 20, 5], True, 0, 128),
+    ("qp_tall", 16, 80, 300, [300, 299, 251, 200, 150, 100, 64, 33, 300, 17, 9, 5, 3, 2, 1, 280],
+     True, 0, 0),
+    ("qp_f16", 4, 16, 23, [23, 9, 1, 14], True, 0, 0),
+    ("qp_f18_phase", 2, 18, 9, [9, 4], False, 1, 128),
+]
+
+
+@pytest.mark.parametrize("case", QPACK_CASES, ids=[c[0] for c in QPACK_CASES])
+def test_conv_qpack_vs_reference(cuda_lib, case):
+    """Stage-1 conv over the QPACK layout (four frequency pixels per row, the
+    (time tap, pixel shift) MMA schedule) against the f32 conv of the same f16 values:
+    rel-L2 <= 1e-3 over valid pixels, exact zeros at borders, past each clip's length
+    and past the padded grid; optional QPACK residual (the BasicBlock identity) and the
+    PHASE output of the last stage-1 conv."""
+    import torch
+    vd = cuda_lib
+    name, B, F, T, tv, use_res, y_phase, tile_m = case
+    g = torch.Generator().manual_seed(99)
+    x = _h(torch.relu(torch.randn(B, 32, F, T, generator=g)))
+    for b, t in enumerate(tv):
+        x[b, :, :, t:] = 0
+    w = _h(torch.randn(32, 32, 3, 3, generator=g) * (2.0 / (32 * 9)) ** 0.5)
+    bias = torch.randn(32, generator=g) * 0.1
+    res = None
+    if use_res:
+        res = _h(torch.relu(torch.randn(B, 32, F, T, generator=g)))
+        for b, t in enumerate(tv):
+            res[b, :, :, t:] = 0
+    ref = _ref_conv(x, w, bias, 1, residual=res, relu=True, tvalid_out=tv,
+                    use_oracle=B * 32 * F * T * 288 < 2e7)
+    dev = "cuda"
+    tv_dev = torch.tensor(tv, dtype=torch.int32, device=dev)
+    wq = vd.qpack_weights(vd.pack_conv_weight(w.to(dev)))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    y = vd.conv(vd.to_qpack(x.to(dev), tv), wq, bias.float().to(dev), tv_dev, batch=B, t_out=T,
+                f_out=F, oc=32, k0=3, ic0=32, relu=True, err=err, tile_m=tile_m, qpack=True,
+                residual=vd.to_qpack(res.to(dev), tv) if use_res else None, y_phase=y_phase)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    if y_phase:
+        got = vd.from_phase(y, B, 32, F, T).cpu()
+    else:
+        got = vd.from_qpack(y, B, F, T).cpu()
+        full = vd.from_qpack(y, B, F, T, interior=False).cpu()  # (B, 32, 4Wq, T+2)
+        assert torch.all(full[:, :, :, 0] == 0) and torch.all(full[:, :, 0] == 0)
+        assert torch.all(full[:, :, F + 1:] == 0)  # right border and past the grid
+        for b, t in enumerate(tv):
+            assert torch.all(full[b, :, :, 1 + t:] == 0)
+    rel = float((got - ref).norm() / max(ref.norm(), 1e-12))
+    assert rel <= REL_L2_TOL, f"{name}: rel-L2 {rel:.3e}"

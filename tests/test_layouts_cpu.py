@@ -77,3 +77,26 @@ def test_seq_zero_and_reflect_padding():
             assert torch.equal(r[b, P - j], r[b, P + j])
             assert torch.equal(r[b, P + t - 1 + j], r[b, P + t - 1 - j])
     assert torch.equal(vd.from_seq(z.reshape(-1, C), B, C, T, P)[1, :, :6], x[1, :, :6])
+
+
+def test_qpack_round_trip_and_row_formula():
+    """QPACK: row (b*(T+2) + t')*Wq + q holds padded pixels f' = 4q + j as channels
+    j*32 .. j*32 + 31; a round trip returns the interior and every other slot is 0."""
+    import torch
+    import vd_b200 as vd
+    B, F, T = 2, 18, 5
+    x = torch.randn(B, 32, F, T)
+    q = vd.to_qpack(x, [5, 3])
+    Wq = vd.qpack_width(F)
+    assert Wq == 5 and q.shape == (B * (T + 2) * Wq, 128)
+    back = vd.from_qpack(q, B, F, T)
+    want = x.half().float().clone()
+    want[1, :, :, 3:] = 0
+    assert torch.equal(back, want)
+    b, t, f, c = 1, 2, 13, 7  # padded (t+1, f+1)
+    row = (b * (T + 2) + t + 1) * Wq + (f + 1) // 4
+    assert q[row, ((f + 1) % 4) * 32 + c] == x[b, c, f, t].half()
+    full = vd.from_qpack(q, B, F, T, interior=False)
+    mask = torch.zeros_like(full, dtype=torch.bool)
+    mask[:, :, 1:F + 1, 1:T + 1] = True
+    assert torch.all(full[~mask] == 0)

@@ -143,6 +143,10 @@ struct ConvDev {
     const float* x_scale;
     const float* x_shift;
     int n_iss;               // MMA-issuing warps (2-D tiles of 2+ row blocks: 2)
+    // QPACK (stage-1 3x3, 32 -> 32): rows of four frequency pixels x 32 channels. Wp is
+    // then the row count per time step (Wq = ceil((F + 2) / 4)) and qp_res the optional
+    // QPACK residual added in the epilogue (the BasicBlock identity shortcut).
+    const __half* qp_res;
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -156,7 +160,7 @@ __device__ __forceinline__ int fdiv(int n, uint32_t mul, int sh) {
 // True when rows [m0, m0+BM) contain at least one pixel inside a clip's valid
 // time range (conservative: border columns of those rows count). Every role
 // evaluates it identically, so skipped tiles never touch the pipeline.
-template <bool SEQ>
+template <bool SEQ, bool QP = false>
 __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m0) {
     const int img = p.Hp * p.Wp;
     const int mend = min(m0 + p.BM, p.M);
@@ -165,8 +169,9 @@ __device__ __forceinline__ bool tile_live(const ConvDev& p, const int* tv, int m
         const int r1 = min(mend - b * img, img);
         const int t = tv[b];
         if (t <= 0) continue;
-        const int lo = SEQ ? p.pad : p.Wp + 1;
-        const int hi = SEQ ? p.pad + t : p.Wp * t + p.F + 1;
+        // QPACK: time row t' spans rows [t' * Wp, (t' + 1) * Wp)
+        const int lo = SEQ ? p.pad : (QP ? p.Wp : p.Wp + 1);
+        const int hi = SEQ ? p.pad + t : (QP ? p.Wp * (t + 1) : p.Wp * t + p.F + 1);
         if (r0 < hi && r1 > lo) return true;
     }
     return false;
@@ -518,6 +523,106 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
     }
 }
 
+// ---- QPACK ------------------------------------------------------------------
+// A stage-1 conv (3x3, stride 1, 32 -> 32) over QPACK rows: row (b, t', q) holds the
+// four padded frequency pixels f' = 4q + j (j = 0..3) x 32 channels. Output pixel
+// (t', 4q + j) needs input (t' + kt - 1, 4q + u) with u = j + kf - 1 in [-1, 4], i.e.
+// QPACK row (t' + kt - 1, q + floor(u / 4)) at pixel phase u & 3. So for each (kt, u)
+// one MMA (K = that phase's 32 channels) produces the partial sums of every output
+// pixel phase j it touches (j_min = max(0, u - 1) .. j_max = min(3, u + 1), N = 32 per
+// phase) against packed weights W[kt][u][(j, oc)][ic] = W[oc][kt][u - j + 1][ic]:
+// 18 MMAs of N = 32..96 per 128 rows and K step instead of 36 of N = 32, and a 128-row
+// accumulator holds 512 output pixels. A stage is one 64-channel half of the rows
+// (phases 2h, 2h + 1) as a halo of tile + 2 Wq + 2 rows; the packed weights (3 x 384
+// rows of 32 channels) stay resident.
+__host__ __device__ constexpr int qp_u(int half, int ui) {
+    // stage 0 first issues u = 1 (columns 0..95) and u = 4 (96..127): together they
+    // cover the accumulator, so they overwrite it and every later MMA accumulates
+    return half == 0 ? (ui == 0 ? 1 : (ui == 1 ? 4 : 0)) : (ui == 0 ? -1 : (ui == 1 ? 2 : 3));
+}
+__host__ __device__ constexpr int qp_jmin(int u) { return u - 1 < 0 ? 0 : u - 1; }
+__host__ __device__ constexpr int qp_jmax(int u) { return u + 1 > 3 ? 3 : u + 1; }
+// first packed-weight row of (kt, u): blocks in u order -1..4 of 32 / 64 / 96 / 96 /
+// 64 / 32 rows, 384 rows per kt
+__host__ __device__ constexpr int qp_wrow(int kt, int u) {
+    return kt * 384 + (u == -1 ? 0 : (u == 0 ? 32 : (u == 1 ? 96 : (u == 2 ? 192 : (u == 3 ? 288 : 352)))));
+}
+
+template <int NMB, int HALF, int MB0, int MBS>
+__device__ __forceinline__ void issue_qpack(uint32_t d_tile, uint64_t a_desc, uint32_t wq_units,
+                                            uint64_t b_desc, const uint32_t (&idn)[3],
+                                            bool first) {
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt) {
+#pragma unroll
+        for (int ui = 0; ui < 3; ++ui) {
+            const int u = qp_u(HALF, ui);
+            const int jmin = qp_jmin(u), nn = qp_jmax(u) - jmin + 1;
+            const int rsh = u < 0 ? 0 : (u > 3 ? 2 : 1);  // halo rows past kt * Wq
+            // a 128-byte row is 8 descriptor units; phase u & 3 is the (u & 1)-th 32 channels
+            const uint64_t at = a_desc + (uint64_t)(kt * wq_units + rsh * 8 + ((u & 3) & 1) * 4);
+            const uint64_t bt = b_desc + (uint64_t)(qp_wrow(kt, u) * 4);  // 64-byte rows
+            const uint32_t dt = d_tile + (uint32_t)(32 * jmin);
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const bool init = first && HALF == 0 && kt == 0 && ui < 2 && k == 0;
+#pragma unroll
+                for (int mb = MB0; mb < NMB; mb += MBS)
+                    umma_f16(dt + (uint32_t)(mb * 128), at + (uint64_t)(mb * 128 * 8) + 2 * k,
+                             bt + 2 * k, idn[nn - 1], init ? 0u : 1u);
+            }
+        }
+    }
+}
+
+// Epilogue of pixel phase j of QPACK row m (accumulator columns [32 j, 32 j + 32) in
+// v): + bias [+ residual] -> ReLU -> mask -> f16, stored to the same QPACK row
+// (y_phase 0) or to the pixel's place in the PHASE layout (y_phase 1). res holds the
+// residual's 32 channels when p.qp_res (prefetched by the caller).
+__device__ __forceinline__ void qpack_unit(const ConvDev& p, const int* stv, int m, bool live,
+                                           int j, const uint32_t (&v)[32], const float* sbias,
+                                           const uint4 (&res)[4]) {
+    if (m >= p.M) return;
+    const int img = p.Hp * p.Wp;
+    const int b = fdiv(m, p.img_mul, p.img_sh);
+    const int r = m - b * img;
+    const int tp = fdiv(r, p.wp_mul, p.wp_sh);
+    const int fp = 4 * (r - tp * p.Wp) + j;
+    const bool valid = live && tp >= 1 && tp <= stv[b] && fp >= 1 && fp <= p.F;
+    __half* dst;
+    if (p.y_phase == 1) {
+        if (fp > p.F + 1) return;  // past the padded grid: no PHASE slot
+        const int q = ((tp & 1) << 1) | (fp & 1);
+        dst = p.y + ((long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
+                     (fp >> 1) + 1) * 32;
+    } else {
+        dst = p.y + (long long)m * 128 + j * 32;
+    }
+    const uint32_t keep = valid ? 0xFFFFFFFFu : 0u;
+    const __half2 zero2 = __float2half2_rn(0.0f);
+    uint4* yp = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t rw[4] = {res[c].x, res[c].y, res[c].z, res[c].w};
+        __half2 h[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float a0 = __uint_as_float(v[c * 8 + 2 * q]) + sbias[c * 8 + 2 * q];
+            float a1 = __uint_as_float(v[c * 8 + 2 * q + 1]) + sbias[c * 8 + 2 * q + 1];
+            if (p.qp_res) {
+                a0 += h2f(rw[q] & 0xFFFFu);
+                a1 += h2f(rw[q] >> 16);
+            }
+            h[q] = __floats2half2_rn(a0, a1);
+            if (p.relu) h[q] = __hmax2(h[q], zero2);
+        }
+        yp[c] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
+                           *reinterpret_cast<uint32_t*>(&h[1]) & keep,
+                           *reinterpret_cast<uint32_t*>(&h[2]) & keep,
+                           *reinterpret_cast<uint32_t*>(&h[3]) & keep);
+    }
+}
+
 // ---- MMA issue schedules ---------------------------------------------------
 // The single issuing thread is on the critical path (a tcgen05.mma every ~60
 // cycles at best), so each stage is one fully unrolled, branch-free sequence with
@@ -668,6 +773,28 @@ __device__ __forceinline__ void issue_split(int n_iss, int iss, bool halo, int k
                               idesc, first, hmode, plane_units, taps1d, dil_units);
 }
 
+// The QPACK stage `half` for issuer `iss` of `n_iss` (two issuers take alternate row
+// blocks, as issue_split).
+template <int NMB>
+__device__ __forceinline__ void qpack_stage(int n_iss, int iss, int half, uint32_t d_tile,
+                                            uint64_t a_desc, uint32_t wq_units, uint64_t b_desc,
+                                            const uint32_t (&idn)[3], bool first) {
+    if constexpr (NMB >= 2) {
+        if (n_iss == 2) {
+            if (iss == 0) {
+                if (half) issue_qpack<NMB, 1, 0, 2>(d_tile, a_desc, wq_units, b_desc, idn, first);
+                else issue_qpack<NMB, 0, 0, 2>(d_tile, a_desc, wq_units, b_desc, idn, first);
+            } else {
+                if (half) issue_qpack<NMB, 1, 1, 2>(d_tile, a_desc, wq_units, b_desc, idn, first);
+                else issue_qpack<NMB, 0, 1, 2>(d_tile, a_desc, wq_units, b_desc, idn, first);
+            }
+            return;
+        }
+    }
+    if (half) issue_qpack<NMB, 1, 0, 1>(d_tile, a_desc, wq_units, b_desc, idn, first);
+    else issue_qpack<NMB, 0, 0, 1>(d_tile, a_desc, wq_units, b_desc, idn, first);
+}
+
 // Persistent tile loop bounds. Read from the special registers at each loop rather
 // than held in kernel-lifetime variables: keeping them live across the roles cost
 // the epilogue-bound 2-D convs up to 15% (register pressure in the epilogue).
@@ -685,7 +812,7 @@ __device__ __forceinline__ int tile_stride() {
 // and half of the tile's weight columns; the even CTA issues the pair MMAs and its
 // commits arrive in both CTAs; every load of the pair completes on the even CTA's
 // full barrier, and both CTAs' epilogue warps release the even CTA's accumulator.
-template <int NMB, int J, bool PAIR, bool SEQ, bool PLAIN = false>
+template <int NMB, int J, bool PAIR, bool SEQ, bool PLAIN = false, bool QP = false>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
@@ -711,7 +838,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the MMA-issuing CTA
 
-    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) sbias[i] = p.bias ? p.bias[i] : 0.0f;
+    // QPACK: the 128 accumulator columns are 4 pixel phases x the 32 output channels
+    for (int i = threadIdx.x; i < p.oc; i += blockDim.x)
+        sbias[i] = p.bias ? p.bias[QP ? (i & 31) : i] : 0.0f;
     if (sss)
         for (int i = threadIdx.x; i < p.oc; i += blockDim.x) {
             sss[i] = p.bn_scale[i];
@@ -766,7 +895,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             // Resident weights of HALO segments: every (tap, channel block) box once.
-            if (p.bres_bytes) {
+            if (QP) {
+                // QPACK: the packed weights, 9 boxes of 128 rows x 32 channels
+                mbar_arrive_expect_tx(bar_bres, p.bres_bytes);
+                for (int r = 0; r < 1152; r += 128)
+                    tma_load_2d(base + p.seg[0].bres + (uint32_t)r * 64u, &tmB0, bar_bres, 0, r);
+            } else if (p.bres_bytes) {
                 mbar_arrive_expect_tx(bar_bres, p.bres_bytes);
                 for (int sg = 0; sg < p.n_seg; ++sg) {
                     const SegDev& s = p.seg[sg];
@@ -788,7 +922,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
                     const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
                     const int m0 = mt * p.BM, n0 = nt * p.BN;
-                    if (!tile_live<SEQ>(p, stv, m0)) continue;
+                    if (!tile_live<SEQ, QP>(p, stv, m0)) continue;
                     for (int sg = 0; sg < p.n_seg && ok; ++sg) {
                         const SegDev& s = p.seg[sg];
                         const CUtensorMap* ta = sg ? &tmA1 : &tmA0;
@@ -840,7 +974,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             for (int tile = first_tile<PAIR>(); tile < n_tiles && ok && !p.two_ring; tile += tile_stride<PAIR>()) {
                 const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
                 const int m0 = mt * p.BM, n0 = nt * p.BN;
-                if (!tile_live<SEQ>(p, stv, m0)) continue;
+                if (!tile_live<SEQ, QP>(p, stv, m0)) continue;
                 // this CTA's A rows and weight rows (a pair splits both in halves)
                 [[maybe_unused]] const int am0 = m0 + (int)rank * kMB;
                 [[maybe_unused]] const int bn0 = n0 + (int)rank * (p.BN / 2);
@@ -912,13 +1046,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             uint32_t stage = 0, phase = 0;
             uint32_t acc = 0, acc_phase = 0;
             uint32_t sa = 0, pa = 0, sb = 0, pb = 0;  // two-ring slots and phases
+            [[maybe_unused]] const uint32_t qp_idn[3] = {umma_idesc_f16(kMB, 32), umma_idesc_f16(kMB, 64),
+                                                         umma_idesc_f16(kMB, 96)};
             bool ok = true, issued = false;
             if (p.bres_bytes &&
                 !mbar_wait(bar_bres, 0, p.err, VDB_ERR_TIMEOUT_FULL, abort_flag))
                 ok = false;
             for (int tile = first_tile<PAIR>(); tile < n_tiles && ok; tile += tile_stride<PAIR>()) {
                 const int mt = tile / p.n_nt;
-                if (!tile_live<SEQ>(p, stv, mt * p.BM)) continue;
+                if (!tile_live<SEQ, QP>(p, stv, mt * p.BM)) continue;
                 if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1, p.err,
                                VDB_ERR_TIMEOUT_TEMPTY, abort_flag)) {
                     ok = false;
@@ -996,6 +1132,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                         }
                         tc_fence_after();
                         const uint64_t a_desc = a_desc0 + (uint64_t)(stage * (p.stage_bytes >> 4));
+                        if constexpr (QP) {
+                            if (sg == 0) {
+                                // stage `it` = channel half `it` of the QPACK halo
+                                qpack_stage<NMB>(n_iss, iss, it, d_tile, a_desc, wp_units,
+                                                 umma_sdesc(base + s.bres, 64), qp_idn, first);
+                                goto stage_issued;
+                            }
+                        }
+                        {
                         const uint64_t b_desc = halo ? bres_desc + (uint64_t)(it * b_kb_units)
                                                      : a_desc + (uint64_t)(p.a_region >> 4);
                         issue_split<NMB, J, PAIR, SEQ>(n_iss, iss, halo, ksteps, d_tile,
@@ -1004,6 +1149,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                                        s.halo_mode, s.plane_bytes >> 4,
                                                        SEQ ? s.n_taps : 0,
                                                        SEQ ? (uint32_t)s.dil * rb16 : 0u);
+                        }
+                    stage_issued:
                         first = false;
                         if constexpr (PAIR) umma_commit_pair(bar_empty + 8 * stage, 0x3);
                         else umma_commit(bar_empty + 8 * stage);
@@ -1058,7 +1205,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 for (int tile = first_tile<false>(); tile < n_tiles && ok;
                      tile += tile_stride<false>()) {
                     const int mt = tile / p.n_nt;
-                    if (!tile_live<SEQ>(p, stv, mt * p.BM)) continue;
+                    if (!tile_live<SEQ, QP>(p, stv, mt * p.BM)) continue;
                     for (int it = 0; it < s.n_kb; ++it) {
                         if (!mbar_wait(bar_full + 8 * stage, phase, p.err, VDB_ERR_TIMEOUT_XFORM,
                                        abort_flag)) {
@@ -1115,12 +1262,37 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         for (int tile = first_tile<PAIR>(); tile < n_tiles; tile += tile_stride<PAIR>()) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
             const int m0 = mt * p.BM + (int)rank * kMB, n0 = nt * p.BN;
-            const bool live = tile_live<SEQ>(p, stv, mt * p.BM);
+            const bool live = tile_live<SEQ, QP>(p, stv, mt * p.BM);
             if (live) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag))
                     break;
                 tc_fence_after();
+            }
+            if constexpr (QP) {
+                for (int mb = 0; mb < NMB; ++mb) {
+                    if (mb_split && (mb & 1) != half) continue;
+                    const int m = m0 + mb * kMB + quad * 32 + lane;
+                    const uint32_t tb = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * acc_cols +
+                                        (uint32_t)(mb * p.BN);
+                    for (int c = c_lo; c < c_hi; c += 32) {
+                        uint4 res[4] = {};
+                        if (p.qp_res && m < p.M) {
+                            const uint4* rp = reinterpret_cast<const uint4*>(p.qp_res + (long long)m * 128 + c);
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) res[q] = __ldg(rp + q);
+                        }
+                        uint32_t v[32];
+                        if (live) {
+                            tmem_ld_32x32b_x32(tb + (uint32_t)c, v);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = 0u;
+                        }
+                        qpack_unit(p, stv, m, live, c >> 5, v, sbias + c, res);
+                    }
+                }
+                goto tile_done;
             }
             for (int mb = 0; mb < NMB; ++mb) {
                 if (mb_split && (mb & 1) != half) continue;
@@ -1133,6 +1305,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 else
                     epi_rows<16, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
             }
+        tile_done:
             if (live) {
                 tc_fence_before();
                 if constexpr (PAIR) {
@@ -1266,6 +1439,7 @@ struct SeqArgs {
 };
 
 int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream);
+int conv_qpack_impl(const vdb_conv_args* a, void* stream);
 
 }  // namespace
 }  // namespace vdb
@@ -1286,7 +1460,40 @@ extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
         set_error("vdb_conv: NULL args");
         return 1;
     }
+    if (a->qpack) return conv_qpack_impl(a, stream);
     return conv_impl(a, nullptr, stream);
+}
+
+extern "C" long long vdb_qpack_rows(int batch, int t, int f) {
+    return (long long)batch * (t + 2) * ((f + 2 + 3) / 4);
+}
+
+namespace vdb {
+namespace {
+// out[kt][r][ic], r = the packed row of (u, j, oc) (see qp_wrow): W[oc][kt*3 + u - j + 1][ic]
+__global__ void qpack_pack_kernel(const __half* __restrict__ w, __half* __restrict__ out) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= 3 * 384 * 32) return;
+    const int ic = e & 31, r = (e >> 5) % 384, kt = (e >> 5) / 384;
+    int u = -1;
+    for (int c = 0; c <= 4; ++c)
+        if (r >= qp_wrow(0, c)) u = c;
+    const int rr = r - qp_wrow(0, u);
+    const int j = qp_jmin(u) + rr / 32, oc = rr & 31;
+    out[e] = w[((size_t)oc * 9 + kt * 3 + (u - j + 1)) * 32 + ic];
+}
+}  // namespace
+}  // namespace vdb
+
+extern "C" int vdb_qpack_pack_weights(const void* w_taps, void* out, void* stream) {
+    if (!w_taps || !out) {
+        set_error("vdb_qpack_pack_weights: NULL argument");
+        return 1;
+    }
+    qpack_pack_kernel<<<(3 * 384 * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(w_taps), static_cast<__half*>(out));
+    VDB_CHECK_CUDA(cudaGetLastError());
+    return 0;
 }
 
 extern "C" long long vdb_seq_rows(int batch, int t, int pad) {
@@ -1915,6 +2122,144 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             set_error("vdb_conv: ksplit must be 1, 2, 4 or 8 (1 for tile_m above 256)");
             return 1;
     }
+}
+
+
+// Stage-1 conv over QPACK rows (vdb_conv_args.qpack): see the QPACK section above.
+int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
+    if (a->k0 != 3 || a->stride0 != 1 || a->ic0 != 32 || a->oc != 32 || a->x1 || a->act != 0 ||
+        a->y2 || a->ysum || a->residual2 || a->clamp_hi > 0.0f ||
+        !(a->y_phase == 0 || a->y_phase == 1) || (a->ldx0 && a->ldx0 != 128) ||
+        (a->ldy && a->ldy != 128) || (a->ldr && a->ldr != 128) || a->pair == 1 ||
+        (a->halo != 0 && a->halo != 1) || a->ksplit > 1 || a->tile_n) {
+        set_error("vdb_conv: a QPACK conv is 3x3, stride 1, 32 -> 32 channels, one segment, "
+                  "act 0, y_phase 0 or 1, an optional QPACK residual, no other options");
+        return 1;
+    }
+    if (a->batch <= 0 || a->batch > kMaxBatch || a->t_out <= 0 || a->f_out <= 0) {
+        set_error("vdb_conv: batch must be in [1, 8192] and the output non-empty");
+        return 1;
+    }
+    if (!a->x0 || !a->w0 || !a->tvalid || !a->y) {
+        set_error("vdb_conv: NULL buffer");
+        return 1;
+    }
+    auto misaligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) != 0; };
+    if (misaligned(a->x0) || misaligned(a->y) || (a->residual && misaligned(a->residual))) {
+        set_error("vdb_conv: activation pointers must be 16-byte aligned");
+        return 1;
+    }
+    const int Wq = (a->f_out + 2 + 3) / 4;
+    const long long rows = vdb_qpack_rows(a->batch, a->t_out, a->f_out);
+    if (rows > (1LL << 31) - 1024 || vdb_phase_rows(a->batch, a->t_out, a->f_out) > (1LL << 31) - 1024) {
+        set_error("vdb_conv: tensor too large (more than 2^31 rows); split the batch");
+        return 1;
+    }
+    int BM = a->tile_m ? a->tile_m : 256;
+    if (BM != 128 && BM != 256) {
+        set_error("vdb_conv: a QPACK conv takes tile_m 0, 128 or 256");
+        return 1;
+    }
+    ConvDev p{};
+    p.M = (int)rows;
+    p.n_nt = 1;
+    p.BN = 128;  // 4 pixel phases x 32 output channels
+    p.n_seg = 1;
+    SegDev& s = p.seg[0];
+    s.mode = SEG_HALO;
+    s.ic = 128;
+    s.kb = 64;
+    s.n_kb = 2;
+    s.n_taps = 9;
+    const int H = BM + 2 * Wq + 2;
+    s.halo_back = Wq + 1;
+    s.n_box = (H + 255) / 256;
+    s.box_rows = round_up((H + s.n_box - 1) / s.n_box, 8);
+    s.halo_planes = 1;
+    s.halo_mode = 0;
+    s.plane_bytes = 0;
+    s.bytes = (uint32_t)s.n_box * s.box_rows * 128u;
+    s.bres = 0;
+    p.bres_bytes = 1152u * 64u;  // 3 x 384 rows of 32 channels
+    uint32_t off = p.bres_bytes;   // 72 KB: 1024-byte aligned
+    p.stage0 = off;
+    p.a_region = (uint32_t)round_up((int)s.bytes, 1024);
+    p.stage_bytes = p.a_region;
+    const uint32_t tail = (uint32_t)round_up(128 * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
+                          8 * (3 * kMaxStages + 5) + 16;
+    const int budget = kSmemMax - 1024 - (int)off - (int)tail;
+    p.n_stages = (uint32_t)std::min<int>(kMaxStages, budget / (int)p.stage_bytes);
+    if (p.n_stages < 2) {
+        set_error("vdb_conv: QPACK tile does not fit in shared memory");
+        return 1;
+    }
+    off += p.n_stages * p.stage_bytes;
+    p.bias_off = off;
+    off += (uint32_t)round_up(128 * 4, 16);
+    p.tv_off = off;
+    off += (uint32_t)round_up(a->batch * 4, 16);
+    p.ss_off = 0;
+    p.bar_off = (uint32_t)round_up((int)off, 8);
+    off = p.bar_off + 8 * (3 * p.n_stages + 5) + 16;
+    const size_t smem = (size_t)off + 1024;
+    p.BM = BM;
+    p.n_mblk = BM / kMB;
+    p.J = 1;
+    p.n_acc = 2;
+    p.n_iss = p.n_mblk >= 2 ? 2 : 1;
+    p.n_mt = (p.M + BM - 1) / BM;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(p.n_acc * p.n_mblk * 128)) cols <<= 1;
+    p.tmem_cols = cols;
+    p.bias = a->bias;
+    p.relu = a->relu;
+    p.y = static_cast<__half*>(a->y);
+    p.ldy = 128;
+    p.act = 0;
+    p.y_phase = a->y_phase;
+    p.Hp = a->t_out + 2;
+    p.Wp = Wq;
+    magic_div((uint32_t)p.Hp * (uint32_t)Wq, p.img_mul, p.img_sh);
+    magic_div((uint32_t)Wq, p.wp_mul, p.wp_sh);
+    p.T = a->t_out;
+    p.F = a->f_out;
+    p.Hq = (a->t_out - 1) / 2 + 1 + 2;  // PHASE output: the stride-2 consumer's grid
+    p.Wq = (a->f_out - 1) / 2 + 1 + 2;
+    p.plane_rows = (long long)a->batch * p.Hq * p.Wq;
+    p.tvalid = a->tvalid;
+    p.batch = a->batch;
+    p.oc = 128;
+    p.err = a->err;
+    p.qp_res = static_cast<const __half*>(a->residual);
+    CUtensorMap tm[4];
+    if (!make_map_a(&tm[0], a->x0, 128, 128, rows, 1, 64, s.box_rows) ||
+        !make_map_b(&tm[1], a->w0, 32, 1152, 128, 32)) {
+        set_error("vdb_conv: cuTensorMapEncodeTiled failed");
+        return 1;
+    }
+    tm[2] = tm[0];
+    tm[3] = tm[1];
+    const size_t smem_launch = std::max<size_t>(smem, 120 * 1024);
+    const int grid = std::max(1, std::min(p.n_mt, num_sms()));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    auto kern = p.n_mblk == 2 ? conv_tc_kernel<2, 1, false, false, true, true>
+                              : conv_tc_kernel<1, 1, false, false, true, true>;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    VDB_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs == cudaStreamCaptureStatusNone)
+        VDB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_launch;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
+    return 0;
 }
 
 }  // namespace

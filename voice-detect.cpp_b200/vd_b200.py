@@ -45,7 +45,7 @@ class ConvArgs(C.Structure):
         ("ksplit", C.c_int), ("ldx0", C.c_int), ("ldx1", C.c_int), ("ldy", C.c_int),
         ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
         ("act", C.c_int), ("ysum", C.c_void_p), ("ldsum", C.c_int), ("addend", C.c_void_p),
-        ("ldaddend", C.c_int), ("y_pad", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int),
+        ("ldaddend", C.c_int), ("y_pad", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int), ("qpack", C.c_int),
     ]
 
 
@@ -145,6 +145,10 @@ def lib() -> C.CDLL:
                                                            C.POINTER(C.POINTER(C.c_float)),
                                                            C.POINTER(C.c_int)]
         L.voicedetect_b200_audio_error.restype = C.c_char_p
+        L.vdb_qpack_rows.restype = C.c_longlong
+        L.vdb_qpack_rows.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.vdb_qpack_pack_weights.restype = C.c_int
+        L.vdb_qpack_pack_weights.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
         L.vdb_resampled_length.restype = C.c_longlong
         L.vdb_resampled_length.argtypes = [C.c_longlong, C.c_int, C.c_int]
         L.vdb_pcm_ingest.restype = C.c_int
@@ -377,6 +381,47 @@ def from_grid(g, B: int, C_: int, F: int, T: int):
     return x.permute(0, 3, 2, 1).float().contiguous()
 
 
+def qpack_width(F: int) -> int:
+    """QPACK rows per time step: ceil((F + 2) / 4)."""
+    return (F + 2 + 3) // 4
+
+
+def to_qpack(x, tvalid=None):
+    """(B, 32, F, T) -> QPACK f16 tensor (B*(T+2)*Wq, 128): four padded frequency
+    pixels per row (include/vdb_ops.h, vdb_qpack_rows)."""
+    import torch
+    B, Cc, F, T = x.shape
+    assert Cc == 32
+    Wq = qpack_width(F)
+    g = torch.zeros(B, T + 2, 4 * Wq, Cc, dtype=torch.float16, device=x.device)
+    g[:, 1:T + 1, 1:F + 1, :] = x.permute(0, 3, 2, 1).to(torch.float16)
+    if tvalid is not None:
+        for b, tv in enumerate(tvalid):
+            g[b, 1 + int(tv):, :, :] = 0
+    return g.reshape(B * (T + 2) * Wq, 4 * Cc).contiguous()
+
+
+def from_qpack(q, B: int, F: int, T: int, interior: bool = True):
+    """QPACK (rows, 128) -> (B, 32, F, T) float32 (valid interior), or with
+    interior=False the whole padded (B, 32, 4*Wq, T+2) grid."""
+    Wq = qpack_width(F)
+    g = q.reshape(B, T + 2, 4 * Wq, 32)
+    if interior:
+        g = g[:, 1:T + 1, 1:F + 1, :]
+    return g.permute(0, 3, 2, 1).float().contiguous()
+
+
+def qpack_weights(w_taps):
+    """f16 [32][9][32] conv weight (pack_conv_weight) -> the packed [1152][32] weight of
+    a QPACK conv (vdb_qpack_pack_weights, on the device)."""
+    import torch
+    out = torch.empty(1152, 32, dtype=torch.float16, device=w_taps.device)
+    s = torch.cuda.current_stream().cuda_stream
+    _check(lib().vdb_qpack_pack_weights(w_taps.contiguous().data_ptr(), out.data_ptr(),
+                                        C.c_void_p(s)), "vdb_qpack_pack_weights")
+    return out
+
+
 def to_phase(x, tvalid=None):
     """(B, C, F, T) -> PHASE f16 tensor (4*B*(To+2)*(Fo+2), C) for a stride-2 consumer."""
     import torch
@@ -485,7 +530,8 @@ def _ptr(t):
 def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=None,
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
          y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
-         y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0, tile_n=0, pair=0):
+         y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0, tile_n=0, pair=0,
+         qpack=False):
     """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
     tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
     the row pitch is taken from the view's stride); y2 is an extra PHASE output,
@@ -497,6 +543,10 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
     y_phase 3: a TPHASE output for a time-stride-2 1-D consumer with y_pad padding
     rows, shaped (2*B*(To+2*y_pad), f_out*oc)."""
     import torch
+    if y is None and qpack:
+        y = torch.empty(lib().vdb_phase_rows(batch, t_out, f_out) if y_phase
+                        else lib().vdb_qpack_rows(batch, t_out, f_out), 32 if y_phase else 128,
+                        dtype=torch.float16, device=x0.device)
     if y is None:
         yp = int(y_phase)
         if yp == 3:
@@ -508,7 +558,7 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                     else 2 * batch * (t_out + 2) * (out_extent(f_out, 2) + 2) if yp == 2
                     else lib().vdb_grid_rows(batch, t_out, f_out))
             y = torch.empty(rows, oc, dtype=torch.float16, device=x0.device)
-    ldy = 0 if int(y_phase) == 3 else _ld(y)
+    ldy = 0 if (int(y_phase) == 3 or qpack) else _ld(y)
     a = ConvArgs(batch=batch, t_out=t_out, f_out=f_out, oc=oc, k0=k0, stride0=stride0,
                  ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(),
                  w0=w0.data_ptr(), stride1=stride1,
@@ -520,7 +570,7 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
                  ldr2=_ld(residual2), act=int(act), ysum=_ptr(ysum), ldsum=_ld(ysum),
                  addend=_ptr(addend), ldaddend=_ld(addend), y_pad=int(y_pad),
-                 tile_n=int(tile_n), pair=int(pair))
+                 tile_n=int(tile_n), pair=int(pair), qpack=int(bool(qpack)))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
