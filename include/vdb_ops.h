@@ -277,6 +277,13 @@ int vdb_cmn_stem(const float* feats, const int* frames, int batch, int t_max, in
                  int cmn, const float* stem_w, const float* stem_b, int oc,
                  float* mean_scratch, void* y, void* stream);
 
+/* vdb_cmn_stem with 32 stem channels and the output in the QPACK layout
+ * QP(batch, t_max, n_mels) (vdb_qpack_rows x 128 channels): the input of the QPACK
+ * stage-1 convs. Same arithmetic, so the values equal vdb_cmn_stem's. */
+int vdb_cmn_stem_qpack(const float* feats, const int* frames, int batch, int t_max, int n_mels,
+                       int cmn, const float* stem_w, const float* stem_b, float* mean_scratch,
+                       void* y, void* stream);
+
 /* The same CMN + stem as vdb_cmn_stem, for callers that cannot allocate device
  * memory: no counterpart exists in the reference. A streaming audio callback must
  * not call cudaMalloc/cudaFree (they can stall the whole device for an unbounded

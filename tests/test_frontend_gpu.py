@@ -120,3 +120,30 @@ def test_pool_embed_matches_oracle(cuda_lib, B, T, F, Cc, D):
         assert np.linalg.norm(p - e) / np.linalg.norm(e) <= 1e-4
         en = e / np.linalg.norm(e)
         assert float(np.dot(emb[i].cpu().numpy(), en)) >= 0.9999
+
+
+def test_cmn_stem_qpack_equals_grid(cuda_lib):
+    """vdb_cmn_stem_qpack (the QPACK input of the stage-1 convs) holds exactly the
+    values vdb_cmn_stem writes in the GRID layout, and zeros in every other slot
+    (borders, frames past each clip, the pixels past the padded grid)."""
+    import torch
+    L = cuda_lib.lib()
+    rng = np.random.default_rng(17)
+    B, t_max, M, OC = 4, 29, 80, 32
+    frames = [29, 11, 1, 20]
+    feats = torch.from_numpy(rng.standard_normal((B, t_max, M)).astype(np.float32) * 3 + 1).cuda()
+    fr = torch.tensor(frames, dtype=torch.int32, device="cuda")
+    w = torch.from_numpy((rng.standard_normal((OC, 9)) * 0.4).astype(np.float32)).cuda()
+    b = torch.from_numpy((rng.standard_normal(OC) * 0.1).astype(np.float32)).cuda()
+    mean = torch.empty(B, M, device="cuda")
+    yg = torch.full((L.vdb_grid_rows(B, t_max, M), OC), 3.0, dtype=torch.float16, device="cuda")
+    yq = torch.full((L.vdb_qpack_rows(B, t_max, M), 128), 3.0, dtype=torch.float16, device="cuda")
+    assert L.vdb_cmn_stem(feats.data_ptr(), fr.data_ptr(), B, t_max, M, 1, w.data_ptr(),
+                          b.data_ptr(), OC, mean.data_ptr(), yg.data_ptr(), None) == 0
+    assert L.vdb_cmn_stem_qpack(feats.data_ptr(), fr.data_ptr(), B, t_max, M, 1, w.data_ptr(),
+                                b.data_ptr(), mean.data_ptr(), yq.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    g = yg.reshape(B, t_max + 2, M + 2, OC).permute(0, 3, 2, 1).cpu()  # (B, C, F+2, T+2)
+    q = cuda_lib.from_qpack(yq, B, M, t_max, interior=False).cpu()     # (B, C, 4Wq, T+2)
+    assert torch.equal(q[:, :, :M + 2], g)
+    assert torch.all(q[:, :, M + 2:] == 0)

@@ -95,6 +95,26 @@ std::vector<float> pack_taps(const std::vector<float>& w, int oc, int ic, int k)
     return out;
 }
 
+// The QPACK weight of a stage-1 conv from its packed taps ([32][9][32], tap kt*3 + kf):
+// for time tap kt and input pixel shift u = -1..4, the rows (j, oc) of the output pixel
+// phases j with 0 <= u - j + 1 <= 2 (blocks of 32 / 64 / 96 / 96 / 64 / 32 rows, 384
+// per kt) hold W[oc][kt*3 + u - j + 1][:] (the layout vdb_qpack_pack_weights writes).
+std::vector<float> pack_qpack(const std::vector<float>& taps) {
+    std::vector<float> out((size_t)1152 * 32, 0.0f);
+    for (int kt = 0; kt < 3; ++kt) {
+        int row = kt * 384;
+        for (int u = -1; u <= 4; ++u) {
+            const int jmin = std::max(0, u - 1), jmax = std::min(3, u + 1);
+            for (int j = jmin; j <= jmax; ++j)
+                for (int oc = 0; oc < 32; ++oc, ++row)
+                    for (int ic = 0; ic < 32; ++ic)
+                        out[(size_t)row * 32 + ic] =
+                            taps[((size_t)oc * 9 + kt * 3 + (u - j + 1)) * 32 + ic];
+        }
+    }
+    return out;
+}
+
 inline int frames_of(int n, int win, int hop) { return n >= win ? 1 + (n - win) / hop : 0; }
 inline int half_extent(int n) { return (n - 1) / 2 + 1; }
 
@@ -325,9 +345,13 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
             err = "block channels must be multiples of 16";
             return nullptr;
         }
-        if (!upload_h(pack_taps(w1, oc, ic, 3), &blk.w1) || !upload(b1, &blk.b1) ||
-            !upload_h(pack_taps(w2, oc, oc, 3), &blk.w2) || !upload(b2, &blk.b2))
+        const std::vector<float> t1 = pack_taps(w1, oc, ic, 3), t2 = pack_taps(w2, oc, oc, 3);
+        if (!upload_h(t1, &blk.w1) || !upload(b1, &blk.b1) || !upload_h(t2, &blk.w2) ||
+            !upload(b2, &blk.b2))
             return nullptr;
+        if (ic == 32 && oc == 32 && blk.stride == 1 && blk.identity)
+            if (!upload_h(pack_qpack(t1), &blk.w1q) || !upload_h(pack_qpack(t2), &blk.w2q))
+                return nullptr;
         e->blocks_.push_back(blk);
         if (blk.stride == 2) F = half_extent(F);
         cin = oc;
@@ -360,6 +384,15 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
             if (!L.vec(mvn, mv, D) || !upload(mv, &e->mean_vec_)) return nullptr;
         }
         e->var_eps_ = g.f32(pre + "var_eps", 1e-8f);
+    }
+    // QPACK stage 1: every block before the first stride-2 one packed (32 -> 32,
+    // identity), 32 stem channels, and a stride-2 block after them
+    {
+        size_t i = 0;
+        bool ok = e->stem_oc_ == 32;
+        for (; i < e->blocks_.size() && e->blocks_[i].stride == 1; ++i)
+            ok = ok && e->blocks_[i].w1q != nullptr;
+        e->qpack_ = ok && i > 0 && i < e->blocks_.size();
     }
     // workspace levels: channels of the activation kept at each resolution level
     e->levels_.clear();
@@ -809,7 +842,9 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
     int T = t_max, F = cfg_.n_mels;
     for (size_t li = 0; li < levels_.size(); ++li) {
         Level& L = levels_[li];
-        const size_t g = (size_t)vdb_grid_rows(B, T, F) * L.c * sizeof(__half);
+        size_t g = (size_t)vdb_grid_rows(B, T, F) * L.c * sizeof(__half);
+        if (li == 0 && qpack_)  // QPACK rows of 4 pixels x 32 channels
+            g = std::max(g, (size_t)vdb_qpack_rows(B, T, F) * 128 * sizeof(__half));
         size_t have = L.g_bytes;
         for (int k = 0; k < 3; ++k) {
             size_t h = have;
@@ -992,8 +1027,9 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
     if (cfg_.arch == "campplus") return run_campplus(B, t_max, tv_sum, st, d_out, launches, err);
     const int ps = prof_begin(st, 4);
     const bool eres = cfg_.arch == "eres2net";
-    if (vdb_cmn_stem(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
-                     stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0], st)) {
+    if (cmn_stem_launch(feats_, meta_, B, t_max, cfg_.n_mels, cfg_.cmn ? 1 : 0, stem_w_, stem_b_,
+                        stem_oc_, mean_, eres ? ebufs_[e_stem_buf_].p : levels_[0].g[0],
+                        (!eres && qpack_) ? 2 : 0, st)) {
         err = vdb_last_error();
         return 1;
     }
@@ -1019,6 +1055,8 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         const int* tv_out = meta_ + (size_t)lev_out * B;
         const int h_slot = (lev_out == lev) ? (cur + 1) % 3 : 0;
         const int o_slot = (lev_out == lev) ? (cur + 2) % 3 : 1;
+        // stage-1 blocks over QPACK rows (lev 0, identity shortcut as the epilogue residual)
+        const bool qp = qpack_ && lev == 0 && blk.stride == 1;
         vdb_conv_args a{};
         a.batch = B;
         a.t_out = To;
@@ -1028,12 +1066,13 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         a.stride0 = blk.stride;
         a.ic0 = blk.ic;
         a.x0 = x;
-        a.w0 = blk.w1;
+        a.w0 = qp ? blk.w1q : blk.w1;
         a.bias = blk.b1;
         a.relu = 1;
         a.tvalid = tv_out;
         a.y = Lo.g[h_slot];
         a.err = errword_;
+        a.qpack = qp ? 1 : 0;
         // algorithmic FLOPs over valid output frames only (padding excluded)
         const double valid_px = (double)Fo * (double)tv_sum[lev_out];
         int pe = prof_begin(st);
@@ -1051,16 +1090,23 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         c2.stride0 = 1;
         c2.ic0 = blk.oc;
         c2.x0 = Lo.g[h_slot];
-        c2.w0 = blk.w2;
+        c2.w0 = qp ? blk.w2q : blk.w2;
         c2.bias = blk.b2;
         c2.relu = 1;
         c2.tvalid = tv_out;
         c2.err = errword_;
-        // 1x1 downsample, or the identity shortcut, as input segment 1
-        c2.x1 = x;
-        c2.w1 = blk.wd;
-        c2.ic1 = blk.ic;
-        c2.stride1 = blk.stride;
+        if (qp) {
+            // QPACK: the identity shortcut is the epilogue residual (the block input's
+            // QPACK row is contiguous with the output row)
+            c2.qpack = 1;
+            c2.residual = x;
+        } else {
+            // 1x1 downsample, or the identity shortcut, as input segment 1
+            c2.x1 = x;
+            c2.w1 = blk.wd;
+            c2.ic1 = blk.ic;
+            c2.stride1 = blk.stride;
+        }
         c2.y_phase = next_s2 ? 1 : 0;
         c2.y = next_s2 ? Lo.p : Lo.g[o_slot];
         pe = prof_begin(st);

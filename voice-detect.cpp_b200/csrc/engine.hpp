@@ -40,6 +40,10 @@ struct ResBlockDev {
     float* b2 = nullptr;    // conv2 bias (+ downsample bias when fused)
     __half* wd = nullptr;   // [oc][ic], or the [oc][oc] identity for an identity shortcut
     bool identity = false;
+    // stage-1 blocks run over the QPACK layout: conv1 / conv2 weights packed for it
+    // (vdb_qpack_pack_weights, [3][384][32])
+    __half* w1q = nullptr;
+    __half* w2q = nullptr;
 };
 
 // ERes2Net runs from a plan compiled once at load from the conv manifest
@@ -235,6 +239,11 @@ private:
     vdb_fbank_plan* plan_ = nullptr;
     // weights
     int stem_oc_ = 0;
+    // ResNet stage 1 (every block before the first stride-2 one: 32 -> 32 with identity
+    // shortcuts, 32 stem channels) runs over QPACK rows: the stem writes QPACK, its convs
+    // take the (time tap, pixel shift) schedule and the last one writes the PHASE input
+    // of the first stride-2 block.
+    bool qpack_ = false;
     float* stem_w_ = nullptr;   // [oc][9], tap kt*3 + kf
     float* stem_b_ = nullptr;
     std::vector<ResBlockDev> blocks_;

@@ -92,10 +92,13 @@ stem_kernel(const float* __restrict__ feats, const int* __restrict__ frames,
 #pragma unroll
     for (int o = 0; o < 8; ++o) br[o] = __ldg(bias + g * 8 + o);
     __syncthreads();
-    const int rows = min(kStemRows, Hp - tp0) * Wp;
+    // QPACK (fphase 2) rows carry 4 * Wq pixels: the ones past the padded grid are 0
+    const int Wq4 = 4 * ((n_mels + 2 + 3) / 4);
+    const int Wx = fphase == 2 ? Wq4 : Wp;  // pixels stored per time row
+    const int rows = min(kStemRows, Hp - tp0) * Wx;
     uint4* yb = reinterpret_cast<uint4*>(y) + ((long long)b * Hp + tp0) * Wp * G;
     for (int q = pl; q < rows; q += PPB) {
-        const int r = q / Wp, fp = q - r * Wp;
+        const int r = q / Wx, fp = q - r * Wx;
         const int tp = tp0 + r;
         float acc[8];
 #pragma unroll
@@ -130,7 +133,12 @@ stem_kernel(const float* __restrict__ feats, const int* __restrict__ frames,
         v.y = *reinterpret_cast<uint32_t*>(&h1);
         v.z = *reinterpret_cast<uint32_t*>(&h2);
         v.w = *reinterpret_cast<uint32_t*>(&h3);
-        if (fphase) {
+        if (fphase == 2) {
+            // QPACK output (vdb_ops.h): pixel fp of time row tp is channels
+            // (fp & 3) * OC .. of QPACK row (b * Hp + tp) * Wq + fp / 4
+            const long long row = ((long long)b * Hp + tp) * (Wq4 / 4) + (fp >> 2);
+            reinterpret_cast<uint4*>(y)[(row * 4 + (fp & 3)) * G + g] = v;
+        } else if (fphase) {
             // FPHASE output for a frequency-stride-2 consumer (vdb_ops.h)
             const int Wq = (n_mels - 1) / 2 + 1 + 2;
             const long long dst = (long long)(fp & 1) * batch * Hp * Wq +
@@ -423,11 +431,22 @@ extern "C" int vdb_cmn_stem(const float* feats, const int* frames, int batch, in
                                 mean_scratch, y, 0, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int vdb_cmn_stem_qpack(const float* feats, const int* frames, int batch, int t_max,
+                                  int n_mels, int cmn, const float* stem_w, const float* stem_b,
+                                  float* mean_scratch, void* y, void* stream) {
+    return vdb::cmn_stem_launch(feats, frames, batch, t_max, n_mels, cmn, stem_w, stem_b, 32,
+                                mean_scratch, y, 2, static_cast<cudaStream_t>(stream));
+}
+
 int vdb::cmn_stem_launch(const float* feats, const int* frames, int batch, int t_max,
                          int n_mels, int cmn, const float* stem_w, const float* stem_b, int oc,
                          float* mean_scratch, void* y, int fphase, cudaStream_t stream) {
     if (!feats || !frames || !stem_w || !stem_b || !y || (cmn && !mean_scratch)) {
         set_error("vdb_cmn_stem: NULL argument");
+        return 1;
+    }
+    if (fphase == 2 && oc != 32) {
+        set_error("vdb_cmn_stem: the QPACK output needs 32 stem channels");
         return 1;
     }
     if (batch <= 0 || batch > 65535 || t_max <= 0 || t_max > (1 << 22) || n_mels <= 0 ||

@@ -46,8 +46,9 @@ int fc_embed_launch(const float* pooled, int batch, int P, const float* seg_w,
                     const int* out_rows, float* emb_out, float* prenorm_out, float* part,
                     cudaStream_t stream);
 
-// CMN + stem of vdb_cmn_stem with the output in GRID (fphase 0) or FPHASE (fphase 1,
-// for a frequency-stride-2 consumer: CAM++'s FCM) layout.
+// CMN + stem of vdb_cmn_stem with the output in GRID (fphase 0), FPHASE (fphase 1,
+// for a frequency-stride-2 consumer: CAM++'s FCM) or QPACK (fphase 2, oc 32: the
+// ResNet stage-1 convs) layout.
 int cmn_stem_launch(const float* feats, const int* frames, int batch, int t_max, int n_mels,
                     int cmn, const float* stem_w, const float* stem_b, int oc,
                     float* mean_scratch, void* y, int fphase, cudaStream_t stream);

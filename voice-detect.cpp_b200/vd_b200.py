@@ -93,6 +93,10 @@ def lib() -> C.CDLL:
         L.vdb_cmn_stem.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                    C.c_void_p]
+        L.vdb_cmn_stem_qpack.restype = C.c_int
+        L.vdb_cmn_stem_qpack.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                         C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p]
         L.vdb_cmn_stem_noalloc.restype = C.c_int
         L.vdb_cmn_stem_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                            C.c_int, C.c_void_p, C.c_void_p, C.c_int,
