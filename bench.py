@@ -99,6 +99,89 @@ def lpt_shard(lengths: np.ndarray, world: int) -> list[list[int]]:
     return shards
 
 
+# Seconds a rank waits for its peers: the bound of rank_checkpoint's host-side
+# exchange and the process group's collective timeout. Under NCCL, torch's watchdog
+# aborts a collective that exceeds it and ends the process (asynchronous error
+# handling), so a rank never blocks for longer than this on a peer that died.
+PG_TIMEOUT_S = float(os.environ.get("VDB_PG_TIMEOUT_S", "120"))
+
+
+class RankFailure(RuntimeError):
+    """A peer rank failed, or did not report, before a collective phase."""
+
+
+def _store():
+    import torch.distributed as dist
+    return dist.distributed_c10d._get_default_store()
+
+
+def init_ranks(backend: str, local: int | None = None, timeout_s: float | None = None):
+    """One process per GPU (or gloo rank): the default group with a short timeout."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    kw = {"timeout": timedelta(seconds=PG_TIMEOUT_S if timeout_s is None else timeout_s)}
+    if backend == "nccl":
+        kw["device_id"] = torch.device("cuda", local)
+    dist.init_process_group(backend, **kw)
+
+
+def report_rank_error(exc: BaseException) -> None:
+    """Publishes this rank's failure in the group's store, so that peers waiting in
+    rank_checkpoint stop at once instead of at their timeout. Best effort: the store
+    may already be gone."""
+    import torch.distributed as dist
+    try:
+        if not dist.is_initialized() or dist.get_world_size() == 1:
+            return
+        msg = f"{type(exc).__name__}: {exc}"[:400]
+        _store().set(f"vdb/err/{dist.get_rank()}", msg)
+    except Exception:
+        pass
+
+
+def rank_checkpoint(tag: str, timeout_s: float | None = None, poll_s: float = 0.02) -> None:
+    """Host-side readiness exchange before a phase's first collective. Every rank
+    publishes that it reached `tag` and waits, bounded by `timeout_s`, for all its
+    peers. A peer that published a failure (report_rank_error) raises RankFailure
+    naming it on every waiting rank at once; one that never reports (it exited or
+    hangs) raises after the timeout; an unreachable store (the rank hosting it is
+    gone) raises immediately. No rank therefore enters a collective that a failed
+    peer would leave hanging. `tag` must be unique within the job."""
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return
+    timeout_s = PG_TIMEOUT_S if timeout_s is None else timeout_s
+    world, me = dist.get_world_size(), dist.get_rank()
+    st = _store()
+    try:
+        st.set(f"vdb/{tag}/{me}", "ok")
+    except Exception as e:
+        raise RankFailure(f"rank {me}: store unreachable at '{tag}' ({e})") from e
+    pending = [r for r in range(world) if r != me]
+    deadline = time.monotonic() + timeout_s
+    while True:
+        left = []
+        for r in pending:
+            try:
+                if st.check([f"vdb/err/{r}"]):
+                    why = st.get(f"vdb/err/{r}").decode(errors="replace")
+                    raise RankFailure(f"rank {r} failed before '{tag}': {why}")
+                if not st.check([f"vdb/{tag}/{r}"]):
+                    left.append(r)
+            except RankFailure:
+                raise
+            except Exception as e:
+                raise RankFailure(f"rank {me}: store unreachable at '{tag}' while waiting "
+                                  f"for rank {r} ({e})") from e
+        if not left:
+            return
+        if time.monotonic() > deadline:
+            raise RankFailure(f"rank(s) {left} did not reach '{tag}' within {timeout_s:g} s")
+        pending = left
+        time.sleep(poll_s)
+
+
 def gather_embeddings(local, gathered, world: int) -> None:
     """The path's only collective: every rank's [n_max, D] embeddings into
     `gathered` [world * n_max, D], rank-major (NCCL on GPUs, gloo on CPU)."""
@@ -318,6 +401,7 @@ def bench_parity(m: dict, host_pcm, offs, lens, d_out, rank: int, world: int, de
         want = ref(host_pcm[offs[i]:offs[i] + lens[i]]).astype(np.float64)
         g = got[i].astype(np.float64)
         coss.append(float(g @ want / (np.linalg.norm(g) * np.linalg.norm(want))))
+    rank_checkpoint("parity")
     t = torch.tensor([min(coss)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
@@ -334,9 +418,7 @@ def run_b200(args) -> int:
     world, rank, local = dist_env()
     if world > 1:
         torch.cuda.set_device(local)
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        init_ranks("nccl", local)
     else:
         torch.cuda.set_device(0)
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -376,6 +458,7 @@ def run_b200(args) -> int:
         model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
         gather_embeddings(d_out, gathered, world)
 
+    rank_checkpoint("setup")  # before the first all-gather
     for _ in range(args.warmup):
         step()
     model.sync()
@@ -682,16 +765,10 @@ def run_eres2net(args, family: str = "eres2net") -> int:
     import vd_b200
 
     world, rank, local = dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    dev = torch.device("cuda", local if world > 1 else 0)
     fam = _Family(family, args)
     if args.impl == "reference":
+        # the reference's CPU path on rank 0 alone; other ranks exit without work
+        # and no process group is formed (nothing is exchanged)
         if rank == 0:
             m = fam.weights_as_loaded(fam.model())
             pool = make_pool(max(4, fam.ref_clips), float(fam.seconds))
@@ -713,10 +790,14 @@ def run_eres2net(args, family: str = "eres2net") -> int:
                                  "kind": kind, "sample": sample},
                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}), flush=True)
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
         return 0
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        init_ranks("nccl", local)
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local if world > 1 else 0)
 
     tmp = tempfile.mkdtemp(prefix="vdbench_")
     m = fam.model()
@@ -739,6 +820,7 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
         gather_embeddings(d_out, gathered, world)
 
+    rank_checkpoint("setup")  # before the first all-gather
     for _ in range(args.warmup):
         step()
     model.sync()
@@ -952,6 +1034,14 @@ def main() -> int:
                     help="CAM++ (reference topology) f16, batch of 4 s clips")
     ap.add_argument("--campplus-batch", type=int, default=512)
     args = ap.parse_args()
+    try:
+        return _dispatch(args)
+    except BaseException as e:
+        report_rank_error(e)  # peers waiting in rank_checkpoint stop at once
+        raise
+
+
+def _dispatch(args) -> int:
     if args.op_sweep:
         return run_sweep(args)
     if args.eres2net:

@@ -128,6 +128,13 @@ int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx);
 /* Synchronise the context's stream and report any kernel-side timeout. */
 int voicedetect_b200_sync(voicedetect_ctx* ctx);
 
+/* Synchronise, then drop the context's captured CUDA graphs and free its workspace on
+ * every device it uses (weights stay resident). The next embed call re-allocates
+ * and re-captures; its results are bit-identical to those before the release.
+ * No reference counterpart (the reference frees everything only in
+ * voicedetect_capi_free). */
+int voicedetect_b200_release_cache(voicedetect_ctx* ctx);
+
 /* Conv-kernel profiling: while enabled, every tensor-core conv launch is bracketed
  * by CUDA events on its own stream. profile_read synchronises and returns, since
  * the previous read, the summed launch durations (ms), the algorithmic conv FLOPs

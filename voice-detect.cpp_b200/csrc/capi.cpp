@@ -551,6 +551,24 @@ extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
     return 0;
 }
 
+extern "C" int voicedetect_b200_release_cache(voicedetect_ctx* ctx) {
+    if (!ctx || !ctx->engine) return 1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceRestore keep_device;
+    std::string err;
+    auto drop = [&](vdb::Engine& e) -> bool {
+        if (cudaSetDevice(e.device()) != cudaSuccess) {
+            err = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+            return false;
+        }
+        return e.release_cache(err) == 0;
+    };
+    bool ok = drop(*ctx->engine);
+    for (auto& e : ctx->extra) ok = drop(*e) && ok;
+    if (!ok) ctx->last_error = err;
+    return ok ? 0 : 1;
+}
+
 namespace {
 thread_local std::string g_audio_error;
 }

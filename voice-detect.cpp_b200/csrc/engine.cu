@@ -1006,6 +1006,16 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     return 0;
 }
 
+int Engine::release_cache(std::string& err) {
+    if (cudaStreamSynchronize(stream_) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        err = std::string("CUDA error: ") + cudaGetErrorString(cudaGetLastError());
+        return 1;
+    }
+    clear_graphs();
+    free_workspace();
+    return 0;
+}
+
 void Engine::clear_graphs() {
     for (GraphEntry& g : graphs_)
         if (g.exec) cudaGraphExecDestroy(g.exec);

@@ -181,6 +181,11 @@ public:
     // Reads and clears the device error word (kernel timeouts). Synchronises.
     int check_device_error(std::string& err);
 
+    // Synchronises, then drops every captured CUDA graph and frees the workspace
+    // (activations, staging and ring buffers); weights stay resident. The next embed
+    // call re-allocates and re-captures, producing identical results.
+    int release_cache(std::string& err);
+
     // Bucketing policy.
     int max_clips = 512;
     long long max_frames = 262144;

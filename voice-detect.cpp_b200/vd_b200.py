@@ -177,6 +177,8 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_embedding_dim.argtypes = [C.c_void_p]
         L.voicedetect_b200_sync.restype = C.c_int
         L.voicedetect_b200_sync.argtypes = [C.c_void_p]
+        L.voicedetect_b200_release_cache.restype = C.c_int
+        L.voicedetect_b200_release_cache.argtypes = [C.c_void_p]
         L.voicedetect_b200_profile.restype = C.c_int
         L.voicedetect_b200_profile.argtypes = [C.c_void_p, C.c_int]
         L.voicedetect_b200_profile_read.restype = C.c_int
@@ -329,6 +331,11 @@ class Model:
 
     def sync(self) -> None:
         if self._L.voicedetect_b200_sync(self.ctx) != 0:
+            raise VoiceDetectError(self.last_error())
+
+    def release_cache(self) -> None:
+        """Drops the captured CUDA graphs and the workspace (weights stay resident)."""
+        if self._L.voicedetect_b200_release_cache(self.ctx) != 0:
             raise VoiceDetectError(self.last_error())
 
     def profile(self, enable: bool) -> None:
