@@ -43,6 +43,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "sm100_ptx.cuh"
@@ -58,6 +59,15 @@ constexpr int kEpiWarp0 = 4;
 constexpr int kEpiThreads = 256;
 constexpr int kMaxStages = 8;
 constexpr int kSmemMax = 232448;   // 227 KB opt-in dynamic shared memory
+// staged output: two 2 KB boxes per epilogue warp
+constexpr uint32_t kOstageBytes = 8u * 2u * 2048u;
+
+// Output store policy (VDB_CONV_TMA_STORE): 0 direct row stores only; 1 staged TMA box
+// stores wherever they fit; unset or 2 staged where they leave enough pipeline slots.
+int conv_tma_store_mode() {
+    const char* e = std::getenv("VDB_CONV_TMA_STORE");
+    return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : 2;
+}
 constexpr int kMaxBatch = 8192;
 
 // SEG_TAP: one A tile and one weight tile per (tap, channel block).
@@ -147,6 +157,11 @@ struct ConvDev {
     // then the row count per time step (Wq = ceil((F + 2) / 4)) and qp_res the optional
     // QPACK residual added in the epilogue (the BasicBlock identity shortcut).
     const __half* qp_res;
+    // Output through TMA stores (GRID / QPACK y, no other output): each epilogue warp
+    // stages its 32 rows x 32 columns in one of two 2 KB buffers at ostage_off (64-byte
+    // swizzle) and one lane stores the box through the output map; 0 = the threads
+    // store their rows directly
+    uint32_t ostage_off;
 };
 
 // Division by a runtime-invariant divisor d (Granlund & Montgomery, "Division by
@@ -251,6 +266,27 @@ __device__ __forceinline__ void load_res(const __half* rrow, uint4 (&r)[NC / 8])
     for (int j = 0; j < NC / 8; ++j) r[j] = __ldg(reinterpret_cast<const uint4*>(rrow) + j);
 }
 
+// This thread's f16 row chunk: to global memory, or (sbuf != 0, NC = 32) to its row of
+// the warp's staged 32 x 32 box: 16-byte chunk k of row r at r*64 + 16*(k ^ ((r >> 1)
+// & 3)), the 64-byte swizzle the output map's TMA store reads (conflict-free stores).
+template <int NC>
+__device__ __forceinline__ void store_row(__half* yrow, const uint4 (&out)[NC / 8], uint32_t sbuf) {
+    if constexpr (NC == 32) {
+        if (sbuf) {
+            const uint32_t r = threadIdx.x & 31;
+            const uint32_t sw = (r >> 1) & 3;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                st_shared_v4(sbuf + r * 64u + (((uint32_t)k ^ sw) << 4), out[k].x, out[k].y,
+                             out[k].z, out[k].w);
+            return;
+        }
+    }
+    uint4* yp = reinterpret_cast<uint4*>(yrow);
+#pragma unroll
+    for (int j = 0; j < NC / 8; ++j) yp[j] = out[j];
+}
+
 // One epilogue chunk of NC (32 or 16) accumulator columns for this thread's row:
 // TMEM (sum of the J partial accumulators) -> + bias [+ residual] -> ReLU / clamp
 // -> mask -> f16 store. The TMEM loads are warp-collective, so every lane executes
@@ -263,7 +299,8 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
                                           uint32_t taddr, const float* sbias, const float* sss,
                                           bool has_res, const uint4 (&res)[NC / 8],
                                           const __half* r2ptr, __half* yrow, __half* y2row,
-                                          __half* srow, const __half* arow, bool add_in_res) {
+                                          __half* srow, const __half* arow, bool add_in_res,
+                                          uint32_t sbuf) {
     float f[NC];
 #pragma unroll
     for (int i = 0; i < NC; ++i) f[i] = 0.0f;
@@ -300,7 +337,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         // (every other epilogue mode compiled out, so the hot code stays small)
         const uint32_t keep = ri.valid ? 0xFFFFFFFFu : 0u;
         const __half2 zero2 = __float2half2_rn(0.0f);
-        uint4* yp = reinterpret_cast<uint4*>(yrow);
+        uint4 out[NC / 8];
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) {
             __half2 h[4];
@@ -310,11 +347,12 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
                                          f[j * 8 + 2 * q + 1] + sbias[j * 8 + 2 * q + 1]);
                 if (p.relu) h[q] = __hmax2(h[q], zero2);
             }
-            yp[j] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
-                               *reinterpret_cast<uint32_t*>(&h[1]) & keep,
-                               *reinterpret_cast<uint32_t*>(&h[2]) & keep,
-                               *reinterpret_cast<uint32_t*>(&h[3]) & keep);
+            out[j] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
+                                *reinterpret_cast<uint32_t*>(&h[1]) & keep,
+                                *reinterpret_cast<uint32_t*>(&h[2]) & keep,
+                                *reinterpret_cast<uint32_t*>(&h[3]) & keep);
         }
+        store_row<NC>(yrow, out, sbuf);
         return;
     }
     if constexpr (SEQ) {
@@ -436,9 +474,7 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
         out[j].z = *reinterpret_cast<uint32_t*>(&h[2]) & keep;
         out[j].w = *reinterpret_cast<uint32_t*>(&h[3]) & keep;
     }
-    uint4* yp = reinterpret_cast<uint4*>(yrow);
-#pragma unroll
-    for (int j = 0; j < NC / 8; ++j) yp[j] = out[j];
+    store_row<NC>(yrow, out, sbuf);
     if (y2row) {
         uint4* y2p = reinterpret_cast<uint4*>(y2row);
 #pragma unroll
@@ -485,17 +521,50 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
 // Epilogue of one (tile, row block) for this thread: columns [c_lo, c_hi) of the
 // tile in chunks of NC, with the residual of the next chunk loaded before the
 // current one is finished.
+// Staged output (stage != 0): before a chunk, lane 0 waits until the store issued
+// from the same buffer two chunks ago has read it; after it, the warp's box goes out
+// by one TMA store from lane 0 (rows past M clipped by the map). One bulk group per
+// chunk, even when empty, so the wait's count stays exact.
+struct EpiStage {
+    const CUtensorMap* map;
+    uint32_t base;  // this warp's two 2 KB buffers; 0 = direct stores
+    uint32_t n;     // chunks staged so far (buffer parity)
+    int row0;       // first row of the warp's 32
+};
+
+__device__ __forceinline__ uint32_t stage_begin(EpiStage& st) {
+    if (!st.base) return 0u;
+    const uint32_t buf = st.base + (st.n & 1u) * 2048u;
+    if ((threadIdx.x & 31) == 0) bulk_wait_read<1>();
+    __syncwarp();
+    return buf;
+}
+
+__device__ __forceinline__ void stage_end(EpiStage& st, uint32_t buf, int col, int M) {
+    if (!st.base) return;
+    fence_proxy_async_smem();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+        if (st.row0 < M) tma_store_3d(st.map, buf, col, st.row0, 0);
+        bulk_commit();
+    }
+    ++st.n;
+}
+
 template <int NC, int J, bool SEQ, bool PLAIN>
 __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowInfo& ri, int m,
                                          int n0, int c_lo, int c_hi, uint32_t tbase,
-                                         const float* sbias, const float* sss) {
+                                         const float* sbias, const float* sss, EpiStage& st) {
     if constexpr (PLAIN) {
         __half* yrow = p.y + ri.dst * p.ldy + n0;
         const uint4 none[NC / 8] = {};
-        for (int c = c_lo; c < c_hi; c += NC)
+        for (int c = c_lo; c < c_hi; c += NC) {
+            const uint32_t buf = stage_begin(st);
             epi_chunk<NC, J, SEQ, true>(p, live, ri, n0 + c, tbase + (uint32_t)c,
                                         sbias + n0 + c, sss, false, none, nullptr, yrow + c,
-                                        nullptr, nullptr, nullptr, false);
+                                        nullptr, nullptr, nullptr, false, buf);
+            stage_end(st, buf, n0 + c, p.M);
+        }
         return;
     }
     const bool has_res = p.residual != nullptr && ri.valid;
@@ -516,10 +585,12 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
         if (prow && c + NC < c_hi) load_res<NC>(prow + c + NC, res);
+        const uint32_t buf = stage_begin(st);
         epi_chunk<NC, J, SEQ, false>(p, live, ri, n0 + c, tbase + (uint32_t)c, sbias ? sbias + n0 + c : nullptr,
                          sss, has_res, cur, has_res2 ? r2row + c : nullptr, yrow + c,
                          y2row ? y2row + c : nullptr, srow ? srow + c : nullptr,
-                         arow ? arow + c : nullptr, add_in_res);
+                         arow ? arow + c : nullptr, add_in_res, buf);
+        stage_end(st, buf, n0 + c, p.M);
     }
 }
 
@@ -579,32 +650,32 @@ __device__ __forceinline__ void issue_qpack(uint32_t d_tile, uint64_t a_desc, ui
 // v): + bias [+ residual] -> ReLU -> mask -> f16, stored to the same QPACK row
 // (y_phase 0) or to the pixel's place in the PHASE layout (y_phase 1). res holds the
 // residual's 32 channels when p.qp_res (prefetched by the caller).
-__device__ __forceinline__ void qpack_unit(const ConvDev& p, const int* stv, int m, bool live,
+// One QPACK output unit of a thread: row m, pixel phase j (its 32 channels): bias,
+// the optional residual, ReLU and the padding mask applied, packed as f16 pairs.
+// Returns false for a PHASE output pixel past the padded grid (nothing to store).
+__device__ __forceinline__ bool qpack_pack(const ConvDev& p, const int* stv, int m, bool live,
                                            int j, const uint32_t (&v)[32], const float* sbias,
-                                           const uint4 (&res)[4]) {
-    if (m >= p.M) return;
+                                           const uint4 (&res)[4], uint32_t (&o)[16],
+                                           __half** dst) {
     const int img = p.Hp * p.Wp;
     const int b = fdiv(m, p.img_mul, p.img_sh);
     const int r = m - b * img;
     const int tp = fdiv(r, p.wp_mul, p.wp_sh);
     const int fp = 4 * (r - tp * p.Wp) + j;
     const bool valid = live && tp >= 1 && tp <= stv[b] && fp >= 1 && fp <= p.F;
-    __half* dst;
     if (p.y_phase == 1) {
-        if (fp > p.F + 1) return;  // past the padded grid: no PHASE slot
+        if (fp > p.F + 1) return false;  // past the padded grid: no PHASE slot
         const int q = ((tp & 1) << 1) | (fp & 1);
-        dst = p.y + ((long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
-                     (fp >> 1) + 1) * 32;
+        *dst = p.y + ((long long)q * p.plane_rows + ((long long)b * p.Hq + (tp >> 1) + 1) * p.Wq +
+                      (fp >> 1) + 1) * 32;
     } else {
-        dst = p.y + (long long)m * 128 + j * 32;
+        *dst = p.y + (long long)m * 128 + j * 32;
     }
     const uint32_t keep = valid ? 0xFFFFFFFFu : 0u;
     const __half2 zero2 = __float2half2_rn(0.0f);
-    uint4* yp = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const uint32_t rw[4] = {res[c].x, res[c].y, res[c].z, res[c].w};
-        __half2 h[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float a0 = __uint_as_float(v[c * 8 + 2 * q]) + sbias[c * 8 + 2 * q];
@@ -613,14 +684,12 @@ __device__ __forceinline__ void qpack_unit(const ConvDev& p, const int* stv, int
                 a0 += h2f(rw[q] & 0xFFFFu);
                 a1 += h2f(rw[q] >> 16);
             }
-            h[q] = __floats2half2_rn(a0, a1);
-            if (p.relu) h[q] = __hmax2(h[q], zero2);
+            __half2 h = __floats2half2_rn(a0, a1);
+            if (p.relu) h = __hmax2(h, zero2);
+            o[c * 4 + q] = *reinterpret_cast<uint32_t*>(&h) & keep;
         }
-        yp[c] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
-                           *reinterpret_cast<uint32_t*>(&h[1]) & keep,
-                           *reinterpret_cast<uint32_t*>(&h[2]) & keep,
-                           *reinterpret_cast<uint32_t*>(&h[3]) & keep);
     }
+    return true;
 }
 
 // ---- MMA issue schedules ---------------------------------------------------
@@ -816,7 +885,7 @@ template <int NMB, int J, bool PAIR, bool SEQ, bool PLAIN = false, bool QP = fal
 __global__ void __launch_bounds__(kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
-               const __grid_constant__ ConvDev p) {
+               const __grid_constant__ CUtensorMap tmY, const __grid_constant__ ConvDev p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     const uint32_t base = (raw_u32 + 1023u) & ~1023u;
@@ -1259,10 +1328,34 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         const int c_lo = split ? half * (p.BN / 2) : 0;
         const int c_hi = mb_split ? p.BN : (split ? c_lo + p.BN / 2 : (half == 0 ? p.BN : 0));
         uint32_t acc = 0, acc_phase = 0;
+        // staged output: this warp's two buffers and the chunks it has staged
+        const uint32_t stage_base = base + p.ostage_off + (uint32_t)ew * 4096u;
+        uint32_t stage_n = 0;
         for (int tile = first_tile<PAIR>(); tile < n_tiles; tile += tile_stride<PAIR>()) {
             const int mt = tile / p.n_nt, nt = tile - mt * p.n_nt;
             const int m0 = mt * p.BM + (int)rank * kMB, n0 = nt * p.BN;
             const bool live = tile_live<SEQ, QP>(p, stv, mt * p.BM);
+            // QPACK residual: the (mb, 32-column chunk) units this thread stores, in
+            // order; the first unit's residual is loaded before the accumulator wait and
+            // each next one while the current unit is converted, so the residual read
+            // overlaps the MMAs and the stores instead of following them
+            const int qp_mb0 = mb_split ? half : 0, qp_mbs = mb_split ? 2 : 1;
+            const int qp_nc = (c_hi - c_lo) >> 5;
+            const int qp_units = QP ? ((NMB - qp_mb0 + qp_mbs - 1) / qp_mbs) * qp_nc : 0;
+            uint4 res[4] = {};
+            auto qp_res_load = [&](int u, uint4 (&r)[4]) {
+                const int mb = qp_mb0 + (u / qp_nc) * qp_mbs;
+                const int c = c_lo + (u % qp_nc) * 32;
+                const int m = m0 + mb * kMB + quad * 32 + lane;
+                if (p.qp_res && m < p.M) {
+                    const uint4* rp = reinterpret_cast<const uint4*>(p.qp_res + (long long)m * 128 + c);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) r[q] = __ldg(rp + q);
+                }
+            };
+            if constexpr (QP) {
+                if (qp_units > 0) qp_res_load(0, res);
+            }
             if (live) {
                 if (!mbar_wait(bar_tfull + 8 * acc, acc_phase, p.err, VDB_ERR_TIMEOUT_TFULL,
                                abort_flag))
@@ -1270,27 +1363,54 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 tc_fence_after();
             }
             if constexpr (QP) {
-                for (int mb = 0; mb < NMB; ++mb) {
-                    if (mb_split && (mb & 1) != half) continue;
+                for (int u = 0; u < qp_units; ++u) {
+                    const int mb = qp_mb0 + (u / qp_nc) * qp_mbs;
+                    const int c = c_lo + (u % qp_nc) * 32;
                     const int m = m0 + mb * kMB + quad * 32 + lane;
                     const uint32_t tb = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * acc_cols +
                                         (uint32_t)(mb * p.BN);
-                    for (int c = c_lo; c < c_hi; c += 32) {
-                        uint4 res[4] = {};
-                        if (p.qp_res && m < p.M) {
-                            const uint4* rp = reinterpret_cast<const uint4*>(p.qp_res + (long long)m * 128 + c);
+                    uint4 nres[4] = {};
+                    if (u + 1 < qp_units) qp_res_load(u + 1, nres);
+                    uint32_t v[32];
+                    if (live) {
+                        tmem_ld_32x32b_x32(tb + (uint32_t)c, v);
+                    } else {
 #pragma unroll
-                            for (int q = 0; q < 4; ++q) res[q] = __ldg(rp + q);
-                        }
-                        uint32_t v[32];
-                        if (live) {
-                            tmem_ld_32x32b_x32(tb + (uint32_t)c, v);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) v[i] = 0u;
-                        }
-                        qpack_unit(p, stv, m, live, c >> 5, v, sbias + c, res);
+                        for (int i = 0; i < 32; ++i) v[i] = 0u;
                     }
+                    uint32_t o[16] = {};
+                    __half* dst = nullptr;
+                    const bool has = m < p.M &&
+                                     qpack_pack(p, stv, m, live, c >> 5, v, sbias + c, res, o, &dst);
+                    if (p.ostage_off) {
+                        // the warp's 32 consecutive rows x these 32 columns are one box of
+                        // the output map: stage it (64-byte swizzle: 16-byte chunk k of
+                        // row r at r*64 + 16*(k ^ ((r >> 1) & 3)), conflict-free) and let
+                        // one lane store it; rows past M are clipped by the map
+                        const uint32_t buf = stage_base + (stage_n & 1u) * 2048u;
+                        if (lane == 0) bulk_wait_read<1>();  // this buffer's last store has read it
+                        __syncwarp();
+                        const uint32_t sw = (uint32_t)((lane >> 1) & 3);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            st_shared_v4(buf + (uint32_t)lane * 64u + (((uint32_t)k ^ sw) << 4),
+                                         o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            const int row0 = m0 + mb * kMB + quad * 32;
+                            if (row0 < p.M) tma_store_3d(&tmY, buf, c, row0, 0);
+                            bulk_commit();  // one group per unit, even when empty
+                        }
+                        ++stage_n;
+                    } else if (has) {
+                        uint4* yp = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            yp[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) res[q] = nres[q];
                 }
                 goto tile_done;
             }
@@ -1300,10 +1420,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) +
                                        acc * acc_cols + (uint32_t)(mb * J * p.BN);
                 const RowInfo ri = row_info<SEQ>(p, stv, m, live);
+                // the host stages only outputs whose chunks are 32 columns wide
+                EpiStage st{&tmY, (p.ostage_off && (c_hi - c_lo) % 32 == 0) ? stage_base : 0u,
+                            stage_n, m0 + mb * kMB + quad * 32};
                 if ((c_hi - c_lo) % 32 == 0)
-                    epi_rows<32, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<32, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss, st);
                 else
-                    epi_rows<16, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss);
+                    epi_rows<16, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss, st);
+                stage_n = st.n;
             }
         tile_done:
             if (live) {
@@ -1323,6 +1447,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 }
             }
         }
+        // the staged TMA stores have written global memory before the CTA retires
+        if (p.ostage_off && lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -1900,15 +2026,37 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const uint32_t ss_bytes = has_bn ? 2u * (uint32_t)round_up(a->oc * 4, 16) : 0u;
     const uint32_t tail = (uint32_t)round_up(a->oc * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
                           ss_bytes + 8 * (3 * kMaxStages + 5) + 16;
-    const int budget = kSmemMax - 1024 - (int)off - (int)tail;
+    uint32_t ab = 0, bb = 0;  // two-ring slot sizes
+    for (int sg = 0; sg < p.n_seg; ++sg) {
+        ab = std::max(ab, p.seg[sg].a_bytes);
+        bb = std::max(bb, p.seg[sg].b_bytes);
+    }
+    // pipeline slots that fit a budget: weight slots (two-ring) or stages
+    auto slots = [&](int bud) {
+        return two_ring ? std::min<int>(kMaxStages - 2, (bud - 2 * round_up((int)ab, 1024)) /
+                                                            round_up((int)bb, 1024))
+                        : std::min<int>(kMaxStages, bud / (int)p.stage_bytes);
+    };
+    // Staged output (GRID y only, 32-column chunks, a 16-byte aligned row pitch): the
+    // epilogue warps' stores become one TMA box store per 32 rows x 32 columns instead
+    // of 32 row stores of 64 bytes, which otherwise saturate the LSU data path on the
+    // small-channel convs. Taken when it leaves at least min(3, the slots without it)
+    // pipeline slots.
+    const bool chunk32 = BN % 64 == 0 || (p.n_mblk >= 2 && BN % 32 == 0);
+    const int ldy_el = a->ldy ? a->ldy : a->oc;
+    const int store_mode = conv_tma_store_mode();
+    bool staged = store_mode != 0 && !seq && a->y_phase == 0 && !a->y2 && !a->ysum && chunk32 &&
+                  (reinterpret_cast<uintptr_t>(a->y) & 15u) == 0 && ldy_el % 8 == 0;
+    const int budget0 = kSmemMax - 1024 - (int)off - (int)tail;
+    if (staged) {
+        const int with = slots(budget0 - (int)kOstageBytes), without = slots(budget0);
+        staged = with >= 2 && (store_mode == 1 || with >= std::min(3, without));
+    }
+    const uint32_t ostage_bytes = staged ? kOstageBytes : 0u;
+    const int budget = budget0 - (int)ostage_bytes;
     p.two_ring = two_ring ? 1 : 0;
     if (two_ring) {
         // 2 A slots (a halo per channel block) + as many weight slots as fit
-        uint32_t ab = 0, bb = 0;
-        for (int sg = 0; sg < p.n_seg; ++sg) {
-            ab = std::max(ab, p.seg[sg].a_bytes);
-            bb = std::max(bb, p.seg[sg].b_bytes);
-        }
         p.ra = 2;
         p.a_stride = (uint32_t)round_up((int)ab, 1024);
         p.b_stride = (uint32_t)round_up((int)bb, 1024);
@@ -1929,6 +2077,8 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         }
         off += p.n_stages * p.stage_bytes;
     }
+    p.ostage_off = staged ? off : 0u;  // 1024-byte aligned: every slot is
+    off += ostage_bytes;
     p.bias_off = off;
     off += (uint32_t)round_up(a->oc * 4, 16);
     p.tv_off = off;
@@ -2007,7 +2157,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // Input row extents: stride 1 reads G(B, t_out, f_out); stride 2 reads the
     // 4 planes of a PHASE tensor, each shaped like the output grid.
     const long long rows_out = p.M;
-    CUtensorMap tm[4];
+    CUtensorMap tm[5];
     for (int sg = 0; sg < p.n_seg; ++sg) {
         const SegDev& s = p.seg[sg];
         const void* x = sg ? a->x1 : a->x0;
@@ -2027,6 +2177,14 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     if (p.n_seg == 1) {
         tm[2] = tm[0];
         tm[3] = tm[1];
+    }
+    if (staged) {
+        if (!make_map_a(&tm[4], a->y, a->oc, ldy_el, rows_out, 1, 32, 32)) {
+            set_error("vdb_conv: cuTensorMapEncodeTiled failed");
+            return 1;
+        }
+    } else {
+        tm[4] = tm[0];
     }
     // One CTA per SM: more than 256 TMEM columns, or most of shared memory.
     const size_t smem_launch = std::max<size_t>(smem, 120 * 1024);
@@ -2055,7 +2213,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
+        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], tm[4], p));
         return 0;
     };
     // The plain epilogue (bias, ReLU, mask, GRID / PHASE store): every ResNet34 conv.
@@ -2084,7 +2242,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
+        VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], tm[4], p));
         return 0;
     }
     if (seq) {
@@ -2126,6 +2284,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
 
 
 // Stage-1 conv over QPACK rows (vdb_conv_args.qpack): see the QPACK section above.
+
 int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     if (a->k0 != 3 || a->stride0 != 1 || a->ic0 != 32 || a->oc != 32 || a->x1 || a->act != 0 ||
         a->y2 || a->ysum || a->residual2 || a->clamp_hi > 0.0f ||
@@ -2185,8 +2344,11 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     p.stage0 = off;
     p.a_region = (uint32_t)round_up((int)s.bytes, 1024);
     p.stage_bytes = p.a_region;
-    const uint32_t tail = (uint32_t)round_up(128 * 4, 16) + (uint32_t)round_up(a->batch * 4, 16) +
-                          8 * (3 * kMaxStages + 5) + 16;
+    // y_phase 0 stores through TMA from 2 staging buffers of 2 KB per epilogue warp
+    const bool staged = a->y_phase == 0 && conv_tma_store_mode() != 0;
+    const uint32_t ostage_bytes = staged ? kOstageBytes : 0u;
+    const uint32_t tail = ostage_bytes + (uint32_t)round_up(128 * 4, 16) +
+                          (uint32_t)round_up(a->batch * 4, 16) + 8 * (3 * kMaxStages + 5) + 16;
     const int budget = kSmemMax - 1024 - (int)off - (int)tail;
     p.n_stages = (uint32_t)std::min<int>(kMaxStages, budget / (int)p.stage_bytes);
     if (p.n_stages < 2) {
@@ -2194,6 +2356,8 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
         return 1;
     }
     off += p.n_stages * p.stage_bytes;
+    p.ostage_off = staged ? off : 0u;  // 1024-byte aligned: the stages are
+    off += ostage_bytes;
     p.bias_off = off;
     off += (uint32_t)round_up(128 * 4, 16);
     p.tv_off = off;
@@ -2231,7 +2395,7 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     p.oc = 128;
     p.err = a->err;
     p.qp_res = static_cast<const __half*>(a->residual);
-    CUtensorMap tm[4];
+    CUtensorMap tm[5];
     if (!make_map_a(&tm[0], a->x0, 128, 128, rows, 1, 64, s.box_rows) ||
         !make_map_b(&tm[1], a->w0, 32, 1152, 128, 32)) {
         set_error("vdb_conv: cuTensorMapEncodeTiled failed");
@@ -2239,6 +2403,14 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     }
     tm[2] = tm[0];
     tm[3] = tm[1];
+    if (staged) {
+        if (!make_map_a(&tm[4], a->y, 128, 128, rows, 1, 32, 32)) {
+            set_error("vdb_conv: cuTensorMapEncodeTiled failed");
+            return 1;
+        }
+    } else {
+        tm[4] = tm[0];
+    }
     const size_t smem_launch = std::max<size_t>(smem, 120 * 1024);
     const int grid = std::max(1, std::min(p.n_mt, num_sms()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -2258,7 +2430,7 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], p));
+    VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], tm[4], p));
     return 0;
 }
 
