@@ -11,6 +11,10 @@ are device resident for `value`; larger than L2, so no flush is needed.
 `e2e` runs the same shard through the public C ABI call a user makes
 (voicedetect_capi_embed_pcm_batch) from host PCM to host embeddings.
 
+The same run adds an `eres2net` key (skip with --no-eres-leg): BASELINE config 2,
+ERes2Net-base f16 on a batch of 256 x 10 s clips per GPU and step, measured the same
+way (device-resident `value`, public-API `e2e`, conv roofline, CPU baseline).
+
 `--impl reference` times the reference's own CPU implementation of this path
 (src/fbank.cpp + src/directconv.cpp compiled unmodified, oracle/_ref) on this
 host's cores, on a bounded sample of the same workload per step.
@@ -42,10 +46,39 @@ CLIPS_PER_GPU = 8192
 POOL = 64            # distinct synthetic sources the clips are cut from
 SEED = 20261201
 METRIC = "utterance-sec/sec ResNet34 embed"
-# DRAM bytes (read + write) per algorithmic conv FLOP, measured with ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum over every conv launch) on this
-# workload at the same bucket sizes: 344.6 GB over 77.4 TFLOP.
-CONV_DRAM_BYTES_PER_FLOP = 4.45e-3
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum of one launch, ncu) per
+# algorithmic kFLOP of each ResNet34 conv launch shape, from single-launch captures at
+# batch 512 x 300 frames (every tensor above the 126 MB L2); the command and the table
+# are in profiles/conv_tc__dram_by_shape_b512.md. Key: (ic, oc, stride, second input
+# segment's channels (0: none), epilogue residual, QPACK). A conv's traffic scales
+# with its rows, as its FLOPs do, so bytes = ratio x the launch's algorithmic FLOPs.
+CONV_DRAM_B_PER_KFLOP = {
+    (32, 32, 1, 0, 0, 1): 7.112, (32, 32, 1, 0, 1, 1): 10.846,
+    (32, 64, 2, 0, 0, 0): 10.765,
+    (64, 64, 1, 32, 0, 0): 4.181, (64, 64, 1, 0, 0, 0): 3.444, (64, 64, 1, 64, 0, 0): 5.398,
+    (64, 128, 2, 0, 0, 0): 5.591,
+    (128, 128, 1, 64, 0, 0): 2.162, (128, 128, 1, 0, 0, 0): 1.756,
+    (128, 128, 1, 128, 0, 0): 2.800,
+    (128, 256, 2, 0, 0, 0): 3.015,
+    (256, 256, 1, 128, 0, 0): 1.158, (256, 256, 1, 0, 0, 0): 0.910,
+    (256, 256, 1, 256, 0, 0): 1.517,
+}
+
+
+def conv_traffic(convs: list[dict]):
+    """(mean DRAM bytes per conv launch, share of the conv FLOPs whose shape has a
+    measured ratio) for the profiled launches `convs` (Model.profile_convs())."""
+    tot, fl_known, fl_all = 0.0, 0.0, 0.0
+    for r in convs:
+        fl_all += r["flops"]
+        key = (r["ic"], r["oc"], r["stride"], r["ic1"], r["res"], r["qpack"])
+        if key in CONV_DRAM_B_PER_KFLOP:
+            tot += CONV_DRAM_B_PER_KFLOP[key] * r["flops"] / 1e3
+            fl_known += r["flops"]
+    if not convs or fl_known == 0.0:
+        return None, 0.0
+    # launches of an unmeasured shape count at the measured launches' mean ratio
+    return tot * (fl_all / fl_known) / len(convs), fl_known / fl_all
 UNIT = "utterance-sec/sec"
 E2E_WARMUP = 2  # untimed public-API calls before the e2e timing (see run_b200)
 
@@ -479,6 +512,7 @@ def run_b200(args) -> int:
     elapsed_ms = start.elapsed_time(end)
     clk = clocks.stop()
     conv_ms, conv_flops, conv_n, stages, prof_steps = profiled_steps(model, step, args.steps)
+    traffic, traffic_cov = conv_traffic(model.profile_convs())
     model.sync()
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -564,11 +598,12 @@ def run_b200(args) -> int:
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured)"
                      if peaks else "fallback 1.4 PFLOP/s sustained",
-                     "traffic": (CONV_DRAM_BYTES_PER_FLOP * conv_flops / conv_n) if conv_n else None,
+                     "traffic": traffic,
                      "traffic_unit": "bytes per conv launch (dram read+write)",
-                     "traffic_source": "ncu capture summarised in "
-                                       "profiles/launches__bench_c4_512clips.md, scaled by "
-                                       "this run's FLOPs per launch",
+                     "traffic_source": "per-shape single-launch ncu captures "
+                                       "(profiles/conv_tc__dram_by_shape_b512.md) x this "
+                                       "run's per-launch FLOPs (profiled launches)",
+                     "traffic_shape_coverage": traffic_cov,
                      "conv_launches": conv_n, "profiled_steps": prof_steps,
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
@@ -589,9 +624,13 @@ def run_b200(args) -> int:
             "sample": f"{args.ref_clips} clips ({audio:.0f} audio-s) drawn from the same "
                       "workload; reference FBank + blocked directconv ResNet34 compiled "
                       "unmodified (oracle/_ref), all host threads"}
+    model.close()
+    if not args.no_eres_leg:
+        # BASELINE config 2 beside the headline: ERes2Net-base f16, --eres-batch 10 s
+        # clips per GPU and step, with its own roofline, e2e and CPU baseline
+        result["eres2net"] = measure_family(_Family("eres2net", args), args, world, rank, dev)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -799,6 +838,22 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         torch.cuda.set_device(0)
     dev = torch.device("cuda", local if world > 1 else 0)
 
+    result = measure_family(fam, args, world, rank, dev)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
+    """One family's fixed-batch measurement on this rank's GPU (all ranks take part:
+    the all-gather per step and the max over ranks), returning the result dict."""
+    import torch
+    import torch.distributed as dist
+    import vd_b200
+
     tmp = tempfile.mkdtemp(prefix="vdbench_")
     m = fam.model()
     gguf = os.path.join(tmp, fam.gguf_name)
@@ -820,7 +875,7 @@ def run_eres2net(args, family: str = "eres2net") -> int:
         model.embed_device(d_pcm, offs, lens, d_out, stream.cuda_stream)
         gather_embeddings(d_out, gathered, world)
 
-    rank_checkpoint("setup")  # before the first all-gather
+    rank_checkpoint(f"{fam.name}-setup")  # before the first all-gather
     for _ in range(args.warmup):
         step()
     model.sync()
@@ -888,13 +943,8 @@ def run_eres2net(args, family: str = "eres2net") -> int:
                                             threads)
         result["cpu_baseline"] = {"value": audio / wall, "unit": UNIT, "cores": threads,
                                   "kind": kind, "sample": sample + " (clips of the same batch)"}
-    if rank == 0:
-        print(json.dumps(result), flush=True)
     model.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return result
 
 
 def ecapa_config(args, world):
@@ -927,47 +977,78 @@ def eres_config(args, world):
 
 # every distinct ResNet34 3x3 conv shape (stage entries carry the
 # fused 1x1 downsample in conv2), batch B, T = 300 frames, 80 mels.
-SWEEP_SHAPES = [  # (ic, oc, t_in, f_in, stride, fused_down)
-    (32, 32, 300, 80, 1, False), (32, 64, 300, 80, 2, False), (64, 64, 150, 40, 1, True),
-    (64, 64, 150, 40, 1, False), (64, 128, 150, 40, 2, False), (128, 128, 75, 20, 1, True),
-    (128, 128, 75, 20, 1, False), (128, 256, 75, 20, 2, False), (256, 256, 38, 10, 1, True),
-    (256, 256, 38, 10, 1, False)]
+# Every distinct conv launch of the ResNet34 engine at batch B x 300 frames:
+# (ic, oc, t_in, f_in, stride, kind). kind: "qp" / "qp+res" the stage-1 QPACK convs
+# (conv1; conv2 with the identity shortcut as the epilogue residual), "plain" a
+# one-segment conv (a block's conv1), "down" a block's conv2 with the 1x1 stride-2
+# downsample as input segment 1, "id" a block's conv2 with the identity shortcut as
+# input segment 1 (identity weights; not counted in the algorithmic FLOPs, as in the
+# engine), "res" the same conv with the shortcut added in the epilogue instead.
+SWEEP_SHAPES = [
+    (32, 32, 300, 80, 1, "qp"), (32, 32, 300, 80, 1, "qp+res"),
+    (32, 64, 300, 80, 2, "plain"), (64, 64, 150, 40, 1, "down"),
+    (64, 64, 150, 40, 1, "plain"), (64, 64, 150, 40, 1, "id"),
+    (64, 128, 150, 40, 2, "plain"), (128, 128, 75, 20, 1, "down"),
+    (128, 128, 75, 20, 1, "plain"), (128, 128, 75, 20, 1, "id"),
+    (128, 256, 75, 20, 2, "plain"), (256, 256, 38, 10, 1, "down"),
+    (256, 256, 38, 10, 1, "plain"), (256, 256, 38, 10, 1, "id")]
+# launches of each sweep shape per ResNet34 forward (blocks 3 / 4 / 6 / 3)
+SWEEP_COUNTS = [3, 3, 1, 1, 3, 3, 1, 1, 5, 5, 1, 1, 2, 2]
 
 
 def run_sweep(args) -> int:
     """Per-shape vdb_conv timing (CUDA events, device-resident f16 inputs),
-    one JSON line per shape: algorithmic TFLOP/s over valid pixels."""
+    one JSON line per shape: algorithmic TFLOP/s over valid pixels; the total weights
+    each shape by its launches per ResNet34 forward."""
     import torch
     import vd_b200 as vd
     torch.manual_seed(0)
     B = args.op_sweep
     L = vd.lib()
     out = []
-    for ic, oc, T, F, s, down in SWEEP_SHAPES:
+    for (ic, oc, T, F, s, kind), cnt in zip(SWEEP_SHAPES, SWEEP_COUNTS):
         To, Fo = vd.out_extent(T, s), vd.out_extent(F, s)
-        icc = oc if down else ic
-        rows = L.vdb_phase_rows(B, T, F) if s == 2 else L.vdb_grid_rows(B, T, F)
-        x = torch.empty(rows, icc, dtype=torch.float16, device="cuda").normal_().relu_()
-        w = (torch.randn(oc, 9, icc, device="cuda") * (2 / (9 * icc)) ** 0.5).half()
+        qp = kind.startswith("qp")
+        icc = oc if kind == "down" else ic
+        if qp:
+            rows = L.vdb_qpack_rows(B, T, F)
+            x = torch.empty(rows, 128, dtype=torch.float16, device="cuda").normal_().relu_()
+            w = vd.qpack_weights(vd.pack_conv_weight(
+                (torch.randn(32, 32, 3, 3, device="cuda") * (2 / 288) ** 0.5).half()))
+            y = torch.empty_like(x)
+        else:
+            rows = L.vdb_phase_rows(B, T, F) if s == 2 else L.vdb_grid_rows(B, T, F)
+            x = torch.empty(rows, icc, dtype=torch.float16, device="cuda").normal_().relu_()
+            w = (torch.randn(oc, 9, icc, device="cuda") * (2 / (9 * icc)) ** 0.5).half()
+            y = torch.empty(L.vdb_grid_rows(B, To, Fo), oc, dtype=torch.float16, device="cuda")
         b = torch.zeros(oc, device="cuda")
         tv = torch.full((B,), To, dtype=torch.int32, device="cuda")
         kw = {}
-        if down:
+        if kind == "down":
             x1 = torch.empty(L.vdb_phase_rows(B, 2 * To, 2 * Fo), ic // 2, dtype=torch.float16,
                              device="cuda").normal_().relu_()
             kw = dict(x1=x1, w1=(torch.randn(oc, ic // 2, device="cuda") * 0.1).half(),
                       stride1=2)
-        y = torch.empty(L.vdb_grid_rows(B, To, Fo), oc, dtype=torch.float16, device="cuda")
+        elif kind == "id":
+            kw = dict(x1=torch.empty_like(x).normal_().relu_(),
+                      w1=torch.eye(oc, device="cuda").half(), stride1=1)
+        elif kind == "qp+res":
+            kw = dict(residual=torch.empty_like(x).normal_().relu_())
+        elif kind == "res":
+            kw = dict(residual=torch.empty_like(y).normal_().relu_())
+        if qp:
+            kw.update(qpack=True)
 
         def run():
             vd.conv(x, w, b, tv, batch=B, t_out=To, f_out=Fo, oc=oc, k0=3,
-                    stride0=1 if down else s, ic0=icc, relu=True, y=y,
+                    stride0=1 if kind == "down" else s, ic0=icc, relu=True, y=y,
                     tile_m=args.sweep_tile_m, halo=args.sweep_halo, ksplit=args.sweep_ksplit,
                     tile_n=args.sweep_tile_n, pair=args.sweep_pair, **kw)
+        name = f"{icc}->{oc} s{s} {kind} out {Fo}x{To}"
         try:
             run()  # validates the requested tiling for this shape
         except RuntimeError as e:
-            print(json.dumps({"shape": f"{icc}->{oc} s{s}", "skipped": str(e)}), flush=True)
+            print(json.dumps({"shape": name, "skipped": str(e)}), flush=True)
             continue
         for _ in range(args.sweep_warmup):
             run()
@@ -979,21 +1060,156 @@ def run_sweep(args) -> int:
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / args.sweep_reps
-        fl = 2.0 * oc * icc * 9 * To * Fo * B + (2.0 * oc * (ic // 2) * To * Fo * B if down else 0)
-        r = dict(shape=f"{icc}->{oc} s{s}{'+down' if down else ''} out {Fo}x{To}", batch=B,
-                 ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1),
-                 gflop=round(fl / 1e9, 2))
+        fl = 2.0 * oc * icc * 9 * To * Fo * B + (2.0 * oc * (ic // 2) * To * Fo * B
+                                                 if kind == "down" else 0)
+        r = dict(shape=name, batch=B, ms=round(ms, 4), tflops=round(fl / ms / 1e9, 1),
+                 gflop=round(fl / 1e9, 2), per_forward=cnt)
         out.append(r)
         print(json.dumps(r), flush=True)
-    tot_fl = sum(r["gflop"] for r in out)
-    tot_ms = sum(r["ms"] for r in out)
+    tot_fl = sum(r["gflop"] * r["per_forward"] for r in out)
+    tot_ms = sum(r["ms"] * r["per_forward"] for r in out)
     print(json.dumps({"sweep_total": {"gflop": round(tot_fl, 1), "ms": round(tot_ms, 3),
-                                      "tflops": round(tot_fl / tot_ms, 1)}}), flush=True)
+                                      "tflops": round(tot_fl / tot_ms, 1),
+                                      "weights": "launches per ResNet34 forward"}}), flush=True)
+    return 0
+
+
+PROFILE_CASES = ("front", "tail", "identify", "ingest", "eres2net", "qpack")
+
+
+def run_profile_case(args) -> int:
+    """Small single-GPU invocations of one kernel family each (`reps` times after
+    one warm-up), sized for ncu captures: inputs above L2 (126 MB) where the kernel
+    streams memory, a few GB on the device at most. The ncu summaries in profiles/
+    name the case they were taken on.
+      front     vdb_fbank + vdb_cmn_stem_qpack on one bucket of 131 x 20 s clips
+      tail      one 131 x 20 s bucket through the ResNet34 q8_0 engine (the TSTP,
+                FC partial / finish kernels close it)
+      identify  vdb_identify, 8192 queries x 100,000 x 256, top-5
+      ingest    vdb_pcm_ingest, 64 int16 clips of 20 s at 44.1 kHz -> 16 kHz
+      eres2net  a batch of 64 x 10 s clips through the ERes2Net-base f16 engine
+      qpack     stage-1 QPACK convs (plain, then with the residual), batch 128"""
+    import ctypes as C
+    import torch
+    import vd_b200 as vd
+    case, reps = args.profile_case, args.profile_reps
+    L = vd.lib()
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(SEED)
+    runs = []
+    keep = []
+    if case in ("front", "tail"):
+        B, n = 131, 20 * SR
+        pcm = np.concatenate([vd_synth.clip_f32(vd_synth.make_clip(SEED + i, n)) for i in range(B)])
+        if case == "front":
+            d_pcm = torch.from_numpy(pcm).to(dev)
+            T = (n - 400) // 160 + 1
+            offs = torch.arange(B, dtype=torch.int64, device=dev) * n
+            ns = torch.full((B,), n, dtype=torch.int32, device=dev)
+            fr = torch.full((B,), T, dtype=torch.int32, device=dev)
+            feats = torch.empty(B, T, 80, device=dev)
+            sw = torch.randn(32, 9, device=dev) * 0.3
+            sb = torch.zeros(32, device=dev)
+            mean = torch.empty(B, 80, device=dev)
+            y = torch.empty(L.vdb_qpack_rows(B, T, 80), 128, dtype=torch.float16, device=dev)
+            plan = L.vdb_fbank_plan_create(16000, 80, 512, 400, 160, 0.97, 20.0, 0.0)
+            keep += [d_pcm, offs, ns, fr, feats, sw, sb, mean, y]
+
+            def run():
+                st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                assert L.vdb_fbank(plan, d_pcm.data_ptr(), offs.data_ptr(), ns.data_ptr(), B, T,
+                                   feats.data_ptr(), st) == 0, vd.last_error()
+                assert L.vdb_cmn_stem_qpack(feats.data_ptr(), fr.data_ptr(), B, T, 80, 1,
+                                            sw.data_ptr(), sb.data_ptr(), mean.data_ptr(),
+                                            y.data_ptr(), st) == 0, vd.last_error()
+            runs.append(run)
+        else:
+            tmp = tempfile.mkdtemp(prefix="vdprof_")
+            gguf = os.path.join(tmp, "resnet34_q8_0.gguf")
+            vd_synth.write_resnet_gguf(gguf, vd_synth.resnet34_model(SEED), "q8_0")
+            model = vd.Model(gguf)
+            d_pcm = torch.from_numpy(pcm).to(dev)
+            offs = np.arange(B, dtype=np.int64) * n
+            d_out = torch.zeros(B, model.dim, device=dev)
+            keep += [model, d_pcm, d_out]
+            runs.append(lambda: model.embed_device(d_pcm, offs, [n] * B, d_out))
+    elif case == "identify":
+        reg = torch.nn.functional.normalize(torch.randn(100000, 256, device=dev), dim=1)
+        q = torch.randn(8192, 256, device=dev)
+        oi = torch.empty(8192, 5, dtype=torch.int32, device=dev)
+        os_ = torch.empty(8192, 5, device=dev)
+        keep += [reg, q, oi, os_]
+
+        def run():
+            assert L.vdb_identify(q.data_ptr(), 8192, reg.data_ptr(), 100000, 256, 5,
+                                  oi.data_ptr(), os_.data_ptr(), None) == 0, vd.last_error()
+        runs.append(run)
+    elif case == "ingest":
+        clips = [torch.from_numpy(rng.integers(-20000, 20000, 20 * 44100).astype(np.int16)).to(dev)
+                 for _ in range(64)]
+        keep += clips
+        runs.append(lambda: vd.pcm_ingest(clips, 44100, 16000))
+    elif case == "eres2net":
+        tmp = tempfile.mkdtemp(prefix="vdprof_")
+        gguf = os.path.join(tmp, "eres2net_f16.gguf")
+        vd_synth.write_eres2net_gguf(gguf, vd_synth.eres2net_model(SEED), "f16")
+        model = vd.Model(gguf)
+        B, n = 64, 10 * SR
+        pool = make_pool(16, 10.0)
+        d_pcm = torch.from_numpy(np.concatenate([pool[i % 16] for i in range(B)])).to(dev)
+        offs = np.arange(B, dtype=np.int64) * n
+        d_out = torch.zeros(B, model.dim, device=dev)
+        keep += [model, d_pcm, d_out]
+        runs.append(lambda: model.embed_device(d_pcm, offs, [n] * B, d_out))
+    elif case == "qpack":
+        B, T, F = 128, 300, 80
+        tv = torch.full((B,), T, dtype=torch.int32, device=dev)
+        w = vd.qpack_weights(vd.pack_conv_weight(
+            (torch.randn(32, 32, 3, 3, device=dev) * (2 / 288) ** 0.5).half()))
+        bias = torch.zeros(32, device=dev)
+        rows = L.vdb_qpack_rows(B, T, F)
+        x = torch.empty(rows, 128, dtype=torch.float16, device=dev).normal_().relu_()
+        r = torch.empty_like(x).normal_().relu_()
+        y = torch.empty_like(x)
+        keep += [tv, w, bias, x, r, y]
+        for res in (None, r):
+            runs.append(lambda res=res: vd.conv(x, w, bias, tv, batch=B, t_out=T, f_out=F, oc=32,
+                                                k0=3, ic0=32, relu=True, y=y, qpack=True,
+                                                residual=res))
+    for fn in runs:  # warm-up (graph capture, lazy allocations)
+        fn()
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        for fn in runs:
+            fn()
+    torch.cuda.synchronize()
+    models = [k for k in keep if isinstance(k, vd.Model)]
+    if args.conv_table and models:
+        # one more pass with per-launch conv events: a JSON line per conv launch
+        m = models[0]
+        m.profile(True)
+        runs[0]()
+        m.profile_read()
+        m.profile(False)
+        for i, r in enumerate(m.profile_convs()):
+            r["tflops"] = round(r["flops"] / r["ms"] / 1e9, 1) if r["ms"] > 0 else 0.0
+            print(json.dumps({"conv": i, **{k: (round(v, 4) if isinstance(v, float) else v)
+                                             for k, v in r.items()}}), flush=True)
+    for k in keep:
+        if isinstance(k, vd.Model):
+            k.close()
+    print(json.dumps({"profile_case": case, "reps": reps, "ok": True}), flush=True)
     return 0
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
+                    help="run one small case of a kernel family for an ncu capture and exit")
+    ap.add_argument("--profile-reps", type=int, default=2)
+    ap.add_argument("--conv-table", action="store_true",
+                    help="with --profile-case tail / eres2net: print every conv launch's "
+                         "duration, FLOPs and shape")
     ap.add_argument("--op-sweep", type=int, default=0, metavar="B",
                     help="time every distinct ResNet34 conv shape at batch B and exit")
     ap.add_argument("--sweep-reps", type=int, default=20)
@@ -1023,6 +1239,8 @@ def main() -> int:
                     help="BASELINE config 2 (ERes2Net-base f16, 10 s clips) instead of the "
                          "ResNet34 headline workload")
     ap.add_argument("--eres-batch", type=int, default=256)
+    ap.add_argument("--no-eres-leg", action="store_true",
+                    help="skip the ERes2Net (config 2) key of the default run")
     ap.add_argument("--latency", action="store_true",
                     help="BASELINE config 0: single 3 s clip latency through the C ABI")
     ap.add_argument("--ref-eres-clips", type=int, default=8)
@@ -1042,6 +1260,8 @@ def main() -> int:
 
 
 def _dispatch(args) -> int:
+    if args.profile_case:
+        return run_profile_case(args)
     if args.op_sweep:
         return run_sweep(args)
     if args.eres2net:

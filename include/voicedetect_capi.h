@@ -146,6 +146,13 @@ int voicedetect_b200_profile_read(voicedetect_ctx* ctx, double* conv_ms, double*
  * the order: convs, FBank, CMN + stem, TSTP + FC + L2, element-wise adds (ERes2Net).
  * No reference counterpart. */
 int voicedetect_b200_profile_stages(voicedetect_ctx* ctx, double* ms, int n);
+/* The conv launches of the same read, in launch order: for launch i, rec[12*i ..
+ * 12*i+11] = duration (ms), algorithmic FLOPs, input channels, output channels, kernel
+ * size, stride, output frequency bins, output frames, batch, the second input
+ * segment's channels (0 for one segment), 1 when an epilogue residual is read, 1 for a QPACK conv. Writes at most n records; returns the
+ * number of launches (so n = 0 sizes the buffer), or -1 for a NULL context. No
+ * reference counterpart. */
+int voicedetect_b200_profile_convs(voicedetect_ctx* ctx, double* rec, int n);
 
 #ifdef __cplusplus
 }

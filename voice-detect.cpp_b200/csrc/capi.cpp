@@ -551,6 +551,30 @@ extern "C" int voicedetect_b200_sync(voicedetect_ctx* ctx) {
     return 0;
 }
 
+extern "C" int voicedetect_b200_profile_convs(voicedetect_ctx* ctx, double* rec, int n) {
+    if (!ctx || !ctx->engine) return -1;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    const auto& v = ctx->engine->conv_records;
+    const int k = std::min<int>(n, (int)v.size());
+    for (int i = 0; i < k && rec; ++i) {
+        const auto& r = v[i];
+        double* o = rec + 12 * i;
+        o[0] = r.ms;
+        o[1] = r.flops;
+        o[2] = r.ic;
+        o[3] = r.oc;
+        o[4] = r.k;
+        o[5] = r.stride;
+        o[6] = r.f_out;
+        o[7] = r.t_out;
+        o[8] = r.batch;
+        o[9] = r.ic1;
+        o[10] = r.res;
+        o[11] = r.qpack;
+    }
+    return (int)v.size();
+}
+
 extern "C" int voicedetect_b200_release_cache(voicedetect_ctx* ctx) {
     if (!ctx || !ctx->engine) return 1;
     std::lock_guard<std::mutex> lk(ctx->mu);

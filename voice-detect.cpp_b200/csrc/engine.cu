@@ -1090,7 +1090,7 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
             err = vdb_last_error();
             return 1;
         }
-        prof_end(pe, st, 2.0 * blk.oc * blk.ic * 9 * valid_px);
+        prof_end(pe, st, 2.0 * blk.oc * blk.ic * 9 * valid_px, &a);
         vdb_conv_args c2{};
         c2.batch = B;
         c2.t_out = To;
@@ -1126,7 +1126,8 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         }
         prof_end(pe, st,
                  2.0 * blk.oc * blk.oc * 9 * valid_px +
-                     (blk.identity ? 0.0 : 2.0 * blk.oc * blk.ic * valid_px));
+                     (blk.identity ? 0.0 : 2.0 * blk.oc * blk.ic * valid_px),
+                 &c2);
         launches += 2;
         lev = lev_out;
         T = To;
@@ -1218,7 +1219,7 @@ int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum,
             err = vdb_last_error();
             return 1;
         }
-        prof_end(pe, st, s.flops_px * (double)Fo * (double)tv_sum[s.level]);
+        prof_end(pe, st, s.flops_px * (double)Fo * (double)tv_sum[s.level], &a);
         ++launches;
     }
     const int lev = e_out_level_;
@@ -1556,14 +1557,30 @@ int Engine::prof_begin(cudaStream_t st, int stage) {
     prof_used_ += 2;
     prof_stage_.resize(prof_used_ / 2);
     prof_stage_[idx / 2] = stage;
+    prof_conv_.resize(prof_used_ / 2);
+    prof_conv_[idx / 2] = ConvRecord{0.0, 0.0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
     cudaEventRecord(prof_ev_[idx], st);
     return idx;
 }
 
-void Engine::prof_end(int idx, cudaStream_t st, double flops) {
+void Engine::prof_end(int idx, cudaStream_t st, double flops, const vdb_conv_args* conv) {
     if (idx < 0) return;
     cudaEventRecord(prof_ev_[idx + 1], st);
     if (prof_stage_[idx / 2] == 0) prof_flops_ += flops;
+    ConvRecord& r = prof_conv_[idx / 2];
+    r.flops = flops;
+    if (conv) {
+        r.ic = conv->ic0;
+        r.oc = conv->oc;
+        r.k = conv->k0;
+        r.stride = conv->stride0;
+        r.f_out = conv->f_out;
+        r.t_out = conv->t_out;
+        r.batch = conv->batch;
+        r.ic1 = conv->x1 ? conv->ic1 : 0;
+        r.res = conv->residual ? 1 : 0;
+        r.qpack = conv->qpack;
+    }
 }
 
 int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_launches,
@@ -1572,6 +1589,7 @@ int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_la
     conv_flops = prof_flops_;
     conv_launches = 0;
     for (double& v : stage_ms) v = 0.0;
+    conv_records.clear();
     for (size_t i = 0; i + 1 < prof_used_; i += 2) {
         if (cudaEventSynchronize(prof_ev_[i + 1]) != cudaSuccess) {
             err = "profile event failed";
@@ -1590,6 +1608,8 @@ int Engine::read_profile(double& conv_ms, double& conv_flops, long long& conv_la
         if (stg == 0) {
             conv_ms += ms;
             ++conv_launches;
+            conv_records.push_back(prof_conv_[i / 2]);
+            conv_records.back().ms = ms;
         }
     }
     prof_used_ = 0;

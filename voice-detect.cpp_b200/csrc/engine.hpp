@@ -335,11 +335,20 @@ private:
     // Event pairs are tagged with a stage: 0 conv, 1 FBank, 2 pooling (TSTP + FC +
     // L2), 3 other (element-wise adds), 4 CMN + stem.
     int prof_begin(cudaStream_t st, int stage = 0);  // returns event-pair index or -1
-    void prof_end(int idx, cudaStream_t st, double flops);
+    void prof_end(int idx, cudaStream_t st, double flops, const vdb_conv_args* conv = nullptr);
     std::vector<int> prof_stage_;
 public:
+    // One profiled conv launch: its duration, algorithmic FLOPs and shape.
+    struct ConvRecord {
+        double ms, flops;
+        int ic, oc, k, stride, f_out, t_out, batch, ic1, res, qpack;  // ic1 0: one segment
+    };
     // Per-stage summed launch durations (ms) of the last read_profile call.
     double stage_ms[5] = {0, 0, 0, 0, 0};
+    // The conv launches of the last read_profile call, in launch order.
+    std::vector<ConvRecord> conv_records;
+private:
+    std::vector<ConvRecord> prof_conv_;  // per event pair (stage 0 only meaningful)
 private:
 };
 

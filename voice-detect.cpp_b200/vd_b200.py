@@ -177,6 +177,8 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_embedding_dim.argtypes = [C.c_void_p]
         L.voicedetect_b200_sync.restype = C.c_int
         L.voicedetect_b200_sync.argtypes = [C.c_void_p]
+        L.voicedetect_b200_profile_convs.restype = C.c_int
+        L.voicedetect_b200_profile_convs.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         L.voicedetect_b200_release_cache.restype = C.c_int
         L.voicedetect_b200_release_cache.argtypes = [C.c_void_p]
         L.voicedetect_b200_profile.restype = C.c_int
@@ -332,6 +334,18 @@ class Model:
     def sync(self) -> None:
         if self._L.voicedetect_b200_sync(self.ctx) != 0:
             raise VoiceDetectError(self.last_error())
+
+    def profile_convs(self) -> list[dict]:
+        """The conv launches of the last profile read (profile_read), in order."""
+        n = self._L.voicedetect_b200_profile_convs(self.ctx, None, 0)
+        if n <= 0:
+            return []
+        buf = (C.c_double * (12 * n))()
+        self._L.voicedetect_b200_profile_convs(self.ctx, buf, n)
+        keys = ("ms", "flops", "ic", "oc", "k", "stride", "f_out", "t_out", "batch", "ic1",
+                "res", "qpack")
+        return [{k: (buf[12 * i + j] if j < 2 else int(buf[12 * i + j]))
+                 for j, k in enumerate(keys)} for i in range(n)]
 
     def release_cache(self) -> None:
         """Drops the captured CUDA graphs and the workspace (weights stay resident)."""
