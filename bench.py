@@ -1010,16 +1010,25 @@ def run_sweep(args) -> int:
         To, Fo = vd.out_extent(T, s), vd.out_extent(F, s)
         qp = kind.startswith("qp")
         icc = oc if kind == "down" else ic
+        wkw = {}
         if qp:
             rows = L.vdb_qpack_rows(B, T, F)
             x = torch.empty(rows, 128, dtype=torch.float16, device="cuda").normal_().relu_()
-            w = vd.qpack_weights(vd.pack_conv_weight(
-                (torch.randn(32, 32, 3, 3, device="cuda") * (2 / 288) ** 0.5).half()))
+            wt = (torch.randn(32, 9, 32, device="cuda") * (2 / 288) ** 0.5).half()
+            if args.sweep_q8:
+                q8, d8, _ = vd.q8_planes(wt)
+                w, dq = vd.qpack_q8(q8, d8)
+                wkw = dict(w0_scale=dq)
+            else:
+                w = vd.qpack_weights(wt)
             y = torch.empty_like(x)
         else:
             rows = L.vdb_phase_rows(B, T, F) if s == 2 else L.vdb_grid_rows(B, T, F)
             x = torch.empty(rows, icc, dtype=torch.float16, device="cuda").normal_().relu_()
             w = (torch.randn(oc, 9, icc, device="cuda") * (2 / (9 * icc)) ** 0.5).half()
+            if args.sweep_q8:
+                w, d8, _ = vd.q8_planes(w)
+                wkw = dict(w0_scale=d8)
             y = torch.empty(L.vdb_grid_rows(B, To, Fo), oc, dtype=torch.float16, device="cuda")
         b = torch.zeros(oc, device="cuda")
         tv = torch.full((B,), To, dtype=torch.int32, device="cuda")
@@ -1027,8 +1036,12 @@ def run_sweep(args) -> int:
         if kind == "down":
             x1 = torch.empty(L.vdb_phase_rows(B, 2 * To, 2 * Fo), ic // 2, dtype=torch.float16,
                              device="cuda").normal_().relu_()
-            kw = dict(x1=x1, w1=(torch.randn(oc, ic // 2, device="cuda") * 0.1).half(),
-                      stride1=2)
+            w1 = (torch.randn(oc, ic // 2, device="cuda") * 0.1).half()
+            if args.sweep_q8:
+                q1, d1, _ = vd.q8_planes(w1)
+                kw = dict(x1=x1, w1=q1, w1_scale=d1, stride1=2)
+            else:
+                kw = dict(x1=x1, w1=w1, stride1=2)
         elif kind == "id":
             kw = dict(x1=torch.empty_like(x).normal_().relu_(),
                       w1=torch.eye(oc, device="cuda").half(), stride1=1)
@@ -1038,6 +1051,7 @@ def run_sweep(args) -> int:
             kw = dict(residual=torch.empty_like(y).normal_().relu_())
         if qp:
             kw.update(qpack=True)
+        kw.update(wkw)
 
         def run():
             vd.conv(x, w, b, tv, batch=B, t_out=To, f_out=Fo, oc=oc, k0=3,
@@ -1222,6 +1236,8 @@ def main() -> int:
                     help="0 auto, else output columns per tile (divides oc)")
     ap.add_argument("--sweep-pair", type=int, default=0,
                     help="0 auto, 1 CTA pairs (cta_group::2), -1 off")
+    ap.add_argument("--sweep-q8", action="store_true",
+                    help="q8_0 weights (expanded in shared memory) instead of f16")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)

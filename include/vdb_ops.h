@@ -126,6 +126,20 @@ typedef struct vdb_conv_args {
                                w0 is the packed weight of vdb_qpack_pack_weights, residual
                                (optional) is added before the ReLU, y_phase 1 writes the
                                PHASE layout instead; no second segment */
+    /* q8_0 weights (NULL = f16 weights), 2-D convs only: w0 / w1 then hold int8 values
+       in the same layout as the f16 weights ([oc][k*k][ic], or the QPACK packing) and
+       w0_scale / w1_scale one f16 scale per 32 consecutive input channels of a tap
+       (the gguf q8_0 block: weight = q * scale), block-major: [k*k*ic / 32][oc] (QPACK:
+       one per packed row, [1152]). The segment's input channels must be a multiple of
+       32. Resident weights (the automatic halo feeds, weights <= 96 KB, and QPACK) are
+       expanded to f16 in each CTA's shared memory; streamed ones are expanded once per
+       launch into w_scratch (2 bytes per weight of those segments, 256-byte aligned;
+       stream-ordered, so one buffer serves every conv on a stream), then streamed as
+       f16. Either way the f16 values are f16(float(q) * float(scale)). */
+    const void* w0_scale;
+    const void* w1_scale;
+    void* w_scratch;
+    long long w_scratch_bytes;
 } vdb_conv_args;
 
 /* QPACK layout QP(B, T, F): the zero-bordered grid of G(B, T, F, 32) with four

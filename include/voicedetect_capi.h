@@ -122,6 +122,13 @@ int voicedetect_b200_set_bucketing(voicedetect_ctx* ctx, int max_clips, long lon
 /* GPU kernels launched by the last embed call on ctx. */
 long long voicedetect_b200_last_launches(voicedetect_ctx* ctx);
 
+/* Device bytes held by the ResNet block conv weights: f16 values, or q8_0 int8 values
+ * plus their f16 scales (q8_0 GGUF tensors stay q8_0 on the device: the convs with
+ * resident weights expand them in shared memory, the others into one f16 scratch the
+ * size of the largest conv, ~1.25 MB for ResNet34, not counted here), QPACK copies
+ * included; 0 for other models or NULL. No reference counterpart. */
+long long voicedetect_b200_conv_weight_bytes(voicedetect_ctx* ctx);
+
 /* Embedding dimension of the loaded model (0 for NULL). */
 int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx);
 

@@ -419,3 +419,101 @@ def test_conv_qpack_vs_reference(cuda_lib, case):
             assert torch.all(full[b, :, :, 1 + t:] == 0)
     rel = float((got - ref).norm() / max(ref.norm(), 1e-12))
     assert rel <= REL_L2_TOL, f"{name}: rel-L2 {rel:.3e}"
+
+
+Q8_CASES = [
+    # name, B, IC, OC, F, T, stride, second segment ("down" 1x1 s2 / "id" / None), kwargs
+    ("halo_resident_64", 3, 64, 64, 20, 24, 1, None, {}),
+    ("halo_streamed_128", 3, 128, 128, 10, 20, 1, None, {}),
+    ("pair_256", 3, 256, 256, 10, 12, 1, None, {}),
+    ("tap_s2_32_64", 3, 32, 64, 40, 30, 2, None, {}),
+    ("tap_forced_64", 3, 64, 64, 20, 24, 1, None, {"halo": -1}),
+    ("down_64", 3, 64, 64, 20, 24, 1, "down", {}),
+    ("id_128_mixed", 3, 128, 128, 10, 20, 1, "id", {}),
+    ("halo_s2_32_64", 3, 32, 64, 40, 30, 2, None, {"halo": 1}),
+    # several tiles per CTA: stages reused across tiles by q8_0 and f16 segments
+    ("id_128_multi", 64, 128, 128, 20, 75, 1, "id", {}),
+    ("pair_id_256_multi", 256, 256, 256, 10, 38, 1, "id", {}),
+    ("down_64_multi", 64, 64, 64, 40, 150, 1, "down", {}),
+    ("tap_s2_64_128_multi", 64, 64, 128, 40, 150, 2, None, {}),
+    ("down_256_pair_multi", 256, 256, 256, 10, 38, 1, "down", {}),
+]
+
+
+@pytest.mark.parametrize("case", Q8_CASES, ids=[c[0] for c in Q8_CASES])
+def test_conv_q8_weights_equal_their_f16_expansion(cuda_lib, case):
+    """q8_0 weights (int8 values + an f16 scale per 32 input channels) expanded in
+    shared memory give bit-identical outputs to the same conv fed the f16 weights
+    f16(q * d): every weight feed (resident halo, streamed halo, CTA pairs, one tap per
+    stage, the 1x1 downsample segment; an f16 identity segment beside a q8_0 one)."""
+    import torch
+    vd = cuda_lib
+    name, B, IC, OC, F, T, stride, seg1, kw = case
+    g = torch.Generator().manual_seed(7)
+    dev = "cuda"
+    To, Fo = vd.out_extent(T, stride), vd.out_extent(F, stride)
+    tv = ([To, max(1, To // 2), 1] * B)[:B]
+    x = _h(torch.relu(torch.randn(B, IC, F, T, generator=g)))
+    xg = (vd.to_phase if stride == 2 else vd.to_grid)(x.to(dev))
+    w = torch.randn(OC, 9, IC, generator=g) * (2.0 / (9 * IC)) ** 0.5
+    q, d, w16 = vd.q8_planes(w.to(dev))
+    bias = (torch.randn(OC, generator=g) * 0.1).to(dev)
+    tvd = torch.tensor(tv, dtype=torch.int32, device=dev)
+    extra_f16, extra_q8 = {}, {}
+    if seg1 == "down":
+        x1 = vd.to_phase(_h(torch.relu(torch.randn(B, IC // 2, 2 * Fo, 2 * To, generator=g))).to(dev))
+        w1 = torch.randn(OC, IC // 2, generator=g) * 0.1
+        q1, d1, w1_16 = vd.q8_planes(w1.to(dev))
+        extra_f16 = dict(x1=x1, w1=w1_16, stride1=2)
+        extra_q8 = dict(x1=x1, w1=q1, w1_scale=d1, stride1=2)
+    elif seg1 == "id":
+        x1 = vd.to_grid(_h(torch.relu(torch.randn(B, OC, Fo, To, generator=g))).to(dev))
+        eye = torch.eye(OC, device=dev).half()
+        extra_f16 = dict(x1=x1, w1=eye, stride1=1)
+        extra_q8 = dict(x1=x1, w1=eye, stride1=1)
+    args = dict(batch=B, t_out=To, f_out=Fo, oc=OC, k0=3, stride0=stride, ic0=IC, relu=True, **kw)
+    y16 = vd.conv(xg, w16, bias, tvd, **args, **extra_f16)
+    y8 = vd.conv(xg, q, bias, tvd, w0_scale=d, **args, **extra_q8)
+    torch.cuda.synchronize()
+    assert torch.equal(y8, y16), (name, (y8.float() - y16.float()).abs().max().item())
+    assert y16.float().abs().sum().item() > 0
+
+
+def test_conv_qpack_q8_weights_equal_their_f16_expansion(cuda_lib):
+    """The QPACK stage-1 conv with q8_0 packed weights (expanded once per CTA) equals
+    the same conv on the f16 packed weights, with the residual and both outputs."""
+    import torch
+    vd = cuda_lib
+    B, F, T, dev = 4, 80, 41, "cuda"
+    g = torch.Generator().manual_seed(11)
+    tv = torch.tensor([41, 30, 7, 1], dtype=torch.int32, device=dev)
+    x = vd.to_qpack(_h(torch.relu(torch.randn(B, 32, F, T, generator=g))).to(dev))
+    r = vd.to_qpack(_h(torch.relu(torch.randn(B, 32, F, T, generator=g))).to(dev))
+    w = torch.randn(32, 9, 32, generator=g) * (2.0 / 288) ** 0.5
+    q, d, w16 = vd.q8_planes(w.to(dev))
+    wq16 = vd.qpack_weights(w16)
+    qq, dq = vd.qpack_q8(q, d)
+    bias = (torch.randn(32, generator=g) * 0.1).to(dev)
+    L = vd.lib()
+    for y_phase in (0, 1):
+        kw = dict(batch=B, t_out=T, f_out=F, oc=32, k0=3, ic0=32, relu=True, qpack=True,
+                  residual=r, y_phase=y_phase)
+        # the PHASE output has slots the conv never writes: start both from zeros
+        shape = (L.vdb_phase_rows(B, T, F), 32) if y_phase else tuple(x.shape)
+        y16 = vd.conv(x, wq16, bias, tv, y=torch.zeros(shape, dtype=torch.float16, device=dev), **kw)
+        y8 = vd.conv(x, qq, bias, tv, w0_scale=dq,
+                     y=torch.zeros(shape, dtype=torch.float16, device=dev), **kw)
+        torch.cuda.synchronize()
+        assert torch.equal(y8, y16), y_phase
+
+
+def test_conv_q8_rejects_bad_channel_counts(cuda_lib):
+    import torch
+    vd = cuda_lib
+    dev = "cuda"
+    x = torch.zeros(vd.lib().vdb_grid_rows(1, 8, 8), 16, dtype=torch.float16, device=dev)
+    q = torch.zeros(16, 9, 16, dtype=torch.int8, device=dev)
+    d = torch.ones(16, 9, 1, dtype=torch.float16, device=dev)
+    tv = torch.tensor([8], dtype=torch.int32, device=dev)
+    with pytest.raises(RuntimeError, match="multiple of 32"):
+        vd.conv(x, q, None, tv, batch=1, t_out=8, f_out=8, oc=16, k0=3, ic0=16, w0_scale=d)

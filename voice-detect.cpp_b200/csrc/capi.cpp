@@ -494,6 +494,10 @@ extern "C" long long voicedetect_b200_last_launches(voicedetect_ctx* ctx) {
     return (ctx && ctx->engine) ? ctx->engine->last_launches : 0;
 }
 
+extern "C" long long voicedetect_b200_conv_weight_bytes(voicedetect_ctx* ctx) {
+    return (ctx && ctx->engine) ? ctx->engine->conv_weight_bytes : 0;
+}
+
 extern "C" int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx) {
     return (ctx && ctx->engine) ? ctx->engine->emb_dim() : 0;
 }

@@ -93,6 +93,12 @@ struct SegDev {
     int n_box, box_rows;  // TMA A boxes per stage and their height (TAP: BM split in <= 256)
     uint32_t bres;   // HALO: resident weights, byte offset from the smem base
     uint32_t a_bytes, b_bytes;  // two-ring pipeline: A bytes per channel block, weight bytes per tap
+    // q8_0 resident weights (wq != nullptr): int8 values in the f16 layout [oc][wk]
+    // (wk = taps * ic, K-major) and one f16 scale per 32 of them, [wk / 32][wn] (wn =
+    // oc); every CTA expands them to f16 in shared memory once
+    const int8_t* wq;
+    const __half* wd;
+    int wk, wn;
 };
 
 struct ConvDev {
@@ -102,6 +108,7 @@ struct ConvDev {
     int n_seg;
     SegDev seg[2];
     uint32_t stage0, stage_bytes, a_region, n_stages, tmem_cols, bres_bytes;
+    uint32_t bres_tx;  // resident weight bytes loaded by TMA (the rest are q8_0-expanded)
     // two-ring pipeline (HALO_S): ra A slots of a_stride bytes from stage0, then rb
     // weight slots of b_stride bytes from b_ring0; barriers [0, ra) are the A
     // ring's, [ra, ra + rb) the weight ring's.
@@ -594,6 +601,66 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
     }
 }
 
+// ---- q8_0 weights ------------------------------------------------------------
+// 8 int8 values (two 32-bit words) times the f16 scale d as 8 f16, each the exact
+// product q * d rounded once to nearest: the same bits as converting float(q) *
+// float(d) (exact in f32) to f16 on the host. q becomes f16 exactly by the byte-plane
+// construction 0x64 : (q + 128) = the f16 1024 + q + 128, minus 1152 (0x6480).
+__device__ __forceinline__ uint4 q8_to_f16x8(uint2 q, __half d) {
+    const uint32_t x0 = q.x ^ 0x80808080u, x1 = q.y ^ 0x80808080u;
+    uint32_t w[4] = {__byte_perm(x0, 0x64646464u, 0x5140), __byte_perm(x0, 0x64646464u, 0x5342),
+                     __byte_perm(x1, 0x64646464u, 0x5140), __byte_perm(x1, 0x64646464u, 0x5342)};
+    const __half2 off2 = __half2half2(__ushort_as_half((unsigned short)0x6480));
+    const __half2 d2 = __half2half2(d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&w[i]), off2), d2);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Rows [row0, row0 + R) x channels [k0, k0 + kb) of a q8_0 segment's weights, expanded
+// into the f16 tile at shared address dst as TMA would have written it: rows of 2*kb
+// bytes with the kb-dependent swizzle (16-byte chunk bits [4, 7) XOR address bits
+// [7, 10), masked to the swizzle width). Threads t, t + nt, ... of the caller.
+__device__ __forceinline__ void q8_expand(const SegDev& s, int kb, int row0, int R, int k0,
+                                          uint32_t dst, int t, int nt) {
+    const int cpr = kb >> 3;  // 16-byte chunks per row
+    const int sh = cpr == 8 ? 3 : (cpr == 4 ? 2 : 1);
+    const uint32_t mask = kb == 64 ? 7u : (kb == 32 ? 3u : 1u);
+    for (int i = t; i < R * cpr; i += nt) {
+        const int r = i >> sh, j = i & (cpr - 1);
+        const long long row = (long long)row0 + r;
+        const int k = k0 + 8 * j;
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(s.wq + row * s.wk + k));
+        const __half d = s.wd[(long long)(k >> 5) * s.wn + row];
+        const uint4 o = q8_to_f16x8(q, d);
+        const uint32_t off = (uint32_t)(r * kb * 2 + 16 * j);
+        st_shared_v4(dst + (off ^ (((off >> 7) & mask) << 4)), o.x, o.y, o.z, o.w);
+    }
+}
+
+// Streamed q8_0 weights: one pass per launch expands the segment's int8 values and
+// scales into f16 [oc][K] in a scratch buffer (L2-resident, at most a few MB), which the
+// conv then streams by TMA like f16 weights. Expanding them per stage in shared memory
+// instead measured 2-4x slower on those convs: the expansion's shared-memory traffic
+// (8 KB read + 16 KB written per stage, repeated for every M tile) competes with the
+// tensor cores' operand fetch for shared-memory bandwidth.
+__global__ void __launch_bounds__(256)
+q8_dequant_kernel(const int8_t* __restrict__ q, const __half* __restrict__ d, int oc, int K,
+                  __half* __restrict__ out) {
+    const long long n8 = (long long)oc * K / 8;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long e = i * 8;
+        const int row = (int)(e / K), k = (int)(e - (long long)row * K);
+        const uint2 qq = __ldg(reinterpret_cast<const uint2*>(q + e));
+        const __half dd = d[(long long)(k >> 5) * oc + row];
+        *reinterpret_cast<uint4*>(out + e) = q8_to_f16x8(qq, dd);
+    }
+}
+
 // ---- QPACK ------------------------------------------------------------------
 // A stage-1 conv (3x3, stride 1, 32 -> 32) over QPACK rows: row (b, t', q) holds the
 // four padded frequency pixels f' = 4q + j (j = 0..3) x 32 channels. Output pixel
@@ -944,6 +1011,31 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         if constexpr (PAIR) tmem_alloc_pair(smem_u32(tmem_slot), p.tmem_cols);
         else tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
     }
+    // resident q8_0 weights: every thread expands its share once (the weights predate
+    // this kernel, so this may overlap the previous one's tail)
+    {
+        bool wrote = false;
+        if (QP) {
+            if (p.seg[0].wq) {
+                // the packed rows: 32 channels (64 bytes, 64-byte swizzle) each
+                q8_expand(p.seg[0], 32, 0, 1152, 0, base + p.seg[0].bres, threadIdx.x, blockDim.x);
+                wrote = true;
+            }
+        } else {
+            for (int sg = 0; sg < p.n_seg; ++sg) {
+                const SegDev& s = p.seg[sg];
+                if (s.mode != SEG_HALO || !s.wq) continue;
+                const uint32_t box = (uint32_t)p.BN * s.kb * 2;
+                for (int tap = 0; tap < s.n_taps; ++tap)
+                    for (int kbi = 0; kbi < s.n_kb; ++kbi)
+                        q8_expand(s, s.kb, 0, p.BN, tap * s.ic + kbi * s.kb,
+                                  base + s.bres + (uint32_t)(tap * s.n_kb + kbi) * box,
+                                  threadIdx.x, blockDim.x);
+                wrote = true;
+            }
+        }
+        if (wrote) fence_proxy_async_smem();  // generic writes -> the tensor cores' view
+    }
     tc_fence_before();
     if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any signal
     else __syncthreads();
@@ -966,14 +1058,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             // Resident weights of HALO segments: every (tap, channel block) box once.
             if (QP) {
                 // QPACK: the packed weights, 9 boxes of 128 rows x 32 channels
-                mbar_arrive_expect_tx(bar_bres, p.bres_bytes);
-                for (int r = 0; r < 1152; r += 128)
-                    tma_load_2d(base + p.seg[0].bres + (uint32_t)r * 64u, &tmB0, bar_bres, 0, r);
-            } else if (p.bres_bytes) {
-                mbar_arrive_expect_tx(bar_bres, p.bres_bytes);
+                if (p.bres_tx) {
+                    mbar_arrive_expect_tx(bar_bres, p.bres_tx);
+                    for (int r = 0; r < 1152; r += 128)
+                        tma_load_2d(base + p.seg[0].bres + (uint32_t)r * 64u, &tmB0, bar_bres, 0, r);
+                }
+            } else if (p.bres_tx) {
+                mbar_arrive_expect_tx(bar_bres, p.bres_tx);
                 for (int sg = 0; sg < p.n_seg; ++sg) {
                     const SegDev& s = p.seg[sg];
-                    if (s.mode != SEG_HALO) continue;
+                    if (s.mode != SEG_HALO || s.wq) continue;
                     const CUtensorMap* tb = sg ? &tmB1 : &tmB0;
                     const uint32_t box = (uint32_t)p.BN * s.kb * 2;
                     for (int tap = 0; tap < s.n_taps; ++tap)
@@ -1118,7 +1212,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             [[maybe_unused]] const uint32_t qp_idn[3] = {umma_idesc_f16(kMB, 32), umma_idesc_f16(kMB, 64),
                                                          umma_idesc_f16(kMB, 96)};
             bool ok = true, issued = false;
-            if (p.bres_bytes &&
+            if (p.bres_tx &&
                 !mbar_wait(bar_bres, 0, p.err, VDB_ERR_TIMEOUT_FULL, abort_flag))
                 ok = false;
             for (int tile = first_tile<PAIR>(); tile < n_tiles && ok; tile += tile_stride<PAIR>()) {
@@ -1581,7 +1675,15 @@ extern "C" long long vdb_phase_rows(int batch, int t, int f) {
     return 4LL * batch * (to + 2) * (fo + 2);
 }
 
+namespace vdb {
+namespace {
+thread_local int g_conv_launches = 0;
+}
+int last_conv_launches() { return g_conv_launches; }
+}  // namespace vdb
+
 extern "C" int vdb_conv(const vdb_conv_args* a, void* stream) {
+    g_conv_launches = 1;
     if (!a) {
         set_error("vdb_conv: NULL args");
         return 1;
@@ -1627,6 +1729,7 @@ extern "C" long long vdb_seq_rows(int batch, int t, int pad) {
 }
 
 extern "C" int vdb_conv1d(const vdb_conv1d_args* c, void* stream) {
+    g_conv_launches = 1;
     if (!c) {
         set_error("vdb_conv1d: NULL args");
         return 1;
@@ -1962,6 +2065,18 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     p.BM = BM;
     p.n_mblk = pair ? 1 : BM / kMB;
     p.n_iss = (!seq && !pair && p.n_mblk >= 2) ? 2 : 1;
+    // q8_0 weights (2-D convs): an f16 scale per 32 input channels of a tap
+    const void* wsc[2] = {a->w0_scale, a->x1 ? a->w1_scale : nullptr};
+    if (wsc[0] || wsc[1]) {
+        if (seq) {
+            set_error("vdb_conv1d: q8_0 weights are supported by the 2-D conv only");
+            return 1;
+        }
+        if ((wsc[0] && a->ic0 % 32) || (wsc[1] && a->ic1 % 32)) {
+            set_error("vdb_conv: q8_0 weights need input channels that are a multiple of 32");
+            return 1;
+        }
+    }
     p.J = J;
     p.n_acc = (2 * p.n_mblk * J * BN <= 512) ? 2 : 1;
     const int cta_rows = pair ? kMB : BM;   // A rows one CTA loads per stage
@@ -2006,6 +2121,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             const uint32_t w = (uint32_t)s.n_taps * s.n_kb * BN * row_bytes;
             off += w;
             p.bres_bytes += w;
+            if (!wsc[sg]) p.bres_tx += w;  // q8_0 weights are expanded, not loaded
             a_bytes = std::max(a_bytes, (uint32_t)(s.halo_planes - 1) * s.plane_bytes + one);
         } else {
             s.mode = SEG_TAP;
@@ -2017,6 +2133,30 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
             a_bytes = std::max(a_bytes, (uint32_t)cta_rows * row_bytes);
             b_bytes = std::max(b_bytes, (uint32_t)cta_bn * row_bytes);
         }
+    }
+    // q8_0 segments: resident (HALO) weights are expanded to f16 in shared memory by
+    // every CTA (q8_expand); streamed ones are expanded once for this launch into the
+    // caller's scratch (q8_dequant_kernel, below) and then streamed as f16
+    const void* wseg[2] = {a->w0, a->x1 ? a->w1 : nullptr};
+    size_t scratch_need[2] = {0, 0};
+    for (int sg = 0; sg < p.n_seg; ++sg) {
+        SegDev& s = p.seg[sg];
+        if (!wsc[sg]) continue;
+        if (s.mode == SEG_HALO) {
+            s.wq = static_cast<const int8_t*>(wseg[sg]);
+            s.wd = static_cast<const __half*>(wsc[sg]);
+            s.wk = s.n_taps * s.ic;
+            s.wn = a->oc;
+        } else {
+            scratch_need[sg] = (size_t)round_up(a->oc * s.n_taps * s.ic * 2, 256);
+        }
+    }
+    if (scratch_need[0] + scratch_need[1] > 0 &&
+        (!a->w_scratch || (long long)(scratch_need[0] + scratch_need[1]) > a->w_scratch_bytes ||
+         (reinterpret_cast<uintptr_t>(a->w_scratch) & 255u))) {
+        set_error("vdb_conv: q8_0 weights this conv streams need w_scratch (256-byte aligned) "
+                  "of at least 2 bytes per weight of those segments");
+        return 1;
     }
     off = (uint32_t)round_up((int)off, 1024);
     p.stage0 = off;
@@ -2158,21 +2298,40 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     // 4 planes of a PHASE tensor, each shaped like the output grid.
     const long long rows_out = p.M;
     CUtensorMap tm[5];
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int sg = 0; sg < p.n_seg; ++sg) {
+        if (!scratch_need[sg]) continue;
+        const SegDev& s = p.seg[sg];
+        __half* dst = reinterpret_cast<__half*>(static_cast<char*>(a->w_scratch) +
+                                                (sg ? scratch_need[0] : 0));
+        const int K = s.n_taps * s.ic;
+        const long long n8 = (long long)a->oc * K / 8;
+        const int blocks = (int)std::min<long long>((n8 + 255) / 256, (long long)num_sms() * 8);
+        q8_dequant_kernel<<<blocks, 256, 0, st>>>(static_cast<const int8_t*>(wseg[sg]),
+                                                   static_cast<const __half*>(wsc[sg]), a->oc, K,
+                                                   dst);
+        VDB_CHECK_CUDA(cudaGetLastError());
+        ++g_conv_launches;
+        wseg[sg] = dst;  // this segment streams the f16 expansion
+    }
     for (int sg = 0; sg < p.n_seg; ++sg) {
         const SegDev& s = p.seg[sg];
         const void* x = sg ? a->x1 : a->x0;
-        const void* w = sg ? a->w1 : a->w0;
+        const void* w = wseg[sg];
         const int stride = sg ? a->stride1 : a->stride0;
         const int box_rows = s.box_rows;
         const int ldx = sg ? (a->ldx1 ? a->ldx1 : a->ic1) : (a->ldx0 ? a->ldx0 : a->ic0);
         // planes: PHASE 4, FPHASE 2 (2-D stride 3), TPHASE 2 (1-D stride 2)
         const int planes = seq ? ((sg == 0 && sq->stride0 == 2) ? 2 : 1)
                                : (stride == 2 ? 4 : (stride == 3 ? 2 : 1));
+        // q8_0 resident weights are expanded from global memory (no weight map)
+        const bool q8_res = s.wq != nullptr;
         if (!make_map_a(&tm[2 * sg], x, s.ic, ldx, rows_out, planes, s.kb, box_rows) ||
-            !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, cta_bn, s.kb)) {
+            (!q8_res && !make_map_b(&tm[2 * sg + 1], w, s.n_taps * s.ic, a->oc, cta_bn, s.kb))) {
             set_error("vdb_conv: cuTensorMapEncodeTiled failed");
             return 1;
         }
+        if (q8_res) tm[2 * sg + 1] = tm[2 * sg];
     }
     if (p.n_seg == 1) {
         tm[2] = tm[0];
@@ -2191,7 +2350,6 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const int n_tiles = p.n_mt * p.n_nt;
     const int grid = pair ? 2 * std::max(1, std::min(n_tiles, num_sms() / 2))
                           : std::max(1, std::min(n_tiles, num_sms()));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto launch = [&](auto kern) -> int {
         // The shared-memory opt-in. While a stream is being captured into a CUDA graph
         // it is skipped: the engine captures a bucket only after launching it plainly
@@ -2340,6 +2498,15 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     s.bytes = (uint32_t)s.n_box * s.box_rows * 128u;
     s.bres = 0;
     p.bres_bytes = 1152u * 64u;  // 3 x 384 rows of 32 channels
+    if (a->w0_scale) {
+        // q8_0: one f16 scale per packed row (32 channels), expanded once per CTA
+        s.wq = static_cast<const int8_t*>(a->w0);
+        s.wd = static_cast<const __half*>(a->w0_scale);
+        s.wk = 32;
+        s.wn = 1152;  // scales [1][1152]: one per packed row
+    } else {
+        p.bres_tx = p.bres_bytes;
+    }
     uint32_t off = p.bres_bytes;   // 72 KB: 1024-byte aligned
     p.stage0 = off;
     p.a_region = (uint32_t)round_up((int)s.bytes, 1024);
@@ -2397,10 +2564,11 @@ int conv_qpack_impl(const vdb_conv_args* a, void* stream) {
     p.qp_res = static_cast<const __half*>(a->residual);
     CUtensorMap tm[5];
     if (!make_map_a(&tm[0], a->x0, 128, 128, rows, 1, 64, s.box_rows) ||
-        !make_map_b(&tm[1], a->w0, 32, 1152, 128, 32)) {
+        (!s.wq && !make_map_b(&tm[1], a->w0, 32, 1152, 128, 32))) {
         set_error("vdb_conv: cuTensorMapEncodeTiled failed");
         return 1;
     }
+    if (s.wq) tm[1] = tm[0];  // q8_0 weights are expanded, not loaded by TMA
     tm[2] = tm[0];
     tm[3] = tm[1];
     if (staged) {

@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <thread>
@@ -24,6 +25,49 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restri
 struct Loader {
     const Gguf& g;
     std::string& err;
+
+    bool is_q8(const std::string& name) const {
+        const GgufTensor* t = g.tensor(name);
+        return t && t->type == GGML_Q8_0;
+    }
+
+    // A q8_0 conv tensor as stored (OHWI, ne = [IC, KW, KH, OC], 32-element blocks
+    // along IC), split into its int8 values in the packed tap layout of pack_taps,
+    // [oc][kw*k + kh][ic] (tap = time tap * k + frequency tap), and its f16 scale bits
+    // block-major, [(kw*k + kh) * ic / 32 + block][oc] (the conv's w_scale layout).
+    bool conv_q8(const std::string& name, std::vector<int8_t>& q, std::vector<uint16_t>& d,
+                 int& oc, int& ic, int& k) {
+        const GgufTensor* t = g.tensor(name);
+        if (!t || t->type != GGML_Q8_0) {
+            err = "tensor '" + name + "' is not q8_0";
+            return false;
+        }
+        std::vector<int64_t> ne = t->ne;
+        while (ne.size() < 4) ne.push_back(1);
+        ic = (int)ne[0];
+        k = (int)ne[1];
+        oc = (int)ne[3];
+        const int64_t n = t->nelements();
+        if (ne[2] != ne[1] || ic % 32 != 0 || (size_t)(n / 32) * 34 > t->nbytes) {
+            err = "tensor '" + name + "': q8_0 conv weight must be [IC, K, K, OC], IC % 32 == 0";
+            return false;
+        }
+        q.resize((size_t)n);
+        d.resize((size_t)(n / 32));
+        const int nbk = ic / 32;  // blocks per (oc, kh, kw)
+        for (int o = 0; o < oc; ++o)
+            for (int kh = 0; kh < k; ++kh)
+                for (int kw = 0; kw < k; ++kw)
+                    for (int c = 0; c < nbk; ++c) {
+                        const int64_t src = (((int64_t)o * k + kh) * k + kw) * nbk + c;
+                        const int64_t kblk = ((int64_t)kw * k + kh) * nbk + c;  // K block
+                        const int64_t dst = (int64_t)o * k * k * nbk + kblk;
+                        const uint8_t* blk = t->data + src * 34;
+                        std::memcpy(&d[(size_t)(kblk * oc + o)], blk, 2);
+                        std::memcpy(&q[(size_t)dst * 32], blk + 2, 32);
+                    }
+        return true;
+    }
 
     // Conv weight as torch-order f32 [OC][IC][K][K]. f32/f16 tensors use the
     // reference's ggml layout ne = [KW, KH, IC, OC] (src/encoder_resnet.cpp:16-20);
@@ -113,6 +157,27 @@ std::vector<float> pack_qpack(const std::vector<float>& taps) {
         }
     }
     return out;
+}
+
+// The same packing of q8_0 weights: rows of 32 int8 values (one q8_0 block) and their
+// scales (one per packed row), from the [oc][9][32] tap layout and its block-major
+// scales [tap][oc].
+void pack_qpack_q8(const std::vector<int8_t>& q, const std::vector<uint16_t>& d,
+                   std::vector<int8_t>& pq, std::vector<uint16_t>& pd) {
+    pq.assign((size_t)1152 * 32, 0);
+    pd.assign(1152, 0);
+    for (int kt = 0; kt < 3; ++kt) {
+        int row = kt * 384;
+        for (int u = -1; u <= 4; ++u) {
+            const int jmin = std::max(0, u - 1), jmax = std::min(3, u + 1);
+            for (int j = jmin; j <= jmax; ++j)
+                for (int oc = 0; oc < 32; ++oc, ++row) {
+                    const size_t tap = (size_t)kt * 3 + (u - j + 1);
+                    std::memcpy(&pq[(size_t)row * 32], &q[((size_t)oc * 9 + tap) * 32], 32);
+                    pd[(size_t)row] = d[tap * 32 + oc];
+                }
+        }
+    }
 }
 
 inline int frames_of(int n, int win, int hop) { return n >= win ? 1 + (n - win) / hop : 0; }
@@ -270,8 +335,27 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
     auto upload = [&](const std::vector<float>& v, float** dst) -> bool {
         return e->upload_f32(v, dst, err);
     };
-    auto upload_h = [&](const std::vector<float>& v, __half** dst) -> bool {
-        return e->upload_f16(v, dst, err);
+    auto upload_h = [&](const std::vector<float>& v, void** dst) -> bool {
+        __half* h = nullptr;
+        if (!e->upload_f16(v, &h, err)) return false;
+        *dst = h;
+        e->conv_weight_bytes += (long long)v.size() * 2;
+        return true;
+    };
+    // q8_0 conv tensors stay q8_0 on the device (int8 values + f16 scales, expanded in
+    // the conv kernel's shared memory) unless VDB_Q8_WIDEN=1 asks for f16 weights
+    // widened on the host (the same f16 values either way)
+    const char* widen = std::getenv("VDB_Q8_WIDEN");
+    const bool q8_dev = !(widen && widen[0] == '1');
+    auto upload_q8 = [&](const std::vector<int8_t>& q, const std::vector<uint16_t>& d, void** dq,
+                         const void** dd) -> bool {
+        void* ps = nullptr;
+        if (!e->upload_bytes(q.data(), q.size(), dq, err) ||
+            !e->upload_bytes(d.data(), d.size() * 2, &ps, err))
+            return false;
+        *dd = ps;
+        e->conv_weight_bytes += (long long)q.size() + (long long)d.size() * 2;
+        return true;
     };
 
     // ResNet manifest, src/model_loader.cpp:138-152.
@@ -331,31 +415,67 @@ std::unique_ptr<Engine> Engine::load(const std::string& path, std::string& err) 
                 return nullptr;
             }
             for (int o = 0; o < oc; ++o) b2[o] += bd[o];  // both biases land in one epilogue
-            if (!upload_h(wd, &blk.wd)) return nullptr;
+            if (q8_dev && L.is_q8(dw[i]) && ic % 32 == 0) {
+                std::vector<int8_t> q;
+                std::vector<uint16_t> d;
+                int o2, i2, k2d;
+                if (!L.conv_q8(dw[i], q, d, o2, i2, k2d) || !upload_q8(q, d, &blk.wd, &blk.wds))
+                    return nullptr;
+            } else if (!upload_h(wd, &blk.wd)) {
+                return nullptr;
+            }
         } else if (ic != oc || blk.stride != 1) {
             err = "block " + std::to_string(i) + ": identity shortcut needs equal shapes";
             return nullptr;
         } else {
             const __half* eye = e->identity(oc, err);
             if (!eye) return nullptr;
-            blk.wd = const_cast<__half*>(eye);
+            blk.wd = const_cast<__half*>(eye);  // f16 (wds stays null)
             blk.identity = true;
         }
         if (ic % 16 != 0 || oc % 16 != 0) {
             err = "block channels must be multiples of 16";
             return nullptr;
         }
-        const std::vector<float> t1 = pack_taps(w1, oc, ic, 3), t2 = pack_taps(w2, oc, oc, 3);
-        if (!upload_h(t1, &blk.w1) || !upload(b1, &blk.b1) || !upload_h(t2, &blk.w2) ||
-            !upload(b2, &blk.b2))
-            return nullptr;
-        if (ic == 32 && oc == 32 && blk.stride == 1 && blk.identity)
-            if (!upload_h(pack_qpack(t1), &blk.w1q) || !upload_h(pack_qpack(t2), &blk.w2q))
+        const bool qp_blk = ic == 32 && oc == 32 && blk.stride == 1 && blk.identity;
+        if (!upload(b1, &blk.b1) || !upload(b2, &blk.b2)) return nullptr;
+        if (q8_dev && L.is_q8(c1w[i]) && L.is_q8(c2w[i]) && ic % 32 == 0 && oc % 32 == 0) {
+            std::vector<int8_t> q1, q2;
+            std::vector<uint16_t> d1, d2;
+            int o_, i_, k_;
+            if (!L.conv_q8(c1w[i], q1, d1, o_, i_, k_) || !L.conv_q8(c2w[i], q2, d2, o_, i_, k_) ||
+                !upload_q8(q1, d1, &blk.w1, &blk.w1s) || !upload_q8(q2, d2, &blk.w2, &blk.w2s))
                 return nullptr;
+            if (qp_blk) {
+                std::vector<int8_t> pq;
+                std::vector<uint16_t> pd;
+                pack_qpack_q8(q1, d1, pq, pd);
+                if (!upload_q8(pq, pd, &blk.w1q, &blk.w1qs)) return nullptr;
+                pack_qpack_q8(q2, d2, pq, pd);
+                if (!upload_q8(pq, pd, &blk.w2q, &blk.w2qs)) return nullptr;
+            }
+        } else {
+            const std::vector<float> t1 = pack_taps(w1, oc, ic, 3), t2 = pack_taps(w2, oc, oc, 3);
+            if (!upload_h(t1, &blk.w1) || !upload_h(t2, &blk.w2)) return nullptr;
+            if (qp_blk)
+                if (!upload_h(pack_qpack(t1), &blk.w1q) || !upload_h(pack_qpack(t2), &blk.w2q))
+                    return nullptr;
+        }
         e->blocks_.push_back(blk);
         if (blk.stride == 2) F = half_extent(F);
         cin = oc;
     }
+    // scratch for the f16 expansion of streamed q8_0 weights (both segments of the
+    // largest block conv)
+    for (const ResBlockDev& b : e->blocks_) {
+        if (!b.w1s && !b.w2s) continue;
+        const long long need = 2LL * b.oc * 9 * std::max(b.ic, b.oc) + 256 + 2LL * b.oc * b.ic + 256;
+        e->wscratch_bytes_ = std::max(e->wscratch_bytes_, need);
+    }
+    if (e->wscratch_bytes_ > 0 &&
+        !e->upload_bytes(std::vector<uint8_t>((size_t)e->wscratch_bytes_).data(),
+                         (size_t)e->wscratch_bytes_, &e->wscratch_, err))
+        return nullptr;
     for (size_t i = 0; i < nb; ++i)
         if (e->blocks_[i].stride == 2 && i == 0) {
             err = "the first block may not be strided";
@@ -452,6 +572,19 @@ bool Engine::upload_f16(const std::vector<float>& v, __half** dst, std::string& 
     }
     weight_allocs_.push_back(p);
     *dst = static_cast<__half*>(p);
+    return true;
+}
+
+bool Engine::upload_bytes(const void* src, size_t n, void** dst, std::string& err) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, n) != cudaSuccess ||
+        cudaMemcpy(p, src, n, cudaMemcpyHostToDevice) != cudaSuccess) {
+        err = "weight upload failed";
+        if (p) cudaFree(p);
+        return false;
+    }
+    weight_allocs_.push_back(p);
+    *dst = p;
     return true;
 }
 
@@ -1077,6 +1210,9 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         a.ic0 = blk.ic;
         a.x0 = x;
         a.w0 = qp ? blk.w1q : blk.w1;
+        a.w0_scale = qp ? blk.w1qs : blk.w1s;
+        a.w_scratch = wscratch_;
+        a.w_scratch_bytes = wscratch_bytes_;
         a.bias = blk.b1;
         a.relu = 1;
         a.tvalid = tv_out;
@@ -1090,6 +1226,7 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
             err = vdb_last_error();
             return 1;
         }
+        launches += last_conv_launches();
         prof_end(pe, st, 2.0 * blk.oc * blk.ic * 9 * valid_px, &a);
         vdb_conv_args c2{};
         c2.batch = B;
@@ -1101,6 +1238,9 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
         c2.ic0 = blk.oc;
         c2.x0 = Lo.g[h_slot];
         c2.w0 = qp ? blk.w2q : blk.w2;
+        c2.w0_scale = qp ? blk.w2qs : blk.w2s;
+        c2.w_scratch = wscratch_;
+        c2.w_scratch_bytes = wscratch_bytes_;
         c2.bias = blk.b2;
         c2.relu = 1;
         c2.tvalid = tv_out;
@@ -1114,6 +1254,7 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
             // 1x1 downsample, or the identity shortcut, as input segment 1
             c2.x1 = x;
             c2.w1 = blk.wd;
+            c2.w1_scale = blk.wds;
             c2.ic1 = blk.ic;
             c2.stride1 = blk.stride;
         }
@@ -1124,11 +1265,11 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
             err = vdb_last_error();
             return 1;
         }
+        launches += last_conv_launches();
         prof_end(pe, st,
                  2.0 * blk.oc * blk.oc * 9 * valid_px +
                      (blk.identity ? 0.0 : 2.0 * blk.oc * blk.ic * valid_px),
                  &c2);
-        launches += 2;
         lev = lev_out;
         T = To;
         F = Fo;
@@ -1220,7 +1361,7 @@ int Engine::run_eres2net(int B, int t_max, const std::vector<long long>& tv_sum,
             return 1;
         }
         prof_end(pe, st, s.flops_px * (double)Fo * (double)tv_sum[s.level], &a);
-        ++launches;
+        launches += last_conv_launches();
     }
     const int lev = e_out_level_;
     const int pp = prof_begin(st, 2);

@@ -32,18 +32,26 @@ struct EngineConfig {
     bool cmn = true;
 };
 
+// Conv weights are f16, or (q8_0 GGUF tensors) int8 values in the same layout with an
+// f16 scale per 32 input channels of a tap (the `...s` pointers, null for f16); the
+// conv kernel expands q8_0 to f16 in shared memory.
 struct ResBlockDev {
     int ic = 0, oc = 0, stride = 1;
-    __half* w1 = nullptr;   // [oc][9][ic]
+    void* w1 = nullptr;          // [oc][9][ic]
+    const void* w1s = nullptr;   // q8_0 scales [oc][9][ic / 32]
     float* b1 = nullptr;
-    __half* w2 = nullptr;   // [oc][9][oc]
+    void* w2 = nullptr;          // [oc][9][oc]
+    const void* w2s = nullptr;
     float* b2 = nullptr;    // conv2 bias (+ downsample bias when fused)
-    __half* wd = nullptr;   // [oc][ic], or the [oc][oc] identity for an identity shortcut
+    void* wd = nullptr;     // [oc][ic], or the f16 [oc][oc] identity for an identity shortcut
+    const void* wds = nullptr;
     bool identity = false;
     // stage-1 blocks run over the QPACK layout: conv1 / conv2 weights packed for it
-    // (vdb_qpack_pack_weights, [3][384][32])
-    __half* w1q = nullptr;
-    __half* w2q = nullptr;
+    // (vdb_qpack_pack_weights, [3][384][32]; q8_0: one scale per packed row)
+    void* w1q = nullptr;
+    const void* w1qs = nullptr;
+    void* w2q = nullptr;
+    const void* w2qs = nullptr;
 };
 
 // ERes2Net runs from a plan compiled once at load from the conv manifest
@@ -192,6 +200,8 @@ public:
 
     // Number of GPU kernels launched by the last embed call (for benchmarks).
     long long last_launches = 0;
+    // Device bytes of the ResNet block conv weights (values, q8_0 scales, QPACK copies).
+    long long conv_weight_bytes = 0;
 
     // Conv-kernel profiling: when enabled, every tensor-core conv launch is
     // bracketed by CUDA events on its stream and its algorithmic FLOPs
@@ -232,6 +242,7 @@ private:
     size_t campp_ws_bytes(int B, int t_max) const;
     bool upload_f32(const std::vector<float>& v, float** dst, std::string& err);
     bool upload_f16(const std::vector<float>& v, __half** dst, std::string& err);
+    bool upload_bytes(const void* src, size_t n, void** dst, std::string& err);
     // f16 identity [c][c]: an identity shortcut added on the tensor cores as a 1x1
     // input segment of the conv that ends the block (x * 1.0 is exact, and the sum
     // is accumulated in f32 like the epilogue add it replaces). One per width.
@@ -258,6 +269,10 @@ private:
     int pooled_ = 0;
     float var_eps_ = 1e-8f;
     std::vector<void*> weight_allocs_;
+    // f16 expansion target of the q8_0 weights a conv streams (one conv at a time on the
+    // engine's stream): sized at load for the largest block conv
+    void* wscratch_ = nullptr;
+    long long wscratch_bytes_ = 0;
     // CUDA graphs of a bucket's launch sequence, keyed by everything its kernel
     // arguments depend on (the per-clip metadata lives in device buffers that are
     // refreshed before each launch). A shape is captured the second time it is seen;

@@ -363,6 +363,8 @@ identify_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         tmem_ld_32x32b_x32_nowait(taddr + (uint32_t)cb, v[0]);
                         tmem_ld_32x32b_x32_nowait(taddr + (uint32_t)cb + 32u, v[1]);
                         tmem_wait_ld();
+                        tmem_regs_ready(v[0]);
+                        tmem_regs_ready(v[1]);
                         float thr = res.n < LR ? floor_s : fmaxf(floor_s, res.mn);
                         // strictly above: a later row with an equal score has a higher
                         // index, so it never displaces an earlier one

@@ -12,6 +12,10 @@ namespace vdb {
 void set_error(const std::string& msg);
 const std::string& get_error();
 
+// Kernels the calling thread's last vdb_conv / vdb_conv1d call launched (the conv, plus
+// one per q8_0 weight segment it expanded into the scratch).
+int last_conv_launches();
+
 // cuTensorMapEncodeTiled resolved through the runtime's driver entry point
 // (no link-time dependency on libcuda).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

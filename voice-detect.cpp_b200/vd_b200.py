@@ -46,6 +46,8 @@ class ConvArgs(C.Structure):
         ("y2", C.c_void_p), ("ldr", C.c_int), ("residual2", C.c_void_p), ("ldr2", C.c_int),
         ("act", C.c_int), ("ysum", C.c_void_p), ("ldsum", C.c_int), ("addend", C.c_void_p),
         ("ldaddend", C.c_int), ("y_pad", C.c_int), ("tile_n", C.c_int), ("pair", C.c_int), ("qpack", C.c_int),
+        ("w0_scale", C.c_void_p), ("w1_scale", C.c_void_p),
+        ("w_scratch", C.c_void_p), ("w_scratch_bytes", C.c_longlong),
     ]
 
 
@@ -179,6 +181,8 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_sync.argtypes = [C.c_void_p]
         L.voicedetect_b200_profile_convs.restype = C.c_int
         L.voicedetect_b200_profile_convs.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.voicedetect_b200_conv_weight_bytes.restype = C.c_longlong
+        L.voicedetect_b200_conv_weight_bytes.argtypes = [C.c_void_p]
         L.voicedetect_b200_release_cache.restype = C.c_int
         L.voicedetect_b200_release_cache.argtypes = [C.c_void_p]
         L.voicedetect_b200_profile.restype = C.c_int
@@ -347,6 +351,11 @@ class Model:
         return [{k: (buf[12 * i + j] if j < 2 else int(buf[12 * i + j]))
                  for j, k in enumerate(keys)} for i in range(n)]
 
+    @property
+    def conv_weight_bytes(self) -> int:
+        """Device bytes of the ResNet block conv weights (q8_0 stays q8_0)."""
+        return int(self._L.voicedetect_b200_conv_weight_bytes(self.ctx))
+
     def release_cache(self) -> None:
         """Drops the captured CUDA graphs and the workspace (weights stay resident)."""
         if self._L.voicedetect_b200_release_cache(self.ctx) != 0:
@@ -447,6 +456,26 @@ def qpack_weights(w_taps):
     return out
 
 
+def qpack_rows():
+    """Source row (oc * 9 + tap) of each of the 1152 rows of the QPACK packed weight
+    (the layout vdb_qpack_pack_weights writes)."""
+    src = []
+    for kt in range(3):
+        for u in range(-1, 5):
+            for j in range(max(0, u - 1), min(3, u + 1) + 1):
+                src += [oc * 9 + kt * 3 + (u - j + 1) for oc in range(32)]
+    return src
+
+
+def qpack_q8(q, d):
+    """q8_0 operands of a 32 -> 32 conv ((32, 9, 32) int8, (9, 32) block-major f16
+    scales, as q8_planes returns them) -> the QPACK packing of both ((1152, 32) int8,
+    (1152,) f16: one scale per packed row)."""
+    import torch
+    idx = torch.tensor(qpack_rows(), device=q.device)
+    return q.reshape(288, 32)[idx].contiguous(), d.t().reshape(288)[idx].contiguous()
+
+
 def to_phase(x, tvalid=None):
     """(B, C, F, T) -> PHASE f16 tensor (4*B*(To+2)*(Fo+2), C) for a stride-2 consumer."""
     import torch
@@ -536,6 +565,24 @@ def to_tphase(x, pad: int, tvalid=None):
     return out.reshape(-1, Cc).contiguous()
 
 
+def q8_planes(w):
+    """f16/f32 weights with input channels last (a multiple of 32), e.g. the packed
+    (OC, k*k, IC) conv weight -> the q8_0 operands of vdb_conv: the gguf q8_0 rule
+    d = max|w| / 127 per block of 32, q = round(w / d). Returns (q, d, w16): q int8 in
+    w's shape, d the f16 scales block-major (K / 32, OC) (the w_scale layout), and
+    w16 = f16(q * d), the f16 weights the kernel expands them to."""
+    import torch
+    wf = w.float()
+    blk = wf.reshape(*wf.shape[:-1], wf.shape[-1] // 32, 32)
+    d = (blk.abs().amax(-1) / 127.0).to(torch.float16)
+    df = d.float()
+    q = torch.where(df[..., None] > 0, torch.round(blk / df[..., None].clamp_min(1e-30)),
+                    torch.zeros_like(blk)).clamp(-127, 127).to(torch.int8)
+    w16 = (q.float() * df[..., None]).to(torch.float16).reshape(wf.shape)
+    d_t = d.reshape(wf.shape[0], -1).t().contiguous()
+    return q.reshape(wf.shape).contiguous(), d_t, w16.contiguous()
+
+
 def pack_conv_weight(w):
     """torch (OC, IC, KF, KT) -> f16 (OC, KT*KF, IC) (tap = kt*k + kf)."""
     OC, IC, KF, KT = w.shape
@@ -556,7 +603,7 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
          x1=None, w1=None, stride1=1, ic1=None, residual=None, relu=False, clamp_hi=0.0,
          y=None, y_phase=False, err=None, stream=None, tile_m=0, halo=0, ksplit=0,
          y2=None, residual2=None, act=0, ysum=None, addend=None, y_pad=0, tile_n=0, pair=0,
-         qpack=False):
+         qpack=False, w0_scale=None, w1_scale=None, w_scratch=None):
     """vdb_conv on device tensors. x0/x1/residual/residual2/y are f16 GRID or PHASE
     tensors of shape (rows, C), or channel-slice views of wider ones (x[:, c0:c1]:
     the row pitch is taken from the view's stride); y2 is an extra PHASE output,
@@ -584,6 +631,10 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                     else lib().vdb_grid_rows(batch, t_out, f_out))
             y = torch.empty(rows, oc, dtype=torch.float16, device=x0.device)
     ldy = 0 if (int(y_phase) == 3 or qpack) else _ld(y)
+    if w_scratch is None and (w0_scale is not None or w1_scale is not None):
+        # room for the f16 expansion of both segments' weights (used if they stream)
+        n = w0.numel() + (w1.numel() if (w1 is not None and w1_scale is not None) else 0)
+        w_scratch = torch.empty(2 * n + 512, dtype=torch.uint8, device=x0.device)
     a = ConvArgs(batch=batch, t_out=t_out, f_out=f_out, oc=oc, k0=k0, stride0=stride0,
                  ic0=ic0 if ic0 is not None else x0.shape[1], x0=x0.data_ptr(),
                  w0=w0.data_ptr(), stride1=stride1,
@@ -595,7 +646,11 @@ def conv(x0, w0, bias, tvalid, *, batch, t_out, f_out, oc, k0=3, stride0=1, ic0=
                  y2=_ptr(y2), ldr=_ld(residual), residual2=_ptr(residual2),
                  ldr2=_ld(residual2), act=int(act), ysum=_ptr(ysum), ldsum=_ld(ysum),
                  addend=_ptr(addend), ldaddend=_ld(addend), y_pad=int(y_pad),
-                 tile_n=int(tile_n), pair=int(pair), qpack=int(bool(qpack)))
+                 tile_n=int(tile_n), pair=int(pair), qpack=int(bool(qpack)),
+                 w0_scale=_ptr(w0_scale), w1_scale=_ptr(w1_scale),
+                 w_scratch=_ptr(w_scratch),
+                 w_scratch_bytes=(w_scratch.numel() * w_scratch.element_size()
+                                  if w_scratch is not None else 0))
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     _check(lib().vdb_conv(C.byref(a), C.c_void_p(s)), "vdb_conv")
     return y
