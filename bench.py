@@ -65,6 +65,35 @@ CONV_DRAM_B_PER_KFLOP = {
 }
 
 
+def launch_roofline(convs: list[dict], peaks: dict) -> dict | None:
+    """Each profiled conv launch's own roofline, max(FLOPs / tensor peak, bytes / HBM
+    peak), summed and set against the launches' measured time. Bytes are the
+    tensors the launch must move once: its input rows (a stride-2 conv's 4 PHASE planes
+    of output-grid size), the second segment's rows, the residual and the output, all
+    f16 over the padded output grid B x (T_out + 2) x (F_out + 2) (extra copies some
+    ERes2Net convs write are not counted, so the floors are lower bounds). frac =
+    floor / measured; tensor_ceiling = the tensor-peak fraction the stack would reach if
+    every launch ran at its floor."""
+    if not convs:
+        return None
+    pt = (peaks.get("bf16_tflops_sustained") or 1400.0) * 1e12
+    pb = (peaks.get("hbm_gbs") or 6650.0) * 1e9
+    meas = floor = hbm = fl = 0.0
+    for r in convs:
+        rows = r["batch"] * (r["t_out"] + 2) * (r["f_out"] + 2)
+        byts = 2.0 * rows * (r["ic"] * (4 if r["stride"] == 2 else 1) + r["ic1"] +
+                             r["oc"] * (2 if r["res"] else 1))
+        t_t, t_b = r["flops"] / pt, byts / pb
+        floor += max(t_t, t_b)
+        hbm += t_b if t_b > t_t else 0.0
+        meas += r["ms"] / 1e3
+        fl += r["flops"]
+    return {"floor_ms": floor * 1e3, "measured_ms": meas * 1e3, "frac": floor / meas,
+            "hbm_bound_share_of_floor": hbm / floor, "launches": len(convs),
+            "tensor_ceiling": fl / floor / pt,
+            "peaks": "tensor bf16_tflops_sustained, HBM hbm_gbs (MEASURED_PEAKS.json)"}
+
+
 def conv_traffic(convs: list[dict]):
     """(mean DRAM bytes per conv launch, share of the conv FLOPs whose shape has a
     measured ratio) for the profiled launches `convs` (Model.profile_convs())."""
@@ -148,11 +177,43 @@ def _store():
     return dist.distributed_c10d._get_default_store()
 
 
+def pin_to_gpu_cores(local: int):
+    """Restricts this rank (and the host gather threads its engine starts) to the CPU
+    cores NVML reports as local to its GPU, so each rank's PCM gather and pinned staging
+    ring stay in its own NUMA node's memory instead of crossing sockets. Returns the
+    cores kept, or None when NVML cannot tell (the affinity is then left alone)."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(local)
+        try:
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(local)
+        words = ((os.cpu_count() or 64) + 63) // 64
+        mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {64 * i + b for i, w in enumerate(mask) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return sorted(cpus)
+    except Exception:
+        return None
+
+
 def init_ranks(backend: str, local: int | None = None, timeout_s: float | None = None):
-    """One process per GPU (or gloo rank): the default group with a short timeout."""
+    """One process per GPU (or gloo rank): the default group with a short timeout.
+    Under NCCL a collective that exceeds it is aborted by torch's watchdog
+    (ncclCommAbort) and the process torn down (TORCH_NCCL_ASYNC_ERROR_HANDLING=1
+    unless the environment sets it)."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
+    if backend == "nccl":
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
     kw = {"timeout": timedelta(seconds=PG_TIMEOUT_S if timeout_s is None else timeout_s)}
     if backend == "nccl":
         kw["device_id"] = torch.device("cuda", local)
@@ -449,8 +510,10 @@ def run_b200(args) -> int:
     import vd_b200
 
     world, rank, local = dist_env()
+    cores = None
     if world > 1:
         torch.cuda.set_device(local)
+        cores = pin_to_gpu_cores(local)
         init_ranks("nccl", local)
     else:
         torch.cuda.set_device(0)
@@ -512,7 +575,8 @@ def run_b200(args) -> int:
     elapsed_ms = start.elapsed_time(end)
     clk = clocks.stop()
     conv_ms, conv_flops, conv_n, stages, prof_steps = profiled_steps(model, step, args.steps)
-    traffic, traffic_cov = conv_traffic(model.profile_convs())
+    prof_convs = model.profile_convs()
+    traffic, traffic_cov = conv_traffic(prof_convs)
     model.sync()
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -591,7 +655,9 @@ def run_b200(args) -> int:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * total,
                 "d2h_bytes_per_step": 4 * n_local * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": E2E_WARMUP,
-                "timed_calls": args.e2e_steps},
+                "timed_calls": args.e2e_steps,
+                "h2d_gbs_per_rank": 4 * total / e_sec / 1e9,
+                "host_cores_per_rank": len(cores) if cores else (os.cpu_count() or 0)},
         "e2e_s16": e2e_s16,
         "gpu_launches": launches,  # our kernels only (the NCCL all-gather is not counted)
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
@@ -609,6 +675,7 @@ def run_b200(args) -> int:
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
         "rooflines_other": hbm_rooflines(stages, args.steps, lens, peaks),
+        "conv_launch_roofline": launch_roofline(prof_convs, peaks),
         "identify": ident,
         "parity": parity,
         "clocks": clk,
@@ -896,6 +963,7 @@ def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
     elapsed_ms = start.elapsed_time(end)
     clk = clocks.stop()
     conv_ms, conv_flops, conv_n, stages, prof_steps = profiled_steps(model, step, args.steps)
+    prof_convs = model.profile_convs()
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -935,6 +1003,7 @@ def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
                      "conv_ms_per_step": conv_ms / args.steps,
                      "conv_tflop_per_step": conv_flops / args.steps / 1e12},
         "stage_ms_per_step": {k: v / args.steps for k, v in stages.items()},
+        "conv_launch_roofline": launch_roofline(prof_convs, peaks),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1101,7 +1170,8 @@ def run_profile_case(args) -> int:
                 FC partial / finish kernels close it)
       identify  vdb_identify, 8192 queries x 100,000 x 256, top-5
       ingest    vdb_pcm_ingest, 64 int16 clips of 20 s at 44.1 kHz -> 16 kHz
-      eres2net  a batch of 64 x 10 s clips through the ERes2Net-base f16 engine
+      eres2net  a batch of 64 (--profile-batch) x 10 s clips through the ERes2Net-base
+                f16 engine
       qpack     stage-1 QPACK convs (plain, then with the residual), batch 128"""
     import ctypes as C
     import torch
@@ -1168,7 +1238,7 @@ def run_profile_case(args) -> int:
         gguf = os.path.join(tmp, "eres2net_f16.gguf")
         vd_synth.write_eres2net_gguf(gguf, vd_synth.eres2net_model(SEED), "f16")
         model = vd.Model(gguf)
-        B, n = 64, 10 * SR
+        B, n = args.profile_batch or 64, 10 * SR
         pool = make_pool(16, 10.0)
         d_pcm = torch.from_numpy(np.concatenate([pool[i % 16] for i in range(B)])).to(dev)
         offs = np.arange(B, dtype=np.int64) * n
@@ -1221,6 +1291,8 @@ def main() -> int:
     ap.add_argument("--profile-case", choices=PROFILE_CASES, default=None,
                     help="run one small case of a kernel family for an ncu capture and exit")
     ap.add_argument("--profile-reps", type=int, default=2)
+    ap.add_argument("--profile-batch", type=int, default=0,
+                    help="clips of the eres2net profile case (0 = 64)")
     ap.add_argument("--conv-table", action="store_true",
                     help="with --profile-case tail / eres2net: print every conv launch's "
                          "duration, FLOPs and shape")
