@@ -1052,15 +1052,16 @@ def eres_config(args, world):
 # one-segment conv (a block's conv1), "down" a block's conv2 with the 1x1 stride-2
 # downsample as input segment 1, "id" a block's conv2 with the identity shortcut as
 # input segment 1 (identity weights; not counted in the algorithmic FLOPs, as in the
-# engine), "res" the same conv with the shortcut added in the epilogue instead.
+# engine at 64 channels), "res" the same conv with the shortcut added in the epilogue
+# instead (what the engine does at 128 and 256 channels).
 SWEEP_SHAPES = [
     (32, 32, 300, 80, 1, "qp"), (32, 32, 300, 80, 1, "qp+res"),
     (32, 64, 300, 80, 2, "plain"), (64, 64, 150, 40, 1, "down"),
     (64, 64, 150, 40, 1, "plain"), (64, 64, 150, 40, 1, "id"),
     (64, 128, 150, 40, 2, "plain"), (128, 128, 75, 20, 1, "down"),
-    (128, 128, 75, 20, 1, "plain"), (128, 128, 75, 20, 1, "id"),
+    (128, 128, 75, 20, 1, "plain"), (128, 128, 75, 20, 1, "res"),
     (128, 256, 75, 20, 2, "plain"), (256, 256, 38, 10, 1, "down"),
-    (256, 256, 38, 10, 1, "plain"), (256, 256, 38, 10, 1, "id")]
+    (256, 256, 38, 10, 1, "plain"), (256, 256, 38, 10, 1, "res")]
 # launches of each sweep shape per ResNet34 forward (blocks 3 / 4 / 6 / 3)
 SWEEP_COUNTS = [3, 3, 1, 1, 3, 3, 1, 1, 5, 5, 1, 1, 2, 2]
 

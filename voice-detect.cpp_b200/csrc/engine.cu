@@ -1250,6 +1250,11 @@ int Engine::launch_bucket(const float* d_pcm, int B, int t_max,
             // QPACK row is contiguous with the output row)
             c2.qpack = 1;
             c2.residual = x;
+        } else if (blk.identity && blk.oc >= 128) {
+            // identity shortcut of a 128 / 256-channel block as the epilogue residual:
+            // 3.5-4.7 % faster than the identity MMA segment at batch 512 (at 64
+            // channels the segment is the faster one)
+            c2.residual = x;
         } else {
             // 1x1 downsample, or the identity shortcut, as input segment 1
             c2.x1 = x;
