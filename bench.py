@@ -58,10 +58,10 @@ CONV_DRAM_B_PER_KFLOP = {
     (64, 64, 1, 32, 0, 0): 4.181, (64, 64, 1, 0, 0, 0): 3.444, (64, 64, 1, 64, 0, 0): 5.398,
     (64, 128, 2, 0, 0, 0): 5.591,
     (128, 128, 1, 64, 0, 0): 2.162, (128, 128, 1, 0, 0, 0): 1.756,
-    (128, 128, 1, 128, 0, 0): 2.800,
+    (128, 128, 1, 128, 0, 0): 2.800, (128, 128, 1, 0, 1, 0): 2.676,
     (128, 256, 2, 0, 0, 0): 3.015,
     (256, 256, 1, 128, 0, 0): 1.158, (256, 256, 1, 0, 0, 0): 0.910,
-    (256, 256, 1, 256, 0, 0): 1.517,
+    (256, 256, 1, 256, 0, 0): 1.517, (256, 256, 1, 0, 1, 0): 1.392,
 }
 
 

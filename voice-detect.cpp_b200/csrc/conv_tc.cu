@@ -340,18 +340,25 @@ __device__ __forceinline__ void epi_chunk(const ConvDev& p, bool live, const Row
     }
     if (!ri.in_range) return;
     if constexpr (PLAIN) {
-        // (acc + bias) -> ReLU -> valid-pixel mask -> f16: the ResNet BasicBlock convs
-        // (every other epilogue mode compiled out, so the hot code stays small)
+        // (acc + bias) [+ residual] -> ReLU -> valid-pixel mask -> f16: the ResNet
+        // BasicBlock convs (every other epilogue mode compiled out, so the hot code stays
+        // small); the residual is added in the general path's order
         const uint32_t keep = ri.valid ? 0xFFFFFFFFu : 0u;
         const __half2 zero2 = __float2half2_rn(0.0f);
         uint4 out[NC / 8];
 #pragma unroll
         for (int j = 0; j < NC / 8; ++j) {
+            const uint32_t w[4] = {res[j].x, res[j].y, res[j].z, res[j].w};
             __half2 h[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                h[q] = __floats2half2_rn(f[j * 8 + 2 * q] + sbias[j * 8 + 2 * q],
-                                         f[j * 8 + 2 * q + 1] + sbias[j * 8 + 2 * q + 1]);
+                float a0 = f[j * 8 + 2 * q] + sbias[j * 8 + 2 * q];
+                float a1 = f[j * 8 + 2 * q + 1] + sbias[j * 8 + 2 * q + 1];
+                if (has_res) {
+                    a0 += h2f(w[q] & 0xFFFFu);
+                    a1 += h2f(w[q] >> 16);
+                }
+                h[q] = __floats2half2_rn(a0, a1);
                 if (p.relu) h[q] = __hmax2(h[q], zero2);
             }
             out[j] = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]) & keep,
@@ -564,11 +571,19 @@ __device__ __forceinline__ void epi_rows(const ConvDev& p, bool live, const RowI
                                          const float* sbias, const float* sss, EpiStage& st) {
     if constexpr (PLAIN) {
         __half* yrow = p.y + ri.dst * p.ldy + n0;
-        const uint4 none[NC / 8] = {};
+        // the residual of the next chunk is loaded before the current one is finished
+        const bool has_res = p.residual != nullptr && ri.valid;
+        const __half* rrow = has_res ? p.residual + (long long)m * p.ldr + n0 : nullptr;
+        uint4 res[NC / 8] = {};
+        if (rrow) load_res<NC>(rrow + c_lo, res);
         for (int c = c_lo; c < c_hi; c += NC) {
+            uint4 cur[NC / 8];
+#pragma unroll
+            for (int j = 0; j < NC / 8; ++j) cur[j] = res[j];
+            if (rrow && c + NC < c_hi) load_res<NC>(rrow + c + NC, res);
             const uint32_t buf = stage_begin(st);
             epi_chunk<NC, J, SEQ, true>(p, live, ri, n0 + c, tbase + (uint32_t)c,
-                                        sbias + n0 + c, sss, false, none, nullptr, yrow + c,
+                                        sbias + n0 + c, sss, has_res, cur, nullptr, yrow + c,
                                         nullptr, nullptr, nullptr, false, buf);
             stage_end(st, buf, n0 + c, p.M);
         }
@@ -2374,9 +2389,10 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
         VDB_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tm[0], tm[1], tm[2], tm[3], tm[4], p));
         return 0;
     };
-    // The plain epilogue (bias, ReLU, mask, GRID / PHASE store): every ResNet34 conv.
-    const bool plain = !seq && a->act == 0 && !a->residual && !a->residual2 && !a->y2 &&
-                       !a->ysum && a->clamp_hi <= 0.0f && (a->y_phase == 0 || a->y_phase == 1);
+    // The plain epilogue (bias, optional residual, ReLU, mask, GRID / PHASE store): every
+    // ResNet34 conv.
+    const bool plain = !seq && a->act == 0 && !a->residual2 && !a->y2 && !a->ysum &&
+                       a->clamp_hi <= 0.0f && (a->y_phase == 0 || a->y_phase == 1);
     if (pair) {
         auto kern = seq ? conv_tc_kernel<1, 1, true, true>
                         : (plain ? conv_tc_kernel<1, 1, true, false, true>
