@@ -1530,7 +1530,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                                        acc * acc_cols + (uint32_t)(mb * J * p.BN);
                 const RowInfo ri = row_info<SEQ>(p, stv, m, live);
                 // the host stages only outputs whose chunks are 32 columns wide
-                EpiStage st{&tmY, (p.ostage_off && (c_hi - c_lo) % 32 == 0) ? stage_base : 0u,
+                // (the 1-D and K-split kernels store directly: a compile-time 0 folds the
+                // staging code away there)
+                EpiStage st{&tmY, (!SEQ && J == 1 && p.ostage_off && (c_hi - c_lo) % 32 == 0)
+                                      ? stage_base : 0u,
                             stage_n, m0 + mb * kMB + quad * 32};
                 if ((c_hi - c_lo) % 32 == 0)
                     epi_rows<32, J, SEQ, PLAIN>(p, live, ri, m, n0, c_lo, c_hi, tbase, sbias, sss, st);
@@ -2200,7 +2203,7 @@ int conv_impl(const vdb_conv_args* a, const SeqArgs* sq, void* stream) {
     const bool chunk32 = BN % 64 == 0 || (p.n_mblk >= 2 && BN % 32 == 0);
     const int ldy_el = a->ldy ? a->ldy : a->oc;
     const int store_mode = conv_tma_store_mode();
-    bool staged = store_mode != 0 && !seq && a->y_phase == 0 && !a->y2 && !a->ysum && chunk32 &&
+    bool staged = store_mode != 0 && !seq && J == 1 && a->y_phase == 0 && !a->y2 && !a->ysum && chunk32 &&
                   (reinterpret_cast<uintptr_t>(a->y) & 15u) == 0 && ldy_el % 8 == 0;
     const int budget0 = kSmemMax - 1024 - (int)off - (int)tail;
     if (staged) {
