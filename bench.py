@@ -173,8 +173,16 @@ class RankFailure(RuntimeError):
 
 
 def _store():
+    """The default process group's key-value store (the one init_process_group
+    rendezvoused through). torch exposes it only as distributed_c10d's private
+    _get_default_store; a torch without it fails here with a clear error rather than
+    skipping the checkpoints."""
     import torch.distributed as dist
-    return dist.distributed_c10d._get_default_store()
+    get = getattr(dist.distributed_c10d, "_get_default_store", None)
+    if get is None:
+        raise RuntimeError("this torch exposes no default process-group store "
+                           "(distributed_c10d._get_default_store)")
+    return get()
 
 
 def pin_to_gpu_cores(local: int):
