@@ -73,6 +73,38 @@ def test_bucketing_splits_are_exact(resnet):
         assert _cos(full[i], split[i]) >= 0.99999
 
 
+def test_odd_staging_capacity_both_slots(resnet, tmp_path, cuda_lib):
+    """A fresh engine whose first bucket holds an odd number of clips (65, above the
+    64-clip floor) sizes its two per-bucket metadata slots from that count; four
+    buckets alternate between the slots, so the staging kernel reads int64 clip
+    offsets from both. Both the device-resident and the host-PCM call must give the
+    same embeddings as the shared engine's one-bucket batch."""
+    import torch
+    m, model = resnet
+    path = tmp_path / "resnet34_f32.gguf"
+    vd_synth.write_resnet_gguf(str(path), m, "f32")
+    fresh = cuda_lib.Model(str(path))
+    try:
+        lens = [8000 + 160 * (i % 7) for i in range(200)]
+        clips = [vd_synth.clip_f32(vd_synth.make_clip(900 + i, n)) for i, n in enumerate(lens)]
+        want = model.embed_batch(clips)
+        fresh.set_bucketing(65, 10_000_000)
+        pcm = np.concatenate(clips)
+        offs = np.zeros(len(lens), np.int64)
+        offs[1:] = np.cumsum(lens)[:-1]
+        d_pcm = torch.from_numpy(pcm).cuda()
+        d_out = torch.zeros(len(lens), fresh.dim, device="cuda")
+        fresh.embed_device(d_pcm, offs, lens, d_out, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        got_dev = d_out.cpu().numpy()
+        got_host = fresh.embed_batch(clips)
+    finally:
+        fresh.close()
+    for i in range(len(clips)):
+        assert _cos(got_dev[i], want[i]) >= 0.99999, i
+        assert _cos(got_host[i], want[i]) >= 0.99999, i
+
+
 def test_verify_verdicts_match_oracle(resnet, tmp_path):
     import wave
     m, model = resnet

@@ -22,6 +22,28 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restri
     if (i < n) out[i] = __float2half_rn(in[i]);
 }
 
+// Copies one bucket's metadata from its pinned staging slot, read through the slot's
+// mapped device address, into the device buffers the bucket's kernels read: n_meta ints
+// (valid lengths per level, output rows), then B offsets and B sample counts. A kernel
+// rather than cudaMemcpyAsync: a host-to-device copy on the compute stream waits on the
+// copy engine behind whatever transfer holds it, and in the host-PCM path that is the
+// next bucket's PCM (160+ MB, ~3 ms), which held every bucket's compute back as long.
+__global__ void stage_meta_kernel(const int* __restrict__ hm, int n_meta,
+                                  const long long* __restrict__ ho, const int* __restrict__ hn,
+                                  int B, int* __restrict__ meta, long long* __restrict__ offs,
+                                  int* __restrict__ nsamp) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_meta + B;
+         i += gridDim.x * blockDim.x) {
+        if (i < n_meta) {
+            meta[i] = hm[i];
+        } else {
+            const int b = i - n_meta;
+            offs[b] = ho[b];
+            nsamp[b] = hn[b];
+        }
+    }
+}
+
 struct Loader {
     const Gguf& g;
     std::string& err;
@@ -243,6 +265,7 @@ void Engine::free_workspace() {
     meta_cap_ = 0;
     cudaFreeHost(h_stage_);
     h_stage_ = nullptr;
+    d_stage_ = nullptr;
     h_stage_bytes_ = 0;
     for (int s = 0; s < 2; ++s) {
         cudaFreeHost(h_ring_[s]);
@@ -1027,14 +1050,19 @@ int Engine::ensure_workspace(int B, int t_max, std::string& err) {
         offs_ = nullptr;
         nsamp_ = nullptr;
         h_stage_ = nullptr;
+        d_stage_ = nullptr;
         const int cap = std::max(B, 64);
         const size_t nlev = levels_.size();
-        // two staging slots so the host can fill bucket k+1 while bucket k copies
-        h_stage_bytes_ = (size_t)cap * (sizeof(long long) + sizeof(int) * (nlev + 3)) + 64;
+        // two staging slots so the host can fill bucket k+1 while bucket k copies; a
+        // slot's size is a multiple of 256 bytes so that both slots, and the int64
+        // offsets inside each, are 8-byte aligned for the staging kernel's loads
+        h_stage_bytes_ =
+            ((size_t)cap * (sizeof(long long) + sizeof(int) * (nlev + 3)) + 64 + 255) & ~(size_t)255;
         if (cudaMalloc(&meta_, sizeof(int) * cap * (nlev + 2)) != cudaSuccess ||
             cudaMalloc(&offs_, sizeof(long long) * cap) != cudaSuccess ||
             cudaMalloc(&nsamp_, sizeof(int) * cap) != cudaSuccess ||
-            cudaMallocHost(&h_stage_, 2 * h_stage_bytes_) != cudaSuccess) {
+            cudaHostAlloc(&h_stage_, 2 * h_stage_bytes_, cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostGetDevicePointer(&d_stage_, h_stage_, 0) != cudaSuccess) {
             err = "device out of memory (metadata)";
             return 1;
         }
@@ -1065,7 +1093,7 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     }
     if (ensure_workspace(B, t_max, err)) return 1;
     // Per-bucket metadata: [tvalid level 0..nlev-1][B], [outrow][B], then offsets, nsamp.
-    // A staging slot is only rewritten after the copies that last read it finished.
+    // A staging slot is only rewritten after the kernel that last read it finished.
     const int slot = stage_slot_;
     stage_slot_ ^= 1;
     if (stage_used_[slot]) VDB_CHECK_CUDA(cudaEventSynchronize(stage_ev_[slot]));
@@ -1084,10 +1112,18 @@ int Engine::run_bucket(const float* d_pcm, const long long* h_off, const int* h_
     int* hn = reinterpret_cast<int*>(ho + B);
     std::memcpy(ho, h_off, sizeof(long long) * B);
     std::memcpy(hn, h_ns, sizeof(int) * B);
-    VDB_CHECK_CUDA(cudaMemcpyAsync(meta_, hm, sizeof(int) * (nlev + 1) * B,
-                                   cudaMemcpyHostToDevice, st));
-    VDB_CHECK_CUDA(cudaMemcpyAsync(offs_, ho, sizeof(long long) * B, cudaMemcpyHostToDevice, st));
-    VDB_CHECK_CUDA(cudaMemcpyAsync(nsamp_, hn, sizeof(int) * B, cudaMemcpyHostToDevice, st));
+    {
+        // the same slot through its mapped device address
+        const ptrdiff_t d = static_cast<char*>(d_stage_) - static_cast<char*>(h_stage_);
+        const int n_meta = (int)((nlev + 1) * B);
+        stage_meta_kernel<<<(n_meta + B + 255) / 256, 256, 0, st>>>(
+            reinterpret_cast<const int*>(reinterpret_cast<const char*>(hm) + d), n_meta,
+            reinterpret_cast<const long long*>(reinterpret_cast<const char*>(ho) + d),
+            reinterpret_cast<const int*>(reinterpret_cast<const char*>(hn) + d), B, meta_, offs_,
+            nsamp_);
+        VDB_CHECK_CUDA(cudaGetLastError());
+        ++last_launches;
+    }
     VDB_CHECK_CUDA(cudaEventRecord(stage_ev_[slot], st));
     stage_used_[slot] = true;
     long long launches = 0;

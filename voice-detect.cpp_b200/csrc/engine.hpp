@@ -316,8 +316,10 @@ private:
     int* nsamp_ = nullptr;
     int meta_cap_ = 0;
     int* errword_ = nullptr;
-    // pinned staging for small per-bucket host->device metadata
+    // pinned, mapped staging for small per-bucket host->device metadata, which a kernel
+    // reads through d_stage_ (the same memory's device address)
     void* h_stage_ = nullptr;
+    void* d_stage_ = nullptr;
     size_t h_stage_bytes_ = 0;   // bytes per slot (two slots)
     int stage_slot_ = 0;
     bool stage_used_[2] = {false, false};
