@@ -60,7 +60,10 @@ char* voicedetect_capi_analyze_path_json(voicedetect_ctx* ctx, const char* wav_p
 
 /* Batched embed (the throughput path): n_clips mono f32 clips pcm[i] of
  * n_samples[i] samples at sample_rate; writes n_clips * dim floats to the caller's
- * `out` (row i = clip i, L2-normalised) and *out_dim = dim. */
+ * `out` (row i = clip i, L2-normalised) and *out_dim = dim. Clips in page-locked
+ * memory (cudaHostAlloc / cudaHostRegister) are copied to the GPU straight from the
+ * caller's buffers; pageable clips are first gathered into the engine's pinned ring,
+ * which costs host memory bandwidth. Results are identical either way. */
 int voicedetect_capi_embed_pcm_batch(voicedetect_ctx* ctx, const float* const* pcm,
                                      const int* n_samples, int n_clips, int sample_rate,
                                      float* out, int* out_dim);

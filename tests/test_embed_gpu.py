@@ -105,6 +105,37 @@ def test_odd_staging_capacity_both_slots(resnet, tmp_path, cuda_lib):
         assert _cos(got_host[i], want[i]) >= 0.99999, i
 
 
+def test_page_locked_clips_copied_directly(resnet):
+    """Clips in page-locked host memory (cudaHostRegister) reach the device by one DMA
+    each from the caller's buffer instead of the engine's gather. The embeddings must
+    equal the pageable call's bit for bit, for f32 and int16 input, with every clip
+    locked and with a batch that mixes locked and pageable clips (gathered)."""
+    import torch
+    _, model = resnet
+    cr = torch.cuda.cudart()
+    lens = [16000 + 1000 * i for i in range(12)]
+    parts = [vd_synth.clip_f32(vd_synth.make_clip(700 + i, n)) for i, n in enumerate(lens)]
+    pcm = np.concatenate(parts)
+    offs = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    clips = [pcm[o:o + n] for o, n in zip(offs, lens)]
+    pcm16 = np.round(pcm * 32768.0).astype(np.int16)
+    clips16 = [pcm16[o:o + n] for o, n in zip(offs, lens)]
+    want = model.embed_batch(clips)
+    want16 = model.embed_batch_s16(clips16)
+    locked = []
+    try:
+        for a in (pcm, pcm16):
+            assert cr.cudaHostRegister(a.ctypes.data, a.nbytes, 0) == cr.cudaError.success
+            locked.append(a)
+        np.testing.assert_array_equal(model.embed_batch(clips), want)
+        np.testing.assert_array_equal(model.embed_batch_s16(clips16), want16)
+        mixed = [c if i % 2 else c.copy() for i, c in enumerate(clips)]  # copies are pageable
+        np.testing.assert_array_equal(model.embed_batch(mixed), want)
+    finally:
+        for a in locked:
+            cr.cudaHostUnregister(a.ctypes.data)
+
+
 def test_verify_verdicts_match_oracle(resnet, tmp_path):
     import wave
     m, model = resnet
@@ -184,7 +215,8 @@ def test_device_path_matches_host_path(resnet):
     torch.cuda.synchronize()
     dev = out.cpu().numpy()
     assert np.allclose(dev, host, atol=1e-6)
-    assert model.last_launches() == 38  # fbank + cmn + stem + 32 convs + TSTP, FC, finish
+    # metadata staging + fbank + cmn + stem + 32 convs + TSTP, FC, finish
+    assert model.last_launches() == 39
 
 
 def test_identify_matches_oracle(resnet):

@@ -1509,6 +1509,23 @@ static void gather_clips(char* dst, const void* const* pcm, const int* nsamp, si
     for (std::thread& x : th) x.join();
 }
 
+// True when the `bytes` at p lie in page-locked host memory (cudaHostAlloc /
+// cudaMallocHost / cudaHostRegister): the copy engine can then read them directly.
+// Pageable, managed or device memory answers false. Both ends of the range are
+// checked, so a clip that runs past a registered region is gathered instead.
+static bool host_pinned(const void* p, size_t bytes) {
+    if (!p || bytes == 0) return false;
+    for (const void* q : {p, static_cast<const void*>(static_cast<const char*>(p) + bytes - 1)}) {
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (a.type != cudaMemoryTypeHost) return false;
+    }
+    return true;
+}
+
 int Engine::embed_host(const float* const* pcm, const int* nsamp, int n, float* out,
                        std::string& err) {
     return embed_host_raw(reinterpret_cast<const void* const*>(pcm), 0, nsamp, n, 16000, out,
@@ -1638,8 +1655,16 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         out_bytes_ = ob;
     }
     last_launches = 0;
-    std::vector<long long> bo;
+    std::vector<long long> bo, bi;
     std::vector<int> bn;
+    // Clips in page-locked memory go to the device by one DMA each, straight from the
+    // caller's buffers; a bucket with any pageable clip is gathered into the pinned
+    // ring and copied in one piece. The gather costs the host three passes over its
+    // DRAM per input byte (read the caller's array, write the ring, DMA out of it)
+    // against one for the direct copy, and with eight ranks per host that memory
+    // bandwidth, not PCIe, bounded the f32 call.
+    std::vector<char> pinned((size_t)n);
+    for (int i = 0; i < n; ++i) pinned[i] = host_pinned(pcm[i], (size_t)n_in[i] * esz) ? 1 : 0;
     // Buckets run shortest clips first: the first bucket's host gather and copy are
     // the only ones nothing overlaps, so it should be the smallest.
     const size_t nbk = bk.size() - 1;
@@ -1648,10 +1673,14 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         const int s = (int)(step & 1);
         const int cnt = (int)(bk[k + 1] - bk[k]);
         const int* idx = order.data() + bk[k];
-        // the pinned slot is free once its previous H2D copy finished
+        bool direct = true;
+        for (int j = 0; j < cnt && direct; ++j) direct = pinned[idx[j]] != 0;
+        // the pinned slots (PCM ring, conversion metadata) are free once their
+        // previous H2D copies finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaEventSynchronize(h2d_ev_[s]));
-        gather_clips(reinterpret_cast<char*>(h_ring_[s]), pcm, n_in, esz, idx, cnt);
+        if (!direct) gather_clips(reinterpret_cast<char*>(h_ring_[s]), pcm, n_in, esz, idx, cnt);
         bo.assign((size_t)cnt, 0);
+        bi.assign((size_t)cnt, 0);
         bn.assign((size_t)cnt, 0);
         long long tot = 0, tot_in = 0;
         int max_out = 0;
@@ -1659,6 +1688,7 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         long long* mi = convert ? static_cast<long long*>(h_imeta_[s]) : nullptr;
         for (int j = 0; j < cnt; ++j) {
             bo[j] = tot;
+            bi[j] = tot_in;
             bn[j] = ns[idx[j]];
             if (convert) {
                 mi[j] = tot_in;
@@ -1673,8 +1703,16 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         }
         // the device slot is free once the bucket that last read it finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaStreamWaitEvent(copy_stream_, comp_ev_[s], 0));
-        VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot_in * esz,
-                                       cudaMemcpyHostToDevice, copy_stream_));
+        if (direct) {
+            // the same packed layout the gather writes: clip j at input offset bi[j]
+            for (int j = 0; j < cnt; ++j)
+                VDB_CHECK_CUDA(cudaMemcpyAsync(static_cast<char*>(d_ring_[s]) + (size_t)bi[j] * esz,
+                                               pcm[idx[j]], (size_t)n_in[idx[j]] * esz,
+                                               cudaMemcpyHostToDevice, copy_stream_));
+        } else {
+            VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot_in * esz,
+                                           cudaMemcpyHostToDevice, copy_stream_));
+        }
         if (convert)
             VDB_CHECK_CUDA(cudaMemcpyAsync(d_imeta_[s], h_imeta_[s],
                                            (size_t)imeta_cap_ * (2 * sizeof(long long) + 2 * sizeof(int)),

@@ -327,6 +327,8 @@ private:
     // Host PCM path: a two-slot ring of pinned host + device PCM buffers, each
     // holding one bucket. The host gathers bucket k+1 into its pinned slot while
     // the GPU runs bucket k; the H2D copy runs on copy_stream_ and overlaps compute.
+    // A bucket whose clips all lie in page-locked caller memory skips the host slot:
+    // one DMA per clip into the device slot.
     cudaStream_t copy_stream_ = nullptr;
     void* h_ring_[2] = {nullptr, nullptr};   // raw PCM of one bucket (f32 or int16)
     void* d_ring_[2] = {nullptr, nullptr};
