@@ -106,14 +106,21 @@ def test_odd_staging_capacity_both_slots(resnet, tmp_path, cuda_lib):
 
 
 def test_page_locked_clips_copied_directly(resnet):
-    """Clips in page-locked host memory (cudaHostRegister) reach the device by one DMA
-    each from the caller's buffer instead of the engine's gather. The embeddings must
-    equal the pageable call's bit for bit, for f32 and int16 input, with every clip
-    locked and with a batch that mixes locked and pageable clips (gathered)."""
+    """Clips in page-locked host memory (cudaHostRegister) reach the device by DMA from
+    the caller's buffer instead of the engine's gather. The embeddings must equal the
+    pageable call's bit for bit, for f32 and int16 input, with every clip locked and
+    with a batch that mixes locked and pageable clips (gathered). Clips stored in
+    ascending length are copied one by one (the engine runs them longest first, so
+    neighbours in its order are not neighbours in memory); stored in descending length
+    they follow one another in both and go as merged copies."""
+    for lens in ([16000 + 1000 * i for i in range(12)], [27000 - 1000 * i for i in range(12)]):
+        _check_page_locked(resnet, lens)
+
+
+def _check_page_locked(resnet, lens):
     import torch
     _, model = resnet
     cr = torch.cuda.cudart()
-    lens = [16000 + 1000 * i for i in range(12)]
     parts = [vd_synth.clip_f32(vd_synth.make_clip(700 + i, n)) for i, n in enumerate(lens)]
     pcm = np.concatenate(parts)
     offs = np.concatenate([[0], np.cumsum(lens)[:-1]])

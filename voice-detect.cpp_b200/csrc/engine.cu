@@ -1663,8 +1663,6 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
     // DRAM per input byte (read the caller's array, write the ring, DMA out of it)
     // against one for the direct copy, and with eight ranks per host that memory
     // bandwidth, not PCIe, bounded the f32 call.
-    std::vector<char> pinned((size_t)n);
-    for (int i = 0; i < n; ++i) pinned[i] = host_pinned(pcm[i], (size_t)n_in[i] * esz) ? 1 : 0;
     // Buckets run shortest clips first: the first bucket's host gather and copy are
     // the only ones nothing overlaps, so it should be the smallest.
     const size_t nbk = bk.size() - 1;
@@ -1673,8 +1671,11 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         const int s = (int)(step & 1);
         const int cnt = (int)(bk[k + 1] - bk[k]);
         const int* idx = order.data() + bk[k];
+        // checked bucket by bucket, so that all but the first bucket's checks overlap
+        // the previous bucket's compute
         bool direct = true;
-        for (int j = 0; j < cnt && direct; ++j) direct = pinned[idx[j]] != 0;
+        for (int j = 0; j < cnt && direct; ++j)
+            direct = host_pinned(pcm[idx[j]], (size_t)n_in[idx[j]] * esz);
         // the pinned slots (PCM ring, conversion metadata) are free once their
         // previous H2D copies finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaEventSynchronize(h2d_ev_[s]));
@@ -1704,11 +1705,20 @@ int Engine::embed_host_raw(const void* const* pcm, int type, const int* n_in, in
         // the device slot is free once the bucket that last read it finished
         if (ring_used_[s]) VDB_CHECK_CUDA(cudaStreamWaitEvent(copy_stream_, comp_ev_[s], 0));
         if (direct) {
-            // the same packed layout the gather writes: clip j at input offset bi[j]
-            for (int j = 0; j < cnt; ++j)
+            // the same packed layout the gather writes: clip j at input offset bi[j];
+            // clips that also follow one another in the caller's memory go as one copy
+            for (int j = 0; j < cnt;) {
+                const char* src = static_cast<const char*>(pcm[idx[j]]);
+                size_t bytes = (size_t)n_in[idx[j]] * esz;
+                int e = j + 1;
+                while (e < cnt && static_cast<const char*>(pcm[idx[e]]) == src + bytes) {
+                    bytes += (size_t)n_in[idx[e]] * esz;
+                    ++e;
+                }
                 VDB_CHECK_CUDA(cudaMemcpyAsync(static_cast<char*>(d_ring_[s]) + (size_t)bi[j] * esz,
-                                               pcm[idx[j]], (size_t)n_in[idx[j]] * esz,
-                                               cudaMemcpyHostToDevice, copy_stream_));
+                                               src, bytes, cudaMemcpyHostToDevice, copy_stream_));
+                j = e;
+            }
         } else {
             VDB_CHECK_CUDA(cudaMemcpyAsync(d_ring_[s], h_ring_[s], (size_t)tot_in * esz,
                                            cudaMemcpyHostToDevice, copy_stream_));
