@@ -7,6 +7,8 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+
+#include "host_copy.h"
 #include <numeric>
 #include <thread>
 
@@ -1478,7 +1480,8 @@ void Engine::plan_buckets(const int* nsamp, int n, long long frame_cap, std::vec
 // Copies clips into one pinned buffer, splitting the bytes over threads (one per
 // 4 MB, at most 16 and the host's cores): one core's memcpy moves ~5 GB/s, and with
 // 8 MB per thread the gather of a 128-clip bucket of 4 s clips took longer than its
-// compute, which bounded the host-PCM path at half the device rate.
+// compute, which bounded the host-PCM path at half the device rate. The buffer is
+// written with streaming stores (host_copy.h): only the copy engine reads it.
 // Gather `count` clips (elements of `esz` bytes; clip idx[k] has nsamp[idx[k]]
 // elements at pcm[idx[k]]) back to back into dst.
 static void gather_clips(char* dst, const void* const* pcm, const int* nsamp, size_t esz,
@@ -1495,9 +1498,11 @@ static void gather_clips(char* dst, const void* const* pcm, const int* nsamp, si
         for (size_t pos = lo; pos < hi && k < count; ++k) {
             const size_t a = std::max(pos, off[k]), b = std::min(hi, off[k + 1]);
             if (b > a)
-                std::memcpy(dst + a, static_cast<const char*>(pcm[idx[k]]) + (a - off[k]), b - a);
+                vdb_stream_copy(dst + a, static_cast<const char*>(pcm[idx[k]]) + (a - off[k]),
+                                b - a);
             pos = b;
         }
+        vdb_stream_fence();  // visible before the caller issues the DMA
     };
     if (nt <= 1) {
         work(0);
