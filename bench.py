@@ -122,16 +122,17 @@ def make_pool(n: int = POOL, seconds: float = 20.0) -> list[np.ndarray]:
 
 
 def host_register(arr: np.ndarray):
-    """Page-lock a host array in place (cudaHostRegister, its exact bytes) and return
-    the call that unlocks it. The engine's host batch calls copy clips that lie in
-    page-locked memory to the device directly, without gathering them on the host."""
-    import torch
-    cr = torch.cuda.cudart()
-    ptr, nb = arr.ctypes.data, arr.nbytes
-    rc = cr.cudaHostRegister(ptr, nb, 0)
-    if rc != cr.cudaError.success:
-        raise RuntimeError(f"cudaHostRegister of {nb} bytes failed: {cr.cudaGetErrorString(rc)}")
-    return lambda: cr.cudaHostUnregister(ptr)
+    """Page-lock a host array in place (voicedetect_b200_host_register, its exact
+    bytes). Returns (unlock, note): the call that unlocks it and a description of the
+    memory for the JSON line. The engine's host batch calls copy clips that lie in
+    page-locked memory to the device directly, without gathering them on the host.
+    Where the host refuses (a locked-memory limit), the array stays pageable and the
+    note says why."""
+    import vd_b200
+    if not vd_b200.host_register(arr):
+        return (lambda: None), f"pageable (page-locking refused: {vd_b200.last_error()})"
+    return (lambda: vd_b200.host_unregister(arr)), \
+        "page-locked (voicedetect_b200_host_register)"
 
 
 def timed_calls(call, warmup: int, steps: int, dev, world: int) -> float:
@@ -654,22 +655,22 @@ def run_b200(args) -> int:
     # clip from the caller's buffer).
     p_sec = timed_calls(lambda: model.embed_batch(clips), E2E_WARMUP, args.e2e_steps, dev,
                         world)
-    unlock = [host_register(host_pcm)]
+    unlock, mem_note = host_register(host_pcm)
     e_sec = timed_calls(lambda: model.embed_batch(clips), E2E_WARMUP, args.e2e_steps, dev, world)
     e2e_value = float(tot_audio.item()) / e_sec
     # the same shard as int16 (the generator's samples; f32 = int16 / 32768 exactly)
     # through voicedetect_b200_embed_s16_batch: half the PCIe bytes, converted on the GPU
     host16 = np.round(host_pcm * 32768.0).astype(np.int16)
-    unlock.append(host_register(host16))
+    unlock16, mem16_note = host_register(host16)
     clips16 = [host16[offs[k]:offs[k] + lens[k]] for k in range(n_local)]
     s_sec = timed_calls(lambda: model.embed_batch_s16(clips16), E2E_WARMUP, args.e2e_steps, dev,
                         world)
-    for u in unlock:
-        u()
+    unlock()
+    unlock16()
     e2e_s16 = {"value": float(tot_audio.item()) / s_sec, "unit": UNIT,
                "h2d_bytes_per_step": 2 * total, "d2h_bytes_per_step": 4 * n_local * model.dim,
                "api": "voicedetect_b200_embed_s16_batch", "warmup_calls": E2E_WARMUP,
-               "timed_calls": args.e2e_steps}
+               "timed_calls": args.e2e_steps, "host_memory": mem16_note}
 
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -686,7 +687,7 @@ def run_b200(args) -> int:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * total,
                 "d2h_bytes_per_step": 4 * n_local * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": E2E_WARMUP,
-                "timed_calls": args.e2e_steps, "host_memory": "page-locked (cudaHostRegister)",
+                "timed_calls": args.e2e_steps, "host_memory": mem_note,
                 "h2d_gbs_per_rank": 4 * total / e_sec / 1e9,
                 "host_cores_per_rank": len(cores) if cores else (os.cpu_count() or 0)},
         "e2e_pageable": {"value": float(tot_audio.item()) / p_sec, "unit": UNIT,
@@ -1011,14 +1012,14 @@ def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
     # one warm-up call: its equal-shape buckets are launched, captured and replayed;
     # pageable first, then the same arrays page-locked in place (the e2e figure)
     p_sec = timed_calls(lambda: model.embed_batch(clips), 1, args.e2e_steps, dev, world)
-    unlock = [host_register(host_pcm)]
+    unlock, mem_note = host_register(host_pcm)
     e_sec = timed_calls(lambda: model.embed_batch(clips), 1, args.e2e_steps, dev, world)
     host16 = np.round(host_pcm * 32768.0).astype(np.int16)
-    unlock.append(host_register(host16))
+    unlock16, mem16_note = host_register(host16)
     clips16 = [host16[i * n:(i + 1) * n] for i in range(B)]
     s_sec = timed_calls(lambda: model.embed_batch_s16(clips16), 1, args.e2e_steps, dev, world)
-    for u in unlock:
-        u()
+    unlock()
+    unlock16()
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
@@ -1033,7 +1034,7 @@ def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
         "e2e": {"value": audio_step / e_sec, "unit": UNIT,
                 "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
                 "api": "voicedetect_capi_embed_pcm_batch", "warmup_calls": 1,
-                "timed_calls": args.e2e_steps, "host_memory": "page-locked (cudaHostRegister)"},
+                "timed_calls": args.e2e_steps, "host_memory": mem_note},
         "e2e_pageable": {"value": audio_step / p_sec, "unit": UNIT,
                          "h2d_bytes_per_step": 4 * B * n,
                          "d2h_bytes_per_step": 4 * B * model.dim,
@@ -1043,7 +1044,7 @@ def measure_family(fam: "_Family", args, world: int, rank: int, dev) -> dict:
         "e2e_s16": {"value": audio_step / s_sec, "unit": UNIT,
                     "h2d_bytes_per_step": 2 * B * n, "d2h_bytes_per_step": 4 * B * model.dim,
                     "api": "voicedetect_b200_embed_s16_batch", "warmup_calls": 1,
-                    "timed_calls": args.e2e_steps},
+                    "timed_calls": args.e2e_steps, "host_memory": mem16_note},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                      "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,

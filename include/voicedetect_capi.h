@@ -23,6 +23,7 @@
 #ifndef VOICEDETECT_CAPI_H
 #define VOICEDETECT_CAPI_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -131,6 +132,15 @@ long long voicedetect_b200_last_launches(voicedetect_ctx* ctx);
  * size of the largest conv, ~1.25 MB for ResNet34, not counted here), QPACK copies
  * included; 0 for other models or NULL. No reference counterpart. */
 long long voicedetect_b200_conv_weight_bytes(voicedetect_ctx* ctx);
+
+/* Page-lock `bytes` of the caller's host memory at `ptr` in place (for every device of
+ * the process), so that the batch calls copy clips stored there straight to the GPU
+ * instead of gathering them first; voicedetect_b200_host_unregister(ptr) undoes it
+ * before the memory is freed. 0 on success; otherwise 1 with the reason in
+ * vdb_last_error() (e.g. a locked-memory limit), and the memory stays usable as
+ * pageable. No reference counterpart. */
+int voicedetect_b200_host_register(void* ptr, size_t bytes);
+int voicedetect_b200_host_unregister(void* ptr);
 
 /* Embedding dimension of the loaded model (0 for NULL). */
 int voicedetect_b200_embedding_dim(voicedetect_ctx* ctx);

@@ -48,6 +48,10 @@ def test_abi_version_and_null_safety():
     assert L.voicedetect_capi_verify_paths(None, b"a", b"b", 0.25, None, None) == 1
     assert L.voicedetect_capi_analyze_path_json(None, b"a") is None
     assert L.voicedetect_capi_set_devices(None, 1) == 1
+    # the page-locking helpers refuse NULL / empty ranges before touching CUDA
+    assert L.voicedetect_b200_host_register(None, 16) == 1
+    assert b"NULL" in L.vdb_last_error()
+    assert L.voicedetect_b200_host_unregister(None) == 1
 
 
 def test_load_rejects_corrupt_gguf(tmp_path):

@@ -106,21 +106,20 @@ def test_odd_staging_capacity_both_slots(resnet, tmp_path, cuda_lib):
 
 
 def test_page_locked_clips_copied_directly(resnet):
-    """Clips in page-locked host memory (cudaHostRegister) reach the device by DMA from
-    the caller's buffer instead of the engine's gather. The embeddings must equal the
-    pageable call's bit for bit, for f32 and int16 input, with every clip locked and
-    with a batch that mixes locked and pageable clips (gathered). Clips stored in
-    ascending length are copied one by one (the engine runs them longest first, so
-    neighbours in its order are not neighbours in memory); stored in descending length
-    they follow one another in both and go as merged copies."""
+    """Clips in page-locked host memory (voicedetect_b200_host_register) reach the device
+    by DMA from the caller's buffer instead of the engine's gather. The embeddings must
+    equal the pageable call's bit for bit, for f32 and int16 input, with every clip
+    locked and with a batch that mixes locked and pageable clips (gathered). Clips
+    stored in ascending length are copied one by one (the engine runs them longest
+    first, so neighbours in its order are not neighbours in memory); stored in
+    descending length they follow one another in both and go as merged copies."""
     for lens in ([16000 + 1000 * i for i in range(12)], [27000 - 1000 * i for i in range(12)]):
         _check_page_locked(resnet, lens)
 
 
 def _check_page_locked(resnet, lens):
-    import torch
+    import vd_b200
     _, model = resnet
-    cr = torch.cuda.cudart()
     parts = [vd_synth.clip_f32(vd_synth.make_clip(700 + i, n)) for i, n in enumerate(lens)]
     pcm = np.concatenate(parts)
     offs = np.concatenate([[0], np.cumsum(lens)[:-1]])
@@ -132,7 +131,7 @@ def _check_page_locked(resnet, lens):
     locked = []
     try:
         for a in (pcm, pcm16):
-            assert cr.cudaHostRegister(a.ctypes.data, a.nbytes, 0) == cr.cudaError.success
+            assert vd_b200.host_register(a), vd_b200.last_error()
             locked.append(a)
         np.testing.assert_array_equal(model.embed_batch(clips), want)
         np.testing.assert_array_equal(model.embed_batch_s16(clips16), want16)
@@ -140,7 +139,7 @@ def _check_page_locked(resnet, lens):
         np.testing.assert_array_equal(model.embed_batch(mixed), want)
     finally:
         for a in locked:
-            cr.cudaHostUnregister(a.ctypes.data)
+            vd_b200.host_unregister(a)
 
 
 def test_verify_verdicts_match_oracle(resnet, tmp_path):

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "engine.hpp"
+#include "vdb_internal.h"
 
 #define VOICEDETECT_CAPI_ABI_VERSION 1
 
@@ -642,3 +643,31 @@ extern "C" int voicedetect_b200_load_audio_16k_mono(const char* wav_path, float*
 }
 
 extern "C" const char* voicedetect_b200_audio_error(void) { return g_audio_error.c_str(); }
+
+extern "C" int voicedetect_b200_host_register(void* ptr, size_t bytes) {
+    if (!ptr || bytes == 0) {
+        vdb::set_error("voicedetect_b200_host_register: NULL pointer or zero bytes");
+        return 1;
+    }
+    const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // a failed registration must not surface at a later launch check
+        vdb::set_error(std::string("voicedetect_b200_host_register: ") + cudaGetErrorString(e));
+        return 1;
+    }
+    return 0;
+}
+
+extern "C" int voicedetect_b200_host_unregister(void* ptr) {
+    if (!ptr) {
+        vdb::set_error("voicedetect_b200_host_unregister: NULL pointer");
+        return 1;
+    }
+    const cudaError_t e = cudaHostUnregister(ptr);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        vdb::set_error(std::string("voicedetect_b200_host_unregister: ") + cudaGetErrorString(e));
+        return 1;
+    }
+    return 0;
+}

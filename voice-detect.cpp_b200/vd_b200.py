@@ -185,6 +185,10 @@ def lib() -> C.CDLL:
         L.voicedetect_b200_conv_weight_bytes.argtypes = [C.c_void_p]
         L.voicedetect_b200_release_cache.restype = C.c_int
         L.voicedetect_b200_release_cache.argtypes = [C.c_void_p]
+        L.voicedetect_b200_host_register.restype = C.c_int
+        L.voicedetect_b200_host_register.argtypes = [C.c_void_p, C.c_size_t]
+        L.voicedetect_b200_host_unregister.restype = C.c_int
+        L.voicedetect_b200_host_unregister.argtypes = [C.c_void_p]
         L.voicedetect_b200_profile.restype = C.c_int
         L.voicedetect_b200_profile.argtypes = [C.c_void_p, C.c_int]
         L.voicedetect_b200_profile_read.restype = C.c_int
@@ -382,6 +386,18 @@ class Model:
 
 def last_error() -> str:
     return lib().vdb_last_error().decode()
+
+
+def host_register(arr) -> bool:
+    """Page-lock a contiguous numpy array in place (voicedetect_b200_host_register), so
+    the batch calls copy clips stored in it straight to the GPU. Returns False, with
+    the reason in last_error(), where the host refuses; the array stays usable."""
+    return lib().voicedetect_b200_host_register(arr.ctypes.data, arr.nbytes) == 0
+
+
+def host_unregister(arr) -> None:
+    """Undo host_register(arr) (before the array is freed)."""
+    _check(lib().voicedetect_b200_host_unregister(arr.ctypes.data), "host_unregister")
 
 
 def _check(rc: int, what: str) -> None:
